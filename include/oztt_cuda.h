@@ -1,0 +1,161 @@
+/* SPDX-License-Identifier: Apache-2.0
+ *
+ * C ABI of the B200 Ozaki backend (liboztt.so). Plain pointers and sizes only; every entry point
+ * returns OZTT_OK or an error code and writes a message into err[errlen] (NUL-terminated, may be
+ * NULL). The C++ public API (ozTTgemm/ozTTgemm.hpp) turns the codes into the reference's exception
+ * types: OZTT_EINVAL -> std::invalid_argument, OZTT_ERUNTIME -> std::runtime_error,
+ * OZTT_ENOMEM -> std::bad_alloc.
+ *
+ * Layering, with the reference interface each entry point stands in for (paths relative to the
+ * reference project root):
+ *   oztt_gemm                 Context::gemm (src/context.cpp:182-186): validation, planning, GPU run
+ *   oztt_ii_int8_plan         choose_moduli_and_width (src/backend/ozaki2/plan.hpp:258-306) for INT8
+ *   oztt_ii_int8_run          ozaki2_int8::run (src/ozaki2.cpp:439-478) on host buffers: the backend
+ *                             seam Backend = Output(*)(Device&, const Problem&)
+ *                             (src/backend_interface.hpp:34)
+ *   oztt_ii_int8_run_device   the same pipeline on device-resident operands (the whole-pass replay
+ *                             of src/evaluation_hooks.hpp:175-214 times this part)
+ *   oztt_ii_scale_rows/cols   scale_f64_reader.cpp:129-198 + expdelta.cpp:44-91 (row maxima of A,
+ *                             column maxima of B, exponent deltas, range flags)
+ *   oztt_ii_split_rows/cols   slice_f64_reader.cpp + ozaki2/kernels/modslice_int8.cpp (residues)
+ *   oztt_ii_residue_gemm      run_int8_gemms (src/ozaki2.cpp:333-348) with bmm_int32_spill.cpp
+ *   oztt_ii_recon             recon_crt.cpp + recon_reader.cpp/recon_writer.cpp (CRT to FP64)
+ */
+#ifndef OZTT_CUDA_H
+#define OZTT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OZTT_OK 0
+#define OZTT_EINVAL 1   /* invalid argument (std::invalid_argument) */
+#define OZTT_ERUNTIME 2 /* configuration cannot be executed, or a CUDA failure (std::runtime_error) */
+#define OZTT_ENOMEM 3   /* host memory exhausted (std::bad_alloc) */
+
+#define OZTT_MAXS 24
+
+/* Values of the public enums (ozTTgemm::Scheme, Format, Reconstruction), in declaration order. */
+enum { OZTT_SCHEME_I = 0, OZTT_SCHEME_II = 1 };
+enum {
+    OZTT_FMT_BF16 = 0,
+    OZTT_FMT_FP16 = 1,
+    OZTT_FMT_TF32 = 2,
+    OZTT_FMT_BFP8 = 3,
+    OZTT_FMT_FP8 = 4,
+    OZTT_FMT_INT8 = 5,
+    OZTT_FMT_BFP4 = 6,
+    OZTT_FMT_BFP2 = 7
+};
+enum { OZTT_RECON_AUTO = 0, OZTT_RECON_ONE = 1, OZTT_RECON_TWO = 2 };
+
+typedef struct oztt_options {
+    int32_t scheme;
+    int32_t format;
+    uint32_t slices;
+    uint32_t max_moduli;
+    int32_t reconstruction;
+} oztt_options;
+
+typedef struct oztt_info {
+    int32_t scheme;
+    int32_t format;
+    uint32_t slices;
+    uint32_t moduli;
+    uint32_t integer_bits;
+    uint32_t reconstruction_passes;
+    uint64_t padded_m, padded_n, padded_k;
+} oztt_info;
+
+/* Plan of one Scheme II INT8 call (the decisions of choose_moduli_and_width and the constants of
+ * oz2_crt_constants, src/backend/ozaki2/moduli.hpp:615-703, that the kernels need). */
+typedef struct oztt_ii_plan {
+    uint32_t M, N, K;      /* planning dimensions: m, n rounded up to 64, k to 32 */
+    int32_t S;             /* number of moduli */
+    int32_t b;             /* integer width */
+    int32_t nd;            /* radix-2^20 digits of A' (3, 4 or 5) */
+    int32_t shift;         /* b - 20*(nd-1) */
+    int32_t two_pass;      /* 1 if the reference would run two reconstruction passes */
+    int32_t b_cap;         /* width cap passed to the moduli selection */
+    int32_t S_req;         /* limit on the number of moduli */
+    int32_t moduli[OZTT_MAXS];
+    int32_t yi[OZTT_MAXS];         /* (M/m_i)^-1 mod m_i */
+    float rinv[OZTT_MAXS];         /* fl32(1/m_i) */
+    float c[4][OZTT_MAXS];         /* 2^20, 2^40, 2^60, 2^80 mod m_i */
+    double TA, TB, nA, nB, nC;     /* input statistics of the precision policy (0 when not measured) */
+    double recon1_log2;            /* estimated log2 error of one reconstruction pass */
+} oztt_ii_plan;
+
+/* ---- whole calls ---------------------------------------------------------------------------- */
+
+/* Context::gemm on host row-major buffers (a: m*k, b: k*n, c: m*n; the *_len are the span sizes).
+ * Validates exactly like the reference front end, plans, runs on CUDA device device_id, writes C
+ * and info. c may overlap a or b. */
+int oztt_gemm(int device_id, const double* a, uint64_t a_len, const double* b, uint64_t b_len, double* c,
+              uint64_t c_len, uint64_t m, uint64_t n, uint64_t k, const oztt_options* opt, oztt_info* info, char* err,
+              size_t errlen);
+
+/* Scheme II INT8 plan for row-major a (m x k) and b (k x n) on the host. reconstruction is an
+ * OZTT_RECON_* value; fixed_bits > 0 fixes the width (the reference evaluator's fixed_bits), 0 lets
+ * the library choose it from the input. */
+int oztt_ii_int8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
+                      int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan* plan, char* err, size_t errlen);
+
+/* The Scheme II INT8 pipeline for host buffers (copies in, runs, copies C back). */
+int oztt_ii_int8_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                     const oztt_ii_plan* plan, char* err, size_t errlen);
+
+/* The pipeline on device buffers (row-major, lda = k, ldb = n, ldc = n) on a cudaStream_t (NULL:
+ * the legacy default stream). Scratch comes from the stream-ordered allocator and is released
+ * before return. Synchronises the stream before returning. */
+int oztt_ii_int8_run_device(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                            uint64_t k, const oztt_ii_plan* plan, void* stream, char* err, size_t errlen);
+
+/* ---- stages (device pointers; asynchronous on `stream`) -------------------------------------- */
+
+/* Tile-padded dimensions of the residue planes: mp = m rounded up to 128, np = n rounded up to 256,
+ * kp = k rounded up to 128. */
+void oztt_ii_padded_dims(uint64_t m, uint64_t n, uint64_t k, uint64_t* mp, uint64_t* np, uint64_t* kp);
+
+/* Row maxima of a (m x k, lda): BF16 of max|a_ij| rounded up (bf16max, may be NULL), delta[i] =
+ * shift - ceil(log2 bf16max) (0 exponent for a zero row), flags |= 1 (above BF16), 2 (below
+ * 2^-126), 4 (Inf/NaN). flags must be zeroed by the caller; delta has m entries. */
+int oztt_ii_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t shift, int32_t* delta,
+                       uint16_t* bf16max, uint32_t* flags, void* stream, char* err, size_t errlen);
+/* Column maxima of b (k x n, ldb); delta has n entries. Uses n*8 bytes of stream-ordered scratch. */
+int oztt_ii_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
+                       uint16_t* bf16max, uint32_t* flags, void* stream, char* err, size_t errlen);
+
+/* Residues of a (m x k, lda) with delta per row: planes [S][mp][kp] int8, zero in the padding. */
+int oztt_ii_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
+                       const oztt_ii_plan* plan, int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err,
+                       size_t errlen);
+/* Residues of b (k x n, ldb) with delta per column, transposed: planes [S][np][kp] int8. */
+int oztt_ii_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
+                       const oztt_ii_plan* plan, int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err,
+                       size_t errlen);
+
+/* Per-modulus products of the planes on the tensor cores (tcgen05 kind::i8, s32 in TMEM).
+ * mode 0: out is int32 [S][mp][np], C_s = A_s * B_s^T exactly.
+ * mode 1: out is uint8 [S][mp][np], k_s = (C_s mod m_s) * y_s mod m_s in [0, m_s). */
+int oztt_ii_residue_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp, uint64_t np, uint64_t kp,
+                         const oztt_ii_plan* plan, int32_t mode, void* out, void* stream, char* err, size_t errlen);
+
+/* Exact CRT reconstruction from the uint8 planes k_s [S][mp][np]: C[i][j] (i < m, j < n, ldc) =
+ * C'_ij * 2^(2*shift - delta_a[i] - delta_b[j] - 2b), rounded once to nearest even; results below
+ * 2^-1022 are returned as signed zero. */
+int oztt_ii_recon(const uint8_t* k_planes, uint64_t mp, uint64_t np, const int32_t* delta_a, const int32_t* delta_b,
+                  const oztt_ii_plan* plan, double* c, uint64_t m, uint64_t n, uint64_t ldc, void* stream, char* err,
+                  size_t errlen);
+
+/* Number of SMs and compute capability of a device (0 on success). */
+int oztt_device_info(int device_id, int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OZTT_CUDA_H */

@@ -1,0 +1,275 @@
+"""ozTTgemm for NVIDIA B200 — Python mirror of the reference's public interface.
+
+The product is the C++/CUDA library ``oztt_b200/liboztt.so`` (C ABI in ``include/oztt_cuda.h``, C++
+API in ``include/ozTTgemm/ozTTgemm.hpp``). This module binds its C ABI with ctypes and mirrors the
+reference's C++ interface (mukunoki/ozTT ``include/ozTTgemm/ozTTgemm.hpp:25-121``) one to one:
+
+    Scheme, Format, Reconstruction, Options, DeviceOptions, Info, is_available, format_name,
+    Context.gemm / Context.multiply
+
+with the same argument meaning and the same error behaviour: ``ValueError`` where the reference
+throws ``std::invalid_argument``, ``RuntimeError`` for ``std::runtime_error``, ``MemoryError`` for
+``std::bad_alloc``. The lower-level functions (``ii_int8_plan``, ``ii_int8_run``, the stage calls)
+expose the backend seam and the individual kernels for tests and benchmarks.
+
+There is no CPU fallback: every compute call goes to the CUDA kernels, and importing the module
+fails if the library has not been built.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import enum
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+
+__all__ = [
+    "Scheme", "Format", "Reconstruction", "Options", "DeviceOptions", "Info", "Context",
+    "is_available", "format_name", "IIPlan", "ii_int8_plan", "ii_int8_run", "ii_int8_run_device",
+    "lib", "library_path",
+]
+
+_HERE = Path(__file__).resolve().parent
+library_path = _HERE / "liboztt.so"
+
+OK, EINVAL, ERUNTIME, ENOMEM = 0, 1, 2, 3
+MAXS = 24
+
+
+class Scheme(enum.IntEnum):
+    I = 0
+    II = 1
+
+
+class Format(enum.IntEnum):
+    BF16 = 0
+    FP16 = 1
+    TF32 = 2
+    BFP8 = 3
+    FP8 = 4
+    INT8 = 5
+    BFP4 = 6
+    BFP2 = 7
+
+
+class Reconstruction(enum.IntEnum):
+    Automatic = 0
+    OnePass = 1
+    TwoPass = 2
+
+
+@dataclass
+class Options:
+    scheme: int = Scheme.II
+    format: int = Format.BFP8
+    slices: int = 0
+    max_moduli: int = 0
+    reconstruction: int = Reconstruction.Automatic
+
+
+@dataclass
+class DeviceOptions:
+    device_id: int = 0
+    kernel_directory: str = ""
+
+
+@dataclass
+class Info:
+    scheme: Scheme = Scheme.II
+    format: Format = Format.INT8
+    slices: int = 0
+    moduli: int = 0
+    integer_bits: int = 0
+    reconstruction_passes: int = 0
+    padded_m: int = 0
+    padded_n: int = 0
+    padded_k: int = 0
+
+
+class _COptions(ctypes.Structure):
+    _fields_ = [("scheme", ctypes.c_int32), ("format", ctypes.c_int32), ("slices", ctypes.c_uint32),
+                ("max_moduli", ctypes.c_uint32), ("reconstruction", ctypes.c_int32)]
+
+
+class _CInfo(ctypes.Structure):
+    _fields_ = [("scheme", ctypes.c_int32), ("format", ctypes.c_int32), ("slices", ctypes.c_uint32),
+                ("moduli", ctypes.c_uint32), ("integer_bits", ctypes.c_uint32),
+                ("reconstruction_passes", ctypes.c_uint32), ("padded_m", ctypes.c_uint64),
+                ("padded_n", ctypes.c_uint64), ("padded_k", ctypes.c_uint64)]
+
+
+class IIPlan(ctypes.Structure):
+    """oztt_ii_plan: the decisions and CRT constants of one Scheme II INT8 call."""
+    _fields_ = [("M", ctypes.c_uint32), ("N", ctypes.c_uint32), ("K", ctypes.c_uint32),
+                ("S", ctypes.c_int32), ("b", ctypes.c_int32), ("nd", ctypes.c_int32), ("shift", ctypes.c_int32),
+                ("two_pass", ctypes.c_int32), ("b_cap", ctypes.c_int32), ("S_req", ctypes.c_int32),
+                ("moduli", ctypes.c_int32 * MAXS), ("yi", ctypes.c_int32 * MAXS), ("rinv", ctypes.c_float * MAXS),
+                ("c", (ctypes.c_float * MAXS) * 4), ("TA", ctypes.c_double), ("TB", ctypes.c_double),
+                ("nA", ctypes.c_double), ("nB", ctypes.c_double), ("nC", ctypes.c_double),
+                ("recon1_log2", ctypes.c_double)]
+
+    @property
+    def moduli_list(self) -> list[int]:
+        return [int(self.moduli[i]) for i in range(self.S)]
+
+
+_P = ctypes.c_void_p
+_U64 = ctypes.c_uint64
+_I32 = ctypes.c_int32
+_ERR = ctypes.c_char_p
+_SZ = ctypes.c_size_t
+
+_SIGNATURES = {
+    "oztt_gemm": [ctypes.c_int, _P, _U64, _P, _U64, _P, _U64, _U64, _U64, _U64, ctypes.POINTER(_COptions),
+                  ctypes.POINTER(_CInfo), _ERR, _SZ],
+    "oztt_ii_int8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, _I32, _I32, ctypes.POINTER(IIPlan), _ERR, _SZ],
+    "oztt_ii_int8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IIPlan), _ERR, _SZ],
+    "oztt_ii_int8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IIPlan), _P, _ERR, _SZ],
+    "oztt_ii_scale_rows": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _P, _ERR, _SZ],
+    "oztt_ii_scale_cols": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _P, _ERR, _SZ],
+    "oztt_ii_split_rows": [_P, _U64, _U64, _U64, _P, ctypes.POINTER(IIPlan), _P, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_ii_split_cols": [_P, _U64, _U64, _U64, _P, ctypes.POINTER(IIPlan), _P, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_ii_residue_gemm": [_P, _P, _U64, _U64, _U64, ctypes.POINTER(IIPlan), _I32, _P, _P, _ERR, _SZ],
+    "oztt_ii_recon": [_P, _U64, _U64, _P, _P, ctypes.POINTER(IIPlan), _P, _U64, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_device_info": [ctypes.c_int, ctypes.POINTER(_I32), ctypes.POINTER(_I32), ctypes.POINTER(_I32)],
+    "oztt_ii_padded_dims": [_U64, _U64, _U64, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
+    "oztt_test_udiv_small": [ctypes.c_uint32, ctypes.c_uint32],
+}
+
+# Symbols declared in include/oztt_cuda.h (the tests check that the library exports each of them).
+C_ABI_SYMBOLS = [name for name in _SIGNATURES if name != "oztt_test_udiv_small"]
+
+
+def _load() -> ctypes.CDLL:
+    if not library_path.exists():
+        raise ImportError(f"{library_path} is not built; run `python -m oztt_b200.build` "
+                          "(or __graft_entry__.build()) first")
+    lib_ = ctypes.CDLL(str(library_path))
+    for name, args in _SIGNATURES.items():
+        fn = getattr(lib_, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_uint32 if name == "oztt_test_udiv_small" else (
+            None if name == "oztt_ii_padded_dims" else ctypes.c_int)
+    return lib_
+
+
+lib = _load()
+
+
+def _raise(code: int, msg: bytes | str) -> None:
+    text = msg.decode(errors="replace") if isinstance(msg, bytes) else msg
+    if code == EINVAL:
+        raise ValueError(text)
+    if code == ENOMEM:
+        raise MemoryError(text)
+    raise RuntimeError(text)
+
+
+def _errbuf() -> ctypes.Array:
+    return ctypes.create_string_buffer(1024)
+
+
+def is_available(fmt) -> bool:
+    """False for formats this build does not provide (mirrors ozTTgemm::is_available)."""
+    return int(fmt) == Format.INT8
+
+
+def format_name(fmt) -> str:
+    try:
+        return Format(int(fmt)).name
+    except ValueError:
+        return "unknown"
+
+
+def _as_f64(x, name: str) -> np.ndarray:
+    arr = np.ascontiguousarray(x, dtype=np.float64).reshape(-1)
+    return arr
+
+
+class Context:
+    """Owns one CUDA device (ozTTgemm::Context); calls of all contexts are serialised by the library."""
+
+    def __init__(self, options: DeviceOptions | None = None):
+        self.options = options or DeviceOptions()
+        if self.options.device_id < 0:
+            raise ValueError("device_id must be nonnegative")
+
+    def gemm(self, a, b, c, m: int, n: int, k: int, options: Options | None = None) -> Info:
+        """C = A*B for row-major FP64 A[m,k], B[k,n]; C (a writable float64 buffer of m*n) is
+        overwritten. Raises ValueError / RuntimeError / MemoryError like the reference."""
+        opt = options or Options()
+        av, bv = _as_f64(a, "a"), _as_f64(b, "b")
+        if not (isinstance(c, np.ndarray) and c.dtype == np.float64 and c.flags.c_contiguous and c.flags.writeable):
+            raise ValueError("c must be a writable C-contiguous float64 array")
+        cv = c.reshape(-1)
+        co = _COptions(int(opt.scheme), int(opt.format), int(opt.slices), int(opt.max_moduli), int(opt.reconstruction))
+        ci = _CInfo()
+        err = _errbuf()
+        rc = lib.oztt_gemm(self.options.device_id, av.ctypes.data, av.size, bv.ctypes.data, bv.size, cv.ctypes.data,
+                           cv.size, m, n, k, ctypes.byref(co), ctypes.byref(ci), err, len(err))
+        if rc != OK:
+            _raise(rc, err.value)
+        return Info(Scheme(ci.scheme), Format(ci.format), ci.slices, ci.moduli, ci.integer_bits,
+                    ci.reconstruction_passes, ci.padded_m, ci.padded_n, ci.padded_k)
+
+    def multiply(self, a, b, m: int, n: int, k: int, options: Options | None = None) -> np.ndarray:
+        if m <= 0 or n <= 0:
+            # the library raises the reference's message for zero dimensions
+            c = np.zeros(0, dtype=np.float64)
+        else:
+            c = np.empty(m * n, dtype=np.float64)
+        self.gemm(a, b, c, m, n, k, options)
+        return c
+
+
+def ii_int8_plan(a, b, m: int, n: int, k: int, max_moduli: int = 0, reconstruction: int = 0,
+                 fixed_bits: int = 0) -> IIPlan:
+    """Scheme II INT8 plan for row-major host matrices (oztt_ii_int8_plan)."""
+    av, bv = _as_f64(a, "a"), _as_f64(b, "b")
+    if av.size != m * k or bv.size != k * n:
+        raise ValueError("matrix span sizes do not match m, n, k")
+    plan = IIPlan()
+    err = _errbuf()
+    rc = lib.oztt_ii_int8_plan(av.ctypes.data, bv.ctypes.data, m, n, k, max_moduli, reconstruction, fixed_bits,
+                               ctypes.byref(plan), err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return plan
+
+
+def ii_int8_run(a, b, m: int, n: int, k: int, plan: IIPlan, device_id: int = 0) -> np.ndarray:
+    """Run the Scheme II INT8 pipeline on host matrices with a given plan (oztt_ii_int8_run)."""
+    av, bv = _as_f64(a, "a"), _as_f64(b, "b")
+    c = np.empty(m * n, dtype=np.float64)
+    err = _errbuf()
+    rc = lib.oztt_ii_int8_run(device_id, av.ctypes.data, bv.ctypes.data, c.ctypes.data, m, n, k, ctypes.byref(plan),
+                              err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return c
+
+
+def ii_int8_run_device(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, plan: IIPlan,
+                       stream: int = 0, device_id: int = 0) -> None:
+    """The pipeline on device pointers (oztt_ii_int8_run_device); synchronises `stream`."""
+    err = _errbuf()
+    rc = lib.oztt_ii_int8_run_device(device_id, a_ptr, b_ptr, c_ptr, m, n, k, ctypes.byref(plan), stream, err,
+                                     len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+
+
+def padded_dims(m: int, n: int, k: int) -> tuple[int, int, int]:
+    mp, np_, kp = _U64(), _U64(), _U64()
+    lib.oztt_ii_padded_dims(m, n, k, ctypes.byref(mp), ctypes.byref(np_), ctypes.byref(kp))
+    return mp.value, np_.value, kp.value
+
+
+def call(name: str, *args) -> None:
+    """Call a stage entry point of the C ABI; the trailing (err, errlen) are appended here."""
+    err = _errbuf()
+    rc = getattr(lib, name)(*args, err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)

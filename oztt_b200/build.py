@@ -1,0 +1,107 @@
+"""Build the B200 Ozaki backend in-tree.
+
+Produces
+  oztt_b200/liboztt.so            the CUDA kernels for sm_100a, the planner, the C ABI
+                                  (include/oztt_cuda.h) and the C++ API (include/ozTTgemm/ozTTgemm.hpp)
+  oztt_b200/_build/gemm_example   examples/gemm.cpp linked against it
+  oztt_b200/_build/correctness    tests/cpp/correctness.cpp linked against it
+Object files go to oztt_b200/_build/. Nothing is installed outside the repository; the built files
+travel with the repository snapshot to the GPU machine.
+
+Run as ``python -m oztt_b200.build`` or through ``__graft_entry__.build()``.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+PKG = ROOT / "oztt_b200"
+CSRC = PKG / "csrc"
+OUT = PKG / "_build"
+LIB = PKG / "liboztt.so"
+
+NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+# The system compiler: the environment's CXX may name a toolchain without OpenMP support files.
+CXX = "/usr/bin/g++" if Path("/usr/bin/g++").exists() else (shutil.which("g++") or "g++")
+CUDA_HOME = Path(NVCC).resolve().parent.parent
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-ffp-contract=off",
+              "-ccbin", CXX, f"-I{ROOT / 'include'}"]
+CXX_FLAGS = ["-std=gnu++20", "-O2", "-fPIC", "-fno-fast-math", "-ffp-contract=off", "-pthread",
+             f"-I{ROOT / 'include'}", f"-I{CUDA_HOME / 'include'}"]
+
+CU_SOURCES = ["split.cu", "gemm_i8.cu", "recon.cu", "ii_int8.cu"]
+CPP_SOURCES = ["planner.cpp", "context.cpp"]
+
+
+def _run(cmd: list[str]) -> None:
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"build step failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+
+
+def _stale(target: Path, deps: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def build_library(force: bool = False) -> Path:
+    OUT.mkdir(parents=True, exist_ok=True)
+    headers = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.hpp")) + [ROOT / "include" / "oztt_cuda.h",
+                                                                      ROOT / "include" / "ozTTgemm" / "ozTTgemm.hpp"]
+    objs = []
+    for src in CU_SOURCES:
+        s, o = CSRC / src, OUT / (src + ".o")
+        if force or _stale(o, [s] + headers):
+            _run([NVCC, *ARCH, *NVCC_FLAGS, "-c", str(s), "-o", str(o)])
+        objs.append(o)
+    for src in CPP_SOURCES:
+        s, o = CSRC / src, OUT / (src + ".o")
+        if force or _stale(o, [s] + headers):
+            _run([CXX, *CXX_FLAGS, "-c", str(s), "-o", str(o)])
+        objs.append(o)
+    if force or _stale(LIB, objs):
+        _run([NVCC, *ARCH, "-shared", "-ccbin", CXX, "-o", str(LIB), *map(str, objs), "-lpthread"])
+    return LIB
+
+
+def build_programs(force: bool = False) -> None:
+    progs = {
+        "gemm_example": ROOT / "examples" / "gemm.cpp",
+        "correctness": ROOT / "tests" / "cpp" / "correctness.cpp",
+    }
+    for name, src in progs.items():
+        if not src.exists():
+            continue
+        exe = OUT / name
+        if force or _stale(exe, [src, LIB]):
+            _run([CXX, "-std=gnu++20", "-O2", f"-I{ROOT / 'include'}", str(src), "-o", str(exe),
+                  f"-L{PKG}", "-loztt", f"-Wl,-rpath,{PKG}", "-pthread"])
+
+
+def build_oracle() -> None:
+    """The CPU checker libraries (test infrastructure): oracle/liboz2oracle.so always, and
+    oracle/_ref/*.so when the reference tree is present on this machine."""
+    make = shutil.which("make") or "make"
+    _run([make, "-s", "-C", str(ROOT / "oracle"), "all"])
+    if Path("/root/reference/src/backend").is_dir():
+        _run([make, "-s", "-C", str(ROOT / "oracle"), "ref"])
+
+
+def build(force: bool = False) -> None:
+    build_library(force)
+    build_programs(force)
+    build_oracle()
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv)
+    print(f"built {LIB}")

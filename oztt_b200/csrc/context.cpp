@@ -1,0 +1,233 @@
+// SPDX-License-Identifier: Apache-2.0
+//
+// Public C++ API (include/ozTTgemm/ozTTgemm.hpp) on top of the CUDA backend, and its C-ABI form
+// oztt_gemm. Front-end semantics follow the reference's src/context.cpp:
+//   * the same checks in the same order, before the device is touched and before C is written
+//     (check_options :82-93, span sizes, padding to 64/64/32 with the 32-bit tile-offset limit
+//     :103-117, finiteness and the [2^-126, largest BF16] range of every nonzero row maximum of A and
+//     column maximum of B :37-62), with the same exception types and messages;
+//   * one process-wide mutex serialises the calls of all contexts (:19, :152);
+//   * the device is opened on the first valid call; Info reports the padded dimensions (:176-180);
+//   * all input is consumed before C is written, so C may overlap A or B.
+// Dispatch (src/dispatch.cpp:18-50): INT8 is built; the Tenstorrent block formats BFP8/BFP4/BFP2
+// are not available on this hardware, and the other formats are not built yet.
+#include <ozTTgemm/ozTTgemm.hpp>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <mutex>
+#include <optional>
+#include <stdexcept>
+#include <string>
+
+#include "oztt_cuda.h"
+#include "planner.hpp"
+
+namespace oztt {
+void run_ii_int8_host(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                      const oztt_ii_plan& p);
+void open_device_checked(int device_id);
+struct Error;
+}  // namespace oztt
+
+namespace ozTTgemm {
+namespace {
+
+std::mutex runtime_mutex;
+
+std::size_t checked_product(std::size_t a, std::size_t b) {
+    if (a == 0 || b == 0 || a > std::numeric_limits<std::size_t>::max() / sizeof(double) / b)
+        throw std::invalid_argument("matrix dimensions are zero or overflow the address space");
+    return a * b;
+}
+std::uint32_t padded(std::size_t value, std::size_t quantum) {
+    constexpr std::size_t limit = std::numeric_limits<std::int32_t>::max();
+    if (value == 0 || value > limit - quantum)
+        throw std::invalid_argument("matrix dimension exceeds the supported device index range");
+    return static_cast<std::uint32_t>((value + quantum - 1) / quantum * quantum);
+}
+void check_values(std::span<const double> a, std::span<const double> b, std::size_t m, std::size_t n, std::size_t k) {
+    constexpr double maximum = 0x1.fep127;
+    constexpr double minimum = 0x1p-126;
+    const auto check_max = [&](double x) {
+        if (x != 0 && (x < minimum || x > maximum))
+            throw std::invalid_argument(
+                "each nonzero row maximum of A and column maximum of B must be in [2^-126, max_BF16]");
+    };
+    for (std::size_t i = 0; i < m; ++i) {
+        double mx = 0;
+        for (std::size_t j = 0; j < k; ++j) {
+            const double x = a[i * k + j];
+            if (!std::isfinite(x)) throw std::invalid_argument("A contains NaN or infinity");
+            mx = std::max(mx, std::abs(x));
+        }
+        check_max(mx);
+    }
+    std::vector<double> maxima(n, 0);
+    for (std::size_t i = 0; i < k; ++i)
+        for (std::size_t j = 0; j < n; ++j) {
+            const double x = b[i * n + j];
+            if (!std::isfinite(x)) throw std::invalid_argument("B contains NaN or infinity");
+            maxima[j] = std::max(maxima[j], std::abs(x));
+        }
+    for (double x : maxima) check_max(x);
+}
+void check_options(const Options& o) {
+    if (o.scheme != Scheme::I && o.scheme != Scheme::II) throw std::invalid_argument("unknown Ozaki scheme");
+    if (!is_available(o.format)) throw std::invalid_argument("format is unknown or was not built");
+    if (o.reconstruction != Reconstruction::Automatic && o.reconstruction != Reconstruction::OnePass &&
+        o.reconstruction != Reconstruction::TwoPass)
+        throw std::invalid_argument("unknown reconstruction mode");
+    if (o.slices > 256) throw std::invalid_argument("slices must be zero (automatic) or at most 256");
+    if (o.max_moduli > 24) throw std::invalid_argument("max_moduli exceeds the supported bound of 24");
+    if (o.scheme == Scheme::I && (o.max_moduli != 0 || o.reconstruction != Reconstruction::Automatic))
+        throw std::invalid_argument("max_moduli and reconstruction apply only to Ozaki II");
+    if (o.scheme == Scheme::II && o.slices != 0) throw std::invalid_argument("slices applies only to Ozaki I");
+}
+struct Checked {
+    std::uint32_t mp, np, kp;
+    std::size_t c_size;
+};
+Checked validate(const Options& options, std::span<const double> a, std::span<const double> b,
+                 std::optional<std::size_t> c_size, std::size_t m, std::size_t n, std::size_t k) {
+    check_options(options);
+    if (a.size() != checked_product(m, k) || b.size() != checked_product(k, n))
+        throw std::invalid_argument("matrix span sizes do not match m, n, k");
+    const std::size_t mn = checked_product(m, n);
+    if (c_size && *c_size != mn) throw std::invalid_argument("matrix span sizes do not match m, n, k");
+    const Checked v{padded(m, 64), padded(n, 64), padded(k, 32), mn};
+    for (auto count : {std::uint64_t(v.mp / 32) * (v.kp / 32), std::uint64_t(v.kp / 32) * (v.np / 32),
+                       std::uint64_t(v.mp / 32) * (v.np / 32)})
+        if (count > std::numeric_limits<std::uint32_t>::max() / 4096u)
+            throw std::invalid_argument("matrix is too large for the device's 32-bit offsets");
+    check_values(a, b, m, n, k);
+    return v;
+}
+int32_t recon_code(Reconstruction r) {
+    return r == Reconstruction::OnePass ? OZTT_RECON_ONE : (r == Reconstruction::TwoPass ? OZTT_RECON_TWO : OZTT_RECON_AUTO);
+}
+[[noreturn]] void rethrow(int code, const std::string& msg) {
+    if (code == OZTT_EINVAL) throw std::invalid_argument(msg);
+    if (code == OZTT_ENOMEM) throw std::bad_alloc();
+    throw std::runtime_error(msg);
+}
+
+}  // namespace
+
+bool is_available(Format format) noexcept { return format == Format::INT8; }
+
+const char* format_name(Format format) noexcept {
+    switch (format) {
+    case Format::BF16: return "BF16";
+    case Format::FP16: return "FP16";
+    case Format::TF32: return "TF32";
+    case Format::BFP8: return "BFP8";
+    case Format::FP8: return "FP8";
+    case Format::INT8: return "INT8";
+    case Format::BFP4: return "BFP4";
+    case Format::BFP2: return "BFP2";
+    default: return "unknown";
+    }
+}
+
+struct Context::Impl {
+    explicit Impl(DeviceOptions o) : options(std::move(o)) {
+        if (options.device_id < 0) throw std::invalid_argument("device_id must be nonnegative");
+    }
+    Info execute(std::span<const double> a, std::span<const double> b, std::span<double> c, std::size_t m,
+                 std::size_t n, std::size_t k, const Options& opt, const Checked& v);
+    DeviceOptions options;
+    bool opened = false;
+};
+
+Context::Context(DeviceOptions options) : impl_(std::make_unique<Impl>(std::move(options))) {}
+Context::~Context() = default;
+
+Info Context::Impl::execute(std::span<const double> a, std::span<const double> b, std::span<double> c, std::size_t m,
+                            std::size_t n, std::size_t k, const Options& opt, const Checked& v) {
+    std::lock_guard lock(runtime_mutex);
+    if (opt.scheme == Scheme::I)
+        throw std::runtime_error("Ozaki scheme I is not available in this build of ozTTgemm for B200");
+    oztt_ii_plan plan;
+    std::string msg;
+    int rc = oztt::plan_ii_int8(a.data(), b.data(), m, n, k, opt.max_moduli, recon_code(opt.reconstruction), 0, plan, msg);
+    if (rc != OZTT_OK) rethrow(rc, msg);
+    char err[512] = {0};
+    rc = oztt_ii_int8_run(options.device_id, a.data(), b.data(), c.data(), m, n, k, &plan, err, sizeof err);
+    if (rc != OZTT_OK) rethrow(rc, err);
+    opened = true;
+    Info info{Scheme::II, opt.format};
+    info.moduli = (std::uint32_t)plan.S;
+    info.integer_bits = (std::uint32_t)plan.b;
+    info.reconstruction_passes = plan.two_pass ? 2u : 1u;
+    info.padded_m = v.mp;
+    info.padded_n = v.np;
+    info.padded_k = v.kp;
+    return info;
+}
+
+Info Context::gemm(std::span<const double> a, std::span<const double> b, std::span<double> c, std::size_t m,
+                   std::size_t n, std::size_t k, const Options& options) {
+    const Checked v = validate(options, a, b, c.size(), m, n, k);
+    return impl_->execute(a, b, c, m, n, k, options, v);
+}
+
+std::vector<double> Context::multiply(std::span<const double> a, std::span<const double> b, std::size_t m,
+                                      std::size_t n, std::size_t k, const Options& options) {
+    const Checked v = validate(options, a, b, std::nullopt, m, n, k);
+    std::vector<double> c(v.c_size);
+    impl_->execute(a, b, c, m, n, k, options, v);
+    return c;
+}
+
+}  // namespace ozTTgemm
+
+extern "C" int oztt_gemm(int device_id, const double* a, uint64_t a_len, const double* b, uint64_t b_len, double* c,
+                         uint64_t c_len, uint64_t m, uint64_t n, uint64_t k, const oztt_options* opt, oztt_info* info,
+                         char* err, size_t errlen) {
+    auto put = [&](const char* s) {
+        if (err && errlen) {
+            std::strncpy(err, s, errlen - 1);
+            err[errlen - 1] = 0;
+        }
+    };
+    try {
+        if (!opt) throw std::invalid_argument("null options");
+        ozTTgemm::Options o;
+        o.scheme = static_cast<ozTTgemm::Scheme>(opt->scheme);
+        o.format = static_cast<ozTTgemm::Format>(opt->format);
+        o.slices = opt->slices;
+        o.max_moduli = opt->max_moduli;
+        o.reconstruction = static_cast<ozTTgemm::Reconstruction>(opt->reconstruction);
+        ozTTgemm::DeviceOptions d;
+        d.device_id = device_id;
+        ozTTgemm::Context ctx(d);
+        const ozTTgemm::Info in = ctx.gemm(std::span<const double>(a, a ? a_len : 0),
+                                           std::span<const double>(b, b ? b_len : 0), std::span<double>(c, c ? c_len : 0),
+                                           m, n, k, o);
+        if (info) {
+            info->scheme = (int32_t)in.scheme;
+            info->format = (int32_t)in.format;
+            info->slices = in.slices;
+            info->moduli = in.moduli;
+            info->integer_bits = in.integer_bits;
+            info->reconstruction_passes = in.reconstruction_passes;
+            info->padded_m = in.padded_m;
+            info->padded_n = in.padded_n;
+            info->padded_k = in.padded_k;
+        }
+        put("");
+        return OZTT_OK;
+    } catch (const std::invalid_argument& e) {
+        put(e.what());
+        return OZTT_EINVAL;
+    } catch (const std::bad_alloc&) {
+        put("host memory exhausted");
+        return OZTT_ENOMEM;
+    } catch (const std::exception& e) {
+        put(e.what());
+        return OZTT_ERUNTIME;
+    }
+}

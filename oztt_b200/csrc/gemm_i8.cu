@@ -1,0 +1,424 @@
+// SPDX-License-Identifier: Apache-2.0
+//
+// Per-modulus residue products on the 5th-generation tensor cores (sm_100a):
+//     C_s = A_s * B_s^T,  A_s [mp x kp] int8, B_s [np x kp] int8 (both K-major), s = 0..S-1,
+// exactly, in s32 accumulators in tensor memory, with the modular reduction fused into the epilogue.
+// Replaces the reference's GEMM stage (run_int8_gemms, src/ozaki2.cpp:333-348, one Metalium
+// workload per modulus and output panel; kernels/bmm_int32_spill.cpp) by one persistent launch for
+// all S moduli.
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: 128x128 A and 256x128 B int8 boxes (128-byte swizzle) into a 4-stage
+//               shared-memory ring; completion is counted in bytes on the stage's mbarrier.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma.cta_group::1.kind::i8 (M=128, N=256, K=32;
+//               4 per stage) into one of two 256-column TMEM accumulators and releases each stage
+//               with tcgen05.commit; allocates and frees the 512 TMEM columns.
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator rows (warp w reads lanes 32*(w%4)..+31),
+//               then either the raw int32 C_s (mode 0, for bit-exact checks) or the CRT digit
+//               k_s = (C_s mod m_s) * y_s mod m_s as uint8 (mode 1), stored to HBM; the accumulator
+//               is handed back to the MMA warp while the next tile accumulates in the other one.
+// Tiles are scheduled persistently: tile t -> (modulus s, tile row, tile column) with the rows of
+// each modulus taken in groups of 16 so that the CTAs running at one time share A and B panels in
+// L2. TMA loads never use cluster multicast.
+//
+// Every mbarrier wait is bounded (2 s of global time). On a timeout the CTA records an error code,
+// all roles leave their loops, the producer waits (bounded) for the loads it issued, the MMA thread
+// waits (bounded) for its last commit, and the TMEM is freed before the kernel returns; the host
+// reports the code as a runtime error.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "oztt_common.cuh"
+
+namespace oztt {
+namespace gemm {
+
+constexpr uint32_t BM = 128, BN = 256, BK = 128, UK = 32;
+constexpr uint32_t STAGES = 4;
+constexpr uint32_t A_BYTES = BM * BK;
+constexpr uint32_t B_BYTES = BN * BK;
+constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t ACC_COLS = BN;
+constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+constexpr uint32_t NUM_THREADS = 192;
+constexpr uint32_t GROUP_M = 16;
+constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+constexpr uint64_t TIMEOUT_NS = 2000000000ull;
+
+// Instruction descriptor of kind::i8: s32 accumulator, signed A and B, both K-major, N=256, M=128.
+constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) | ((BM >> 4) << 24);
+
+enum ErrCode : int { ERR_WAIT_PRODUCER = 1, ERR_WAIT_MMA_FULL = 2, ERR_WAIT_MMA_EMPTY = 4, ERR_WAIT_EPILOGUE = 8 };
+
+struct EpiConst {
+    uint32_t S;
+    uint32_t m[OZTT_MAXS], y[OZTT_MAXS], magic[OZTT_MAXS], shift[OZTT_MAXS];
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Waits for the phase of `parity` to complete. Gives up when another role raised the abort flag or
+// after TIMEOUT_NS (then records `code` and raises the flag). Returns true when the phase completed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63) == 0) {
+            if (*abort_flag) return false;
+            if (global_timer_ns() - t0 > TIMEOUT_NS) {
+                atomicOr(err, code);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+// Bounded wait used on the abort path only (ignores the abort flag).
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (global_timer_ns() - t0 > limit_ns) return;
+}
+
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint32_t dst, uint64_t* bar, int32_t c0,
+                                            int32_t c1, int32_t c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+            "r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand in 128-byte-swizzled 8-row atoms (1024 bytes
+// apart), descriptor version 1.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) |
+           ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// floor(a / m) for a < 2^31 with a precomputed (magic, shift) pair (round-up reciprocal method).
+__device__ __forceinline__ uint32_t udiv_small(uint32_t a, uint32_t magic, uint32_t shift) {
+    return (__umulhi(a, magic) + a) >> shift;
+}
+
+__device__ __forceinline__ void decode_tile(uint32_t tile, uint32_t tiles_m, uint32_t tiles_n, uint32_t& s,
+                                            uint32_t& tm, uint32_t& tn) {
+    const uint32_t per_s = tiles_m * tiles_n;
+    s = tile / per_s;
+    const uint32_t r = tile - s * per_s;
+    const uint32_t span = GROUP_M * tiles_n;
+    const uint32_t g = r / span;
+    const uint32_t first = g * GROUP_M;
+    const uint32_t gsz = min(tiles_m - first, GROUP_M);
+    const uint32_t rr = r - g * span;
+    tm = first + rr % gsz;
+    tn = rr / gsz;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    residue_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        void* __restrict__ out, uint32_t tiles_m, uint32_t tiles_n, uint32_t num_kb, uint64_t mp,
+                        uint64_t np, const EpiConst ec, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty_bar = full_bar + STAGES;
+    uint64_t* tfull_bar = empty_bar + STAGES;
+    uint64_t* tempty_bar = tfull_bar + 2;
+    uint64_t* drain_bar = tempty_bar + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t num_tiles = ec.S * tiles_m * tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar + s, 1);
+            mbar_init(empty_bar + s, 1);
+        }
+        for (uint32_t a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar + a, 1);
+            mbar_init(tempty_bar + a, 128);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+            uint32_t stage = 0, phase = 0;
+            uint32_t filled = 0, last_phase = 0;  // per-stage bit masks of the last fill
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                uint32_t s, tm, tn;
+                decode_tile(tile, tiles_m, tiles_n, s, tm, tn);
+                for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(empty_bar + stage, phase ^ 1u, abort_flag, err, ERR_WAIT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(full_bar + stage, STAGE_BYTES);
+                    const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+                    tma_load_3d(&tmA, sa, full_bar + stage, (int32_t)(kb * BK), (int32_t)(tm * BM), (int32_t)s);
+                    tma_load_3d(&tmB, sa + A_BYTES, full_bar + stage, (int32_t)(kb * BK), (int32_t)(tn * BN),
+                                (int32_t)s);
+                    filled |= 1u << stage;
+                    last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok)  // let every load this thread issued land before the CTA may exit
+                for (uint32_t st = 0; st < STAGES; ++st)
+                    if (filled & (1u << st)) mbar_wait_drain(full_bar + st, (last_phase >> st) & 1u, 200000000ull);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                if (!mbar_wait(tempty_bar + acc, acc_phase ^ 1u, abort_flag, err, ERR_WAIT_MMA_EMPTY)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+                for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(full_bar + stage, phase, abort_flag, err, ERR_WAIT_MMA_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES), sb = sa + A_BYTES;
+#pragma unroll
+                    for (uint32_t k = 0; k < BK / UK; ++k)
+                        umma_i8(d_tmem, sdesc_sw128(sa + k * UK), sdesc_sw128(sb + k * UK), (kb | k) != 0u);
+                    umma_commit(empty_bar + stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(tfull_bar + acc);
+                acc ^= 1u;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            // Every MMA this thread issued completes before the columns are freed.
+            umma_commit(drain_bar);
+            mbar_wait_drain(drain_bar, 0, 1000000000ull);
+        }
+    } else {
+        const uint32_t quarter = warp & 3u;
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            uint32_t s, tm, tn;
+            decode_tile(tile, tiles_m, tiles_n, s, tm, tn);
+            if (!mbar_wait(tfull_bar + acc, acc_phase, abort_flag, err, ERR_WAIT_EPILOGUE)) break;
+            tc_fence_after();
+            const uint64_t row = (uint64_t)tm * BM + quarter * 32u + lane;
+            const uint32_t tbase = tmem_base + ((quarter * 32u) << 16) + acc * ACC_COLS;
+            const uint32_t m = ec.m[s], y = ec.y[s], mg = ec.magic[s], sh = ec.shift[s];
+#pragma unroll 1
+            for (uint32_t c = 0; c < BN; c += 32) {
+                uint32_t v[32];
+                tmem_ld32(tbase + c, v);
+                const uint64_t off = ((uint64_t)s * mp + row) * np + (uint64_t)tn * BN + c;
+                if constexpr (MODE == 0) {
+                    uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<int32_t*>(out) + off);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) o[q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                } else {
+                    uint32_t w[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) w[q] = 0;
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const int32_t cv = (int32_t)v[e];
+                        const uint32_t a = cv < 0 ? (uint32_t)(-cv) : (uint32_t)cv;
+                        uint32_t r = a - udiv_small(a, mg, sh) * m;
+                        if (cv < 0 && r) r = m - r;
+                        const uint32_t t = r * y;
+                        const uint32_t kk = t - udiv_small(t, mg, sh) * m;
+                        w[e >> 2] |= kk << (8 * (e & 3));
+                    }
+                    uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out) + off);
+                    o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(tempty_bar + acc);
+            acc ^= 1u;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---- host side -------------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    if (!fn) throw Error(OZTT_ERUNTIME, "cuTensorMapEncodeTiled is not available from the CUDA driver");
+    return fn;
+}
+
+// 3-D map over S planes of rows x kp int8 (K innermost), box BK x box_rows x 1, 128-byte swizzle.
+static CUtensorMap make_plane_map(const int8_t* base, uint64_t rows, uint64_t kp, uint64_t S, uint32_t box_rows) {
+    CUtensorMap map;
+    const cuuint64_t dims[3] = {kp, rows, S};
+    const cuuint64_t strides[2] = {kp, rows * kp};
+    const cuuint32_t box[3] = {BK, box_rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(base), dims, strides,
+                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw Error(OZTT_ERUNTIME, "cuTensorMapEncodeTiled failed for a residue plane map");
+    return map;
+}
+
+// (magic, shift) with floor(a/d) = (umulhi(a, magic) + a) >> shift for all a < 2^31.
+static void udiv_magic(uint32_t d, uint32_t& magic, uint32_t& shift) {
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;
+    magic = (uint32_t)((((1ull << 32) * ((1ull << l) - d)) / d) + 1);
+    shift = l;
+}
+
+}  // namespace gemm
+
+void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
+                         const oztt_ii_plan& p, int mode, void* out, int* err_word, cudaStream_t st) {
+    using namespace gemm;
+    if (mp % BM || np % BN || kp % BK || mp == 0 || np == 0 || kp == 0)
+        throw Error(OZTT_EINVAL, "residue_gemm: mp, np, kp must be positive multiples of 128, 256 and 128");
+    if (p.S < 1 || p.S > OZTT_MAXS) throw Error(OZTT_EINVAL, "residue_gemm: bad number of moduli");
+    if ((reinterpret_cast<uintptr_t>(ap) | reinterpret_cast<uintptr_t>(bp)) & 15)
+        throw Error(OZTT_EINVAL, "residue_gemm: planes must be 16-byte aligned");
+    if (mode != 0 && mode != 1) throw Error(OZTT_EINVAL, "residue_gemm: mode must be 0 or 1");
+    if (mp / BM * (np / BN) * (uint64_t)p.S >= (1ull << 31) || kp / BK >= (1ull << 31))
+        throw Error(OZTT_EINVAL, "residue_gemm: problem too large");
+    EpiConst ec{};
+    ec.S = (uint32_t)p.S;
+    for (int s = 0; s < p.S; ++s) {
+        ec.m[s] = (uint32_t)p.moduli[s];
+        ec.y[s] = (uint32_t)p.yi[s];
+        udiv_magic(ec.m[s], ec.magic[s], ec.shift[s]);
+    }
+    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p.S, BM);
+    const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p.S, BN);
+    int dev = 0, sms = 148;
+    OZTT_CUDA(cudaGetDevice(&dev));
+    OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const uint32_t tiles_m = (uint32_t)(mp / BM), tiles_n = (uint32_t)(np / BN);
+    const uint64_t num_tiles = (uint64_t)p.S * tiles_m * tiles_n;
+    const unsigned grid = (unsigned)std::min<uint64_t>(num_tiles, (uint64_t)sms);
+    if (mode == 0) {
+        OZTT_CUDA(cudaFuncSetAttribute(residue_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)SMEM_BYTES));
+        residue_gemm_kernel<0><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, out, tiles_m, tiles_n,
+                                                                     (uint32_t)(kp / BK), mp, np, ec, err_word);
+    } else {
+        OZTT_CUDA(cudaFuncSetAttribute(residue_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)SMEM_BYTES));
+        residue_gemm_kernel<1><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, out, tiles_m, tiles_n,
+                                                                     (uint32_t)(kp / BK), mp, np, ec, err_word);
+    }
+    OZTT_CUDA(cudaGetLastError());
+}
+
+// Host model of the epilogue's division, for the CPU tests of the C ABI.
+extern "C" uint32_t oztt_test_udiv_small(uint32_t a, uint32_t d) {
+    uint32_t mg, sh;
+    gemm::udiv_magic(d, mg, sh);
+    const uint32_t hi = (uint32_t)(((uint64_t)a * mg) >> 32);
+    return (uint32_t)(hi + a) >> sh;
+}
+
+}  // namespace oztt

@@ -1,0 +1,267 @@
+// SPDX-License-Identifier: Apache-2.0
+//
+// Scheme II INT8 pipeline on one B200 and the C-ABI entry points of its stages.
+//
+// The reference's backend (ozaki2_int8::run, src/ozaki2.cpp:439-478) plans, uploads FP64 tiles,
+// scales, slices, runs one GEMM workload per modulus and output panel, reconstructs in one or two
+// passes and reads back. Here one call is six kernel launches on one CUDA stream:
+//     scale_rows(A) -> scale_cols(B) -> split_rows(A) -> split_cols(B) -> residue_gemm (all S moduli)
+//     -> recon
+// with the intermediate planes in HBM ([S][mp][kp] and [S][np][kp] int8 residues, [S][mp][np] uint8
+// CRT digits) taken from the stream-ordered allocator and released at the end of the call (the pool
+// keeps them for the next call). The range flags of the scaling stage and the wait-timeout word of
+// the GEMM are read back after C, as the reference reads its flags after C (src/ozaki2.cpp:469-472).
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "oztt_common.cuh"
+
+namespace oztt {
+
+void launch_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t shift, int32_t* delta,
+                       uint16_t* bfmax, uint32_t* flags, cudaStream_t st);
+void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
+                       uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax, cudaStream_t st);
+void launch_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st);
+void launch_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st);
+void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
+                         const oztt_ii_plan& p, int mode, void* out, int* err_word, cudaStream_t st);
+void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB,
+                  const oztt_ii_plan& p, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st);
+
+namespace {
+
+// Selects the device, checks that it is a Blackwell data-centre GPU (compute capability 10.x, the
+// sm_100a code in this library) and keeps the stream-ordered pool's memory between calls.
+void open_device(int device_id) {
+    if (device_id < 0) throw Error(OZTT_EINVAL, "device_id must be nonnegative");
+    int count = 0;
+    OZTT_CUDA(cudaGetDeviceCount(&count));
+    if (device_id >= count) throw Error(OZTT_ERUNTIME, "CUDA device " + std::to_string(device_id) + " does not exist");
+    OZTT_CUDA(cudaSetDevice(device_id));
+    int major = 0, minor = 0;
+    OZTT_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device_id));
+    OZTT_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device_id));
+    if (major != 10 || minor != 0)
+        throw Error(OZTT_ERUNTIME, "ozTTgemm for B200 runs on compute capability 10.0 (sm_100a) devices only");
+    static std::mutex mu;
+    static std::vector<int> configured;
+    std::lock_guard<std::mutex> lock(mu);
+    if (std::find(configured.begin(), configured.end(), device_id) == configured.end()) {
+        cudaMemPool_t pool;
+        OZTT_CUDA(cudaDeviceGetDefaultMemPool(&pool, device_id));
+        uint64_t keep = UINT64_MAX;
+        OZTT_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+        configured.push_back(device_id);
+    }
+}
+
+// Stream-ordered device buffer, released on the stream when it goes out of scope.
+struct DevBuf {
+    void* p = nullptr;
+    cudaStream_t st;
+    explicit DevBuf(cudaStream_t s) : st(s) {}
+    DevBuf(cudaStream_t s, size_t bytes) : st(s) { alloc(bytes); }
+    ~DevBuf() {
+        if (p) cudaFreeAsync(p, st);
+    }
+    void alloc(size_t bytes) {
+        const cudaError_t e = cudaMallocAsync(&p, std::max<size_t>(bytes, 256), st);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            p = nullptr;
+            throw Error(OZTT_ERUNTIME, "device memory allocation of " + std::to_string(bytes) +
+                                           " bytes failed: " + cudaGetErrorString(e));
+        }
+    }
+    template <class T>
+    T* as() const {
+        return reinterpret_cast<T*>(p);
+    }
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+};
+
+void check_plan(const oztt_ii_plan& p) {
+    if (p.S < 1 || p.S > OZTT_MAXS) throw Error(OZTT_EINVAL, "plan: the number of moduli must be 1..24");
+    if (p.nd < 3 || p.nd > 5) throw Error(OZTT_EINVAL, "plan: the number of digits must be 3..5");
+    for (int s = 0; s < p.S; ++s)
+        if (p.moduli[s] < 3 || p.moduli[s] > 255) throw Error(OZTT_EINVAL, "plan: INT8 moduli must be in 3..255");
+}
+
+void check_flags(uint32_t flags, int gemm_err) {
+    if (gemm_err)
+        throw Error(OZTT_ERUNTIME, "the residue GEMM kernel gave up waiting (code " + std::to_string(gemm_err) +
+                                       "); the result was not written");
+    if (flags) {
+        std::string why;
+        if (flags & 1u) why += " a row or column maximum above the largest BF16;";
+        if (flags & 2u) why += " a nonzero row or column maximum below 2^-126;";
+        if (flags & 4u) why += " an Inf or NaN element;";
+        throw Error(OZTT_ERUNTIME, "the scaling stage flagged inputs outside the supported range:" + why);
+    }
+}
+
+}  // namespace
+
+// The device pipeline on device buffers (row-major, lda = k, ldb = n, ldc = n).
+void run_ii_int8_device(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                        const oztt_ii_plan& p, cudaStream_t st) {
+    check_plan(p);
+    const uint64_t S = (uint64_t)p.S;
+    const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
+    DevBuf dA(st, mp * 4), dB(st, np * 4), colmax(st, n * 8), words(st, 16);
+    DevBuf ra(st, S * mp * kp), rb(st, S * np * kp), kpl(st, S * mp * np);
+    OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
+    uint32_t* flags = words.as<uint32_t>();
+    int* gemm_err = words.as<int>() + 1;
+    launch_scale_rows(a, m, k, k, p.shift, dA.as<int32_t>(), nullptr, flags, st);
+    launch_scale_cols(b, k, n, n, p.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
+    launch_split_rows(a, m, k, k, dA.as<int32_t>(), p, ra.as<int8_t>(), mp, kp, st);
+    launch_split_cols(b, k, n, n, dB.as<int32_t>(), p, rb.as<int8_t>(), np, kp, st);
+    launch_residue_gemm(ra.as<int8_t>(), rb.as<int8_t>(), mp, np, kp, p, 1, kpl.p, gemm_err, st);
+    launch_recon(kpl.as<uint8_t>(), mp, np, dA.as<int32_t>(), dB.as<int32_t>(), p, c, m, n, n, st);
+    uint32_t host_words[2] = {0, 0};
+    OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
+    OZTT_CUDA(cudaStreamSynchronize(st));
+    check_flags(host_words[0], (int)host_words[1]);
+}
+
+void run_ii_int8_host(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                      const oztt_ii_plan& p) {
+    open_device(device_id);
+    cudaStream_t st;
+    OZTT_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    struct StreamGuard {
+        cudaStream_t s;
+        ~StreamGuard() {
+            cudaStreamSynchronize(s);
+            cudaStreamDestroy(s);
+        }
+    } guard{st};
+    {
+        DevBuf da(st, m * k * 8), db(st, k * n * 8), dc(st, m * n * 8);
+        OZTT_CUDA(cudaMemcpyAsync(da.p, a, m * k * 8, cudaMemcpyHostToDevice, st));
+        OZTT_CUDA(cudaMemcpyAsync(db.p, b, k * n * 8, cudaMemcpyHostToDevice, st));
+        run_ii_int8_device(da.as<double>(), db.as<double>(), dc.as<double>(), m, n, k, p, st);
+        OZTT_CUDA(cudaMemcpyAsync(c, dc.p, m * n * 8, cudaMemcpyDeviceToHost, st));
+        OZTT_CUDA(cudaStreamSynchronize(st));
+    }
+}
+
+void open_device_checked(int device_id) { open_device(device_id); }
+
+}  // namespace oztt
+
+using oztt::Error;
+using oztt::guarded;
+
+extern "C" {
+
+int oztt_ii_int8_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                     const oztt_ii_plan* plan, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a || !b || !c || !plan) throw Error(OZTT_EINVAL, "null argument");
+        if (!m || !n || !k) throw Error(OZTT_EINVAL, "matrix dimensions are zero");
+        oztt::run_ii_int8_host(device_id, a, b, c, m, n, k, *plan);
+    });
+}
+
+int oztt_ii_int8_run_device(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                            uint64_t k, const oztt_ii_plan* plan, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a || !b || !c || !plan) throw Error(OZTT_EINVAL, "null argument");
+        if (!m || !n || !k) throw Error(OZTT_EINVAL, "matrix dimensions are zero");
+        oztt::open_device(device_id);
+        oztt::run_ii_int8_device(a, b, c, m, n, k, *plan, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+void oztt_ii_padded_dims(uint64_t m, uint64_t n, uint64_t k, uint64_t* mp, uint64_t* np, uint64_t* kp) {
+    if (mp) *mp = oztt::round_up(m, 128);
+    if (np) *np = oztt::round_up(n, 256);
+    if (kp) *kp = oztt::round_up(k, 128);
+}
+
+int oztt_ii_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t shift, int32_t* delta,
+                       uint16_t* bf16max, uint32_t* flags, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a || !delta || !flags || lda < k) throw Error(OZTT_EINVAL, "scale_rows: bad arguments");
+        oztt::launch_scale_rows(a, m, k, lda, shift, delta, bf16max, flags, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+int oztt_ii_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
+                       uint16_t* bf16max, uint32_t* flags, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!b || !delta || !flags || ldb < n) throw Error(OZTT_EINVAL, "scale_cols: bad arguments");
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        oztt::DevBuf colmax(st, n * 8);
+        oztt::launch_scale_cols(b, k, n, ldb, shift, delta, bf16max, flags, colmax.as<unsigned long long>(), st);
+    });
+}
+
+int oztt_ii_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
+                       const oztt_ii_plan* plan, int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err,
+                       size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a || !delta || !plan || !planes || lda < k || mp < m || kp < k)
+            throw Error(OZTT_EINVAL, "split_rows: bad arguments");
+        oztt::check_plan(*plan);
+        oztt::launch_split_rows(a, m, k, lda, delta, *plan, planes, mp, kp, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+int oztt_ii_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
+                       const oztt_ii_plan* plan, int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err,
+                       size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!b || !delta || !plan || !planes || ldb < n || np < n || kp < k)
+            throw Error(OZTT_EINVAL, "split_cols: bad arguments");
+        oztt::check_plan(*plan);
+        oztt::launch_split_cols(b, k, n, ldb, delta, *plan, planes, np, kp, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+int oztt_ii_residue_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp, uint64_t np, uint64_t kp,
+                         const oztt_ii_plan* plan, int32_t mode, void* out, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a_planes || !b_planes || !plan || !out) throw Error(OZTT_EINVAL, "residue_gemm: null argument");
+        oztt::check_plan(*plan);
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        oztt::DevBuf word(st, 16);
+        OZTT_CUDA(cudaMemsetAsync(word.p, 0, 16, st));
+        oztt::launch_residue_gemm(a_planes, b_planes, mp, np, kp, *plan, mode, out, word.as<int>(), st);
+        int host_err = 0;
+        OZTT_CUDA(cudaMemcpyAsync(&host_err, word.p, 4, cudaMemcpyDeviceToHost, st));
+        OZTT_CUDA(cudaStreamSynchronize(st));
+        oztt::check_flags(0, host_err);
+    });
+}
+
+int oztt_ii_recon(const uint8_t* k_planes, uint64_t mp, uint64_t np, const int32_t* delta_a, const int32_t* delta_b,
+                  const oztt_ii_plan* plan, double* c, uint64_t m, uint64_t n, uint64_t ldc, void* stream, char* err,
+                  size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!k_planes || !delta_a || !delta_b || !plan || !c || ldc < n) throw Error(OZTT_EINVAL, "recon: bad arguments");
+        oztt::check_plan(*plan);
+        oztt::launch_recon(k_planes, mp, np, delta_a, delta_b, *plan, c, m, n, ldc,
+                           reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+int oztt_device_info(int device_id, int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device_id) != cudaSuccess) return OZTT_ERUNTIME;
+    if (sm_count) *sm_count = v;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrComputeCapabilityMajor, device_id) != cudaSuccess) return OZTT_ERUNTIME;
+    if (cc_major) *cc_major = v;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrComputeCapabilityMinor, device_id) != cudaSuccess) return OZTT_ERUNTIME;
+    if (cc_minor) *cc_minor = v;
+    return OZTT_OK;
+}
+
+}  // extern "C"

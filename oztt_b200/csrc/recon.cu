@@ -1,0 +1,198 @@
+// SPDX-License-Identifier: Apache-2.0
+//
+// Scheme II reconstruction on sm_100a: exact Chinese-remainder reconstruction of C' from the CRT
+// digits k_s written by the GEMM epilogue, one rounding to FP64, exact power-of-two scale.
+//
+// Reference counterpart: recon_crt.cpp:219-338 with recon_crt_proc.h and the assembly of
+// recon_elem.h / f64_tf.h:296-400. The reference evaluates frac = sum_s k_s/m_s mod 1 in FP32
+// triple-float because its device has no FP64 (absolute error about 2^-67 for one pass), folds it in
+// 128-bit fixed point and multiplies by M*2^-2b. Here the same quantity is computed without error:
+//     X  = sum_s k_s * (M/m_s)                  (multiword integer, NW 32-bit words, mod 2^(32 NW))
+//     q  = rint(sum_s k_s * (1/m_s))            (FP64; the window margin |C'|/M <= 1/2 - 2^-31.4
+//                                                makes q = round(X/M) exact)
+//     C' = X - q*M                              (|C'| < M/2, two's complement in NW words)
+//     C  = C' * 2^(2 shift - dA_i - dB_j - 2b)  (one round-to-nearest-even; below 2^-1022 -> +-0,
+//                                                as pack_f64 of the reference flushes)
+// One pass and two passes of the reference therefore give the same B200 result, which is at least as
+// accurate as either; the tests bound |C - C_reference| componentwise.
+//
+// HBM traffic per output element: S bytes of digits in, 8 bytes out, plus the two deltas.
+#include <algorithm>
+
+#include "oztt_common.cuh"
+
+namespace oztt {
+
+struct ReconConst {
+    uint32_t S;
+    int32_t two_b, sh2;
+    uint32_t M[8];
+    uint32_t Q[OZTT_MAXS][8];
+    double invm[OZTT_MAXS];
+};
+
+// Finishes one element from its column sums acc (X = sum_w acc[w] 2^(32w)) and fr ~ X/M.
+template <int NW>
+__device__ __forceinline__ double crt_finish(const uint64_t (&acc)[NW], double fr, int32_t g, const ReconConst& rc) {
+    const uint32_t q = (uint32_t)rint(fr);
+    // y = X - q*M modulo 2^(32 NW), carrying the sum of the columns and the subtraction together.
+    uint32_t y[NW];
+    uint64_t cx = 0;
+    int64_t br = 0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        const uint64_t sx = acc[w] + cx;
+        cx = sx >> 32;
+        const int64_t d = (int64_t)(uint32_t)sx - (int64_t)((uint64_t)q * rc.M[w]) + br;
+        y[w] = (uint32_t)d;
+        br = d >> 32;
+    }
+    const bool neg = (y[NW - 1] >> 31) != 0;
+    if (neg) {
+        uint32_t c = 1;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const uint64_t t = (uint64_t)(~y[w]) + c;
+            y[w] = (uint32_t)t;
+            c = (uint32_t)(t >> 32);
+        }
+    }
+    int hw = -1;
+#pragma unroll
+    for (int w = 0; w < NW; ++w)
+        if (y[w]) hw = w;
+    if (hw < 0) return 0.0;
+    uint32_t w0 = 0, w1 = 0, w2 = 0;
+    bool sticky = false;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        if (w == hw) w0 = y[w];
+        if (w == hw - 1) w1 = y[w];
+        if (w == hw - 2) w2 = y[w];
+        if (w < hw - 2 && y[w]) sticky = true;
+    }
+    const int lz = __clz(w0);
+    const uint64_t top = ((uint64_t)w0 << 32) | w1;
+    const uint64_t top64 = lz ? ((top << lz) | (w2 >> (32 - lz))) : top;
+    const uint32_t rem = lz ? (w2 << lz) : w2;
+    sticky = sticky || rem != 0u;
+    const double v = __ull2double_rn(top64 | (sticky ? 1ull : 0ull));  // in [2^63, 2^64]
+    const int p = 32 * hw + 31 - lz;                                    // position of the leading bit
+    const int lead = p + g - rc.two_b + (v == 18446744073709551616.0 ? 1 : 0);
+    double r;
+    if (lead < -1022)
+        r = 0.0;
+    else if (lead > 1023)
+        r = __longlong_as_double(0x7FF0000000000000ll);
+    else
+        r = ldexp(v, p - 63 + g - rc.two_b);
+    return neg ? -r : r;
+}
+
+// One thread = 4 consecutive columns of one row: S 32-bit loads (one per digit plane), 32 bytes out.
+template <int NW>
+__global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ kp, uint64_t mp, uint64_t np,
+                                                    const int32_t* __restrict__ dA, const int32_t* __restrict__ dB,
+                                                    double* __restrict__ c, uint64_t m, uint64_t n, uint64_t ldc,
+                                                    const ReconConst rc) {
+    const uint64_t nq = (n + 3) >> 2, total = m * nq, plane = mp * np;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t i = t / nq, j0 = (t - i * nq) << 2;
+        const uint8_t* base = kp + i * np + j0;
+        uint64_t acc[4][NW];
+        double fr[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            fr[e] = 0.0;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) acc[e][w] = 0;
+        }
+        for (uint32_t s = 0; s < rc.S; ++s) {
+            const uint32_t kw = __ldg(reinterpret_cast<const uint32_t*>(base + s * plane));
+            const double im = rc.invm[s];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t k = (kw >> (8 * e)) & 0xFFu;
+#pragma unroll
+                for (int w = 0; w < NW; ++w) acc[e][w] += (uint64_t)k * rc.Q[s][w];
+                fr[e] = fma((double)k, im, fr[e]);
+            }
+        }
+        const int32_t da = __ldg(dA + i);
+        double* crow = c + i * ldc + j0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if (j0 + e < n) {
+                const int32_t g = rc.sh2 - (da + __ldg(dB + j0 + e));
+                crow[e] = crt_finish<NW>(acc[e], fr[e], g, rc);
+            }
+        }
+    }
+}
+
+// ---- host side -------------------------------------------------------------------------------
+namespace {
+struct Big {
+    uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+};
+Big big_mul(const Big& a, uint32_t k) {
+    Big r;
+    uint64_t c = 0;
+    for (int i = 0; i < 8; ++i) {
+        c += (uint64_t)a.w[i] * k;
+        r.w[i] = (uint32_t)c;
+        c >>= 32;
+    }
+    if (c) throw Error(OZTT_EINVAL, "recon: the product of the moduli exceeds 256 bits");
+    return r;
+}
+int big_bits(const Big& a) {
+    for (int i = 7; i >= 0; --i)
+        if (a.w[i]) return 32 * i + 32 - __builtin_clz(a.w[i]);
+    return 0;
+}
+}  // namespace
+
+void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB,
+                  const oztt_ii_plan& p, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st) {
+    if (p.S < 1 || p.S > OZTT_MAXS) throw Error(OZTT_EINVAL, "recon: bad number of moduli");
+    if (np % 4 || (reinterpret_cast<uintptr_t>(kp) & 3)) throw Error(OZTT_EINVAL, "recon: np must be a multiple of 4");
+    if (m > mp || n > np) throw Error(OZTT_EINVAL, "recon: output larger than the digit planes");
+    ReconConst rc{};
+    rc.S = (uint32_t)p.S;
+    rc.two_b = 2 * p.b;
+    rc.sh2 = 2 * p.shift;
+    Big M;
+    M.w[0] = 1;
+    for (int s = 0; s < p.S; ++s) M = big_mul(M, (uint32_t)p.moduli[s]);
+    for (int w = 0; w < 8; ++w) rc.M[w] = M.w[w];
+    for (int s = 0; s < p.S; ++s) {
+        Big q;
+        q.w[0] = 1;
+        for (int t = 0; t < p.S; ++t)
+            if (t != s) q = big_mul(q, (uint32_t)p.moduli[t]);
+        for (int w = 0; w < 8; ++w) rc.Q[s][w] = q.w[w];
+        rc.invm[s] = 1.0 / (double)p.moduli[s];
+    }
+    const int nw = std::max(1, (big_bits(M) + 31) / 32);
+    const uint64_t total = m * ((n + 3) / 4);
+    if (total == 0) return;
+    int dev = 0, sms = 148;
+    OZTT_CUDA(cudaGetDevice(&dev));
+    OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sms * 16);
+    switch (nw) {
+    case 1:
+    case 2:
+    case 3:
+    case 4: recon_kernel<4><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+    case 5: recon_kernel<5><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+    case 6: recon_kernel<6><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+    case 7: recon_kernel<7><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+    default: recon_kernel<8><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+    }
+    OZTT_CUDA(cudaGetLastError());
+}
+
+}  // namespace oztt

@@ -1,0 +1,394 @@
+// SPDX-License-Identifier: Apache-2.0
+//
+// Scheme II scaling and slicing on sm_100a (HBM-bound stages of the INT8 pipeline).
+//
+//   scale_rows / scale_cols   max |x| per row of A / column of B on the 63-bit FP64 patterns, BF16
+//                             rounded up, e = ceil(log2), delta = shift - e, range flags
+//                             (reference: scale_f64_reader.cpp:129-198, scale_bits.h:33-63,
+//                             expdelta.cpp:44-91)
+//   split_rows / split_cols   the S residues of every element in one pass over the FP64 operand
+//                             (reference: slice_f64_reader.cpp with split_f64, f64_tf.h:141-168;
+//                             tf_load_f64, slice_tf_core.h:67-75; oz2_make_digits and oz2_residue,
+//                             ozaki2/kernels/digits.h:80-179; modslice_int8.cpp)
+//
+// The residues must be bit-identical to the reference's. Its integer A' is not the rounded value of
+// x*2^(b-e): only the top limb of a triple-float is rounded (|A' - X| <= 1), and for an even modulus
+// the sign of a residue of m/2 depends on the binary32 rounding inside ModRound. The digit kernel
+// therefore executes the reference's binary32 operation sequence one PTX instruction at a time with
+// round-to-nearest-even and flush-to-zero (oztt_common.cuh). Values differ from the reference's model
+// at most in the sign of a zero, which no later step can turn into a different number.
+//
+// Layout in HBM: A is read row-major (m x k, lda) and written as S planes [S][mp][kp] int8 (K
+// contiguous). B is read row-major (k x n, ldb) and written transposed, [S][np][kp] int8, so that
+// both GEMM operands are K-major for the tensor cores. Padding rows/columns are written as zeros.
+#include <algorithm>
+
+#include "oztt_common.cuh"
+
+namespace oztt {
+
+struct SplitConst {
+    int32_t S;
+    float m[OZTT_MAXS], rinv[OZTT_MAXS];
+    float c[4][OZTT_MAXS];
+};
+
+// ---- scaling -------------------------------------------------------------------------------
+// |x| pattern (sign cleared) -> BF16 rounded up; out-of-range markers 0xFFC0 (Inf/NaN), 0xFF80
+// (nonzero below 2^-126), 0x7F80 (above BF16).
+__device__ __forceinline__ uint32_t bf16_round_up(uint64_t mag) {
+    const uint32_t h = (uint32_t)(mag >> 32), l = (uint32_t)mag;
+    const int32_t E = (int32_t)((h >> 20) & 0x7FFu);
+    if (E == 0x7FF) return 0xFFC0u;
+    const int32_t e8 = E - 896;
+    if (e8 <= 0) return (h | l) ? 0xFF80u : 0u;
+    if (e8 >= 255) return 0x7F80u;
+    uint32_t v = ((uint32_t)e8 << 7) | ((h >> 13) & 0x7Fu);
+    if ((h & 0x1FFFu) || l) v += 1u;
+    return v;
+}
+// e = ceil(log2 u); flags for the markers.
+__device__ __forceinline__ int32_t bf16_ceil_log2(uint32_t u, uint32_t& flags) {
+    const uint32_t E = (u >> 7) & 0xFFu, mant = u & 0x7Fu;
+    if (E == 0u) return 0;
+    if (E == 0xFFu) {
+        flags |= !(u & 0x8000u) ? 1u : (mant ? 4u : 2u);
+        return 0;
+    }
+    return (int32_t)E - 127 + (mant ? 1 : 0);
+}
+
+__device__ __forceinline__ void finish_scale(uint64_t mx, int32_t shift, int32_t* delta, uint16_t* bfmax,
+                                             uint32_t* flags, uint64_t idx) {
+    const uint32_t u = bf16_round_up(mx);
+    uint32_t fl = 0;
+    const int32_t e = bf16_ceil_log2(u, fl);
+    delta[idx] = shift - e;
+    if (bfmax) bfmax[idx] = (uint16_t)u;
+    if (fl) atomicOr(flags, fl);
+}
+
+__device__ __forceinline__ uint64_t mx64(uint64_t a, uint64_t b) { return a > b ? a : b; }
+
+// One warp per row; 16-byte loads when the row is 16-byte aligned.
+__global__ void __launch_bounds__(256) scale_rows_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
+                                                         uint64_t lda, int32_t shift, int32_t* __restrict__ delta,
+                                                         uint16_t* __restrict__ bfmax, uint32_t* flags) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x >> 5);
+    constexpr uint64_t MASK = 0x7FFFFFFFFFFFFFFFull;
+    for (uint64_t row = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < m; row += nwarps) {
+        const double* p = a + row * lda;
+        uint64_t mx = 0;
+        uint64_t j0 = 0;
+        if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+            const ulonglong2* p2 = reinterpret_cast<const ulonglong2*>(p);
+            const uint64_t n2 = k >> 1;
+            uint64_t j = lane;
+            for (; j + 96 < n2; j += 128) {
+                const ulonglong2 v0 = __ldg(p2 + j), v1 = __ldg(p2 + j + 32), v2 = __ldg(p2 + j + 64),
+                                 v3 = __ldg(p2 + j + 96);
+                mx = mx64(mx, mx64(mx64(v0.x & MASK, v0.y & MASK), mx64(v1.x & MASK, v1.y & MASK)));
+                mx = mx64(mx, mx64(mx64(v2.x & MASK, v2.y & MASK), mx64(v3.x & MASK, v3.y & MASK)));
+            }
+            for (; j < n2; j += 32) {
+                const ulonglong2 v = __ldg(p2 + j);
+                mx = mx64(mx, mx64(v.x & MASK, v.y & MASK));
+            }
+            j0 = n2 << 1;
+        }
+        const unsigned long long* pu = reinterpret_cast<const unsigned long long*>(p);
+        for (uint64_t j = j0 + lane; j < k; j += 32) mx = mx64(mx, (uint64_t)__ldg(pu + j) & MASK);
+        for (int o = 16; o; o >>= 1) mx = mx64(mx, (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)mx, o));
+        if (lane == 0) finish_scale(mx, shift, delta, bfmax, flags, row);
+    }
+}
+
+// Column maxima: each thread reduces one column over a chunk of rows, then atomicMax into colmax
+// (non-negative FP64 patterns order like unsigned integers).
+__global__ void __launch_bounds__(256) col_max_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
+                                                      uint64_t ldb, uint64_t rows_per_chunk,
+                                                      unsigned long long* __restrict__ colmax) {
+    const uint64_t col = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (col >= n) return;
+    const uint64_t r0 = (uint64_t)blockIdx.y * rows_per_chunk, r1 = min(k, r0 + rows_per_chunk);
+    const unsigned long long* pu = reinterpret_cast<const unsigned long long*>(b);
+    uint64_t mx = 0;
+    uint64_t r = r0;
+    for (; r + 4 <= r1; r += 4) {
+        const uint64_t v0 = __ldg(pu + r * ldb + col), v1 = __ldg(pu + (r + 1) * ldb + col),
+                       v2 = __ldg(pu + (r + 2) * ldb + col), v3 = __ldg(pu + (r + 3) * ldb + col);
+        constexpr uint64_t MASK = 0x7FFFFFFFFFFFFFFFull;
+        mx = mx64(mx, mx64(mx64(v0 & MASK, v1 & MASK), mx64(v2 & MASK, v3 & MASK)));
+    }
+    for (; r < r1; ++r) mx = mx64(mx, (uint64_t)__ldg(pu + r * ldb + col) & 0x7FFFFFFFFFFFFFFFull);
+    if (mx) atomicMax(colmax + col, (unsigned long long)mx);
+}
+
+__global__ void col_finish_kernel(const unsigned long long* __restrict__ colmax, uint64_t n, int32_t shift,
+                                  int32_t* __restrict__ delta, uint16_t* __restrict__ bfmax, uint32_t* flags) {
+    const uint64_t col = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (col < n) finish_scale(colmax[col], shift, delta, bfmax, flags, col);
+}
+
+// ---- digits and residues -------------------------------------------------------------------
+// FP64 -> triple-float (x0, x1, x2) of x*2^d, integer bit split then binary32 assembly.
+__device__ __forceinline__ void tf_load(double xv, int32_t d, float& x0, float& x1, float& x2) {
+    const uint64_t bits = (uint64_t)__double_as_longlong(xv);
+    const uint32_t w1 = (uint32_t)(bits >> 32), w0 = (uint32_t)bits;
+    const uint32_t sgn = w1 & 0x80000000u;
+    const int32_t E = (int32_t)((w1 >> 20) & 0x7FFu);
+    uint32_t hi, braw, craw, s;
+    if (E == 0) {
+        hi = 0u;
+        braw = craw = 0x4B000000u;
+        s = 0u;
+    } else {
+        // 53-bit significand split into 30 (rounded to nearest, ties up) / 23 / 7 bits.
+        uint32_t top = 0x400000u | ((w1 & 0xFFFFFu) << 2) | (w0 >> 30);
+        const uint32_t low30 = w0 & 0x3FFFFFFFu;
+        int32_t rest = (int32_t)low30;
+        if (low30 >= 0x20000000u) {
+            top += 1u;
+            rest = (int32_t)low30 - 0x40000000;
+        }
+        const int32_t mid = rest >> 7;
+        const uint32_t lo = (uint32_t)rest & 0x7Fu;
+        const int32_t elsb = E - 1075 + d;
+        const bool carry = top == 0x800000u;
+        const int32_t eh = elsb + (carry ? 180 : 179);
+        const uint32_t mh = carry ? 0u : ((top << 1) & 0x7FFFFFu);
+        const int32_t es = elsb + 134;
+        hi = (eh > 0 && eh < 255) ? (sgn | ((uint32_t)eh << 23) | mh) : 0u;
+        s = (es > 0 && es < 255) ? (sgn | ((uint32_t)es << 23)) : 0u;
+        braw = 0x4B000000u | ((uint32_t)(mid + 0x400000) & 0x7FFFFFu);
+        craw = 0x4B000000u | lo;
+    }
+    const float sc = __uint_as_float(s);
+    x0 = __uint_as_float(hi);
+    x1 = f32_mul(f32_add(__uint_as_float(braw), -12582912.0f), sc);
+    x2 = f32_mul(f32_mul(f32_add(__uint_as_float(craw), -8388608.0f), sc), 0.0078125f);
+}
+
+// TwoSum (Knuth) in the reference's operation order.
+__device__ __forceinline__ void two_sum(float x, float y, float& s, float& e) {
+    s = f32_add(x, y);
+    const float bb = f32_sub(s, x);
+    const float a = f32_sub(x, f32_sub(s, bb));
+    e = f32_add(a, f32_sub(y, bb));
+}
+
+// The ND radix-2^20 digits, top digit first: round the top limb, subtract, multiply the triple by
+// 2^20 and renormalise (TwoSum, TwoSum, FastTwoSum).
+template <int ND>
+__device__ __forceinline__ void make_digits(double xv, int32_t d, float* dg) {
+    float x0, x1, x2;
+    tf_load(xv, d, x0, x1, x2);
+#pragma unroll
+    for (int i = 0; i < ND; ++i) {
+        if (i > 0) {
+            x0 = f32_mul(x0, 1048576.0f);
+            x1 = f32_mul(x1, 1048576.0f);
+            x2 = f32_mul(x2, 1048576.0f);
+            float s3, e4, s5, e6;
+            two_sum(x1, x2, s3, e4);
+            two_sum(x0, s3, s5, e6);
+            x0 = s5;
+            x1 = f32_add(e6, e4);
+            x2 = f32_sub(e4, f32_sub(x1, e6));
+        }
+        const float dig = f32_rint(x0);
+        dg[i] = dig;
+        x0 = f32_sub(x0, dig);
+    }
+}
+
+// ModRound d - rint(d*rinv)*m. For the INT8 moduli every input is an integer below 2^22, so
+// rint(d*rinv)*m is an exact integer and the fused form equals the reference's separate
+// multiply and subtract.
+__device__ __forceinline__ float mod_round(float d, float m, float rinv) {
+    return f32_fma(-f32_rint(f32_mul(d, rinv)), m, d);
+}
+
+// Residue of A' from its digits (top first), the reference's chain; products of a reduced digit
+// and a weight, and the partial sums, are exact integers below 2^22 (fused multiply-add = the
+// separate operations).
+template <int ND>
+__device__ __forceinline__ float residue(const float* dg, float m, float ri, float c0, float c1, float c2,
+                                         float c3) {
+    float acc = f32_fma(mod_round(dg[ND - 2], m, ri), c0, dg[ND - 1]);
+    acc = f32_fma(mod_round(dg[ND - 3], m, ri), c1, acc);
+    if constexpr (ND >= 4) {
+        acc = mod_round(acc, m, ri);
+        if constexpr (ND >= 5) {
+            acc = f32_fma(mod_round(dg[0], m, ri), c3, acc);
+            acc = mod_round(acc, m, ri);
+        }
+        acc = f32_fma(mod_round(dg[ND - 4], m, ri), c2, acc);
+    }
+    return mod_round(acc, m, ri);
+}
+
+__device__ __forceinline__ uint32_t pack4(float r0, float r1, float r2, float r3) {
+    const uint32_t b0 = (uint32_t)__float2int_rn(r0) & 0xFFu, b1 = (uint32_t)__float2int_rn(r1) & 0xFFu,
+                   b2 = (uint32_t)__float2int_rn(r2) & 0xFFu, b3 = (uint32_t)__float2int_rn(r3) & 0xFFu;
+    return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+}
+
+// Writes the S residue planes of 16 elements whose digits are in dg (16 x ND) to dst + s*plane.
+template <int ND>
+__device__ __forceinline__ void store_residues(const float (&dg)[16][ND], const SplitConst& sc, int8_t* dst,
+                                               uint64_t plane) {
+    for (int s = 0; s < sc.S; ++s) {
+        const float m = sc.m[s], ri = sc.rinv[s];
+        const float c0 = sc.c[0][s], c1 = sc.c[1][s], c2 = sc.c[2][s], c3 = sc.c[3][s];
+        float r[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) r[e] = residue<ND>(dg[e], m, ri, c0, c1, c2, c3);
+        uint4 v;
+        v.x = pack4(r[0], r[1], r[2], r[3]);
+        v.y = pack4(r[4], r[5], r[6], r[7]);
+        v.z = pack4(r[8], r[9], r[10], r[11]);
+        v.w = pack4(r[12], r[13], r[14], r[15]);
+        *reinterpret_cast<uint4*>(dst + (uint64_t)s * plane) = v;
+    }
+}
+
+// A: one thread = 16 consecutive elements of one row.
+template <int ND>
+__global__ void __launch_bounds__(256) split_rows_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
+                                                         uint64_t lda, const int32_t* __restrict__ delta,
+                                                         int8_t* __restrict__ planes, uint64_t mp, uint64_t kp,
+                                                         const SplitConst sc) {
+    const uint64_t chunks = kp >> 4, total = mp * chunks, plane = mp * kp;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t row = t / chunks, k0 = (t - row * chunks) << 4;
+        double x[16];
+        const bool in_row = row < m;
+        const double* p = a + row * lda + k0;
+        if (in_row && k0 + 16 <= k && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+                const double2 v = __ldg(reinterpret_cast<const double2*>(p + e));
+                x[e] = v.x;
+                x[e + 1] = v.y;
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) x[e] = (in_row && k0 + e < k) ? __ldg(p + e) : 0.0;
+        }
+        const int32_t d = in_row ? __ldg(delta + row) : 0;
+        float dg[16][ND];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) make_digits<ND>(x[e], d, dg[e]);
+        store_residues<ND>(dg, sc, planes + row * kp + k0, plane);
+    }
+}
+
+// B: a warp covers 16 columns x 32 rows of B; lane l takes column (l & 15) and the 16 rows of half
+// (l >> 4), so lanes l and l+16 write the two halves of one 32-byte sector of the transposed plane.
+template <int ND>
+__global__ void __launch_bounds__(256) split_cols_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
+                                                         uint64_t ldb, const int32_t* __restrict__ delta,
+                                                         int8_t* __restrict__ planes, uint64_t np, uint64_t kp,
+                                                         const SplitConst sc) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t col_groups = np >> 4, row_groups = kp >> 5, total = col_groups * row_groups;
+    const uint64_t plane = np * kp;
+    for (uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total;
+         w += ((uint64_t)gridDim.x * blockDim.x) >> 5) {
+        const uint64_t cg = w % col_groups, rg = w / col_groups;
+        const uint64_t col = (cg << 4) + (lane & 15), r0 = (rg << 5) + ((lane >> 4) << 4);
+        const bool in_col = col < n;
+        double x[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) x[e] = (in_col && r0 + e < k) ? __ldg(b + (r0 + e) * ldb + col) : 0.0;
+        const int32_t d = in_col ? __ldg(delta + col) : 0;
+        float dg[16][ND];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) make_digits<ND>(x[e], d, dg[e]);
+        store_residues<ND>(dg, sc, planes + col * kp + r0, plane);
+    }
+}
+
+// ---- host side -------------------------------------------------------------------------------
+static int device_sms() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+static SplitConst split_const(const oztt_ii_plan& p) {
+    SplitConst sc{};
+    sc.S = p.S;
+    for (int s = 0; s < p.S; ++s) {
+        sc.m[s] = (float)p.moduli[s];
+        sc.rinv[s] = p.rinv[s];
+        for (int j = 0; j < 4; ++j) sc.c[j][s] = p.c[j][s];
+    }
+    return sc;
+}
+
+void launch_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t shift, int32_t* delta,
+                       uint16_t* bfmax, uint32_t* flags, cudaStream_t st) {
+    if (m == 0) return;
+    const uint64_t warps_needed = m;
+    const uint64_t blocks = std::min<uint64_t>((warps_needed + 7) / 8, (uint64_t)device_sms() * 16);
+    scale_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(a, m, k, lda, shift, delta, bfmax, flags);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
+                       uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax, cudaStream_t st) {
+    if (n == 0) return;
+    OZTT_CUDA(cudaMemsetAsync(colmax, 0, n * sizeof(unsigned long long), st));
+    const uint64_t colblocks = (n + 255) / 256;
+    // Enough row chunks to give every SM several blocks.
+    const uint64_t want = std::max<uint64_t>(1, ((uint64_t)device_sms() * 8 + colblocks - 1) / colblocks);
+    const uint64_t chunks = std::min<uint64_t>(std::min<uint64_t>(want, 65535), std::max<uint64_t>(1, k));
+    const uint64_t rows_per_chunk = (k + chunks - 1) / chunks;
+    const uint64_t nchunks = (k + rows_per_chunk - 1) / rows_per_chunk;
+    if (k > 0) {
+        col_max_kernel<<<dim3((unsigned)colblocks, (unsigned)nchunks), 256, 0, st>>>(b, k, n, ldb, rows_per_chunk,
+                                                                                   colmax);
+        OZTT_CUDA(cudaGetLastError());
+    }
+    col_finish_kernel<<<(unsigned)colblocks, 256, 0, st>>>(colmax, n, shift, delta, bfmax, flags);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void launch_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
+    if (mp % 16 || kp % 16) throw Error(OZTT_EINVAL, "split_rows: padded dimensions must be multiples of 16");
+    const SplitConst sc = split_const(p);
+    const uint64_t total = mp * (kp / 16);
+    const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)device_sms() * 32);
+    if (total == 0) return;
+    switch (p.nd) {
+    case 3: split_rows_kernel<3><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
+    case 4: split_rows_kernel<4><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
+    case 5: split_rows_kernel<5><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
+    default: throw Error(OZTT_EINVAL, "split: the number of digits must be 3, 4 or 5");
+    }
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void launch_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
+    if (np % 16 || kp % 32) throw Error(OZTT_EINVAL, "split_cols: np must be a multiple of 16 and kp of 32");
+    const SplitConst sc = split_const(p);
+    const uint64_t warps = (np / 16) * (kp / 32);
+    if (warps == 0) return;
+    const unsigned blocks = (unsigned)std::min<uint64_t>((warps + 7) / 8, (uint64_t)device_sms() * 32);
+    switch (p.nd) {
+    case 3: split_cols_kernel<3><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
+    case 4: split_cols_kernel<4><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
+    case 5: split_cols_kernel<5><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
+    default: throw Error(OZTT_EINVAL, "split: the number of digits must be 3, 4 or 5");
+    }
+    OZTT_CUDA(cudaGetLastError());
+}
+
+}  // namespace oztt

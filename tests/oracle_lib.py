@@ -1,0 +1,215 @@
+"""ctypes bindings of the CPU checkers (test infrastructure only).
+
+* ``Oracle``  — oracle/liboz2oracle.so, this project's CPU restatement of the reference's Scheme II
+  INT8 path (oracle/oz2_oracle.h documents every function and the reference source it follows).
+* ``RefPlan`` / ``RefEmu`` — oracle/_ref/*.so, the reference's own host code compiled in place
+  (oracle/Makefile, target ``ref``); present only where they were built.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent.parent
+ORACLE_SO = ROOT / "oracle" / "liboz2oracle.so"
+REF_PLAN_SO = ROOT / "oracle" / "_ref" / "libozref_plan.so"
+REF_EMU_SO = ROOT / "oracle" / "_ref" / "libozref_emu.so"
+
+MAXS, MAXRP = 24, 5
+P = ctypes.c_void_p
+
+
+class OzoPlan(ctypes.Structure):
+    _fields_ = [
+        ("ok", ctypes.c_int32), ("acc_ok", ctypes.c_int32), ("S", ctypes.c_int32), ("b", ctypes.c_int32),
+        ("nd", ctypes.c_int32), ("shift", ctypes.c_int32), ("two_pass", ctypes.c_int32), ("b_cap", ctypes.c_int32),
+        ("m_cap", ctypes.c_int32), ("ncand", ctypes.c_int32), ("S_req", ctypes.c_int32),
+        ("m", ctypes.c_int32 * MAXS), ("yi", ctypes.c_int32 * MAXS), ("rinv", ctypes.c_float * MAXS),
+        ("c", (ctypes.c_float * MAXS) * 4), ("m16", ctypes.c_float * MAXS),
+        ("rp0", (ctypes.c_float * MAXRP) * MAXS), ("rp1", (ctypes.c_float * MAXRP) * MAXS),
+        ("rp2", (ctypes.c_float * MAXRP) * MAXS),
+        ("nsmall0", ctypes.c_int32), ("nsmall1", ctypes.c_int32), ("nsmall2", ctypes.c_int32),
+        ("W_hi", ctypes.c_uint32), ("W_lo", ctypes.c_uint32), ("qw", ctypes.c_int32), ("logM", ctypes.c_double),
+        ("TA", ctypes.c_double), ("TB", ctypes.c_double), ("nA", ctypes.c_double), ("nB", ctypes.c_double),
+        ("nC", ctypes.c_double), ("recon1_log2", ctypes.c_double),
+    ]
+
+    @property
+    def moduli(self) -> list[int]:
+        return [int(self.m[i]) for i in range(self.S)]
+
+
+def ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class Oracle:
+    def __init__(self, path: Path = ORACLE_SO):
+        if not path.exists():
+            raise FileNotFoundError(f"{path} is not built (python -m oztt_b200.build)")
+        self.lib = ctypes.CDLL(str(path))
+        L = self.lib
+        L.ozo_output_hash.restype = ctypes.c_uint64
+        L.ozo_output_hash.argtypes = [P, ctypes.c_uint64]
+        L.ozo_time_dot2_rows.restype = ctypes.c_double
+        L.ozo_time_dot2_rows.argtypes = [P, P, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int]
+        u64 = ctypes.c_uint64
+        L.ozo_gen_inputs.argtypes = [P, P, u64, u64, u64, ctypes.c_double, ctypes.c_uint32]
+        L.ozo_gen_pattern.argtypes = [P, P, u64, u64, u64, ctypes.c_int]
+        L.ozo_plan_ii_int8.argtypes = [P, P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                       ctypes.c_int, ctypes.c_int, ctypes.POINTER(OzoPlan), ctypes.c_char_p,
+                                       ctypes.c_size_t]
+        L.ozo_choose_moduli_int8.argtypes = [ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.POINTER(OzoPlan)]
+        L.ozo_scale.argtypes = [P, u64, u64, u64, ctypes.c_int, ctypes.c_int32, P, P, P]
+        L.ozo_split.argtypes = [P, u64, u64, u64, ctypes.c_int, P, ctypes.POINTER(OzoPlan), P]
+        L.ozo_digits.argtypes = [ctypes.c_double, ctypes.c_int32, ctypes.c_int, P]
+        L.ozo_gemm_i32.argtypes = [P, P, u64, u64, u64, u64, P]
+        L.ozo_recon_faithful.argtypes = [P, u64, u64, P, P, ctypes.POINTER(OzoPlan), P, u64]
+        L.ozo_recon_exact.argtypes = [P, u64, u64, P, P, ctypes.POINTER(OzoPlan), P, u64]
+        L.ozo_ii_int8_emulate.argtypes = [P, P, P, u64, u64, u64, ctypes.c_uint32, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_int, ctypes.POINTER(OzoPlan), ctypes.c_char_p, ctypes.c_size_t]
+        L.ozo_dot2_gemm.argtypes = [P, P, u64, u64, u64, P, P]
+        L.ozo_accuracy.argtypes = [P, P, P, u64, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
+        L.ozo_maxrel_f128.argtypes = [P, P, P, u64, u64, u64, P, u64, ctypes.POINTER(ctypes.c_double)]
+
+    # -- generators ---------------------------------------------------------------------------
+    def gen_inputs(self, m: int, n: int, k: int, phi: float, seed: int) -> tuple[np.ndarray, np.ndarray]:
+        a, b = np.empty(m * k), np.empty(k * n)
+        self.lib.ozo_gen_inputs(ptr(a), ptr(b), m, n, k, phi, seed)
+        return a, b
+
+    def gen_pattern(self, m: int, n: int, k: int, mode: int) -> tuple[np.ndarray, np.ndarray]:
+        a, b = np.empty(m * k), np.empty(k * n)
+        self.lib.ozo_gen_pattern(ptr(a), ptr(b), m, n, k, mode)
+        return a, b
+
+    # -- planner ------------------------------------------------------------------------------
+    def plan(self, ap: np.ndarray, bp: np.ndarray, M: int, N: int, K: int, max_moduli=0, passes=0,
+             fixed_bits=0) -> tuple[int, OzoPlan, str]:
+        p = OzoPlan()
+        err = ctypes.create_string_buffer(512)
+        rc = self.lib.ozo_plan_ii_int8(ptr(ap), ptr(bp), M, N, K, max_moduli, passes, fixed_bits, ctypes.byref(p),
+                                       err, 512)
+        return rc, p, err.value.decode()
+
+    def choose_moduli(self, K: int, num_moduli: int, b_cap: int) -> OzoPlan:
+        p = OzoPlan()
+        self.lib.ozo_choose_moduli_int8(K, num_moduli, b_cap, ctypes.byref(p))
+        return p
+
+    # -- stages -------------------------------------------------------------------------------
+    def scale(self, x: np.ndarray, rows: int, cols: int, col_mode: int, shift: int):
+        nout = cols if col_mode else rows
+        bf = np.zeros(nout, dtype=np.uint16)
+        d = np.zeros(nout, dtype=np.int32)
+        fl = np.zeros(1, dtype=np.uint32)
+        self.lib.ozo_scale(ptr(x), rows, cols, cols, col_mode, shift, ptr(bf), ptr(d), ptr(fl))
+        return bf, d, int(fl[0])
+
+    def split(self, x: np.ndarray, rows: int, cols: int, col_mode: int, delta: np.ndarray, plan: OzoPlan):
+        out = np.zeros(plan.S * rows * cols, dtype=np.int8)
+        self.lib.ozo_split(ptr(x), rows, cols, cols, col_mode, ptr(delta), ctypes.byref(plan), ptr(out))
+        return out
+
+    def digits(self, x: float, delta: int, nd: int) -> np.ndarray:
+        out = np.zeros(nd, dtype=np.float32)
+        self.lib.ozo_digits(x, delta, nd, ptr(out))
+        return out
+
+    def gemm_i32(self, ra: np.ndarray, rb: np.ndarray, S: int, M: int, N: int, K: int) -> np.ndarray:
+        c = np.zeros(S * M * N, dtype=np.int32)
+        bad = self.lib.ozo_gemm_i32(ptr(ra), ptr(rb), S, M, N, K, ptr(c))
+        assert bad == 0, "int32 overflow in the oracle GEMM"
+        return c
+
+    def recon(self, cs: np.ndarray, M: int, N: int, dA: np.ndarray, dB: np.ndarray, plan: OzoPlan,
+              exact: bool) -> np.ndarray:
+        c = np.zeros(M * N)
+        fn = self.lib.ozo_recon_exact if exact else self.lib.ozo_recon_faithful
+        fn(ptr(cs), M, N, ptr(dA), ptr(dB), ctypes.byref(plan), ptr(c), N)
+        return c
+
+    def emulate(self, a, b, m, n, k, max_moduli=0, passes=0, fixed_bits=0, exact=False):
+        c = np.zeros(m * n)
+        p = OzoPlan()
+        err = ctypes.create_string_buffer(512)
+        rc = self.lib.ozo_ii_int8_emulate(ptr(a), ptr(b), ptr(c), m, n, k, max_moduli, passes, fixed_bits,
+                                          1 if exact else 0, ctypes.byref(p), err, 512)
+        return rc, c, p, err.value.decode()
+
+    # -- metrics ------------------------------------------------------------------------------
+    def output_hash(self, c: np.ndarray) -> str:
+        return "%016x" % self.lib.ozo_output_hash(ptr(c), c.size)
+
+    def dot2(self, a, b, m, n, k):
+        hi, lo = np.zeros(m * n), np.zeros(m * n)
+        self.lib.ozo_dot2_gemm(ptr(a), ptr(b), m, n, k, ptr(hi), ptr(lo))
+        return hi, lo
+
+    def accuracy(self, c, hi, lo) -> tuple[float, float]:
+        r, e = ctypes.c_double(), ctypes.c_double()
+        self.lib.ozo_accuracy(ptr(c), ptr(hi), ptr(lo), c.size, ctypes.byref(r), ctypes.byref(e))
+        return r.value, e.value
+
+    def maxrel_f128(self, a, b, c, m, n, k, rows=None) -> float:
+        out = ctypes.c_double()
+        if rows is None:
+            self.lib.ozo_maxrel_f128(ptr(a), ptr(b), ptr(c), m, n, k, None, 0, ctypes.byref(out))
+        else:
+            r = np.ascontiguousarray(rows, dtype=np.uint64)
+            self.lib.ozo_maxrel_f128(ptr(a), ptr(b), ptr(c), m, n, k, ptr(r), r.size, ctypes.byref(out))
+        return out.value
+
+
+class RefPlan:
+    """The reference's planner headers compiled in place (oracle/ref_plan.cpp)."""
+
+    def __init__(self, path: Path = REF_PLAN_SO):
+        if not path.exists():
+            raise FileNotFoundError(str(path))
+        self.lib = ctypes.CDLL(str(path))
+        self.lib.ozr_choose_moduli.argtypes = [ctypes.c_uint32] * 3 + [ctypes.c_int, ctypes.c_int,
+                                                                      ctypes.POINTER(OzoPlan)]
+        self.lib.ozr_plan.argtypes = [P, P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                      ctypes.c_int, ctypes.c_int, ctypes.POINTER(OzoPlan)]
+
+    def choose_moduli(self, K: int, num_moduli: int, b_cap: int, M: int = 0, N: int = 0) -> OzoPlan:
+        p = OzoPlan()
+        self.lib.ozr_choose_moduli(M or K, N or K, K, num_moduli, b_cap, ctypes.byref(p))
+        return p
+
+    def plan(self, ap, bp, M, N, K, max_moduli=0, passes=0, fixed_bits=0) -> tuple[int, OzoPlan]:
+        p = OzoPlan()
+        rc = self.lib.ozr_plan(ptr(ap), ptr(bp), M, N, K, max_moduli, passes, fixed_bits, ctypes.byref(p))
+        return rc, p
+
+
+class RefEmu:
+    """The reference's host emulation of its device kernels, composed (oracle/ref_emu.cpp)."""
+
+    def __init__(self, path: Path = REF_EMU_SO):
+        if not path.exists():
+            raise FileNotFoundError(str(path))
+        self.lib = ctypes.CDLL(str(path))
+        self.lib.ozr_emulate_int8.argtypes = [P, P, P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                              ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
+
+    def emulate(self, ap, bp, M, N, K, b_fixed, num_moduli=16, two_pass=False):
+        c = np.zeros(M * N)
+        mods = np.zeros(MAXS, dtype=np.int32)
+        s = self.lib.ozr_emulate_int8(ptr(ap), ptr(bp), ptr(c), M, N, K, b_fixed, num_moduli, 1 if two_pass else 0,
+                                      ptr(mods))
+        return s, c, [int(x) for x in mods[:max(s, 0)]]
+
+
+def pad(a: np.ndarray, rows: int, cols: int, prow: int, pcol: int) -> np.ndarray:
+    out = np.zeros((prow, pcol))
+    out[:rows, :cols] = a.reshape(rows, cols)
+    return out.reshape(-1)
+
+
+def round_up(v: int, q: int) -> int:
+    return (v + q - 1) // q * q
