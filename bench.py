@@ -1,0 +1,403 @@
+#!/usr/bin/env python
+"""Benchmark: Ozaki-II INT8 effective FP64 TFLOPS on B200 (the metric of BASELINE.json).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl oztt|reference]
+
+One step is one pass of the Scheme II INT8 pipeline (scale -> split -> residue GEMM on the tensor
+cores -> exact CRT reconstruction) over one m x n x k problem with FP64 operands already resident in
+HBM. The workload at N=1 is the metric point m=n=k=16384, phi=0.5, seed 0 of the reference
+evaluator's generator (evaluation/numerics.hpp:19-38, synthetic data). With N>1 ranks (one process
+per GPU, torchrun) the problem grows with N: rank r owns one 16384 x 16384 output tile of a P x Q grid
+of tiles (k = 16384), with its A row-panel and B column-panel generated in its own HBM; there is no
+collective on the data path (weak scaling; at N=4 the global problem is 32768 x 32768 x 16384).
+
+Printed (rank 0, one JSON line): value = 2*m*n*k*N / (max over ranks of the device time of one step),
+e2e = the same metric through the public API (ozTTgemm::Context::gemm via the C ABI) from pinned host
+buffers including the host planning, the copies in and the copy of C back, the roofline of the residue
+GEMM (int8 tensor ops per launch / its CUDA-event duration against the B200 dense int8 peak), the
+reference's host FP64 GEMM (Dot2, compiled from the reference sources in oracle/_ref) timed on a sample
+of rows as the CPU baseline, cuBLAS DGEMM on the same GPU for comparison, and the maximum relative error
+of sampled rows against a binary128 reference.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+DEFAULT_SIZE = 16384
+METRIC = "Ozaki-II INT8 effective FP64 TFLOPS at m=n=k=16384; max rel err vs binary128"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["oztt", "reference"], default="oztt")
+    ap.add_argument("--size", type=int, default=DEFAULT_SIZE, help="per-GPU tile side m = n = k")
+    ap.add_argument("--phi", type=float, default=0.5)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-accuracy", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d.get("hbm_gbs", 6650.0), "bf16_tflops": d.get("bf16_tflops", 1590.0),
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", 1400.0), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock and throttle-reason samples (200 ms) during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(prefix="oztt_clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in Path(self.path).read_text().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return float("nan")
+
+        sm = [num(r[1]) for r in rows]
+        smax = max(num(r[2]) for r in rows)
+        loaded = [s for s in sm if s > 0.5 * smax] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(num(r[3]) for r in rows)}
+
+
+# ---- CPU baseline: the reference's host FP64 GEMM (Dot2) -------------------------------------------
+def cpu_dot2_library():
+    ref = ROOT / "oracle" / "_ref" / "libozref_dot2.so"
+    if ref.exists():
+        lib = ctypes.CDLL(str(ref))
+        lib.ozr_dot2_prepare.argtypes = [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_uint32] * 3
+        lib.ozr_dot2_run.restype = ctypes.c_double
+        lib.ozr_dot2_run.argtypes = [ctypes.c_int]
+        return lib, "reference"
+    return None, "port"
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def time_cpu_dot2(a: np.ndarray, b: np.ndarray, n: int, k: int, target_s: float) -> dict:
+    """Times the reference's Dot2 GEMM on the first rows of C, sized to about target_s seconds."""
+    threads = cpu_threads()
+    lib, kind = cpu_dot2_library()
+    if lib is None:  # the oracle's restatement of the same routine
+        sys.path.insert(0, str(ROOT / "tests"))
+        from oracle_lib import Oracle  # noqa: E402
+
+        orc = Oracle()
+
+        def run(rows):
+            return orc.lib.ozo_time_dot2_rows(a.ctypes.data, b.ctypes.data, rows, n, k, threads)
+    else:
+        def run(rows):
+            lib.ozr_dot2_prepare(a.ctypes.data, b.ctypes.data, rows, n, k)
+            return lib.ozr_dot2_run(threads)
+    rows = max(threads, 8)
+    t = run(rows)
+    rows = int(min(n, max(threads, rows * target_s / max(t, 1e-3))))
+    rows = max(threads, rows // threads * threads)
+    t = run(rows)
+    flops = 2.0 * rows * n * k
+    return {"value": flops / t / 1e12, "unit": "TFLOPS", "cores": threads, "kind": kind,
+            "sample": f"Dot2 reference_gemm (evaluation/numerics.hpp) on the first {rows} rows of C "
+                      f"({rows}x{n}x{k}), {t:.2f} s"}
+
+
+def run_reference(args) -> None:
+    """--impl reference: the reference's own CPU FP64 GEMM on the box's host cores, per step a bounded
+    row sample of the same workload; rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    n = k = args.size
+    sys.path.insert(0, str(ROOT))
+    import oztt_b200 as oz
+
+    a, b = oz.eval_inputs(n, n, k, args.phi, args.seed)
+    threads = cpu_threads()
+    lib, kind = cpu_dot2_library()
+    if lib is None:
+        sys.path.insert(0, str(ROOT / "tests"))
+        from oracle_lib import Oracle  # noqa: E402
+
+        orc = Oracle()
+
+        def run(rows):
+            return orc.lib.ozo_time_dot2_rows(a.ctypes.data, b.ctypes.data, rows, n, k, threads)
+    else:
+        def run(rows):
+            lib.ozr_dot2_prepare(a.ctypes.data, b.ctypes.data, rows, n, k)
+            return lib.ozr_dot2_run(threads)
+    rows = max(threads, 8)
+    t0 = run(rows)
+    # each step about 10 s of CPU work
+    rows = int(min(n, max(threads, rows * 10.0 / max(t0, 1e-3))))
+    times = []
+    for _ in range(args.warmup):
+        run(rows)
+    for _ in range(args.steps):
+        times.append(run(rows))
+    t = statistics.median(times)
+    value = 2.0 * rows * n * k / t / 1e12
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "TFLOPS", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": f"II INT8 {n}x{n}x{k} phi={args.phi} seed={args.seed}; reference CPU FP64 GEMM "
+                                   f"on a {rows}-row sample per step"},
+            "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": kind,
+                             "sample": f"first {rows} rows of C per step"},
+            "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- the GPU arm --------------------------------------------------------------------------------------
+def grid_shape(world: int) -> tuple[int, int]:
+    p = int(math.sqrt(world))
+    while world % p:
+        p -= 1
+    return world // p, p  # rows of tiles, columns of tiles
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    import oztt_b200 as oz
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    m = n = k = args.size
+    P, Q = grid_shape(world)
+    p_idx, q_idx = rank // Q, rank % Q
+    # Inputs: at N=1 exactly the evaluator's stream (all of A, then all of B). With several ranks each
+    # rank generates its own A row-panel and B column-panel from per-panel seeds.
+    if world == 1:
+        a, b = oz.eval_inputs(m, n, k, args.phi, args.seed)
+    else:
+        a, _ = oz.eval_inputs(m, 1, k, args.phi, args.seed + 1000 * p_idx + 1)
+        _, b = oz.eval_inputs(1, n, k, args.phi, args.seed + 1000 * q_idx + 2)
+    t_plan = time.perf_counter()
+    plan = oz.ii_int8_plan(a, b, m, n, k)
+    t_plan = time.perf_counter() - t_plan
+    if world > 1:  # one set of constants for all tiles: rank 0's decision
+        buf = torch.frombuffer(bytearray(bytes(plan)), dtype=torch.uint8).cuda()
+        dist.broadcast(buf, 0)
+        ctypes.memmove(ctypes.addressof(plan), bytes(buf.cpu().numpy()), ctypes.sizeof(plan))
+    A = torch.from_numpy(a).cuda()
+    B = torch.from_numpy(b).cuda()
+    C = torch.empty(m * n, dtype=torch.float64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step():
+        return oz.ii_int8_run_device_timed(A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, plan, stream, local)
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    stage_sum = [0.0] * 6
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(args.steps):
+            st = step()
+            stage_sum = [x + y for x, y in zip(stage_sum, st)]
+        ev1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    stage_ms = [x / args.steps for x in stage_sum]
+    if world > 1:
+        t = torch.tensor([ms] + stage_ms, dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, stage_ms = float(t[0]), [float(x) for x in t[1:]]
+    flops = 2.0 * m * n * k * world
+    value = flops / (ms * 1e-3) / 1e12
+    clk = clocks.summary()
+
+    # ---- roofline of the residue GEMM (dominant kernel) --------------------------------------------
+    peaks = measured_peaks()
+    S = plan.S
+    gemm_ops = 2.0 * m * n * k * S  # int8 multiply-adds of all moduli in one launch (x2 ops)
+    gemm_tops = gemm_ops / (stage_ms[4] * 1e-3) / 1e12
+    int8_peak = 2.0 * peaks["bf16_tflops"]  # B200 dense int8 = 2 x dense bf16
+    # HBM-bound stages against the measured copy bandwidth
+    split_bytes = 8.0 * (m * k + k * n) + S * (m * k + k * n)
+    recon_bytes = S * m * n + 8.0 * m * n
+    result = {"metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+              "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+              "vs_baseline": None, "dtype": "f64 (int8 residue products, s32 accumulate)",
+              "data": "synthetic: evaluation/numerics.hpp generator (u-0.5)*exp(phi*z), mt19937 seed "
+                      f"{args.seed}" + ("" if world == 1 else " per panel"),
+              "config": {"workload": f"Scheme II INT8, {m}x{n}x{k} per GPU" +
+                                     ("" if world == 1 else f" ({P}x{Q} tiles: global {P * m}x{Q * n}x{k})") +
+                                     f", phi={args.phi}, auto precision",
+                         "moduli": S, "integer_bits": plan.b, "reconstruction_passes": 2 if plan.two_pass else 1,
+                         "l2": "inputs (2.1 GB each) larger than the 126 MB L2; no flush",
+                         "planning_s_host": round(t_plan, 3)},
+              "stage_ms": {"scale_rows": stage_ms[0], "scale_cols": stage_ms[1], "split_rows": stage_ms[2],
+                           "split_cols": stage_ms[3], "residue_gemm": stage_ms[4], "recon": stage_ms[5]},
+              "roofline": {"bound": "tensor", "kernel": "residue_gemm_kernel<1> (tcgen05 kind::i8)",
+                           "achieved": gemm_tops, "peak": int8_peak, "unit": "TOP/s (int8)",
+                           "frac": gemm_tops / int8_peak,
+                           "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({peaks['source']})",
+                           "traffic": None,
+                           "algorithmic": f"2*m*n*k*S = {gemm_ops:.4g} int8 ops per launch"},
+              "hbm_stages": {
+                  "split_GBps": (split_bytes / ((stage_ms[2] + stage_ms[3]) * 1e-3)) / 1e9,
+                  "recon_GBps": (recon_bytes / (stage_ms[5] * 1e-3)) / 1e9,
+                  "peak_GBps": peaks["hbm_gbs"]},
+              "gpu_launches": 7 * args.steps,
+              "clocks": clk}
+
+    # ---- cuBLAS DGEMM on the same GPU, and the accuracy of both on sampled rows ----------------------
+    if rank == 0:
+        A2, B2 = A.view(m, k), B.view(k, n)
+        for _ in range(2):
+            D = A2 @ B2
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            D = A2 @ B2
+        e1.record()
+        torch.cuda.synchronize()
+        dms = e0.elapsed_time(e1) / 3
+        result["cublas_dgemm"] = {"ms": dms, "tflops": 2.0 * m * n * k / (dms * 1e-3) / 1e12}
+        result["vs_cublas_dgemm"] = (2.0 * m * n * k / (ms * 1e-3) / 1e12) / result["cublas_dgemm"]["tflops"]
+        if not args.no_accuracy:
+            sys.path.insert(0, str(ROOT / "tests"))
+            try:
+                from oracle_lib import Oracle  # checker only
+
+                orc = Oracle()
+                rows = np.linspace(0, m - 1, 8).astype(np.uint64)
+                c_oz = C.cpu().numpy()
+                c_dg = D.reshape(-1).cpu().numpy()
+                result["max_rel_err"] = orc.maxrel_f128(a, b, c_oz, m, n, k, rows=rows)
+                result["cublas_dgemm"]["max_rel_err"] = orc.maxrel_f128(a, b, c_dg, m, n, k, rows=rows)
+                result["accuracy_sample"] = "8 rows of C (all columns) vs a binary128 reference"
+            except Exception as exc:  # noqa: BLE001
+                result["max_rel_err"] = None
+                result["accuracy_error"] = str(exc)
+        del D
+
+    # ---- end to end through the public API --------------------------------------------------------
+    if args.e2e_steps > 0:
+        ha = torch.from_numpy(a).pin_memory().numpy()
+        hb = torch.from_numpy(b).pin_memory().numpy()
+        hc = torch.empty(m * n, dtype=torch.float64).pin_memory().numpy()
+        ctx = oz.Context(oz.DeviceOptions(device_id=local))
+        opt = oz.Options(format=oz.Format.INT8)
+        ctx.gemm(ha, hb, hc, m, n, k, opt)  # warm-up
+        if world > 1:
+            dist.barrier()
+        times = []
+        for _ in range(args.e2e_steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            ctx.gemm(ha, hb, hc, m, n, k, opt)
+            times.append(time.perf_counter() - t0)
+        e2e_s = statistics.median(times)
+        if world > 1:
+            t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t[0])
+        result["e2e"] = {"value": flops / e2e_s / 1e12, "unit": "TFLOPS", "s_per_step": e2e_s,
+                         "h2d_bytes_per_step": 8 * (m * k + k * n), "d2h_bytes_per_step": 8 * m * n,
+                         "path": "ozTTgemm::Context::gemm via oztt_gemm (validation, host planning, pinned H2D, "
+                                 "GPU pipeline, D2H)"}
+    # ---- CPU baseline (rank 0 at N=1) ------------------------------------------------------------------
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = time_cpu_dot2(a, b, n, k, target_s=12.0)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

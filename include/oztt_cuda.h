@@ -114,6 +114,12 @@ int oztt_ii_int8_run(int device_id, const double* a, const double* b, double* c,
 int oztt_ii_int8_run_device(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
                             uint64_t k, const oztt_ii_plan* plan, void* stream, char* err, size_t errlen);
 
+/* The same, also returning the device time of each stage in stage_ms[6] (scale rows, scale columns,
+ * split rows, split columns, residue GEMM, reconstruction), from CUDA events on `stream`. */
+int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* b, double* c, uint64_t m,
+                                  uint64_t n, uint64_t k, const oztt_ii_plan* plan, void* stream, double* stage_ms,
+                                  char* err, size_t errlen);
+
 /* ---- stages (device pointers; asynchronous on `stream`) -------------------------------------- */
 
 /* Tile-padded dimensions of the residue planes: mp = m rounded up to 128, np = n rounded up to 256,
@@ -150,6 +156,15 @@ int oztt_ii_residue_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_
 int oztt_ii_recon(const uint8_t* k_planes, uint64_t mp, uint64_t np, const int32_t* delta_a, const int32_t* delta_b,
                   const oztt_ii_plan* plan, double* c, uint64_t m, uint64_t n, uint64_t ldc, void* stream, char* err,
                   size_t errlen);
+
+/* ---- evaluation utilities (the reference evaluator's input generator and output hash) ----------- */
+
+/* Seeded inputs of evaluation/numerics.hpp:19-38 with the seed as a parameter: std::mt19937(seed); A
+ * (m x k) then B (k x n), row-major; phi < 0: uniform(-1, 1); else (u - 1/2) * exp(phi * z) with
+ * u ~ U[0,1) then z ~ N(0,1) per element. Host memory. */
+void oztt_eval_inputs(double* a, double* b, uint64_t m, uint64_t n, uint64_t k, double phi, uint32_t seed);
+/* Hash of the output bit patterns (evaluation/numerics.hpp:46-57). */
+uint64_t oztt_eval_output_hash(const double* c, uint64_t count);
 
 /* Number of SMs and compute capability of a device (0 on success). */
 int oztt_device_info(int device_id, int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor);

@@ -127,6 +127,10 @@ _SIGNATURES = {
     "oztt_ii_int8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, _I32, _I32, ctypes.POINTER(IIPlan), _ERR, _SZ],
     "oztt_ii_int8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IIPlan), _ERR, _SZ],
     "oztt_ii_int8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IIPlan), _P, _ERR, _SZ],
+    "oztt_ii_int8_run_device_timed": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IIPlan), _P, _P,
+                                      _ERR, _SZ],
+    "oztt_eval_inputs": [_P, _P, _U64, _U64, _U64, ctypes.c_double, ctypes.c_uint32],
+    "oztt_eval_output_hash": [_P, _U64],
     "oztt_ii_scale_rows": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _P, _ERR, _SZ],
     "oztt_ii_scale_cols": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _P, _ERR, _SZ],
     "oztt_ii_split_rows": [_P, _U64, _U64, _U64, _P, ctypes.POINTER(IIPlan), _P, _U64, _U64, _P, _ERR, _SZ],
@@ -137,6 +141,9 @@ _SIGNATURES = {
     "oztt_ii_padded_dims": [_U64, _U64, _U64, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
     "oztt_test_udiv_small": [ctypes.c_uint32, ctypes.c_uint32],
 }
+
+_RESTYPES = {"oztt_test_udiv_small": ctypes.c_uint32, "oztt_ii_padded_dims": None, "oztt_eval_inputs": None,
+             "oztt_eval_output_hash": ctypes.c_uint64}
 
 # Symbols declared in include/oztt_cuda.h (the tests check that the library exports each of them).
 C_ABI_SYMBOLS = [name for name in _SIGNATURES if name != "oztt_test_udiv_small"]
@@ -150,12 +157,25 @@ def _load() -> ctypes.CDLL:
     for name, args in _SIGNATURES.items():
         fn = getattr(lib_, name)
         fn.argtypes = args
-        fn.restype = ctypes.c_uint32 if name == "oztt_test_udiv_small" else (
-            None if name == "oztt_ii_padded_dims" else ctypes.c_int)
+        fn.restype = _RESTYPES.get(name, ctypes.c_int)
     return lib_
 
 
-lib = _load()
+_LIB = None
+
+
+def _lib() -> ctypes.CDLL:
+    """The loaded library (loaded on first use, so that building does not need it)."""
+    global _LIB
+    if _LIB is None:
+        _LIB = _load()
+    return _LIB
+
+
+def __getattr__(name: str):
+    if name == "lib":
+        return _lib()
+    raise AttributeError(name)
 
 
 def _raise(code: int, msg: bytes | str) -> None:
@@ -207,7 +227,7 @@ class Context:
         co = _COptions(int(opt.scheme), int(opt.format), int(opt.slices), int(opt.max_moduli), int(opt.reconstruction))
         ci = _CInfo()
         err = _errbuf()
-        rc = lib.oztt_gemm(self.options.device_id, av.ctypes.data, av.size, bv.ctypes.data, bv.size, cv.ctypes.data,
+        rc = _lib().oztt_gemm(self.options.device_id, av.ctypes.data, av.size, bv.ctypes.data, bv.size, cv.ctypes.data,
                            cv.size, m, n, k, ctypes.byref(co), ctypes.byref(ci), err, len(err))
         if rc != OK:
             _raise(rc, err.value)
@@ -232,7 +252,7 @@ def ii_int8_plan(a, b, m: int, n: int, k: int, max_moduli: int = 0, reconstructi
         raise ValueError("matrix span sizes do not match m, n, k")
     plan = IIPlan()
     err = _errbuf()
-    rc = lib.oztt_ii_int8_plan(av.ctypes.data, bv.ctypes.data, m, n, k, max_moduli, reconstruction, fixed_bits,
+    rc = _lib().oztt_ii_int8_plan(av.ctypes.data, bv.ctypes.data, m, n, k, max_moduli, reconstruction, fixed_bits,
                                ctypes.byref(plan), err, len(err))
     if rc != OK:
         _raise(rc, err.value)
@@ -244,7 +264,7 @@ def ii_int8_run(a, b, m: int, n: int, k: int, plan: IIPlan, device_id: int = 0) 
     av, bv = _as_f64(a, "a"), _as_f64(b, "b")
     c = np.empty(m * n, dtype=np.float64)
     err = _errbuf()
-    rc = lib.oztt_ii_int8_run(device_id, av.ctypes.data, bv.ctypes.data, c.ctypes.data, m, n, k, ctypes.byref(plan),
+    rc = _lib().oztt_ii_int8_run(device_id, av.ctypes.data, bv.ctypes.data, c.ctypes.data, m, n, k, ctypes.byref(plan),
                               err, len(err))
     if rc != OK:
         _raise(rc, err.value)
@@ -255,21 +275,47 @@ def ii_int8_run_device(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: in
                        stream: int = 0, device_id: int = 0) -> None:
     """The pipeline on device pointers (oztt_ii_int8_run_device); synchronises `stream`."""
     err = _errbuf()
-    rc = lib.oztt_ii_int8_run_device(device_id, a_ptr, b_ptr, c_ptr, m, n, k, ctypes.byref(plan), stream, err,
+    rc = _lib().oztt_ii_int8_run_device(device_id, a_ptr, b_ptr, c_ptr, m, n, k, ctypes.byref(plan), stream, err,
                                      len(err))
     if rc != OK:
         _raise(rc, err.value)
 
 
+def ii_int8_run_device_timed(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, plan: IIPlan,
+                             stream: int = 0, device_id: int = 0) -> list[float]:
+    """As ii_int8_run_device; returns the device milliseconds of the six stages (scale rows, scale
+    columns, split rows, split columns, residue GEMM, reconstruction)."""
+    ms = (ctypes.c_double * 6)()
+    err = _errbuf()
+    rc = _lib().oztt_ii_int8_run_device_timed(device_id, a_ptr, b_ptr, c_ptr, m, n, k, ctypes.byref(plan), stream, ms,
+                                           err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return list(ms)
+
+
+def eval_inputs(m: int, n: int, k: int, phi: float, seed: int) -> tuple[np.ndarray, np.ndarray]:
+    """The reference evaluator's seeded inputs (evaluation/numerics.hpp:19-38) with a seed parameter."""
+    a = np.empty(m * k, dtype=np.float64)
+    b = np.empty(k * n, dtype=np.float64)
+    _lib().oztt_eval_inputs(a.ctypes.data, b.ctypes.data, m, n, k, phi, seed)
+    return a, b
+
+
+def eval_output_hash(c: np.ndarray) -> str:
+    c = np.ascontiguousarray(c, dtype=np.float64).reshape(-1)
+    return "%016x" % _lib().oztt_eval_output_hash(c.ctypes.data, c.size)
+
+
 def padded_dims(m: int, n: int, k: int) -> tuple[int, int, int]:
     mp, np_, kp = _U64(), _U64(), _U64()
-    lib.oztt_ii_padded_dims(m, n, k, ctypes.byref(mp), ctypes.byref(np_), ctypes.byref(kp))
+    _lib().oztt_ii_padded_dims(m, n, k, ctypes.byref(mp), ctypes.byref(np_), ctypes.byref(kp))
     return mp.value, np_.value, kp.value
 
 
 def call(name: str, *args) -> None:
     """Call a stage entry point of the C ABI; the trailing (err, errlen) are appended here."""
     err = _errbuf()
-    rc = getattr(lib, name)(*args, err, len(err))
+    rc = getattr(_lib(), name)(*args, err, len(err))
     if rc != OK:
         _raise(rc, err.value)

@@ -37,7 +37,7 @@ CXX_FLAGS = ["-std=gnu++20", "-O2", "-fPIC", "-fno-fast-math", "-ffp-contract=of
              f"-I{ROOT / 'include'}", f"-I{CUDA_HOME / 'include'}"]
 
 CU_SOURCES = ["split.cu", "gemm_i8.cu", "recon.cu", "ii_int8.cu"]
-CPP_SOURCES = ["planner.cpp", "context.cpp"]
+CPP_SOURCES = ["planner.cpp", "context.cpp", "evaluation.cpp"]
 
 
 def _run(cmd: list[str]) -> None:

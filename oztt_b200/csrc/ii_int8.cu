@@ -108,8 +108,10 @@ void check_flags(uint32_t flags, int gemm_err) {
 }  // namespace
 
 // The device pipeline on device buffers (row-major, lda = k, ldb = n, ldc = n).
+// stage_ms (optional, 6 entries): device time of scale rows, scale cols, split rows, split cols, residue
+// GEMM and reconstruction, from CUDA events recorded on `st` between the launches.
 void run_ii_int8_device(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
-                        const oztt_ii_plan& p, cudaStream_t st) {
+                        const oztt_ii_plan& p, cudaStream_t st, double* stage_ms = nullptr) {
     check_plan(p);
     const uint64_t S = (uint64_t)p.S;
     const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
@@ -118,15 +120,43 @@ void run_ii_int8_device(const double* a, const double* b, double* c, uint64_t m,
     OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
+    cudaEvent_t ev[7] = {};
+    struct Events {
+        cudaEvent_t* e;
+        bool on;
+        ~Events() {
+            if (on)
+                for (int i = 0; i < 7; ++i)
+                    if (e[i]) cudaEventDestroy(e[i]);
+        }
+    } events{ev, stage_ms != nullptr};
+    auto mark = [&](int i) {
+        if (stage_ms) OZTT_CUDA(cudaEventRecord(ev[i], st));
+    };
+    if (stage_ms)
+        for (auto& e : ev) OZTT_CUDA(cudaEventCreate(&e));
+    mark(0);
     launch_scale_rows(a, m, k, k, p.shift, dA.as<int32_t>(), nullptr, flags, st);
+    mark(1);
     launch_scale_cols(b, k, n, n, p.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
+    mark(2);
     launch_split_rows(a, m, k, k, dA.as<int32_t>(), p, ra.as<int8_t>(), mp, kp, st);
+    mark(3);
     launch_split_cols(b, k, n, n, dB.as<int32_t>(), p, rb.as<int8_t>(), np, kp, st);
+    mark(4);
     launch_residue_gemm(ra.as<int8_t>(), rb.as<int8_t>(), mp, np, kp, p, 1, kpl.p, gemm_err, st);
+    mark(5);
     launch_recon(kpl.as<uint8_t>(), mp, np, dA.as<int32_t>(), dB.as<int32_t>(), p, c, m, n, n, st);
+    mark(6);
     uint32_t host_words[2] = {0, 0};
     OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
     OZTT_CUDA(cudaStreamSynchronize(st));
+    if (stage_ms)
+        for (int i = 0; i < 6; ++i) {
+            float ms = 0;
+            OZTT_CUDA(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+            stage_ms[i] = ms;
+        }
     check_flags(host_words[0], (int)host_words[1]);
 }
 
@@ -177,6 +207,17 @@ int oztt_ii_int8_run_device(int device_id, const double* a, const double* b, dou
         if (!m || !n || !k) throw Error(OZTT_EINVAL, "matrix dimensions are zero");
         oztt::open_device(device_id);
         oztt::run_ii_int8_device(a, b, c, m, n, k, *plan, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                                  uint64_t k, const oztt_ii_plan* plan, void* stream, double* stage_ms, char* err,
+                                  size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a || !b || !c || !plan || !stage_ms) throw Error(OZTT_EINVAL, "null argument");
+        if (!m || !n || !k) throw Error(OZTT_EINVAL, "matrix dimensions are zero");
+        oztt::open_device(device_id);
+        oztt::run_ii_int8_device(a, b, c, m, n, k, *plan, reinterpret_cast<cudaStream_t>(stream), stage_ms);
     });
 }
 

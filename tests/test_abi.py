@@ -16,7 +16,7 @@ ROOT = Path(__file__).resolve().parent.parent
 
 def declared_symbols() -> list[str]:
     text = (ROOT / "include" / "oztt_cuda.h").read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|void)\s+(oztt_[a-z0-9_]+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|void|uint64_t)\s+(oztt_[a-z0-9_]+)\s*\(", text, flags=re.M)))
 
 
 def test_library_exports_every_declared_symbol(oztt):
@@ -117,3 +117,13 @@ def test_plan_rejections(oztt):
     k = 1 << 24
     with pytest.raises(RuntimeError, match="K="):
         oztt.ii_int8_plan(np.ones(k), np.ones(k), 1, 1, k, fixed_bits=0, reconstruction=1)
+
+
+def test_eval_generator_matches_oracle(oztt, oracle):
+    """The library's evaluation generator and hash equal the oracle's restatement (which reproduces the
+    reference's published hash from the same inputs)."""
+    for (m, n, k, phi, seed) in [(5, 7, 3, -1.0, 7), (16, 8, 4, 0.5, 0), (3, 3, 3, 4.0, 123)]:
+        a1, b1 = oztt.eval_inputs(m, n, k, phi, seed)
+        a2, b2 = oracle.gen_inputs(m, n, k, phi, seed)
+        assert np.array_equal(a1, a2) and np.array_equal(b1, b2)
+        assert oztt.eval_output_hash(a1) == oracle.output_hash(a2)

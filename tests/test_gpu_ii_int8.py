@@ -196,7 +196,7 @@ def test_residue_gemm_large_vs_cublas(oztt, cuda):
     """A full-size tile grid (several waves of the persistent kernel) checked against an exact int8
     GEMM from torch for two moduli."""
     mp, np_, kp = 2048, 2048, 4096
-    a = np.ones(4)
+    a = np.ones(2)
     plan = plan_for(oztt, a, a, 2, 2, 1, fixed_bits=54, reconstruction=1, max_moduli=16)
     S = plan.S
     g = torch.Generator(device="cuda").manual_seed(1)
