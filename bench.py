@@ -162,6 +162,7 @@ def time_cpu_dot2(a: np.ndarray, b: np.ndarray, n: int, k: int, target_s: float)
             lib.ozr_dot2_prepare(a.ctypes.data, b.ctypes.data, rows, n, k)
             return lib.ozr_dot2_run(threads)
     rows = max(threads, 8)
+    run(rows)  # warm-up: first touch of the copies and the thread pool
     t = run(rows)
     rows = int(min(n, max(threads, rows * target_s / max(t, 1e-3))))
     rows = max(threads, rows // threads * threads)
@@ -198,6 +199,7 @@ def run_reference(args) -> None:
             lib.ozr_dot2_prepare(a.ctypes.data, b.ctypes.data, rows, n, k)
             return lib.ozr_dot2_run(threads)
     rows = max(threads, 8)
+    run(rows)  # warm-up
     t0 = run(rows)
     # each step about 10 s of CPU work
     rows = int(min(n, max(threads, rows * 10.0 / max(t0, 1e-3))))
