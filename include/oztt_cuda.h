@@ -135,6 +135,18 @@ int oztt_ii_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, in
 int oztt_ii_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
                        uint16_t* bf16max, uint32_t* flags, void* stream, char* err, size_t errlen);
 
+/* Largest n accepted by oztt_ii_scale_cols_noalloc (2 MiB of column scratch per device). */
+#define OZTT_NOALLOC_MAX_COLS 262144u
+/* No counterpart in the reference: oztt_ii_scale_cols without any device allocation, for callers that
+ * cannot let a library allocate device memory (all memory owned by their own allocator or reserved up
+ * front, or latency-critical paths where an allocation may synchronise or fail). Its scratch is a
+ * fixed static device array that every GPU loading the library keeps until exit; n is limited to
+ * OZTT_NOALLOC_MAX_COLS (larger n: OZTT_EINVAL). The first call on a device looks up the array's
+ * address with that device current; make it before any stream capture. Calls on one device share the
+ * array (each clears the part it uses first); calls that overlap on the GPU race. */
+int oztt_ii_scale_cols_noalloc(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
+                               uint16_t* bf16max, uint32_t* flags, void* stream, char* err, size_t errlen);
+
 /* Residues of a (m x k, lda) with delta per row: planes [S][mp][kp] int8, zero in the padding. */
 int oztt_ii_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
                        const oztt_ii_plan* plan, int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err,

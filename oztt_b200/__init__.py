@@ -133,6 +133,7 @@ _SIGNATURES = {
     "oztt_eval_output_hash": [_P, _U64],
     "oztt_ii_scale_rows": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _P, _ERR, _SZ],
     "oztt_ii_scale_cols": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _P, _ERR, _SZ],
+    "oztt_ii_scale_cols_noalloc": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _P, _ERR, _SZ],
     "oztt_ii_split_rows": [_P, _U64, _U64, _U64, _P, ctypes.POINTER(IIPlan), _P, _U64, _U64, _P, _ERR, _SZ],
     "oztt_ii_split_cols": [_P, _U64, _U64, _U64, _P, ctypes.POINTER(IIPlan), _P, _U64, _U64, _P, _ERR, _SZ],
     "oztt_ii_residue_gemm": [_P, _P, _U64, _U64, _U64, ctypes.POINTER(IIPlan), _I32, _P, _P, _ERR, _SZ],

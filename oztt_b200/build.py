@@ -36,7 +36,7 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompil
 CXX_FLAGS = ["-std=gnu++20", "-O2", "-fPIC", "-fno-fast-math", "-ffp-contract=off", "-pthread",
              f"-I{ROOT / 'include'}", f"-I{CUDA_HOME / 'include'}"]
 
-CU_SOURCES = ["split.cu", "gemm_i8.cu", "recon.cu", "ii_int8.cu"]
+CU_SOURCES = ["split.cu", "gemm_i8.cu", "recon.cu", "ii_int8.cu", "noalloc.cu"]
 CPP_SOURCES = ["planner.cpp", "context.cpp", "evaluation.cpp"]
 
 
