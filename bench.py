@@ -145,6 +145,20 @@ def cpu_threads() -> int:
         return os.cpu_count() or 1
 
 
+def calibrate_rows(run, threads: int, n: int, target_s: float) -> tuple[int, float]:
+    """Grows the row sample (a multiple of the thread count, at most n) until one run takes at least
+    half of target_s; returns the rows and the time of the last run. The first run warms the thread
+    pool and the copies up and is not used."""
+    rows = max(threads, 8)
+    run(rows)
+    t = run(rows)
+    while t < 0.5 * target_s and rows < n:
+        grow = min(8.0, target_s / max(t, 1e-3))
+        rows = min(n, max(rows + threads, int(rows * grow) // threads * threads))
+        t = run(rows)
+    return rows, t
+
+
 def time_cpu_dot2(a: np.ndarray, b: np.ndarray, n: int, k: int, target_s: float) -> dict:
     """Times the reference's Dot2 GEMM on the first rows of C, sized to about target_s seconds."""
     threads = cpu_threads()
@@ -161,12 +175,7 @@ def time_cpu_dot2(a: np.ndarray, b: np.ndarray, n: int, k: int, target_s: float)
         def run(rows):
             lib.ozr_dot2_prepare(a.ctypes.data, b.ctypes.data, rows, n, k)
             return lib.ozr_dot2_run(threads)
-    rows = max(threads, 8)
-    run(rows)  # warm-up: first touch of the copies and the thread pool
-    t = run(rows)
-    rows = int(min(n, max(threads, rows * target_s / max(t, 1e-3))))
-    rows = max(threads, rows // threads * threads)
-    t = run(rows)
+    rows, t = calibrate_rows(run, threads, n, target_s)
     flops = 2.0 * rows * n * k
     return {"value": flops / t / 1e12, "unit": "TFLOPS", "cores": threads, "kind": kind,
             "sample": f"Dot2 reference_gemm (evaluation/numerics.hpp) on the first {rows} rows of C "
@@ -198,11 +207,7 @@ def run_reference(args) -> None:
         def run(rows):
             lib.ozr_dot2_prepare(a.ctypes.data, b.ctypes.data, rows, n, k)
             return lib.ozr_dot2_run(threads)
-    rows = max(threads, 8)
-    run(rows)  # warm-up
-    t0 = run(rows)
-    # each step about 10 s of CPU work
-    rows = int(min(n, max(threads, rows * 10.0 / max(t0, 1e-3))))
+    rows, _ = calibrate_rows(run, threads, n, 10.0)  # each step about 10 s of CPU work
     times = []
     for _ in range(args.warmup):
         run(rows)

@@ -89,6 +89,14 @@ typedef struct oztt_ii_plan {
     double recon1_log2;            /* estimated log2 error of one reconstruction pass */
 } oztt_ii_plan;
 
+/* Plan of one Scheme I INT8 call (src/ozaki1.cpp:192-210): the number of slices p (radix 254, digits
+ * +-127, target 2^-1), the last diagonal L = p-1 kept. */
+typedef struct oztt_i_plan {
+    uint32_t M, N, K;  /* planning dimensions: m, n rounded up to 64, k to 32 */
+    int32_t p;         /* number of slices (Info::slices) */
+    int32_t auto_p;    /* 1 if p was chosen from the input (oz_fp64_p), 0 if requested */
+} oztt_i_plan;
+
 /* ---- whole calls ---------------------------------------------------------------------------- */
 
 /* Context::gemm on host row-major buffers (a: m*k, b: k*n, c: m*n; the *_len are the span sizes).
@@ -119,6 +127,21 @@ int oztt_ii_int8_run_device(int device_id, const double* a, const double* b, dou
 int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* b, double* c, uint64_t m,
                                   uint64_t n, uint64_t k, const oztt_ii_plan* plan, void* stream, double* stage_ms,
                                   char* err, size_t errlen);
+
+/* Scheme I INT8 plan (plan_issue and the slice count of src/backend/ozaki1/plan.hpp:128-250 and
+ * auto_precision.hpp:506): slices > 0 fixes p, 0 chooses it from the input. OZTT_ERUNTIME when the
+ * reference would throw (K blocking needed, Horner exponent budget exceeded). */
+int oztt_i_int8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
+                     oztt_i_plan* plan, char* err, size_t errlen);
+/* The Scheme I INT8 pipeline on host buffers (ozaki1_int8::run, src/ozaki1.cpp:192-282). */
+int oztt_i_int8_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                    const oztt_i_plan* plan, char* err, size_t errlen);
+/* The same on device buffers (lda = k, ldb = n, ldc = n); synchronises `stream`. stage_ms (NULL or 5
+ * entries) receives the device time of scale rows, scale columns, slicing, diagonal GEMMs and
+ * reconstruction. */
+int oztt_i_int8_run_device(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                           uint64_t k, const oztt_i_plan* plan, void* stream, double* stage_ms, char* err,
+                           size_t errlen);
 
 /* ---- stages (device pointers; asynchronous on `stream`) -------------------------------------- */
 
@@ -177,6 +200,22 @@ int oztt_ii_recon(const uint8_t* k_planes, uint64_t mp, uint64_t np, const int32
 void oztt_eval_inputs(double* a, double* b, uint64_t m, uint64_t n, uint64_t k, double phi, uint32_t seed);
 /* Hash of the output bit patterns (evaluation/numerics.hpp:46-57). */
 uint64_t oztt_eval_output_hash(const double* c, uint64_t count);
+
+/* Scheme I slices (slice_tf_sm8.cpp): p radix-254 digits in [-127, 127] of x * 2^delta per element;
+ * rows: A (m x k) -> [p][mp][kp]; cols: B (k x n) -> [p][np][kp] (transposed). Deltas from
+ * oztt_ii_scale_rows/cols with shift -1. */
+int oztt_i_slice_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int32_t p,
+                      int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err, size_t errlen);
+int oztt_i_slice_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta, int32_t p,
+                      int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err, size_t errlen);
+/* Diagonal products P_d = sum_{i=0..d} A_i B_{d-i}^T (int32 [p][mp][np]) on the tensor cores: the
+ * concatenated per-diagonal GEMMs of issue_panel_diagonals (src/backend/ozaki1/stages.hpp). */
+int oztt_i_diag_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp, uint64_t np, uint64_t kp, int32_t p,
+                     int32_t* out, void* stream, char* err, size_t errlen);
+/* Scheme I reconstruction (recon_tf_i32in.cpp + recon_f64_writer.cpp): C = sum_d 254^(p-1-d) P_d *
+ * 254^-(p+1) * 2^-(dA_i + dB_j), the sum exact, one rounding. */
+int oztt_i_recon(const int32_t* diag, uint64_t mp, uint64_t np, const int32_t* delta_a, const int32_t* delta_b,
+                 int32_t p, double* c, uint64_t m, uint64_t n, uint64_t ldc, void* stream, char* err, size_t errlen);
 
 /* Number of SMs and compute capability of a device (0 on success). */
 int oztt_device_info(int device_id, int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor);

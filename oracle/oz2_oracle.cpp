@@ -1101,3 +1101,313 @@ double ozo_time_dot2_rows(const double* a, const double* b, uint64_t rows, uint6
 }
 
 }  // extern "C"
+
+// =================================================================================================
+// Scheme I INT8 (src/ozaki1.cpp, src/backend/ozaki1/*): radix 254, digits +-127, target 2^-1.
+// =================================================================================================
+namespace {
+
+// Triple-float times a radix that is not a power of two, with Dekker splits (tfMulR,
+// sfpu_tf_proc.h:108-133); the constant of the split is 4097.
+void tf_mul_r(float& x0, float& x1, float& x2, float r) {
+    const float spl = 4097.0f;
+    const float lo_r = fmul(x2, r);
+    float t1 = fmul(x1, spl);
+    float t2 = fsub(t1, x1);
+    float hm = fsub(t1, t2);
+    float lm = fsub(x1, hm);
+    hm = fmul(hm, r);
+    lm = fmul(lm, r);
+    const float P1 = fadd(hm, lm);
+    float kk = fsub(P1, hm);
+    const float F1 = fsub(lm, kk);
+    t1 = fmul(x0, spl);
+    t2 = fsub(t1, x0);
+    float hh = fsub(t1, t2);
+    float lh = fsub(x0, hh);
+    hh = fmul(hh, r);
+    lh = fmul(lh, r);
+    const float P0 = fadd(hh, lh);
+    kk = fsub(P0, hh);
+    const float F0 = fsub(lh, kk);
+    const float G1 = fadd(F1, lo_r);
+    float sa, ea, sb, eb, r0, ec;
+    two_sum(P1, G1, sa, ea);
+    two_sum(F0, sa, sb, eb);
+    two_sum(P0, sb, r0, ec);
+    const float G = fadd(ea, eb);
+    x0 = r0;
+    fast_two_sum(ec, G, x1, x2);
+}
+
+// The p slices of one element (slice_tf_body.h): t *= 254; d = clamp(Rnd(t0), +-127); t0 -= d.
+void make_slices(double x, int32_t d, int p, int8_t* out, uint64_t stride) {
+    float x0, x1, x2;
+    tf_load(x, d, x0, x1, x2);
+    for (int i = 0; i < p; ++i) {
+        tf_mul_r(x0, x1, x2, 254.0f);
+        float dig = frnd(x0);
+        if (dig < -127.0f)
+            dig = -127.0f;
+        else if (dig >= 127.0f)
+            dig = 127.0f;
+        out[(uint64_t)i * stride] = (int8_t)(int)dig;
+        x0 = fsub(x0, dig);
+    }
+}
+
+// 64-bit significand and exponent of 254^-(L+2) in long double (recon_scale, ozaki1/plan.hpp:437-465).
+void radix_scale(int L, uint64_t& W, int32_t& q) {
+    long double w = 1.0L;
+    for (int i = 0; i < L + 2; ++i) w /= 254.0L;
+    int e;
+    const long double f = frexpl(w, &e);
+    W = (unsigned long long)ldexpl(f, 64);
+    q = e - 64;
+}
+
+// Rounds +-A * W * 2^total to FP64 the way pack_f64 does (f64_tf.h:189-213): top 64 bits of the
+// product, guard-bit rounding, subnormals flushed.
+double pack_like_reference(uint64_t A, uint64_t W, int32_t total, bool neg) {
+    const uint64_t hi = (uint64_t)(((unsigned __int128)A * W) >> 64);
+    const int32_t nb = (hi >> 63) ? 63 : 62;
+    int32_t exp2 = nb + 64 + total;
+    uint64_t mant;
+    bool up;
+    if (nb == 63) {
+        mant = hi >> 11;
+        up = (hi & 0x400ull) != 0;
+    } else {
+        mant = hi >> 10;
+        up = (hi & 0x200ull) != 0;
+    }
+    if (up) {
+        mant += 1;
+        if (mant >> 53) {
+            mant >>= 1;
+            exp2 += 1;
+        }
+    }
+    const uint64_t sgn = neg ? 0x8000000000000000ull : 0ull;
+    const int32_t eb = exp2 + 1023;
+    uint64_t ub;
+    if (eb <= 0)
+        ub = sgn;
+    else if (eb >= 2047)
+        ub = sgn | 0x7FF0000000000000ull;
+    else
+        ub = sgn | ((uint64_t)eb << 52) | (mant & 0x000FFFFFFFFFFFFFull);
+    double out;
+    std::memcpy(&out, &ub, 8);
+    return out;
+}
+
+// The scheme I exit (assemble_tf_f64, f64_tf.h:269-300): three limbs collected in a 64-bit window
+// 37 bits above the largest exponent, re-collected when the window cancels to zero.
+int64_t acc64_term(int32_t sig, int32_t sh) {
+    if (!sig) return 0;
+    if (sh >= 0) return (int64_t)((uint64_t)(int64_t)sig << sh);
+    if (sh <= -32) return 0;
+    const uint32_t nsh = (uint32_t)(-sh);
+    const int32_t mg = sig < 0 ? -sig : sig;
+    const int64_t q = (int64_t)(mg >> nsh);
+    return sig < 0 ? -q : q;
+}
+void dec32(uint32_t u, int32_t& e, int32_t& sig) {
+    const int32_t ee = (int32_t)((u >> 23) & 0xFFu);
+    if (ee == 0) {
+        e = 0;
+        sig = 0;
+        return;
+    }
+    e = ee;
+    const int32_t s = (int32_t)(0x800000u | (u & 0x7FFFFFu));
+    sig = (u & 0x80000000u) ? -s : s;
+}
+double assemble_tf(uint32_t hb, uint32_t mb, uint32_t lb, int32_t g, uint64_t W, int32_t qw) {
+    int32_t eh, em, el, gh, gm, gl;
+    dec32(hb, eh, gh);
+    dec32(mb, em, gm);
+    dec32(lb, el, gl);
+    if (gh == 0 && gm == 0 && gl == 0) return 0.0;
+    int32_t eb = std::max(eh, std::max(em, el));
+    const int64_t ch = acc64_term(gh, eh - eb + 37), cm = acc64_term(gm, em - eb + 37), cl = acc64_term(gl, el - eb + 37);
+    int64_t acc = ch + cm + cl;
+    if (acc == 0) {
+        if (ch) eh = gh = 0;
+        if (cm) em = gm = 0;
+        if (cl) el = gl = 0;
+        if (gh == 0 && gm == 0 && gl == 0) return 0.0;
+        eb = std::max(eh, std::max(em, el));
+        acc = acc64_term(gh, eh - eb + 37) + acc64_term(gm, em - eb + 37) + acc64_term(gl, el - eb + 37);
+    }
+    if (acc == 0) return 0.0;
+    const bool neg = acc < 0;
+    uint64_t A = neg ? (uint64_t)(-acc) : (uint64_t)acc;
+    const int32_t shA = __builtin_clzll(A);
+    A <<= shA;
+    return pack_like_reference(A, W, qw + g + (eb - 187) - shA, neg);
+}
+
+}  // namespace
+
+extern "C" {
+
+int ozo_i_slice(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, const int32_t* delta, int p,
+                int8_t* planes) {
+    const uint64_t plane = rows * cols;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < (int64_t)rows; ++r)
+        for (uint64_t c = 0; c < cols; ++c) {
+            const uint64_t idx = col_mode ? c * rows + (uint64_t)r : (uint64_t)r * cols + c;
+            make_slices(x[(uint64_t)r * ld + c], col_mode ? delta[c] : delta[r], p, planes + idx, plane);
+        }
+    return 0;
+}
+
+int ozo_i_gemm(const int8_t* ap, const int8_t* bp, int p, uint64_t M, uint64_t N, uint64_t K, int32_t* pd) {
+    int bad = 0;
+#pragma omp parallel for collapse(2) schedule(static) reduction(| : bad)
+    for (int64_t d = 0; d < (int64_t)p; ++d)
+        for (int64_t i = 0; i < (int64_t)M; ++i)
+            for (uint64_t j = 0; j < N; ++j) {
+                int64_t acc = 0;
+                for (int64_t s = 0; s <= d; ++s) {
+                    const int8_t* ar = ap + ((uint64_t)s * M + (uint64_t)i) * K;
+                    const int8_t* br = bp + ((uint64_t)(d - s) * N + j) * K;
+                    for (uint64_t kk = 0; kk < K; ++kk) acc += (int32_t)ar[kk] * (int32_t)br[kk];
+                }
+                if (acc > INT32_MAX || acc < -INT32_MAX) bad = 1;
+                pd[((uint64_t)d * M + (uint64_t)i) * N + j] = (int32_t)acc;
+            }
+    return bad;
+}
+
+int ozo_i_recon_faithful(const int32_t* pd, int p, uint64_t M, uint64_t N, const int32_t* dA, const int32_t* dB,
+                         double* c, uint64_t ldc) {
+    const int L = p - 1;
+    uint64_t W;
+    int32_t qw;
+    radix_scale(L, W, qw);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)M; ++i)
+        for (uint64_t j = 0; j < N; ++j) {
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+            for (int d = 0; d < p; ++d) {
+                if (d > 0) tf_mul_r(a0, a1, a2, 254.0f);
+                // Sign-magnitude decoding into two exact FP32 values (recon_tf_i32in.cpp decode,
+                // masks 0x7FFFFF00 / 0xFF of recon_reader_i32in.cpp:34-35).
+                const int32_t v = pd[((uint64_t)d * M + (uint64_t)i) * N + j];
+                const uint32_t mag = (uint32_t)(v < 0 ? -(int64_t)v : v);
+                const uint32_t w = (v < 0 ? 0x80000000u : 0u) | mag;
+                const float sgn = v > 0 ? 1.f : (v < 0 ? -1.f : 0.f);
+                const float vh = fmul((float)(w & 0x7FFFFF00u), sgn), vl = fmul((float)(w & 0xFFu), sgn);
+                if (d == 0) a0 = a1 = a2 = 0.f;
+                tf_add(a0, a1, a2, vh);
+                tf_add(a0, a1, a2, vl);
+            }
+            c[(uint64_t)i * ldc + j] =
+                assemble_tf(f_to_bits(a0), f_to_bits(a1), f_to_bits(a2), -(dA[i] + dB[j]), W, qw);
+        }
+    return 0;
+}
+
+int ozo_i_recon_exact(const int32_t* pd, int p, uint64_t M, uint64_t N, const int32_t* dA, const int32_t* dB,
+                      double* c, uint64_t ldc) {
+    const int L = p - 1;
+    uint64_t W;
+    int32_t qw;
+    radix_scale(L, W, qw);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)M; ++i)
+        for (uint64_t j = 0; j < N; ++j) {
+            // S = sum_d P_d 254^(L-d) by Horner in exact 256-bit two's complement.
+            Big S;
+            bool negS = false;
+            for (int d = 0; d < p; ++d) {
+                if (d > 0) S = big_mul_small(S, 254u);
+                const int32_t v = pd[((uint64_t)d * M + (uint64_t)i) * N + j];
+                Big t;
+                t.w[0] = (uint32_t)(v < 0 ? -(int64_t)v : v);
+                if (v < 0)
+                    big_sub(S, t);
+                else
+                    big_add(S, t);
+            }
+            negS = (S.w[7] >> 31) != 0;
+            if (negS) {
+                Big z;
+                big_sub(z, S);
+                S = z;
+            }
+            int top = -1;
+            for (int w = 7; w >= 0 && top < 0; --w)
+                if (S.w[w]) top = 32 * w + 31 - __builtin_clz(S.w[w]);
+            double out = 0.0;
+            if (top >= 0) {
+                // top 64 bits of |S| with a sticky bit, times W (64 bits), one rounding to 53 bits.
+                auto bit = [&](int kbit) -> uint64_t { return kbit < 0 ? 0 : (S.w[kbit >> 5] >> (kbit & 31)) & 1u; };
+                uint64_t A = 0;
+                for (int kbit = top; kbit > top - 64; --kbit) A = (A << 1) | bit(kbit);
+                bool sticky = false;
+                for (int kbit = top - 64; kbit >= 0 && !sticky; --kbit) sticky = bit(kbit) != 0;
+                const unsigned __int128 prod = (unsigned __int128)A * W;  // |S| * W / 2^(top-63)
+                // product bits: leading bit at 127 or 126; keep 64 + sticky
+                const uint64_t ph = (uint64_t)(prod >> 64), pl = (uint64_t)prod;
+                const int lead = (ph >> 63) ? 127 : 126;
+                const int sh = lead - 63;  // bits dropped below the 64-bit window
+                const uint64_t win = (uint64_t)(prod >> sh);
+                const bool st = sticky || (sh == 64 ? pl != 0 : (pl & ((1ull << sh) - 1)) != 0);
+                // value = win * 2^(sh + (top - 63) + qw - (dA+dB))
+                int32_t e2 = sh + (top - 63) + qw - (dA[i] + dB[j]);
+                // round win (64 bits, leading bit 63) to 53 bits, ties to even with the sticky bit
+                uint64_t mant = win >> 11;
+                const uint64_t rem = win & 0x7FF;
+                const bool half = rem == 0x400 && !st;
+                if (rem > 0x400 || (rem == 0x400 && st) || (half && (mant & 1))) {
+                    mant += 1;
+                    if (mant >> 53) {
+                        mant >>= 1;
+                        e2 += 1;
+                    }
+                }
+                const int lead_exp = 52 + 11 + e2;  // exponent of the leading bit of mant * 2^(11+e2)
+                if (lead_exp < -1022)
+                    out = 0.0;
+                else if (lead_exp > 1023)
+                    out = INFINITY;
+                else
+                    out = std::ldexp((double)mant, 11 + e2);
+                if (negS) out = -out;
+            }
+            c[(uint64_t)i * ldc + j] = out;
+        }
+    return 0;
+}
+
+int ozo_i_emulate(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k, int p, int exact) {
+    auto pad = [](uint64_t v, uint64_t q) { return (v + q - 1) / q * q; };
+    const uint64_t M = pad(m, 64), N = pad(n, 64), K = pad(k, 32);
+    std::vector<double> ap(M * K, 0.0), bp(K * N, 0.0);
+    for (uint64_t i = 0; i < m; ++i) std::copy_n(a + i * k, k, ap.data() + i * K);
+    for (uint64_t i = 0; i < k; ++i) std::copy_n(b + i * n, n, bp.data() + i * N);
+    std::vector<int32_t> dA(M), dB(N);
+    uint32_t fa = 0, fb = 0;
+    ozo_scale(ap.data(), M, K, K, 0, -1, nullptr, dA.data(), &fa);
+    ozo_scale(bp.data(), K, N, N, 1, -1, nullptr, dB.data(), &fb);
+    if (fa | fb) return 1;
+    std::vector<int8_t> sa((uint64_t)p * M * K), sb((uint64_t)p * N * K);
+    ozo_i_slice(ap.data(), M, K, K, 0, dA.data(), p, sa.data());
+    ozo_i_slice(bp.data(), K, N, N, 1, dB.data(), p, sb.data());
+    std::vector<int32_t> pd((uint64_t)p * M * N);
+    if (ozo_i_gemm(sa.data(), sb.data(), p, M, N, K, pd.data())) return 1;
+    std::vector<double> cp(M * N);
+    if (exact)
+        ozo_i_recon_exact(pd.data(), p, M, N, dA.data(), dB.data(), cp.data(), N);
+    else
+        ozo_i_recon_faithful(pd.data(), p, M, N, dA.data(), dB.data(), cp.data(), N);
+    for (uint64_t i = 0; i < m; ++i) std::copy_n(cp.data() + i * N, n, c + i * n);
+    return 0;
+}
+
+}  // extern "C"

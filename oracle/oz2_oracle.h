@@ -124,6 +124,26 @@ int ozo_maxrel_f128(const double* a, const double* b, const double* c, uint64_t 
 // (m x n x k problem); returns seconds.
 double ozo_time_dot2_rows(const double* a, const double* b, uint64_t rows, uint64_t n, uint64_t k, int threads);
 
+// ---- Scheme I INT8 (src/ozaki1.cpp:192-282) -------------------------------------------------------
+// Scaling with the scheme I target 2^-1 (OZ1_NSHIFT, ozaki1/format.hpp): delta = -1 - e; then p
+// radix-254 slices per element (slice_tf_body.h with tfMulR, sfpu_tf_proc.h:108-133), digits clamped
+// to +-127. planes: A [p][rows][cols], B (col_mode=1) [p][cols][rows].
+int ozo_i_slice(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, const int32_t* delta, int p,
+                int8_t* planes);
+// Diagonal products P_d = sum_{i+j=d} A_i B_j^T, d = 0..p-1 (the concatenated GEMMs of
+// issue_panel_diagonals), int32 [p][M][N].
+int ozo_i_gemm(const int8_t* ap, const int8_t* bp, int p, uint64_t M, uint64_t N, uint64_t K, int32_t* pd);
+// Reference reconstruction: triple-float Horner S = sum_d 254^(L-d) P_d (recon_tf_i32in.cpp) and the
+// FP64 assembly times 254^-(L+2) 2^-(dA+dB) (recon_f64_writer.cpp, assemble_tf_f64 of f64_tf.h).
+int ozo_i_recon_faithful(const int32_t* pd, int p, uint64_t M, uint64_t N, const int32_t* dA, const int32_t* dB,
+                         double* c, uint64_t ldc);
+// The B200 reconstruction restated: S exactly (multiword), top 64 bits times the 64-bit significand
+// of 254^-(L+2), one round-to-nearest-even, subnormal results flushed to +-0.
+int ozo_i_recon_exact(const int32_t* pd, int p, uint64_t M, uint64_t N, const int32_t* dA, const int32_t* dB,
+                      double* c, uint64_t ldc);
+// Whole scheme I INT8 pipeline with p slices (p > 0) for unpadded inputs (padded like the reference).
+int ozo_i_emulate(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k, int p, int exact);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,16 @@
+// TEST INFRASTRUCTURE — checker only, never shipped.
+//
+// Stands in for src/backend/ozaki1/format.hpp when oracle/ref_plan1.cpp compiles the reference's
+// ozaki1/auto_precision.hpp in place: that header needs only the four INT8 constants below, while the
+// real format.hpp pulls in the TT-Metalium device API. The values are the ones the real header derives
+// for OZ_FMT_ID == INT8 (ozaki1/param.hpp:47 radix 254; digit bound radix/2; target 2^-1; maxima
+// rounded up to BF16, CEIL mode 1).
+#pragma once
+#include <cstdint>
+
+namespace ozTTgemm::detail::OZTTGEMM_BACKEND_NS {
+inline constexpr uint32_t OZ1_RADIX = 254;
+inline constexpr uint32_t OZ1_DMAX = 127;
+inline constexpr int32_t OZ1_NSHIFT = -1;
+inline constexpr uint32_t OZ1_CEIL_MODE = 1;
+}  // namespace ozTTgemm::detail::OZTTGEMM_BACKEND_NS

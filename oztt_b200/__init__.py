@@ -115,6 +115,12 @@ class IIPlan(ctypes.Structure):
         return [int(self.moduli[i]) for i in range(self.S)]
 
 
+class IPlan(ctypes.Structure):
+    """oztt_i_plan: the slice count of one Scheme I INT8 call."""
+    _fields_ = [("M", ctypes.c_uint32), ("N", ctypes.c_uint32), ("K", ctypes.c_uint32), ("p", ctypes.c_int32),
+                ("auto_p", ctypes.c_int32)]
+
+
 _P = ctypes.c_void_p
 _U64 = ctypes.c_uint64
 _I32 = ctypes.c_int32
@@ -140,6 +146,13 @@ _SIGNATURES = {
     "oztt_ii_recon": [_P, _U64, _U64, _P, _P, ctypes.POINTER(IIPlan), _P, _U64, _U64, _U64, _P, _ERR, _SZ],
     "oztt_device_info": [ctypes.c_int, ctypes.POINTER(_I32), ctypes.POINTER(_I32), ctypes.POINTER(_I32)],
     "oztt_ii_padded_dims": [_U64, _U64, _U64, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
+    "oztt_i_int8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _ERR, _SZ],
+    "oztt_i_int8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _ERR, _SZ],
+    "oztt_i_int8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _P, _P, _ERR, _SZ],
+    "oztt_i_slice_rows": [_P, _U64, _U64, _U64, _P, _I32, _P, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_i_slice_cols": [_P, _U64, _U64, _U64, _P, _I32, _P, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_i_diag_gemm": [_P, _P, _U64, _U64, _U64, _I32, _P, _P, _ERR, _SZ],
+    "oztt_i_recon": [_P, _U64, _U64, _P, _P, _I32, _P, _U64, _U64, _U64, _P, _ERR, _SZ],
     "oztt_test_udiv_small": [ctypes.c_uint32, ctypes.c_uint32],
 }
 
@@ -293,6 +306,45 @@ def ii_int8_run_device_timed(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int,
     if rc != OK:
         _raise(rc, err.value)
     return list(ms)
+
+
+def i_int8_plan(a, b, m: int, n: int, k: int, slices: int = 0) -> IPlan:
+    """Scheme I INT8 plan (oztt_i_int8_plan): slices > 0 fixes p, 0 selects it from the input."""
+    av, bv = _as_f64(a, "a"), _as_f64(b, "b")
+    if av.size != m * k or bv.size != k * n:
+        raise ValueError("matrix span sizes do not match m, n, k")
+    plan = IPlan()
+    err = _errbuf()
+    rc = _lib().oztt_i_int8_plan(av.ctypes.data, bv.ctypes.data, m, n, k, slices, ctypes.byref(plan), err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return plan
+
+
+def i_int8_run(a, b, m: int, n: int, k: int, plan: IPlan, device_id: int = 0) -> np.ndarray:
+    """The Scheme I INT8 pipeline on host matrices with a given plan (oztt_i_int8_run)."""
+    av, bv = _as_f64(a, "a"), _as_f64(b, "b")
+    c = np.empty(m * n, dtype=np.float64)
+    err = _errbuf()
+    rc = _lib().oztt_i_int8_run(device_id, av.ctypes.data, bv.ctypes.data, c.ctypes.data, m, n, k, ctypes.byref(plan),
+                                err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return c
+
+
+def i_int8_run_device(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, plan: IPlan, stream: int = 0,
+                      device_id: int = 0, timed: bool = False) -> list[float] | None:
+    """The Scheme I pipeline on device pointers (oztt_i_int8_run_device); synchronises `stream`. With
+    timed=True returns the device milliseconds of scale rows, scale columns, slicing, diagonal GEMMs and
+    reconstruction."""
+    ms = (ctypes.c_double * 5)()
+    err = _errbuf()
+    rc = _lib().oztt_i_int8_run_device(device_id, a_ptr, b_ptr, c_ptr, m, n, k, ctypes.byref(plan), stream,
+                                       ms if timed else None, err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return list(ms) if timed else None
 
 
 def eval_inputs(m: int, n: int, k: int, phi: float, seed: int) -> tuple[np.ndarray, np.ndarray]:

@@ -36,8 +36,8 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompil
 CXX_FLAGS = ["-std=gnu++20", "-O2", "-fPIC", "-fno-fast-math", "-ffp-contract=off", "-pthread",
              f"-I{ROOT / 'include'}", f"-I{CUDA_HOME / 'include'}"]
 
-CU_SOURCES = ["split.cu", "gemm_i8.cu", "recon.cu", "ii_int8.cu", "noalloc.cu"]
-CPP_SOURCES = ["planner.cpp", "context.cpp", "evaluation.cpp"]
+CU_SOURCES = ["split.cu", "gemm_i8.cu", "recon.cu", "ii_int8.cu", "noalloc.cu", "scheme1.cu"]
+CPP_SOURCES = ["planner.cpp", "planner1.cpp", "context.cpp", "evaluation.cpp"]
 
 
 def _run(cmd: list[str]) -> None:

@@ -148,8 +148,22 @@ Context::~Context() = default;
 Info Context::Impl::execute(std::span<const double> a, std::span<const double> b, std::span<double> c, std::size_t m,
                             std::size_t n, std::size_t k, const Options& opt, const Checked& v) {
     std::lock_guard lock(runtime_mutex);
-    if (opt.scheme == Scheme::I)
-        throw std::runtime_error("Ozaki scheme I is not available in this build of ozTTgemm for B200");
+    if (opt.scheme == Scheme::I) {
+        oztt_i_plan plan;
+        std::string msg;
+        int rc = oztt::plan_i_int8(a.data(), b.data(), m, n, k, opt.slices, plan, msg);
+        if (rc != OZTT_OK) rethrow(rc, msg);
+        char err[512] = {0};
+        rc = oztt_i_int8_run(options.device_id, a.data(), b.data(), c.data(), m, n, k, &plan, err, sizeof err);
+        if (rc != OZTT_OK) rethrow(rc, err);
+        opened = true;
+        Info info{Scheme::I, opt.format};
+        info.slices = (std::uint32_t)plan.p;
+        info.padded_m = v.mp;
+        info.padded_n = v.np;
+        info.padded_k = v.kp;
+        return info;
+    }
     oztt_ii_plan plan;
     std::string msg;
     int rc = oztt::plan_ii_int8(a.data(), b.data(), m, n, k, opt.max_moduli, recon_code(opt.reconstruction), 0, plan, msg);

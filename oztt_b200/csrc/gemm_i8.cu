@@ -169,6 +169,39 @@ __device__ __forceinline__ void decode_tile(uint32_t tile, uint32_t tiles_m, uin
     tn = rr / gsz;
 }
 
+// Work of one output tile: the output plane, the tile row and column, and the number of 128-wide
+// K blocks. Modes 0 and 1 (scheme II): plane = modulus s, num_kb blocks of A_s and B_s. Mode 2
+// (scheme I): plane = diagonal d, taken from the largest down so that the longest tiles start first,
+// over the concatenation of the d+1 slice pairs (A_i, B_{d-i}): (d+1)*num_kb blocks.
+template <int MODE>
+__device__ __forceinline__ void tile_work(uint32_t tile, uint32_t planes, uint32_t tiles_m, uint32_t tiles_n,
+                                          uint32_t num_kb, uint32_t& plane, uint32_t& tm, uint32_t& tn,
+                                          uint32_t& kb_total) {
+    uint32_t s;
+    decode_tile(tile, tiles_m, tiles_n, s, tm, tn);
+    if constexpr (MODE == 2) {
+        plane = planes - 1u - s;
+        kb_total = (plane + 1u) * num_kb;
+    } else {
+        plane = s;
+        kb_total = num_kb;
+    }
+}
+// Coordinates (K offset, slice/modulus plane) of K block kb of a tile for A and for B.
+template <int MODE>
+__device__ __forceinline__ void kblock_coords(uint32_t kb, uint32_t plane, uint32_t num_kb, int32_t& k_el,
+                                              int32_t& pa, int32_t& pb) {
+    if constexpr (MODE == 2) {
+        const uint32_t i = kb / num_kb;
+        k_el = (int32_t)((kb - i * num_kb) * BK);
+        pa = (int32_t)i;
+        pb = (int32_t)(plane - i);
+    } else {
+        k_el = (int32_t)(kb * BK);
+        pa = pb = (int32_t)plane;
+    }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     residue_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -220,18 +253,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t filled = 0, last_phase = 0;  // per-stage bit masks of the last fill
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-                uint32_t s, tm, tn;
-                decode_tile(tile, tiles_m, tiles_n, s, tm, tn);
-                for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                uint32_t plane, tm, tn, kb_total;
+                tile_work<MODE>(tile, ec.S, tiles_m, tiles_n, num_kb, plane, tm, tn, kb_total);
+                for (uint32_t kb = 0; kb < kb_total; ++kb) {
                     if (!mbar_wait(empty_bar + stage, phase ^ 1u, abort_flag, err, ERR_WAIT_PRODUCER)) {
                         ok = false;
                         break;
                     }
+                    int32_t k_el, pa, pb;
+                    kblock_coords<MODE>(kb, plane, num_kb, k_el, pa, pb);
                     mbar_expect_tx(full_bar + stage, STAGE_BYTES);
                     const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
-                    tma_load_3d(&tmA, sa, full_bar + stage, (int32_t)(kb * BK), (int32_t)(tm * BM), (int32_t)s);
-                    tma_load_3d(&tmB, sa + A_BYTES, full_bar + stage, (int32_t)(kb * BK), (int32_t)(tn * BN),
-                                (int32_t)s);
+                    tma_load_3d(&tmA, sa, full_bar + stage, k_el, (int32_t)(tm * BM), pa);
+                    tma_load_3d(&tmB, sa + A_BYTES, full_bar + stage, k_el, (int32_t)(tn * BN), pb);
                     filled |= 1u << stage;
                     last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
@@ -249,10 +283,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                uint32_t plane, tm, tn, kb_total;
+                tile_work<MODE>(tile, ec.S, tiles_m, tiles_n, num_kb, plane, tm, tn, kb_total);
                 if (!mbar_wait(tempty_bar + acc, acc_phase ^ 1u, abort_flag, err, ERR_WAIT_MMA_EMPTY)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
-                for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                for (uint32_t kb = 0; kb < kb_total; ++kb) {
                     if (!mbar_wait(full_bar + stage, phase, abort_flag, err, ERR_WAIT_MMA_FULL)) {
                         ok = false;
                         break;
@@ -281,19 +317,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t quarter = warp & 3u;
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            uint32_t s, tm, tn;
-            decode_tile(tile, tiles_m, tiles_n, s, tm, tn);
+            uint32_t s, tm, tn, kb_total;
+            tile_work<MODE>(tile, ec.S, tiles_m, tiles_n, num_kb, s, tm, tn, kb_total);
             if (!mbar_wait(tfull_bar + acc, acc_phase, abort_flag, err, ERR_WAIT_EPILOGUE)) break;
             tc_fence_after();
             const uint64_t row = (uint64_t)tm * BM + quarter * 32u + lane;
             const uint32_t tbase = tmem_base + ((quarter * 32u) << 16) + acc * ACC_COLS;
-            const uint32_t m = ec.m[s], y = ec.y[s], mg = ec.magic[s], sh = ec.shift[s];
+            const uint32_t m = ec.m[s % OZTT_MAXS], y = ec.y[s % OZTT_MAXS], mg = ec.magic[s % OZTT_MAXS],
+                           sh = ec.shift[s % OZTT_MAXS];
 #pragma unroll 1
             for (uint32_t c = 0; c < BN; c += 32) {
                 uint32_t v[32];
                 tmem_ld32(tbase + c, v);
                 const uint64_t off = ((uint64_t)s * mp + row) * np + (uint64_t)tn * BN + c;
-                if constexpr (MODE == 0) {
+                if constexpr (MODE == 0 || MODE == 2) {
                     uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<int32_t*>(out) + off);
 #pragma unroll
                     for (int q = 0; q < 8; ++q) o[q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
@@ -410,6 +447,36 @@ void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64
         residue_gemm_kernel<1><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, out, tiles_m, tiles_n,
                                                                      (uint32_t)(kp / BK), mp, np, ec, err_word);
     }
+    OZTT_CUDA(cudaGetLastError());
+}
+
+// Scheme I diagonal products P_d = sum_{i=0..d} A_i B_{d-i}^T, d = 0..p-1, int32 [p][mp][np], from
+// slice planes A [p][mp][kp] and B [p][np][kp] (tcgen05 kind::i8, s32 accumulation over the
+// concatenated K of (d+1)*kp).
+void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp, int p,
+                      int32_t* out, int* err_word, cudaStream_t st) {
+    using namespace gemm;
+    if (mp % BM || np % BN || kp % BK || mp == 0 || np == 0 || kp == 0)
+        throw Error(OZTT_EINVAL, "diag_gemm: mp, np, kp must be positive multiples of 128, 256 and 128");
+    if (p < 1 || p > 64) throw Error(OZTT_EINVAL, "diag_gemm: the number of slices must be 1..64");
+    if ((reinterpret_cast<uintptr_t>(ap) | reinterpret_cast<uintptr_t>(bp)) & 15)
+        throw Error(OZTT_EINVAL, "diag_gemm: planes must be 16-byte aligned");
+    if (mp / BM * (np / BN) * (uint64_t)p >= (1ull << 31) || (uint64_t)p * (kp / BK) >= (1ull << 31))
+        throw Error(OZTT_EINVAL, "diag_gemm: problem too large");
+    EpiConst ec{};
+    ec.S = (uint32_t)p;
+    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p, BM);
+    const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p, BN);
+    int dev = 0, sms = 148;
+    OZTT_CUDA(cudaGetDevice(&dev));
+    OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const uint32_t tiles_m = (uint32_t)(mp / BM), tiles_n = (uint32_t)(np / BN);
+    const uint64_t num_tiles = (uint64_t)p * tiles_m * tiles_n;
+    const unsigned grid = (unsigned)std::min<uint64_t>(num_tiles, (uint64_t)sms);
+    OZTT_CUDA(cudaFuncSetAttribute(residue_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)SMEM_BYTES));
+    residue_gemm_kernel<2><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, out, tiles_m, tiles_n, (uint32_t)(kp / BK),
+                                                                 mp, np, ec, err_word);
     OZTT_CUDA(cudaGetLastError());
 }
 

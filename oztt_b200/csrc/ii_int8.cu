@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "oztt_common.cuh"
+#include "runtime.cuh"
 
 namespace oztt {
 
@@ -31,8 +32,6 @@ void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64
                          const oztt_ii_plan& p, int mode, void* out, int* err_word, cudaStream_t st);
 void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB,
                   const oztt_ii_plan& p, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st);
-
-namespace {
 
 // Selects the device, checks that it is a Blackwell data-centre GPU (compute capability 10.x, the
 // sm_100a code in this library) and keeps the stream-ordered pool's memory between calls.
@@ -59,32 +58,6 @@ void open_device(int device_id) {
     }
 }
 
-// Stream-ordered device buffer, released on the stream when it goes out of scope.
-struct DevBuf {
-    void* p = nullptr;
-    cudaStream_t st;
-    explicit DevBuf(cudaStream_t s) : st(s) {}
-    DevBuf(cudaStream_t s, size_t bytes) : st(s) { alloc(bytes); }
-    ~DevBuf() {
-        if (p) cudaFreeAsync(p, st);
-    }
-    void alloc(size_t bytes) {
-        const cudaError_t e = cudaMallocAsync(&p, std::max<size_t>(bytes, 256), st);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            p = nullptr;
-            throw Error(OZTT_ERUNTIME, "device memory allocation of " + std::to_string(bytes) +
-                                           " bytes failed: " + cudaGetErrorString(e));
-        }
-    }
-    template <class T>
-    T* as() const {
-        return reinterpret_cast<T*>(p);
-    }
-    DevBuf(const DevBuf&) = delete;
-    DevBuf& operator=(const DevBuf&) = delete;
-};
-
 void check_plan(const oztt_ii_plan& p) {
     if (p.S < 1 || p.S > OZTT_MAXS) throw Error(OZTT_EINVAL, "plan: the number of moduli must be 1..24");
     if (p.nd < 3 || p.nd > 5) throw Error(OZTT_EINVAL, "plan: the number of digits must be 3..5");
@@ -105,7 +78,6 @@ void check_flags(uint32_t flags, int gemm_err) {
     }
 }
 
-}  // namespace
 
 // The device pipeline on device buffers (row-major, lda = k, ldb = n, ldc = n).
 // stage_ms (optional, 6 entries): device time of scale rows, scale cols, split rows, split cols, residue

@@ -46,24 +46,6 @@ constexpr int kTable[] = {255, 254, 253, 251, 247, 241, 239, 233, 229, 227, 223,
                           211, 199, 197, 193, 191, 181, 179, 173, 167, 163, 157, 151};
 constexpr int kTableMin = 151;
 
-// Runs f(begin, end) over [0, n) on up to hardware_concurrency threads.
-template <class F>
-void parallel_ranges(uint64_t n, F&& f) {
-    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-    const uint64_t nt = std::min<uint64_t>(hw, std::max<uint64_t>(1, n / 64));
-    if (nt <= 1) {
-        f(0, n);
-        return;
-    }
-    std::vector<std::thread> th;
-    th.reserve(nt);
-    for (uint64_t t = 0; t < nt; ++t) {
-        const uint64_t b = n * t / nt, e = n * (t + 1) / nt;
-        th.emplace_back([&f, b, e] { f(b, e); });
-    }
-    for (auto& x : th) x.join();
-}
-
 bool fits_int32(uint32_t K, int m) {
     const unsigned __int128 r = (unsigned)(m / 2);
     return (unsigned __int128)K * r * r <= (((unsigned __int128)1 << kAccBits) - 1);
@@ -202,6 +184,42 @@ double pow2_normalizer(const double* v, uint64_t rows, uint64_t cols, uint64_t l
     return std::ldexp(1.0, e);
 }
 
+double product_norm_estimate(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
+                             double rgA, double rgB) {
+    // Hutchinson estimate of ||C||_F^2 with 8 Gaussian vectors of the padded length N from
+    // mt19937(12345); the largest sample is dropped and the mean divided by 1 + 2 sqrt(2/8).
+    // Padding rows and columns contribute exact zeros, so only the real block is traversed.
+    const uint32_t L = 8;
+    std::mt19937 rng(12345);
+    std::normal_distribution<double> normal(0.0, 1.0);
+    std::vector<double> g(N), y(k, 0.0), s(m);
+    double cs2 = 0, cmax = 0;
+    for (uint32_t l = 0; l < L; ++l) {
+        for (uint32_t j = 0; j < N; ++j) g[j] = normal(rng);
+        parallel_ranges(k, [&](uint64_t r0, uint64_t r1) {
+            for (uint64_t r = r0; r < r1; ++r) {
+                long double acc = 0;
+                const double* p = b + r * n;
+                for (uint64_t j = 0; j < n; ++j) acc += (long double)(p[j] * rgB) * g[j];
+                y[r] = (double)acc;
+            }
+        });
+        parallel_ranges(m, [&](uint64_t r0, uint64_t r1) {
+            for (uint64_t i = r0; i < r1; ++i) {
+                long double acc = 0;
+                const double* p = a + i * k;
+                for (uint64_t c = 0; c < k; ++c) acc += (long double)(p[c] * rgA) * y[c];
+                s[i] = (double)acc;
+            }
+        });
+        double q = 0;
+        for (uint64_t i = 0; i < m; ++i) q += s[i] * s[i];
+        cs2 += q;
+        cmax = std::max(cmax, q);
+    }
+    return (cs2 - cmax) / (L - 1) / (1.0 + 2.0 * std::sqrt(2.0 / (double)L));
+}
+
 PolicyStats measure_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
                                  uint32_t K) {
     PolicyStats st;
@@ -252,40 +270,7 @@ PolicyStats measure_policy_stats(const double* a, const double* b, uint64_t m, u
             st.nB += s2[c];
         }
     }
-    // Hutchinson estimate of ||C||_F^2 with 8 Gaussian vectors of the padded length N from
-    // mt19937(12345); the largest sample is dropped and the mean divided by 1 + 2 sqrt(2/8).
-    // Padding rows and columns contribute exact zeros, so only the real block is traversed.
-    {
-        const uint32_t L = 8;
-        std::mt19937 rng(12345);
-        std::normal_distribution<double> normal(0.0, 1.0);
-        std::vector<double> g(N), y(K, 0.0), s(m);
-        double cs2 = 0, cmax = 0;
-        for (uint32_t l = 0; l < L; ++l) {
-            for (uint32_t j = 0; j < N; ++j) g[j] = normal(rng);
-            parallel_ranges(k, [&](uint64_t r0, uint64_t r1) {
-                for (uint64_t r = r0; r < r1; ++r) {
-                    long double acc = 0;
-                    const double* p = b + r * n;
-                    for (uint64_t j = 0; j < n; ++j) acc += (long double)(p[j] * rgB) * g[j];
-                    y[r] = (double)acc;
-                }
-            });
-            parallel_ranges(m, [&](uint64_t r0, uint64_t r1) {
-                for (uint64_t i = r0; i < r1; ++i) {
-                    long double acc = 0;
-                    const double* p = a + i * k;
-                    for (uint64_t c = 0; c < k; ++c) acc += (long double)(p[c] * rgA) * y[c];
-                    s[i] = (double)acc;
-                }
-            });
-            double q = 0;
-            for (uint64_t i = 0; i < m; ++i) q += s[i] * s[i];
-            cs2 += q;
-            cmax = std::max(cmax, q);
-        }
-        st.nC = (cs2 - cmax) / (L - 1) / (1.0 + 2.0 * std::sqrt(2.0 / (double)L));
-    }
+    st.nC = product_norm_estimate(a, b, m, n, k, N, rgA, rgB);
     st.measured = true;
     return st;
 }

@@ -1,13 +1,41 @@
 // SPDX-License-Identifier: Apache-2.0
-// Scheme II INT8 planner (host side); see planner.cpp.
+// Host planners: Scheme II INT8 (planner.cpp) and Scheme I INT8 (planner1.cpp).
 #pragma once
+#include <algorithm>
 #include <cstdint>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "oztt_cuda.h"
 
 namespace oztt {
+
+// Runs f(begin, end) over [0, n) on up to hardware_concurrency threads.
+template <class F>
+void parallel_ranges(uint64_t n, F&& f) {
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const uint64_t nt = std::min<uint64_t>(hw, std::max<uint64_t>(1, n / 64));
+    if (nt <= 1) {
+        f(0, n);
+        return;
+    }
+    std::vector<std::thread> th;
+    th.reserve(nt);
+    for (uint64_t t = 0; t < nt; ++t) {
+        const uint64_t b = n * t / nt, e = n * (t + 1) / nt;
+        th.emplace_back([&f, b, e] { f(b, e); });
+    }
+    for (auto& x : th) x.join();
+}
+
+// Power of two by which a matrix is divided before sums of squares are formed: 2^e for the exponent e
+// of its largest magnitude, clamped to [-1000, 1000] (oz_pow2_scale, src/backend/common/norm_estimate.hpp:20-28).
+double pow2_normalizer(const double* v, uint64_t rows, uint64_t cols, uint64_t ld);
+// Low-biased Hutchinson estimate of ||(rgA A)(rgB B)||_F^2 for row-major a (m x k), b (k x n) with random
+// vectors of the padded length N (estimate_product_norm, src/backend/common/norm_estimate.hpp:48-73).
+double product_norm_estimate(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
+                             double rgA, double rgB);
 
 struct ModuliChoice {
     bool ok = false, acc_ok = true;
@@ -33,5 +61,12 @@ void fill_crt_constants(const std::vector<int>& mods, oztt_ii_plan& p);
 // The whole plan; returns an OZTT_* code and a message.
 int plan_ii_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
                  int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan& p, std::string& err);
+
+// Scheme I INT8 (planner1.cpp): the slice count oz_fp64_p selects for row-major a (m x k), b (k x n)
+// with padded planning dimensions M, N, K; and the whole plan (slices > 0 fixes p).
+int select_slices_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,
+                       uint32_t K);
+int plan_i_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
+                oztt_i_plan& p, std::string& err);
 
 }  // namespace oztt

@@ -7,9 +7,9 @@
 // recon_elem.h / f64_tf.h:296-400. The reference evaluates frac = sum_s k_s/m_s mod 1 in FP32
 // triple-float because its device has no FP64 (absolute error about 2^-67 for one pass), folds it in
 // 128-bit fixed point and multiplies by M*2^-2b. Here the same quantity is computed without error:
-//     X  = sum_s k_s * (M/m_s)                  (multiword integer, NW 32-bit words, mod 2^(32 NW))
-//     q  = rint(sum_s k_s * (1/m_s))            (FP64; the window margin |C'|/M <= 1/2 - 2^-31.4
-//                                                makes q = round(X/M) exact)
+//     X  = sum_s k_s * (M/m_s)                  (multiword integer, NW 32-bit words, X < S*M < 2^(32 NW))
+//     q  = rint(top 64 bits of X * 2^t / M)     (FP64; the window margin |C'|/M <= 1/2 - 2^-31.4
+//                                                makes this q = round(X/M) exactly)
 //     C' = X - q*M                              (|C'| < M/2, two's complement in NW words)
 //     C  = C' * 2^(2 shift - dA_i - dB_j - 2b)  (one round-to-nearest-even; below 2^-1022 -> +-0,
 //                                                as pack_f64 of the reference flushes)
@@ -28,22 +28,32 @@ struct ReconConst {
     int32_t two_b, sh2;
     uint32_t M[8];
     uint32_t Q[OZTT_MAXS][8];
-    double invm[OZTT_MAXS];
+    double top_scale;  // 2^(32 (NW-3)) / M: X/M from the top three words of X
 };
 
-// Finishes one element from its column sums acc (X = sum_w acc[w] 2^(32w)) and fr ~ X/M.
+// Finishes one element from its column sums acc (X = sum_w acc[w] 2^(32w)).
 template <int NW>
-__device__ __forceinline__ double crt_finish(const uint64_t (&acc)[NW], double fr, int32_t g, const ReconConst& rc) {
-    const uint32_t q = (uint32_t)rint(fr);
-    // y = X - q*M modulo 2^(32 NW), carrying the sum of the columns and the subtraction together.
-    uint32_t y[NW];
+__device__ __forceinline__ double crt_finish(const uint64_t (&acc)[NW], int32_t g, const ReconConst& rc) {
+    // X in words (carry the column sums).
+    uint32_t x[NW];
     uint64_t cx = 0;
-    int64_t br = 0;
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
         const uint64_t sx = acc[w] + cx;
+        x[w] = (uint32_t)sx;
         cx = sx >> 32;
-        const int64_t d = (int64_t)(uint32_t)sx - (int64_t)((uint64_t)q * rc.M[w]) + br;
+    }
+    // q = round(X/M) from the top three words of X: the dropped words change X/M by less than
+    // 2^(32(NW-3))/M <= 2^-40, far inside the window margin.
+    const double xtop = fma(__ull2double_rn(((uint64_t)x[NW - 1] << 32) | x[NW - 2]), 4294967296.0,
+                            (double)x[NW - 3]);
+    const uint32_t q = (uint32_t)rint(xtop * rc.top_scale);
+    // y = X - q*M modulo 2^(32 NW).
+    uint32_t y[NW];
+    int64_t br = 0;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        const int64_t d = (int64_t)x[w] - (int64_t)((uint64_t)q * rc.M[w]) + br;
         y[w] = (uint32_t)d;
         br = d >> 32;
     }
@@ -101,22 +111,17 @@ __global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ 
         const uint64_t i = t / nq, j0 = (t - i * nq) << 2;
         const uint8_t* base = kp + i * np + j0;
         uint64_t acc[4][NW];
-        double fr[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            fr[e] = 0.0;
+        for (int e = 0; e < 4; ++e)
 #pragma unroll
             for (int w = 0; w < NW; ++w) acc[e][w] = 0;
-        }
         for (uint32_t s = 0; s < rc.S; ++s) {
             const uint32_t kw = __ldg(reinterpret_cast<const uint32_t*>(base + s * plane));
-            const double im = rc.invm[s];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const uint32_t k = (kw >> (8 * e)) & 0xFFu;
 #pragma unroll
                 for (int w = 0; w < NW; ++w) acc[e][w] += (uint64_t)k * rc.Q[s][w];
-                fr[e] = fma((double)k, im, fr[e]);
             }
         }
         const int32_t da = __ldg(dA + i);
@@ -125,7 +130,7 @@ __global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ 
         for (int e = 0; e < 4; ++e) {
             if (j0 + e < n) {
                 const int32_t g = rc.sh2 - (da + __ldg(dB + j0 + e));
-                crow[e] = crt_finish<NW>(acc[e], fr[e], g, rc);
+                crow[e] = crt_finish<NW>(acc[e], g, rc);
             }
         }
     }
@@ -173,9 +178,19 @@ void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA
         for (int t = 0; t < p.S; ++t)
             if (t != s) q = big_mul(q, (uint32_t)p.moduli[t]);
         for (int w = 0; w < 8; ++w) rc.Q[s][w] = q.w[w];
-        rc.invm[s] = 1.0 / (double)p.moduli[s];
     }
-    const int nw = std::max(1, (big_bits(M) + 31) / 32);
+    // X = sum_s k_s (M/m_s) < S*M must fit the words, and the three top words must carry X/M to
+    // better than the window margin: 32 (NW-3) <= bits(M) - 40 holds for this choice of NW.
+    int sbits = 0;
+    while ((1 << sbits) < p.S) ++sbits;
+    const int nw = std::max(3, (big_bits(M) + sbits + 31) / 32);
+    if (nw > 8) throw Error(OZTT_EINVAL, "recon: the product of the moduli is too large");
+    if (32 * (nw - 3) > big_bits(M) - 40) throw Error(OZTT_EINVAL, "recon: the moduli product is too small");
+    {
+        long double Ml = 0;
+        for (int w = 7; w >= 0; --w) Ml = Ml * 4294967296.0L + (long double)M.w[w];
+        rc.top_scale = (double)(ldexpl(1.0L, 32 * (nw - 3)) / Ml);
+    }
     const uint64_t total = m * ((n + 3) / 4);
     if (total == 0) return;
     int dev = 0, sms = 148;
@@ -183,9 +198,7 @@ void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA
     OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sms * 16);
     switch (nw) {
-    case 1:
-    case 2:
-    case 3:
+    case 3: recon_kernel<3><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
     case 4: recon_kernel<4><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
     case 5: recon_kernel<5><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
     case 6: recon_kernel<6><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;

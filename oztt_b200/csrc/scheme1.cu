@@ -1,0 +1,481 @@
+// SPDX-License-Identifier: Apache-2.0
+//
+// Ozaki scheme I with INT8 slices on sm_100a (reference: src/ozaki1.cpp:192-282).
+//
+//   scale        the scheme II scaling kernels with the scheme I target: delta = -1 - e
+//                (OZ1_NSHIFT = -1, rounding the maxima up: ozaki1/format.hpp, CEIL mode 1)
+//   slice        p radix-254 slices per element, digits in [-127, 127]: t *= 254 (Dekker-split
+//                triple-float product, tfMulR of sfpu_tf_proc.h:108-133), d = clamp(rint(t0)),
+//                t0 -= d (slice_tf_body.h). The binary32 operation sequence is the reference's,
+//                one PTX instruction with round-to-nearest-even and flush-to-zero at a time, so the
+//                slices are bit-identical. Layout: A [p][mp][kp], B transposed [p][np][kp] (int8).
+//   diagonals    P_d = sum_{i=0..d} A_i B_{d-i}^T for d = 0..p-1 on the tensor cores (gemm_i8.cu,
+//                mode 2): the concatenated GEMMs of issue_panel_diagonals with K_eff = (d+1) K,
+//                exact in s32 because the planner keeps (L+1) K 127^2 < 2^31.
+//   recon        S = sum_d P_d 254^(L-d) exactly (Horner in 192-bit two's complement), then
+//                C = S * 254^-(L+2) * 2^-(dA_i + dB_j): the top 64 bits of |S| times the 64-bit
+//                significand W of 254^-(L+2) (the reference's long double constant, recon_scale in
+//                ozaki1/plan.hpp:437-465), one round-to-nearest-even, results below 2^-1022 -> +-0.
+//                The reference accumulates S in binary32 triple-float (recon_tf_i32in.cpp) and
+//                assembles in a 64-bit window (assemble_tf_f64); the B200 result is within that
+//                error of the reference's.
+#include <algorithm>
+
+#include "oztt_common.cuh"
+
+namespace oztt {
+
+namespace {
+
+// Triple-float times 254 with Dekker splits (the constant of the split is 4097), in the
+// reference's operation order.
+__device__ __forceinline__ void two_sum1(float x, float y, float& s, float& e) {
+    s = f32_add(x, y);
+    const float bb = f32_sub(s, x);
+    const float a = f32_sub(x, f32_sub(s, bb));
+    e = f32_add(a, f32_sub(y, bb));
+}
+__device__ __forceinline__ void tf_mul_254(float& x0, float& x1, float& x2) {
+    const float r = 254.0f, spl = 4097.0f;
+    const float lo_r = f32_mul(x2, r);
+    float t1 = f32_mul(x1, spl);
+    float t2 = f32_sub(t1, x1);
+    float hm = f32_sub(t1, t2);
+    float lm = f32_sub(x1, hm);
+    hm = f32_mul(hm, r);
+    lm = f32_mul(lm, r);
+    const float P1 = f32_add(hm, lm);
+    float kk = f32_sub(P1, hm);
+    const float F1 = f32_sub(lm, kk);
+    t1 = f32_mul(x0, spl);
+    t2 = f32_sub(t1, x0);
+    float hh = f32_sub(t1, t2);
+    float lh = f32_sub(x0, hh);
+    hh = f32_mul(hh, r);
+    lh = f32_mul(lh, r);
+    const float P0 = f32_add(hh, lh);
+    kk = f32_sub(P0, hh);
+    const float F0 = f32_sub(lh, kk);
+    const float G1 = f32_add(F1, lo_r);
+    float sa, ea, sb, eb, r0, ec;
+    two_sum1(P1, G1, sa, ea);
+    two_sum1(F0, sa, sb, eb);
+    two_sum1(P0, sb, r0, ec);
+    const float G = f32_add(ea, eb);
+    x0 = r0;
+    x1 = f32_add(ec, G);
+    x2 = f32_sub(G, f32_sub(x1, ec));
+}
+
+// FP64 x*2^d -> triple-float (the split of split.cu, repeated here so that this file stands alone).
+__device__ __forceinline__ void tf_load1(double xv, int32_t d, float& x0, float& x1, float& x2) {
+    const uint64_t bits = (uint64_t)__double_as_longlong(xv);
+    const uint32_t w1 = (uint32_t)(bits >> 32), w0 = (uint32_t)bits;
+    const uint32_t sgn = w1 & 0x80000000u;
+    const int32_t E = (int32_t)((w1 >> 20) & 0x7FFu);
+    uint32_t hi, braw, craw, s;
+    if (E == 0) {
+        hi = 0u;
+        braw = craw = 0x4B000000u;
+        s = 0u;
+    } else {
+        uint32_t top = 0x400000u | ((w1 & 0xFFFFFu) << 2) | (w0 >> 30);
+        const uint32_t low30 = w0 & 0x3FFFFFFFu;
+        int32_t rest = (int32_t)low30;
+        if (low30 >= 0x20000000u) {
+            top += 1u;
+            rest = (int32_t)low30 - 0x40000000;
+        }
+        const int32_t mid = rest >> 7;
+        const uint32_t lo = (uint32_t)rest & 0x7Fu;
+        const int32_t elsb = E - 1075 + d;
+        const bool carry = top == 0x800000u;
+        const int32_t eh = elsb + (carry ? 180 : 179);
+        const uint32_t mh = carry ? 0u : ((top << 1) & 0x7FFFFFu);
+        const int32_t es = elsb + 134;
+        hi = (eh > 0 && eh < 255) ? (sgn | ((uint32_t)eh << 23) | mh) : 0u;
+        s = (es > 0 && es < 255) ? (sgn | ((uint32_t)es << 23)) : 0u;
+        braw = 0x4B000000u | ((uint32_t)(mid + 0x400000) & 0x7FFFFFu);
+        craw = 0x4B000000u | lo;
+    }
+    const float sc = __uint_as_float(s);
+    x0 = __uint_as_float(hi);
+    x1 = f32_mul(f32_add(__uint_as_float(braw), -12582912.0f), sc);
+    x2 = f32_mul(f32_mul(f32_add(__uint_as_float(craw), -8388608.0f), sc), 0.0078125f);
+}
+
+__device__ __forceinline__ uint32_t next_digit(float& x0, float& x1, float& x2) {
+    tf_mul_254(x0, x1, x2);
+    float d = f32_rint(x0);
+    d = d < -127.0f ? -127.0f : (d >= 127.0f ? 127.0f : d);
+    x0 = f32_sub(x0, d);
+    return (uint32_t)__float2int_rn(d) & 0xFFu;
+}
+
+// 16 elements -> p slices of 16 bytes each; element states stay in registers across the slices.
+__device__ __forceinline__ void slice16(const double (&x)[16], int32_t d, int p, int8_t* dst, uint64_t plane) {
+    float s0[16], s1[16], s2[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) tf_load1(x[e], d, s0[e], s1[e], s2[e]);
+    for (int i = 0; i < p; ++i) {
+        uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int e = 0; e < 16; ++e) w[e >> 2] |= next_digit(s0[e], s1[e], s2[e]) << (8 * (e & 3));
+        *reinterpret_cast<uint4*>(dst + (uint64_t)i * plane) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+__global__ void __launch_bounds__(256) slice_rows_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
+                                                         uint64_t lda, const int32_t* __restrict__ delta, int p,
+                                                         int8_t* __restrict__ planes, uint64_t mp, uint64_t kp) {
+    const uint64_t chunks = kp >> 4, total = mp * chunks, plane = mp * kp;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t row = t / chunks, k0 = (t - row * chunks) << 4;
+        const bool in_row = row < m;
+        const double* src = a + row * lda + k0;
+        double x[16];
+        if (in_row && k0 + 16 <= k && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+                const double2 v = __ldg(reinterpret_cast<const double2*>(src + e));
+                x[e] = v.x;
+                x[e + 1] = v.y;
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) x[e] = (in_row && k0 + e < k) ? __ldg(src + e) : 0.0;
+        }
+        slice16(x, in_row ? __ldg(delta + row) : 0, p, planes + row * kp + k0, plane);
+    }
+}
+
+__global__ void __launch_bounds__(256) slice_cols_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
+                                                         uint64_t ldb, const int32_t* __restrict__ delta, int p,
+                                                         int8_t* __restrict__ planes, uint64_t np, uint64_t kp) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t col_groups = np >> 4, total = col_groups * (kp >> 5), plane = np * kp;
+    for (uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total;
+         w += ((uint64_t)gridDim.x * blockDim.x) >> 5) {
+        const uint64_t cg = w % col_groups, rg = w / col_groups;
+        const uint64_t col = (cg << 4) + (lane & 15), r0 = (rg << 5) + ((lane >> 4) << 4);
+        const bool in_col = col < n;
+        double x[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) x[e] = (in_col && r0 + e < k) ? __ldg(b + (r0 + e) * ldb + col) : 0.0;
+        slice16(x, in_col ? __ldg(delta + col) : 0, p, planes + col * kp + r0, plane);
+    }
+}
+
+// ---- exact Horner reconstruction ------------------------------------------------------------
+constexpr int HW = 6;  // 192-bit two's complement: |S| < 2^31 * 254^(p-1) < 2^151 for p <= 16
+
+struct HornerConst {
+    int32_t p;
+    uint64_t W;   // 64-bit significand of 254^-(L+2)
+    int32_t qw;   // its exponent
+};
+
+__device__ __forceinline__ double horner_element(const int32_t* pd, uint64_t plane, const HornerConst& hc,
+                                                 int32_t g) {
+    uint32_t s[HW];
+#pragma unroll
+    for (int w = 0; w < HW; ++w) s[w] = 0;
+    for (int d = 0; d < hc.p; ++d) {
+        // s = s * 254 + P_d  (mod 2^192)
+        const int32_t v = __ldg(pd + (uint64_t)d * plane);
+        uint64_t carry = 0;
+#pragma unroll
+        for (int w = 0; w < HW; ++w) {
+            const uint64_t t = (uint64_t)s[w] * 254u + carry;
+            s[w] = (uint32_t)t;
+            carry = t >> 32;
+        }
+        int64_t add = v;
+#pragma unroll
+        for (int w = 0; w < HW; ++w) {
+            const int64_t t = (int64_t)s[w] + add;
+            s[w] = (uint32_t)t;
+            add = t >> 32;
+        }
+    }
+    const bool neg = (s[HW - 1] >> 31) != 0;
+    if (neg) {
+        uint32_t c = 1;
+#pragma unroll
+        for (int w = 0; w < HW; ++w) {
+            const uint64_t t = (uint64_t)(~s[w]) + c;
+            s[w] = (uint32_t)t;
+            c = (uint32_t)(t >> 32);
+        }
+    }
+    int hw = -1;
+#pragma unroll
+    for (int w = 0; w < HW; ++w)
+        if (s[w]) hw = w;
+    if (hw < 0) return 0.0;
+    uint32_t w0 = 0, w1 = 0, w2 = 0;
+    bool sticky = false;
+#pragma unroll
+    for (int w = 0; w < HW; ++w) {
+        if (w == hw) w0 = s[w];
+        if (w == hw - 1) w1 = s[w];
+        if (w == hw - 2) w2 = s[w];
+        if (w < hw - 2 && s[w]) sticky = true;
+    }
+    const int lz = __clz(w0);
+    const uint64_t top = ((uint64_t)w0 << 32) | w1;
+    const uint64_t A = lz ? ((top << lz) | (w2 >> (32 - lz))) : top;
+    sticky = sticky || (lz ? (w2 << lz) : w2) != 0u;
+    const int topbit = 32 * hw + 31 - lz;
+    // A * W, 128 bits; keep a 64-bit window with its leading bit at 63, plus a sticky bit.
+    const uint64_t ph = __umul64hi(A, hc.W), pl = A * hc.W;
+    const int lead = (ph >> 63) ? 127 : 126;
+    const int sh = lead - 63;  // 63 or 64
+    uint64_t win;
+    bool st;
+    if (sh == 64) {
+        win = ph;
+        st = sticky || pl != 0;
+    } else {
+        win = (ph << 1) | (pl >> 63);
+        st = sticky || (pl << 1) != 0;
+    }
+    int32_t e2 = sh + (topbit - 63) + hc.qw + g;
+    uint64_t mant = win >> 11;
+    const uint64_t rem = win & 0x7FFull;
+    if (rem > 0x400ull || (rem == 0x400ull && (st || (mant & 1ull)))) {
+        mant += 1;
+        if (mant >> 53) {
+            mant >>= 1;
+            e2 += 1;
+        }
+    }
+    const int lead_exp = 63 + e2;
+    double r;
+    if (lead_exp < -1022)
+        r = 0.0;
+    else if (lead_exp > 1023)
+        r = __longlong_as_double(0x7FF0000000000000ll);
+    else
+        r = ldexp((double)mant, 11 + e2);
+    return neg ? -r : r;
+}
+
+__global__ void __launch_bounds__(256) horner_kernel(const int32_t* __restrict__ pd, uint64_t mp, uint64_t np,
+                                                     const int32_t* __restrict__ dA, const int32_t* __restrict__ dB,
+                                                     double* __restrict__ c, uint64_t m, uint64_t n, uint64_t ldc,
+                                                     const HornerConst hc) {
+    const uint64_t total = m * n, plane = mp * np;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t i = t / n, j = t - i * n;
+        const int32_t g = -(__ldg(dA + i) + __ldg(dB + j));
+        c[i * ldc + j] = horner_element(pd + i * np + j, plane, hc, g);
+    }
+}
+
+int sm_count() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+}  // namespace
+
+// 64-bit significand and exponent of 254^-(L+2), from the long double quotient as the reference
+// forms it.
+void scheme1_radix_scale(int p, uint64_t& W, int32_t& qw) {
+    long double w = 1.0L;
+    for (int i = 0; i < p + 1; ++i) w /= 254.0L;
+    int e;
+    const long double f = frexpl(w, &e);
+    W = (unsigned long long)ldexpl(f, 64);
+    qw = e - 64;
+}
+
+void launch_slice_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int p,
+                       int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
+    if (mp % 16 || kp % 16) throw Error(OZTT_EINVAL, "slice_rows: padded dimensions must be multiples of 16");
+    const uint64_t total = mp * (kp / 16);
+    if (!total) return;
+    slice_rows_kernel<<<(unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 32), 256, 0, st>>>(
+        a, m, k, lda, delta, p, planes, mp, kp);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void launch_slice_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta, int p,
+                       int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
+    if (np % 16 || kp % 32) throw Error(OZTT_EINVAL, "slice_cols: np must be a multiple of 16 and kp of 32");
+    const uint64_t warps = (np / 16) * (kp / 32);
+    if (!warps) return;
+    slice_cols_kernel<<<(unsigned)std::min<uint64_t>((warps + 7) / 8, (uint64_t)sm_count() * 32), 256, 0, st>>>(
+        b, k, n, ldb, delta, p, planes, np, kp);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void launch_horner(const int32_t* pd, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB, int p,
+                   double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st) {
+    if (p < 1 || p > 16) throw Error(OZTT_EINVAL, "horner: the number of slices must be 1..16");
+    HornerConst hc{};
+    hc.p = p;
+    scheme1_radix_scale(p, hc.W, hc.qw);
+    const uint64_t total = m * n;
+    if (!total) return;
+    horner_kernel<<<(unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 16), 256, 0, st>>>(
+        pd, mp, np, dA, dB, c, m, n, ldc, hc);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+}  // namespace oztt
+
+// ---- pipeline and C ABI ---------------------------------------------------------------------------
+#include "runtime.cuh"
+
+namespace oztt {
+
+void launch_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t shift, int32_t* delta,
+                       uint16_t* bfmax, uint32_t* flags, cudaStream_t st);
+void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
+                       uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax, cudaStream_t st);
+void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp, int p,
+                      int32_t* out, int* err_word, cudaStream_t st);
+
+void run_i_int8_device(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k, int p,
+                       cudaStream_t st, double* stage_ms) {
+    if (p < 1 || p > 16) throw Error(OZTT_EINVAL, "scheme I: the number of slices must be 1..16 for INT8");
+    const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
+    const uint64_t P = (uint64_t)p;
+    DevBuf dA(st, mp * 4), dB(st, np * 4), colmax(st, n * 8), words(st, 16);
+    DevBuf sa(st, P * mp * kp), sb(st, P * np * kp), pd(st, P * mp * np * 4);
+    OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
+    uint32_t* flags = words.as<uint32_t>();
+    int* gemm_err = words.as<int>() + 1;
+    cudaEvent_t ev[6] = {};
+    struct Events {
+        cudaEvent_t* e;
+        ~Events() {
+            for (int i = 0; i < 6; ++i)
+                if (e[i]) cudaEventDestroy(e[i]);
+        }
+    } events{ev};
+    if (stage_ms)
+        for (auto& e : ev) OZTT_CUDA(cudaEventCreate(&e));
+    auto mark = [&](int i) {
+        if (stage_ms) OZTT_CUDA(cudaEventRecord(ev[i], st));
+    };
+    mark(0);
+    launch_scale_rows(a, m, k, k, -1, dA.as<int32_t>(), nullptr, flags, st);
+    mark(1);
+    launch_scale_cols(b, k, n, n, -1, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
+    mark(2);
+    launch_slice_rows(a, m, k, k, dA.as<int32_t>(), p, sa.as<int8_t>(), mp, kp, st);
+    launch_slice_cols(b, k, n, n, dB.as<int32_t>(), p, sb.as<int8_t>(), np, kp, st);
+    mark(3);
+    launch_diag_gemm(sa.as<int8_t>(), sb.as<int8_t>(), mp, np, kp, p, pd.as<int32_t>(), gemm_err, st);
+    mark(4);
+    launch_horner(pd.as<int32_t>(), mp, np, dA.as<int32_t>(), dB.as<int32_t>(), p, c, m, n, n, st);
+    mark(5);
+    uint32_t host_words[2] = {0, 0};
+    OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
+    OZTT_CUDA(cudaStreamSynchronize(st));
+    if (stage_ms)
+        for (int i = 0; i < 5; ++i) {
+            float ms = 0;
+            OZTT_CUDA(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+            stage_ms[i] = ms;
+        }
+    check_flags(host_words[0], (int)host_words[1]);
+}
+
+void run_i_int8_host(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                     int p) {
+    open_device(device_id);
+    cudaStream_t st;
+    OZTT_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    struct StreamGuard {
+        cudaStream_t s;
+        ~StreamGuard() {
+            cudaStreamSynchronize(s);
+            cudaStreamDestroy(s);
+        }
+    } guard{st};
+    DevBuf da(st, m * k * 8), db(st, k * n * 8), dc(st, m * n * 8);
+    OZTT_CUDA(cudaMemcpyAsync(da.p, a, m * k * 8, cudaMemcpyHostToDevice, st));
+    OZTT_CUDA(cudaMemcpyAsync(db.p, b, k * n * 8, cudaMemcpyHostToDevice, st));
+    run_i_int8_device(da.as<double>(), db.as<double>(), dc.as<double>(), m, n, k, p, st, nullptr);
+    OZTT_CUDA(cudaMemcpyAsync(c, dc.p, m * n * 8, cudaMemcpyDeviceToHost, st));
+    OZTT_CUDA(cudaStreamSynchronize(st));
+}
+
+}  // namespace oztt
+
+using oztt::Error;
+using oztt::guarded;
+
+extern "C" {
+
+int oztt_i_int8_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                    const oztt_i_plan* plan, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a || !b || !c || !plan) throw Error(OZTT_EINVAL, "null argument");
+        if (!m || !n || !k) throw Error(OZTT_EINVAL, "matrix dimensions are zero");
+        oztt::run_i_int8_host(device_id, a, b, c, m, n, k, plan->p);
+    });
+}
+
+int oztt_i_int8_run_device(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                           uint64_t k, const oztt_i_plan* plan, void* stream, double* stage_ms, char* err,
+                           size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a || !b || !c || !plan) throw Error(OZTT_EINVAL, "null argument");
+        if (!m || !n || !k) throw Error(OZTT_EINVAL, "matrix dimensions are zero");
+        oztt::open_device(device_id);
+        oztt::run_i_int8_device(a, b, c, m, n, k, plan->p, reinterpret_cast<cudaStream_t>(stream), stage_ms);
+    });
+}
+
+int oztt_i_slice_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int32_t p,
+                      int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a || !delta || !planes || lda < k || mp < m || kp < k || p < 1 || p > 64)
+            throw Error(OZTT_EINVAL, "slice_rows: bad arguments");
+        oztt::launch_slice_rows(a, m, k, lda, delta, p, planes, mp, kp, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+int oztt_i_slice_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta, int32_t p,
+                      int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!b || !delta || !planes || ldb < n || np < n || kp < k || p < 1 || p > 64)
+            throw Error(OZTT_EINVAL, "slice_cols: bad arguments");
+        oztt::launch_slice_cols(b, k, n, ldb, delta, p, planes, np, kp, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+int oztt_i_diag_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp, uint64_t np, uint64_t kp, int32_t p,
+                     int32_t* out, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a_planes || !b_planes || !out) throw Error(OZTT_EINVAL, "diag_gemm: null argument");
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        oztt::DevBuf word(st, 16);
+        OZTT_CUDA(cudaMemsetAsync(word.p, 0, 16, st));
+        oztt::launch_diag_gemm(a_planes, b_planes, mp, np, kp, p, out, word.as<int>(), st);
+        int host_err = 0;
+        OZTT_CUDA(cudaMemcpyAsync(&host_err, word.p, 4, cudaMemcpyDeviceToHost, st));
+        OZTT_CUDA(cudaStreamSynchronize(st));
+        oztt::check_flags(0, host_err);
+    });
+}
+
+int oztt_i_recon(const int32_t* diag, uint64_t mp, uint64_t np, const int32_t* delta_a, const int32_t* delta_b,
+                 int32_t p, double* c, uint64_t m, uint64_t n, uint64_t ldc, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!diag || !delta_a || !delta_b || !c || ldc < n || m > mp || n > np)
+            throw Error(OZTT_EINVAL, "recon: bad arguments");
+        oztt::launch_horner(diag, mp, np, delta_a, delta_b, p, c, m, n, ldc, reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+}  // extern "C"

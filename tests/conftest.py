@@ -16,7 +16,7 @@ for p in (str(ROOT), str(ROOT / "tests")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
-from oracle_lib import Oracle, RefEmu, RefPlan  # noqa: E402
+from oracle_lib import Oracle, RefEmu, RefPlan, RefPlan1  # noqa: E402
 
 
 def pytest_configure(config):
@@ -32,6 +32,14 @@ def oracle():
 def ref_plan():
     try:
         return RefPlan()
+    except FileNotFoundError:
+        pytest.skip("oracle/_ref was not built on this machine (needs the reference tree)")
+
+
+@pytest.fixture(scope="session")
+def ref_plan1():
+    try:
+        return RefPlan1()
     except FileNotFoundError:
         pytest.skip("oracle/_ref was not built on this machine (needs the reference tree)")
 

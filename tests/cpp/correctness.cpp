@@ -142,8 +142,9 @@ double check(ozTTgemm::Context& ctx, const ozTTgemm::Options& o, std::size_t m, 
         }
     const double rel = norm > 0 ? double(std::sqrt(err / norm)) : double(std::sqrt(err));
     std::cout << (o.scheme == ozTTgemm::Scheme::I ? "I " : "II ") << ozTTgemm::format_name(o.format) << ' ' << m
-              << 'x' << n << 'x' << k << " pattern=" << int(p) << " error=" << rel << " moduli=" << info.moduli
-              << " bits=" << info.integer_bits << " passes=" << info.reconstruction_passes << '\n';
+              << 'x' << n << 'x' << k << " pattern=" << int(p) << " error=" << rel << " slices=" << info.slices
+              << " moduli=" << info.moduli << " bits=" << info.integer_bits << " passes=" << info.reconstruction_passes
+              << '\n';
     expect(rel <= 8 * std::numeric_limits<double>::epsilon(), "error above 8 eps");
     return rel;
 }
@@ -166,17 +167,27 @@ int main(int argc, char** argv) {
             std::cout << "input validation passed\n";
             return 0;
         }
+        for (auto scheme : {ozTTgemm::Scheme::I, ozTTgemm::Scheme::II}) {
+            ozTTgemm::Options o;
+            o.format = first;
+            o.scheme = scheme;
+            check(ctx, o, 64, 64, 64, Pattern::Uniform);
+            check(ctx, o, 3, 5, 7, Pattern::Nonnegative);
+            check(ctx, o, 65, 67, 97, Pattern::Scaled);
+            check(ctx, o, 9, 11, 17, Pattern::ZeroA);
+            check(ctx, o, 3, 5, 64, Pattern::Cancellation);
+            check(ctx, o, 3, 5, 7, Pattern::ZeroRowColumn);
+            check(ctx, o, 1, 1, 1, Pattern::Smallest);
+            check(ctx, o, 1, 1, 1, Pattern::Largest);
+        }
         ozTTgemm::Options o;
         o.format = first;
+        o.scheme = ozTTgemm::Scheme::I;
+        o.slices = 8;  // the fixed slice count of the reference's test for INT8
+        check(ctx, o, 3, 5, 7, Pattern::Uniform);
+        o = {};
+        o.format = first;
         o.scheme = ozTTgemm::Scheme::II;
-        check(ctx, o, 64, 64, 64, Pattern::Uniform);
-        check(ctx, o, 3, 5, 7, Pattern::Nonnegative);
-        check(ctx, o, 65, 67, 97, Pattern::Scaled);
-        check(ctx, o, 9, 11, 17, Pattern::ZeroA);
-        check(ctx, o, 3, 5, 64, Pattern::Cancellation);
-        check(ctx, o, 3, 5, 7, Pattern::ZeroRowColumn);
-        check(ctx, o, 1, 1, 1, Pattern::Smallest);
-        check(ctx, o, 1, 1, 1, Pattern::Largest);
         check(ctx, o, 5056, 64, 32, Pattern::Uniform);
         o.reconstruction = ozTTgemm::Reconstruction::TwoPass;
         check(ctx, o, 64, 64, 64, Pattern::Uniform);

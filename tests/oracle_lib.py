@@ -2,7 +2,7 @@
 
 * ``Oracle``  — oracle/liboz2oracle.so, this project's CPU restatement of the reference's Scheme II
   INT8 path (oracle/oz2_oracle.h documents every function and the reference source it follows).
-* ``RefPlan`` / ``RefEmu`` — oracle/_ref/*.so, the reference's own host code compiled in place
+* ``RefPlan`` / ``RefPlan1`` / ``RefEmu`` — oracle/_ref/*.so, the reference's own host code compiled in place
   (oracle/Makefile, target ``ref``); present only where they were built.
 """
 
@@ -17,6 +17,7 @@ ROOT = Path(__file__).resolve().parent.parent
 ORACLE_SO = ROOT / "oracle" / "liboz2oracle.so"
 REF_PLAN_SO = ROOT / "oracle" / "_ref" / "libozref_plan.so"
 REF_EMU_SO = ROOT / "oracle" / "_ref" / "libozref_emu.so"
+REF_PLAN1_SO = ROOT / "oracle" / "_ref" / "libozref_plan1.so"
 
 MAXS, MAXRP = 24, 5
 P = ctypes.c_void_p
@@ -74,6 +75,11 @@ class Oracle:
         L.ozo_dot2_gemm.argtypes = [P, P, u64, u64, u64, P, P]
         L.ozo_accuracy.argtypes = [P, P, P, u64, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
         L.ozo_maxrel_f128.argtypes = [P, P, P, u64, u64, u64, P, u64, ctypes.POINTER(ctypes.c_double)]
+        L.ozo_i_slice.argtypes = [P, u64, u64, u64, ctypes.c_int, P, ctypes.c_int, P]
+        L.ozo_i_gemm.argtypes = [P, P, ctypes.c_int, u64, u64, u64, P]
+        L.ozo_i_recon_faithful.argtypes = [P, ctypes.c_int, u64, u64, P, P, P, u64]
+        L.ozo_i_recon_exact.argtypes = [P, ctypes.c_int, u64, u64, P, P, P, u64]
+        L.ozo_i_emulate.argtypes = [P, P, P, u64, u64, u64, ctypes.c_int, ctypes.c_int]
 
     # -- generators ---------------------------------------------------------------------------
     def gen_inputs(self, m: int, n: int, k: int, phi: float, seed: int) -> tuple[np.ndarray, np.ndarray]:
@@ -140,6 +146,29 @@ class Oracle:
                                           1 if exact else 0, ctypes.byref(p), err, 512)
         return rc, c, p, err.value.decode()
 
+    # -- Scheme I ------------------------------------------------------------------------------
+    def i_slice(self, x: np.ndarray, rows: int, cols: int, col_mode: int, delta: np.ndarray, p: int) -> np.ndarray:
+        out = np.zeros(p * rows * cols, dtype=np.int8)
+        self.lib.ozo_i_slice(ptr(x), rows, cols, cols, col_mode, ptr(delta), p, ptr(out))
+        return out
+
+    def i_gemm(self, sa: np.ndarray, sb: np.ndarray, p: int, M: int, N: int, K: int) -> np.ndarray:
+        out = np.zeros(p * M * N, dtype=np.int32)
+        assert self.lib.ozo_i_gemm(ptr(sa), ptr(sb), p, M, N, K, ptr(out)) == 0, "int32 overflow in the oracle"
+        return out
+
+    def i_recon(self, pd: np.ndarray, p: int, M: int, N: int, dA: np.ndarray, dB: np.ndarray,
+                exact: bool) -> np.ndarray:
+        c = np.zeros(M * N)
+        fn = self.lib.ozo_i_recon_exact if exact else self.lib.ozo_i_recon_faithful
+        fn(ptr(pd), p, M, N, ptr(dA), ptr(dB), ptr(c), N)
+        return c
+
+    def i_emulate(self, a, b, m, n, k, p, exact=False) -> np.ndarray:
+        c = np.zeros(m * n)
+        self.lib.ozo_i_emulate(ptr(a), ptr(b), ptr(c), m, n, k, p, 1 if exact else 0)
+        return c
+
     # -- metrics ------------------------------------------------------------------------------
     def output_hash(self, c: np.ndarray) -> str:
         return "%016x" % self.lib.ozo_output_hash(ptr(c), c.size)
@@ -203,6 +232,19 @@ class RefEmu:
         s = self.lib.ozr_emulate_int8(ptr(ap), ptr(bp), ptr(c), M, N, K, b_fixed, num_moduli, 1 if two_pass else 0,
                                       ptr(mods))
         return s, c, [int(x) for x in mods[:max(s, 0)]]
+
+
+class RefPlan1:
+    """The reference's Scheme I slice-count selection compiled in place (oracle/ref_plan1.cpp)."""
+
+    def __init__(self, path: Path = REF_PLAN1_SO):
+        if not path.exists():
+            raise FileNotFoundError(str(path))
+        self.lib = ctypes.CDLL(str(path))
+        self.lib.ozr_i_slices.argtypes = [P, P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32]
+
+    def slices(self, ap, bp, M, N, K) -> int:
+        return self.lib.ozr_i_slices(ptr(ap), ptr(bp), M, N, K)
 
 
 def pad(a: np.ndarray, rows: int, cols: int, prow: int, pcol: int) -> np.ndarray:

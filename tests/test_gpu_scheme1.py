@@ -1,0 +1,233 @@
+"""Scheme I INT8 on the B200, stage by stage and end to end, against the oracle.
+
+Every call goes through the C ABI of liboztt.so. Bars:
+  * slices (radix-254 digits of every element): bit-exact against the oracle's restatement of the
+    reference slicer (slice_tf_body.h with tfMulR);
+  * diagonal products P_d (int32): bit-exact;
+  * the FP64 output: bit-exact against the oracle's restatement of the B200 exact Horner
+    reconstruction, and within |C - C_ref| <= 2 ulp(C) + 2^-58 (|A| |B|)_ij of the reference's own
+    triple-float reconstruction;
+  * the acceptance cases of the reference's tests/correctness.cpp (relative Frobenius error <= 8 eps).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle_lib import pad, round_up
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def gpu_deltas(oztt, x, rows, cols, col_mode):
+    X = dev(x)
+    nout = cols if col_mode else rows
+    delta = torch.zeros(nout, dtype=torch.int32, device="cuda")
+    flags = torch.zeros(1, dtype=torch.int32, device="cuda")
+    name = "oztt_ii_scale_cols" if col_mode else "oztt_ii_scale_rows"
+    oztt.call(name, X.data_ptr(), rows, cols, cols, -1, delta.data_ptr(), None, flags.data_ptr(), stream())
+    return X, delta, flags
+
+
+def hard_matrix(rng, rows, cols):
+    """Random values plus the slicer's corner cases: exact powers of two (a digit of exactly 127 after
+    the first step), values just around the row maximum, halves of 254^-i (rounding ties of later
+    digits), tiny elements beside large ones (underflow of the triple-float limbs), zeros, negatives."""
+    x = rng.standard_normal(rows * cols) * np.exp2(rng.integers(-30, 30, rows * cols))
+    x = x.reshape(rows, cols)
+    x[:, 0] = np.exp2(rng.integers(-5, 5, rows)).astype(np.float64)
+    if cols > 3:
+        x[:, 1] = x[:, 0] * (1 - 2.0 ** -52)
+        x[:, 2] = -x[:, 0] * (0.5 + 0.5 / 254)
+        x[:, 3] = x[:, 0] * 2.0 ** -200
+    if cols > 8:
+        x[:, 4] = 0.0
+        x[:, 5] = x[:, 0] * (0.5 / 254 + 0.5 / 254 ** 2)
+        x[:, 6] = x[:, 0] * (1.0 / 254 ** 3) * 0.5
+        x[:, 7] = 5e-324
+        x[:, 8] = -x[:, 0] * 2.0 ** -60
+    if rows > 2:
+        x[1, :] = 0.0
+    return x.reshape(-1)
+
+
+SLICE_CASES = [(64, 64, 8), (33, 100, 7), (257, 129, 13), (5, 4097, 3), (128, 256, 1), (300, 45, 16)]
+
+
+@pytest.mark.parametrize("m,k,p", SLICE_CASES)
+def test_slice_rows_match_oracle(oztt, oracle, cuda, m, k, p):
+    rng = np.random.default_rng(m * 1000 + k)
+    a = hard_matrix(rng, m, k)
+    A, delta, flags = gpu_deltas(oztt, a, m, k, 0)
+    _, od, ofl = oracle.scale(a, m, k, 0, -1)
+    mp, kp = round_up(m, 128), round_up(k, 128)
+    planes = torch.full((p * mp * kp,), 99, dtype=torch.int8, device="cuda")
+    oztt.call("oztt_i_slice_rows", A.data_ptr(), m, k, k, delta.data_ptr(), p, planes.data_ptr(), mp, kp, stream())
+    torch.cuda.synchronize()
+    assert np.array_equal(delta.cpu().numpy(), od) and int(flags.cpu()[0]) == ofl
+    got = planes.cpu().numpy().reshape(p, mp, kp)
+    want = oracle.i_slice(a, m, k, 0, od, p).reshape(p, m, k)
+    assert np.array_equal(got[:, :m, :k], want)
+    assert not got[:, m:, :].any() and not got[:, :, k:].any()
+
+
+@pytest.mark.parametrize("k,n,p", SLICE_CASES)
+def test_slice_cols_match_oracle(oztt, oracle, cuda, k, n, p):
+    rng = np.random.default_rng(k * 1000 + n + 1)
+    b = np.ascontiguousarray(hard_matrix(rng, n, k).reshape(n, k).T).reshape(-1)
+    B, delta, flags = gpu_deltas(oztt, b, k, n, 1)
+    _, od, ofl = oracle.scale(b, k, n, 1, -1)
+    np_, kp = round_up(n, 256), round_up(k, 128)
+    planes = torch.full((p * np_ * kp,), 99, dtype=torch.int8, device="cuda")
+    oztt.call("oztt_i_slice_cols", B.data_ptr(), k, n, n, delta.data_ptr(), p, planes.data_ptr(), np_, kp, stream())
+    torch.cuda.synchronize()
+    assert np.array_equal(delta.cpu().numpy(), od) and int(flags.cpu()[0]) == ofl
+    got = planes.cpu().numpy().reshape(p, np_, kp)
+    want = oracle.i_slice(b, k, n, 1, od, p).reshape(p, n, k)
+    assert np.array_equal(got[:, :n, :k], want)
+    assert not got[:, n:, :].any() and not got[:, :, k:].any()
+
+
+def gpu_diag(oztt, sa, sb, mp, np_, kp, p):
+    SA, SB = dev(sa), dev(sb)
+    out = torch.full((p * mp * np_,), 7, dtype=torch.int32, device="cuda")
+    oztt.call("oztt_i_diag_gemm", SA.data_ptr(), SB.data_ptr(), mp, np_, kp, p, out.data_ptr(), stream())
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("mp,np_,kp,p", [(128, 256, 128, 1), (128, 256, 256, 4), (384, 512, 640, 8),
+                                         (256, 768, 128, 13), (1280, 256, 384, 3)])
+def test_diag_gemm_matches_oracle(oztt, oracle, cuda, mp, np_, kp, p):
+    rng = np.random.default_rng(mp + np_ + kp + p)
+    sa = rng.integers(-127, 128, p * mp * kp, dtype=np.int8)
+    sb = rng.integers(-127, 128, p * np_ * kp, dtype=np.int8)
+    assert np.array_equal(gpu_diag(oztt, sa, sb, mp, np_, kp, p), oracle.i_gemm(sa, sb, p, mp, np_, kp))
+
+
+def test_diag_gemm_at_the_int32_budget(oztt, cuda):
+    # 8 slices, K = 2^17 / 8: every product is +127 * +127 (or -127 * +127), the largest diagonal sum is
+    # 8 * 16384 * 127^2 = 2113667072 < 2^31 - 1.
+    mp, np_, kp, p = 128, 256, 16384, 8
+    sa = np.full(p * mp * kp, 127, dtype=np.int8)
+    sa.reshape(p, mp, kp)[:, 1::2, :] = -127
+    sb = np.full(p * np_ * kp, 127, dtype=np.int8)
+    got = gpu_diag(oztt, sa, sb, mp, np_, kp, p).reshape(p, mp, np_)
+    for d in range(p):
+        want = (d + 1) * kp * 127 * 127
+        assert np.all(got[d, 0::2, :] == want) and np.all(got[d, 1::2, :] == -want)
+
+
+@pytest.mark.parametrize("m,n,p", [(64, 64, 1), (100, 70, 5), (128, 256, 8), (33, 300, 13)])
+def test_recon_matches_oracle(oztt, oracle, cuda, m, n, p):
+    rng = np.random.default_rng(m * n + p)
+    mp, np_ = round_up(m, 128), round_up(n, 256)
+    K = 2048
+    bound = np.array([(d + 1) * K * 127 * 127 for d in range(p)], dtype=np.int64)
+    pd = (rng.uniform(-1, 1, (p, mp, np_)) * bound[:, None, None] * rng.uniform(0, 1, (p, 1, 1))).astype(np.int32)
+    pd[:, 0, 0] = 0                     # zero result
+    pd[:, 0, 1] = bound.astype(np.int32)  # largest positive
+    pd[:, 0, 2] = -bound.astype(np.int32)
+    pd[0, 0, 3], pd[1:, 0, 3] = 1, 0    # one unit in the top diagonal only
+    dA = rng.integers(-40, 40, mp).astype(np.int32)
+    dB = rng.integers(-40, 40, np_).astype(np.int32)
+    dA[2] = 1000                        # results far below 2^-1022: flushed to zero
+    PD, DA, DB = dev(pd.reshape(-1)), dev(dA), dev(dB)
+    c = torch.full((m * n,), 3.0, dtype=torch.float64, device="cuda")
+    oztt.call("oztt_i_recon", PD.data_ptr(), mp, np_, DA.data_ptr(), DB.data_ptr(), p, c.data_ptr(), m, n, n,
+              stream())
+    torch.cuda.synchronize()
+    got = c.cpu().numpy().reshape(m, n)
+    exact = oracle.i_recon(pd.reshape(-1), p, mp, np_, dA, dB, exact=True).reshape(mp, np_)[:m, :n]
+    assert np.array_equal(got.view(np.uint64), exact.view(np.uint64))
+    faithful = oracle.i_recon(pd.reshape(-1), p, mp, np_, dA, dB, exact=False).reshape(mp, np_)[:m, :n]
+    # magnitude bound of the sum: sum_d |P_d| 254^(L-d) 254^-(L+2) 2^-(dA+dB)
+    w = np.array([254.0 ** (-(d + 2)) for d in range(p)])
+    mag = np.tensordot(w, np.abs(pd[:, :m, :n].astype(np.float64)), axes=1)
+    mag *= np.exp2(-(dA[:m, None] + dB[None, :n]).astype(np.float64))
+    assert np.all(np.abs(got - faithful) <= 2 * np.spacing(np.abs(got)) + 2.0 ** -58 * mag)
+
+
+def run_gpu(oztt, a, b, m, n, k, p=0):
+    plan = oztt.i_int8_plan(a, b, m, n, k, slices=p)
+    return oztt.i_int8_run(a, b, m, n, k, plan), plan
+
+
+def absprod(a, b, m, n, k):
+    return np.abs(a.reshape(m, k)) @ np.abs(b.reshape(k, n))
+
+
+PIPE_CASES = [("uniform", 128, 128, 128, -1.0, 8), ("phi1", 100, 70, 45, 1.0, 0), ("phi4", 64, 200, 300, 4.0, 0),
+              ("tall", 1000, 3, 64, 0.5, 6), ("wide", 3, 1000, 96, -1.0, 0), ("one", 1, 1, 1, -1.0, 2)]
+
+
+@pytest.mark.parametrize("name,m,n,k,phi,p", PIPE_CASES)
+def test_pipeline_matches_oracle(oztt, oracle, cuda, name, m, n, k, phi, p):
+    a, b = oracle.gen_inputs(m, n, k, phi, 17)
+    c, plan = run_gpu(oztt, a, b, m, n, k, p)
+    assert p == 0 or plan.p == p
+    exact = oracle.i_emulate(a, b, m, n, k, plan.p, exact=True)
+    assert np.array_equal(c.view(np.uint64), exact.view(np.uint64)), name
+    faithful = oracle.i_emulate(a, b, m, n, k, plan.p, exact=False)
+    tol = 2 * np.spacing(np.abs(c)) + 2.0 ** -58 * absprod(a, b, m, n, k).reshape(-1)
+    assert np.all(np.abs(c - faithful) <= tol), name
+
+
+@pytest.mark.parametrize("mode", [2, 3, 4, 5, 6, 7])
+def test_pipeline_patterns(oztt, oracle, cuda, mode):
+    m, n, k = (65, 67, 97) if mode < 6 else (1, 1, 1)
+    a, b = oracle.gen_pattern(m, n, k, mode)
+    c, plan = run_gpu(oztt, a, b, m, n, k)
+    exact = oracle.i_emulate(a, b, m, n, k, plan.p, exact=True)
+    assert np.array_equal(c.view(np.uint64), exact.view(np.uint64))
+
+
+def test_published_case(oztt, oracle, cuda):
+    # tools/validated/quick.csv:12: n=128, seed 7, 8 slices; the reference's device output has relative
+    # Frobenius error 4.68786522126e-17 against Dot2 and hash 6c9693442bfc11b0.
+    n = 128
+    a, b = oracle.gen_inputs(n, n, n, -1.0, 7)
+    c, _ = run_gpu(oztt, a, b, n, n, n, 8)
+    ref = oracle.i_emulate(a, b, n, n, n, 8, exact=False)
+    assert oracle.output_hash(ref) == "6c9693442bfc11b0"
+    assert np.all(np.abs(c - ref) <= 2 * np.spacing(np.abs(c)))
+    hi, lo = oracle.dot2(a, b, n, n, n)
+    rel, _ = oracle.accuracy(c, hi, lo)
+    assert abs(rel - 4.68786522126e-17) <= 1e-3 * 4.68786522126e-17
+
+
+def test_device_entry_matches_host_entry(oztt, oracle, cuda):
+    m, n, k = 200, 300, 160
+    a, b = oracle.gen_inputs(m, n, k, 0.5, 9)
+    host, plan = run_gpu(oztt, a, b, m, n, k)
+    A, B = dev(a), dev(b)
+    C = torch.zeros(m * n, dtype=torch.float64, device="cuda")
+    ms = oztt.i_int8_run_device(A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, plan, stream(), timed=True)
+    assert len(ms) == 5 and all(t >= 0 for t in ms)
+    assert np.array_equal(C.cpu().numpy().view(np.uint64), host.view(np.uint64))
+
+
+def test_context_scheme_i(oztt, oracle, cuda):
+    ctx = oztt.Context()
+    m, n, k = 65, 67, 97
+    a, b = oracle.gen_inputs(m, n, k, 1.0, 4)
+    opts = oztt.Options(scheme=oztt.Scheme.I, format=oztt.Format.INT8)
+    c = np.empty(m * n)
+    info = ctx.gemm(a, b, c, m, n, k, opts)
+    plan = oztt.i_int8_plan(a, b, m, n, k)
+    assert info.scheme == oztt.Scheme.I and info.slices == plan.p and info.moduli == 0
+    assert (info.padded_m, info.padded_n, info.padded_k) == (128, 128, 128)
+    exact = oracle.i_emulate(a, b, m, n, k, plan.p, exact=True)
+    assert np.array_equal(c.view(np.uint64), exact.view(np.uint64))
+    hi, lo = oracle.dot2(a, b, m, n, k)
+    assert oracle.accuracy(c, hi, lo)[0] <= 8 * np.finfo(np.float64).eps
+    with pytest.raises(RuntimeError, match="reconstruction would overflow FP32"):
+        ctx.multiply(a, b, m, n, k, oztt.Options(scheme=oztt.Scheme.I, format=oztt.Format.INT8, slices=15))
