@@ -36,6 +36,11 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompil
 CXX_FLAGS = ["-std=gnu++20", "-O2", "-fPIC", "-fno-fast-math", "-ffp-contract=off", "-pthread",
              f"-I{ROOT / 'include'}", f"-I{CUDA_HOME / 'include'}"]
 
+# The host planners run the reference's selection arithmetic over every input element: built for the
+# x86-64-v3 level (AVX2, FMA, SSE4.1 rounding) so that fma and nearbyint are single instructions.
+# Contraction stays off, so every operation rounds as written and the decisions do not change.
+CXX_FLAGS_BY_SOURCE = {"planner.cpp": ["-O3", "-march=x86-64-v3"], "planner1.cpp": ["-O3", "-march=x86-64-v3"]}
+
 CU_SOURCES = ["split.cu", "gemm_i8.cu", "recon.cu", "ii_int8.cu", "noalloc.cu", "scheme1.cu"]
 CPP_SOURCES = ["planner.cpp", "planner1.cpp", "context.cpp", "evaluation.cpp"]
 
@@ -66,7 +71,7 @@ def build_library(force: bool = False) -> Path:
     for src in CPP_SOURCES:
         s, o = CSRC / src, OUT / (src + ".o")
         if force or _stale(o, [s] + headers):
-            _run([CXX, *CXX_FLAGS, "-c", str(s), "-o", str(o)])
+            _run([CXX, *CXX_FLAGS, *CXX_FLAGS_BY_SOURCE.get(src, []), "-c", str(s), "-o", str(o)])
         objs.append(o)
     if force or _stale(LIB, objs):
         _run([NVCC, *ARCH, "-shared", "-ccbin", CXX, "-o", str(LIB), *map(str, objs), "-lpthread"])

@@ -151,35 +151,84 @@ std::vector<double> independent_error(const double* a, const double* b, const Di
     const size_t P1 = (size_t)pmax + 1, K = d.k;
     // Per k: slice contributions S[i][k], residual contributions R[q][k], column norms N[k].
     std::vector<double> SA(P1 * K, 0.0), RA(P1 * K, 0.0), SB(P1 * K, 0.0), RB(P1 * K, 0.0), NA(K, 0.0), NB(K, 0.0);
-    auto cut = [&](double x, double s, double* S, double* R) {
-        Expansion t;
-        t.th = x;
+    // Expands up to four elements of different k side by side (their chains are independent, so they
+    // overlap in the pipeline); each element adds its slice and residual terms to its own column k, in
+    // the order of its own steps, and stops once its residual is exactly zero.
+    constexpr int LANES = 4;
+    auto cut = [&](const double (&x)[LANES], const double (&s)[LANES], const size_t (&col)[LANES], double* S,
+                   double* R) {
+        Expansion t[LANES];
+        bool active[LANES];
+        int live = 0;
+        for (int l = 0; l < LANES; ++l) {
+            t[l].th = x[l];
+            active[l] = s[l] > 0;
+            live += active[l];
+        }
         double w = 1.0;
-        for (int i = 0; i < pmax; ++i) {
-            const double dg = t.step();
+        for (int i = 0; i < pmax && live; ++i) {
             w /= kRadix;
-            S[(size_t)i * K] += (s * dg * w) * (s * dg * w);
-            const double r = s * t.value() * w;
-            R[(size_t)(i + 1) * K] += r * r;
-            if (t.th == 0) break;
+            for (int l = 0; l < LANES; ++l) {
+                if (!active[l]) continue;
+                const double dg = t[l].step();
+                S[(size_t)i * K + col[l]] += (s[l] * dg * w) * (s[l] * dg * w);
+                const double r = s[l] * t[l].value() * w;
+                R[(size_t)(i + 1) * K + col[l]] += r * r;
+                if (t[l].th == 0) {
+                    active[l] = false;
+                    --live;
+                }
+            }
         }
     };
+    // Collects the elements to expand of one row (A) or one k (B) in groups of LANES.
+    struct Batch {
+        double x[LANES] = {}, s[LANES] = {};
+        size_t col[LANES] = {};
+        int n = 0;
+    };
+    auto flush = [&](Batch& bt, double* S, double* R) {
+        for (int l = bt.n; l < LANES; ++l) bt.s[l] = 0.0;
+        cut(bt.x, bt.s, bt.col, S, R);
+        bt.n = 0;
+    };
+    auto push = [&](Batch& bt, double x, double sc, size_t c, double* S, double* R) {
+        bt.x[bt.n] = x;
+        bt.s[bt.n] = sc;
+        bt.col[bt.n] = c;
+        if (++bt.n == LANES) flush(bt, S, R);
+    };
+    // Per k, the rows of A and the columns of B are visited in ascending order (the reference's order of
+    // the sums); for A the loops are interchanged so that each thread walks its k range of a row
+    // contiguously, which leaves the order of every per-k sum unchanged.
+    // The lanes of a batch always belong to different k (distinct accumulators): for A the elements of
+    // one row, for B the elements of one column at LANES consecutive k. Every per-k sum still receives
+    // its terms row by row (A) or column by column (B), as in the reference's sequential loops.
     parallel_ranges(K, [&](uint64_t k0, uint64_t k1) {
-        for (uint64_t c = k0; c < k1; ++c) {
-            double na = 0, nb = 0;
-            for (uint64_t i = 0; i < d.m; ++i) {
-                const double v = a[i * d.k + c];
-                na += (v * nm.rgA) * (v * nm.rgA);
-                if (v != 0 && nm.sA[i] > 0) cut(std::ldexp(v, kNshift - nm.eA[i]), nm.sA[i], &SA[c], &RA[c]);
+        Batch bt;
+        for (uint64_t i = 0; i < d.m; ++i) {
+            const double* row = a + i * d.k;
+            const bool counted = nm.sA[i] > 0;
+            for (uint64_t c = k0; c < k1; ++c) {
+                const double v = row[c];
+                NA[c] += (v * nm.rgA) * (v * nm.rgA);
+                if (v != 0 && counted) push(bt, std::ldexp(v, kNshift - nm.eA[i]), nm.sA[i], c, SA.data(), RA.data());
             }
-            const double* row = b + c * d.n;
+            if (bt.n) flush(bt, SA.data(), RA.data());
+        }
+        for (uint64_t c0 = k0; c0 < k1; c0 += LANES) {
+            const int nl = (int)std::min<uint64_t>(LANES, k1 - c0);
+            double nb[LANES] = {};
             for (uint64_t j = 0; j < d.n; ++j) {
-                const double v = row[j];
-                nb += (v * nm.rgB) * (v * nm.rgB);
-                if (v != 0 && nm.sB[j] > 0) cut(std::ldexp(v, kNshift - nm.eB[j]), nm.sB[j], &SB[c], &RB[c]);
+                const bool counted = nm.sB[j] > 0;
+                for (int l = 0; l < nl; ++l) {
+                    const double v = b[(c0 + l) * d.n + j];
+                    nb[l] += (v * nm.rgB) * (v * nm.rgB);
+                    if (v != 0 && counted) push(bt, std::ldexp(v, kNshift - nm.eB[j]), nm.sB[j], c0 + l, SB.data(), RB.data());
+                }
+                if (bt.n) flush(bt, SB.data(), RB.data());
             }
-            NA[c] = na;
-            NB[c] = nb;
+            for (int l = 0; l < nl; ++l) NB[c0 + l] = nb[l];
         }
     });
     // G[i][j] = sum_k SA_i[k] SB_j[k]: the pairs the device drops.

@@ -1,0 +1,90 @@
+"""The B200 integer stages against the reference device's published outputs at n = 3520 and 7040
+(tools/validated/all.csv:12-13, 28-29).
+
+The scaling, splitting/slicing and the tensor-core products run on the GPU through the C ABI; the
+int32 products are then reconstructed on the host by the oracle's restatement of the reference's own
+(triple-float) reconstruction. Matching the published FNV hash means every output bit equals the
+reference device's, so the GPU's residues/slices and products are the reference's at full size.
+Inputs: the evaluator's table suite (mt19937 seed 7, uniform(-1, 1)); Scheme II INT8 with max_moduli
+16, one pass, b = 54; Scheme I INT8 with 8 slices.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle_lib import pad, round_up
+
+pytestmark = pytest.mark.gpu
+
+PUBLISHED = {3520: {"II": "a7bb9bd6f452e753", "I": "3ec48d5faecdf98f"},
+             7040: {"II": "a2a3d9c61f79b001", "I": "316f280769f1f880"}}
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def scale(oztt, X, rows, cols, col_mode, shift):
+    nout = cols if col_mode else rows
+    delta = torch.zeros(nout, dtype=torch.int32, device="cuda")
+    flags = torch.zeros(1, dtype=torch.int32, device="cuda")
+    name = "oztt_ii_scale_cols" if col_mode else "oztt_ii_scale_rows"
+    oztt.call(name, X.data_ptr(), rows, cols, cols, shift, delta.data_ptr(), None, flags.data_ptr(), stream())
+    return delta
+
+
+@pytest.mark.parametrize("n", [3520, 7040])
+def test_scheme_ii_published(oztt, oracle, cuda, n):
+    a, b = oracle.gen_inputs(n, n, n, -1.0, 7)
+    plan = oztt.ii_int8_plan(a, b, n, n, n, max_moduli=16, reconstruction=1, fixed_bits=54)
+    M = round_up(n, 64)
+    rc, oplan, err = oracle.plan(pad(a, n, n, M, M), pad(b, n, n, M, M), M, M, M, 16, 1, 54)
+    assert rc == 0, err
+    assert plan.moduli_list == oplan.moduli and plan.shift == oplan.shift
+    S = plan.S
+    mp, np_, kp = round_up(n, 128), round_up(n, 256), round_up(n, 128)
+    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    dA, dB = scale(oztt, A, n, n, 0, plan.shift), scale(oztt, B, n, n, 1, plan.shift)
+    ra = torch.zeros(S * mp * kp, dtype=torch.int8, device="cuda")
+    rb = torch.zeros(S * np_ * kp, dtype=torch.int8, device="cuda")
+    oztt.call("oztt_ii_split_rows", A.data_ptr(), n, n, n, dA.data_ptr(), plan, ra.data_ptr(), mp, kp, stream())
+    oztt.call("oztt_ii_split_cols", B.data_ptr(), n, n, n, dB.data_ptr(), plan, rb.data_ptr(), np_, kp, stream())
+    del A, B
+    cs = torch.empty(S * mp * np_, dtype=torch.int32, device="cuda")
+    oztt.call("oztt_ii_residue_gemm", ra.data_ptr(), rb.data_ptr(), mp, np_, kp, plan, 0, cs.data_ptr(), stream())
+    torch.cuda.synchronize()
+    del ra, rb
+    host = np.ascontiguousarray(cs.view(S, mp, np_)[:, :M, :M].cpu().numpy())
+    del cs
+    da = np.zeros(M, dtype=np.int32)
+    db = np.zeros(M, dtype=np.int32)
+    da[:n], db[:n] = dA.cpu().numpy(), dB.cpu().numpy()
+    c = oracle.recon(host.reshape(-1), M, M, da, db, oplan, exact=False).reshape(M, M)[:n, :n]
+    assert oracle.output_hash(np.ascontiguousarray(c).reshape(-1)) == PUBLISHED[n]["II"]
+
+
+@pytest.mark.parametrize("n", [3520, 7040])
+def test_scheme_i_published(oztt, oracle, cuda, n):
+    a, b = oracle.gen_inputs(n, n, n, -1.0, 7)
+    p = 8
+    M = round_up(n, 64)
+    mp, np_, kp = round_up(n, 128), round_up(n, 256), round_up(n, 128)
+    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    dA, dB = scale(oztt, A, n, n, 0, -1), scale(oztt, B, n, n, 1, -1)
+    sa = torch.zeros(p * mp * kp, dtype=torch.int8, device="cuda")
+    sb = torch.zeros(p * np_ * kp, dtype=torch.int8, device="cuda")
+    oztt.call("oztt_i_slice_rows", A.data_ptr(), n, n, n, dA.data_ptr(), p, sa.data_ptr(), mp, kp, stream())
+    oztt.call("oztt_i_slice_cols", B.data_ptr(), n, n, n, dB.data_ptr(), p, sb.data_ptr(), np_, kp, stream())
+    del A, B
+    pd = torch.empty(p * mp * np_, dtype=torch.int32, device="cuda")
+    oztt.call("oztt_i_diag_gemm", sa.data_ptr(), sb.data_ptr(), mp, np_, kp, p, pd.data_ptr(), stream())
+    torch.cuda.synchronize()
+    del sa, sb
+    host = np.ascontiguousarray(pd.view(p, mp, np_)[:, :M, :M].cpu().numpy())
+    del pd
+    da = np.zeros(M, dtype=np.int32)
+    db = np.zeros(M, dtype=np.int32)
+    da[:n], db[:n] = dA.cpu().numpy(), dB.cpu().numpy()
+    c = oracle.i_recon(host.reshape(-1), p, M, M, da, db, exact=False).reshape(M, M)[:n, :n]
+    assert oracle.output_hash(np.ascontiguousarray(c).reshape(-1)) == PUBLISHED[n]["I"]
