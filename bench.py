@@ -2,6 +2,7 @@
 """Benchmark: Ozaki-II INT8 effective FP64 TFLOPS on B200 (the metric of BASELINE.json).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl oztt|reference]
+    python bench.py --scheme I [--slices 0,4,8,12]     (Scheme I INT8, 8192^3, phi=1: one line per p)
 
 One step is one pass of the Scheme II INT8 pipeline (scale -> split -> residue GEMM on the tensor
 cores -> exact CRT reconstruction) over one m x n x k problem with FP64 operands already resident in
@@ -49,13 +50,21 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["oztt", "reference"], default="oztt")
-    ap.add_argument("--size", type=int, default=DEFAULT_SIZE, help="per-GPU tile side m = n = k")
-    ap.add_argument("--phi", type=float, default=0.5)
+    ap.add_argument("--size", type=int, default=None, help="per-GPU tile side m = n = k")
+    ap.add_argument("--phi", type=float, default=None)
+    ap.add_argument("--scheme", choices=["II", "I"], default="II",
+                    help="I: the Scheme I INT8 workload (default 8192^3, phi=1.0), one JSON line per slice count")
+    ap.add_argument("--slices", default="0", help="Scheme I: comma-separated slice counts, 0 = selected from the input")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-accuracy", action="store_true")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.size is None:
+        args.size = DEFAULT_SIZE if args.scheme == "II" else 8192
+    if args.phi is None:
+        args.phi = 0.5 if args.scheme == "II" else 1.0
+    return args
 
 
 def measured_peaks() -> dict:
@@ -226,6 +235,68 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---- Scheme I INT8 (a separate workload, one GPU) -------------------------------------------------------
+def run_scheme_i(args) -> None:
+    """One step = one pass of the Scheme I INT8 pipeline (scale -> slice -> diagonal products on the
+    tensor cores -> exact Horner reconstruction) with the operands resident in HBM."""
+    import torch
+
+    import oztt_b200 as oz
+
+    m = n = k = args.size
+    a, b = oz.eval_inputs(m, n, k, args.phi, args.seed)
+    A = torch.from_numpy(a).cuda()
+    B = torch.from_numpy(b).cuda()
+    C = torch.empty(m * n, dtype=torch.float64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    peaks = measured_peaks()
+    for req in [int(x) for x in args.slices.split(",")]:
+        t_plan = time.perf_counter()
+        plan = oz.i_int8_plan(a, b, m, n, k, slices=req)
+        t_plan = time.perf_counter() - t_plan
+        p = plan.p
+
+        def step():
+            return oz.i_int8_run_device(A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, plan, stream, 0,
+                                        timed=True)
+
+        for _ in range(max(args.warmup, 0)):
+            step()
+        stage_sum = [0.0] * 5
+        with ClockSampler(0) as clocks:
+            torch.cuda.synchronize()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            for _ in range(args.steps):
+                stage_sum = [x + y for x, y in zip(stage_sum, step())]
+            ev1.record()
+            torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / args.steps
+        st = [x / args.steps for x in stage_sum]
+        pairs = p * (p + 1) // 2
+        gemm_ops = 2.0 * m * n * k * pairs
+        gemm_tops = gemm_ops / (st[3] * 1e-3) / 1e12
+        int8_peak = 2.0 * peaks["bf16_tflops"]
+        line = {"metric": f"Ozaki-I INT8 effective FP64 TFLOPS at m=n=k={m}", "value": 2.0 * m * n * k / (ms * 1e-3) / 1e12,
+                "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f64 (int8 slice products, s32 accumulate)",
+                "data": f"synthetic: evaluation/numerics.hpp generator, phi={args.phi}, mt19937 seed {args.seed}",
+                "config": {"workload": f"Scheme I INT8 {m}x{n}x{k}", "slices": p,
+                           "slices_selected_from_input": bool(plan.auto_p), "slice_pair_products": pairs,
+                           "planning_s_host": round(t_plan, 3),
+                           "l2": "inputs larger than the 126 MB L2; no flush"},
+                "stage_ms": {"scale_rows": st[0], "scale_cols": st[1], "slice": st[2], "diag_gemm": st[3],
+                             "recon": st[4]},
+                "roofline": {"bound": "tensor", "kernel": "residue_gemm_kernel<2> (tcgen05 kind::i8, diagonals)",
+                             "achieved": gemm_tops, "peak": int8_peak, "unit": "TOP/s (int8)",
+                             "frac": gemm_tops / int8_peak,
+                             "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({peaks['source']})",
+                             "algorithmic": f"2*m*n*k*p(p+1)/2 = {gemm_ops:.4g} int8 ops per launch"},
+                "gpu_launches": 7 * args.steps, "clocks": clocks.summary()}
+        print(json.dumps(line), flush=True)
+
+
 # ---- the GPU arm --------------------------------------------------------------------------------------
 def grid_shape(world: int) -> tuple[int, int]:
     p = int(math.sqrt(world))
@@ -238,6 +309,9 @@ def main() -> None:
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.scheme == "I":
+        run_scheme_i(args)
         return
     import torch
     import torch.distributed as dist

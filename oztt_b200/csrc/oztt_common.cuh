@@ -88,6 +88,52 @@ __device__ __forceinline__ float f32_fma(float a, float b, float c) {
     return r;
 }
 
+// ---- the same operations on pairs of binary32 values (sm_100 packed FP32 pipe) ---------------
+// A pair lives in one 64-bit register, first element in the low half. Each operation is one
+// f32x2 instruction with the same rounding (.rn) and flushing (.ftz) as the scalar forms above, so
+// each half is bit-identical to the scalar operation on that half.
+typedef uint64_t f32x2;
+__device__ __forceinline__ f32x2 pk2(float lo, float hi) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpk2(f32x2 v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f32x2 splat2(float v) { return pk2(v, v); }
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 sub2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// a*b + c rounded once.
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 r;
+    asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// a*b rounded once, for two values. The assembler treats a packed multiply followed by an addition
+// as a candidate for fusion (one rounding instead of two), which would change the reference's
+// results; the product is therefore formed as fma(a, b, nz) with nz = -0.0 that the caller receives
+// at run time (a kernel argument), so nothing can be folded into it. a*b + (-0) equals a*b in every
+// case, the sign of a zero product included.
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b, f32x2 nz) { return fma2(a, b, nz); }
+// Round to the nearest integer, ties to even, for |x| < 2^22: adding 1.5 * 2^23 moves x into the
+// binade where the spacing is 1, so the addition itself rounds to an integer (ties to even, since the
+// added constant is even), and subtracting the constant again is exact. The value equals
+// cvt.rni.f32.f32; only the sign of a zero result can differ (+0 where cvt.rni would give -0).
+constexpr float kRoundMagic = 12582912.0f;
+__device__ __forceinline__ f32x2 rint2(f32x2 x) {
+    const f32x2 m = splat2(kRoundMagic);
+    return sub2(add2(x, m), m);
+}
+
 // Global nanosecond timer, for bounded waits.
 __device__ __forceinline__ uint64_t global_timer_ns() {
     uint64_t t;

@@ -6,9 +6,9 @@
 //                (OZ1_NSHIFT = -1, rounding the maxima up: ozaki1/format.hpp, CEIL mode 1)
 //   slice        p radix-254 slices per element, digits in [-127, 127]: t *= 254 (Dekker-split
 //                triple-float product, tfMulR of sfpu_tf_proc.h:108-133), d = clamp(rint(t0)),
-//                t0 -= d (slice_tf_body.h). The binary32 operation sequence is the reference's,
-//                one PTX instruction with round-to-nearest-even and flush-to-zero at a time, so the
-//                slices are bit-identical. Layout: A [p][mp][kp], B transposed [p][np][kp] (int8).
+//                t0 -= d (slice_tf_body.h). The binary32 operation sequence is the reference's, with
+//                round-to-nearest-even and flush-to-zero, two elements per packed-FP32 instruction,
+//                so the slices are bit-identical. Layout: A [p][mp][kp], B transposed [p][np][kp].
 //   diagonals    P_d = sum_{i=0..d} A_i B_{d-i}^T for d = 0..p-1 on the tensor cores (gemm_i8.cu,
 //                mode 2): the concatenated GEMMs of issue_panel_diagonals with K_eff = (d+1) K,
 //                exact in s32 because the planner keeps (L+1) K 127^2 < 2^31.
@@ -28,43 +28,43 @@ namespace oztt {
 namespace {
 
 // Triple-float times 254 with Dekker splits (the constant of the split is 4097), in the
-// reference's operation order.
-__device__ __forceinline__ void two_sum1(float x, float y, float& s, float& e) {
-    s = f32_add(x, y);
-    const float bb = f32_sub(s, x);
-    const float a = f32_sub(x, f32_sub(s, bb));
-    e = f32_add(a, f32_sub(y, bb));
+// reference's operation order, for two elements at once (packed FP32; each half rounds as the
+// scalar binary32 operation would).
+__device__ __forceinline__ void two_sum2(f32x2 x, f32x2 y, f32x2& s, f32x2& e) {
+    s = add2(x, y);
+    const f32x2 bb = sub2(s, x);
+    e = add2(sub2(x, sub2(s, bb)), sub2(y, bb));
 }
-__device__ __forceinline__ void tf_mul_254(float& x0, float& x1, float& x2) {
-    const float r = 254.0f, spl = 4097.0f;
-    const float lo_r = f32_mul(x2, r);
-    float t1 = f32_mul(x1, spl);
-    float t2 = f32_sub(t1, x1);
-    float hm = f32_sub(t1, t2);
-    float lm = f32_sub(x1, hm);
-    hm = f32_mul(hm, r);
-    lm = f32_mul(lm, r);
-    const float P1 = f32_add(hm, lm);
-    float kk = f32_sub(P1, hm);
-    const float F1 = f32_sub(lm, kk);
-    t1 = f32_mul(x0, spl);
-    t2 = f32_sub(t1, x0);
-    float hh = f32_sub(t1, t2);
-    float lh = f32_sub(x0, hh);
-    hh = f32_mul(hh, r);
-    lh = f32_mul(lh, r);
-    const float P0 = f32_add(hh, lh);
-    kk = f32_sub(P0, hh);
-    const float F0 = f32_sub(lh, kk);
-    const float G1 = f32_add(F1, lo_r);
-    float sa, ea, sb, eb, r0, ec;
-    two_sum1(P1, G1, sa, ea);
-    two_sum1(F0, sa, sb, eb);
-    two_sum1(P0, sb, r0, ec);
-    const float G = f32_add(ea, eb);
+__device__ __forceinline__ void tf_mul_254(f32x2& x0, f32x2& x1, f32x2& x2, f32x2 nz) {
+    const f32x2 r = splat2(254.0f), spl = splat2(4097.0f);
+    const f32x2 lo_r = mul2(x2, r, nz);
+    f32x2 t1 = mul2(x1, spl, nz);
+    f32x2 t2 = sub2(t1, x1);
+    f32x2 hm = sub2(t1, t2);
+    f32x2 lm = sub2(x1, hm);
+    hm = mul2(hm, r, nz);
+    lm = mul2(lm, r, nz);
+    const f32x2 P1 = add2(hm, lm);
+    f32x2 kk = sub2(P1, hm);
+    const f32x2 F1 = sub2(lm, kk);
+    t1 = mul2(x0, spl, nz);
+    t2 = sub2(t1, x0);
+    f32x2 hh = sub2(t1, t2);
+    f32x2 lh = sub2(x0, hh);
+    hh = mul2(hh, r, nz);
+    lh = mul2(lh, r, nz);
+    const f32x2 P0 = add2(hh, lh);
+    kk = sub2(P0, hh);
+    const f32x2 F0 = sub2(lh, kk);
+    const f32x2 G1 = add2(F1, lo_r);
+    f32x2 sa, ea, sb, eb, r0, ec;
+    two_sum2(P1, G1, sa, ea);
+    two_sum2(F0, sa, sb, eb);
+    two_sum2(P0, sb, r0, ec);
+    const f32x2 G = add2(ea, eb);
     x0 = r0;
-    x1 = f32_add(ec, G);
-    x2 = f32_sub(G, f32_sub(x1, ec));
+    x1 = add2(ec, G);
+    x2 = sub2(G, sub2(x1, ec));
 }
 
 // FP64 x*2^d -> triple-float (the split of split.cu, repeated here so that this file stands alone).
@@ -104,30 +104,58 @@ __device__ __forceinline__ void tf_load1(double xv, int32_t d, float& x0, float&
     x2 = f32_mul(f32_mul(f32_add(__uint_as_float(craw), -8388608.0f), sc), 0.0078125f);
 }
 
-__device__ __forceinline__ uint32_t next_digit(float& x0, float& x1, float& x2) {
-    tf_mul_254(x0, x1, x2);
-    float d = f32_rint(x0);
-    d = d < -127.0f ? -127.0f : (d >= 127.0f ? 127.0f : d);
-    x0 = f32_sub(x0, d);
-    return (uint32_t)__float2int_rn(d) & 0xFFu;
+// One slice of two elements: t *= 254, d = clamp(rint(t0), +-127), t0 -= d. |t0| <= 254 here, inside
+// the range of rint2 (the 1.5*2^23 rounding, whose values equal cvt.rni's).
+__device__ __forceinline__ f32x2 next_digit2(f32x2& x0, f32x2& x1, f32x2& x2, f32x2 nz) {
+    tf_mul_254(x0, x1, x2, nz);
+    float da, db;
+    unpk2(rint2(x0), da, db);
+    da = fminf(fmaxf(da, -127.0f), 127.0f);
+    db = fminf(fmaxf(db, -127.0f), 127.0f);
+    const f32x2 d = pk2(da, db);
+    x0 = sub2(x0, d);
+    return d;
+}
+
+// Bytes of four integer digits in [-127, 127]: the low byte of the binary32 pattern of d + 1.5*2^23.
+__device__ __forceinline__ uint32_t pack_digits4(f32x2 d01, f32x2 d23) {
+    const f32x2 m = splat2(kRoundMagic);
+    float f0, f1, f2, f3;
+    unpk2(add2(d01, m), f0, f1);
+    unpk2(add2(d23, m), f2, f3);
+    const uint32_t lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x0040);
+    const uint32_t hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x0040);
+    return __byte_perm(lo, hi, 0x5410);
 }
 
 // 16 elements -> p slices of 16 bytes each; element states stay in registers across the slices.
-__device__ __forceinline__ void slice16(const double (&x)[16], int32_t d, int p, int8_t* dst, uint64_t plane) {
-    float s0[16], s1[16], s2[16];
+__device__ __forceinline__ void slice16(const double (&x)[16], int32_t d, int p, float nzf, int8_t* dst,
+                                        uint64_t plane) {
+    const f32x2 nz = splat2(nzf);
+    f32x2 s0[8], s1[8], s2[8];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) tf_load1(x[e], d, s0[e], s1[e], s2[e]);
+    for (int e = 0; e < 8; ++e) {
+        float a0, a1, a2, b0, b1, b2;
+        tf_load1(x[2 * e], d, a0, a1, a2);
+        tf_load1(x[2 * e + 1], d, b0, b1, b2);
+        s0[e] = pk2(a0, b0);
+        s1[e] = pk2(a1, b1);
+        s2[e] = pk2(a2, b2);
+    }
     for (int i = 0; i < p; ++i) {
-        uint32_t w[4] = {0, 0, 0, 0};
+        f32x2 dg[8];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) w[e >> 2] |= next_digit(s0[e], s1[e], s2[e]) << (8 * (e & 3));
-        *reinterpret_cast<uint4*>(dst + (uint64_t)i * plane) = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int e = 0; e < 8; ++e) dg[e] = next_digit2(s0[e], s1[e], s2[e], nz);
+        *reinterpret_cast<uint4*>(dst + (uint64_t)i * plane) =
+            make_uint4(pack_digits4(dg[0], dg[1]), pack_digits4(dg[2], dg[3]), pack_digits4(dg[4], dg[5]),
+                       pack_digits4(dg[6], dg[7]));
     }
 }
 
 __global__ void __launch_bounds__(256) slice_rows_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
                                                          uint64_t lda, const int32_t* __restrict__ delta, int p,
-                                                         int8_t* __restrict__ planes, uint64_t mp, uint64_t kp) {
+                                                         float nz, int8_t* __restrict__ planes, uint64_t mp,
+                                                         uint64_t kp) {
     const uint64_t chunks = kp >> 4, total = mp * chunks, plane = mp * kp;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
          t += (uint64_t)gridDim.x * blockDim.x) {
@@ -146,13 +174,14 @@ __global__ void __launch_bounds__(256) slice_rows_kernel(const double* __restric
 #pragma unroll
             for (int e = 0; e < 16; ++e) x[e] = (in_row && k0 + e < k) ? __ldg(src + e) : 0.0;
         }
-        slice16(x, in_row ? __ldg(delta + row) : 0, p, planes + row * kp + k0, plane);
+        slice16(x, in_row ? __ldg(delta + row) : 0, p, nz, planes + row * kp + k0, plane);
     }
 }
 
 __global__ void __launch_bounds__(256) slice_cols_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
                                                          uint64_t ldb, const int32_t* __restrict__ delta, int p,
-                                                         int8_t* __restrict__ planes, uint64_t np, uint64_t kp) {
+                                                         float nz, int8_t* __restrict__ planes, uint64_t np,
+                                                         uint64_t kp) {
     const int lane = threadIdx.x & 31;
     const uint64_t col_groups = np >> 4, total = col_groups * (kp >> 5), plane = np * kp;
     for (uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total;
@@ -163,7 +192,7 @@ __global__ void __launch_bounds__(256) slice_cols_kernel(const double* __restric
         double x[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) x[e] = (in_col && r0 + e < k) ? __ldg(b + (r0 + e) * ldb + col) : 0.0;
-        slice16(x, in_col ? __ldg(delta + col) : 0, p, planes + col * kp + r0, plane);
+        slice16(x, in_col ? __ldg(delta + col) : 0, p, nz, planes + col * kp + r0, plane);
     }
 }
 
@@ -301,7 +330,7 @@ void launch_slice_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, co
     const uint64_t total = mp * (kp / 16);
     if (!total) return;
     slice_rows_kernel<<<(unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 32), 256, 0, st>>>(
-        a, m, k, lda, delta, p, planes, mp, kp);
+        a, m, k, lda, delta, p, -0.0f, planes, mp, kp);
     OZTT_CUDA(cudaGetLastError());
 }
 
@@ -311,7 +340,7 @@ void launch_slice_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, co
     const uint64_t warps = (np / 16) * (kp / 32);
     if (!warps) return;
     slice_cols_kernel<<<(unsigned)std::min<uint64_t>((warps + 7) / 8, (uint64_t)sm_count() * 32), 256, 0, st>>>(
-        b, k, n, ldb, delta, p, planes, np, kp);
+        b, k, n, ldb, delta, p, -0.0f, planes, np, kp);
     OZTT_CUDA(cudaGetLastError());
 }
 

@@ -14,9 +14,12 @@
 // The residues must be bit-identical to the reference's. Its integer A' is not the rounded value of
 // x*2^(b-e): only the top limb of a triple-float is rounded (|A' - X| <= 1), and for an even modulus
 // the sign of a residue of m/2 depends on the binary32 rounding inside ModRound. The digit kernel
-// therefore executes the reference's binary32 operation sequence one PTX instruction at a time with
-// round-to-nearest-even and flush-to-zero (oztt_common.cuh). Values differ from the reference's model
-// at most in the sign of a zero, which no later step can turn into a different number.
+// therefore executes the reference's binary32 operation sequence with round-to-nearest-even and
+// flush-to-zero (oztt_common.cuh), two elements per instruction on the packed FP32 pipe. Rounding to
+// an integer uses the 1.5*2^23 addition instead of the conversion unit (a quarter-rate pipe that
+// would otherwise bound the kernel); its values equal the reference's, and like the rest of the
+// sequence they differ at most in the sign of a zero, which no later step can turn into a different
+// number. The residue bytes come from the binary32 patterns directly, again without conversions.
 //
 // Layout in HBM: A is read row-major (m x k, lda) and written as S planes [S][mp][kp] int8 (K
 // contiguous). B is read row-major (k x n, ldb) and written transposed, [S][np][kp] int8, so that
@@ -29,6 +32,7 @@ namespace oztt {
 
 struct SplitConst {
     int32_t S;
+    float nz;  // -0.0, the run-time addend of the packed multiplies (mul2 in oztt_common.cuh)
     float m[OZTT_MAXS], rinv[OZTT_MAXS];
     float c[4][OZTT_MAXS];
 };
@@ -178,78 +182,92 @@ __device__ __forceinline__ void two_sum(float x, float y, float& s, float& e) {
     e = f32_add(a, f32_sub(y, bb));
 }
 
-// The ND radix-2^20 digits, top digit first: round the top limb, subtract, multiply the triple by
-// 2^20 and renormalise (TwoSum, TwoSum, FastTwoSum).
+// The ND radix-2^20 digits of two elements, top digit first: round the top limb, subtract, multiply
+// the triple by 2^20 and renormalise (TwoSum, TwoSum, FastTwoSum); every operation on both elements
+// at once. |x0| < 2^21 wherever it is rounded (the top limb is below 2^shift <= 2^20, later ones
+// below 2^19 + 1), inside the range of rint2.
 template <int ND>
-__device__ __forceinline__ void make_digits(double xv, int32_t d, float* dg) {
-    float x0, x1, x2;
-    tf_load(xv, d, x0, x1, x2);
+__device__ __forceinline__ void make_digits2(double xa, double xb, int32_t d, f32x2 nz, f32x2* dg) {
+    float a0, a1, a2, b0, b1, b2;
+    tf_load(xa, d, a0, a1, a2);
+    tf_load(xb, d, b0, b1, b2);
+    f32x2 x0 = pk2(a0, b0), x1 = pk2(a1, b1), x2 = pk2(a2, b2);
+    const f32x2 radix = splat2(1048576.0f);
 #pragma unroll
     for (int i = 0; i < ND; ++i) {
         if (i > 0) {
-            x0 = f32_mul(x0, 1048576.0f);
-            x1 = f32_mul(x1, 1048576.0f);
-            x2 = f32_mul(x2, 1048576.0f);
-            float s3, e4, s5, e6;
-            two_sum(x1, x2, s3, e4);
-            two_sum(x0, s3, s5, e6);
+            x0 = mul2(x0, radix, nz);
+            x1 = mul2(x1, radix, nz);
+            x2 = mul2(x2, radix, nz);
+            // TwoSum(x1, x2) -> (s3, e4); TwoSum(x0, s3) -> (s5, e6)
+            const f32x2 s3 = add2(x1, x2);
+            f32x2 bb = sub2(s3, x1);
+            const f32x2 e4 = add2(sub2(x1, sub2(s3, bb)), sub2(x2, bb));
+            const f32x2 s5 = add2(x0, s3);
+            bb = sub2(s5, x0);
+            const f32x2 e6 = add2(sub2(x0, sub2(s5, bb)), sub2(s3, bb));
             x0 = s5;
-            x1 = f32_add(e6, e4);
-            x2 = f32_sub(e4, f32_sub(x1, e6));
+            x1 = add2(e6, e4);
+            x2 = sub2(e4, sub2(x1, e6));
         }
-        const float dig = f32_rint(x0);
+        const f32x2 dig = rint2(x0);
         dg[i] = dig;
-        x0 = f32_sub(x0, dig);
+        x0 = sub2(x0, dig);
     }
 }
 
-// ModRound d - rint(d*rinv)*m. For the INT8 moduli every input is an integer below 2^22, so
-// rint(d*rinv)*m is an exact integer and the fused form equals the reference's separate
-// multiply and subtract.
-__device__ __forceinline__ float mod_round(float d, float m, float rinv) {
-    return f32_fma(-f32_rint(f32_mul(d, rinv)), m, d);
+// ModRound d - rint(d*rinv)*m for two values; the products and sums are exact integers below 2^22.
+__device__ __forceinline__ f32x2 mod_round2(f32x2 d, f32x2 negm, f32x2 rinv, f32x2 nz) {
+    return fma2(rint2(mul2(d, rinv, nz)), negm, d);
 }
 
-// Residue of A' from its digits (top first), the reference's chain; products of a reduced digit
-// and a weight, and the partial sums, are exact integers below 2^22 (fused multiply-add = the
-// separate operations).
+// Residues of A' from its digits (top first), the reference's chain; products of a reduced digit
+// and a weight, and the partial sums, are exact integers below 2^22.
 template <int ND>
-__device__ __forceinline__ float residue(const float* dg, float m, float ri, float c0, float c1, float c2,
-                                         float c3) {
-    float acc = f32_fma(mod_round(dg[ND - 2], m, ri), c0, dg[ND - 1]);
-    acc = f32_fma(mod_round(dg[ND - 3], m, ri), c1, acc);
+__device__ __forceinline__ f32x2 residue2(const f32x2* dg, f32x2 negm, f32x2 ri, f32x2 c0, f32x2 c1, f32x2 c2,
+                                          f32x2 c3, f32x2 nz) {
+    f32x2 acc = fma2(mod_round2(dg[ND - 2], negm, ri, nz), c0, dg[ND - 1]);
+    acc = fma2(mod_round2(dg[ND - 3], negm, ri, nz), c1, acc);
     if constexpr (ND >= 4) {
-        acc = mod_round(acc, m, ri);
+        acc = mod_round2(acc, negm, ri, nz);
         if constexpr (ND >= 5) {
-            acc = f32_fma(mod_round(dg[0], m, ri), c3, acc);
-            acc = mod_round(acc, m, ri);
+            acc = fma2(mod_round2(dg[0], negm, ri, nz), c3, acc);
+            acc = mod_round2(acc, negm, ri, nz);
         }
-        acc = f32_fma(mod_round(dg[ND - 4], m, ri), c2, acc);
+        acc = fma2(mod_round2(dg[ND - 4], negm, ri, nz), c2, acc);
     }
-    return mod_round(acc, m, ri);
+    return mod_round2(acc, negm, ri, nz);
 }
 
-__device__ __forceinline__ uint32_t pack4(float r0, float r1, float r2, float r3) {
-    const uint32_t b0 = (uint32_t)__float2int_rn(r0) & 0xFFu, b1 = (uint32_t)__float2int_rn(r1) & 0xFFu,
-                   b2 = (uint32_t)__float2int_rn(r2) & 0xFFu, b3 = (uint32_t)__float2int_rn(r3) & 0xFFu;
-    return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+// The low bytes of four integer-valued residues r + 1.5*2^23 (binary32 patterns whose low 22 bits are
+// the two's complement integer), packed into one word, first residue in the low byte.
+__device__ __forceinline__ uint32_t pack4(f32x2 r01, f32x2 r23) {
+    const f32x2 m = splat2(kRoundMagic);
+    float f0, f1, f2, f3;
+    unpk2(add2(r01, m), f0, f1);
+    unpk2(add2(r23, m), f2, f3);
+    const uint32_t lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x0040);
+    const uint32_t hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x0040);
+    return __byte_perm(lo, hi, 0x5410);
 }
 
-// Writes the S residue planes of 16 elements whose digits are in dg (16 x ND) to dst + s*plane.
+// Writes the S residue planes of 16 elements whose digits are in dg (8 pairs x ND) to dst + s*plane.
 template <int ND>
-__device__ __forceinline__ void store_residues(const float (&dg)[16][ND], const SplitConst& sc, int8_t* dst,
+__device__ __forceinline__ void store_residues(const f32x2 (&dg)[8][ND], const SplitConst& sc, int8_t* dst,
                                                uint64_t plane) {
+    const f32x2 nz = splat2(sc.nz);
     for (int s = 0; s < sc.S; ++s) {
-        const float m = sc.m[s], ri = sc.rinv[s];
-        const float c0 = sc.c[0][s], c1 = sc.c[1][s], c2 = sc.c[2][s], c3 = sc.c[3][s];
-        float r[16];
+        const f32x2 negm = splat2(-sc.m[s]), ri = splat2(sc.rinv[s]);
+        const f32x2 c0 = splat2(sc.c[0][s]), c1 = splat2(sc.c[1][s]), c2 = splat2(sc.c[2][s]),
+                    c3 = splat2(sc.c[3][s]);
+        f32x2 r[8];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) r[e] = residue<ND>(dg[e], m, ri, c0, c1, c2, c3);
+        for (int e = 0; e < 8; ++e) r[e] = residue2<ND>(dg[e], negm, ri, c0, c1, c2, c3, nz);
         uint4 v;
-        v.x = pack4(r[0], r[1], r[2], r[3]);
-        v.y = pack4(r[4], r[5], r[6], r[7]);
-        v.z = pack4(r[8], r[9], r[10], r[11]);
-        v.w = pack4(r[12], r[13], r[14], r[15]);
+        v.x = pack4(r[0], r[1]);
+        v.y = pack4(r[2], r[3]);
+        v.z = pack4(r[4], r[5]);
+        v.w = pack4(r[6], r[7]);
         *reinterpret_cast<uint4*>(dst + (uint64_t)s * plane) = v;
     }
 }
@@ -279,9 +297,9 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const double* __restric
             for (int e = 0; e < 16; ++e) x[e] = (in_row && k0 + e < k) ? __ldg(p + e) : 0.0;
         }
         const int32_t d = in_row ? __ldg(delta + row) : 0;
-        float dg[16][ND];
+        f32x2 dg[8][ND];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) make_digits<ND>(x[e], d, dg[e]);
+        for (int e = 0; e < 8; ++e) make_digits2<ND>(x[2 * e], x[2 * e + 1], d, splat2(sc.nz), dg[e]);
         store_residues<ND>(dg, sc, planes + row * kp + k0, plane);
     }
 }
@@ -305,9 +323,9 @@ __global__ void __launch_bounds__(256) split_cols_kernel(const double* __restric
 #pragma unroll
         for (int e = 0; e < 16; ++e) x[e] = (in_col && r0 + e < k) ? __ldg(b + (r0 + e) * ldb + col) : 0.0;
         const int32_t d = in_col ? __ldg(delta + col) : 0;
-        float dg[16][ND];
+        f32x2 dg[8][ND];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) make_digits<ND>(x[e], d, dg[e]);
+        for (int e = 0; e < 8; ++e) make_digits2<ND>(x[2 * e], x[2 * e + 1], d, splat2(sc.nz), dg[e]);
         store_residues<ND>(dg, sc, planes + col * kp + r0, plane);
     }
 }
@@ -323,6 +341,7 @@ static int device_sms() {
 static SplitConst split_const(const oztt_ii_plan& p) {
     SplitConst sc{};
     sc.S = p.S;
+    sc.nz = -0.0f;
     for (int s = 0; s < p.S; ++s) {
         sc.m[s] = (float)p.moduli[s];
         sc.rinv[s] = p.rinv[s];
