@@ -94,12 +94,14 @@ __device__ __forceinline__ double crt_finish(const uint64_t (&acc)[NW], int32_t 
         r = 0.0;
     else if (lead > 1023)
         r = __longlong_as_double(0x7FF0000000000000ll);
-    else
-        r = ldexp(v, p - 63 + g - rc.two_b);
+    else  // v * 2^(p - 63 + g - 2b), a normal number: add the scale to the exponent field
+        r = __longlong_as_double(__double_as_longlong(v) + ((long long)(p - 63 + g - rc.two_b) << 52));
     return neg ? -r : r;
 }
 
-// One thread = 4 consecutive columns of one row: S 32-bit loads (one per digit plane), 32 bytes out.
+// One thread = 4 consecutive columns of one row: the S digit words (one 32-bit load per plane) are all
+// requested before any is used, so the loads of a thread overlap instead of waiting one by one; then
+// X = sum_s k_s (M/m_s) column by column; 32 bytes out.
 template <int NW>
 __global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ kp, uint64_t mp, uint64_t np,
                                                     const int32_t* __restrict__ dA, const int32_t* __restrict__ dB,
@@ -110,16 +112,21 @@ __global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ 
          t += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t i = t / nq, j0 = (t - i * nq) << 2;
         const uint8_t* base = kp + i * np + j0;
+        uint32_t kw[OZTT_MAXS];
+#pragma unroll
+        for (int s = 0; s < OZTT_MAXS; ++s)
+            kw[s] = (uint32_t)s < rc.S ? __ldg(reinterpret_cast<const uint32_t*>(base + s * plane)) : 0u;
         uint64_t acc[4][NW];
 #pragma unroll
         for (int e = 0; e < 4; ++e)
 #pragma unroll
             for (int w = 0; w < NW; ++w) acc[e][w] = 0;
-        for (uint32_t s = 0; s < rc.S; ++s) {
-            const uint32_t kw = __ldg(reinterpret_cast<const uint32_t*>(base + s * plane));
+#pragma unroll
+        for (int s = 0; s < OZTT_MAXS; ++s) {
+            if ((uint32_t)s >= rc.S) break;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const uint32_t k = (kw >> (8 * e)) & 0xFFu;
+                const uint32_t k = (kw[s] >> (8 * e)) & 0xFFu;
 #pragma unroll
                 for (int w = 0; w < NW; ++w) acc[e][w] += (uint64_t)k * rc.Q[s][w];
             }
