@@ -468,7 +468,7 @@ def main() -> None:
             e2e_s = float(t[0])
         result["e2e"] = {"value": flops / e2e_s / 1e12, "unit": "TFLOPS", "s_per_step": e2e_s,
                          "h2d_bytes_per_step": 8 * (m * k + k * n), "d2h_bytes_per_step": 8 * m * n,
-                         "path": "ozTTgemm::Context::gemm via oztt_gemm (validation, host planning, pinned H2D, "
+                         "path": "ozTTgemm::Context::gemm via oztt_gemm (host validation, pinned H2D, device-measured plan statistics, "
                                  "GPU pipeline, D2H)"}
     # ---- CPU baseline (rank 0 at N=1) ------------------------------------------------------------------
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

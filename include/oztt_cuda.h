@@ -133,6 +133,12 @@ int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* 
  * reference would throw (K blocking needed, Horner exponent budget exceeded). */
 int oztt_i_int8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
                      oztt_i_plan* plan, char* err, size_t errlen);
+/* Scheme II INT8 plan for operands already on the device (a: m x k, b: k x n, row-major): the input
+ * statistics of the precision policy are measured by kernels on `stream` (bit-identical to the host
+ * measurement of oztt_ii_int8_plan), the decisions made on the host. Synchronises `stream`. */
+int oztt_ii_int8_plan_device(int device_id, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                             uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan* plan,
+                             void* stream, char* err, size_t errlen);
 /* The Scheme I INT8 pipeline on host buffers (ozaki1_int8::run, src/ozaki1.cpp:192-282). */
 int oztt_i_int8_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
                     const oztt_i_plan* plan, char* err, size_t errlen);

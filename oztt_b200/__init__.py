@@ -146,6 +146,8 @@ _SIGNATURES = {
     "oztt_ii_recon": [_P, _U64, _U64, _P, _P, ctypes.POINTER(IIPlan), _P, _U64, _U64, _U64, _P, _ERR, _SZ],
     "oztt_device_info": [ctypes.c_int, ctypes.POINTER(_I32), ctypes.POINTER(_I32), ctypes.POINTER(_I32)],
     "oztt_ii_padded_dims": [_U64, _U64, _U64, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
+    "oztt_ii_int8_plan_device": [ctypes.c_int, _P, _P, _U64, _U64, _U64, ctypes.c_uint32, _I32, _I32,
+                                 ctypes.POINTER(IIPlan), _P, _ERR, _SZ],
     "oztt_i_int8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _P, _P, _ERR, _SZ],
@@ -154,13 +156,14 @@ _SIGNATURES = {
     "oztt_i_diag_gemm": [_P, _P, _U64, _U64, _U64, _I32, _P, _P, _ERR, _SZ],
     "oztt_i_recon": [_P, _U64, _U64, _P, _P, _I32, _P, _U64, _U64, _U64, _P, _ERR, _SZ],
     "oztt_test_udiv_small": [ctypes.c_uint32, ctypes.c_uint32],
+    "oztt_test_ext80_dot": [_P, _P, _U64, ctypes.c_double],
 }
 
-_RESTYPES = {"oztt_test_udiv_small": ctypes.c_uint32, "oztt_ii_padded_dims": None, "oztt_eval_inputs": None,
+_RESTYPES = {"oztt_test_udiv_small": ctypes.c_uint32, "oztt_test_ext80_dot": ctypes.c_double, "oztt_ii_padded_dims": None, "oztt_eval_inputs": None,
              "oztt_eval_output_hash": ctypes.c_uint64}
 
 # Symbols declared in include/oztt_cuda.h (the tests check that the library exports each of them).
-C_ABI_SYMBOLS = [name for name in _SIGNATURES if name != "oztt_test_udiv_small"]
+C_ABI_SYMBOLS = [name for name in _SIGNATURES if not name.startswith("oztt_test_")]
 
 
 def _load() -> ctypes.CDLL:
@@ -268,6 +271,19 @@ def ii_int8_plan(a, b, m: int, n: int, k: int, max_moduli: int = 0, reconstructi
     err = _errbuf()
     rc = _lib().oztt_ii_int8_plan(av.ctypes.data, bv.ctypes.data, m, n, k, max_moduli, reconstruction, fixed_bits,
                                ctypes.byref(plan), err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return plan
+
+
+def ii_int8_plan_device(a_ptr: int, b_ptr: int, m: int, n: int, k: int, max_moduli: int = 0, reconstruction: int = 0,
+                        fixed_bits: int = 0, stream: int = 0, device_id: int = 0) -> IIPlan:
+    """Scheme II INT8 plan for device-resident operands, the statistics measured on the device
+    (oztt_ii_int8_plan_device)."""
+    plan = IIPlan()
+    err = _errbuf()
+    rc = _lib().oztt_ii_int8_plan_device(device_id, a_ptr, b_ptr, m, n, k, max_moduli, reconstruction, fixed_bits,
+                                         ctypes.byref(plan), stream, err, len(err))
     if rc != OK:
         _raise(rc, err.value)
     return plan

@@ -26,10 +26,8 @@
 #include "planner.hpp"
 
 namespace oztt {
-void run_ii_int8_host(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
-                      const oztt_ii_plan& p);
-void open_device_checked(int device_id);
-struct Error;
+int run_ii_int8_planned(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                        uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_ii_plan& p, std::string& err);
 }  // namespace oztt
 
 namespace ozTTgemm {
@@ -48,31 +46,51 @@ std::uint32_t padded(std::size_t value, std::size_t quantum) {
         throw std::invalid_argument("matrix dimension exceeds the supported device index range");
     return static_cast<std::uint32_t>((value + quantum - 1) / quantum * quantum);
 }
+// Finiteness and the range of every nonzero row maximum of A and column maximum of B, with the
+// reference's order of reports (context.cpp:37-62): A's rows in order (a row's NaN/Inf before its
+// maximum), then any NaN/Inf in B, then B's column maxima. The scans run on all host threads; each
+// thread records per row (per column block) what it found, and the reports are made in order after.
 void check_values(std::span<const double> a, std::span<const double> b, std::size_t m, std::size_t n, std::size_t k) {
     constexpr double maximum = 0x1.fep127;
     constexpr double minimum = 0x1p-126;
-    const auto check_max = [&](double x) {
-        if (x != 0 && (x < minimum || x > maximum))
-            throw std::invalid_argument(
-                "each nonzero row maximum of A and column maximum of B must be in [2^-126, max_BF16]");
-    };
-    for (std::size_t i = 0; i < m; ++i) {
-        double mx = 0;
-        for (std::size_t j = 0; j < k; ++j) {
-            const double x = a[i * k + j];
-            if (!std::isfinite(x)) throw std::invalid_argument("A contains NaN or infinity");
-            mx = std::max(mx, std::abs(x));
+    const auto out_of_range = [&](double x) { return x != 0 && (x < minimum || x > maximum); };
+    const char* range_msg = "each nonzero row maximum of A and column maximum of B must be in [2^-126, max_BF16]";
+    std::vector<double> row_max(m);
+    std::vector<unsigned char> row_bad(m, 0);
+    oztt::parallel_ranges(m, [&](std::uint64_t r0, std::uint64_t r1) {
+        for (std::uint64_t i = r0; i < r1; ++i) {
+            double mx = 0;
+            bool bad = false;
+            const double* p = a.data() + i * k;
+            for (std::size_t j = 0; j < k; ++j) {
+                const double x = p[j];
+                bad |= !std::isfinite(x);
+                mx = std::max(mx, std::abs(x));
+            }
+            row_max[i] = mx;
+            row_bad[i] = bad;
         }
-        check_max(mx);
+    });
+    for (std::size_t i = 0; i < m; ++i) {
+        if (row_bad[i]) throw std::invalid_argument("A contains NaN or infinity");
+        if (out_of_range(row_max[i])) throw std::invalid_argument(range_msg);
     }
     std::vector<double> maxima(n, 0);
-    for (std::size_t i = 0; i < k; ++i)
-        for (std::size_t j = 0; j < n; ++j) {
-            const double x = b[i * n + j];
-            if (!std::isfinite(x)) throw std::invalid_argument("B contains NaN or infinity");
-            maxima[j] = std::max(maxima[j], std::abs(x));
+    std::vector<unsigned char> col_bad(n, 0);
+    oztt::parallel_ranges(n, [&](std::uint64_t c0, std::uint64_t c1) {
+        for (std::size_t i = 0; i < k; ++i) {
+            const double* p = b.data() + i * n;
+            for (std::uint64_t j = c0; j < c1; ++j) {
+                const double x = p[j];
+                col_bad[j] |= !std::isfinite(x);
+                maxima[j] = std::max(maxima[j], std::abs(x));
+            }
         }
-    for (double x : maxima) check_max(x);
+    });
+    for (std::size_t j = 0; j < n; ++j)
+        if (col_bad[j]) throw std::invalid_argument("B contains NaN or infinity");
+    for (double x : maxima)
+        if (out_of_range(x)) throw std::invalid_argument(range_msg);
 }
 void check_options(const Options& o) {
     if (o.scheme != Scheme::I && o.scheme != Scheme::II) throw std::invalid_argument("unknown Ozaki scheme");
@@ -164,13 +182,13 @@ Info Context::Impl::execute(std::span<const double> a, std::span<const double> b
         info.padded_k = v.kp;
         return info;
     }
+    // A and B go to the device first; the precision policy measures them there (bit-identical to the
+    // host measurement) and the host makes the decisions; C is written only after the pipeline ran.
     oztt_ii_plan plan;
     std::string msg;
-    int rc = oztt::plan_ii_int8(a.data(), b.data(), m, n, k, opt.max_moduli, recon_code(opt.reconstruction), 0, plan, msg);
+    const int rc = oztt::run_ii_int8_planned(options.device_id, a.data(), b.data(), c.data(), m, n, k, opt.max_moduli,
+                                             recon_code(opt.reconstruction), plan, msg);
     if (rc != OZTT_OK) rethrow(rc, msg);
-    char err[512] = {0};
-    rc = oztt_ii_int8_run(options.device_id, a.data(), b.data(), c.data(), m, n, k, &plan, err, sizeof err);
-    if (rc != OZTT_OK) rethrow(rc, err);
     opened = true;
     Info info{Scheme::II, opt.format};
     info.moduli = (std::uint32_t)plan.S;

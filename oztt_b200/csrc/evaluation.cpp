@@ -44,3 +44,14 @@ extern "C" uint64_t oztt_eval_output_hash(const double* c, uint64_t count) {
     }
     return h;
 }
+
+// Host model of one row of the device's long-double sketch (stats.cu, sketch_kernel): the sum
+// (double) sum_j (long double)(x[j]*rg) * g[j] in the 64-bit-significand arithmetic of ext80.h, for
+// the CPU tests of that arithmetic against the host's own long double.
+#include "ext80.h"
+extern "C" double oztt_test_ext80_dot(const double* x, const double* g, uint64_t n, double rg) {
+    namespace e = oztt::ext80;
+    e::Ext acc = e::zero();
+    for (uint64_t j = 0; j < n; ++j) acc = e::add(acc, e::mul(e::from_double(x[j] * rg), e::from_double(g[j])));
+    return e::to_double(acc);
+}

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "oztt_common.cuh"
+#include "planner.hpp"
 #include "runtime.cuh"
 
 namespace oztt {
@@ -154,6 +155,57 @@ void run_ii_int8_host(int device_id, const double* a, const double* b, double* c
     }
 }
 
+PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
+                                cudaStream_t st);
+
+// Plan from device-resident operands: the input statistics are measured on the device
+// (device_policy_stats, bit-identical to the host measurement), the decisions made on the host.
+int plan_ii_int8_device(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
+                        int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan& p, std::string& err,
+                        cudaStream_t st) {
+    return plan_ii_int8_with([&](uint32_t N, uint32_t) { return device_policy_stats(a, b, m, n, k, N, st); }, m, n,
+                             k, max_moduli, reconstruction, fixed_bits, p, err);
+}
+
+// The whole call as Context::gemm makes it: A and B to the device, the plan from device statistics,
+// the pipeline, C back. Returns OZTT_OK, or an error code with its message (C is then untouched).
+static int run_ii_int8_planned_impl(int device_id, const double* a, const double* b, double* c, uint64_t m,
+                                    uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction,
+                                    oztt_ii_plan& p, std::string& err) {
+    open_device(device_id);
+    cudaStream_t st;
+    OZTT_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    struct StreamGuard {
+        cudaStream_t s;
+        ~StreamGuard() {
+            cudaStreamSynchronize(s);
+            cudaStreamDestroy(s);
+        }
+    } guard{st};
+    DevBuf da(st, m * k * 8), db(st, k * n * 8);
+    OZTT_CUDA(cudaMemcpyAsync(da.p, a, m * k * 8, cudaMemcpyHostToDevice, st));
+    OZTT_CUDA(cudaMemcpyAsync(db.p, b, k * n * 8, cudaMemcpyHostToDevice, st));
+    const int rc = plan_ii_int8_device(da.as<double>(), db.as<double>(), m, n, k, max_moduli, reconstruction, 0, p,
+                                       err, st);
+    if (rc != OZTT_OK) return rc;
+    DevBuf dc(st, m * n * 8);
+    run_ii_int8_device(da.as<double>(), db.as<double>(), dc.as<double>(), m, n, k, p, st);
+    OZTT_CUDA(cudaMemcpyAsync(c, dc.p, m * n * 8, cudaMemcpyDeviceToHost, st));
+    OZTT_CUDA(cudaStreamSynchronize(st));
+    return OZTT_OK;
+}
+
+int run_ii_int8_planned(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                        uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_ii_plan& p, std::string& err) {
+    char buf[1024];
+    int inner = OZTT_OK;
+    const int rc = guarded(buf, sizeof buf, [&] {
+        inner = run_ii_int8_planned_impl(device_id, a, b, c, m, n, k, max_moduli, reconstruction, p, err);
+    });
+    if (rc != OZTT_OK) err = buf;
+    return rc != OZTT_OK ? rc : inner;
+}
+
 void open_device_checked(int device_id) { open_device(device_id); }
 
 }  // namespace oztt
@@ -169,6 +221,19 @@ int oztt_ii_int8_run(int device_id, const double* a, const double* b, double* c,
         if (!a || !b || !c || !plan) throw Error(OZTT_EINVAL, "null argument");
         if (!m || !n || !k) throw Error(OZTT_EINVAL, "matrix dimensions are zero");
         oztt::run_ii_int8_host(device_id, a, b, c, m, n, k, *plan);
+    });
+}
+
+int oztt_ii_int8_plan_device(int device_id, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                             uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan* plan,
+                             void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a || !b || !plan) throw Error(OZTT_EINVAL, "null argument");
+        oztt::open_device(device_id);
+        std::string msg;
+        const int rc = oztt::plan_ii_int8_device(a, b, m, n, k, max_moduli, reconstruction, fixed_bits, *plan, msg,
+                                                 reinterpret_cast<cudaStream_t>(stream));
+        if (rc != OZTT_OK) throw Error(rc, msg);
     });
 }
 

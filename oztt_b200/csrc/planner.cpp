@@ -334,6 +334,14 @@ void fill_crt_constants(const std::vector<int>& mods, oztt_ii_plan& p) {
 
 int plan_ii_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
                  int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan& p, std::string& err) {
+    return plan_ii_int8_with(
+        [&](uint32_t N, uint32_t K) { return measure_policy_stats(a, b, m, n, k, N, K); }, m, n, k, max_moduli,
+        reconstruction, fixed_bits, p, err);
+}
+
+int plan_ii_int8_with(const std::function<PolicyStats(uint32_t, uint32_t)>& stats, uint64_t m, uint64_t n, uint64_t k,
+                      uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan& p,
+                      std::string& err) {
     std::memset(&p, 0, sizeof(p));
     if (m == 0 || n == 0 || k == 0) {
         err = "matrix dimensions are zero";
@@ -357,11 +365,11 @@ int plan_ii_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint6
     if (b_fixed) {
         b_cap = fixed_bits;
     } else {
-        st = measure_policy_stats(a, b, m, n, k, p.N, p.K);
+        st = stats(p.N, p.K);
         b_cap = policy_width_cap(st);
     }
     const uint32_t S_req = max_moduli ? max_moduli : (b_fixed ? kDefSInt8 : (uint32_t)kMaxS);
-    if (b_fixed && reconstruction == OZTT_RECON_AUTO) st = measure_policy_stats(a, b, m, n, k, p.N, p.K);
+    if (b_fixed && reconstruction == OZTT_RECON_AUTO) st = stats(p.N, p.K);
     const ModuliChoice mo = choose_moduli_int8(p.K, (int)S_req, b_cap);
     p.b_cap = b_cap;
     p.S_req = (int32_t)S_req;

@@ -3,6 +3,7 @@
 #pragma once
 #include <algorithm>
 #include <cstdint>
+#include <functional>
 #include <string>
 #include <thread>
 #include <vector>
@@ -61,6 +62,12 @@ void fill_crt_constants(const std::vector<int>& mods, oztt_ii_plan& p);
 // The whole plan; returns an OZTT_* code and a message.
 int plan_ii_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
                  int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan& p, std::string& err);
+
+// The same with the input statistics from `stats(N, K)` (padded N and K), e.g. measured on the device
+// (device_policy_stats in stats.cu); called only when the policy needs them.
+int plan_ii_int8_with(const std::function<PolicyStats(uint32_t, uint32_t)>& stats, uint64_t m, uint64_t n, uint64_t k,
+                      uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan& p,
+                      std::string& err);
 
 // Scheme I INT8 (planner1.cpp): the slice count oz_fp64_p selects for row-major a (m x k), b (k x n)
 // with padded planning dimensions M, N, K; and the whole plan (slices > 0 fixes p).
