@@ -28,6 +28,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "oztt_common.cuh"
@@ -367,6 +368,266 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
 }
 
+// ---- CTA pairs: tcgen05.mma.cta_group::2 -------------------------------------------------------
+// The same work with two CTAs (one per SM of a cluster pair) sharing each MMA: M = 256 rows of A
+// (128 in each CTA's shared memory) against N = 256 rows of B (128 in each CTA), so that each SM
+// stages 32 KB per 128-deep K block instead of 48 KB for the same 128 x 256 output per SM. The leader
+// CTA (rank 0) issues the MMAs; both CTAs load their halves with TMA (no multicast), completing bytes
+// on the leader's stage barrier; the leader's tcgen05.commit releases the stage in both CTAs and hands
+// each CTA its 128 x 256 accumulator half; the epilogue warps of both CTAs report a drained
+// accumulator to the leader. Six stages of 32 KB per CTA.
+namespace pair {
+
+constexpr uint32_t BM = 128, BN = 256, BNH = 128, BK = 128, UK = 32;
+constexpr uint32_t STAGES = 6;
+constexpr uint32_t A_BYTES = BM * BK;
+constexpr uint32_t B_BYTES = BNH * BK;
+constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t ACC_COLS = BN;
+constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+constexpr uint32_t NUM_THREADS = 192;
+constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+// kind::i8, s32 accumulator, signed A and B, K-major, N = 256, M = 256 (the pair).
+constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) | ((256u >> 4) << 24);
+constexpr uint64_t PEER_DRAIN_NS = 5000000ull;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to(uint32_t smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA load into this CTA's shared memory, completing its bytes on a barrier of either CTA of the pair.
+__device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* map, uint32_t dst, uint32_t bar_cluster,
+                                                 int32_t c0, int32_t c1, int32_t c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+        "%5}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate)
+        : "memory");
+}
+// Arrives once on the barrier at `bar_cluster` (either CTA) when all MMAs issued so far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+                 : "memory");
+}
+
+}  // namespace pair
+
+template <int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::NUM_THREADS, 1)
+    residue_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             void* __restrict__ out, uint32_t tiles_m2, uint32_t tiles_n, uint32_t num_kb, uint64_t mp,
+                             uint64_t np, const EpiConst ec, int* err) {
+    // the pair's tile constants (they shadow the single-CTA ones of namespace gemm)
+    constexpr uint32_t BM = pair::BM, BN = pair::BN, BNH = pair::BNH, BK = pair::BK, UK = pair::UK;
+    constexpr uint32_t STAGES = pair::STAGES, A_BYTES = pair::A_BYTES, STAGE_BYTES = pair::STAGE_BYTES;
+    constexpr uint32_t ACC_COLS = pair::ACC_COLS, TMEM_COLS = pair::TMEM_COLS;
+    using pair::arrive_remote;
+    using pair::cluster_rank;
+    using pair::cluster_sync;
+    using pair::map_to;
+    using pair::tma_load_3d_pair;
+    using pair::umma_commit_pair;
+    using pair::umma_i8_pair;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty_bar = full_bar + STAGES;
+    uint64_t* tfull_bar = empty_bar + STAGES;
+    uint64_t* tempty_bar = tfull_bar + 2;
+    uint64_t* drain_bar = tempty_bar + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const uint32_t first_tile = blockIdx.x >> 1, tile_step = gridDim.x >> 1;
+    const uint32_t num_tiles = ec.S * tiles_m2 * tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar + s, 1);
+            mbar_init(empty_bar + s, 1);
+        }
+        for (uint32_t a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar + a, 1);
+            mbar_init(tempty_bar + a, 8);  // 4 epilogue warps in each CTA of the pair
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the peer's barriers are initialised before anything is signalled across the pair
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+            uint32_t stage = 0, phase = 0;
+            uint32_t filled = 0, last_phase = 0;
+            bool ok = true, issued = false;
+            for (uint32_t tile = first_tile; ok && tile < num_tiles; tile += tile_step) {
+                uint32_t plane, tm2, tn, kb_total;
+                tile_work<MODE>(tile, ec.S, tiles_m2, tiles_n, num_kb, plane, tm2, tn, kb_total);
+                for (uint32_t kb = 0; kb < kb_total; ++kb) {
+                    if (!mbar_wait(empty_bar + stage, phase ^ 1u, abort_flag, err, ERR_WAIT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    int32_t k_el, pa, pb;
+                    kblock_coords<MODE>(kb, plane, num_kb, k_el, pa, pb);
+                    if (rank == 0) mbar_expect_tx(full_bar + stage, 2 * STAGE_BYTES);
+                    const uint32_t full_leader = map_to(smem_u32(full_bar + stage), 0);
+                    const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+                    tma_load_3d_pair(&tmA, sa, full_leader, k_el, (int32_t)(tm2 * 2 * BM + rank * BM), pa);
+                    tma_load_3d_pair(&tmB, sa + A_BYTES, full_leader, k_el, (int32_t)(tn * BN + rank * BNH), pb);
+                    issued = true;
+                    filled |= 1u << stage;
+                    last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {  // let the loads this thread issued land before the CTA may exit
+                if (rank == 0) {
+                    for (uint32_t st = 0; st < STAGES; ++st)
+                        if (filled & (1u << st)) mbar_wait_drain(full_bar + st, (last_phase >> st) & 1u, 200000000ull);
+                } else if (issued) {  // the peer's loads complete on the leader's barriers: wait a fixed time
+                    const uint64_t t0 = global_timer_ns();
+                    while (global_timer_ns() - t0 < pair::PEER_DRAIN_NS) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true;
+            for (uint32_t tile = first_tile; ok && tile < num_tiles; tile += tile_step) {
+                uint32_t plane, tm2, tn, kb_total;
+                tile_work<MODE>(tile, ec.S, tiles_m2, tiles_n, num_kb, plane, tm2, tn, kb_total);
+                if (!mbar_wait(tempty_bar + acc, acc_phase ^ 1u, abort_flag, err, ERR_WAIT_MMA_EMPTY)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+                for (uint32_t kb = 0; kb < kb_total; ++kb) {
+                    if (!mbar_wait(full_bar + stage, phase, abort_flag, err, ERR_WAIT_MMA_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES), sb = sa + A_BYTES;
+#pragma unroll
+                    for (uint32_t k = 0; k < BK / UK; ++k)
+                        umma_i8_pair(d_tmem, sdesc_sw128(sa + k * UK), sdesc_sw128(sb + k * UK), (kb | k) != 0u);
+                    const uint32_t eb = smem_u32(empty_bar + stage);
+                    umma_commit_pair(eb);
+                    umma_commit_pair(map_to(eb, 1));
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                const uint32_t tb = smem_u32(tfull_bar + acc);
+                umma_commit_pair(tb);
+                umma_commit_pair(map_to(tb, 1));
+                acc ^= 1u;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            // Every MMA this thread issued completes before the columns of either CTA are freed.
+            umma_commit_pair(smem_u32(drain_bar));
+            mbar_wait_drain(drain_bar, 0, 1000000000ull);
+        }
+    } else {
+        const uint32_t quarter = warp & 3u;
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t tile = first_tile; tile < num_tiles; tile += tile_step) {
+            uint32_t s, tm2, tn, kb_total;
+            tile_work<MODE>(tile, ec.S, tiles_m2, tiles_n, num_kb, s, tm2, tn, kb_total);
+            if (!mbar_wait(tfull_bar + acc, acc_phase, abort_flag, err, ERR_WAIT_EPILOGUE)) break;
+            tc_fence_after();
+            const uint64_t row = (uint64_t)tm2 * 2 * BM + rank * BM + quarter * 32u + lane;
+            const uint32_t tbase = tmem_base + ((quarter * 32u) << 16) + acc * ACC_COLS;
+            const uint32_t m = ec.m[s % OZTT_MAXS], y = ec.y[s % OZTT_MAXS], mg = ec.magic[s % OZTT_MAXS],
+                           sh = ec.shift[s % OZTT_MAXS];
+#pragma unroll 1
+            for (uint32_t c = 0; c < BN; c += 32) {
+                uint32_t v[32];
+                tmem_ld32(tbase + c, v);
+                if (row >= mp) continue;  // rows of the last pair tile beyond the planes (zero-filled loads)
+                const uint64_t off = ((uint64_t)s * mp + row) * np + (uint64_t)tn * BN + c;
+                if constexpr (MODE == 0 || MODE == 2) {
+                    uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<int32_t*>(out) + off);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) o[q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                } else {
+                    uint32_t w[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) w[q] = 0;
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const int32_t cv = (int32_t)v[e];
+                        const uint32_t a = cv < 0 ? (uint32_t)(-cv) : (uint32_t)cv;
+                        uint32_t r = a - udiv_small(a, mg, sh) * m;
+                        if (cv < 0 && r) r = m - r;
+                        const uint32_t t = r * y;
+                        const uint32_t kk = t - udiv_small(t, mg, sh) * m;
+                        w[e >> 2] |= kk << (8 * (e & 3));
+                    }
+                    uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out) + off);
+                    o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_remote(map_to(smem_u32(tempty_bar + acc), 0));
+            acc ^= 1u;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+    }
+    __syncthreads();
+    cluster_sync();  // no CTA frees its tensor memory or exits while the pair may still use it
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
 // ---- host side -------------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -410,6 +671,64 @@ static void udiv_magic(uint32_t d, uint32_t& magic, uint32_t& shift) {
 
 }  // namespace gemm
 
+namespace {
+
+// The single-CTA kernel is the default; OZTT_GEMM_CTA_PAIRS=1 selects the CTA-pair kernel. Both give
+// identical results. Measured on B200 at 16384^3 (S = 17, 20 steps): the pair kernel needs about 9 %
+// fewer SM cycles for the residue GEMM, but it draws more power per cycle, and under the 1 kW cap the
+// SM clock settles near 1130 MHz instead of 1500 MHz, so it takes 64 ms instead of 53 ms. In short
+// runs that stay below the cap (Scheme I at 8192^3) it is the faster of the two.
+bool use_pairs() {
+    const char* v = std::getenv("OZTT_GEMM_CTA_PAIRS");
+    return v && v[0] == '1';
+}
+
+// Launches mode MODE of the GEMM over `planes` planes of tiles (a plane = a modulus or a diagonal).
+template <int MODE>
+void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* out, uint64_t mp, uint64_t np, uint64_t kp,
+                 uint32_t planes, const gemm::EpiConst& ec, int* err_word, cudaStream_t st) {
+    using namespace gemm;
+    int dev = 0, sms = 148;
+    OZTT_CUDA(cudaGetDevice(&dev));
+    OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const uint32_t tiles_n = (uint32_t)(np / BN), num_kb = (uint32_t)(kp / BK);
+    if (use_pairs()) {
+        const uint32_t tiles_m2 = (uint32_t)((mp / 128 + 1) / 2);
+        const uint64_t num_tiles = (uint64_t)planes * tiles_m2 * tiles_n;
+        OZTT_CUDA(cudaFuncSetAttribute(residue_gemm_pair_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)pair::SMEM_BYTES));
+        // one resident pair per two SMs, as many pairs as the GPCs can hold at once (persistent)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(sms & ~1), 1, 1);
+        cfg.blockDim = dim3(pair::NUM_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = pair::SMEM_BYTES;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        OZTT_CUDA(cudaOccupancyMaxActiveClusters(&clusters, residue_gemm_pair_kernel<MODE>, &cfg));
+        if (clusters < 1) throw Error(OZTT_ERUNTIME, "residue_gemm: no CTA pair fits on this device");
+        const unsigned grid = 2u * (unsigned)std::min<uint64_t>(num_tiles, (uint64_t)clusters);
+        residue_gemm_pair_kernel<MODE><<<grid, pair::NUM_THREADS, pair::SMEM_BYTES, st>>>(
+            ta, tb, out, tiles_m2, tiles_n, num_kb, mp, np, ec, err_word);
+    } else {
+        const uint32_t tiles_m = (uint32_t)(mp / BM);
+        const uint64_t num_tiles = (uint64_t)planes * tiles_m * tiles_n;
+        OZTT_CUDA(cudaFuncSetAttribute(residue_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)SMEM_BYTES));
+        const unsigned grid = (unsigned)std::min<uint64_t>(num_tiles, (uint64_t)sms);
+        residue_gemm_kernel<MODE><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, out, tiles_m, tiles_n, num_kb, mp, np,
+                                                                        ec, err_word);
+    }
+    OZTT_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
 void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
                          const oztt_ii_plan& p, int mode, void* out, int* err_word, cudaStream_t st) {
     using namespace gemm;
@@ -428,26 +747,13 @@ void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64
         ec.y[s] = (uint32_t)p.yi[s];
         udiv_magic(ec.m[s], ec.magic[s], ec.shift[s]);
     }
-    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p.S, BM);
-    const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p.S, BN);
-    int dev = 0, sms = 148;
-    OZTT_CUDA(cudaGetDevice(&dev));
-    OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const uint32_t tiles_m = (uint32_t)(mp / BM), tiles_n = (uint32_t)(np / BN);
-    const uint64_t num_tiles = (uint64_t)p.S * tiles_m * tiles_n;
-    const unsigned grid = (unsigned)std::min<uint64_t>(num_tiles, (uint64_t)sms);
-    if (mode == 0) {
-        OZTT_CUDA(cudaFuncSetAttribute(residue_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)SMEM_BYTES));
-        residue_gemm_kernel<0><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, out, tiles_m, tiles_n,
-                                                                     (uint32_t)(kp / BK), mp, np, ec, err_word);
-    } else {
-        OZTT_CUDA(cudaFuncSetAttribute(residue_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)SMEM_BYTES));
-        residue_gemm_kernel<1><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, out, tiles_m, tiles_n,
-                                                                     (uint32_t)(kp / BK), mp, np, ec, err_word);
-    }
-    OZTT_CUDA(cudaGetLastError());
+    const bool pairs = use_pairs();
+    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p.S, pairs ? pair::BM : BM);
+    const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p.S, pairs ? pair::BNH : BN);
+    if (mode == 0)
+        launch_gemm<0>(ta, tb, out, mp, np, kp, (uint32_t)p.S, ec, err_word, st);
+    else
+        launch_gemm<1>(ta, tb, out, mp, np, kp, (uint32_t)p.S, ec, err_word, st);
 }
 
 // Scheme I diagonal products P_d = sum_{i=0..d} A_i B_{d-i}^T, d = 0..p-1, int32 [p][mp][np], from
@@ -465,19 +771,10 @@ void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t 
         throw Error(OZTT_EINVAL, "diag_gemm: problem too large");
     EpiConst ec{};
     ec.S = (uint32_t)p;
-    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p, BM);
-    const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p, BN);
-    int dev = 0, sms = 148;
-    OZTT_CUDA(cudaGetDevice(&dev));
-    OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const uint32_t tiles_m = (uint32_t)(mp / BM), tiles_n = (uint32_t)(np / BN);
-    const uint64_t num_tiles = (uint64_t)p * tiles_m * tiles_n;
-    const unsigned grid = (unsigned)std::min<uint64_t>(num_tiles, (uint64_t)sms);
-    OZTT_CUDA(cudaFuncSetAttribute(residue_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)SMEM_BYTES));
-    residue_gemm_kernel<2><<<grid, NUM_THREADS, SMEM_BYTES, st>>>(ta, tb, out, tiles_m, tiles_n, (uint32_t)(kp / BK),
-                                                                 mp, np, ec, err_word);
-    OZTT_CUDA(cudaGetLastError());
+    const bool pairs = use_pairs();
+    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p, pairs ? pair::BM : BM);
+    const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p, pairs ? pair::BNH : BN);
+    launch_gemm<2>(ta, tb, out, mp, np, kp, (uint32_t)p, ec, err_word, st);
 }
 
 // Host model of the epilogue's division, for the CPU tests of the C ABI.
