@@ -18,16 +18,21 @@
 //
 // HBM traffic per output element: S bytes of digits in, 8 bytes out, plus the two deltas.
 #include <algorithm>
+#include <cstdlib>
 
 #include "oztt_common.cuh"
 
 namespace oztt {
+
+constexpr int kLimbBits = 39;  // radix of the FP64 limbs of M/m_s: S * 255 * 2^39 < 2^52 for S <= 24
+constexpr int kMaxLimbs = 5;   // M <= 255^24 < 2^192 < 2^(39*5)
 
 struct ReconConst {
     uint32_t S;
     int32_t two_b, sh2;
     uint32_t M[8];
     uint32_t Q[OZTT_MAXS][8];
+    double Qd[OZTT_MAXS][kMaxLimbs];  // M/m_s in radix-2^39 limbs, as doubles (exact)
     double top_scale;  // 2^(32 (NW-3)) / M: X/M from the top three words of X
 };
 
@@ -143,6 +148,69 @@ __global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ 
     }
 }
 
+// The same with X = sum_s k_s (M/m_s) accumulated on the FP64 pipe: M/m_s is held in NL radix-2^39
+// limbs, each limb sum sum_s k_s q_{s,l} < 24 * 255 * 2^39 < 2^52 is exact in binary64 (every fused
+// multiply-add of two integers below 2^53 with an integer sum below 2^53 is exact), and the limbs are
+// then read back as integers (adding 2^52 puts the integer in the significand bits) and placed at their
+// bit offsets 39 l in the 32-bit column sums of crt_finish. The integer pipe keeps only the final
+// step, so the two pipes share the work.
+template <int NW, int NL>
+__global__ void __launch_bounds__(256) recon_fp64_kernel(const uint8_t* __restrict__ kp, uint64_t mp, uint64_t np,
+                                                         const int32_t* __restrict__ dA,
+                                                         const int32_t* __restrict__ dB, double* __restrict__ c,
+                                                         uint64_t m, uint64_t n, uint64_t ldc, const ReconConst rc) {
+    const uint64_t nq = (n + 3) >> 2, total = m * nq, plane = mp * np;
+    constexpr double two52 = 4503599627370496.0;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t i = t / nq, j0 = (t - i * nq) << 2;
+        const uint8_t* base = kp + i * np + j0;
+        uint32_t kw[OZTT_MAXS];
+#pragma unroll
+        for (int s = 0; s < OZTT_MAXS; ++s)
+            kw[s] = (uint32_t)s < rc.S ? __ldg(reinterpret_cast<const uint32_t*>(base + s * plane)) : 0u;
+        double lim[4][NL];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+#pragma unroll
+            for (int l = 0; l < NL; ++l) lim[e][l] = 0.0;
+#pragma unroll
+        for (int s = 0; s < OZTT_MAXS; ++s) {
+            if ((uint32_t)s >= rc.S) break;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                // k as a double: 2^52 + k has k in its low significand bits; subtracting 2^52 is exact
+                const double kd = __dsub_rn(__hiloint2double(0x43300000, (kw[s] >> (8 * e)) & 0xFFu), two52);
+#pragma unroll
+                for (int l = 0; l < NL; ++l) lim[e][l] = __fma_rn(kd, rc.Qd[s][l], lim[e][l]);
+            }
+        }
+        const int32_t da = __ldg(dA + i);
+        double* crow = c + i * ldc + j0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            uint64_t acc[NW];
+#pragma unroll
+            for (int w = 0; w < NW; ++w) acc[w] = 0;
+#pragma unroll
+            for (int l = 0; l < NL; ++l) {
+                const uint64_t v = (uint64_t)__double_as_longlong(__dadd_rn(lim[e][l], two52)) & 0xFFFFFFFFFFFFFull;
+                const int off = kLimbBits * l, w0 = off >> 5, sh = off & 31;
+                // v * 2^sh spans at most three 32-bit words from w0 (52 + 31 bits)
+                const uint64_t lo = v << sh;
+                const uint64_t hi = sh ? (v >> (64 - sh)) : 0;
+                if (w0 < NW) acc[w0] += lo & 0xFFFFFFFFull;
+                if (w0 + 1 < NW) acc[w0 + 1] += lo >> 32;
+                if (w0 + 2 < NW) acc[w0 + 2] += hi;
+            }
+            if (j0 + e < n) {
+                const int32_t g = rc.sh2 - (da + __ldg(dB + j0 + e));
+                crow[e] = crt_finish<NW>(acc, g, rc);
+            }
+        }
+    }
+}
+
 // ---- host side -------------------------------------------------------------------------------
 namespace {
 struct Big {
@@ -186,6 +254,16 @@ void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA
             if (t != s) q = big_mul(q, (uint32_t)p.moduli[t]);
         for (int w = 0; w < 8; ++w) rc.Q[s][w] = q.w[w];
     }
+    for (int s = 0; s < p.S; ++s)
+        for (int l = 0; l < kMaxLimbs; ++l) {
+            // bits [39 l, 39 l + 39) of Q_s
+            uint64_t v = 0;
+            for (int b = 0; b < kLimbBits; ++b) {
+                const int bit = kLimbBits * l + b;
+                if (bit < 256 && ((rc.Q[s][bit >> 5] >> (bit & 31)) & 1u)) v |= 1ull << b;
+            }
+            rc.Qd[s][l] = (double)v;
+        }
     // X = sum_s k_s (M/m_s) < S*M must fit the words, and the three top words must carry X/M to
     // better than the window margin: 32 (NW-3) <= bits(M) - 40 holds for this choice of NW.
     int sbits = 0;
@@ -204,13 +282,31 @@ void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA
     OZTT_CUDA(cudaGetDevice(&dev));
     OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sms * 16);
-    switch (nw) {
-    case 3: recon_kernel<3><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
-    case 4: recon_kernel<4><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
-    case 5: recon_kernel<5><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
-    case 6: recon_kernel<6><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
-    case 7: recon_kernel<7><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
-    default: recon_kernel<8><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+    // limbs needed for the largest M/m_s (below M)
+    const int nl = std::max(1, (big_bits(M) + kLimbBits - 1) / kLimbBits);
+    const bool fp64 = !(std::getenv("OZTT_RECON_INT") && std::getenv("OZTT_RECON_INT")[0] == '1');
+    if (fp64) {
+#define OZTT_RECON_FP64(NW_, NL_) \
+    recon_fp64_kernel<NW_, NL_><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc)
+        switch (nw * 10 + std::min(nl, kMaxLimbs)) {
+        case 31: case 32: case 33: OZTT_RECON_FP64(3, 3); break;
+        case 41: case 42: case 43: OZTT_RECON_FP64(4, 3); break;
+        case 44: OZTT_RECON_FP64(4, 4); break;
+        case 51: case 52: case 53: case 54: OZTT_RECON_FP64(5, 4); break;
+        case 55: OZTT_RECON_FP64(5, 5); break;
+        case 61: case 62: case 63: case 64: case 65: OZTT_RECON_FP64(6, 5); break;
+        default: OZTT_RECON_FP64(7, 5); break;
+        }
+#undef OZTT_RECON_FP64
+    } else {
+        switch (nw) {
+        case 3: recon_kernel<3><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+        case 4: recon_kernel<4><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+        case 5: recon_kernel<5><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+        case 6: recon_kernel<6><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+        case 7: recon_kernel<7><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+        default: recon_kernel<8><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+        }
     }
     OZTT_CUDA(cudaGetLastError());
 }
