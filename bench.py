@@ -154,6 +154,14 @@ def cpu_threads() -> int:
         return os.cpu_count() or 1
 
 
+def gemm_traffic(m: int, n: int, k: int, S: int) -> float:
+    """DRAM bytes per launch of the residue GEMM: the ncu capture at 4096^3 (S = 16) scaled by the
+    units the launch processes (every residue plane is read from HBM once and every digit plane written
+    once, so the traffic grows with S*(mk + nk + mn))."""
+    captured = 537.35e6 + 246.64e6
+    return captured * (S * (m * k + n * k + m * n)) / (16 * 3 * 4096.0 ** 2)
+
+
 def calibrate_rows(run, threads: int, n: int, target_s: float) -> tuple[int, float]:
     """Grows the row sample (a multiple of the thread count, at most n) until one run takes at least
     half of target_s; returns the rows and the time of the last run. The first run warms the thread
@@ -404,7 +412,10 @@ def main() -> None:
                            "achieved": gemm_tops, "peak": int8_peak, "unit": "TOP/s (int8)",
                            "frac": gemm_tops / int8_peak,
                            "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({peaks['source']})",
-                           "traffic": None,
+                           "traffic": gemm_traffic(m, n, k, S),
+                           "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of residue_gemm_kernel<1> "
+                                             "captured at 4096^3 with S = 16 (537.35 MB + 246.64 MB, profiles/"
+                                             "residue_gemm_4096.md), scaled by S*(mk + nk + mn) to this launch",
                            "algorithmic": f"2*m*n*k*S = {gemm_ops:.4g} int8 ops per launch"},
               "hbm_stages": {
                   "split_GBps": (split_bytes / ((stage_ms[2] + stage_ms[3]) * 1e-3)) / 1e9,
