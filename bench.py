@@ -391,7 +391,10 @@ def main() -> None:
     S = plan.S
     gemm_ops = 2.0 * m * n * k * S  # int8 multiply-adds of all moduli in one launch (x2 ops)
     gemm_tops = gemm_ops / (stage_ms[4] * 1e-3) / 1e12
-    int8_peak = 2.0 * peaks["bf16_tflops"]  # B200 dense int8 = 2 x dense bf16
+    # B200 dense int8 = 2 x dense bf16. The GEMM is timed inside back-to-back steps (a long run under
+    # the power cap), so the sustained figure is its denominator; the burst one is reported beside it.
+    int8_peak = 2.0 * peaks["bf16_tflops_sustained"]
+    int8_burst = 2.0 * peaks["bf16_tflops"]
     # HBM-bound stages against the measured copy bandwidth
     split_bytes = 8.0 * (m * k + k * n) + S * (m * k + k * n)
     recon_bytes = S * m * n + 8.0 * m * n
@@ -410,8 +413,9 @@ def main() -> None:
                            "split_cols": stage_ms[3], "residue_gemm": stage_ms[4], "recon": stage_ms[5]},
               "roofline": {"bound": "tensor", "kernel": "residue_gemm_kernel<1> (tcgen05 kind::i8)",
                            "achieved": gemm_tops, "peak": int8_peak, "unit": "TOP/s (int8)",
-                           "frac": gemm_tops / int8_peak,
-                           "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({peaks['source']})",
+                           "frac": gemm_tops / int8_peak, "frac_of_burst": gemm_tops / int8_burst,
+                           "peak_source": f"2 x bf16_tflops_sustained of MEASURED_PEAKS.json ({peaks['source']}); "
+                                          f"burst 2 x bf16_tflops = {int8_burst:.1f}",
                            "traffic": gemm_traffic(m, n, k, S),
                            "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of residue_gemm_kernel<1> "
                                              "captured at 4096^3 with S = 16 (537.35 MB + 246.64 MB, profiles/"
