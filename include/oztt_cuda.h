@@ -139,6 +139,29 @@ int oztt_i_int8_plan(const double* a, const double* b, uint64_t m, uint64_t n, u
 int oztt_ii_int8_plan_device(int device_id, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
                              uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan* plan,
                              void* stream, char* err, size_t errlen);
+/* The statistics stages of the Scheme II precision policy (estimate_product_norm and oz2_measure_stats,
+ * src/backend/common/norm_estimate.hpp:20-73, src/backend/ozaki2/auto_precision.hpp:24-80), for callers
+ * whose A and B are split into panels over several devices: each device measures its panels, the
+ * caller combines them (all-reduce) and plans once with oztt_ii_int8_plan_from_stats.
+ *   absmax  exact max |x| per row (mode 0) or per column (mode 1) of a row-major rows x cols matrix,
+ *           written as doubles to device memory;
+ *   sumsq   sum of (x*rg)^2 per row (mode 0) or column (mode 1), in index order, one rounding per step;
+ *   sketch  out[l*ostride + r] = (double) sum_j (long double)(x[r][j]*rg) * v[l*vstride + j], l = 0..7,
+ *           j ascending, in 64-bit-significand arithmetic (the reference's long double). */
+int oztt_stats_absmax(const double* x, uint64_t rows, uint64_t cols, int32_t mode, double* out, void* stream,
+                      char* err, size_t errlen);
+int oztt_stats_sumsq(const double* x, uint64_t rows, uint64_t cols, int32_t mode, double rg, double* out,
+                     void* stream, char* err, size_t errlen);
+int oztt_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double rg, const double* v, uint64_t vstride,
+                      double* out, uint64_t ostride, void* stream, char* err, size_t errlen);
+/* The 8 x N Gaussian vectors of the norm estimate (mt19937 seeded 12345, the reference's draw order). */
+void oztt_policy_vectors(uint32_t N, double* out);
+/* Scheme II INT8 plan from the five input statistics of the precision policy (TA, TB: sums of squared
+ * power-of-two row/column scales; nA, nB: squared Frobenius norms; nC: the low-biased estimate of
+ * ||AB||_F^2, all after the power-of-two normalisation) for an m x k by k x n problem. */
+int oztt_ii_int8_plan_from_stats(uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction,
+                                 int32_t fixed_bits, double TA, double TB, double nA, double nB, double nC,
+                                 oztt_ii_plan* plan, char* err, size_t errlen);
 /* The Scheme I INT8 pipeline on host buffers (ozaki1_int8::run, src/ozaki1.cpp:192-282). */
 int oztt_i_int8_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
                     const oztt_i_plan* plan, char* err, size_t errlen);

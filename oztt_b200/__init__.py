@@ -148,6 +148,13 @@ _SIGNATURES = {
     "oztt_ii_padded_dims": [_U64, _U64, _U64, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
     "oztt_ii_int8_plan_device": [ctypes.c_int, _P, _P, _U64, _U64, _U64, ctypes.c_uint32, _I32, _I32,
                                  ctypes.POINTER(IIPlan), _P, _ERR, _SZ],
+    "oztt_stats_absmax": [_P, _U64, _U64, _I32, _P, _P, _ERR, _SZ],
+    "oztt_stats_sumsq": [_P, _U64, _U64, _I32, ctypes.c_double, _P, _P, _ERR, _SZ],
+    "oztt_stats_sketch": [_P, _U64, _U64, ctypes.c_double, _P, _U64, _P, _U64, _P, _ERR, _SZ],
+    "oztt_policy_vectors": [ctypes.c_uint32, _P],
+    "oztt_ii_int8_plan_from_stats": [_U64, _U64, _U64, ctypes.c_uint32, _I32, _I32, ctypes.c_double, ctypes.c_double,
+                                     ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.POINTER(IIPlan), _ERR,
+                                     _SZ],
     "oztt_i_int8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _P, _P, _ERR, _SZ],
@@ -159,7 +166,7 @@ _SIGNATURES = {
     "oztt_test_ext80_dot": [_P, _P, _U64, ctypes.c_double],
 }
 
-_RESTYPES = {"oztt_test_udiv_small": ctypes.c_uint32, "oztt_test_ext80_dot": ctypes.c_double, "oztt_ii_padded_dims": None, "oztt_eval_inputs": None,
+_RESTYPES = {"oztt_policy_vectors": None, "oztt_test_udiv_small": ctypes.c_uint32, "oztt_test_ext80_dot": ctypes.c_double, "oztt_ii_padded_dims": None, "oztt_eval_inputs": None,
              "oztt_eval_output_hash": ctypes.c_uint64}
 
 # Symbols declared in include/oztt_cuda.h (the tests check that the library exports each of them).
@@ -284,6 +291,26 @@ def ii_int8_plan_device(a_ptr: int, b_ptr: int, m: int, n: int, k: int, max_modu
     err = _errbuf()
     rc = _lib().oztt_ii_int8_plan_device(device_id, a_ptr, b_ptr, m, n, k, max_moduli, reconstruction, fixed_bits,
                                          ctypes.byref(plan), stream, err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return plan
+
+
+def policy_vectors(N: int) -> np.ndarray:
+    """The 8 x N Gaussian vectors of the precision policy's norm estimate (oztt_policy_vectors)."""
+    out = np.empty((8, N), dtype=np.float64)
+    _lib().oztt_policy_vectors(N, out.ctypes.data)
+    return out
+
+
+def ii_int8_plan_from_stats(m: int, n: int, k: int, TA: float, TB: float, nA: float, nB: float, nC: float,
+                            max_moduli: int = 0, reconstruction: int = 0, fixed_bits: int = 0) -> IIPlan:
+    """Scheme II INT8 plan from the precision policy's five input statistics
+    (oztt_ii_int8_plan_from_stats)."""
+    plan = IIPlan()
+    err = _errbuf()
+    rc = _lib().oztt_ii_int8_plan_from_stats(m, n, k, max_moduli, reconstruction, fixed_bits, TA, TB, nA, nB, nC,
+                                             ctypes.byref(plan), err, len(err))
     if rc != OK:
         _raise(rc, err.value)
     return plan

@@ -25,9 +25,10 @@
 #include "runtime.cuh"
 
 namespace oztt {
-namespace {
 
 constexpr int kVectors = 8;
+
+namespace {
 
 // One warp per row: the largest |a| as the 63-bit pattern (nonnegative doubles order like integers).
 __global__ void __launch_bounds__(256) row_absmax_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
@@ -212,3 +213,92 @@ PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, ui
 }
 
 }  // namespace oztt
+
+// ---- C ABI: the statistics stages, for callers that hold panels of A and B on several devices ------
+using oztt::Error;
+using oztt::guarded;
+
+extern "C" {
+
+int oztt_stats_absmax(const double* x, uint64_t rows, uint64_t cols, int32_t mode, double* out, void* stream,
+                      char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!x || !out || (mode != 0 && mode != 1)) throw Error(OZTT_EINVAL, "stats_absmax: bad arguments");
+        if (!rows || !cols) return;
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        int dev = 0, sms = 148;
+        OZTT_CUDA(cudaGetDevice(&dev));
+        OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        auto* o = reinterpret_cast<unsigned long long*>(out);  // nonnegative doubles order like their patterns
+        if (mode == 0) {
+            oztt::row_absmax_kernel<<<(unsigned)std::min<uint64_t>((rows + 7) / 8, (uint64_t)sms * 32), 256, 0, st>>>(
+                x, rows, cols, o);
+        } else {
+            OZTT_CUDA(cudaMemsetAsync(out, 0, cols * 8, st));
+            const uint64_t col_blocks = (cols + 255) / 256;
+            const uint64_t want = std::max<uint64_t>(1, (uint64_t)sms * 8 / std::max<uint64_t>(col_blocks, 1));
+            const uint64_t chunks = std::min<uint64_t>(std::min<uint64_t>(want, rows), 65535);
+            const uint64_t rpc = (rows + chunks - 1) / chunks;
+            oztt::col_absmax_kernel<<<dim3((unsigned)col_blocks, (unsigned)((rows + rpc - 1) / rpc)), 256, 0, st>>>(
+                x, rows, cols, rpc, o);
+        }
+        OZTT_CUDA(cudaGetLastError());
+    });
+}
+
+int oztt_stats_sumsq(const double* x, uint64_t rows, uint64_t cols, int32_t mode, double rg, double* out,
+                     void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!x || !out || (mode != 0 && mode != 1)) throw Error(OZTT_EINVAL, "stats_sumsq: bad arguments");
+        if (!rows || !cols) return;
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        if (mode == 0)
+            oztt::row_sumsq_kernel<<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(x, rows, cols, rg, out);
+        else
+            oztt::col_sumsq_kernel<<<(unsigned)((cols + 127) / 128), 128, 0, st>>>(x, rows, cols, rg, out);
+        OZTT_CUDA(cudaGetLastError());
+    });
+}
+
+int oztt_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double rg, const double* v, uint64_t vstride,
+                      double* out, uint64_t ostride, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!x || !v || !out || vstride < cols || ostride < rows) throw Error(OZTT_EINVAL, "stats_sketch: bad arguments");
+        if (!rows) return;
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        oztt::sketch_kernel<<<(unsigned)((rows * oztt::kVectors + 255) / 256), 256, 0, st>>>(x, rows, cols, rg, v,
+                                                                                             vstride, out, ostride);
+        OZTT_CUDA(cudaGetLastError());
+    });
+}
+
+int oztt_ii_int8_plan_from_stats(uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction,
+                                 int32_t fixed_bits, double TA, double TB, double nA, double nB, double nC,
+                                 oztt_ii_plan* plan, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!plan) throw Error(OZTT_EINVAL, "null argument");
+        oztt::PolicyStats ps;
+        ps.TA = TA;
+        ps.TB = TB;
+        ps.nA = nA;
+        ps.nB = nB;
+        ps.nC = nC;
+        ps.measured = true;
+        std::string msg;
+        const int rc = oztt::plan_ii_int8_with([&](uint32_t, uint32_t) { return ps; }, m, n, k, max_moduli,
+                                               reconstruction, fixed_bits, *plan, msg);
+        if (rc != OZTT_OK) throw Error(rc, msg);
+    });
+}
+
+}  // extern "C"
+
+// The 8 Gaussian vectors of the precision policy's norm estimate: 8 x N values of
+// std::normal_distribution<double> over std::mt19937(12345), vector after vector, as the reference draws
+// them (estimate_product_norm, src/backend/common/norm_estimate.hpp:48-73).
+extern "C" void oztt_policy_vectors(uint32_t N, double* out) {
+    std::mt19937 rng(12345);
+    std::normal_distribution<double> normal(0.0, 1.0);
+    for (int l = 0; l < oztt::kVectors; ++l)
+        for (uint32_t j = 0; j < N; ++j) out[(size_t)l * N + j] = normal(rng);
+}

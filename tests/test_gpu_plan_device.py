@@ -42,3 +42,13 @@ def test_context_uses_the_same_plan(oztt, oracle, cuda):
     assert (info.moduli, info.integer_bits, info.reconstruction_passes) == (plan.S, plan.b, 2 if plan.two_pass else 1)
     ref = oztt.ii_int8_run(a, b, m, n, k, plan)
     assert np.array_equal(c.view(np.uint64), ref.view(np.uint64))
+
+
+def test_tiled_plan_on_one_rank_equals_host_plan(oztt, oracle, cuda):
+    from oztt_b200.distributed import Grid, plan_ii_int8_tiled
+
+    m, n, k = 200, 300, 160
+    a, b = oracle.gen_inputs(m, n, k, 1.0, 13)
+    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    plan = plan_ii_int8_tiled(A.view(m, k), B.view(k, n), m, n, k, Grid(1, 1, 0, 0), stream=_stream())
+    assert bytes(plan) == bytes(oztt.ii_int8_plan(a, b, m, n, k))
