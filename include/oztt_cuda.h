@@ -89,6 +89,34 @@ typedef struct oztt_ii_plan {
     double recon1_log2;            /* estimated log2 error of one reconstruction pass */
 } oztt_ii_plan;
 
+/* ---- Scheme II with FP8 (e4m3) digits (route OZ2_ROUTE_FP8 of src/backend/ozaki2/split.hpp) ----
+ * Residues are split into two or three small digits per modulus; the products of digit planes are
+ * grouped by weight (concatenated along K) into GEMM outputs, which the composition combines into the
+ * residue of C modulo m. Splitting methods (OZ2_SPLIT_* of split.hpp): */
+#define OZTT_SPLIT_SQ 0   /* square m = q^2, digits by rounding to nearest, 3 products */
+#define OZTT_SPLIT_KAR 1  /* radix-16 Karatsuba (l, h, s = h + l), 3 products */
+#define OZTT_SPLIT_WIDE 2 /* two digits of radix ~sqrt(m), 4 products */
+#define OZTT_SPLIT_SQS 4  /* square of odd q with the sparse e4m3 digits (|x| <= 16, or even and <= 32) */
+#define OZTT_MAXOUT 96    /* GEMM outputs: at most 4 per modulus */
+
+typedef struct oztt_fp8_plan {
+    oztt_ii_plan base; /* moduli, width, digits of A', passes, CRT constants, statistics */
+    int32_t nplane;    /* digit planes per operand */
+    int32_t nprod;     /* digit products */
+    int32_t nout;      /* GEMM outputs after concatenation */
+    int32_t fold_first;
+    int32_t q[OZTT_MAXS], mode[OZTT_MAXS], poff[OZTT_MAXS], npl[OZTT_MAXS];
+    int32_t oout[OZTT_MAXS + 1]; /* outputs of modulus i: oout[i] .. oout[i+1]-1 */
+    /* output o = sum_{t < out_g[o]} A digit plane (out_a[o] + t) x B digit plane (out_b[o] - t), with the
+     * composition coefficient coeff[o] (mod the modulus out_mod[o]) */
+    int32_t out_a[OZTT_MAXOUT], out_b[OZTT_MAXOUT], out_g[OZTT_MAXOUT], out_mod[OZTT_MAXOUT], coeff[OZTT_MAXOUT];
+} oztt_fp8_plan;
+
+/* Scheme II FP8 plan (choose_moduli_and_width with the FP8 route, src/backend/ozaki2/plan.hpp:258-306 and
+ * moduli.hpp:710-770); arguments as oztt_ii_int8_plan (default limit 14 moduli with a fixed width). */
+int oztt_ii_fp8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
+                  int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan* plan, char* err, size_t errlen);
+
 /* Plan of one Scheme I INT8 call (src/ozaki1.cpp:192-210): the number of slices p (radix 254, digits
  * +-127, target 2^-1), the last diagonal L = p-1 kept. */
 typedef struct oztt_i_plan {

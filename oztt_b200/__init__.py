@@ -115,6 +115,19 @@ class IIPlan(ctypes.Structure):
         return [int(self.moduli[i]) for i in range(self.S)]
 
 
+MAXOUT = 96
+
+
+class FP8Plan(ctypes.Structure):
+    """oztt_fp8_plan: the Scheme II FP8 digit plan (moduli, splitting, GEMM outputs, coefficients)."""
+    _fields_ = [("base", IIPlan), ("nplane", ctypes.c_int32), ("nprod", ctypes.c_int32), ("nout", ctypes.c_int32),
+                ("fold_first", ctypes.c_int32), ("q", ctypes.c_int32 * MAXS), ("mode", ctypes.c_int32 * MAXS),
+                ("poff", ctypes.c_int32 * MAXS), ("npl", ctypes.c_int32 * MAXS), ("oout", ctypes.c_int32 * (MAXS + 1)),
+                ("out_a", ctypes.c_int32 * MAXOUT), ("out_b", ctypes.c_int32 * MAXOUT),
+                ("out_g", ctypes.c_int32 * MAXOUT), ("out_mod", ctypes.c_int32 * MAXOUT),
+                ("coeff", ctypes.c_int32 * MAXOUT)]
+
+
 class IPlan(ctypes.Structure):
     """oztt_i_plan: the slice count of one Scheme I INT8 call."""
     _fields_ = [("M", ctypes.c_uint32), ("N", ctypes.c_uint32), ("K", ctypes.c_uint32), ("p", ctypes.c_int32),
@@ -155,6 +168,7 @@ _SIGNATURES = {
     "oztt_ii_int8_plan_from_stats": [_U64, _U64, _U64, ctypes.c_uint32, _I32, _I32, ctypes.c_double, ctypes.c_double,
                                      ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.POINTER(IIPlan), _ERR,
                                      _SZ],
+    "oztt_ii_fp8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, _I32, _I32, ctypes.POINTER(FP8Plan), _ERR, _SZ],
     "oztt_i_int8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _P, _P, _ERR, _SZ],
@@ -291,6 +305,21 @@ def ii_int8_plan_device(a_ptr: int, b_ptr: int, m: int, n: int, k: int, max_modu
     err = _errbuf()
     rc = _lib().oztt_ii_int8_plan_device(device_id, a_ptr, b_ptr, m, n, k, max_moduli, reconstruction, fixed_bits,
                                          ctypes.byref(plan), stream, err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return plan
+
+
+def fp8_plan(a, b, m: int, n: int, k: int, max_moduli: int = 0, reconstruction: int = 0,
+             fixed_bits: int = 0) -> FP8Plan:
+    """Scheme II FP8 digit plan for row-major host matrices (oztt_ii_fp8_plan); a and b may be None with a
+    fixed width and a fixed number of passes."""
+    av = _as_f64(a, "a") if a is not None else None
+    bv = _as_f64(b, "b") if b is not None else None
+    plan = FP8Plan()
+    err = _errbuf()
+    rc = _lib().oztt_ii_fp8_plan(av.ctypes.data if av is not None else None, bv.ctypes.data if bv is not None else None,
+                                 m, n, k, max_moduli, reconstruction, fixed_bits, ctypes.byref(plan), err, len(err))
     if rc != OK:
         _raise(rc, err.value)
     return plan

@@ -39,10 +39,11 @@ CXX_FLAGS = ["-std=gnu++20", "-O2", "-fPIC", "-fno-fast-math", "-ffp-contract=of
 # The host planners run the reference's selection arithmetic over every input element: built for the
 # x86-64-v3 level (AVX2, FMA, SSE4.1 rounding) so that fma and nearbyint are single instructions.
 # Contraction stays off, so every operation rounds as written and the decisions do not change.
-CXX_FLAGS_BY_SOURCE = {"planner.cpp": ["-O3", "-march=x86-64-v3"], "planner1.cpp": ["-O3", "-march=x86-64-v3"]}
+CXX_FLAGS_BY_SOURCE = {"planner.cpp": ["-O3", "-march=x86-64-v3"], "planner1.cpp": ["-O3", "-march=x86-64-v3"],
+                       "planner_digit.cpp": ["-O3", "-march=x86-64-v3"]}
 
 CU_SOURCES = ["split.cu", "gemm_i8.cu", "recon.cu", "ii_int8.cu", "noalloc.cu", "scheme1.cu", "stats.cu"]
-CPP_SOURCES = ["planner.cpp", "planner1.cpp", "context.cpp", "evaluation.cpp"]
+CPP_SOURCES = ["planner.cpp", "planner1.cpp", "planner_digit.cpp", "context.cpp", "evaluation.cpp"]
 
 
 def _run(cmd: list[str]) -> None:

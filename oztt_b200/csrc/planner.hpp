@@ -69,6 +69,12 @@ int plan_ii_int8_with(const std::function<PolicyStats(uint32_t, uint32_t)>& stat
                       uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan& p,
                       std::string& err);
 
+// Scheme II FP8 digits (planner_digit.cpp).
+int plan_fp8_with(const std::function<PolicyStats(uint32_t, uint32_t)>& stats, uint64_t m, uint64_t n, uint64_t k,
+                  uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan& p, std::string& err);
+int plan_fp8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
+             int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan& p, std::string& err);
+
 // Scheme I INT8 (planner1.cpp): the slice count oz_fp64_p selects for row-major a (m x k), b (k x n)
 // with padded planning dimensions M, N, K; and the whole plan (slices > 0 fixes p).
 int select_slices_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,

@@ -16,7 +16,7 @@ for p in (str(ROOT), str(ROOT / "tests")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
-from oracle_lib import Oracle, RefEmu, RefPlan, RefPlan1  # noqa: E402
+from oracle_lib import Oracle, RefEmu, RefPlan, RefPlan1, RefPlanF8  # noqa: E402
 
 
 def pytest_configure(config):
@@ -40,6 +40,14 @@ def ref_plan():
 def ref_plan1():
     try:
         return RefPlan1()
+    except FileNotFoundError:
+        pytest.skip("oracle/_ref was not built on this machine (needs the reference tree)")
+
+
+@pytest.fixture(scope="session")
+def ref_plan_f8():
+    try:
+        return RefPlanF8()
     except FileNotFoundError:
         pytest.skip("oracle/_ref was not built on this machine (needs the reference tree)")
 

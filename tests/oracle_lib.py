@@ -18,6 +18,7 @@ ORACLE_SO = ROOT / "oracle" / "liboz2oracle.so"
 REF_PLAN_SO = ROOT / "oracle" / "_ref" / "libozref_plan.so"
 REF_EMU_SO = ROOT / "oracle" / "_ref" / "libozref_emu.so"
 REF_PLAN1_SO = ROOT / "oracle" / "_ref" / "libozref_plan1.so"
+REF_PLAN_F8_SO = ROOT / "oracle" / "_ref" / "libozref_plan_f8.so"
 
 MAXS, MAXRP = 24, 5
 P = ctypes.c_void_p
@@ -232,6 +233,29 @@ class RefEmu:
         s = self.lib.ozr_emulate_int8(ptr(ap), ptr(bp), ptr(c), M, N, K, b_fixed, num_moduli, 1 if two_pass else 0,
                                       ptr(mods))
         return s, c, [int(x) for x in mods[:max(s, 0)]]
+
+
+class RefPlanF8:
+    """The reference's Scheme II planner headers compiled for FP8 (oracle/ref_plan_f8.cpp)."""
+
+    def __init__(self, path: Path = REF_PLAN_F8_SO):
+        if not path.exists():
+            raise FileNotFoundError(str(path))
+        self.lib = ctypes.CDLL(str(path))
+        self.lib.ozr_f8_choose.argtypes = [ctypes.c_uint32, ctypes.c_int, ctypes.c_int, P, P]
+        self.lib.ozr_f8_plan.argtypes = [P, P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                         ctypes.c_int, ctypes.c_int, P]
+
+    def choose(self, K: int, num_moduli: int, b_cap: int, plan_type):
+        out = plan_type()
+        acc = ctypes.c_int()
+        ok = self.lib.ozr_f8_choose(K, num_moduli, b_cap, ctypes.byref(out), ctypes.byref(acc))
+        return ok, acc.value, out
+
+    def plan(self, ap, bp, M, N, K, plan_type, max_moduli=0, passes=0, fixed_bits=0):
+        out = plan_type()
+        rc = self.lib.ozr_f8_plan(ptr(ap), ptr(bp), M, N, K, max_moduli, passes, fixed_bits, ctypes.byref(out))
+        return rc, out
 
 
 class RefPlan1:
