@@ -776,10 +776,11 @@ int ozo_gemm_i32(const int8_t* ap, const int8_t* bp, uint64_t S, uint64_t M, uin
     return bad;
 }
 
-int ozo_recon_faithful(const int32_t* cs, uint64_t M, uint64_t N, const int32_t* dA, const int32_t* dB,
-                       const ozo_plan* plan, double* c, uint64_t ldc) {
+namespace {
+// The reference's reconstruction of one element from its residues r_s (recon_crt.cpp:296-338 with
+// recon_crt_proc.h and the assembly of recon_elem.h / f64_tf.h:296-400).
+double recon_element_faithful(const float* r, const ozo_plan* plan, int32_t g) {
     const int S = plan->S;
-    const int32_t sh2 = 2 * plan->shift;
     struct Pass {
         const float (*rp)[OZO_MAXRP];
         int nrp, nsmall;
@@ -794,6 +795,100 @@ int ozo_recon_faithful(const int32_t* cs, uint64_t M, uint64_t N, const int32_t*
         passes[0] = {plan->rp0, 5, plan->nsmall0};
         npass = 1;
     }
+    // 128-bit fixed point frac * 2^124 (recon_elem.h:28-60, f64_tf.h:296-400).
+    unsigned __int128 fix = 0;
+    for (int pi = 0; pi < npass; ++pi) {
+        const Pass& ps = passes[pi];
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+        for (int s = 0; s < S; ++s) {
+            const float m = (float)plan->m[s], ri = plan->rinv[s];
+            // term_k and accumulate (recon_crt_proc.h:27-52).
+            const float kk = mod_round(fmul(r[s], (float)plan->yi[s]), m, ri);
+            for (int t = 0; t < ps.nrp; ++t) {
+                const float v = fmul(kk, ps.rp[s][t]);
+                if (t >= ps.nrp - ps.nsmall)
+                    tf_add_small(a1, a2, v);
+                else
+                    tf_add(a0, a1, a2, v);
+            }
+            a0 = fsub(a0, frnd(a0));  // drop_integer (recon_crt_proc.h:56-59)
+        }
+        for (float limb : {a0, a1, a2}) {
+            const uint32_t u = f_to_bits(limb);
+            const int32_t ee = (int32_t)((u >> 23) & 0xFFu);
+            if (ee == 0) continue;
+            const int32_t mag = (int32_t)(0x800000u | (u & 0x7FFFFFu));
+            const int32_t sh = ee - 26;
+            if (sh <= -24 || sh >= 128) continue;  // below the fixed-point LSB / above bit 127
+            const unsigned __int128 v =
+                sh < 0 ? (unsigned __int128)((uint64_t)mag >> (uint32_t)(-sh)) : ((unsigned __int128)mag << sh);
+            if (v == 0) continue;
+            if (u & 0x80000000u)
+                fix -= v;
+            else
+                fix += v;
+        }
+    }
+    // Fold to [-1/2, 1/2] and assemble (a128_frac_to_f64, f64_tf.h:345-400).
+    const uint32_t top = (uint32_t)(fix >> 96);
+    if (top + 0x08000000u >= 0x10000000u || top == 0xF8000000u) {
+        const unsigned __int128 one = (unsigned __int128)1 << 124;
+        if ((int32_t)top >= 0x08000000)
+            fix -= one;
+        else if ((int32_t)top < -0x08000000 || (fix & (((unsigned __int128)1 << 96) - 1)) == 0)
+            fix += one;
+    }
+    const bool neg = (fix >> 127) != 0;
+    unsigned __int128 mag = neg ? (~fix + 1) : fix;
+    double out = 0.0;
+    if (mag != 0) {
+        int lz = 0;
+        {
+            const uint64_t hi = (uint64_t)(mag >> 64), lo = (uint64_t)mag;
+            lz = hi ? __builtin_clzll(hi) : 64 + __builtin_clzll(lo);
+        }
+        const uint64_t A = lz <= 64 ? (uint64_t)(mag >> (64 - lz)) : (uint64_t)(mag << (lz - 64));
+        const int32_t total = plan->qw + g - lz - 60;
+        // pack_f64 (f64_tf.h:189-213): top 64 bits of A*W, guard-bit rounding (ties away).
+        const uint64_t W = ((uint64_t)plan->W_hi << 32) | plan->W_lo;
+        const uint64_t hi = (uint64_t)(((unsigned __int128)A * W) >> 64);
+        const int32_t nb = (hi >> 63) ? 63 : 62;
+        int32_t exp2 = nb + 64 + total;
+        uint64_t mant;
+        bool up;
+        if (nb == 63) {
+            mant = hi >> 11;
+            up = (hi & 0x400ull) != 0;
+        } else {
+            mant = hi >> 10;
+            up = (hi & 0x200ull) != 0;
+        }
+        if (up) {
+            mant += 1;
+            if (mant >> 53) {
+                mant >>= 1;
+                exp2 += 1;
+            }
+        }
+        const uint64_t sgn = neg ? 0x8000000000000000ull : 0ull;
+        const int32_t eb = exp2 + 1023;
+        uint64_t ub;
+        if (eb <= 0)
+            ub = sgn;
+        else if (eb >= 2047)
+            ub = sgn | 0x7FF0000000000000ull;
+        else
+            ub = sgn | ((uint64_t)eb << 52) | (mant & 0x000FFFFFFFFFFFFFull);
+        std::memcpy(&out, &ub, 8);
+    }
+    return out;
+}
+}  // namespace
+
+int ozo_recon_faithful(const int32_t* cs, uint64_t M, uint64_t N, const int32_t* dA, const int32_t* dB,
+                       const ozo_plan* plan, double* c, uint64_t ldc) {
+    const int S = plan->S;
+    const int32_t sh2 = 2 * plan->shift;
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < (int64_t)M; ++i)
         for (uint64_t j = 0; j < N; ++j) {
@@ -811,94 +906,21 @@ int ozo_recon_faithful(const int32_t* cs, uint64_t M, uint64_t N, const int32_t*
                 const float kl = mod_round((float)(w & 0x0000FFFFu), m, ri);
                 r[s] = mod_round(fmul(fadd(kl, kh), sgn), m, ri);
             }
-            // 128-bit fixed point frac * 2^124 (recon_elem.h:28-60, f64_tf.h:296-400).
-            unsigned __int128 fix = 0;
-            for (int pi = 0; pi < npass; ++pi) {
-                const Pass& ps = passes[pi];
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f;
-                for (int s = 0; s < S; ++s) {
-                    const float m = (float)plan->m[s], ri = plan->rinv[s];
-                    // term_k and accumulate (recon_crt_proc.h:27-52).
-                    const float kk = mod_round(fmul(r[s], (float)plan->yi[s]), m, ri);
-                    for (int t = 0; t < ps.nrp; ++t) {
-                        const float v = fmul(kk, ps.rp[s][t]);
-                        if (t >= ps.nrp - ps.nsmall)
-                            tf_add_small(a1, a2, v);
-                        else
-                            tf_add(a0, a1, a2, v);
-                    }
-                    a0 = fsub(a0, frnd(a0));  // drop_integer (recon_crt_proc.h:56-59)
-                }
-                for (float limb : {a0, a1, a2}) {
-                    const uint32_t u = f_to_bits(limb);
-                    const int32_t ee = (int32_t)((u >> 23) & 0xFFu);
-                    if (ee == 0) continue;
-                    const int32_t mag = (int32_t)(0x800000u | (u & 0x7FFFFFu));
-                    const int32_t sh = ee - 26;
-                    if (sh <= -24 || sh >= 128) continue;  // below the fixed-point LSB / above bit 127
-                    const unsigned __int128 v =
-                        sh < 0 ? (unsigned __int128)((uint64_t)mag >> (uint32_t)(-sh)) : ((unsigned __int128)mag << sh);
-                    if (v == 0) continue;
-                    if (u & 0x80000000u)
-                        fix -= v;
-                    else
-                        fix += v;
-                }
-            }
-            // Fold to [-1/2, 1/2] and assemble (a128_frac_to_f64, f64_tf.h:345-400).
-            const uint32_t top = (uint32_t)(fix >> 96);
-            if (top + 0x08000000u >= 0x10000000u || top == 0xF8000000u) {
-                const unsigned __int128 one = (unsigned __int128)1 << 124;
-                if ((int32_t)top >= 0x08000000)
-                    fix -= one;
-                else if ((int32_t)top < -0x08000000 || (fix & (((unsigned __int128)1 << 96) - 1)) == 0)
-                    fix += one;
-            }
-            const bool neg = (fix >> 127) != 0;
-            unsigned __int128 mag = neg ? (~fix + 1) : fix;
-            double out = 0.0;
-            if (mag != 0) {
-                int lz = 0;
-                {
-                    const uint64_t hi = (uint64_t)(mag >> 64), lo = (uint64_t)mag;
-                    lz = hi ? __builtin_clzll(hi) : 64 + __builtin_clzll(lo);
-                }
-                const uint64_t A = lz <= 64 ? (uint64_t)(mag >> (64 - lz)) : (uint64_t)(mag << (lz - 64));
-                const int32_t g = sh2 - (dA[i] + dB[j]);
-                const int32_t total = plan->qw + g - lz - 60;
-                // pack_f64 (f64_tf.h:189-213): top 64 bits of A*W, guard-bit rounding (ties away).
-                const uint64_t W = ((uint64_t)plan->W_hi << 32) | plan->W_lo;
-                const uint64_t hi = (uint64_t)(((unsigned __int128)A * W) >> 64);
-                const int32_t nb = (hi >> 63) ? 63 : 62;
-                int32_t exp2 = nb + 64 + total;
-                uint64_t mant;
-                bool up;
-                if (nb == 63) {
-                    mant = hi >> 11;
-                    up = (hi & 0x400ull) != 0;
-                } else {
-                    mant = hi >> 10;
-                    up = (hi & 0x200ull) != 0;
-                }
-                if (up) {
-                    mant += 1;
-                    if (mant >> 53) {
-                        mant >>= 1;
-                        exp2 += 1;
-                    }
-                }
-                const uint64_t sgn = neg ? 0x8000000000000000ull : 0ull;
-                const int32_t eb = exp2 + 1023;
-                uint64_t ub;
-                if (eb <= 0)
-                    ub = sgn;
-                else if (eb >= 2047)
-                    ub = sgn | 0x7FF0000000000000ull;
-                else
-                    ub = sgn | ((uint64_t)eb << 52) | (mant & 0x000FFFFFFFFFFFFFull);
-                std::memcpy(&out, &ub, 8);
-            }
-            c[(uint64_t)i * ldc + j] = out;
+            c[(uint64_t)i * ldc + j] = recon_element_faithful(r, plan, sh2 - (dA[i] + dB[j]));
+        }
+    return 0;
+}
+
+int ozo_recon_faithful_residue(const float* rs, uint64_t M, uint64_t N, const int32_t* dA, const int32_t* dB,
+                               const ozo_plan* plan, double* c, uint64_t ldc) {
+    const int S = plan->S;
+    const int32_t sh2 = 2 * plan->shift;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)M; ++i)
+        for (uint64_t j = 0; j < N; ++j) {
+            float r[OZO_MAXS];
+            for (int s = 0; s < S; ++s) r[s] = rs[((uint64_t)s * M + (uint64_t)i) * N + j];
+            c[(uint64_t)i * ldc + j] = recon_element_faithful(r, plan, sh2 - (dA[i] + dB[j]));
         }
     return 0;
 }
@@ -1098,6 +1120,205 @@ double ozo_time_dot2_rows(const double* a, const double* b, uint64_t rows, uint6
 #else
     return -1.0;
 #endif
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Scheme II with FP8 (e4m3) digits.
+// ---------------------------------------------------------------------------------------------
+namespace {
+// Integers e4m3 holds exactly (the digit sets of modslice_digit.cpp: |x| <= 16, or even with |x| <= 32).
+bool e4m3_integer(float v) {
+    const float a = std::fabs(v);
+    if (a != std::floor(a)) return false;
+    if (a <= 16.0f) return true;
+    return a <= 32.0f && std::fmod(a, 2.0f) == 0.0f;
+}
+// Parity of an integer-valued float through the units bit of |x| + 2^23 (sparse_fix.h:55-70).
+bool odd_integer(float a) { return (f_to_bits(a + 8388608.0f) & 1u) != 0; }
+
+// Digits of one residue r of a modulus with splitting mode `mode` (modslice_digit.cpp:193-226,
+// sparse_fix.h:52-72); returns the number of digits (l, h[, s]).
+int split_residue(float r, int mode, float q, float qinv, float* dg) {
+    if (mode == OZTT_SPLIT_KAR) {
+        // h = round((r + sign(r) (q/2 - 1/2)) / q), the sign from Ltz: +1 for r >= 0
+        const float ltz = r < 0.0f ? 1.0f : 0.0f;
+        const float sgn = fadd(fmul(ltz, -2.0f), 1.0f);
+        const float t = fmul(sgn, q * 0.5f - 0.5f);
+        const float h = frnd(fmul(fadd(r, t), qinv));
+        const float l = fsub(r, fmul(h, q));
+        dg[0] = l;
+        dg[1] = h;
+        dg[2] = fadd(h, l);
+        return 3;
+    }
+    float h = frnd(fmul(r, qinv));
+    float l = fsub(r, fmul(h, q));
+    if (mode == OZTT_SPLIT_SQS) {
+        const float al = std::fabs(l);
+        if (al > 16.5f && odd_integer(al)) {
+            if (l < 0.0f) {
+                l = l + q;
+                h = h - 1.0f;
+            } else {
+                l = l - q;
+                h = h + 1.0f;
+            }
+        }
+        const float ah = std::fabs(h);
+        if (ah > 16.5f && odd_integer(ah)) h = h < 0.0f ? h + q : h - q;
+    }
+    dg[0] = l;
+    dg[1] = h;
+    return 2;
+}
+}  // namespace
+
+extern "C" {
+
+int ozo_crt_plan(const int32_t* m, int S, int b, int two_pass, ozo_plan* out) {
+    if (S < 1 || S > OZO_MAXS) return 1;
+    Moduli mo;
+    mo.ok = true;
+    mo.b = b;
+    mo.m.assign(m, m + S);
+    mo.logM = 0;
+    for (int i = 0; i < S; ++i) mo.logM += std::log2((double)m[i]);
+    mo.m_cap = *std::max_element(m, m + S);
+    mo.ncand = S;
+    *out = ozo_plan{};
+    fill_plan(mo, *out);
+    out->two_pass = two_pass;
+    out->S_req = S;
+    return 0;
+}
+
+int ozo_fp8_split(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, const int32_t* delta,
+                  const ozo_plan* crt, const oztt_fp8_plan* fp, int8_t* planes) {
+    const int S = crt->S, nd = crt->nd;
+    const uint64_t plane = rows * cols;
+    float qinv[OZO_MAXS];
+    for (int s = 0; s < S; ++s) qinv[s] = 1.0f / (float)fp->q[s];  // sl_qinv, stages.hpp:223
+    int bad = 0;
+#pragma omp parallel for schedule(static) reduction(| : bad)
+    for (int64_t r = 0; r < (int64_t)rows; ++r)
+        for (uint64_t c = 0; c < cols; ++c) {
+            const double v = x[(uint64_t)r * ld + c];
+            const int32_t d = col_mode ? delta[c] : delta[r];
+            float dg[5];
+            make_digits(v, d, nd, dg);
+            const uint64_t idx = col_mode ? c * rows + (uint64_t)r : (uint64_t)r * cols + c;
+            for (int s = 0; s < S; ++s) {
+                const float cc[4] = {crt->c[0][s], crt->c[1][s], crt->c[2][s], crt->c[3][s]};
+                const float res = residue(dg, nd, (float)crt->m[s], crt->rinv[s], cc);
+                float digit[3];
+                const int nd2 = split_residue(res, fp->mode[s], (float)fp->q[s], qinv[s], digit);
+                for (int j = 0; j < nd2; ++j) {
+                    if (!e4m3_integer(digit[j])) bad = 1;
+                    planes[(uint64_t)(fp->poff[s] + j) * plane + idx] = (int8_t)(int)digit[j];
+                }
+            }
+        }
+    return bad;
+}
+
+int ozo_fp8_gemm(const int8_t* ap, const int8_t* bp, const oztt_fp8_plan* fp, uint64_t M, uint64_t N, uint64_t K,
+                 int32_t* out) {
+    int bad = 0;
+    const int64_t nout = fp->nout;
+#pragma omp parallel for collapse(2) schedule(static) reduction(| : bad)
+    for (int64_t o = 0; o < nout; ++o)
+        for (int64_t i = 0; i < (int64_t)M; ++i)
+            for (uint64_t j = 0; j < N; ++j) {
+                int64_t acc = 0;
+                for (int t = 0; t < fp->out_g[o]; ++t) {
+                    const int8_t* ar = ap + ((uint64_t)(fp->out_a[o] + t) * M + (uint64_t)i) * K;
+                    const int8_t* br = bp + ((uint64_t)(fp->out_b[o] - t) * N + j) * K;
+                    for (uint64_t k = 0; k < K; ++k) acc += (int32_t)ar[k] * (int32_t)br[k];
+                }
+                if (acc > (1 << 24) || acc < -(1 << 24)) bad = 1;
+                out[((uint64_t)o * M + (uint64_t)i) * N + j] = (int32_t)acc;
+            }
+    return bad;
+}
+
+int ozo_fp8_compose(const int32_t* P, const oztt_fp8_plan* fp, const ozo_plan* crt, uint64_t M, uint64_t N, float* r) {
+    const int S = crt->S;
+    const uint64_t plane = M * N;
+    for (int s = 0; s < S; ++s) {
+        const float m = (float)crt->m[s], ri = crt->rinv[s];
+        const int o0 = fp->oout[s], o1 = fp->oout[s + 1];
+        float lo[OZTT_MAXOUT], hi[OZTT_MAXOUT];
+        for (int o = o0; o < o1; ++o) {
+            lo[o] = (float)fp->coeff[o];                                   // c mod m (coeff_lo)
+            hi[o] = (float)(((int64_t)fp->coeff[o] * 4096) % crt->m[s]);  // c 2^12 mod m (coeff_hi)
+        }
+#pragma omp parallel for schedule(static)
+        for (int64_t e = 0; e < (int64_t)plane; ++e) {
+            float acc = 0.0f;
+            for (int o = o0; o < o1; ++o) {
+                const float p = (float)P[(uint64_t)o * plane + (uint64_t)e];
+                float v;
+                if (fp->fold_first) {
+                    v = fmul(mod_round(p, m, ri), lo[o]);
+                } else {
+                    const float h = frnd(fmul(p, 1.0f / 4096.0f));
+                    const float l = fsub(p, fmul(h, 4096.0f));
+                    v = fadd(fmul(h, hi[o]), fmul(l, lo[o]));
+                }
+                acc = (o == o0) ? v : fadd(acc, v);
+            }
+            r[(uint64_t)s * plane + (uint64_t)e] = mod_round(acc, m, ri);
+        }
+    }
+    return 0;
+}
+
+int ozo_fp8_emulate(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                    const oztt_fp8_plan* fp, int exact, char* err, size_t errlen) {
+    auto pad = [](uint64_t v, uint64_t q) { return (v + q - 1) / q * q; };
+    const uint64_t M = pad(m, 64), N = pad(n, 64), K = pad(k, 32);
+    std::vector<double> ap(M * K, 0.0), bp(K * N, 0.0);
+    for (uint64_t i = 0; i < m; ++i) std::copy_n(a + i * k, k, ap.data() + i * K);
+    for (uint64_t i = 0; i < k; ++i) std::copy_n(b + i * n, n, bp.data() + i * N);
+    ozo_plan crt;
+    if (ozo_crt_plan(fp->base.moduli, fp->base.S, fp->base.b, fp->base.two_pass, &crt)) {
+        set_err(err, errlen, "bad moduli set");
+        return 1;
+    }
+    std::vector<int32_t> dA(M), dB(N);
+    uint32_t fa = 0, fb = 0;
+    ozo_scale(ap.data(), M, K, K, 0, crt.shift, nullptr, dA.data(), &fa);
+    ozo_scale(bp.data(), K, N, N, 1, crt.shift, nullptr, dB.data(), &fb);
+    if (fa | fb) {
+        set_err(err, errlen, "out-of-range row or column maxima");
+        return 1;
+    }
+    const uint64_t NP = (uint64_t)fp->nplane;
+    std::vector<int8_t> da(NP * M * K), db(NP * N * K);
+    if (ozo_fp8_split(ap.data(), M, K, K, 0, dA.data(), &crt, fp, da.data()) |
+        ozo_fp8_split(bp.data(), K, N, N, 1, dB.data(), &crt, fp, db.data())) {
+        set_err(err, errlen, "a digit outside the integers of e4m3");
+        return 1;
+    }
+    std::vector<int32_t> P((uint64_t)fp->nout * M * N);
+    if (ozo_fp8_gemm(da.data(), db.data(), fp, M, N, K, P.data())) {
+        set_err(err, errlen, "a digit product above 2^24");
+        return 1;
+    }
+    std::vector<float> r((uint64_t)crt.S * M * N);
+    ozo_fp8_compose(P.data(), fp, &crt, M, N, r.data());
+    std::vector<double> cp(M * N);
+    if (exact) {
+        std::vector<int32_t> ri(r.size());
+        for (size_t e = 0; e < r.size(); ++e) ri[e] = (int32_t)r[e];
+        ozo_recon_exact(ri.data(), M, N, dA.data(), dB.data(), &crt, cp.data(), N);
+    } else {
+        ozo_recon_faithful_residue(r.data(), M, N, dA.data(), dB.data(), &crt, cp.data(), N);
+    }
+    for (uint64_t i = 0; i < m; ++i) std::copy_n(cp.data() + i * N, n, c + i * n);
+    return 0;
 }
 
 }  // extern "C"

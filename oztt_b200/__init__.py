@@ -116,6 +116,8 @@ class IIPlan(ctypes.Structure):
 
 
 MAXOUT = 96
+# Digit splitting methods of the FP8 plan (OZTT_SPLIT_* of include/oztt_cuda.h).
+SPLIT_SQ, SPLIT_KAR, SPLIT_WIDE, SPLIT_SQS = 0, 1, 2, 4
 
 
 class FP8Plan(ctypes.Structure):

@@ -81,6 +81,12 @@ class Oracle:
         L.ozo_i_recon_faithful.argtypes = [P, ctypes.c_int, u64, u64, P, P, P, u64]
         L.ozo_i_recon_exact.argtypes = [P, ctypes.c_int, u64, u64, P, P, P, u64]
         L.ozo_i_emulate.argtypes = [P, P, P, u64, u64, u64, ctypes.c_int, ctypes.c_int]
+        L.ozo_crt_plan.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(OzoPlan)]
+        L.ozo_fp8_split.argtypes = [P, u64, u64, u64, ctypes.c_int, P, ctypes.POINTER(OzoPlan), P, P]
+        L.ozo_fp8_gemm.argtypes = [P, P, P, u64, u64, u64, P]
+        L.ozo_fp8_compose.argtypes = [P, P, ctypes.POINTER(OzoPlan), u64, u64, P]
+        L.ozo_recon_faithful_residue.argtypes = [P, u64, u64, P, P, ctypes.POINTER(OzoPlan), P, u64]
+        L.ozo_fp8_emulate.argtypes = [P, P, P, u64, u64, u64, P, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
 
     # -- generators ---------------------------------------------------------------------------
     def gen_inputs(self, m: int, n: int, k: int, phi: float, seed: int) -> tuple[np.ndarray, np.ndarray]:
@@ -169,6 +175,42 @@ class Oracle:
         c = np.zeros(m * n)
         self.lib.ozo_i_emulate(ptr(a), ptr(b), ptr(c), m, n, k, p, 1 if exact else 0)
         return c
+
+    # -- Scheme II FP8 digits ---------------------------------------------------------------
+    # `fp` is an oztt_fp8_plan ctypes structure (the product's FP8Plan or the reference planner's).
+    def crt_plan(self, moduli, b: int, two_pass: int) -> OzoPlan:
+        m = np.asarray(moduli, dtype=np.int32)
+        p = OzoPlan()
+        assert self.lib.ozo_crt_plan(ptr(m), len(m), b, two_pass, ctypes.byref(p)) == 0
+        return p
+
+    def fp8_split(self, x: np.ndarray, rows: int, cols: int, col_mode: int, delta: np.ndarray, crt: OzoPlan,
+                  fp) -> tuple[int, np.ndarray]:
+        out = np.zeros(fp.nplane * rows * cols, dtype=np.int8)
+        bad = self.lib.ozo_fp8_split(ptr(x), rows, cols, cols, col_mode, ptr(delta), ctypes.byref(crt),
+                                     ctypes.byref(fp), ptr(out))
+        return bad, out
+
+    def fp8_gemm(self, da: np.ndarray, db: np.ndarray, fp, M: int, N: int, K: int) -> tuple[int, np.ndarray]:
+        out = np.zeros(fp.nout * M * N, dtype=np.int32)
+        bad = self.lib.ozo_fp8_gemm(ptr(da), ptr(db), ctypes.byref(fp), M, N, K, ptr(out))
+        return bad, out
+
+    def fp8_compose(self, P_: np.ndarray, fp, crt: OzoPlan, M: int, N: int) -> np.ndarray:
+        r = np.zeros(crt.S * M * N, dtype=np.float32)
+        self.lib.ozo_fp8_compose(ptr(P_), ctypes.byref(fp), ctypes.byref(crt), M, N, ptr(r))
+        return r
+
+    def recon_residue(self, r: np.ndarray, M: int, N: int, dA: np.ndarray, dB: np.ndarray, crt: OzoPlan) -> np.ndarray:
+        c = np.zeros(M * N)
+        self.lib.ozo_recon_faithful_residue(ptr(r), M, N, ptr(dA), ptr(dB), ctypes.byref(crt), ptr(c), N)
+        return c
+
+    def fp8_emulate(self, a, b, m, n, k, fp, exact=False) -> tuple[int, np.ndarray, str]:
+        c = np.zeros(m * n)
+        err = ctypes.create_string_buffer(512)
+        rc = self.lib.ozo_fp8_emulate(ptr(a), ptr(b), ptr(c), m, n, k, ctypes.byref(fp), 1 if exact else 0, err, 512)
+        return rc, c, err.value.decode()
 
     # -- metrics ------------------------------------------------------------------------------
     def output_hash(self, c: np.ndarray) -> str:

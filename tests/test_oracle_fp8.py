@@ -1,0 +1,101 @@
+"""The oracle's Scheme II FP8 (e4m3 digit) path pinned against the reference's published device output.
+
+CPU only. The digit plan comes from the library's FP8 planner (itself checked against the reference's
+planner compiled for FP8 in test_planner_fp8.py); the oracle then restates the digit split
+(modslice_digit.cpp, sparse_fix.h), the digit products, the composition (compose.cpp) and the
+reconstruction from residues (recon_crt.cpp with IN_RESIDUE=1).
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import oztt_b200 as oztt
+
+# tools/validated/quick.csv:11 — II FP8, n=128, seed 7, uniform(-1,1), fixed_bits 54, one pass: 12 moduli,
+# 36 digit products.
+PUBLISHED_128 = {"output_hash": "20046e5bb3816cbb", "relative_fro": 4.6875329326e-17,
+                 "effective_bits": 54.2439487868, "moduli": 12, "products": 36}
+
+
+def fp8_case(oracle, m, n, k, phi, seed, **kw):
+    a, b = oracle.gen_inputs(m, n, k, phi, seed)
+    fp = oztt.fp8_plan(a.reshape(m, k), b.reshape(k, n), m, n, k, **kw)
+    return a, b, fp
+
+
+def test_published_fp8_hash(oracle):
+    n = 128
+    a, b, fp = fp8_case(oracle, n, n, n, -1.0, 7, reconstruction=1, fixed_bits=54)
+    assert fp.base.S == PUBLISHED_128["moduli"] and fp.nprod == PUBLISHED_128["products"]
+    assert fp.base.b == 54 and fp.base.two_pass == 0
+    rc, c, err = oracle.fp8_emulate(a, b, n, n, n, fp)
+    assert rc == 0, err
+    assert oracle.output_hash(c) == PUBLISHED_128["output_hash"]
+    hi, lo = oracle.dot2(a, b, n, n, n)
+    rel, ebits = oracle.accuracy(c, hi, lo)
+    assert f"{rel:.10e}" == f"{PUBLISHED_128['relative_fro']:.10e}"
+    assert abs(ebits - PUBLISHED_128["effective_bits"]) < 1e-9
+
+
+def test_plan_uses_every_splitting_method(oracle):
+    """The published plan mixes sparse squares (SQS), squares (SQ) and Karatsuba (KAR); the digit planes of
+    every element are integers that e4m3 represents exactly."""
+    n = 128
+    a, b, fp = fp8_case(oracle, n, n, n, -1.0, 7, reconstruction=1, fixed_bits=54)
+    modes = {fp.mode[i] for i in range(fp.base.S)}
+    assert {oztt.SPLIT_SQ, oztt.SPLIT_KAR, oztt.SPLIT_SQS} <= modes
+    crt = oracle.crt_plan([fp.base.moduli[i] for i in range(fp.base.S)], fp.base.b, fp.base.two_pass)
+    _, dA, _ = oracle.scale(a, n, n, 0, crt.shift)
+    bad, planes = oracle.fp8_split(a, n, n, 0, dA, crt, fp)
+    assert bad == 0
+    vals = np.unique(planes)
+    assert np.all((np.abs(vals) <= 16) | ((np.abs(vals) <= 32) & (vals % 2 == 0)))
+    assert np.abs(vals).max() > 16  # the sparse digits are in use
+
+
+@pytest.mark.parametrize("m,n,k,phi,seed,passes", [(96, 160, 200, 0.5, 3, 1), (64, 64, 1000, 2.0, 5, 2),
+                                                   (130, 70, 64, -1.0, 11, 0)])
+def test_faithful_and_exact_agree(oracle, m, n, k, phi, seed, passes):
+    """The reference's triple-float reconstruction and the exact one give results within a few units in the
+    last place of the exact CRT value (the faithful pass's documented error)."""
+    a, b, fp = fp8_case(oracle, m, n, k, phi, seed, reconstruction=passes)
+    rc, cf, err = oracle.fp8_emulate(a, b, m, n, k, fp)
+    assert rc == 0, err
+    rc, ce, err = oracle.fp8_emulate(a, b, m, n, k, fp, exact=True)
+    assert rc == 0, err
+    hi, lo = oracle.dot2(a, b, m, n, k)
+    scale = np.abs(a.reshape(m, k)) @ np.abs(b.reshape(k, n))
+    err_f = np.abs(cf - ce).reshape(m, n) / np.maximum(scale, 1e-300)
+    assert err_f.max() < 2.0 ** -(fp.base.b + 2) * 64
+    rel, _ = oracle.accuracy(ce, hi, lo)
+    assert rel < 1e-15
+
+
+def test_compose_split_matches_fold_first(oracle):
+    """Both composition methods (reduce first, or split at 2^12 with coeff_hi) give the same residue class:
+    with the exact reconstruction the outputs are identical."""
+    m = n = 64
+    k = 256
+    a, b, fp = fp8_case(oracle, m, n, k, 1.0, 9)
+    rc, c1, err = oracle.fp8_emulate(a, b, m, n, k, fp, exact=True)
+    assert rc == 0, err
+    fp2 = oztt.FP8Plan()
+    ctypes.memmove(ctypes.byref(fp2), ctypes.byref(fp), ctypes.sizeof(fp))
+    fp2.fold_first = 1 - fp.fold_first
+    rc, c2, err = oracle.fp8_emulate(a, b, m, n, k, fp2, exact=True)
+    assert rc == 0, err
+    assert np.array_equal(c1.view(np.uint64), c2.view(np.uint64))
+
+
+def test_reference_plan_reproduces_hash(oracle, ref_plan_f8):
+    """With the reference's own FP8 planner (compiled in place) the oracle reproduces the same hash."""
+    n = 128
+    a, b = oracle.gen_inputs(n, n, n, -1.0, 7)
+    from oracle_lib import pad
+    rc, fp = ref_plan_f8.plan(pad(a, n, n, n, n), pad(b, n, n, n, n), n, n, n, oztt.FP8Plan, 0, 1, 54)
+    assert rc == 0
+    rc, c, err = oracle.fp8_emulate(a, b, n, n, n, fp)
+    assert rc == 0, err
+    assert oracle.output_hash(c) == PUBLISHED_128["output_hash"]
