@@ -9,6 +9,8 @@
  * Layering, with the reference interface each entry point stands in for (paths relative to the
  * reference project root):
  *   oztt_gemm                 Context::gemm (src/context.cpp:182-186): validation, planning, GPU run
+ *   oztt_is_available         ozTTgemm::is_available / format_name (src/dispatch.cpp:18-50)
+ *   oztt_ii_fp8_*             the same stages for the FP8 (e4m3 digit) backend of scheme II
  *   oztt_ii_int8_plan         choose_moduli_and_width (src/backend/ozaki2/plan.hpp:258-306) for INT8
  *   oztt_ii_int8_run          ozaki2_int8::run (src/ozaki2.cpp:439-478) on host buffers: the backend
  *                             seam Backend = Output(*)(Device&, const Problem&)
@@ -116,6 +118,42 @@ typedef struct oztt_fp8_plan {
  * moduli.hpp:710-770); arguments as oztt_ii_int8_plan (default limit 14 moduli with a fixed width). */
 int oztt_ii_fp8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
                   int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan* plan, char* err, size_t errlen);
+/* The same plan from DEVICE operands a (m x k) and b (k x n) on `stream`: the precision policy's statistics
+ * are measured on the GPU (as oztt_ii_int8_plan_device). */
+int oztt_ii_fp8_plan_device(int device_id, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                            uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan* plan,
+                            void* stream, char* err, size_t errlen);
+
+/* Whole FP8 pipeline with a given plan on HOST buffers (row-major, C = A B): upload, scale, digit split,
+ * digit products with the composition fused, reconstruction, download. Replaces the FP8 backend's run
+ * (src/ozaki2.cpp:439-478 compiled with OZ_FMT_FP8). */
+int oztt_ii_fp8_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                    const oztt_fp8_plan* plan, char* err, size_t errlen);
+/* The same on DEVICE buffers, stream-ordered on `stream`; stage_ms (NULL or 6 doubles) receives the device
+ * time of scale rows, scale cols, split rows, split cols, digit GEMM and reconstruction. */
+int oztt_ii_fp8_run_device(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                           uint64_t k, const oztt_fp8_plan* plan, void* stream, double* stage_ms, char* err,
+                           size_t errlen);
+
+/* FP8 stages (device buffers, stream-ordered). Digit split (kernels/modslice_digit.cpp with sparse_fix.h):
+ * the residues of A (m x k, lda) split into the e4m3 digits of each modulus, written as int8 values to
+ * planes [nplane][mp][kp] (plane poff[s] + 0 = l, + 1 = h, + 2 = s); B (k x n, ldb) transposed into
+ * [nplane][np][kp]. delta as from oztt_ii_scale_rows / _cols with the plan's shift. */
+int oztt_ii_fp8_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
+                           const oztt_fp8_plan* plan, int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err,
+                           size_t errlen);
+int oztt_ii_fp8_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
+                           const oztt_fp8_plan* plan, int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err,
+                           size_t errlen);
+/* Digit products (the reference's GEMM stage on digit planes with compose.cpp): mode 0 writes every GEMM
+ * output P_o as int32 [nout][mp][np]; mode 1 composes in the epilogue and writes the CRT digits
+ * k_s = (sum_o coeff_o P_o) y_s mod m_s as uint16 [S][mp][np]. mp, np, kp multiples of 128, 256, 128. */
+int oztt_ii_fp8_digit_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp, uint64_t np, uint64_t kp,
+                           const oztt_fp8_plan* plan, int32_t mode, void* out, void* stream, char* err, size_t errlen);
+/* Reconstruction from uint16 CRT digits [S][mp][np] (as oztt_ii_recon). */
+int oztt_ii_fp8_recon(const uint16_t* k_digits, uint64_t mp, uint64_t np, const int32_t* delta_a,
+                      const int32_t* delta_b, const oztt_fp8_plan* plan, double* c, uint64_t m, uint64_t n,
+                      uint64_t ldc, void* stream, char* err, size_t errlen);
 
 /* Plan of one Scheme I INT8 call (src/ozaki1.cpp:192-210): the number of slices p (radix 254, digits
  * +-127, target 2^-1), the last diagonal L = p-1 kept. */
@@ -133,6 +171,11 @@ typedef struct oztt_i_plan {
 int oztt_gemm(int device_id, const double* a, uint64_t a_len, const double* b, uint64_t b_len, double* c,
               uint64_t c_len, uint64_t m, uint64_t n, uint64_t k, const oztt_options* opt, oztt_info* info, char* err,
               size_t errlen);
+
+/* ozTTgemm::is_available / format_name (src/dispatch.cpp:18-50) for an OZTT_FMT_* value: 1 for the formats
+ * this build provides (INT8; FP8 for scheme II), 0 otherwise; the name, or "unknown". */
+int oztt_is_available(int32_t format);
+const char* oztt_format_name(int32_t format);
 
 /* Scheme II INT8 plan for row-major a (m x k) and b (k x n) on the host. reconstruction is an
  * OZTT_RECON_* value; fixed_bits > 0 fixes the width (the reference evaluator's fixed_bits), 0 lets

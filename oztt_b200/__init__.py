@@ -171,6 +171,15 @@ _SIGNATURES = {
                                      ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.POINTER(IIPlan), _ERR,
                                      _SZ],
     "oztt_ii_fp8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, _I32, _I32, ctypes.POINTER(FP8Plan), _ERR, _SZ],
+    "oztt_ii_fp8_plan_device": [ctypes.c_int, _P, _P, _U64, _U64, _U64, ctypes.c_uint32, _I32, _I32,
+                                ctypes.POINTER(FP8Plan), _P, _ERR, _SZ],
+    "oztt_ii_fp8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(FP8Plan), _ERR, _SZ],
+    "oztt_ii_fp8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(FP8Plan), _P, _P, _ERR,
+                               _SZ],
+    "oztt_ii_fp8_split_rows": [_P, _U64, _U64, _U64, _P, ctypes.POINTER(FP8Plan), _P, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_ii_fp8_split_cols": [_P, _U64, _U64, _U64, _P, ctypes.POINTER(FP8Plan), _P, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_ii_fp8_digit_gemm": [_P, _P, _U64, _U64, _U64, ctypes.POINTER(FP8Plan), _I32, _P, _P, _ERR, _SZ],
+    "oztt_ii_fp8_recon": [_P, _U64, _U64, _P, _P, ctypes.POINTER(FP8Plan), _P, _U64, _U64, _U64, _P, _ERR, _SZ],
     "oztt_i_int8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _P, _P, _ERR, _SZ],
@@ -178,11 +187,13 @@ _SIGNATURES = {
     "oztt_i_slice_cols": [_P, _U64, _U64, _U64, _P, _I32, _P, _U64, _U64, _P, _ERR, _SZ],
     "oztt_i_diag_gemm": [_P, _P, _U64, _U64, _U64, _I32, _P, _P, _ERR, _SZ],
     "oztt_i_recon": [_P, _U64, _U64, _P, _P, _I32, _P, _U64, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_is_available": [_I32],
+    "oztt_format_name": [_I32],
     "oztt_test_udiv_small": [ctypes.c_uint32, ctypes.c_uint32],
     "oztt_test_ext80_dot": [_P, _P, _U64, ctypes.c_double],
 }
 
-_RESTYPES = {"oztt_policy_vectors": None, "oztt_test_udiv_small": ctypes.c_uint32, "oztt_test_ext80_dot": ctypes.c_double, "oztt_ii_padded_dims": None, "oztt_eval_inputs": None,
+_RESTYPES = {"oztt_format_name": ctypes.c_char_p, "oztt_policy_vectors": None, "oztt_test_udiv_small": ctypes.c_uint32, "oztt_test_ext80_dot": ctypes.c_double, "oztt_ii_padded_dims": None, "oztt_eval_inputs": None,
              "oztt_eval_output_hash": ctypes.c_uint64}
 
 # Symbols declared in include/oztt_cuda.h (the tests check that the library exports each of them).
@@ -232,8 +243,8 @@ def _errbuf() -> ctypes.Array:
 
 
 def is_available(fmt) -> bool:
-    """False for formats this build does not provide (mirrors ozTTgemm::is_available)."""
-    return int(fmt) == Format.INT8
+    """False for formats this build does not provide (ozTTgemm::is_available through oztt_is_available)."""
+    return bool(_lib().oztt_is_available(int(fmt)))
 
 
 def format_name(fmt) -> str:
@@ -380,6 +391,47 @@ def ii_int8_run_device_timed(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int,
     if rc != OK:
         _raise(rc, err.value)
     return list(ms)
+
+
+def fp8_plan_device(a_ptr: int, b_ptr: int, m: int, n: int, k: int, max_moduli: int = 0, reconstruction: int = 0,
+                    fixed_bits: int = 0, stream: int = 0, device_id: int = 0) -> FP8Plan:
+    """Scheme II FP8 plan for device-resident operands, the statistics measured on the device
+    (oztt_ii_fp8_plan_device)."""
+    plan = FP8Plan()
+    err = _errbuf()
+    rc = _lib().oztt_ii_fp8_plan_device(device_id, a_ptr, b_ptr, m, n, k, max_moduli, reconstruction, fixed_bits,
+                                        ctypes.byref(plan), stream, err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return plan
+
+
+def fp8_run(a, b, m: int, n: int, k: int, plan: FP8Plan, device_id: int = 0) -> np.ndarray:
+    """The Scheme II FP8 pipeline on host matrices with a given plan (oztt_ii_fp8_run)."""
+    av, bv = _as_f64(a, "a"), _as_f64(b, "b")
+    if av.size != m * k or bv.size != k * n:
+        raise ValueError("matrix span sizes do not match m, n, k")
+    c = np.empty(m * n, dtype=np.float64)
+    err = _errbuf()
+    rc = _lib().oztt_ii_fp8_run(device_id, av.ctypes.data, bv.ctypes.data, c.ctypes.data, m, n, k, ctypes.byref(plan),
+                                err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return c
+
+
+def fp8_run_device(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, plan: FP8Plan, stream: int = 0,
+                   device_id: int = 0, timed: bool = False) -> list[float] | None:
+    """The FP8 pipeline on device pointers (oztt_ii_fp8_run_device); synchronises `stream`. With timed=True
+    returns the device milliseconds of scale rows, scale columns, split rows, split columns, digit GEMM and
+    reconstruction."""
+    ms = (ctypes.c_double * 6)()
+    err = _errbuf()
+    rc = _lib().oztt_ii_fp8_run_device(device_id, a_ptr, b_ptr, c_ptr, m, n, k, ctypes.byref(plan), stream,
+                                       ms if timed else None, err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return list(ms) if timed else None
 
 
 def i_int8_plan(a, b, m: int, n: int, k: int, slices: int = 0) -> IPlan:

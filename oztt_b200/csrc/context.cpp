@@ -9,8 +9,9 @@
 //   * one process-wide mutex serialises the calls of all contexts (:19, :152);
 //   * the device is opened on the first valid call; Info reports the padded dimensions (:176-180);
 //   * all input is consumed before C is written, so C may overlap A or B.
-// Dispatch (src/dispatch.cpp:18-50): INT8 is built; the Tenstorrent block formats BFP8/BFP4/BFP2
-// are not available on this hardware, and the other formats are not built yet.
+// Dispatch (src/dispatch.cpp:18-50): INT8 (schemes I and II) and FP8 (scheme II, e4m3 digits) are built;
+// the Tenstorrent block formats BFP8/BFP4/BFP2 are not available on this hardware, and BF16, FP16 and
+// TF32 are not built yet.
 #include <ozTTgemm/ozTTgemm.hpp>
 
 #include <algorithm>
@@ -28,6 +29,8 @@
 namespace oztt {
 int run_ii_int8_planned(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
                         uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_ii_plan& p, std::string& err);
+int run_ii_fp8_planned(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                       uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_fp8_plan& p, std::string& err);
 }  // namespace oztt
 
 namespace ozTTgemm {
@@ -134,7 +137,7 @@ int32_t recon_code(Reconstruction r) {
 
 }  // namespace
 
-bool is_available(Format format) noexcept { return format == Format::INT8; }
+bool is_available(Format format) noexcept { return format == Format::INT8 || format == Format::FP8; }
 
 const char* format_name(Format format) noexcept {
     switch (format) {
@@ -166,6 +169,24 @@ Context::~Context() = default;
 Info Context::Impl::execute(std::span<const double> a, std::span<const double> b, std::span<double> c, std::size_t m,
                             std::size_t n, std::size_t k, const Options& opt, const Checked& v) {
     std::lock_guard lock(runtime_mutex);
+    if (opt.format == Format::FP8) {
+        if (opt.scheme == Scheme::I)
+            throw std::runtime_error("Ozaki scheme I with FP8 digits is not built in this version");
+        oztt_fp8_plan plan;
+        std::string msg;
+        const int rc = oztt::run_ii_fp8_planned(options.device_id, a.data(), b.data(), c.data(), m, n, k,
+                                                opt.max_moduli, recon_code(opt.reconstruction), plan, msg);
+        if (rc != OZTT_OK) rethrow(rc, msg);
+        opened = true;
+        Info info{Scheme::II, opt.format};
+        info.moduli = (std::uint32_t)plan.base.S;
+        info.integer_bits = (std::uint32_t)plan.base.b;
+        info.reconstruction_passes = plan.base.two_pass ? 2u : 1u;
+        info.padded_m = v.mp;
+        info.padded_n = v.np;
+        info.padded_k = v.kp;
+        return info;
+    }
     if (opt.scheme == Scheme::I) {
         oztt_i_plan plan;
         std::string msg;
@@ -215,6 +236,13 @@ std::vector<double> Context::multiply(std::span<const double> a, std::span<const
 }
 
 }  // namespace ozTTgemm
+
+extern "C" int oztt_is_available(int32_t format) {
+    return ozTTgemm::is_available(static_cast<ozTTgemm::Format>(format)) ? 1 : 0;
+}
+extern "C" const char* oztt_format_name(int32_t format) {
+    return ozTTgemm::format_name(static_cast<ozTTgemm::Format>(format));
+}
 
 extern "C" int oztt_gemm(int device_id, const double* a, uint64_t a_len, const double* b, uint64_t b_len, double* c,
                          uint64_t c_len, uint64_t m, uint64_t n, uint64_t k, const oztt_options* opt, oztt_info* info,

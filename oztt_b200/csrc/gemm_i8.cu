@@ -56,6 +56,12 @@ enum ErrCode : int { ERR_WAIT_PRODUCER = 1, ERR_WAIT_MMA_FULL = 2, ERR_WAIT_MMA_
 struct EpiConst {
     uint32_t S;
     uint32_t m[OZTT_MAXS], y[OZTT_MAXS], magic[OZTT_MAXS], shift[OZTT_MAXS];
+    // FP8 digit products (modes 3 and 4): the outputs of modulus s are oout[s] .. oout[s+1]-1; output u
+    // sums the products of A digit plane out_a[u] + t and B digit plane out_b[u] - t over t < out_g[u]
+    // (the concatenation along K); weight[u] = (composition coefficient * y_s) mod m_s.
+    uint16_t oout[OZTT_MAXS + 1];
+    uint8_t out_a[OZTT_MAXOUT], out_b[OZTT_MAXOUT], out_g[OZTT_MAXOUT];
+    uint16_t weight[OZTT_MAXOUT];
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -203,6 +209,36 @@ __device__ __forceinline__ void kblock_coords(uint32_t kb, uint32_t plane, uint3
     }
 }
 
+// Accumulator units of a tile: one for modes 0-2; for the digit modes 3 and 4 one per GEMM output of
+// the tile's modulus, each accumulated in its own TMEM buffer.
+template <int MODE>
+__device__ __forceinline__ void tile_units(uint32_t plane, const EpiConst& ec, uint32_t& u0, uint32_t& u1) {
+    if constexpr (MODE >= 3) {
+        u0 = ec.oout[plane];
+        u1 = ec.oout[plane + 1];
+    } else {
+        u0 = 0;
+        u1 = 1;
+    }
+}
+// The operand planes of unit u: g pairs (A plane a0 + t, B plane b0 - t), each over all K blocks.
+template <int MODE>
+__device__ __forceinline__ void unit_operands(uint32_t plane, uint32_t u, const EpiConst& ec, uint32_t& a0,
+                                              uint32_t& b0, uint32_t& g) {
+    if constexpr (MODE >= 3) {
+        a0 = ec.out_a[u];
+        b0 = ec.out_b[u];
+        g = ec.out_g[u];
+    } else if constexpr (MODE == 2) {
+        a0 = 0;
+        b0 = plane;
+        g = plane + 1;
+    } else {
+        a0 = b0 = plane;
+        g = 1;
+    }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     residue_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -254,25 +290,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t filled = 0, last_phase = 0;  // per-stage bit masks of the last fill
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-                uint32_t plane, tm, tn, kb_total;
+                uint32_t plane, tm, tn, kb_total, u0, u1;
                 tile_work<MODE>(tile, ec.S, tiles_m, tiles_n, num_kb, plane, tm, tn, kb_total);
-                for (uint32_t kb = 0; kb < kb_total; ++kb) {
-                    if (!mbar_wait(empty_bar + stage, phase ^ 1u, abort_flag, err, ERR_WAIT_PRODUCER)) {
-                        ok = false;
-                        break;
-                    }
-                    int32_t k_el, pa, pb;
-                    kblock_coords<MODE>(kb, plane, num_kb, k_el, pa, pb);
-                    mbar_expect_tx(full_bar + stage, STAGE_BYTES);
-                    const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
-                    tma_load_3d(&tmA, sa, full_bar + stage, k_el, (int32_t)(tm * BM), pa);
-                    tma_load_3d(&tmB, sa + A_BYTES, full_bar + stage, k_el, (int32_t)(tn * BN), pb);
-                    filled |= 1u << stage;
-                    last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
+                tile_units<MODE>(plane, ec, u0, u1);
+                for (uint32_t u = u0; ok && u < u1; ++u) {
+                    uint32_t a0, b0, g;
+                    unit_operands<MODE>(plane, u, ec, a0, b0, g);
+                    for (uint32_t t = 0; ok && t < g; ++t)
+                        for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                            if (!mbar_wait(empty_bar + stage, phase ^ 1u, abort_flag, err, ERR_WAIT_PRODUCER)) {
+                                ok = false;
+                                break;
+                            }
+                            const int32_t k_el = (int32_t)(kb * BK);
+                            mbar_expect_tx(full_bar + stage, STAGE_BYTES);
+                            const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+                            tma_load_3d(&tmA, sa, full_bar + stage, k_el, (int32_t)(tm * BM), (int32_t)(a0 + t));
+                            tma_load_3d(&tmB, sa + A_BYTES, full_bar + stage, k_el, (int32_t)(tn * BN),
+                                        (int32_t)(b0 - t));
+                            filled |= 1u << stage;
+                            last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+                            if (++stage == STAGES) {
+                                stage = 0;
+                                phase ^= 1u;
+                            }
+                        }
                 }
             }
             if (!ok)  // let every load this thread issued land before the CTA may exit
@@ -284,31 +326,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
             bool ok = true;
             for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-                uint32_t plane, tm, tn, kb_total;
+                uint32_t plane, tm, tn, kb_total, u0, u1;
                 tile_work<MODE>(tile, ec.S, tiles_m, tiles_n, num_kb, plane, tm, tn, kb_total);
-                if (!mbar_wait(tempty_bar + acc, acc_phase ^ 1u, abort_flag, err, ERR_WAIT_MMA_EMPTY)) break;
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
-                for (uint32_t kb = 0; kb < kb_total; ++kb) {
-                    if (!mbar_wait(full_bar + stage, phase, abort_flag, err, ERR_WAIT_MMA_FULL)) {
+                tile_units<MODE>(plane, ec, u0, u1);
+                for (uint32_t u = u0; ok && u < u1; ++u) {
+                    uint32_t a0, b0, g;
+                    unit_operands<MODE>(plane, u, ec, a0, b0, g);
+                    if (!mbar_wait(tempty_bar + acc, acc_phase ^ 1u, abort_flag, err, ERR_WAIT_MMA_EMPTY)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES), sb = sa + A_BYTES;
+                    const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+                    for (uint32_t t = 0; ok && t < g; ++t)
+                        for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                            if (!mbar_wait(full_bar + stage, phase, abort_flag, err, ERR_WAIT_MMA_FULL)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES), sb = sa + A_BYTES;
 #pragma unroll
-                    for (uint32_t k = 0; k < BK / UK; ++k)
-                        umma_i8(d_tmem, sdesc_sw128(sa + k * UK), sdesc_sw128(sb + k * UK), (kb | k) != 0u);
-                    umma_commit(empty_bar + stage);
-                    if (++stage == STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
+                            for (uint32_t k = 0; k < BK / UK; ++k)
+                                umma_i8(d_tmem, sdesc_sw128(sa + k * UK), sdesc_sw128(sb + k * UK),
+                                        (t | kb | k) != 0u);
+                            umma_commit(empty_bar + stage);
+                            if (++stage == STAGES) {
+                                stage = 0;
+                                phase ^= 1u;
+                            }
+                        }
+                    if (!ok) break;
+                    umma_commit(tfull_bar + acc);
+                    acc ^= 1u;
+                    if (acc == 0) acc_phase ^= 1u;
                 }
-                if (!ok) break;
-                umma_commit(tfull_bar + acc);
-                acc ^= 1u;
-                if (acc == 0) acc_phase ^= 1u;
             }
             // Every MMA this thread issued completes before the columns are freed.
             umma_commit(drain_bar);
@@ -317,47 +369,89 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else {
         const uint32_t quarter = warp & 3u;
         uint32_t acc = 0, acc_phase = 0;
-        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            uint32_t s, tm, tn, kb_total;
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+            uint32_t s, tm, tn, kb_total, u0, u1;
             tile_work<MODE>(tile, ec.S, tiles_m, tiles_n, num_kb, s, tm, tn, kb_total);
-            if (!mbar_wait(tfull_bar + acc, acc_phase, abort_flag, err, ERR_WAIT_EPILOGUE)) break;
-            tc_fence_after();
-            const uint64_t row = (uint64_t)tm * BM + quarter * 32u + lane;
-            const uint32_t tbase = tmem_base + ((quarter * 32u) << 16) + acc * ACC_COLS;
-            const uint32_t m = ec.m[s % OZTT_MAXS], y = ec.y[s % OZTT_MAXS], mg = ec.magic[s % OZTT_MAXS],
-                           sh = ec.shift[s % OZTT_MAXS];
-#pragma unroll 1
-            for (uint32_t c = 0; c < BN; c += 32) {
-                uint32_t v[32];
-                tmem_ld32(tbase + c, v);
-                const uint64_t off = ((uint64_t)s * mp + row) * np + (uint64_t)tn * BN + c;
-                if constexpr (MODE == 0 || MODE == 2) {
-                    uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<int32_t*>(out) + off);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) o[q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                } else {
-                    uint32_t w[8];
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) w[q] = 0;
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        const int32_t cv = (int32_t)v[e];
-                        const uint32_t a = cv < 0 ? (uint32_t)(-cv) : (uint32_t)cv;
-                        uint32_t r = a - udiv_small(a, mg, sh) * m;
-                        if (cv < 0 && r) r = m - r;
-                        const uint32_t t = r * y;
-                        const uint32_t kk = t - udiv_small(t, mg, sh) * m;
-                        w[e >> 2] |= kk << (8 * (e & 3));
-                    }
-                    uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out) + off);
-                    o[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                    o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            tile_units<MODE>(s, ec, u0, u1);
+            for (uint32_t u = u0; u < u1; ++u) {
+                if (!mbar_wait(tfull_bar + acc, acc_phase, abort_flag, err, ERR_WAIT_EPILOGUE)) {
+                    ok = false;
+                    break;
                 }
+                tc_fence_after();
+                const uint64_t row = (uint64_t)tm * BM + quarter * 32u + lane;
+                const uint32_t tbase = tmem_base + ((quarter * 32u) << 16) + acc * ACC_COLS;
+                const uint32_t m = ec.m[s % OZTT_MAXS], y = ec.y[s % OZTT_MAXS], mg = ec.magic[s % OZTT_MAXS],
+                               sh = ec.shift[s % OZTT_MAXS];
+                const uint32_t out_plane = MODE == 4 ? u : s;
+#pragma unroll 1
+                for (uint32_t c = 0; c < BN; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tbase + c, v);
+                    const uint64_t off = ((uint64_t)out_plane * mp + row) * np + (uint64_t)tn * BN + c;
+                    if constexpr (MODE == 0 || MODE == 2 || MODE == 4) {
+                        uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<int32_t*>(out) + off);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            o[q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    } else if constexpr (MODE == 1) {
+                        uint32_t w[8];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) w[q] = 0;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            const int32_t cv = (int32_t)v[e];
+                            const uint32_t a = cv < 0 ? (uint32_t)(-cv) : (uint32_t)cv;
+                            uint32_t r = a - udiv_small(a, mg, sh) * m;
+                            if (cv < 0 && r) r = m - r;
+                            const uint32_t t = r * y;
+                            const uint32_t kk = t - udiv_small(t, mg, sh) * m;
+                            w[e >> 2] |= kk << (8 * (e & 3));
+                        }
+                        uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out) + off);
+                        o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                        o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                    } else {
+                        // Composition into the CRT digit k_s = sum_u weight_u (P_u mod m) mod m, uint16: the
+                        // first output of the modulus writes its term, the later ones add to what this same
+                        // thread wrote for the previous output (a plain load of its own store).
+                        const uint32_t wgt = ec.weight[u];
+                        uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + off);
+                        uint32_t w[16];
+                        if (u == u0) {
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) w[q] = 0;
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const uint4 pv = o[q];
+                                w[4 * q] = pv.x;
+                                w[4 * q + 1] = pv.y;
+                                w[4 * q + 2] = pv.z;
+                                w[4 * q + 3] = pv.w;
+                            }
+                        }
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            const int32_t cv = (int32_t)v[e];
+                            const uint32_t a = cv < 0 ? (uint32_t)(-cv) : (uint32_t)cv;
+                            uint32_t r = a - udiv_small(a, mg, sh) * m;
+                            if (cv < 0 && r) r = m - r;
+                            const uint32_t t = r * wgt;
+                            uint32_t kk = t - udiv_small(t, mg, sh) * m + ((w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu);
+                            if (kk >= m) kk -= m;
+                            w[e >> 1] = (w[e >> 1] & (0xFFFF0000u >> (16 * (e & 1)))) | (kk << (16 * (e & 1)));
+                        }
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) o[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(tempty_bar + acc);
+                acc ^= 1u;
+                if (acc == 0) acc_phase ^= 1u;
             }
-            tc_fence_before();
-            mbar_arrive(tempty_bar + acc);
-            acc ^= 1u;
-            if (acc == 0) acc_phase ^= 1u;
         }
     }
     __syncthreads();
@@ -692,7 +786,8 @@ void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* out, uint64
     OZTT_CUDA(cudaGetDevice(&dev));
     OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const uint32_t tiles_n = (uint32_t)(np / BN), num_kb = (uint32_t)(kp / BK);
-    if (use_pairs()) {
+    if (MODE < 3 && use_pairs()) {
+        // the CTA-pair kernel covers modes 0-2
         const uint32_t tiles_m2 = (uint32_t)((mp / 128 + 1) / 2);
         const uint64_t num_tiles = (uint64_t)planes * tiles_m2 * tiles_n;
         OZTT_CUDA(cudaFuncSetAttribute(residue_gemm_pair_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -713,8 +808,9 @@ void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* out, uint64
         OZTT_CUDA(cudaOccupancyMaxActiveClusters(&clusters, residue_gemm_pair_kernel<MODE>, &cfg));
         if (clusters < 1) throw Error(OZTT_ERUNTIME, "residue_gemm: no CTA pair fits on this device");
         const unsigned grid = 2u * (unsigned)std::min<uint64_t>(num_tiles, (uint64_t)clusters);
-        residue_gemm_pair_kernel<MODE><<<grid, pair::NUM_THREADS, pair::SMEM_BYTES, st>>>(
-            ta, tb, out, tiles_m2, tiles_n, num_kb, mp, np, ec, err_word);
+        if constexpr (MODE < 3)
+            residue_gemm_pair_kernel<MODE><<<grid, pair::NUM_THREADS, pair::SMEM_BYTES, st>>>(
+                ta, tb, out, tiles_m2, tiles_n, num_kb, mp, np, ec, err_word);
     } else {
         const uint32_t tiles_m = (uint32_t)(mp / BM);
         const uint64_t num_tiles = (uint64_t)planes * tiles_m * tiles_n;
@@ -775,6 +871,61 @@ void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t 
     const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p, pairs ? pair::BM : BM);
     const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p, pairs ? pair::BNH : BN);
     launch_gemm<2>(ta, tb, out, mp, np, kp, (uint32_t)p, ec, err_word, st);
+}
+
+// FP8 digit products on the tensor cores: for each GEMM output u of the plan, P_u = sum_t A_(out_a+t)
+// B_(out_b-t)^T over the digit planes A [nplane][mp][kp] and B [nplane][np][kp] (int8 values of the e4m3
+// digits, exact s32 sums). mode 0: P_u as int32 [nout][mp][np]; mode 1: the composition fused into the
+// epilogue, the CRT digits k_s = (sum_u c_u P_u) y_s mod m_s as uint16 [S][mp][np] (compose.cpp and the
+// term_k of recon_crt_proc.h, as one exact integer computation).
+void launch_digit_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
+                       const oztt_fp8_plan& fp, int mode, void* out, int* err_word, cudaStream_t st) {
+    using namespace gemm;
+    if (mp % BM || np % BN || kp % BK || mp == 0 || np == 0 || kp == 0)
+        throw Error(OZTT_EINVAL, "digit_gemm: mp, np, kp must be positive multiples of 128, 256 and 128");
+    const int S = fp.base.S;
+    if (S < 1 || S > OZTT_MAXS) throw Error(OZTT_EINVAL, "digit_gemm: bad number of moduli");
+    if (fp.nout < 1 || fp.nout > OZTT_MAXOUT || fp.nplane < 1 || fp.nplane > 255 || fp.oout[0] != 0 ||
+        fp.oout[S] != fp.nout)
+        throw Error(OZTT_EINVAL, "digit_gemm: bad digit plan");
+    if ((reinterpret_cast<uintptr_t>(ap) | reinterpret_cast<uintptr_t>(bp)) & 15)
+        throw Error(OZTT_EINVAL, "digit_gemm: planes must be 16-byte aligned");
+    if (mode != 0 && mode != 1) throw Error(OZTT_EINVAL, "digit_gemm: mode must be 0 or 1");
+    EpiConst ec{};
+    ec.S = (uint32_t)S;
+    int max_g = 1;
+    for (int s = 0; s < S; ++s) {
+        const int m = fp.base.moduli[s];
+        if (m < 3 || m > 4096) throw Error(OZTT_EINVAL, "digit_gemm: moduli must be in 3..4096");
+        ec.m[s] = (uint32_t)m;
+        ec.y[s] = (uint32_t)fp.base.yi[s];
+        udiv_magic(ec.m[s], ec.magic[s], ec.shift[s]);
+        if (fp.oout[s + 1] < fp.oout[s]) throw Error(OZTT_EINVAL, "digit_gemm: bad output ranges");
+        ec.oout[s] = (uint16_t)fp.oout[s];
+        for (int u = fp.oout[s]; u < fp.oout[s + 1]; ++u) {
+            const int g = fp.out_g[u];
+            if (fp.out_mod[u] != s || g < 1 || fp.out_a[u] < 0 || fp.out_a[u] + g > fp.nplane ||
+                fp.out_b[u] - g + 1 < 0 || fp.out_b[u] >= fp.nplane)
+                throw Error(OZTT_EINVAL, "digit_gemm: output " + std::to_string(u) + " names planes outside the plan");
+            max_g = std::max(max_g, g);
+            ec.out_a[u] = (uint8_t)fp.out_a[u];
+            ec.out_b[u] = (uint8_t)fp.out_b[u];
+            ec.out_g[u] = (uint8_t)g;
+            const int64_t c = ((int64_t)fp.coeff[u] % m + m) % m;
+            ec.weight[u] = (uint16_t)(c * fp.base.yi[s] % m);
+        }
+    }
+    ec.oout[S] = (uint16_t)fp.nout;
+    // |P_u| <= kp * g * 32^2 must stay below 2^31 (s32 accumulators, the epilogue's division)
+    if ((uint64_t)kp * (uint64_t)max_g * 1024ull >= (1ull << 31))
+        throw Error(OZTT_EINVAL, "digit_gemm: K too large for exact 32-bit digit sums");
+    if (mp / BM * (np / BN) * (uint64_t)S >= (1ull << 31)) throw Error(OZTT_EINVAL, "digit_gemm: problem too large");
+    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)fp.nplane, BM);
+    const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)fp.nplane, BN);
+    if (mode == 0)
+        launch_gemm<4>(ta, tb, out, mp, np, kp, (uint32_t)S, ec, err_word, st);
+    else
+        launch_gemm<3>(ta, tb, out, mp, np, kp, (uint32_t)S, ec, err_word, st);
 }
 
 // Host model of the epilogue's division, for the CPU tests of the C ABI.

@@ -104,23 +104,36 @@ __device__ __forceinline__ double crt_finish(const uint64_t (&acc)[NW], int32_t 
     return neg ? -r : r;
 }
 
-// One thread = 4 consecutive columns of one row: the S digit words (one 32-bit load per plane) are all
+// Four consecutive digits of one plane in one load (uint8 digits of the INT8 path, uint16 digits of
+// the FP8 path), the first in the low bits.
+template <typename D>
+__device__ __forceinline__ uint64_t load_digits4(const D* p) {
+    if constexpr (sizeof(D) == 1) {
+        return __ldg(reinterpret_cast<const uint32_t*>(p));
+    } else {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+        return ((uint64_t)v.y << 32) | v.x;
+    }
+}
+
+// One thread = 4 consecutive columns of one row: the S digit words (one load per plane) are all
 // requested before any is used, so the loads of a thread overlap instead of waiting one by one; then
-// X = sum_s k_s (M/m_s) column by column; 32 bytes out.
-template <int NW>
-__global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ kp, uint64_t mp, uint64_t np,
+// X = sum_s k_s (M/m_s) column by column (k_s < 2^12, so each column sum stays below 2^50); 32 bytes out.
+template <int NW, typename D = uint8_t>
+__global__ void __launch_bounds__(256) recon_kernel(const D* __restrict__ kp, uint64_t mp, uint64_t np,
                                                     const int32_t* __restrict__ dA, const int32_t* __restrict__ dB,
                                                     double* __restrict__ c, uint64_t m, uint64_t n, uint64_t ldc,
                                                     const ReconConst rc) {
+    constexpr int BITS = 8 * (int)sizeof(D);
+    constexpr uint64_t MASK = (1ull << BITS) - 1;
     const uint64_t nq = (n + 3) >> 2, total = m * nq, plane = mp * np;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
          t += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t i = t / nq, j0 = (t - i * nq) << 2;
-        const uint8_t* base = kp + i * np + j0;
-        uint32_t kw[OZTT_MAXS];
+        const D* base = kp + i * np + j0;
+        uint64_t kw[OZTT_MAXS];
 #pragma unroll
-        for (int s = 0; s < OZTT_MAXS; ++s)
-            kw[s] = (uint32_t)s < rc.S ? __ldg(reinterpret_cast<const uint32_t*>(base + s * plane)) : 0u;
+        for (int s = 0; s < OZTT_MAXS; ++s) kw[s] = (uint32_t)s < rc.S ? load_digits4<D>(base + s * plane) : 0u;
         uint64_t acc[4][NW];
 #pragma unroll
         for (int e = 0; e < 4; ++e)
@@ -131,7 +144,7 @@ __global__ void __launch_bounds__(256) recon_kernel(const uint8_t* __restrict__ 
             if ((uint32_t)s >= rc.S) break;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const uint32_t k = (kw[s] >> (8 * e)) & 0xFFu;
+                const uint32_t k = (uint32_t)((kw[s] >> (BITS * e)) & MASK);
 #pragma unroll
                 for (int w = 0; w < NW; ++w) acc[e][w] += (uint64_t)k * rc.Q[s][w];
             }
@@ -234,11 +247,9 @@ int big_bits(const Big& a) {
 }
 }  // namespace
 
-void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB,
-                  const oztt_ii_plan& p, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st) {
-    if (p.S < 1 || p.S > OZTT_MAXS) throw Error(OZTT_EINVAL, "recon: bad number of moduli");
-    if (np % 4 || (reinterpret_cast<uintptr_t>(kp) & 3)) throw Error(OZTT_EINVAL, "recon: np must be a multiple of 4");
-    if (m > mp || n > np) throw Error(OZTT_EINVAL, "recon: output larger than the digit planes");
+// Constants of the reconstruction for the moduli of p, the word count nw of X and the limb count nl
+// of the largest M/m_s.
+static ReconConst recon_const(const oztt_ii_plan& p, int& nw, int& nl) {
     ReconConst rc{};
     rc.S = (uint32_t)p.S;
     rc.two_b = 2 * p.b;
@@ -268,7 +279,7 @@ void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA
     // better than the window margin: 32 (NW-3) <= bits(M) - 40 holds for this choice of NW.
     int sbits = 0;
     while ((1 << sbits) < p.S) ++sbits;
-    const int nw = std::max(3, (big_bits(M) + sbits + 31) / 32);
+    nw = std::max(3, (big_bits(M) + sbits + 31) / 32);
     if (nw > 8) throw Error(OZTT_EINVAL, "recon: the product of the moduli is too large");
     if (32 * (nw - 3) > big_bits(M) - 40) throw Error(OZTT_EINVAL, "recon: the moduli product is too small");
     {
@@ -276,14 +287,30 @@ void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA
         for (int w = 7; w >= 0; --w) Ml = Ml * 4294967296.0L + (long double)M.w[w];
         rc.top_scale = (double)(ldexpl(1.0L, 32 * (nw - 3)) / Ml);
     }
-    const uint64_t total = m * ((n + 3) / 4);
-    if (total == 0) return;
+    // limbs needed for the largest M/m_s (below M)
+    nl = std::max(1, (big_bits(M) + kLimbBits - 1) / kLimbBits);
+    return rc;
+}
+
+static unsigned recon_blocks(uint64_t total) {
     int dev = 0, sms = 148;
     OZTT_CUDA(cudaGetDevice(&dev));
     OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sms * 16);
-    // limbs needed for the largest M/m_s (below M)
-    const int nl = std::max(1, (big_bits(M) + kLimbBits - 1) / kLimbBits);
+    return (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sms * 16);
+}
+
+void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB,
+                  const oztt_ii_plan& p, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st) {
+    if (p.S < 1 || p.S > OZTT_MAXS) throw Error(OZTT_EINVAL, "recon: bad number of moduli");
+    if (np % 4 || (reinterpret_cast<uintptr_t>(kp) & 3)) throw Error(OZTT_EINVAL, "recon: np must be a multiple of 4");
+    if (m > mp || n > np) throw Error(OZTT_EINVAL, "recon: output larger than the digit planes");
+    for (int s = 0; s < p.S; ++s)
+        if (p.moduli[s] < 2 || p.moduli[s] > 255) throw Error(OZTT_EINVAL, "recon: uint8 digits need moduli below 256");
+    int nw = 0, nl = 0;
+    const ReconConst rc = recon_const(p, nw, nl);
+    const uint64_t total = m * ((n + 3) / 4);
+    if (total == 0) return;
+    const unsigned blocks = recon_blocks(total);
     const bool fp64 = !(std::getenv("OZTT_RECON_INT") && std::getenv("OZTT_RECON_INT")[0] == '1');
     if (fp64) {
 #define OZTT_RECON_FP64(NW_, NL_) \
@@ -307,6 +334,31 @@ void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA
         case 7: recon_kernel<7><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
         default: recon_kernel<8><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
         }
+    }
+    OZTT_CUDA(cudaGetLastError());
+}
+
+// The same reconstruction from uint16 CRT digits (the FP8 path's moduli reach 2401), on the integer
+// pipe: k_s < 2^12 times a 32-bit word of M/m_s, summed over at most 24 moduli, stays below 2^50.
+void launch_recon_u16(const uint16_t* kp, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB,
+                      const oztt_ii_plan& p, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st) {
+    if (p.S < 1 || p.S > OZTT_MAXS) throw Error(OZTT_EINVAL, "recon: bad number of moduli");
+    if (np % 4 || (reinterpret_cast<uintptr_t>(kp) & 7)) throw Error(OZTT_EINVAL, "recon: np must be a multiple of 4");
+    if (m > mp || n > np) throw Error(OZTT_EINVAL, "recon: output larger than the digit planes");
+    for (int s = 0; s < p.S; ++s)
+        if (p.moduli[s] < 2 || p.moduli[s] > 4096) throw Error(OZTT_EINVAL, "recon: moduli must be in 2..4096");
+    int nw = 0, nl = 0;
+    const ReconConst rc = recon_const(p, nw, nl);
+    const uint64_t total = m * ((n + 3) / 4);
+    if (total == 0) return;
+    const unsigned blocks = recon_blocks(total);
+    switch (nw) {
+    case 3: recon_kernel<3, uint16_t><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+    case 4: recon_kernel<4, uint16_t><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+    case 5: recon_kernel<5, uint16_t><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+    case 6: recon_kernel<6, uint16_t><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+    case 7: recon_kernel<7, uint16_t><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
+    default: recon_kernel<8, uint16_t><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
     }
     OZTT_CUDA(cudaGetLastError());
 }

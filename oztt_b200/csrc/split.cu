@@ -24,6 +24,12 @@
 // Layout in HBM: A is read row-major (m x k, lda) and written as S planes [S][mp][kp] int8 (K
 // contiguous). B is read row-major (k x n, ldb) and written transposed, [S][np][kp] int8, so that
 // both GEMM operands are K-major for the tensor cores. Padding rows/columns are written as zeros.
+//
+// FP8 digits (the DIG variants): the same residues are then split into the two or three e4m3 digits of
+// their modulus (modslice_digit.cpp:193-226 with sparse_fix.h:52-72) and written as nplane digit planes
+// [nplane][mp][kp] / [nplane][np][kp], plane poff_s + 0 = l, + 1 = h, + 2 = s. Every digit is an integer
+// in [-32, 32] that e4m3 represents exactly; the planes hold it as an int8, the operand type of the
+// tensor-core products (which are then exact in s32 for any K).
 #include <algorithm>
 
 #include "oztt_common.cuh"
@@ -35,6 +41,9 @@ struct SplitConst {
     float nz;  // -0.0, the run-time addend of the packed multiplies (mul2 in oztt_common.cuh)
     float m[OZTT_MAXS], rinv[OZTT_MAXS];
     float c[4][OZTT_MAXS];
+    // FP8 digits: radix q, fl(1/q) (stages.hpp:222-223), splitting method, first digit plane
+    float q[OZTT_MAXS], qinv[OZTT_MAXS];
+    int32_t mode[OZTT_MAXS], poff[OZTT_MAXS];
 };
 
 // ---- scaling -------------------------------------------------------------------------------
@@ -272,8 +281,88 @@ __device__ __forceinline__ void store_residues(const f32x2 (&dg)[8][ND], const S
     }
 }
 
-// A: one thread = 16 consecutive elements of one row.
+// ---- FP8 digits ------------------------------------------------------------------------------
+// Sparse-digit fix of one element (method (E), sparse_fix.h:52-72): an odd digit of magnitude 17 or
+// more is moved by q into the even integers of e4m3 (l -= sgn(l) q carrying sgn(l) into h; then
+// h -= sgn(h) q, which q^2 = 0 (mod m) allows). Parity is the units bit of |x| + 2^23. Exact.
+__device__ __forceinline__ void sqs_fix(float& l, float& h, float q) {
+    const float al = fabsf(l);
+    if (al > 16.5f && (__float_as_uint(f32_add(al, 8388608.0f)) & 1u)) {
+        if (l < 0.0f) {
+            l = f32_add(l, q);
+            h = f32_sub(h, 1.0f);
+        } else {
+            l = f32_sub(l, q);
+            h = f32_add(h, 1.0f);
+        }
+    }
+    const float ah = fabsf(h);
+    if (ah > 16.5f && (__float_as_uint(f32_add(ah, 8388608.0f)) & 1u)) h = h < 0.0f ? f32_add(h, q) : f32_sub(h, q);
+}
+
+// Writes the digit planes of 16 elements (8 pairs x ND digits of A') for every modulus.
+//   rounding to nearest (SQ, WIDE, SQS): h = rint(fl(r * qinv)), l = r - q h (exact); SQS then sqs_fix
+//   Karatsuba (KAR): h = rint((r + sgn(r) (q/2 - 1/2)) * qinv), l = r - q h, s = h + l, sgn(+-0) = +1
+// The products r*qinv are single roundings like the reference's MulS; everything else is exact.
 template <int ND>
+__device__ __forceinline__ void store_digits(const f32x2 (&dg)[8][ND], const SplitConst& sc, int8_t* dst,
+                                             uint64_t plane) {
+    const f32x2 nz = splat2(sc.nz);
+    for (int s = 0; s < sc.S; ++s) {
+        const f32x2 negm = splat2(-sc.m[s]), ri = splat2(sc.rinv[s]);
+        const f32x2 c0 = splat2(sc.c[0][s]), c1 = splat2(sc.c[1][s]), c2 = splat2(sc.c[2][s]),
+                    c3 = splat2(sc.c[3][s]);
+        const float q = sc.q[s];
+        const f32x2 qi = splat2(sc.qinv[s]), negq = splat2(-q);
+        const int mode = sc.mode[s];
+        f32x2 l[8], h[8], t[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const f32x2 r = residue2<ND>(dg[e], negm, ri, c0, c1, c2, c3, nz);
+            if (mode == OZTT_SPLIT_KAR) {
+                float r0, r1;
+                unpk2(r, r0, r1);
+                const float half = q * 0.5f - 0.5f;
+                const f32x2 off = pk2(r0 < 0.0f ? -half : half, r1 < 0.0f ? -half : half);
+                h[e] = rint2(mul2(add2(r, off), qi, nz));
+                l[e] = fma2(h[e], negq, r);
+                t[e] = add2(h[e], l[e]);
+            } else {
+                h[e] = rint2(mul2(r, qi, nz));
+                l[e] = fma2(h[e], negq, r);
+                if (mode == OZTT_SPLIT_SQS) {
+                    float l0, l1, h0, h1;
+                    unpk2(l[e], l0, l1);
+                    unpk2(h[e], h0, h1);
+                    sqs_fix(l0, h0, q);
+                    sqs_fix(l1, h1, q);
+                    l[e] = pk2(l0, l1);
+                    h[e] = pk2(h0, h1);
+                }
+            }
+        }
+        int8_t* p = dst + (uint64_t)sc.poff[s] * plane;
+        *reinterpret_cast<uint4*>(p) =
+            make_uint4(pack4(l[0], l[1]), pack4(l[2], l[3]), pack4(l[4], l[5]), pack4(l[6], l[7]));
+        *reinterpret_cast<uint4*>(p + plane) =
+            make_uint4(pack4(h[0], h[1]), pack4(h[2], h[3]), pack4(h[4], h[5]), pack4(h[6], h[7]));
+        if (mode == OZTT_SPLIT_KAR)
+            *reinterpret_cast<uint4*>(p + 2 * plane) =
+                make_uint4(pack4(t[0], t[1]), pack4(t[2], t[3]), pack4(t[4], t[5]), pack4(t[6], t[7]));
+    }
+}
+
+template <int ND, bool DIG>
+__device__ __forceinline__ void store_planes(const f32x2 (&dg)[8][ND], const SplitConst& sc, int8_t* dst,
+                                             uint64_t plane) {
+    if constexpr (DIG)
+        store_digits<ND>(dg, sc, dst, plane);
+    else
+        store_residues<ND>(dg, sc, dst, plane);
+}
+
+// A: one thread = 16 consecutive elements of one row.
+template <int ND, bool DIG>
 __global__ void __launch_bounds__(256) split_rows_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
                                                          uint64_t lda, const int32_t* __restrict__ delta,
                                                          int8_t* __restrict__ planes, uint64_t mp, uint64_t kp,
@@ -300,13 +389,13 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const double* __restric
         f32x2 dg[8][ND];
 #pragma unroll
         for (int e = 0; e < 8; ++e) make_digits2<ND>(x[2 * e], x[2 * e + 1], d, splat2(sc.nz), dg[e]);
-        store_residues<ND>(dg, sc, planes + row * kp + k0, plane);
+        store_planes<ND, DIG>(dg, sc, planes + row * kp + k0, plane);
     }
 }
 
 // B: a warp covers 16 columns x 32 rows of B; lane l takes column (l & 15) and the 16 rows of half
 // (l >> 4), so lanes l and l+16 write the two halves of one 32-byte sector of the transposed plane.
-template <int ND>
+template <int ND, bool DIG>
 __global__ void __launch_bounds__(256) split_cols_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
                                                          uint64_t ldb, const int32_t* __restrict__ delta,
                                                          int8_t* __restrict__ planes, uint64_t np, uint64_t kp,
@@ -326,7 +415,7 @@ __global__ void __launch_bounds__(256) split_cols_kernel(const double* __restric
         f32x2 dg[8][ND];
 #pragma unroll
         for (int e = 0; e < 8; ++e) make_digits2<ND>(x[2 * e], x[2 * e + 1], d, splat2(sc.nz), dg[e]);
-        store_residues<ND>(dg, sc, planes + col * kp + r0, plane);
+        store_planes<ND, DIG>(dg, sc, planes + col * kp + r0, plane);
     }
 }
 
@@ -378,36 +467,68 @@ void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, in
     OZTT_CUDA(cudaGetLastError());
 }
 
-void launch_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
-                       const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
+template <bool DIG>
+static void split_rows_any(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int nd,
+                           const SplitConst& sc, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
     if (mp % 16 || kp % 16) throw Error(OZTT_EINVAL, "split_rows: padded dimensions must be multiples of 16");
-    const SplitConst sc = split_const(p);
     const uint64_t total = mp * (kp / 16);
     const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)device_sms() * 32);
     if (total == 0) return;
-    switch (p.nd) {
-    case 3: split_rows_kernel<3><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
-    case 4: split_rows_kernel<4><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
-    case 5: split_rows_kernel<5><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
+    switch (nd) {
+    case 3: split_rows_kernel<3, DIG><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
+    case 4: split_rows_kernel<4, DIG><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
+    case 5: split_rows_kernel<5, DIG><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
     default: throw Error(OZTT_EINVAL, "split: the number of digits must be 3, 4 or 5");
     }
     OZTT_CUDA(cudaGetLastError());
 }
 
-void launch_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
-                       const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
+template <bool DIG>
+static void split_cols_any(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta, int nd,
+                           const SplitConst& sc, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
     if (np % 16 || kp % 32) throw Error(OZTT_EINVAL, "split_cols: np must be a multiple of 16 and kp of 32");
-    const SplitConst sc = split_const(p);
     const uint64_t warps = (np / 16) * (kp / 32);
     if (warps == 0) return;
     const unsigned blocks = (unsigned)std::min<uint64_t>((warps + 7) / 8, (uint64_t)device_sms() * 32);
-    switch (p.nd) {
-    case 3: split_cols_kernel<3><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
-    case 4: split_cols_kernel<4><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
-    case 5: split_cols_kernel<5><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
+    switch (nd) {
+    case 3: split_cols_kernel<3, DIG><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
+    case 4: split_cols_kernel<4, DIG><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
+    case 5: split_cols_kernel<5, DIG><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
     default: throw Error(OZTT_EINVAL, "split: the number of digits must be 3, 4 or 5");
     }
     OZTT_CUDA(cudaGetLastError());
+}
+
+void launch_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
+    split_rows_any<false>(a, m, k, lda, delta, p.nd, split_const(p), planes, mp, kp, st);
+}
+
+void launch_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
+    split_cols_any<false>(b, k, n, ldb, delta, p.nd, split_const(p), planes, np, kp, st);
+}
+
+static SplitConst digit_const(const oztt_fp8_plan& fp) {
+    SplitConst sc = split_const(fp.base);
+    for (int s = 0; s < fp.base.S; ++s) {
+        sc.q[s] = (float)fp.q[s];
+        sc.qinv[s] = 1.0f / (float)fp.q[s];
+        sc.mode[s] = fp.mode[s];
+        sc.poff[s] = fp.poff[s];
+    }
+    return sc;
+}
+
+// FP8 digit planes of A ([nplane][mp][kp]) and of B transposed ([nplane][np][kp]).
+void launch_digit_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
+                             const oztt_fp8_plan& fp, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
+    split_rows_any<true>(a, m, k, lda, delta, fp.base.nd, digit_const(fp), planes, mp, kp, st);
+}
+
+void launch_digit_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
+                             const oztt_fp8_plan& fp, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
+    split_cols_any<true>(b, k, n, ldb, delta, fp.base.nd, digit_const(fp), planes, np, kp, st);
 }
 
 }  // namespace oztt

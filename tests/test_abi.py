@@ -16,7 +16,7 @@ ROOT = Path(__file__).resolve().parent.parent
 
 def declared_symbols() -> list[str]:
     text = (ROOT / "include" / "oztt_cuda.h").read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|void|uint64_t)\s+(oztt_[a-z0-9_]+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|void|uint64_t|const char\*)\s+(oztt_[a-z0-9_]+)\s*\(", text, flags=re.M)))
 
 
 def test_library_exports_every_declared_symbol(oztt):
@@ -57,7 +57,7 @@ def test_epilogue_division_magic(oztt):
 
 
 def test_is_available_and_names(oztt):
-    assert oztt.is_available(oztt.Format.INT8)
+    assert oztt.is_available(oztt.Format.INT8) and oztt.is_available(oztt.Format.FP8)
     for f in (oztt.Format.BFP8, oztt.Format.BFP4, oztt.Format.BFP2):
         assert not oztt.is_available(f)
     assert [oztt.format_name(f) for f in oztt.Format] == ["BF16", "FP16", "TF32", "BFP8", "FP8", "INT8", "BFP4",
