@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 
 import oztt_b200 as oztt
+from oracle_lib import pad, round_up
 
 # tools/validated/quick.csv:11 — II FP8, n=128, seed 7, uniform(-1,1), fixed_bits 54, one pass: 12 moduli,
 # 36 digit products.
@@ -58,17 +59,22 @@ def test_plan_uses_every_splitting_method(oracle):
 @pytest.mark.parametrize("m,n,k,phi,seed,passes", [(96, 160, 200, 0.5, 3, 1), (64, 64, 1000, 2.0, 5, 2),
                                                    (130, 70, 64, -1.0, 11, 0)])
 def test_faithful_and_exact_agree(oracle, m, n, k, phi, seed, passes):
-    """The reference's triple-float reconstruction and the exact one give results within a few units in the
-    last place of the exact CRT value (the faithful pass's documented error)."""
+    """The reference's triple-float reconstruction and the exact one agree within the faithful pass's error:
+    2^-65 (one pass) or 2^-90 (two passes) times M 2^-2b 2^(2 shift - dA_i - dB_j), plus 2 ulp."""
     a, b, fp = fp8_case(oracle, m, n, k, phi, seed, reconstruction=passes)
     rc, cf, err = oracle.fp8_emulate(a, b, m, n, k, fp)
     assert rc == 0, err
     rc, ce, err = oracle.fp8_emulate(a, b, m, n, k, fp, exact=True)
     assert rc == 0, err
     hi, lo = oracle.dot2(a, b, m, n, k)
-    scale = np.abs(a.reshape(m, k)) @ np.abs(b.reshape(k, n))
-    err_f = np.abs(cf - ce).reshape(m, n) / np.maximum(scale, 1e-300)
-    assert err_f.max() < 2.0 ** -(fp.base.b + 2) * 64
+    crt = oracle.crt_plan([fp.base.moduli[i] for i in range(fp.base.S)], fp.base.b, fp.base.two_pass)
+    M, N, K = round_up(m, 64), round_up(n, 64), round_up(k, 32)
+    _, dA, _ = oracle.scale(pad(a, m, k, M, K), M, K, 0, crt.shift)
+    _, dB, _ = oracle.scale(pad(b, k, n, K, N), K, N, 1, crt.shift)
+    KM = (crt.W_hi * 2.0 ** 32 + crt.W_lo) * 2.0 ** crt.qw
+    g = 2 * crt.shift - (dA[:m, None] + dB[None, :n])
+    tol = (2.0 ** -90 if crt.two_pass else 2.0 ** -65) * KM * np.exp2(g.astype(np.float64))
+    assert np.all(np.abs(cf - ce).reshape(m, n) <= tol + 2 * np.spacing(np.abs(cf.reshape(m, n))))
     rel, _ = oracle.accuracy(ce, hi, lo)
     assert rel < 1e-15
 
