@@ -3,6 +3,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl oztt|reference]
     python bench.py --scheme I [--slices 0,4,8,12]     (Scheme I INT8, 8192^3, phi=1: one line per p)
+    python bench.py --format FP8 [--moduli 12,16,20,24] [--passes 1,2]
+                                   (Scheme II FP8 digits, 8192 x 8192 x 16384, phi=4: one line per setting)
 
 One step is one pass of the Scheme II INT8 pipeline (scale -> split -> residue GEMM on the tensor
 cores -> exact CRT reconstruction) over one m x n x k problem with FP64 operands already resident in
@@ -55,15 +57,18 @@ def parse_args():
     ap.add_argument("--scheme", choices=["II", "I"], default="II",
                     help="I: the Scheme I INT8 workload (default 8192^3, phi=1.0), one JSON line per slice count")
     ap.add_argument("--slices", default="0", help="Scheme I: comma-separated slice counts, 0 = selected from the input")
+    ap.add_argument("--format", choices=["INT8", "FP8"], default="INT8", help="Scheme II digit format")
+    ap.add_argument("--moduli", default="12,16,20,24", help="FP8: comma-separated max_moduli settings")
+    ap.add_argument("--passes", default="1,2", help="FP8: reconstruction passes to run (1 OnePass, 2 TwoPass)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-accuracy", action="store_true")
     args = ap.parse_args()
     if args.size is None:
-        args.size = DEFAULT_SIZE if args.scheme == "II" else 8192
+        args.size = DEFAULT_SIZE if args.scheme == "II" and args.format == "INT8" else 8192
     if args.phi is None:
-        args.phi = 0.5 if args.scheme == "II" else 1.0
+        args.phi = 4.0 if args.format == "FP8" else (0.5 if args.scheme == "II" else 1.0)
     return args
 
 
@@ -305,6 +310,89 @@ def run_scheme_i(args) -> None:
         print(json.dumps(line), flush=True)
 
 
+def run_fp8(args) -> None:
+    """One step = one pass of the Scheme II FP8 pipeline (scale -> digit split -> digit products on the
+    tensor cores with the composition in the epilogue -> exact CRT reconstruction) with the operands
+    resident in HBM, for each max_moduli and reconstruction setting of the configuration; a setting the
+    planner rejects prints its message instead of a number."""
+    import torch
+
+    import oztt_b200 as oz
+
+    m = n = args.size
+    k = 2 * args.size
+    a, b = oz.eval_inputs(m, n, k, args.phi, args.seed)
+    A = torch.from_numpy(a).cuda()
+    B = torch.from_numpy(b).cuda()
+    C = torch.empty(m * n, dtype=torch.float64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    peaks = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops_sustained"]
+    workload = f"Scheme II FP8 (e4m3 digits) {m}x{n}x{k}, phi={args.phi}"
+    for S_req in [int(x) for x in args.moduli.split(",")]:
+        for passes in [int(x) for x in args.passes.split(",")]:
+            base = {"metric": f"Ozaki-II FP8 effective FP64 TFLOPS at m=n={m}, k={k}", "unit": "TFLOPS",
+                    "n_gpus": 1, "config": {"workload": workload, "max_moduli": S_req, "reconstruction_passes": passes}}
+            t_plan = time.perf_counter()
+            try:
+                plan = oz.fp8_plan_device(A.data_ptr(), B.data_ptr(), m, n, k, max_moduli=S_req,
+                                          reconstruction=passes, stream=stream)
+            except (RuntimeError, ValueError) as exc:
+                print(json.dumps({**base, "value": None, "rejected": str(exc)}), flush=True)
+                continue
+            t_plan = time.perf_counter() - t_plan
+
+            def step():
+                return oz.fp8_run_device(A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, plan, stream, 0,
+                                         timed=True)
+
+            for _ in range(max(args.warmup, 0)):
+                step()
+            stage_sum = [0.0] * 6
+            with ClockSampler(0) as clocks:
+                torch.cuda.synchronize()
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record()
+                for _ in range(args.steps):
+                    stage_sum = [x + y for x, y in zip(stage_sum, step())]
+                ev1.record()
+                torch.cuda.synchronize()
+            ms = ev0.elapsed_time(ev1) / args.steps
+            st = [x / args.steps for x in stage_sum]
+            mp, np_, kp = -(-m // 128) * 128, -(-n // 256) * 256, -(-k // 128) * 128
+            gemm_ops = 2.0 * mp * np_ * kp * plan.nprod
+            gemm_tops = gemm_ops / (st[4] * 1e-3) / 1e12
+            line = {**base, "value": 2.0 * m * n * k / (ms * 1e-3) / 1e12, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "f64 (int8-held e4m3 digit products, s32 accumulate)",
+                    "data": f"synthetic: evaluation/numerics.hpp generator, phi={args.phi}, mt19937 seed {args.seed}",
+                    "config": {**base["config"], "moduli": plan.base.S, "integer_bits": plan.base.b,
+                               "passes_planned": 2 if plan.base.two_pass else 1, "digit_planes": plan.nplane,
+                               "digit_products": plan.nprod, "gemm_outputs": plan.nout,
+                               "planning_s": round(t_plan, 3), "planning": "device-measured statistics",
+                               "l2": "inputs larger than the 126 MB L2; no flush"},
+                    "stage_ms": {"scale_rows": st[0], "scale_cols": st[1], "split_rows": st[2], "split_cols": st[3],
+                                 "digit_gemm": st[4], "recon": st[5]},
+                    "roofline": {"bound": "tensor", "kernel": "residue_gemm_kernel<3> (tcgen05 kind::i8, digit outputs, "
+                                                              "composition in the epilogue)",
+                                 "achieved": gemm_tops, "peak": int8_peak, "unit": "TOP/s (int8)",
+                                 "frac": gemm_tops / int8_peak,
+                                 "peak_source": f"2 x bf16_tflops_sustained of MEASURED_PEAKS.json ({peaks['source']})",
+                                 "algorithmic": f"2*mp*np*kp*nprod = {gemm_ops:.4g} int8 ops per launch"},
+                    "gpu_launches": 7 * args.steps, "clocks": clocks.summary()}
+            if not args.no_accuracy:
+                sys.path.insert(0, str(ROOT / "tests"))
+                try:
+                    from oracle_lib import Oracle  # checker only
+
+                    rows = np.linspace(0, m - 1, 4).astype(np.uint64)
+                    line["max_rel_err"] = Oracle().maxrel_f128(a, b, C.cpu().numpy(), m, n, k, rows=rows)
+                    line["accuracy_sample"] = "4 rows of C (all columns) vs a binary128 reference"
+                except Exception as exc:  # noqa: BLE001
+                    line["accuracy_error"] = str(exc)
+            print(json.dumps(line), flush=True)
+
+
 # ---- the GPU arm --------------------------------------------------------------------------------------
 def grid_shape(world: int) -> tuple[int, int]:
     p = int(math.sqrt(world))
@@ -320,6 +408,9 @@ def main() -> None:
         return
     if args.scheme == "I":
         run_scheme_i(args)
+        return
+    if args.format == "FP8":
+        run_fp8(args)
         return
     import torch
     import torch.distributed as dist

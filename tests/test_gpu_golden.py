@@ -1,12 +1,13 @@
 """The B200 integer stages against the reference device's published outputs at n = 3520 and 7040
-(tools/validated/all.csv:12-13, 28-29).
+(tools/validated/all.csv:11-13, 27-29).
 
 The scaling, splitting/slicing and the tensor-core products run on the GPU through the C ABI; the
 int32 products are then reconstructed on the host by the oracle's restatement of the reference's own
 (triple-float) reconstruction. Matching the published FNV hash means every output bit equals the
 reference device's, so the GPU's residues/slices and products are the reference's at full size.
 Inputs: the evaluator's table suite (mt19937 seed 7, uniform(-1, 1)); Scheme II INT8 with max_moduli
-16, one pass, b = 54; Scheme I INT8 with 8 slices.
+16, one pass, b = 54; Scheme I INT8 with 8 slices; Scheme II FP8 (e4m3 digits) with b = 54, one pass (the
+digit products are composed on the host by the oracle's restatement of compose.cpp).
 """
 
 import numpy as np
@@ -88,3 +89,39 @@ def test_scheme_i_published(oztt, oracle, cuda, n):
     da[:n], db[:n] = dA.cpu().numpy(), dB.cpu().numpy()
     c = oracle.i_recon(host.reshape(-1), p, M, M, da, db, exact=False).reshape(M, M)[:n, :n]
     assert oracle.output_hash(np.ascontiguousarray(c).reshape(-1)) == PUBLISHED[n]["I"]
+
+
+# Scheme II FP8 (tools/validated/all.csv:11, 27): b = 54, one pass, 12 moduli, 36 digit products.
+PUBLISHED_FP8 = {3520: "8c7baeb1b4d34af6", 7040: "2df6cc30b675bba7"}
+
+
+@pytest.mark.parametrize("n", [3520, 7040])
+def test_scheme_ii_fp8_published(oztt, oracle, cuda, n):
+    """GPU scaling, digit split and digit products (raw int32 outputs); the reference's composition
+    (compose.cpp) and triple-float reconstruction restated on the host must give the published bits."""
+    a, b = oracle.gen_inputs(n, n, n, -1.0, 7)
+    fp = oztt.fp8_plan(a, b, n, n, n, reconstruction=1, fixed_bits=54)
+    assert fp.base.S == 12 and fp.nprod == 36
+    crt = oracle.crt_plan([fp.base.moduli[i] for i in range(fp.base.S)], fp.base.b, fp.base.two_pass)
+    M = round_up(n, 64)
+    mp, np_, kp = round_up(n, 128), round_up(n, 256), round_up(n, 128)
+    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    dA, dB = scale(oztt, A, n, n, 0, fp.base.shift), scale(oztt, B, n, n, 1, fp.base.shift)
+    da_ = torch.zeros(fp.nplane * mp * kp, dtype=torch.int8, device="cuda")
+    db_ = torch.zeros(fp.nplane * np_ * kp, dtype=torch.int8, device="cuda")
+    oztt.call("oztt_ii_fp8_split_rows", A.data_ptr(), n, n, n, dA.data_ptr(), fp, da_.data_ptr(), mp, kp, stream())
+    oztt.call("oztt_ii_fp8_split_cols", B.data_ptr(), n, n, n, dB.data_ptr(), fp, db_.data_ptr(), np_, kp, stream())
+    del A, B
+    P = torch.empty(fp.nout * mp * np_, dtype=torch.int32, device="cuda")
+    oztt.call("oztt_ii_fp8_digit_gemm", da_.data_ptr(), db_.data_ptr(), mp, np_, kp, fp, 0, P.data_ptr(), stream())
+    torch.cuda.synchronize()
+    del da_, db_
+    host = np.ascontiguousarray(P.view(fp.nout, mp, np_)[:, :M, :M].cpu().numpy())
+    del P
+    r = oracle.fp8_compose(host.reshape(-1), fp, crt, M, M)
+    del host
+    da = np.zeros(M, dtype=np.int32)
+    db = np.zeros(M, dtype=np.int32)
+    da[:n], db[:n] = dA.cpu().numpy(), dB.cpu().numpy()
+    c = oracle.recon_residue(r, M, M, da, db, crt).reshape(M, M)[:n, :n]
+    assert oracle.output_hash(np.ascontiguousarray(c).reshape(-1)) == PUBLISHED_FP8[n]
