@@ -2,7 +2,8 @@
 """Benchmark: Ozaki-II INT8 effective FP64 TFLOPS on B200 (the metric of BASELINE.json).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl oztt|reference]
-    python bench.py --scheme I [--slices 0,4,8,12]     (Scheme I INT8, 8192^3, phi=1: one line per p)
+    python bench.py --scheme I [--slices 0,4,8,12] [--format FP8]
+                                   (Scheme I INT8 or FP8, 8192^3, phi=1: one line per p)
     python bench.py --format FP8 [--moduli 12,16,20,24] [--passes 1,2]
                                    (Scheme II FP8 digits, 8192 x 8192 x 16384, phi=4: one line per setting)
 
@@ -57,7 +58,7 @@ def parse_args():
     ap.add_argument("--scheme", choices=["II", "I"], default="II",
                     help="I: the Scheme I INT8 workload (default 8192^3, phi=1.0), one JSON line per slice count")
     ap.add_argument("--slices", default="0", help="Scheme I: comma-separated slice counts, 0 = selected from the input")
-    ap.add_argument("--format", choices=["INT8", "FP8"], default="INT8", help="Scheme II digit format")
+    ap.add_argument("--format", choices=["INT8", "FP8"], default="INT8", help="digit format (both schemes)")
     ap.add_argument("--moduli", default="12,16,20,24", help="FP8: comma-separated max_moduli settings")
     ap.add_argument("--passes", default="1,2", help="FP8: reconstruction passes to run (1 OnePass, 2 TwoPass)")
     ap.add_argument("--seed", type=int, default=0)
@@ -68,7 +69,7 @@ def parse_args():
     if args.size is None:
         args.size = DEFAULT_SIZE if args.scheme == "II" and args.format == "INT8" else 8192
     if args.phi is None:
-        args.phi = 4.0 if args.format == "FP8" else (0.5 if args.scheme == "II" else 1.0)
+        args.phi = 1.0 if args.scheme == "I" else (4.0 if args.format == "FP8" else 0.5)
     return args
 
 
@@ -263,9 +264,10 @@ def run_scheme_i(args) -> None:
     C = torch.empty(m * n, dtype=torch.float64, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
     peaks = measured_peaks()
+    fmt = oz.Format.FP8 if args.format == "FP8" else oz.Format.INT8
     for req in [int(x) for x in args.slices.split(",")]:
         t_plan = time.perf_counter()
-        plan = oz.i_int8_plan(a, b, m, n, k, slices=req)
+        plan = oz.i_int8_plan(a, b, m, n, k, slices=req, fmt=fmt)
         t_plan = time.perf_counter() - t_plan
         p = plan.p
 
@@ -290,12 +292,13 @@ def run_scheme_i(args) -> None:
         gemm_ops = 2.0 * m * n * k * pairs
         gemm_tops = gemm_ops / (st[3] * 1e-3) / 1e12
         int8_peak = 2.0 * peaks["bf16_tflops"]
-        line = {"metric": f"Ozaki-I INT8 effective FP64 TFLOPS at m=n=k={m}", "value": 2.0 * m * n * k / (ms * 1e-3) / 1e12,
+        line = {"metric": f"Ozaki-I {args.format} effective FP64 TFLOPS at m=n=k={m}",
+                "value": 2.0 * m * n * k / (ms * 1e-3) / 1e12,
                 "unit": "TFLOPS", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f64 (int8 slice products, s32 accumulate)",
+                "dtype": "f64 (int8-held slice products, s32 accumulate)",
                 "data": f"synthetic: evaluation/numerics.hpp generator, phi={args.phi}, mt19937 seed {args.seed}",
-                "config": {"workload": f"Scheme I INT8 {m}x{n}x{k}", "slices": p,
+                "config": {"workload": f"Scheme I {args.format} {m}x{n}x{k}", "slices": p, "radix": plan.radix,
                            "slices_selected_from_input": bool(plan.auto_p), "slice_pair_products": pairs,
                            "planning_s_host": round(t_plan, 3),
                            "l2": "inputs larger than the 126 MB L2; no flush"},

@@ -155,12 +155,16 @@ int oztt_ii_fp8_recon(const uint16_t* k_digits, uint64_t mp, uint64_t np, const 
                       const int32_t* delta_b, const oztt_fp8_plan* plan, double* c, uint64_t m, uint64_t n,
                       uint64_t ldc, void* stream, char* err, size_t errlen);
 
-/* Plan of one Scheme I INT8 call (src/ozaki1.cpp:192-210): the number of slices p (radix 254, digits
- * +-127, target 2^-1), the last diagonal L = p-1 kept. */
+/* Plan of one Scheme I call (src/ozaki1.cpp:192-210): the number of slices p, the last diagonal L = p-1
+ * kept, and the format's slicing (src/backend/ozaki1/param.hpp:47-50): INT8 radix 254, digits +-127; FP8
+ * radix 32, digits +-16; both normalised to 2^-1. */
 typedef struct oztt_i_plan {
     uint32_t M, N, K;  /* planning dimensions: m, n rounded up to 64, k to 32 */
     int32_t p;         /* number of slices (Info::slices) */
     int32_t auto_p;    /* 1 if p was chosen from the input (oz_fp64_p), 0 if requested */
+    int32_t format;    /* OZTT_FMT_INT8 or OZTT_FMT_FP8 */
+    int32_t radix;     /* 254 or 32 */
+    int32_t dmax;      /* 127 or 16 */
 } oztt_i_plan;
 
 /* ---- whole calls ---------------------------------------------------------------------------- */
@@ -173,7 +177,7 @@ int oztt_gemm(int device_id, const double* a, uint64_t a_len, const double* b, u
               size_t errlen);
 
 /* ozTTgemm::is_available / format_name (src/dispatch.cpp:18-50) for an OZTT_FMT_* value: 1 for the formats
- * this build provides (INT8; FP8 for scheme II), 0 otherwise; the name, or "unknown". */
+ * this build provides (INT8, FP8), 0 otherwise; the name, or "unknown". */
 int oztt_is_available(int32_t format);
 const char* oztt_format_name(int32_t format);
 
@@ -204,6 +208,10 @@ int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* 
  * reference would throw (K blocking needed, Horner exponent budget exceeded). */
 int oztt_i_int8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
                      oztt_i_plan* plan, char* err, size_t errlen);
+/* Scheme I FP8 plan (the same with the FP8 constants: K blocking allowed, the pair loop folding the FP32
+ * partial products into Int32, ozaki1/plan.hpp:141-226). */
+int oztt_i_fp8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
+                    oztt_i_plan* plan, char* err, size_t errlen);
 /* Scheme II INT8 plan for operands already on the device (a: m x k, b: k x n, row-major): the input
  * statistics of the precision policy are measured by kernels on `stream` (bit-identical to the host
  * measurement of oztt_ii_int8_plan), the decisions made on the host. Synchronises `stream`. */
@@ -233,7 +241,8 @@ void oztt_policy_vectors(uint32_t N, double* out);
 int oztt_ii_int8_plan_from_stats(uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction,
                                  int32_t fixed_bits, double TA, double TB, double nA, double nB, double nC,
                                  oztt_ii_plan* plan, char* err, size_t errlen);
-/* The Scheme I INT8 pipeline on host buffers (ozaki1_int8::run, src/ozaki1.cpp:192-282). */
+/* The Scheme I pipeline on host buffers (ozaki1_int8::run and its FP8 counterpart, src/ozaki1.cpp:192-282),
+ * in the plan's format. */
 int oztt_i_int8_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
                     const oztt_i_plan* plan, char* err, size_t errlen);
 /* The same on device buffers (lda = k, ldb = n, ldc = n); synchronises `stream`. stage_ms (NULL or 5
@@ -301,21 +310,31 @@ void oztt_eval_inputs(double* a, double* b, uint64_t m, uint64_t n, uint64_t k, 
 /* Hash of the output bit patterns (evaluation/numerics.hpp:46-57). */
 uint64_t oztt_eval_output_hash(const double* c, uint64_t count);
 
-/* Scheme I slices (slice_tf_sm8.cpp): p radix-254 digits in [-127, 127] of x * 2^delta per element;
- * rows: A (m x k) -> [p][mp][kp]; cols: B (k x n) -> [p][np][kp] (transposed). Deltas from
- * oztt_ii_scale_rows/cols with shift -1. */
+/* Scheme I scaling (scale_f64_reader.cpp + expdelta.cpp with OZ1_NSHIFT = -1): delta = -1 - ceil(log2 u)
+ * of the BF16 u of each row maximum of A (rows) / column maximum of B (cols), rounded up for INT8 and
+ * truncated for FP8 (OZ1_CEIL_MODE, ozaki1/format.hpp:79-97); flags as oztt_ii_scale_rows. */
+int oztt_i_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t format, int32_t* delta,
+                      uint32_t* flags, void* stream, char* err, size_t errlen);
+int oztt_i_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t format, int32_t* delta,
+                      uint32_t* flags, void* stream, char* err, size_t errlen);
+/* Scheme I slices (slice_tf_sm8.cpp / slice_tf_num.cpp): p digits of x * 2^delta per element in the
+ * format's radix (INT8: 254, digits in [-127, 127]; FP8: 32, digits in [-16, 16], each an integer e4m3
+ * holds, stored as int8); rows: A (m x k) -> [p][mp][kp]; cols: B (k x n) -> [p][np][kp] (transposed). */
 int oztt_i_slice_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int32_t p,
-                      int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err, size_t errlen);
+                      int32_t format, int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err,
+                      size_t errlen);
 int oztt_i_slice_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta, int32_t p,
-                      int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err, size_t errlen);
+                      int32_t format, int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err,
+                      size_t errlen);
 /* Diagonal products P_d = sum_{i=0..d} A_i B_{d-i}^T (int32 [p][mp][np]) on the tensor cores: the
  * concatenated per-diagonal GEMMs of issue_panel_diagonals (src/backend/ozaki1/stages.hpp). */
 int oztt_i_diag_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp, uint64_t np, uint64_t kp, int32_t p,
                      int32_t* out, void* stream, char* err, size_t errlen);
-/* Scheme I reconstruction (recon_tf_i32in.cpp + recon_f64_writer.cpp): C = sum_d 254^(p-1-d) P_d *
- * 254^-(p+1) * 2^-(dA_i + dB_j), the sum exact, one rounding. */
+/* Scheme I reconstruction (recon_tf_i32in.cpp + recon_f64_writer.cpp): C = sum_d r^(p-1-d) P_d *
+ * r^-(p+1) * 2^-(dA_i + dB_j) with the format's radix r, the sum exact, one rounding. */
 int oztt_i_recon(const int32_t* diag, uint64_t mp, uint64_t np, const int32_t* delta_a, const int32_t* delta_b,
-                 int32_t p, double* c, uint64_t m, uint64_t n, uint64_t ldc, void* stream, char* err, size_t errlen);
+                 int32_t p, int32_t format, double* c, uint64_t m, uint64_t n, uint64_t ldc, void* stream, char* err,
+                 size_t errlen);
 
 /* Number of SMs and compute capability of a device (0 on success). */
 int oztt_device_info(int device_id, int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor);

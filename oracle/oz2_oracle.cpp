@@ -183,8 +183,9 @@ float residue(const float* dg, int nd, float m, float rinv, const float* c) {
     return mod_round(acc, m, rinv);
 }
 
-// |x| of an FP64 pattern (sign cleared) -> BF16 rounded up (oz_absf64_to_bf16<1>, scale_bits.h:33-44).
-uint16_t abs_to_bf16_up(uint64_t mag) {
+// |x| of an FP64 pattern (sign cleared) -> BF16 rounded up (ceil 1) or truncated (ceil 0)
+// (oz_absf64_to_bf16<CEIL>, scale_bits.h:33-44).
+uint16_t abs_to_bf16(uint64_t mag, int ceil) {
     const uint32_t h = (uint32_t)(mag >> 32), l = (uint32_t)mag;
     const int32_t E = (int32_t)((h >> 20) & 0x7FFu);
     if (E == 0x7FF) return 0xFFC0u;
@@ -192,7 +193,7 @@ uint16_t abs_to_bf16_up(uint64_t mag) {
     if (e8 <= 0) return (h | l) ? 0xFF80u : 0u;
     if (e8 >= 255) return 0x7F80u;
     uint32_t v = ((uint32_t)e8 << 7) | ((h >> 13) & 0x7Fu);
-    if ((h & 0x1FFFu) || l) v += 1u;
+    if (ceil == 1 && ((h & 0x1FFFu) || l)) v += 1u;
     return (uint16_t)v;
 }
 // e = ceil(log2 u) of the BF16 maximum with the out-of-range flags (oz_bf16_scale_exp, scale_bits.h:56-63).
@@ -717,6 +718,11 @@ int ozo_plan_ii_int8(const double* a, const double* b, uint32_t M, uint32_t N, u
 
 int ozo_scale(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, int32_t shift,
               uint16_t* bf16_max, int32_t* delta, uint32_t* flags) {
+    return ozo_scale_mode(x, rows, cols, ld, col_mode, shift, 1, bf16_max, delta, flags);
+}
+
+int ozo_scale_mode(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, int32_t shift, int ceil,
+                   uint16_t* bf16_max, int32_t* delta, uint32_t* flags) {
     uint32_t fl = 0;
     const uint64_t nout = col_mode ? cols : rows, nin = col_mode ? rows : cols;
     for (uint64_t o = 0; o < nout; ++o) {
@@ -725,7 +731,7 @@ int ozo_scale(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int co
             const double v = col_mode ? x[i * ld + o] : x[o * ld + i];
             mx = std::max<uint64_t>(mx, d_to_bits(v) & 0x7FFFFFFFFFFFFFFFull);
         }
-        const uint16_t u = abs_to_bf16_up(mx);
+        const uint16_t u = abs_to_bf16(mx, ceil);
         if (bf16_max) bf16_max[o] = u;
         delta[o] = shift - bf16_scale_exp(u, fl);
     }
@@ -1361,26 +1367,36 @@ void tf_mul_r(float& x0, float& x1, float& x2, float r) {
     fast_two_sum(ec, G, x1, x2);
 }
 
-// The p slices of one element (slice_tf_body.h): t *= 254; d = clamp(Rnd(t0), +-127); t0 -= d.
-void make_slices(double x, int32_t d, int p, int8_t* out, uint64_t stride) {
+// Radix and digit bound of a scheme I format (ozaki1/param.hpp:47-50): INT8 254 / 127, FP8 32 / 16.
+struct I1Fmt {
+    float radix, dmax;
+    bool pow2;  // radix multiplication by tfMulP2 (sfpu_tf.h:121-134)
+};
+I1Fmt i1_fmt(int format) { return format == 4 ? I1Fmt{32.0f, 16.0f, true} : I1Fmt{254.0f, 127.0f, false}; }
+
+// The p slices of one element (slice_tf_body.h): t *= radix; d = clamp(Rnd(t0), +-dmax); t0 -= d.
+void make_slices(double x, int32_t d, int p, const I1Fmt& f, int8_t* out, uint64_t stride) {
     float x0, x1, x2;
     tf_load(x, d, x0, x1, x2);
     for (int i = 0; i < p; ++i) {
-        tf_mul_r(x0, x1, x2, 254.0f);
+        if (f.pow2)
+            tf_mul_p2(x0, x1, x2, f.radix);
+        else
+            tf_mul_r(x0, x1, x2, f.radix);
         float dig = frnd(x0);
-        if (dig < -127.0f)
-            dig = -127.0f;
-        else if (dig >= 127.0f)
-            dig = 127.0f;
+        if (dig < -f.dmax)
+            dig = -f.dmax;
+        else if (dig >= f.dmax)
+            dig = f.dmax;
         out[(uint64_t)i * stride] = (int8_t)(int)dig;
         x0 = fsub(x0, dig);
     }
 }
 
-// 64-bit significand and exponent of 254^-(L+2) in long double (recon_scale, ozaki1/plan.hpp:437-465).
-void radix_scale(int L, uint64_t& W, int32_t& q) {
+// 64-bit significand and exponent of radix^-(L+2) in long double (recon_scale, ozaki1/plan.hpp:437-465).
+void radix_scale(int L, float radix, uint64_t& W, int32_t& q) {
     long double w = 1.0L;
-    for (int i = 0; i < L + 2; ++i) w /= 254.0L;
+    for (int i = 0; i < L + 2; ++i) w /= (long double)radix;
     int e;
     const long double f = frexpl(w, &e);
     W = (unsigned long long)ldexpl(f, 64);
@@ -1476,12 +1492,18 @@ extern "C" {
 
 int ozo_i_slice(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, const int32_t* delta, int p,
                 int8_t* planes) {
+    return ozo_i_slice_fmt(x, rows, cols, ld, col_mode, delta, p, 5, planes);
+}
+
+int ozo_i_slice_fmt(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, const int32_t* delta,
+                    int p, int format, int8_t* planes) {
     const uint64_t plane = rows * cols;
+    const I1Fmt f = i1_fmt(format);
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < (int64_t)rows; ++r)
         for (uint64_t c = 0; c < cols; ++c) {
             const uint64_t idx = col_mode ? c * rows + (uint64_t)r : (uint64_t)r * cols + c;
-            make_slices(x[(uint64_t)r * ld + c], col_mode ? delta[c] : delta[r], p, planes + idx, plane);
+            make_slices(x[(uint64_t)r * ld + c], col_mode ? delta[c] : delta[r], p, f, planes + idx, plane);
         }
     return 0;
 }
@@ -1509,7 +1531,7 @@ int ozo_i_recon_faithful(const int32_t* pd, int p, uint64_t M, uint64_t N, const
     const int L = p - 1;
     uint64_t W;
     int32_t qw;
-    radix_scale(L, W, qw);
+    radix_scale(L, 254.0f, W, qw);
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < (int64_t)M; ++i)
         for (uint64_t j = 0; j < N; ++j) {
@@ -1533,20 +1555,71 @@ int ozo_i_recon_faithful(const int32_t* pd, int p, uint64_t M, uint64_t N, const
     return 0;
 }
 
-int ozo_i_recon_exact(const int32_t* pd, int p, uint64_t M, uint64_t N, const int32_t* dA, const int32_t* dB,
-                      double* c, uint64_t ldc) {
+int ozo_i_recon_faithful_deferred(const int32_t* pd, int p, int format, uint64_t K, uint64_t M, uint64_t N,
+                                  const int32_t* dA, const int32_t* dB, double* c, uint64_t ldc) {
+    const I1Fmt f = i1_fmt(format);
     const int L = p - 1;
     uint64_t W;
     int32_t qw;
-    radix_scale(L, W, qw);
+    radix_scale(L, f.radix, W, qw);
+    // recon_nsmall (ozaki1/plan.hpp:428-433): leading diagonals with (d+1) K dmax^2 <= 2^24 are read with
+    // one conversion; the others are split into (v & 0xFFFFFF00) and (v & 0xFF), two's complement
+    // (recon_reader_i32in.cpp:34-35 with SIGNMAG = 0).
+    const uint64_t per = K * (uint64_t)f.dmax * (uint64_t)f.dmax;
+    const int nsingle = per ? (int)std::min<uint64_t>((1ull << 24) / per, (uint64_t)p) : 0;
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < (int64_t)M; ++i)
         for (uint64_t j = 0; j < N; ++j) {
-            // S = sum_d P_d 254^(L-d) by Horner in exact 256-bit two's complement.
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+            for (int d = 0; d < p; ++d) {
+                if (d > 0) {
+                    if (f.pow2)
+                        tf_mul_p2(a0, a1, a2, f.radix);
+                    else
+                        tf_mul_r(a0, a1, a2, f.radix);
+                }
+                const int32_t v = pd[((uint64_t)d * M + (uint64_t)i) * N + j];
+                if (d < nsingle) {
+                    if (d == 0) {
+                        a0 = (float)v;
+                        a1 = a2 = 0.f;
+                    } else {
+                        tf_add(a0, a1, a2, (float)v);
+                    }
+                    continue;
+                }
+                const float vh = (float)(int32_t)((uint32_t)v & 0xFFFFFF00u), vl = (float)((uint32_t)v & 0xFFu);
+                if (d == 0) a0 = a1 = a2 = 0.f;
+                tf_add(a0, a1, a2, vh);
+                tf_add(a0, a1, a2, vl);
+            }
+            c[(uint64_t)i * ldc + j] =
+                assemble_tf(f_to_bits(a0), f_to_bits(a1), f_to_bits(a2), -(dA[i] + dB[j]), W, qw);
+        }
+    return 0;
+}
+
+int ozo_i_recon_exact(const int32_t* pd, int p, uint64_t M, uint64_t N, const int32_t* dA, const int32_t* dB,
+                      double* c, uint64_t ldc) {
+    return ozo_i_recon_exact_fmt(pd, p, 5, M, N, dA, dB, c, ldc);
+}
+
+int ozo_i_recon_exact_fmt(const int32_t* pd, int p, int format, uint64_t M, uint64_t N, const int32_t* dA,
+                          const int32_t* dB, double* c, uint64_t ldc) {
+    const I1Fmt f = i1_fmt(format);
+    const uint32_t radix = (uint32_t)f.radix;
+    const int L = p - 1;
+    uint64_t W;
+    int32_t qw;
+    radix_scale(L, f.radix, W, qw);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)M; ++i)
+        for (uint64_t j = 0; j < N; ++j) {
+            // S = sum_d P_d radix^(L-d) by Horner in exact 256-bit two's complement.
             Big S;
             bool negS = false;
             for (int d = 0; d < p; ++d) {
-                if (d > 0) S = big_mul_small(S, 254u);
+                if (d > 0) S = big_mul_small(S, radix);
                 const int32_t v = pd[((uint64_t)d * M + (uint64_t)i) * N + j];
                 Big t;
                 t.w[0] = (uint32_t)(v < 0 ? -(int64_t)v : v);
@@ -1607,6 +1680,11 @@ int ozo_i_recon_exact(const int32_t* pd, int p, uint64_t M, uint64_t N, const in
 }
 
 int ozo_i_emulate(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k, int p, int exact) {
+    return ozo_i_emulate_fmt(a, b, c, m, n, k, p, 5, exact);
+}
+
+int ozo_i_emulate_fmt(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k, int p,
+                      int format, int exact) {
     auto pad = [](uint64_t v, uint64_t q) { return (v + q - 1) / q * q; };
     const uint64_t M = pad(m, 64), N = pad(n, 64), K = pad(k, 32);
     std::vector<double> ap(M * K, 0.0), bp(K * N, 0.0);
@@ -1614,17 +1692,20 @@ int ozo_i_emulate(const double* a, const double* b, double* c, uint64_t m, uint6
     for (uint64_t i = 0; i < k; ++i) std::copy_n(b + i * n, n, bp.data() + i * N);
     std::vector<int32_t> dA(M), dB(N);
     uint32_t fa = 0, fb = 0;
-    ozo_scale(ap.data(), M, K, K, 0, -1, nullptr, dA.data(), &fa);
-    ozo_scale(bp.data(), K, N, N, 1, -1, nullptr, dB.data(), &fb);
+    const int ceil = format == 4 ? 0 : 1;  // OZ1_CEIL_MODE: FP8 truncates the maxima, INT8 rounds them up
+    ozo_scale_mode(ap.data(), M, K, K, 0, -1, ceil, nullptr, dA.data(), &fa);
+    ozo_scale_mode(bp.data(), K, N, N, 1, -1, ceil, nullptr, dB.data(), &fb);
     if (fa | fb) return 1;
     std::vector<int8_t> sa((uint64_t)p * M * K), sb((uint64_t)p * N * K);
-    ozo_i_slice(ap.data(), M, K, K, 0, dA.data(), p, sa.data());
-    ozo_i_slice(bp.data(), K, N, N, 1, dB.data(), p, sb.data());
+    ozo_i_slice_fmt(ap.data(), M, K, K, 0, dA.data(), p, format, sa.data());
+    ozo_i_slice_fmt(bp.data(), K, N, N, 1, dB.data(), p, format, sb.data());
     std::vector<int32_t> pd((uint64_t)p * M * N);
     if (ozo_i_gemm(sa.data(), sb.data(), p, M, N, K, pd.data())) return 1;
     std::vector<double> cp(M * N);
     if (exact)
-        ozo_i_recon_exact(pd.data(), p, M, N, dA.data(), dB.data(), cp.data(), N);
+        ozo_i_recon_exact_fmt(pd.data(), p, format, M, N, dA.data(), dB.data(), cp.data(), N);
+    else if (format == 4)
+        ozo_i_recon_faithful_deferred(pd.data(), p, format, K, M, N, dA.data(), dB.data(), cp.data(), N);
     else
         ozo_i_recon_faithful(pd.data(), p, M, N, dA.data(), dB.data(), cp.data(), N);
     for (uint64_t i = 0; i < m; ++i) std::copy_n(cp.data() + i * N, n, c + i * n);

@@ -146,6 +146,23 @@ int ozo_i_recon_exact(const int32_t* pd, int p, uint64_t M, uint64_t N, const in
 // Whole scheme I INT8 pipeline with p slices (p > 0) for unpadded inputs (padded like the reference).
 int ozo_i_emulate(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k, int p, int exact);
 
+// The same stages for a scheme I format (format: 5 INT8, 4 FP8; the OZTT_FMT_* values). FP8
+// (ozaki1/param.hpp:50, format.hpp): radix 32 multiplied by tfMulP2 (sfpu_tf.h:121-134), digits
+// clamped to +-16, row/column maxima truncated to BF16 (CEIL mode 0).
+int ozo_scale_mode(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, int32_t shift, int ceil,
+                   uint16_t* bf16_max, int32_t* delta, uint32_t* flags);
+int ozo_i_slice_fmt(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, const int32_t* delta,
+                    int p, int format, int8_t* planes);
+// The reference's deferred reconstruction (the FP formats' Int32 accumulation of the pair loop,
+// ozaki1/plan.hpp:141-226): recon_tf_i32in.cpp with two's complement input, the first recon_nsmall(K)
+// diagonals converted whole, the radix multiplication of the format; then recon_f64_writer.cpp.
+int ozo_i_recon_faithful_deferred(const int32_t* pd, int p, int format, uint64_t K, uint64_t M, uint64_t N,
+                                  const int32_t* dA, const int32_t* dB, double* c, uint64_t ldc);
+int ozo_i_recon_exact_fmt(const int32_t* pd, int p, int format, uint64_t M, uint64_t N, const int32_t* dA,
+                          const int32_t* dB, double* c, uint64_t ldc);
+int ozo_i_emulate_fmt(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k, int p,
+                      int format, int exact);
+
 // ---- Scheme II with FP8 (e4m3) digits (src/backend/ozaki2/kernels/modslice_digit.cpp, compose.cpp,
 // sparse_fix.h; the digit layout comes from an oztt_fp8_plan) ---------------------------------------
 // CRT constants of a moduli set with integer width b (crt_constants of the INT8 path; nothing in them

@@ -131,9 +131,10 @@ class FP8Plan(ctypes.Structure):
 
 
 class IPlan(ctypes.Structure):
-    """oztt_i_plan: the slice count of one Scheme I INT8 call."""
+    """oztt_i_plan: the slice count and the format's slicing (radix, digit bound) of one Scheme I call."""
     _fields_ = [("M", ctypes.c_uint32), ("N", ctypes.c_uint32), ("K", ctypes.c_uint32), ("p", ctypes.c_int32),
-                ("auto_p", ctypes.c_int32)]
+                ("auto_p", ctypes.c_int32), ("format", ctypes.c_int32), ("radix", ctypes.c_int32),
+                ("dmax", ctypes.c_int32)]
 
 
 _P = ctypes.c_void_p
@@ -183,10 +184,13 @@ _SIGNATURES = {
     "oztt_i_int8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _P, _P, _ERR, _SZ],
-    "oztt_i_slice_rows": [_P, _U64, _U64, _U64, _P, _I32, _P, _U64, _U64, _P, _ERR, _SZ],
-    "oztt_i_slice_cols": [_P, _U64, _U64, _U64, _P, _I32, _P, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_i_fp8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _ERR, _SZ],
+    "oztt_i_scale_rows": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _ERR, _SZ],
+    "oztt_i_scale_cols": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _ERR, _SZ],
+    "oztt_i_slice_rows": [_P, _U64, _U64, _U64, _P, _I32, _I32, _P, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_i_slice_cols": [_P, _U64, _U64, _U64, _P, _I32, _I32, _P, _U64, _U64, _P, _ERR, _SZ],
     "oztt_i_diag_gemm": [_P, _P, _U64, _U64, _U64, _I32, _P, _P, _ERR, _SZ],
-    "oztt_i_recon": [_P, _U64, _U64, _P, _P, _I32, _P, _U64, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_i_recon": [_P, _U64, _U64, _P, _P, _I32, _I32, _P, _U64, _U64, _U64, _P, _ERR, _SZ],
     "oztt_is_available": [_I32],
     "oztt_format_name": [_I32],
     "oztt_test_udiv_small": [ctypes.c_uint32, ctypes.c_uint32],
@@ -434,14 +438,16 @@ def fp8_run_device(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, p
     return list(ms) if timed else None
 
 
-def i_int8_plan(a, b, m: int, n: int, k: int, slices: int = 0) -> IPlan:
-    """Scheme I INT8 plan (oztt_i_int8_plan): slices > 0 fixes p, 0 selects it from the input."""
+def i_int8_plan(a, b, m: int, n: int, k: int, slices: int = 0, fmt=None) -> IPlan:
+    """Scheme I plan (oztt_i_int8_plan, or oztt_i_fp8_plan for fmt=Format.FP8): slices > 0 fixes p, 0
+    selects it from the input."""
     av, bv = _as_f64(a, "a"), _as_f64(b, "b")
     if av.size != m * k or bv.size != k * n:
         raise ValueError("matrix span sizes do not match m, n, k")
     plan = IPlan()
     err = _errbuf()
-    rc = _lib().oztt_i_int8_plan(av.ctypes.data, bv.ctypes.data, m, n, k, slices, ctypes.byref(plan), err, len(err))
+    fn = _lib().oztt_i_fp8_plan if fmt is not None and int(fmt) == Format.FP8 else _lib().oztt_i_int8_plan
+    rc = fn(av.ctypes.data, bv.ctypes.data, m, n, k, slices, ctypes.byref(plan), err, len(err))
     if rc != OK:
         _raise(rc, err.value)
     return plan

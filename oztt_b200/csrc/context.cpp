@@ -9,7 +9,7 @@
 //   * one process-wide mutex serialises the calls of all contexts (:19, :152);
 //   * the device is opened on the first valid call; Info reports the padded dimensions (:176-180);
 //   * all input is consumed before C is written, so C may overlap A or B.
-// Dispatch (src/dispatch.cpp:18-50): INT8 (schemes I and II) and FP8 (scheme II, e4m3 digits) are built;
+// Dispatch (src/dispatch.cpp:18-50): INT8 and FP8 (e4m3 digits) are built, both schemes;
 // the Tenstorrent block formats BFP8/BFP4/BFP2 are not available on this hardware, and BF16, FP16 and
 // TF32 are not built yet.
 #include <ozTTgemm/ozTTgemm.hpp>
@@ -169,9 +169,7 @@ Context::~Context() = default;
 Info Context::Impl::execute(std::span<const double> a, std::span<const double> b, std::span<double> c, std::size_t m,
                             std::size_t n, std::size_t k, const Options& opt, const Checked& v) {
     std::lock_guard lock(runtime_mutex);
-    if (opt.format == Format::FP8) {
-        if (opt.scheme == Scheme::I)
-            throw std::runtime_error("Ozaki scheme I with FP8 digits is not built in this version");
+    if (opt.format == Format::FP8 && opt.scheme == Scheme::II) {
         oztt_fp8_plan plan;
         std::string msg;
         const int rc = oztt::run_ii_fp8_planned(options.device_id, a.data(), b.data(), c.data(), m, n, k,
@@ -190,7 +188,8 @@ Info Context::Impl::execute(std::span<const double> a, std::span<const double> b
     if (opt.scheme == Scheme::I) {
         oztt_i_plan plan;
         std::string msg;
-        int rc = oztt::plan_i_int8(a.data(), b.data(), m, n, k, opt.slices, plan, msg);
+        int rc = oztt::plan_i(a.data(), b.data(), m, n, k, opt.slices,
+                              opt.format == Format::FP8 ? oztt::kI1Fp8 : oztt::kI1Int8, plan, msg);
         if (rc != OZTT_OK) rethrow(rc, msg);
         char err[512] = {0};
         rc = oztt_i_int8_run(options.device_id, a.data(), b.data(), c.data(), m, n, k, &plan, err, sizeof err);

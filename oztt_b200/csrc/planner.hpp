@@ -75,8 +75,24 @@ int plan_fp8_with(const std::function<PolicyStats(uint32_t, uint32_t)>& stats, u
 int plan_fp8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
              int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan& p, std::string& err);
 
-// Scheme I INT8 (planner1.cpp): the slice count oz_fp64_p selects for row-major a (m x k), b (k x n)
-// with padded planning dimensions M, N, K; and the whole plan (slices > 0 fixes p).
+// Scheme I format constants (ozaki1/param.hpp, ozaki1/format.hpp): radix, digit bound, normalization
+// target 2^nshift, BF16 rounding of the maxima (1 up, 0 truncate), exact accumulator bits, Int32 partial
+// products.
+struct I1Format {
+    int32_t format;  // OZTT_FMT_*
+    double radix, dmax;
+    int32_t nshift;
+    uint32_t ceil_mode, acc_bits;
+    bool int32_partial;
+};
+inline constexpr I1Format kI1Int8{OZTT_FMT_INT8, 254.0, 127.0, -1, 1u, 31u, true};
+inline constexpr I1Format kI1Fp8{OZTT_FMT_FP8, 32.0, 16.0, -1, 0u, 24u, false};
+// Scheme I (planner1.cpp): the slice count oz_fp64_p selects for row-major a (m x k), b (k x n) with padded
+// planning dimensions M, N, K; and the whole plan (slices > 0 fixes p).
+int select_slices(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,
+                  uint32_t K, const I1Format& f);
+int plan_i(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices, const I1Format& f,
+           oztt_i_plan& p, std::string& err);
 int select_slices_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,
                        uint32_t K);
 int plan_i_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,

@@ -1,19 +1,23 @@
 // SPDX-License-Identifier: Apache-2.0
 //
-// Scheme I INT8 planner (host). Decides what the reference decides before its device pipeline runs:
+// Scheme I planner (host), INT8 and FP8 formats. Decides what the reference decides before its device
+// pipeline runs:
 //   slices p       as requested, or selected from the input (oz_fp64_p and its helpers,
 //                  src/backend/ozaki1/auto_precision.hpp:65-526): the smallest p in a doubling +
 //                  bisection search for which two models of the truncation error stay below 2^-53
 //                  relative: (1) a sum of squares with independent signs over all elements, against
 //                  the Hutchinson estimate of ||C||_F^2, and (2) a simulation of the device result on
 //                  32 + 32 sampled rows and columns (largest norms plus a seeded uniform draw)
-//   feasibility    plan_issue / issue_feasible for the INT8 route (src/backend/ozaki1/plan.hpp:189-218,
-//                  format.hpp:123-175): the concatenated issue with one K block only (K (L+1) 127^2
-//                  <= 2^31 - 1 and <= 2^17), and the FP32 exponent budget of the Horner evaluation
-// The INT8 constants: radix 254, digit bound 127, normalization target 2^-1 with the row/column maxima
-// rounded up to BF16 (ozaki1/format.hpp:32-97). Every floating-point sum keeps the reference's order
-// (independent quantities run in parallel, sums over them run sequentially or in the reference's fixed
-// chunks), so p is the reference's for the same input. Compiled without floating-point contraction.
+//   feasibility    plan_issue / issue_feasible (src/backend/ozaki1/plan.hpp:141-226, format.hpp:98-190):
+//                  a K block length that keeps the accumulation exact for the chosen issue (INT8: the
+//                  concatenated issue with one K block only, K (L+1) 127^2 <= 2^31 - 1), and the FP32
+//                  exponent budget of the Horner evaluation
+// The format constants (ozaki1/param.hpp:47-50, format.hpp:32-97): INT8 radix 254, digits +-127,
+// Int32 partial sums, row/column maxima rounded up to BF16; FP8 radix 32, digits +-16, FP32 partial
+// sums (24 exact bits), maxima truncated to BF16; both normalize to 2^-1. Every floating-point sum keeps
+// the reference's order (independent quantities run in parallel, sums over them run sequentially or in
+// the reference's fixed chunks), so p is the reference's for the same input. Compiled without
+// floating-point contraction.
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -30,17 +34,14 @@
 namespace oztt {
 namespace {
 
-constexpr double kRadix = 254.0;
-constexpr double kDmax = 127.0;
-constexpr int32_t kNshift = -1;
 constexpr uint32_t kSampleTop = 32, kSampleUniform = 32;
 constexpr uint32_t kSeedRows = 20261021u, kSeedCols = 20261022u;
-constexpr uint32_t kAccBits = 31;
 constexpr uint32_t kTileWidth = 32;
 
-// |mx| -> BF16 rounded up, then e = ceil(log2) of it (scale_bits.h:33-63 with CEIL = 1); in_range is
-// false for 0 and for the values the device flags (above BF16, below 2^-126, Inf/NaN).
-int device_exponent(double mx, bool& in_range) {
+// |mx| -> BF16 (rounded up for ceil_mode 1, truncated for 0), then e = ceil(log2) of it
+// (scale_bits.h:33-63); in_range is false for 0 and for the values the device flags (above BF16, below
+// 2^-126, Inf/NaN).
+int device_exponent(double mx, uint32_t ceil_mode, bool& in_range) {
     uint64_t u;
     std::memcpy(&u, &mx, 8);
     const uint32_t h = (uint32_t)(u >> 32) & 0x7FFFFFFFu, l = (uint32_t)u;
@@ -54,7 +55,7 @@ int device_exponent(double mx, bool& in_range) {
         v = 0x7F80u;
     else {
         v = ((uint32_t)(E - 896) << 7) | ((h >> 13) & 0x7Fu);
-        if ((h & 0x1FFFu) || l) v += 1u;
+        if (ceil_mode == 1 && ((h & 0x1FFFu) || l)) v += 1u;
     }
     const uint32_t be = (v >> 7) & 0xFFu, bm = v & 0x7Fu;
     in_range = v != 0 && be != 0xFFu;
@@ -69,15 +70,16 @@ inline void two_sum(double a, double b, double& s, double& e) {
     e = (a - (s - bb)) + (b - bb);
 }
 
-// The radix-254 expansion of one element, advanced by the device slicer's rule: u = 254 t,
-// d = clamp(round-half-even(fl32(u_hi)), +-127), t = u - d, with t held as two doubles.
+// The balanced radix expansion of one element, advanced by the device slicer's rule: u = radix t,
+// d = clamp(round-half-even(fl32(u_hi)), +-dmax), t = u - d, with t held as two doubles.
 struct Expansion {
     double th = 0.0, tl = 0.0;
+    double radix = 254.0, dmax = 127.0;
     double step() {
-        const double ph = kRadix * th, pe = std::fma(kRadix, th, -ph);
+        const double ph = radix * th, pe = std::fma(radix, th, -ph);
         double uh, ul;
-        two_sum(ph, pe + kRadix * tl, uh, ul);
-        const double d = std::min(kDmax, std::max(-kDmax, std::nearbyint((double)(float)uh)));
+        two_sum(ph, pe + radix * tl, uh, ul);
+        const double d = std::min(dmax, std::max(-dmax, std::nearbyint((double)(float)uh)));
         two_sum(uh - d, ul, th, tl);
         return d;
     }
@@ -88,6 +90,13 @@ struct Dims {
     uint64_t m, n, k;  // the real block
     uint32_t M, N, K;  // padded planning dimensions
     int pmax;
+    I1Format f;
+    Expansion expansion() const {
+        Expansion t;
+        t.radix = f.radix;
+        t.dmax = f.dmax;
+        return t;
+    }
 };
 
 struct Normalization {
@@ -115,10 +124,10 @@ Normalization normalize(const double* a, const double* b, const Dims& d) {
                 nr += (v * nm.rgA) * (v * nm.rgA);
             }
             bool ok = false;
-            const int e = device_exponent(mx, ok);
+            const int e = device_exponent(mx, d.f.ceil_mode, ok);
             if (mx > 0 && ok) {
                 nm.eA[i] = e;
-                nm.sA[i] = std::ldexp(nm.rgA, e - kNshift);
+                nm.sA[i] = std::ldexp(nm.rgA, e - d.f.nshift);
             }
             nm.nrA[i] = nr;
         }
@@ -134,10 +143,10 @@ Normalization normalize(const double* a, const double* b, const Dims& d) {
         }
         for (uint64_t c = c0; c < c1; ++c) {
             bool ok = false;
-            const int e = device_exponent(mx[c], ok);
+            const int e = device_exponent(mx[c], d.f.ceil_mode, ok);
             if (mx[c] > 0 && ok) {
                 nm.eB[c] = e;
-                nm.sB[c] = std::ldexp(nm.rgB, e - kNshift);
+                nm.sB[c] = std::ldexp(nm.rgB, e - d.f.nshift);
             }
         }
     });
@@ -161,13 +170,14 @@ std::vector<double> independent_error(const double* a, const double* b, const Di
         bool active[LANES];
         int live = 0;
         for (int l = 0; l < LANES; ++l) {
+            t[l] = d.expansion();
             t[l].th = x[l];
             active[l] = s[l] > 0;
             live += active[l];
         }
         double w = 1.0;
         for (int i = 0; i < pmax && live; ++i) {
-            w /= kRadix;
+            w /= d.f.radix;
             for (int l = 0; l < LANES; ++l) {
                 if (!active[l]) continue;
                 const double dg = t[l].step();
@@ -212,7 +222,8 @@ std::vector<double> independent_error(const double* a, const double* b, const Di
             for (uint64_t c = k0; c < k1; ++c) {
                 const double v = row[c];
                 NA[c] += (v * nm.rgA) * (v * nm.rgA);
-                if (v != 0 && counted) push(bt, std::ldexp(v, kNshift - nm.eA[i]), nm.sA[i], c, SA.data(), RA.data());
+                if (v != 0 && counted)
+                    push(bt, std::ldexp(v, d.f.nshift - nm.eA[i]), nm.sA[i], c, SA.data(), RA.data());
             }
             if (bt.n) flush(bt, SA.data(), RA.data());
         }
@@ -224,7 +235,8 @@ std::vector<double> independent_error(const double* a, const double* b, const Di
                 for (int l = 0; l < nl; ++l) {
                     const double v = b[(c0 + l) * d.n + j];
                     nb[l] += (v * nm.rgB) * (v * nm.rgB);
-                    if (v != 0 && counted) push(bt, std::ldexp(v, kNshift - nm.eB[j]), nm.sB[j], c0 + l, SB.data(), RB.data());
+                    if (v != 0 && counted)
+                        push(bt, std::ldexp(v, d.f.nshift - nm.eB[j]), nm.sB[j], c0 + l, SB.data(), RB.data());
                 }
                 if (bt.n) flush(bt, SB.data(), RB.data());
             }
@@ -277,23 +289,23 @@ struct Sample {
                 double* acc = &part[(size_t)ch * na * nb];
                 for (uint64_t c = k0; c < k1; ++c) {
                     for (size_t s = 0; s < na; ++s) {
-                        Expansion t;
+                        Expansion t = d->expansion();
                         t.th = X[s * kreal + c];
                         double w = 1.0;
                         for (int i = 0; i < q; ++i) {
                             const double dg = t.step();
-                            w /= kRadix;
+                            w /= d->f.radix;
                             D[s * q + i] = dg * w;
                         }
                         RX[s] = t.value() * w;
                     }
                     for (size_t s = 0; s < nb; ++s) {
-                        Expansion t;
+                        Expansion t = d->expansion();
                         t.th = Yk[s] = Y[s * kreal + c];
                         double w = 1.0;
                         for (int r = 1; r <= q; ++r) {
                             (void)t.step();
-                            w /= kRadix;
+                            w /= d->f.radix;
                             RY[s * (q + 1) + r] = t.value() * w;
                         }
                     }
@@ -369,10 +381,10 @@ Sample sample(const double* a, const double* b, const Dims& d, const Normalizati
     sm.Y.assign(nb * K, 0.0);
     for (size_t s = 0; s < na; ++s)
         for (size_t c = 0; c < K; ++c)
-            sm.X[s * K + c] = std::ldexp(a[(size_t)sm.rows[s] * d.k + c], kNshift - nm.eA[sm.rows[s]]);
+            sm.X[s * K + c] = std::ldexp(a[(size_t)sm.rows[s] * d.k + c], d.f.nshift - nm.eA[sm.rows[s]]);
     for (size_t s = 0; s < nb; ++s)
         for (size_t c = 0; c < K; ++c)
-            sm.Y[s * K + c] = std::ldexp(b[c * d.n + sm.cols[s]], kNshift - nm.eB[sm.cols[s]]);
+            sm.Y[s * K + c] = std::ldexp(b[c * d.n + sm.cols[s]], d.f.nshift - nm.eB[sm.cols[s]]);
     // C of the sampled pairs by a compensated dot product (TwoProduct with an FMA, TwoSum).
     sm.Ch.assign(na * nb, 0.0);
     sm.Cl.assign(na * nb, 0.0);
@@ -434,15 +446,15 @@ int search(const std::vector<double>& r1, const Sample& sm, int pmax, double tgt
     return hi;
 }
 
-// K block length of the concatenated issue (ozaki_block_k for 31 accumulator bits and digits 127):
-// K when no blocking is needed, else the largest multiple of 32 dividing K within the budget, 0 if none.
-uint32_t block_k(uint32_t K, int L) {
-    const uint64_t d2 = (uint64_t)kDmax * (uint64_t)kDmax;
+// K block length (ozaki_block_k, ozaki1/format.hpp:134-156) for L+1 slice pairs per accumulation: K
+// when no blocking is needed, else the largest multiple of 32 dividing K within the budget, 0 if none.
+uint32_t block_k(uint32_t K, int L, const I1Format& f) {
+    const uint64_t d2 = (uint64_t)f.dmax * (uint64_t)f.dmax;
     uint32_t pb = 0;
     while ((1ull << pb) < d2) ++pb;
-    if (kAccBits < pb + 1) return 0;
-    uint64_t keff_max = 1ull << (kAccBits - pb);
-    keff_max = std::min<uint64_t>(keff_max, (uint64_t)INT32_MAX / d2);
+    if (f.acc_bits < pb + 1) return 0;
+    uint64_t keff_max = 1ull << (f.acc_bits - pb);
+    if (f.int32_partial) keff_max = std::min<uint64_t>(keff_max, (uint64_t)INT32_MAX / d2);
     const uint64_t kc_max = keff_max / (uint64_t)(L + 1);
     if (kc_max >= (uint64_t)K) return K;
     uint32_t best = 0;
@@ -453,10 +465,10 @@ uint32_t block_k(uint32_t K, int L) {
 
 }  // namespace
 
-int select_slices_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,
-                       uint32_t K) {
-    Dims d{m, n, k, M, N, K, 0};
-    d.pmax = (int)std::ceil(160.0 / std::log2(kRadix)) + 1;
+int select_slices(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,
+                  uint32_t K, const I1Format& f) {
+    Dims d{m, n, k, M, N, K, 0, f};
+    d.pmax = (int)std::ceil(160.0 / std::log2(f.radix)) + 1;
     const Normalization nm = normalize(a, b, d);
     const std::vector<double> err2 = independent_error(a, b, d, nm);
     const double nC = product_norm_estimate(a, b, m, n, k, N, nm.rgA, nm.rgB);
@@ -467,8 +479,13 @@ int select_slices_int8(const double* a, const double* b, uint64_t m, uint64_t n,
     return search(r1, sm, d.pmax, tgt);
 }
 
-int plan_i_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
-                oztt_i_plan& p, std::string& err) {
+int select_slices_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,
+                       uint32_t K) {
+    return select_slices(a, b, m, n, k, M, N, K, kI1Int8);
+}
+
+int plan_i(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices, const I1Format& f,
+           oztt_i_plan& p, std::string& err) {
     auto pad = [](uint64_t v, uint64_t q) { return (v + q - 1) / q * q; };
     std::memset(&p, 0, sizeof p);
     if (!m || !n || !k) {
@@ -487,10 +504,25 @@ int plan_i_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64
     p.N = (uint32_t)pad(n, 64);
     p.K = (uint32_t)pad(k, 32);
     p.auto_p = slices == 0;
-    p.p = slices ? (int32_t)slices : select_slices_int8(a, b, m, n, k, p.M, p.N, p.K);
+    p.format = f.format;
+    p.radix = (int32_t)f.radix;
+    p.dmax = (int32_t)f.dmax;
+    p.p = slices ? (int32_t)slices : select_slices(a, b, m, n, k, p.M, p.N, p.K, f);
     const int L = p.p - 1;
-    const uint32_t kc = block_k(p.K, L);
     char msg[512];
+    // The issue the reference plans (plan_issue, ozaki1/plan.hpp:141-226): the pair loop or the pairwise
+    // issue when the formats' FP32 partial products can be folded into Int32 (not INT8), else the
+    // concatenated issue; each must have a K block length.
+    const uint32_t kc_cat = block_k(p.K, L, f), kc_pw = block_k(p.K, 0, f);
+    const uint64_t keff = (uint64_t)(L + 1) * p.K, d2 = (uint64_t)f.dmax * (uint64_t)f.dmax;
+    const bool defer_ok = d2 != 0 && keff <= (uint64_t)INT32_MAX / d2;
+    const bool fuse_ok = !f.int32_partial && defer_ok;
+    const uint32_t ndiag = (uint32_t)p.p;
+    const uint64_t n_cat = kc_cat ? (uint64_t)ndiag * (p.K / kc_cat) : UINT64_MAX;
+    const uint64_t n_pw = kc_pw ? (uint64_t)ndiag * (ndiag + 1) / 2 * (p.K / kc_pw) : 0;
+    const bool pairloop = fuse_ok && kc_pw && p.K / kc_pw == 1;
+    const bool pairwise = !pairloop && fuse_ok && kc_pw && n_pw < n_cat;
+    const uint32_t kc = (pairloop || pairwise) ? kc_pw : kc_cat;
     if (kc == 0) {
         std::snprintf(msg, sizeof msg,
                       "Ozaki scheme I: the partial products for k=%u with %d slices cannot be accumulated without "
@@ -501,7 +533,7 @@ int plan_i_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64
         return OZTT_ERUNTIME;
     }
     const uint32_t nkb = p.K / kc;
-    if (nkb > 1) {
+    if (f.int32_partial && nkb > 1) {
         std::snprintf(msg, sizeof msg,
                       "Ozaki scheme I with Format::INT8 does not support K blocking, but k=%u with %d slices needs "
                       "%u K blocks of %u columns. Use a smaller k, fewer slices (Options::slices) or another format.",
@@ -509,22 +541,28 @@ int plan_i_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64
         err = msg;
         return OZTT_ERUNTIME;
     }
-    if (!(std::log2((double)p.K) + (double)(L + 1) * std::log2(kRadix) + 12.0 < 128.0)) {
+    if (!(std::log2((double)p.K) + (double)(L + 1) * std::log2(f.radix) + 12.0 < 128.0)) {
         std::snprintf(msg, sizeof msg,
-                      "Ozaki scheme I: the reconstruction would overflow FP32 for k=%u with %d slices (radix 254): "
+                      "Ozaki scheme I: the reconstruction would overflow FP32 for k=%u with %d slices (radix %d): "
                       "log2(k) + slices*log2(radix) + 12 must be below 128. Use fewer slices (Options::slices) or "
                       "a smaller k.",
-                      p.K, p.p);
+                      p.K, p.p, p.radix);
         err = msg;
         return OZTT_ERUNTIME;
     }
     return OZTT_OK;
 }
 
+int plan_i_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
+                oztt_i_plan& p, std::string& err) {
+    return plan_i(a, b, m, n, k, slices, kI1Int8, p, err);
+}
+
 }  // namespace oztt
 
-extern "C" int oztt_i_int8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
-                                uint32_t slices, oztt_i_plan* plan, char* err, size_t errlen) {
+namespace {
+int plan_i_c(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
+             const oztt::I1Format& f, oztt_i_plan* plan, char* err, size_t errlen) {
     std::string msg;
     int rc;
     try {
@@ -532,7 +570,7 @@ extern "C" int oztt_i_int8_plan(const double* a, const double* b, uint64_t m, ui
             msg = "null argument";
             rc = OZTT_EINVAL;
         } else {
-            rc = oztt::plan_i_int8(a, b, m, n, k, slices, *plan, msg);
+            rc = oztt::plan_i(a, b, m, n, k, slices, f, *plan, msg);
         }
     } catch (const std::bad_alloc&) {
         msg = "out of host memory while planning";
@@ -545,4 +583,15 @@ extern "C" int oztt_i_int8_plan(const double* a, const double* b, uint64_t m, ui
         std::snprintf(err, errlen, "%s", rc == OZTT_OK ? "" : msg.c_str());
     }
     return rc;
+}
+}  // namespace
+
+extern "C" int oztt_i_int8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                                uint32_t slices, oztt_i_plan* plan, char* err, size_t errlen) {
+    return plan_i_c(a, b, m, n, k, slices, oztt::kI1Int8, plan, err, errlen);
+}
+
+extern "C" int oztt_i_fp8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                               uint32_t slices, oztt_i_plan* plan, char* err, size_t errlen) {
+    return plan_i_c(a, b, m, n, k, slices, oztt::kI1Fp8, plan, err, errlen);
 }

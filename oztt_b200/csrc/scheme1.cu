@@ -1,20 +1,24 @@
 // SPDX-License-Identifier: Apache-2.0
 //
-// Ozaki scheme I with INT8 slices on sm_100a (reference: src/ozaki1.cpp:192-282).
+// Ozaki scheme I with INT8 or FP8 slices on sm_100a (reference: src/ozaki1.cpp:192-282).
 //
 //   scale        the scheme II scaling kernels with the scheme I target: delta = -1 - e
-//                (OZ1_NSHIFT = -1, rounding the maxima up: ozaki1/format.hpp, CEIL mode 1)
-//   slice        p radix-254 slices per element, digits in [-127, 127]: t *= 254 (Dekker-split
-//                triple-float product, tfMulR of sfpu_tf_proc.h:108-133), d = clamp(rint(t0)),
-//                t0 -= d (slice_tf_body.h). The binary32 operation sequence is the reference's, with
-//                round-to-nearest-even and flush-to-zero, two elements per packed-FP32 instruction,
-//                so the slices are bit-identical. Layout: A [p][mp][kp], B transposed [p][np][kp].
+//                (OZ1_NSHIFT = -1; the maxima rounded up to BF16 for INT8, CEIL mode 1, truncated for
+//                FP8, CEIL mode 0: ozaki1/format.hpp:79-97)
+//   slice        p slices per element: INT8 radix 254, digits in [-127, 127], t *= 254 by the
+//                Dekker-split triple-float product (tfMulR of sfpu_tf_proc.h:108-133); FP8 radix 32,
+//                digits in [-16, 16] (integers e4m3 holds; stored as int8), t *= 32 by tfMulP2
+//                (sfpu_tf_proc.h:160-169); then d = clamp(rint(t0)), t0 -= d (slice_tf_body.h). The
+//                binary32 operation sequence is the reference's, with round-to-nearest-even and
+//                flush-to-zero, two elements per packed-FP32 instruction, so the slices are
+//                bit-identical. Layout: A [p][mp][kp], B transposed [p][np][kp].
 //   diagonals    P_d = sum_{i=0..d} A_i B_{d-i}^T for d = 0..p-1 on the tensor cores (gemm_i8.cu,
 //                mode 2): the concatenated GEMMs of issue_panel_diagonals with K_eff = (d+1) K,
-//                exact in s32 because the planner keeps (L+1) K 127^2 < 2^31.
-//   recon        S = sum_d P_d 254^(L-d) exactly (Horner in 192-bit two's complement), then
-//                C = S * 254^-(L+2) * 2^-(dA_i + dB_j): the top 64 bits of |S| times the 64-bit
-//                significand W of 254^-(L+2) (the reference's long double constant, recon_scale in
+//                exact in s32 because (L+1) K dmax^2 < 2^31 (the planner's condition for INT8; for
+//                FP8 the condition of the reference's Int32 accumulation, checked here)
+//   recon        S = sum_d P_d r^(L-d) exactly (Horner in 192-bit two's complement), then
+//                C = S * r^-(L+2) * 2^-(dA_i + dB_j): the top 64 bits of |S| times the 64-bit
+//                significand W of r^-(L+2) (the reference's long double constant, recon_scale in
 //                ozaki1/plan.hpp:437-465), one round-to-nearest-even, results below 2^-1022 -> +-0.
 //                The reference accumulates S in binary32 triple-float (recon_tf_i32in.cpp) and
 //                assembles in a 64-bit window (assemble_tf_f64); the B200 result is within that
@@ -67,6 +71,20 @@ __device__ __forceinline__ void tf_mul_254(f32x2& x0, f32x2& x1, f32x2& x2, f32x
     x2 = sub2(G, sub2(x1, ec));
 }
 
+// Triple-float times a power-of-two radix (tfMulP2, sfpu_tf_proc.h:160-169): the three products are
+// exact, then TwoSum(x1, x2), TwoSum(x0, s3) and FastTwoSum renormalise.
+__device__ __forceinline__ void tf_mul_p2(f32x2& x0, f32x2& x1, f32x2& x2, f32x2 r, f32x2 nz) {
+    x0 = mul2(x0, r, nz);
+    x1 = mul2(x1, r, nz);
+    x2 = mul2(x2, r, nz);
+    f32x2 s3, e4, s5, e6;
+    two_sum2(x1, x2, s3, e4);
+    two_sum2(x0, s3, s5, e6);
+    x0 = s5;
+    x1 = add2(e6, e4);
+    x2 = sub2(e4, sub2(x1, e6));
+}
+
 // FP64 x*2^d -> triple-float (the split of split.cu, repeated here so that this file stands alone).
 __device__ __forceinline__ void tf_load1(double xv, int32_t d, float& x0, float& x1, float& x2) {
     const uint64_t bits = (uint64_t)__double_as_longlong(xv);
@@ -104,14 +122,19 @@ __device__ __forceinline__ void tf_load1(double xv, int32_t d, float& x0, float&
     x2 = f32_mul(f32_mul(f32_add(__uint_as_float(craw), -8388608.0f), sc), 0.0078125f);
 }
 
-// One slice of two elements: t *= 254, d = clamp(rint(t0), +-127), t0 -= d. |t0| <= 254 here, inside
-// the range of rint2 (the 1.5*2^23 rounding, whose values equal cvt.rni's).
-__device__ __forceinline__ f32x2 next_digit2(f32x2& x0, f32x2& x1, f32x2& x2, f32x2 nz) {
-    tf_mul_254(x0, x1, x2, nz);
+// One slice of two elements: t *= radix (P2: 32 by tfMulP2; else 254 by tfMulR), d = clamp(rint(t0),
+// +-dmax), t0 -= d. |t0| <= radix here, inside the range of rint2 (the 1.5*2^23 rounding, whose values
+// equal cvt.rni's).
+template <bool P2>
+__device__ __forceinline__ f32x2 next_digit2(f32x2& x0, f32x2& x1, f32x2& x2, float dmax, f32x2 nz) {
+    if constexpr (P2)
+        tf_mul_p2(x0, x1, x2, splat2(32.0f), nz);
+    else
+        tf_mul_254(x0, x1, x2, nz);
     float da, db;
     unpk2(rint2(x0), da, db);
-    da = fminf(fmaxf(da, -127.0f), 127.0f);
-    db = fminf(fmaxf(db, -127.0f), 127.0f);
+    da = fminf(fmaxf(da, -dmax), dmax);
+    db = fminf(fmaxf(db, -dmax), dmax);
     const f32x2 d = pk2(da, db);
     x0 = sub2(x0, d);
     return d;
@@ -129,7 +152,8 @@ __device__ __forceinline__ uint32_t pack_digits4(f32x2 d01, f32x2 d23) {
 }
 
 // 16 elements -> p slices of 16 bytes each; element states stay in registers across the slices.
-__device__ __forceinline__ void slice16(const double (&x)[16], int32_t d, int p, float nzf, int8_t* dst,
+template <bool P2>
+__device__ __forceinline__ void slice16(const double (&x)[16], int32_t d, int p, float dmax, float nzf, int8_t* dst,
                                         uint64_t plane) {
     const f32x2 nz = splat2(nzf);
     f32x2 s0[8], s1[8], s2[8];
@@ -145,17 +169,18 @@ __device__ __forceinline__ void slice16(const double (&x)[16], int32_t d, int p,
     for (int i = 0; i < p; ++i) {
         f32x2 dg[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) dg[e] = next_digit2(s0[e], s1[e], s2[e], nz);
+        for (int e = 0; e < 8; ++e) dg[e] = next_digit2<P2>(s0[e], s1[e], s2[e], dmax, nz);
         *reinterpret_cast<uint4*>(dst + (uint64_t)i * plane) =
             make_uint4(pack_digits4(dg[0], dg[1]), pack_digits4(dg[2], dg[3]), pack_digits4(dg[4], dg[5]),
                        pack_digits4(dg[6], dg[7]));
     }
 }
 
+template <bool P2>
 __global__ void __launch_bounds__(256) slice_rows_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
                                                          uint64_t lda, const int32_t* __restrict__ delta, int p,
-                                                         float nz, int8_t* __restrict__ planes, uint64_t mp,
-                                                         uint64_t kp) {
+                                                         float dmax, float nz, int8_t* __restrict__ planes,
+                                                         uint64_t mp, uint64_t kp) {
     const uint64_t chunks = kp >> 4, total = mp * chunks, plane = mp * kp;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
          t += (uint64_t)gridDim.x * blockDim.x) {
@@ -174,14 +199,15 @@ __global__ void __launch_bounds__(256) slice_rows_kernel(const double* __restric
 #pragma unroll
             for (int e = 0; e < 16; ++e) x[e] = (in_row && k0 + e < k) ? __ldg(src + e) : 0.0;
         }
-        slice16(x, in_row ? __ldg(delta + row) : 0, p, nz, planes + row * kp + k0, plane);
+        slice16<P2>(x, in_row ? __ldg(delta + row) : 0, p, dmax, nz, planes + row * kp + k0, plane);
     }
 }
 
+template <bool P2>
 __global__ void __launch_bounds__(256) slice_cols_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
                                                          uint64_t ldb, const int32_t* __restrict__ delta, int p,
-                                                         float nz, int8_t* __restrict__ planes, uint64_t np,
-                                                         uint64_t kp) {
+                                                         float dmax, float nz, int8_t* __restrict__ planes,
+                                                         uint64_t np, uint64_t kp) {
     const int lane = threadIdx.x & 31;
     const uint64_t col_groups = np >> 4, total = col_groups * (kp >> 5), plane = np * kp;
     for (uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total;
@@ -192,17 +218,19 @@ __global__ void __launch_bounds__(256) slice_cols_kernel(const double* __restric
         double x[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) x[e] = (in_col && r0 + e < k) ? __ldg(b + (r0 + e) * ldb + col) : 0.0;
-        slice16(x, in_col ? __ldg(delta + col) : 0, p, nz, planes + col * kp + r0, plane);
+        slice16<P2>(x, in_col ? __ldg(delta + col) : 0, p, dmax, nz, planes + col * kp + r0, plane);
     }
 }
 
 // ---- exact Horner reconstruction ------------------------------------------------------------
-constexpr int HW = 6;  // 192-bit two's complement: |S| < 2^31 * 254^(p-1) < 2^151 for p <= 16
+constexpr int HW = 6;  // 192-bit two's complement: |S| < 2^32 r^(p-1): < 2^152 for r = 254, p <= 16,
+                       // < 2^187 for r = 32, p <= 32
 
 struct HornerConst {
     int32_t p;
-    uint64_t W;   // 64-bit significand of 254^-(L+2)
-    int32_t qw;   // its exponent
+    uint32_t radix;  // 254 or 32
+    uint64_t W;      // 64-bit significand of radix^-(L+2)
+    int32_t qw;      // its exponent
 };
 
 __device__ __forceinline__ double horner_element(const int32_t* pd, uint64_t plane, const HornerConst& hc,
@@ -211,12 +239,12 @@ __device__ __forceinline__ double horner_element(const int32_t* pd, uint64_t pla
 #pragma unroll
     for (int w = 0; w < HW; ++w) s[w] = 0;
     for (int d = 0; d < hc.p; ++d) {
-        // s = s * 254 + P_d  (mod 2^192)
+        // s = s * radix + P_d  (mod 2^192)
         const int32_t v = __ldg(pd + (uint64_t)d * plane);
         uint64_t carry = 0;
 #pragma unroll
         for (int w = 0; w < HW; ++w) {
-            const uint64_t t = (uint64_t)s[w] * 254u + carry;
+            const uint64_t t = (uint64_t)s[w] * hc.radix + carry;
             s[w] = (uint32_t)t;
             carry = t >> 32;
         }
@@ -313,43 +341,68 @@ int sm_count() {
 
 }  // namespace
 
-// 64-bit significand and exponent of 254^-(L+2), from the long double quotient as the reference
-// forms it.
-void scheme1_radix_scale(int p, uint64_t& W, int32_t& qw) {
+// 64-bit significand and exponent of radix^-(L+2), from the long double quotient as the reference
+// forms it (exact for radix 32).
+void scheme1_radix_scale(int p, uint32_t radix, uint64_t& W, int32_t& qw) {
     long double w = 1.0L;
-    for (int i = 0; i < p + 1; ++i) w /= 254.0L;
+    for (int i = 0; i < p + 1; ++i) w /= (long double)radix;
     int e;
     const long double f = frexpl(w, &e);
     W = (unsigned long long)ldexpl(f, 64);
     qw = e - 64;
 }
 
-void launch_slice_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int p,
+// Format constants of the device stages: radix, digit bound, BF16 rounding of the maxima, and the
+// largest p the exact Horner word count allows.
+struct I1Dev {
+    uint32_t radix;
+    float dmax;
+    uint32_t ceil;
+    int pmax;
+};
+I1Dev i1_dev(int format) {
+    if (format == OZTT_FMT_FP8) return {32u, 16.0f, 0u, 32};
+    if (format == OZTT_FMT_INT8) return {254u, 127.0f, 1u, 16};
+    throw Error(OZTT_EINVAL, "scheme I: the format must be INT8 or FP8");
+}
+
+void launch_slice_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int p, int format,
                        int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
+    const I1Dev f = i1_dev(format);
     if (mp % 16 || kp % 16) throw Error(OZTT_EINVAL, "slice_rows: padded dimensions must be multiples of 16");
     const uint64_t total = mp * (kp / 16);
     if (!total) return;
-    slice_rows_kernel<<<(unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 32), 256, 0, st>>>(
-        a, m, k, lda, delta, p, -0.0f, planes, mp, kp);
+    const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 32);
+    if (f.radix == 32u)
+        slice_rows_kernel<true><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, p, f.dmax, -0.0f, planes, mp, kp);
+    else
+        slice_rows_kernel<false><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, p, f.dmax, -0.0f, planes, mp, kp);
     OZTT_CUDA(cudaGetLastError());
 }
 
-void launch_slice_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta, int p,
+void launch_slice_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta, int p, int format,
                        int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
+    const I1Dev f = i1_dev(format);
     if (np % 16 || kp % 32) throw Error(OZTT_EINVAL, "slice_cols: np must be a multiple of 16 and kp of 32");
     const uint64_t warps = (np / 16) * (kp / 32);
     if (!warps) return;
-    slice_cols_kernel<<<(unsigned)std::min<uint64_t>((warps + 7) / 8, (uint64_t)sm_count() * 32), 256, 0, st>>>(
-        b, k, n, ldb, delta, p, -0.0f, planes, np, kp);
+    const unsigned blocks = (unsigned)std::min<uint64_t>((warps + 7) / 8, (uint64_t)sm_count() * 32);
+    if (f.radix == 32u)
+        slice_cols_kernel<true><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, p, f.dmax, -0.0f, planes, np, kp);
+    else
+        slice_cols_kernel<false><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, p, f.dmax, -0.0f, planes, np, kp);
     OZTT_CUDA(cudaGetLastError());
 }
 
 void launch_horner(const int32_t* pd, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB, int p,
-                   double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st) {
-    if (p < 1 || p > 16) throw Error(OZTT_EINVAL, "horner: the number of slices must be 1..16");
+                   int format, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st) {
+    const I1Dev f = i1_dev(format);
+    if (p < 1 || p > f.pmax)
+        throw Error(OZTT_EINVAL, "horner: the number of slices must be 1.." + std::to_string(f.pmax));
     HornerConst hc{};
     hc.p = p;
-    scheme1_radix_scale(p, hc.W, hc.qw);
+    hc.radix = f.radix;
+    scheme1_radix_scale(p, f.radix, hc.W, hc.qw);
     const uint64_t total = m * n;
     if (!total) return;
     horner_kernel<<<(unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 16), 256, 0, st>>>(
@@ -364,16 +417,29 @@ void launch_horner(const int32_t* pd, uint64_t mp, uint64_t np, const int32_t* d
 
 namespace oztt {
 
-void launch_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t shift, int32_t* delta,
-                       uint16_t* bfmax, uint32_t* flags, cudaStream_t st);
-void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
-                       uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax, cudaStream_t st);
+void launch_scale_rows_mode(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t shift, uint32_t ceil,
+                            int32_t* delta, uint16_t* bfmax, uint32_t* flags, cudaStream_t st);
+void launch_scale_cols_mode(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, uint32_t ceil,
+                            int32_t* delta, uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax,
+                            cudaStream_t st);
 void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp, int p,
                       int32_t* out, int* err_word, cudaStream_t st);
 
-void run_i_int8_device(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k, int p,
-                       cudaStream_t st, double* stage_ms) {
-    if (p < 1 || p > 16) throw Error(OZTT_EINVAL, "scheme I: the number of slices must be 1..16 for INT8");
+void run_i_device(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                  const oztt_i_plan& plan, cudaStream_t st, double* stage_ms) {
+    const int p = plan.p, format = plan.format;
+    const I1Dev f = i1_dev(format);
+    if (p < 1 || p > f.pmax)
+        throw Error(OZTT_EINVAL, "scheme I: the number of slices must be 1.." + std::to_string(f.pmax) + " for " +
+                                     (format == OZTT_FMT_FP8 ? "FP8" : "INT8"));
+    if (plan.radix != (int32_t)f.radix || plan.dmax != (int32_t)f.dmax)
+        throw Error(OZTT_EINVAL, "scheme I: the plan's radix and digit bound do not match its format");
+    // The diagonal sums are exact in the s32 accumulators while (L+1) K dmax^2 <= 2^31 - 1 (the planner
+    // guarantees it for INT8; FP8 inputs beyond it would need the reference's FP32 K blocks).
+    const uint64_t d2 = (uint64_t)f.dmax * (uint64_t)f.dmax;
+    if ((uint64_t)p * round_up(k, 32) > (uint64_t)INT32_MAX / d2)
+        throw Error(OZTT_ERUNTIME, "Ozaki scheme I: k*slices is too large for exact 32-bit diagonal sums in this "
+                                   "build (k=" + std::to_string(k) + ", " + std::to_string(p) + " slices)");
     const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
     const uint64_t P = (uint64_t)p;
     DevBuf dA(st, mp * 4), dB(st, np * 4), colmax(st, n * 8), words(st, 16);
@@ -395,16 +461,17 @@ void run_i_int8_device(const double* a, const double* b, double* c, uint64_t m, 
         if (stage_ms) OZTT_CUDA(cudaEventRecord(ev[i], st));
     };
     mark(0);
-    launch_scale_rows(a, m, k, k, -1, dA.as<int32_t>(), nullptr, flags, st);
+    launch_scale_rows_mode(a, m, k, k, -1, f.ceil, dA.as<int32_t>(), nullptr, flags, st);
     mark(1);
-    launch_scale_cols(b, k, n, n, -1, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
+    launch_scale_cols_mode(b, k, n, n, -1, f.ceil, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(),
+                           st);
     mark(2);
-    launch_slice_rows(a, m, k, k, dA.as<int32_t>(), p, sa.as<int8_t>(), mp, kp, st);
-    launch_slice_cols(b, k, n, n, dB.as<int32_t>(), p, sb.as<int8_t>(), np, kp, st);
+    launch_slice_rows(a, m, k, k, dA.as<int32_t>(), p, format, sa.as<int8_t>(), mp, kp, st);
+    launch_slice_cols(b, k, n, n, dB.as<int32_t>(), p, format, sb.as<int8_t>(), np, kp, st);
     mark(3);
     launch_diag_gemm(sa.as<int8_t>(), sb.as<int8_t>(), mp, np, kp, p, pd.as<int32_t>(), gemm_err, st);
     mark(4);
-    launch_horner(pd.as<int32_t>(), mp, np, dA.as<int32_t>(), dB.as<int32_t>(), p, c, m, n, n, st);
+    launch_horner(pd.as<int32_t>(), mp, np, dA.as<int32_t>(), dB.as<int32_t>(), p, format, c, m, n, n, st);
     mark(5);
     uint32_t host_words[2] = {0, 0};
     OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
@@ -418,8 +485,8 @@ void run_i_int8_device(const double* a, const double* b, double* c, uint64_t m, 
     check_flags(host_words[0], (int)host_words[1]);
 }
 
-void run_i_int8_host(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
-                     int p) {
+void run_i_host(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                const oztt_i_plan& plan) {
     open_device(device_id);
     cudaStream_t st;
     OZTT_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
@@ -433,7 +500,7 @@ void run_i_int8_host(int device_id, const double* a, const double* b, double* c,
     DevBuf da(st, m * k * 8), db(st, k * n * 8), dc(st, m * n * 8);
     OZTT_CUDA(cudaMemcpyAsync(da.p, a, m * k * 8, cudaMemcpyHostToDevice, st));
     OZTT_CUDA(cudaMemcpyAsync(db.p, b, k * n * 8, cudaMemcpyHostToDevice, st));
-    run_i_int8_device(da.as<double>(), db.as<double>(), dc.as<double>(), m, n, k, p, st, nullptr);
+    run_i_device(da.as<double>(), db.as<double>(), dc.as<double>(), m, n, k, plan, st, nullptr);
     OZTT_CUDA(cudaMemcpyAsync(c, dc.p, m * n * 8, cudaMemcpyDeviceToHost, st));
     OZTT_CUDA(cudaStreamSynchronize(st));
 }
@@ -450,7 +517,7 @@ int oztt_i_int8_run(int device_id, const double* a, const double* b, double* c, 
     return guarded(err, errlen, [&] {
         if (!a || !b || !c || !plan) throw Error(OZTT_EINVAL, "null argument");
         if (!m || !n || !k) throw Error(OZTT_EINVAL, "matrix dimensions are zero");
-        oztt::run_i_int8_host(device_id, a, b, c, m, n, k, plan->p);
+        oztt::run_i_host(device_id, a, b, c, m, n, k, *plan);
     });
 }
 
@@ -461,25 +528,49 @@ int oztt_i_int8_run_device(int device_id, const double* a, const double* b, doub
         if (!a || !b || !c || !plan) throw Error(OZTT_EINVAL, "null argument");
         if (!m || !n || !k) throw Error(OZTT_EINVAL, "matrix dimensions are zero");
         oztt::open_device(device_id);
-        oztt::run_i_int8_device(a, b, c, m, n, k, plan->p, reinterpret_cast<cudaStream_t>(stream), stage_ms);
+        oztt::run_i_device(a, b, c, m, n, k, *plan, reinterpret_cast<cudaStream_t>(stream), stage_ms);
+    });
+}
+
+int oztt_i_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t format, int32_t* delta,
+                      uint32_t* flags, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!a || !delta || !flags || lda < k) throw Error(OZTT_EINVAL, "i_scale_rows: bad arguments");
+        oztt::launch_scale_rows_mode(a, m, k, lda, -1, oztt::i1_dev(format).ceil, delta, nullptr, flags,
+                                     reinterpret_cast<cudaStream_t>(stream));
+    });
+}
+
+int oztt_i_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t format, int32_t* delta,
+                      uint32_t* flags, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!b || !delta || !flags || ldb < n) throw Error(OZTT_EINVAL, "i_scale_cols: bad arguments");
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        oztt::DevBuf colmax(st, n * 8);
+        oztt::launch_scale_cols_mode(b, k, n, ldb, -1, oztt::i1_dev(format).ceil, delta, nullptr, flags,
+                                     colmax.as<unsigned long long>(), st);
     });
 }
 
 int oztt_i_slice_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int32_t p,
-                      int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err, size_t errlen) {
+                      int32_t format, int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err,
+                      size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!a || !delta || !planes || lda < k || mp < m || kp < k || p < 1 || p > 64)
             throw Error(OZTT_EINVAL, "slice_rows: bad arguments");
-        oztt::launch_slice_rows(a, m, k, lda, delta, p, planes, mp, kp, reinterpret_cast<cudaStream_t>(stream));
+        oztt::launch_slice_rows(a, m, k, lda, delta, p, format, planes, mp, kp,
+                                reinterpret_cast<cudaStream_t>(stream));
     });
 }
 
 int oztt_i_slice_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta, int32_t p,
-                      int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err, size_t errlen) {
+                      int32_t format, int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err,
+                      size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!b || !delta || !planes || ldb < n || np < n || kp < k || p < 1 || p > 64)
             throw Error(OZTT_EINVAL, "slice_cols: bad arguments");
-        oztt::launch_slice_cols(b, k, n, ldb, delta, p, planes, np, kp, reinterpret_cast<cudaStream_t>(stream));
+        oztt::launch_slice_cols(b, k, n, ldb, delta, p, format, planes, np, kp,
+                                reinterpret_cast<cudaStream_t>(stream));
     });
 }
 
@@ -499,11 +590,13 @@ int oztt_i_diag_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp
 }
 
 int oztt_i_recon(const int32_t* diag, uint64_t mp, uint64_t np, const int32_t* delta_a, const int32_t* delta_b,
-                 int32_t p, double* c, uint64_t m, uint64_t n, uint64_t ldc, void* stream, char* err, size_t errlen) {
+                 int32_t p, int32_t format, double* c, uint64_t m, uint64_t n, uint64_t ldc, void* stream, char* err,
+                 size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!diag || !delta_a || !delta_b || !c || ldc < n || m > mp || n > np)
             throw Error(OZTT_EINVAL, "recon: bad arguments");
-        oztt::launch_horner(diag, mp, np, delta_a, delta_b, p, c, m, n, ldc, reinterpret_cast<cudaStream_t>(stream));
+        oztt::launch_horner(diag, mp, np, delta_a, delta_b, p, format, c, m, n, ldc,
+                            reinterpret_cast<cudaStream_t>(stream));
     });
 }
 

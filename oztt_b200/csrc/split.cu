@@ -47,9 +47,10 @@ struct SplitConst {
 };
 
 // ---- scaling -------------------------------------------------------------------------------
-// |x| pattern (sign cleared) -> BF16 rounded up; out-of-range markers 0xFFC0 (Inf/NaN), 0xFF80
-// (nonzero below 2^-126), 0x7F80 (above BF16).
-__device__ __forceinline__ uint32_t bf16_round_up(uint64_t mag) {
+// |x| pattern (sign cleared) -> BF16, rounded up (ceil = 1; Scheme II and Scheme I INT8) or truncated
+// (ceil = 0; Scheme I FP8, whose span 16/31 absorbs the truncation: ozaki1/format.hpp:79-97); out-of-range
+// markers 0xFFC0 (Inf/NaN), 0xFF80 (nonzero below 2^-126), 0x7F80 (above BF16).
+__device__ __forceinline__ uint32_t bf16_of_max(uint64_t mag, uint32_t ceil) {
     const uint32_t h = (uint32_t)(mag >> 32), l = (uint32_t)mag;
     const int32_t E = (int32_t)((h >> 20) & 0x7FFu);
     if (E == 0x7FF) return 0xFFC0u;
@@ -57,7 +58,7 @@ __device__ __forceinline__ uint32_t bf16_round_up(uint64_t mag) {
     if (e8 <= 0) return (h | l) ? 0xFF80u : 0u;
     if (e8 >= 255) return 0x7F80u;
     uint32_t v = ((uint32_t)e8 << 7) | ((h >> 13) & 0x7Fu);
-    if ((h & 0x1FFFu) || l) v += 1u;
+    if (ceil && ((h & 0x1FFFu) || l)) v += 1u;
     return v;
 }
 // e = ceil(log2 u); flags for the markers.
@@ -71,9 +72,9 @@ __device__ __forceinline__ int32_t bf16_ceil_log2(uint32_t u, uint32_t& flags) {
     return (int32_t)E - 127 + (mant ? 1 : 0);
 }
 
-__device__ __forceinline__ void finish_scale(uint64_t mx, int32_t shift, int32_t* delta, uint16_t* bfmax,
-                                             uint32_t* flags, uint64_t idx) {
-    const uint32_t u = bf16_round_up(mx);
+__device__ __forceinline__ void finish_scale(uint64_t mx, int32_t shift, uint32_t ceil, int32_t* delta,
+                                             uint16_t* bfmax, uint32_t* flags, uint64_t idx) {
+    const uint32_t u = bf16_of_max(mx, ceil);
     uint32_t fl = 0;
     const int32_t e = bf16_ceil_log2(u, fl);
     delta[idx] = shift - e;
@@ -85,7 +86,8 @@ __device__ __forceinline__ uint64_t mx64(uint64_t a, uint64_t b) { return a > b 
 
 // One warp per row; 16-byte loads when the row is 16-byte aligned.
 __global__ void __launch_bounds__(256) scale_rows_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
-                                                         uint64_t lda, int32_t shift, int32_t* __restrict__ delta,
+                                                         uint64_t lda, int32_t shift, uint32_t ceil,
+                                                         int32_t* __restrict__ delta,
                                                          uint16_t* __restrict__ bfmax, uint32_t* flags) {
     const int lane = threadIdx.x & 31;
     const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x >> 5);
@@ -113,7 +115,7 @@ __global__ void __launch_bounds__(256) scale_rows_kernel(const double* __restric
         const unsigned long long* pu = reinterpret_cast<const unsigned long long*>(p);
         for (uint64_t j = j0 + lane; j < k; j += 32) mx = mx64(mx, (uint64_t)__ldg(pu + j) & MASK);
         for (int o = 16; o; o >>= 1) mx = mx64(mx, (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)mx, o));
-        if (lane == 0) finish_scale(mx, shift, delta, bfmax, flags, row);
+        if (lane == 0) finish_scale(mx, shift, ceil, delta, bfmax, flags, row);
     }
 }
 
@@ -139,9 +141,10 @@ __global__ void __launch_bounds__(256) col_max_kernel(const double* __restrict__
 }
 
 __global__ void col_finish_kernel(const unsigned long long* __restrict__ colmax, uint64_t n, int32_t shift,
+                                  uint32_t ceil,
                                   int32_t* __restrict__ delta, uint16_t* __restrict__ bfmax, uint32_t* flags) {
     const uint64_t col = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (col < n) finish_scale(colmax[col], shift, delta, bfmax, flags, col);
+    if (col < n) finish_scale(colmax[col], shift, ceil, delta, bfmax, flags, col);
 }
 
 // ---- digits and residues -------------------------------------------------------------------
@@ -439,17 +442,18 @@ static SplitConst split_const(const oztt_ii_plan& p) {
     return sc;
 }
 
-void launch_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t shift, int32_t* delta,
-                       uint16_t* bfmax, uint32_t* flags, cudaStream_t st) {
+void launch_scale_rows_mode(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t shift, uint32_t ceil,
+                            int32_t* delta, uint16_t* bfmax, uint32_t* flags, cudaStream_t st) {
     if (m == 0) return;
     const uint64_t warps_needed = m;
     const uint64_t blocks = std::min<uint64_t>((warps_needed + 7) / 8, (uint64_t)device_sms() * 16);
-    scale_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(a, m, k, lda, shift, delta, bfmax, flags);
+    scale_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(a, m, k, lda, shift, ceil, delta, bfmax, flags);
     OZTT_CUDA(cudaGetLastError());
 }
 
-void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
-                       uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax, cudaStream_t st) {
+void launch_scale_cols_mode(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, uint32_t ceil,
+                            int32_t* delta, uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax,
+                            cudaStream_t st) {
     if (n == 0) return;
     OZTT_CUDA(cudaMemsetAsync(colmax, 0, n * sizeof(unsigned long long), st));
     const uint64_t colblocks = (n + 255) / 256;
@@ -463,8 +467,18 @@ void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, in
                                                                                    colmax);
         OZTT_CUDA(cudaGetLastError());
     }
-    col_finish_kernel<<<(unsigned)colblocks, 256, 0, st>>>(colmax, n, shift, delta, bfmax, flags);
+    col_finish_kernel<<<(unsigned)colblocks, 256, 0, st>>>(colmax, n, shift, ceil, delta, bfmax, flags);
     OZTT_CUDA(cudaGetLastError());
+}
+
+void launch_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t shift, int32_t* delta,
+                       uint16_t* bfmax, uint32_t* flags, cudaStream_t st) {
+    launch_scale_rows_mode(a, m, k, lda, shift, 1u, delta, bfmax, flags, st);
+}
+
+void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
+                       uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax, cudaStream_t st) {
+    launch_scale_cols_mode(b, k, n, ldb, shift, 1u, delta, bfmax, flags, colmax, st);
 }
 
 template <bool DIG>

@@ -45,6 +45,14 @@ def ref_plan1():
 
 
 @pytest.fixture(scope="session")
+def ref_plan1_f8():
+    try:
+        return RefPlan1(fp8=True)
+    except FileNotFoundError:
+        pytest.skip("oracle/_ref was not built on this machine (needs the reference tree)")
+
+
+@pytest.fixture(scope="session")
 def ref_plan_f8():
     try:
         return RefPlanF8()

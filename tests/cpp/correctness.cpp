@@ -154,10 +154,12 @@ double check(ozTTgemm::Context& ctx, const ozTTgemm::Options& o, std::size_t m, 
 int main(int argc, char** argv) {
     try {
         const bool host_only = argc == 2 && std::string(argv[1]) == "--host-only";
+        const ozTTgemm::Format formats[] = {ozTTgemm::Format::BF16, ozTTgemm::Format::FP16, ozTTgemm::Format::TF32,
+                                            ozTTgemm::Format::BFP8, ozTTgemm::Format::FP8,  ozTTgemm::Format::INT8,
+                                            ozTTgemm::Format::BFP4, ozTTgemm::Format::BFP2};
         ozTTgemm::Context ctx;
         ozTTgemm::Format first = ozTTgemm::Format::INT8;
-        for (auto f : {ozTTgemm::Format::BF16, ozTTgemm::Format::FP16, ozTTgemm::Format::TF32, ozTTgemm::Format::BFP8,
-                       ozTTgemm::Format::FP8, ozTTgemm::Format::INT8, ozTTgemm::Format::BFP4, ozTTgemm::Format::BFP2})
+        for (auto f : formats)
             if (ozTTgemm::is_available(f)) {
                 first = f;
                 break;
@@ -167,31 +169,45 @@ int main(int argc, char** argv) {
             std::cout << "input validation passed\n";
             return 0;
         }
-        for (auto scheme : {ozTTgemm::Scheme::I, ozTTgemm::Scheme::II}) {
+        // every available format with both schemes (the reference's tests/correctness.cpp:259-267)
+        for (auto f : formats)
+            if (ozTTgemm::is_available(f))
+                for (auto scheme : {ozTTgemm::Scheme::I, ozTTgemm::Scheme::II}) {
+                    ozTTgemm::Options o;
+                    o.format = f;
+                    o.scheme = scheme;
+                    check(ctx, o, 64, 64, 64, Pattern::Uniform);
+                    check(ctx, o, 3, 5, 7, Pattern::Nonnegative);
+                }
+        for (auto f : formats) {
+            if (!ozTTgemm::is_available(f)) continue;
+            for (auto scheme : {ozTTgemm::Scheme::I, ozTTgemm::Scheme::II}) {
+                ozTTgemm::Options o;
+                o.format = f;
+                o.scheme = scheme;
+                check(ctx, o, 65, 67, 97, Pattern::Scaled);
+                check(ctx, o, 9, 11, 17, Pattern::ZeroA);
+                check(ctx, o, 3, 5, 64, Pattern::Cancellation);
+                check(ctx, o, 3, 5, 7, Pattern::ZeroRowColumn);
+                check(ctx, o, 1, 1, 1, Pattern::Smallest);
+                check(ctx, o, 1, 1, 1, Pattern::Largest);
+            }
+            // the fixed slice counts of the reference's test per format (tests/correctness.cpp:280)
+            const unsigned fixed_slices[] = {10, 10, 10, 10, 12, 8, 16, 59};
             ozTTgemm::Options o;
-            o.format = first;
-            o.scheme = scheme;
+            o.format = f;
+            o.scheme = ozTTgemm::Scheme::I;
+            o.slices = fixed_slices[static_cast<unsigned>(f)];
+            check(ctx, o, 3, 5, 7, Pattern::Uniform);
+            o = {};
+            o.format = f;
+            o.scheme = ozTTgemm::Scheme::II;
+            check(ctx, o, 5056, 64, 32, Pattern::Uniform);
+            o.reconstruction = ozTTgemm::Reconstruction::TwoPass;
             check(ctx, o, 64, 64, 64, Pattern::Uniform);
-            check(ctx, o, 3, 5, 7, Pattern::Nonnegative);
-            check(ctx, o, 65, 67, 97, Pattern::Scaled);
-            check(ctx, o, 9, 11, 17, Pattern::ZeroA);
-            check(ctx, o, 3, 5, 64, Pattern::Cancellation);
-            check(ctx, o, 3, 5, 7, Pattern::ZeroRowColumn);
-            check(ctx, o, 1, 1, 1, Pattern::Smallest);
-            check(ctx, o, 1, 1, 1, Pattern::Largest);
         }
         ozTTgemm::Options o;
         o.format = first;
-        o.scheme = ozTTgemm::Scheme::I;
-        o.slices = 8;  // the fixed slice count of the reference's test for INT8
-        check(ctx, o, 3, 5, 7, Pattern::Uniform);
-        o = {};
-        o.format = first;
-        o.scheme = ozTTgemm::Scheme::II;
-        check(ctx, o, 5056, 64, 32, Pattern::Uniform);
-        o.reconstruction = ozTTgemm::Reconstruction::TwoPass;
-        check(ctx, o, 64, 64, 64, Pattern::Uniform);
-        o.reconstruction = ozTTgemm::Reconstruction::Automatic;
         std::vector<double> overlap{1, 2, 3, 4};
         const std::vector<double> identity{1, 0, 0, 1};
         ctx.gemm(overlap, identity, overlap, 2, 2, 2, o);

@@ -19,6 +19,7 @@ REF_PLAN_SO = ROOT / "oracle" / "_ref" / "libozref_plan.so"
 REF_EMU_SO = ROOT / "oracle" / "_ref" / "libozref_emu.so"
 REF_PLAN1_SO = ROOT / "oracle" / "_ref" / "libozref_plan1.so"
 REF_PLAN_F8_SO = ROOT / "oracle" / "_ref" / "libozref_plan_f8.so"
+REF_PLAN1_F8_SO = ROOT / "oracle" / "_ref" / "libozref_plan1_f8.so"
 
 MAXS, MAXRP = 24, 5
 P = ctypes.c_void_p
@@ -81,6 +82,11 @@ class Oracle:
         L.ozo_i_recon_faithful.argtypes = [P, ctypes.c_int, u64, u64, P, P, P, u64]
         L.ozo_i_recon_exact.argtypes = [P, ctypes.c_int, u64, u64, P, P, P, u64]
         L.ozo_i_emulate.argtypes = [P, P, P, u64, u64, u64, ctypes.c_int, ctypes.c_int]
+        L.ozo_scale_mode.argtypes = [P, u64, u64, u64, ctypes.c_int, ctypes.c_int32, ctypes.c_int, P, P, P]
+        L.ozo_i_slice_fmt.argtypes = [P, u64, u64, u64, ctypes.c_int, P, ctypes.c_int, ctypes.c_int, P]
+        L.ozo_i_recon_faithful_deferred.argtypes = [P, ctypes.c_int, ctypes.c_int, u64, u64, u64, P, P, P, u64]
+        L.ozo_i_recon_exact_fmt.argtypes = [P, ctypes.c_int, ctypes.c_int, u64, u64, P, P, P, u64]
+        L.ozo_i_emulate_fmt.argtypes = [P, P, P, u64, u64, u64, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.ozo_crt_plan.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(OzoPlan)]
         L.ozo_fp8_split.argtypes = [P, u64, u64, u64, ctypes.c_int, P, ctypes.POINTER(OzoPlan), P, P]
         L.ozo_fp8_gemm.argtypes = [P, P, P, u64, u64, u64, P]
@@ -114,12 +120,13 @@ class Oracle:
         return p
 
     # -- stages -------------------------------------------------------------------------------
-    def scale(self, x: np.ndarray, rows: int, cols: int, col_mode: int, shift: int):
+    def scale(self, x: np.ndarray, rows: int, cols: int, col_mode: int, shift: int, ceil: int = 1):
+        """ceil: 1 rounds the BF16 maxima up (scheme II, scheme I INT8), 0 truncates (scheme I FP8)."""
         nout = cols if col_mode else rows
         bf = np.zeros(nout, dtype=np.uint16)
         d = np.zeros(nout, dtype=np.int32)
         fl = np.zeros(1, dtype=np.uint32)
-        self.lib.ozo_scale(ptr(x), rows, cols, cols, col_mode, shift, ptr(bf), ptr(d), ptr(fl))
+        self.lib.ozo_scale_mode(ptr(x), rows, cols, cols, col_mode, shift, ceil, ptr(bf), ptr(d), ptr(fl))
         return bf, d, int(fl[0])
 
     def split(self, x: np.ndarray, rows: int, cols: int, col_mode: int, delta: np.ndarray, plan: OzoPlan):
@@ -154,9 +161,11 @@ class Oracle:
         return rc, c, p, err.value.decode()
 
     # -- Scheme I ------------------------------------------------------------------------------
-    def i_slice(self, x: np.ndarray, rows: int, cols: int, col_mode: int, delta: np.ndarray, p: int) -> np.ndarray:
+    # fmt: the OZTT_FMT_* value, 5 INT8 (radix 254), 4 FP8 (radix 32).
+    def i_slice(self, x: np.ndarray, rows: int, cols: int, col_mode: int, delta: np.ndarray, p: int,
+                fmt: int = 5) -> np.ndarray:
         out = np.zeros(p * rows * cols, dtype=np.int8)
-        self.lib.ozo_i_slice(ptr(x), rows, cols, cols, col_mode, ptr(delta), p, ptr(out))
+        self.lib.ozo_i_slice_fmt(ptr(x), rows, cols, cols, col_mode, ptr(delta), p, fmt, ptr(out))
         return out
 
     def i_gemm(self, sa: np.ndarray, sb: np.ndarray, p: int, M: int, N: int, K: int) -> np.ndarray:
@@ -165,15 +174,21 @@ class Oracle:
         return out
 
     def i_recon(self, pd: np.ndarray, p: int, M: int, N: int, dA: np.ndarray, dB: np.ndarray,
-                exact: bool) -> np.ndarray:
+                exact: bool, fmt: int = 5, K: int = 0) -> np.ndarray:
+        """FP8 faithful: the reference's deferred reconstruction, whose single-conversion diagonals depend
+        on the padded K."""
         c = np.zeros(M * N)
-        fn = self.lib.ozo_i_recon_exact if exact else self.lib.ozo_i_recon_faithful
-        fn(ptr(pd), p, M, N, ptr(dA), ptr(dB), ptr(c), N)
+        if exact:
+            self.lib.ozo_i_recon_exact_fmt(ptr(pd), p, fmt, M, N, ptr(dA), ptr(dB), ptr(c), N)
+        elif fmt == 4:
+            self.lib.ozo_i_recon_faithful_deferred(ptr(pd), p, fmt, K, M, N, ptr(dA), ptr(dB), ptr(c), N)
+        else:
+            self.lib.ozo_i_recon_faithful(ptr(pd), p, M, N, ptr(dA), ptr(dB), ptr(c), N)
         return c
 
-    def i_emulate(self, a, b, m, n, k, p, exact=False) -> np.ndarray:
+    def i_emulate(self, a, b, m, n, k, p, exact=False, fmt: int = 5) -> np.ndarray:
         c = np.zeros(m * n)
-        self.lib.ozo_i_emulate(ptr(a), ptr(b), ptr(c), m, n, k, p, 1 if exact else 0)
+        self.lib.ozo_i_emulate_fmt(ptr(a), ptr(b), ptr(c), m, n, k, p, fmt, 1 if exact else 0)
         return c
 
     # -- Scheme II FP8 digits ---------------------------------------------------------------
@@ -301,9 +316,12 @@ class RefPlanF8:
 
 
 class RefPlan1:
-    """The reference's Scheme I slice-count selection compiled in place (oracle/ref_plan1.cpp)."""
+    """The reference's Scheme I slice-count selection compiled in place (oracle/ref_plan1.cpp); the FP8
+    build when fp8 is set."""
 
-    def __init__(self, path: Path = REF_PLAN1_SO):
+    def __init__(self, path: Path = REF_PLAN1_SO, fp8: bool = False):
+        if fp8:
+            path = REF_PLAN1_F8_SO
         if not path.exists():
             raise FileNotFoundError(str(path))
         self.lib = ctypes.CDLL(str(path))

@@ -1,5 +1,5 @@
 """The B200 integer stages against the reference device's published outputs at n = 3520 and 7040
-(tools/validated/all.csv:11-13, 27-29).
+(tools/validated/all.csv:10-13, 26-29).
 
 The scaling, splitting/slicing and the tensor-core products run on the GPU through the C ABI; the
 int32 products are then reconstructed on the host by the oracle's restatement of the reference's own
@@ -7,7 +7,8 @@ int32 products are then reconstructed on the host by the oracle's restatement of
 reference device's, so the GPU's residues/slices and products are the reference's at full size.
 Inputs: the evaluator's table suite (mt19937 seed 7, uniform(-1, 1)); Scheme II INT8 with max_moduli
 16, one pass, b = 54; Scheme I INT8 with 8 slices; Scheme II FP8 (e4m3 digits) with b = 54, one pass (the
-digit products are composed on the host by the oracle's restatement of compose.cpp).
+digit products are composed on the host by the oracle's restatement of compose.cpp); Scheme I FP8 with 12
+slices (the reference's deferred reconstruction restated on the host).
 """
 
 import numpy as np
@@ -18,6 +19,7 @@ from oracle_lib import pad, round_up
 
 pytestmark = pytest.mark.gpu
 
+INT8, FP8 = 5, 4  # OZTT_FMT_* values
 PUBLISHED = {3520: {"II": "a7bb9bd6f452e753", "I": "3ec48d5faecdf98f"},
              7040: {"II": "a2a3d9c61f79b001", "I": "316f280769f1f880"}}
 
@@ -75,8 +77,8 @@ def test_scheme_i_published(oztt, oracle, cuda, n):
     dA, dB = scale(oztt, A, n, n, 0, -1), scale(oztt, B, n, n, 1, -1)
     sa = torch.zeros(p * mp * kp, dtype=torch.int8, device="cuda")
     sb = torch.zeros(p * np_ * kp, dtype=torch.int8, device="cuda")
-    oztt.call("oztt_i_slice_rows", A.data_ptr(), n, n, n, dA.data_ptr(), p, sa.data_ptr(), mp, kp, stream())
-    oztt.call("oztt_i_slice_cols", B.data_ptr(), n, n, n, dB.data_ptr(), p, sb.data_ptr(), np_, kp, stream())
+    oztt.call("oztt_i_slice_rows", A.data_ptr(), n, n, n, dA.data_ptr(), p, INT8, sa.data_ptr(), mp, kp, stream())
+    oztt.call("oztt_i_slice_cols", B.data_ptr(), n, n, n, dB.data_ptr(), p, INT8, sb.data_ptr(), np_, kp, stream())
     del A, B
     pd = torch.empty(p * mp * np_, dtype=torch.int32, device="cuda")
     oztt.call("oztt_i_diag_gemm", sa.data_ptr(), sb.data_ptr(), mp, np_, kp, p, pd.data_ptr(), stream())
@@ -125,3 +127,41 @@ def test_scheme_ii_fp8_published(oztt, oracle, cuda, n):
     da[:n], db[:n] = dA.cpu().numpy(), dB.cpu().numpy()
     c = oracle.recon_residue(r, M, M, da, db, crt).reshape(M, M)[:n, :n]
     assert oracle.output_hash(np.ascontiguousarray(c).reshape(-1)) == PUBLISHED_FP8[n]
+
+
+# Scheme I FP8 (tools/validated/all.csv:10, 26): 12 slices of radix 32. The published hash of 3520 is
+# printed without its leading zero digit.
+PUBLISHED_I_FP8 = {3520: 0x03327179e9766269, 7040: 0xdff033d852f50dee}
+
+
+@pytest.mark.parametrize("n", [3520, 7040])
+def test_scheme_i_fp8_published(oztt, oracle, cuda, n):
+    """GPU scaling (BF16 maxima truncated), radix-32 slicing and diagonal products; the reference's deferred
+    reconstruction restated on the host must give the published bits."""
+    a, b = oracle.gen_inputs(n, n, n, -1.0, 7)
+    p = 12
+    M = round_up(n, 64)
+    mp, np_, kp = round_up(n, 128), round_up(n, 256), round_up(n, 128)
+    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    dA = torch.zeros(n, dtype=torch.int32, device="cuda")
+    dB = torch.zeros(n, dtype=torch.int32, device="cuda")
+    flags = torch.zeros(1, dtype=torch.int32, device="cuda")
+    oztt.call("oztt_i_scale_rows", A.data_ptr(), n, n, n, FP8, dA.data_ptr(), flags.data_ptr(), stream())
+    oztt.call("oztt_i_scale_cols", B.data_ptr(), n, n, n, FP8, dB.data_ptr(), flags.data_ptr(), stream())
+    sa = torch.zeros(p * mp * kp, dtype=torch.int8, device="cuda")
+    sb = torch.zeros(p * np_ * kp, dtype=torch.int8, device="cuda")
+    oztt.call("oztt_i_slice_rows", A.data_ptr(), n, n, n, dA.data_ptr(), p, FP8, sa.data_ptr(), mp, kp, stream())
+    oztt.call("oztt_i_slice_cols", B.data_ptr(), n, n, n, dB.data_ptr(), p, FP8, sb.data_ptr(), np_, kp, stream())
+    del A, B
+    pd = torch.empty(p * mp * np_, dtype=torch.int32, device="cuda")
+    oztt.call("oztt_i_diag_gemm", sa.data_ptr(), sb.data_ptr(), mp, np_, kp, p, pd.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert int(flags.cpu()[0]) == 0
+    del sa, sb
+    host = np.ascontiguousarray(pd.view(p, mp, np_)[:, :M, :M].cpu().numpy())
+    del pd
+    da = np.zeros(M, dtype=np.int32)
+    db = np.zeros(M, dtype=np.int32)
+    da[:n], db[:n] = dA.cpu().numpy(), dB.cpu().numpy()
+    c = oracle.i_recon(host.reshape(-1), p, M, M, da, db, exact=False, fmt=FP8, K=M).reshape(M, M)[:n, :n]
+    assert int(oracle.output_hash(np.ascontiguousarray(c).reshape(-1)), 16) == PUBLISHED_I_FP8[n]

@@ -1,8 +1,8 @@
-"""Scheme I INT8 on the B200, stage by stage and end to end, against the oracle.
+"""Scheme I (INT8 and FP8 slices) on the B200, stage by stage and end to end, against the oracle.
 
 Every call goes through the C ABI of liboztt.so. Bars:
-  * slices (radix-254 digits of every element): bit-exact against the oracle's restatement of the
-    reference slicer (slice_tf_body.h with tfMulR);
+  * slices (radix-254 digits of every element for INT8, radix-32 digits for FP8): bit-exact against the
+    oracle's restatement of the reference slicer (slice_tf_body.h with tfMulR / tfMulP2);
   * diagonal products P_d (int32): bit-exact;
   * the FP64 output: bit-exact against the oracle's restatement of the B200 exact Horner
     reconstruction, and within |C - C_ref| <= 2 ulp(C) + 2^-58 (|A| |B|)_ij of the reference's own
@@ -27,13 +27,18 @@ def stream():
     return torch.cuda.current_stream().cuda_stream
 
 
-def gpu_deltas(oztt, x, rows, cols, col_mode):
+INT8, FP8 = 5, 4  # OZTT_FMT_* values
+FORMATS = [INT8, FP8]
+CEIL = {INT8: 1, FP8: 0}  # BF16 rounding of the maxima: up for INT8, truncated for FP8
+
+
+def gpu_deltas(oztt, x, rows, cols, col_mode, fmt=INT8):
     X = dev(x)
     nout = cols if col_mode else rows
     delta = torch.zeros(nout, dtype=torch.int32, device="cuda")
     flags = torch.zeros(1, dtype=torch.int32, device="cuda")
-    name = "oztt_ii_scale_cols" if col_mode else "oztt_ii_scale_rows"
-    oztt.call(name, X.data_ptr(), rows, cols, cols, -1, delta.data_ptr(), None, flags.data_ptr(), stream())
+    name = "oztt_i_scale_cols" if col_mode else "oztt_i_scale_rows"
+    oztt.call(name, X.data_ptr(), rows, cols, cols, fmt, delta.data_ptr(), flags.data_ptr(), stream())
     return X, delta, flags
 
 
@@ -62,36 +67,40 @@ def hard_matrix(rng, rows, cols):
 SLICE_CASES = [(64, 64, 8), (33, 100, 7), (257, 129, 13), (5, 4097, 3), (128, 256, 1), (300, 45, 16)]
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("m,k,p", SLICE_CASES)
-def test_slice_rows_match_oracle(oztt, oracle, cuda, m, k, p):
+def test_slice_rows_match_oracle(oztt, oracle, cuda, m, k, p, fmt):
     rng = np.random.default_rng(m * 1000 + k)
     a = hard_matrix(rng, m, k)
-    A, delta, flags = gpu_deltas(oztt, a, m, k, 0)
-    _, od, ofl = oracle.scale(a, m, k, 0, -1)
+    A, delta, flags = gpu_deltas(oztt, a, m, k, 0, fmt)
+    _, od, ofl = oracle.scale(a, m, k, 0, -1, ceil=CEIL[fmt])
     mp, kp = round_up(m, 128), round_up(k, 128)
     planes = torch.full((p * mp * kp,), 99, dtype=torch.int8, device="cuda")
-    oztt.call("oztt_i_slice_rows", A.data_ptr(), m, k, k, delta.data_ptr(), p, planes.data_ptr(), mp, kp, stream())
+    oztt.call("oztt_i_slice_rows", A.data_ptr(), m, k, k, delta.data_ptr(), p, fmt, planes.data_ptr(), mp, kp,
+              stream())
     torch.cuda.synchronize()
     assert np.array_equal(delta.cpu().numpy(), od) and int(flags.cpu()[0]) == ofl
     got = planes.cpu().numpy().reshape(p, mp, kp)
-    want = oracle.i_slice(a, m, k, 0, od, p).reshape(p, m, k)
+    want = oracle.i_slice(a, m, k, 0, od, p, fmt=fmt).reshape(p, m, k)
     assert np.array_equal(got[:, :m, :k], want)
     assert not got[:, m:, :].any() and not got[:, :, k:].any()
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("k,n,p", SLICE_CASES)
-def test_slice_cols_match_oracle(oztt, oracle, cuda, k, n, p):
+def test_slice_cols_match_oracle(oztt, oracle, cuda, k, n, p, fmt):
     rng = np.random.default_rng(k * 1000 + n + 1)
     b = np.ascontiguousarray(hard_matrix(rng, n, k).reshape(n, k).T).reshape(-1)
-    B, delta, flags = gpu_deltas(oztt, b, k, n, 1)
-    _, od, ofl = oracle.scale(b, k, n, 1, -1)
+    B, delta, flags = gpu_deltas(oztt, b, k, n, 1, fmt)
+    _, od, ofl = oracle.scale(b, k, n, 1, -1, ceil=CEIL[fmt])
     np_, kp = round_up(n, 256), round_up(k, 128)
     planes = torch.full((p * np_ * kp,), 99, dtype=torch.int8, device="cuda")
-    oztt.call("oztt_i_slice_cols", B.data_ptr(), k, n, n, delta.data_ptr(), p, planes.data_ptr(), np_, kp, stream())
+    oztt.call("oztt_i_slice_cols", B.data_ptr(), k, n, n, delta.data_ptr(), p, fmt, planes.data_ptr(), np_, kp,
+              stream())
     torch.cuda.synchronize()
     assert np.array_equal(delta.cpu().numpy(), od) and int(flags.cpu()[0]) == ofl
     got = planes.cpu().numpy().reshape(p, np_, kp)
-    want = oracle.i_slice(b, k, n, 1, od, p).reshape(p, n, k)
+    want = oracle.i_slice(b, k, n, 1, od, p, fmt=fmt).reshape(p, n, k)
     assert np.array_equal(got[:, :n, :k], want)
     assert not got[:, n:, :].any() and not got[:, :, k:].any()
 
@@ -126,12 +135,14 @@ def test_diag_gemm_at_the_int32_budget(oztt, cuda):
         assert np.all(got[d, 0::2, :] == want) and np.all(got[d, 1::2, :] == -want)
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("m,n,p", [(64, 64, 1), (100, 70, 5), (128, 256, 8), (33, 300, 13)])
-def test_recon_matches_oracle(oztt, oracle, cuda, m, n, p):
+def test_recon_matches_oracle(oztt, oracle, cuda, m, n, p, fmt):
     rng = np.random.default_rng(m * n + p)
     mp, np_ = round_up(m, 128), round_up(n, 256)
     K = 2048
-    bound = np.array([(d + 1) * K * 127 * 127 for d in range(p)], dtype=np.int64)
+    radix, dmax = (254, 127) if fmt == INT8 else (32, 16)
+    bound = np.array([(d + 1) * K * dmax * dmax for d in range(p)], dtype=np.int64)
     pd = (rng.uniform(-1, 1, (p, mp, np_)) * bound[:, None, None] * rng.uniform(0, 1, (p, 1, 1))).astype(np.int32)
     pd[:, 0, 0] = 0                     # zero result
     pd[:, 0, 1] = bound.astype(np.int32)  # largest positive
@@ -142,22 +153,22 @@ def test_recon_matches_oracle(oztt, oracle, cuda, m, n, p):
     dA[2] = 1000                        # results far below 2^-1022: flushed to zero
     PD, DA, DB = dev(pd.reshape(-1)), dev(dA), dev(dB)
     c = torch.full((m * n,), 3.0, dtype=torch.float64, device="cuda")
-    oztt.call("oztt_i_recon", PD.data_ptr(), mp, np_, DA.data_ptr(), DB.data_ptr(), p, c.data_ptr(), m, n, n,
+    oztt.call("oztt_i_recon", PD.data_ptr(), mp, np_, DA.data_ptr(), DB.data_ptr(), p, fmt, c.data_ptr(), m, n, n,
               stream())
     torch.cuda.synchronize()
     got = c.cpu().numpy().reshape(m, n)
-    exact = oracle.i_recon(pd.reshape(-1), p, mp, np_, dA, dB, exact=True).reshape(mp, np_)[:m, :n]
+    exact = oracle.i_recon(pd.reshape(-1), p, mp, np_, dA, dB, exact=True, fmt=fmt).reshape(mp, np_)[:m, :n]
     assert np.array_equal(got.view(np.uint64), exact.view(np.uint64))
-    faithful = oracle.i_recon(pd.reshape(-1), p, mp, np_, dA, dB, exact=False).reshape(mp, np_)[:m, :n]
-    # magnitude bound of the sum: sum_d |P_d| 254^(L-d) 254^-(L+2) 2^-(dA+dB)
-    w = np.array([254.0 ** (-(d + 2)) for d in range(p)])
+    faithful = oracle.i_recon(pd.reshape(-1), p, mp, np_, dA, dB, exact=False, fmt=fmt, K=K).reshape(mp, np_)[:m, :n]
+    # magnitude bound of the sum: sum_d |P_d| r^(L-d) r^-(L+2) 2^-(dA+dB)
+    w = np.array([float(radix) ** (-(d + 2)) for d in range(p)])
     mag = np.tensordot(w, np.abs(pd[:, :m, :n].astype(np.float64)), axes=1)
     mag *= np.exp2(-(dA[:m, None] + dB[None, :n]).astype(np.float64))
     assert np.all(np.abs(got - faithful) <= 2 * np.spacing(np.abs(got)) + 2.0 ** -58 * mag)
 
 
-def run_gpu(oztt, a, b, m, n, k, p=0):
-    plan = oztt.i_int8_plan(a, b, m, n, k, slices=p)
+def run_gpu(oztt, a, b, m, n, k, p=0, fmt=INT8):
+    plan = oztt.i_int8_plan(a, b, m, n, k, slices=p, fmt=fmt)
     return oztt.i_int8_run(a, b, m, n, k, plan), plan
 
 
@@ -169,24 +180,27 @@ PIPE_CASES = [("uniform", 128, 128, 128, -1.0, 8), ("phi1", 100, 70, 45, 1.0, 0)
               ("tall", 1000, 3, 64, 0.5, 6), ("wide", 3, 1000, 96, -1.0, 0), ("one", 1, 1, 1, -1.0, 2)]
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("name,m,n,k,phi,p", PIPE_CASES)
-def test_pipeline_matches_oracle(oztt, oracle, cuda, name, m, n, k, phi, p):
+def test_pipeline_matches_oracle(oztt, oracle, cuda, name, m, n, k, phi, p, fmt):
     a, b = oracle.gen_inputs(m, n, k, phi, 17)
-    c, plan = run_gpu(oztt, a, b, m, n, k, p)
+    p = p if fmt == INT8 or p == 0 else p + 4  # radix 32 carries 5 bits a slice, 254 about 8
+    c, plan = run_gpu(oztt, a, b, m, n, k, p, fmt)
     assert p == 0 or plan.p == p
-    exact = oracle.i_emulate(a, b, m, n, k, plan.p, exact=True)
+    exact = oracle.i_emulate(a, b, m, n, k, plan.p, exact=True, fmt=fmt)
     assert np.array_equal(c.view(np.uint64), exact.view(np.uint64)), name
-    faithful = oracle.i_emulate(a, b, m, n, k, plan.p, exact=False)
+    faithful = oracle.i_emulate(a, b, m, n, k, plan.p, exact=False, fmt=fmt)
     tol = 2 * np.spacing(np.abs(c)) + 2.0 ** -58 * absprod(a, b, m, n, k).reshape(-1)
     assert np.all(np.abs(c - faithful) <= tol), name
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("mode", [2, 3, 4, 5, 6, 7])
-def test_pipeline_patterns(oztt, oracle, cuda, mode):
+def test_pipeline_patterns(oztt, oracle, cuda, mode, fmt):
     m, n, k = (65, 67, 97) if mode < 6 else (1, 1, 1)
     a, b = oracle.gen_pattern(m, n, k, mode)
-    c, plan = run_gpu(oztt, a, b, m, n, k)
-    exact = oracle.i_emulate(a, b, m, n, k, plan.p, exact=True)
+    c, plan = run_gpu(oztt, a, b, m, n, k, fmt=fmt)
+    exact = oracle.i_emulate(a, b, m, n, k, plan.p, exact=True, fmt=fmt)
     assert np.array_equal(c.view(np.uint64), exact.view(np.uint64))
 
 
@@ -231,3 +245,34 @@ def test_context_scheme_i(oztt, oracle, cuda):
     assert oracle.accuracy(c, hi, lo)[0] <= 8 * np.finfo(np.float64).eps
     with pytest.raises(RuntimeError, match="reconstruction would overflow FP32"):
         ctx.multiply(a, b, m, n, k, oztt.Options(scheme=oztt.Scheme.I, format=oztt.Format.INT8, slices=15))
+
+
+def test_published_case_fp8(oztt, oracle, cuda):
+    # tools/validated/quick.csv:10: Scheme I FP8, n=128, seed 7, 12 slices; relative Frobenius error
+    # 4.69453713108e-17 against Dot2 and hash 4d24add106258287 on the reference device.
+    n = 128
+    a, b = oracle.gen_inputs(n, n, n, -1.0, 7)
+    c, _ = run_gpu(oztt, a, b, n, n, n, 12, FP8)
+    ref = oracle.i_emulate(a, b, n, n, n, 12, exact=False, fmt=FP8)
+    assert oracle.output_hash(ref) == "4d24add106258287"
+    assert np.all(np.abs(c - ref) <= 2 * np.spacing(np.abs(c)))
+    hi, lo = oracle.dot2(a, b, n, n, n)
+    rel, _ = oracle.accuracy(c, hi, lo)
+    assert abs(rel - 4.69453713108e-17) <= 1e-3 * 4.69453713108e-17
+
+
+def test_context_scheme_i_fp8(oztt, oracle, cuda):
+    ctx = oztt.Context()
+    m, n, k = 65, 67, 97
+    a, b = oracle.gen_inputs(m, n, k, 1.0, 4)
+    c = np.empty(m * n)
+    info = ctx.gemm(a, b, c, m, n, k, oztt.Options(scheme=oztt.Scheme.I, format=oztt.Format.FP8))
+    plan = oztt.i_int8_plan(a, b, m, n, k, fmt=oztt.Format.FP8)
+    assert info.scheme == oztt.Scheme.I and info.format == oztt.Format.FP8 and info.slices == plan.p
+    exact = oracle.i_emulate(a, b, m, n, k, plan.p, exact=True, fmt=FP8)
+    assert np.array_equal(c.view(np.uint64), exact.view(np.uint64))
+    hi, lo = oracle.dot2(a, b, m, n, k)
+    assert oracle.accuracy(c, hi, lo)[0] <= 8 * np.finfo(np.float64).eps
+    # the fixed slice count of the reference's test for FP8 (tests/correctness.cpp:280)
+    c12 = ctx.multiply(a, b, m, n, k, oztt.Options(scheme=oztt.Scheme.I, format=oztt.Format.FP8, slices=12))
+    assert np.array_equal(c12.view(np.uint64), oracle.i_emulate(a, b, m, n, k, 12, exact=True, fmt=FP8).view(np.uint64))

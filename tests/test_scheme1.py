@@ -120,3 +120,66 @@ def test_horner_budget_is_rejected(oztt):
 def test_plan_rejects_invalid_arguments(oztt):
     with pytest.raises(ValueError, match="at most 256"):
         oztt.i_int8_plan(np.ones(4), np.ones(4), 2, 2, 2, slices=257)
+
+
+# ---- Scheme I with FP8 digits (radix 32, digits +-16, maxima truncated to BF16) -----------------------
+FP8 = 4  # OZTT_FMT_FP8
+# tools/validated/quick.csv:10 — the reference device's Scheme I FP8 output for n=128, seed 7, uniform(-1,1),
+# 12 slices.
+PUBLISHED_I_FP8 = {"n": 128, "seed": 7, "slices": 12, "output_hash": "4d24add106258287",
+                   "relative_fro": 4.69453713108e-17}
+
+
+def test_oracle_reproduces_published_scheme_i_fp8_output(oracle):
+    n = PUBLISHED_I_FP8["n"]
+    a, b = oracle.gen_inputs(n, n, n, -1.0, PUBLISHED_I_FP8["seed"])
+    c = oracle.i_emulate(a, b, n, n, n, PUBLISHED_I_FP8["slices"], exact=False, fmt=FP8)
+    assert oracle.output_hash(c) == PUBLISHED_I_FP8["output_hash"]
+    hi, lo = oracle.dot2(a, b, n, n, n)
+    rel, _ = oracle.accuracy(c, hi, lo)
+    assert rel == pytest.approx(PUBLISHED_I_FP8["relative_fro"], rel=1e-10)
+
+
+def test_oracle_fp8_slices_are_digits_of_the_scaled_input(oracle):
+    # sum_i d_i 32^-(i+1) reproduces x 2^delta to within 32^-p * 16/31 (balanced digits, clamp +-16);
+    # the truncated BF16 maxima leave |x 2^delta| up to (1 + 2^-7)/2, inside the span 16/31.
+    rng = np.random.default_rng(6)
+    rows, cols, p = 4, 64, 9
+    x = rng.standard_normal(rows * cols) * np.exp2(rng.integers(-20, 20, rows * cols))
+    x = x.reshape(rows, cols)
+    _, d, flags = oracle.scale(x.reshape(-1), rows, cols, 0, -1, ceil=0)
+    assert flags == 0
+    sl = oracle.i_slice(x.reshape(-1), rows, cols, 0, d, p, fmt=FP8).reshape(p, rows, cols).astype(np.float64)
+    assert np.all(np.abs(sl) <= 16)
+    approx = sum(sl[i] * 32.0 ** -(i + 1) for i in range(p))
+    target = x * np.exp2(d.astype(np.float64))[:, None]
+    assert np.all(np.abs(target) <= 0.5 * (1 + 2.0 ** -7))
+    assert np.all(np.abs(approx - target) <= 32.0 ** -p * 16 / 31 * (1 + 1e-12))
+
+
+def test_oracle_fp8_exact_recon_close_to_faithful(oracle):
+    n = 128
+    a, b = oracle.gen_inputs(n, n, n, 1.0, 3)
+    faithful = oracle.i_emulate(a, b, n, n, n, 12, exact=False, fmt=FP8)
+    exact = oracle.i_emulate(a, b, n, n, n, 12, exact=True, fmt=FP8)
+    assert np.all(np.abs(faithful - exact) <= 2 * np.spacing(np.abs(exact)))
+
+
+def test_fp8_slice_selection_matches_reference(oracle, oztt, ref_plan1_f8):
+    for name, a, b, m, n, k in _selection_cases(oracle):
+        M, N, K = round_up(m, 64), round_up(n, 64), round_up(k, 32)
+        want = ref_plan1_f8.slices(pad(a, m, k, M, K), pad(b, k, n, K, N), M, N, K)
+        plan = oztt.i_int8_plan(a, b, m, n, k, fmt=oztt.Format.FP8)
+        assert plan.p == want, name
+        assert (plan.format, plan.radix, plan.dmax) == (FP8, 32, 16)
+
+
+def test_fp8_plan_feasibility(oztt):
+    a, b = np.ones(32), np.ones(32)
+    # log2(32) + 23 log2(32) + 12 = 132 >= 128: the Horner exponent budget
+    with pytest.raises(RuntimeError, match=r"reconstruction would overflow FP32 for k=32 with 23 slices \(radix 32\)"):
+        oztt.i_int8_plan(a, b, 1, 1, 32, slices=23, fmt=oztt.Format.FP8)
+    assert oztt.i_int8_plan(a, b, 1, 1, 32, slices=22, fmt=oztt.Format.FP8).p == 22
+    # K blocking is allowed for FP8 (no INT8-style rejection)
+    k = 16416
+    assert oztt.i_int8_plan(np.ones(k), np.ones(k), 1, 1, k, slices=8, fmt=oztt.Format.FP8).p == 8
