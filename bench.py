@@ -338,7 +338,7 @@ def run_fp8(args) -> None:
                     "n_gpus": 1, "config": {"workload": workload, "max_moduli": S_req, "reconstruction_passes": passes}}
             t_plan = time.perf_counter()
             try:
-                plan = oz.fp8_plan_device(A.data_ptr(), B.data_ptr(), m, n, k, max_moduli=S_req,
+                plan = oz.digit_plan_device(A.data_ptr(), B.data_ptr(), m, n, k, max_moduli=S_req,
                                           reconstruction=passes, stream=stream)
             except (RuntimeError, ValueError) as exc:
                 print(json.dumps({**base, "value": None, "rejected": str(exc)}), flush=True)
@@ -346,7 +346,7 @@ def run_fp8(args) -> None:
             t_plan = time.perf_counter() - t_plan
 
             def step():
-                return oz.fp8_run_device(A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, plan, stream, 0,
+                return oz.digit_run_device(A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, plan, stream, 0,
                                          timed=True)
 
             for _ in range(max(args.warmup, 0)):

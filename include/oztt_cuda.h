@@ -10,7 +10,7 @@
  * reference project root):
  *   oztt_gemm                 Context::gemm (src/context.cpp:182-186): validation, planning, GPU run
  *   oztt_is_available         ozTTgemm::is_available / format_name (src/dispatch.cpp:18-50)
- *   oztt_ii_fp8_*             the same stages for the FP8 (e4m3 digit) backend of scheme II
+ *   oztt_ii_digit_*           the same stages for the digit formats of scheme II (FP8, BF16, FP16, TF32)
  *   oztt_ii_int8_plan         choose_moduli_and_width (src/backend/ozaki2/plan.hpp:258-306) for INT8
  *   oztt_ii_int8_run          ozaki2_int8::run (src/ozaki2.cpp:439-478) on host buffers: the backend
  *                             seam Backend = Output(*)(Device&, const Problem&)
@@ -91,18 +91,22 @@ typedef struct oztt_ii_plan {
     double recon1_log2;            /* estimated log2 error of one reconstruction pass */
 } oztt_ii_plan;
 
-/* ---- Scheme II with FP8 (e4m3) digits (route OZ2_ROUTE_FP8 of src/backend/ozaki2/split.hpp) ----
- * Residues are split into two or three small digits per modulus; the products of digit planes are
- * grouped by weight (concatenated along K) into GEMM outputs, which the composition combines into the
- * residue of C modulo m. Splitting methods (OZ2_SPLIT_* of split.hpp): */
+/* ---- Scheme II with digit formats: FP8 (e4m3), BF16, FP16, TF32 ------------------------------------
+ * (the routes OZ2_ROUTE_FP8, OZ2_ROUTE_BF16A, OZ2_ROUTE_FP16A, OZ2_ROUTE_D32 of src/backend/ozaki2/split.hpp)
+ * Residues are split into one to three small digits per modulus (|digit| <= 16, or the sparse e4m3 set up
+ * to 32, for FP8; <= 32 for the others); the products of digit planes are grouped by weight (concatenated
+ * along K) into GEMM outputs, which the composition combines into the residue of C modulo m. Splitting
+ * methods (OZ2_SPLIT_* of split.hpp): */
 #define OZTT_SPLIT_SQ 0   /* square m = q^2, digits by rounding to nearest, 3 products */
 #define OZTT_SPLIT_KAR 1  /* radix-16 Karatsuba (l, h, s = h + l), 3 products */
 #define OZTT_SPLIT_WIDE 2 /* two digits of radix ~sqrt(m), 4 products */
 #define OZTT_SPLIT_SQS 4  /* square of odd q with the sparse e4m3 digits (|x| <= 16, or even and <= 32) */
+#define OZTT_SPLIT_ONE 5  /* one digit: the residue itself (|r| <= 32; BF16 and FP16), 1 product */
 #define OZTT_MAXOUT 96    /* GEMM outputs: at most 4 per modulus */
 
-typedef struct oztt_fp8_plan {
+typedef struct oztt_digit_plan {
     oztt_ii_plan base; /* moduli, width, digits of A', passes, CRT constants, statistics */
+    int32_t format;    /* OZTT_FMT_FP8, _BF16, _FP16 or _TF32 */
     int32_t nplane;    /* digit planes per operand */
     int32_t nprod;     /* digit products */
     int32_t nout;      /* GEMM outputs after concatenation */
@@ -112,59 +116,63 @@ typedef struct oztt_fp8_plan {
     /* output o = sum_{t < out_g[o]} A digit plane (out_a[o] + t) x B digit plane (out_b[o] - t), with the
      * composition coefficient coeff[o] (mod the modulus out_mod[o]) */
     int32_t out_a[OZTT_MAXOUT], out_b[OZTT_MAXOUT], out_g[OZTT_MAXOUT], out_mod[OZTT_MAXOUT], coeff[OZTT_MAXOUT];
-} oztt_fp8_plan;
+} oztt_digit_plan;
 
-/* Scheme II FP8 plan (choose_moduli_and_width with the FP8 route, src/backend/ozaki2/plan.hpp:258-306 and
- * moduli.hpp:710-770); arguments as oztt_ii_int8_plan (default limit 14 moduli with a fixed width). */
-int oztt_ii_fp8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
-                  int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan* plan, char* err, size_t errlen);
+/* Scheme II plan of a digit format (choose_moduli_and_width with the format's route,
+ * src/backend/ozaki2/plan.hpp:258-306 and moduli.hpp:700-770; for BF16 and FP16 the moduli set of the
+ * stage-time model search, awe.hpp); arguments as oztt_ii_int8_plan (with a fixed width the default limit
+ * is the route's: 14 moduli for FP8, 11 for TF32, 24 for BF16 and FP16). */
+int oztt_ii_digit_plan(int32_t format, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                       uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_digit_plan* plan,
+                       char* err, size_t errlen);
 /* The same plan from DEVICE operands a (m x k) and b (k x n) on `stream`: the precision policy's statistics
  * are measured on the GPU (as oztt_ii_int8_plan_device). */
-int oztt_ii_fp8_plan_device(int device_id, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
-                            uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan* plan,
-                            void* stream, char* err, size_t errlen);
+int oztt_ii_digit_plan_device(int device_id, int32_t format, const double* a, const double* b, uint64_t m,
+                              uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits,
+                              oztt_digit_plan* plan, void* stream, char* err, size_t errlen);
 
-/* Whole FP8 pipeline with a given plan on HOST buffers (row-major, C = A B): upload, scale, digit split,
- * digit products with the composition fused, reconstruction, download. Replaces the FP8 backend's run
- * (src/ozaki2.cpp:439-478 compiled with OZ_FMT_FP8). */
-int oztt_ii_fp8_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
-                    const oztt_fp8_plan* plan, char* err, size_t errlen);
+/* Whole digit-format pipeline with a given plan on HOST buffers (row-major, C = A B): upload, scale, digit
+ * split, digit products with the composition fused, reconstruction, download. Replaces the digit backends'
+ * run (src/ozaki2.cpp:439-478 compiled with OZ_FMT_FP8 / _BF16 / _FP16 / _FP32). */
+int oztt_ii_digit_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                      const oztt_digit_plan* plan, char* err, size_t errlen);
 /* The same on DEVICE buffers, stream-ordered on `stream`; stage_ms (NULL or 6 doubles) receives the device
  * time of scale rows, scale cols, split rows, split cols, digit GEMM and reconstruction. */
-int oztt_ii_fp8_run_device(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
-                           uint64_t k, const oztt_fp8_plan* plan, void* stream, double* stage_ms, char* err,
-                           size_t errlen);
+int oztt_ii_digit_run_device(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                             uint64_t k, const oztt_digit_plan* plan, void* stream, double* stage_ms, char* err,
+                             size_t errlen);
 
-/* FP8 stages (device buffers, stream-ordered). Digit split (kernels/modslice_digit.cpp with sparse_fix.h):
- * the residues of A (m x k, lda) split into the e4m3 digits of each modulus, written as int8 values to
- * planes [nplane][mp][kp] (plane poff[s] + 0 = l, + 1 = h, + 2 = s); B (k x n, ldb) transposed into
- * [nplane][np][kp]. delta as from oztt_ii_scale_rows / _cols with the plan's shift. */
-int oztt_ii_fp8_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
-                           const oztt_fp8_plan* plan, int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err,
-                           size_t errlen);
-int oztt_ii_fp8_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
-                           const oztt_fp8_plan* plan, int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err,
-                           size_t errlen);
+/* Digit-format stages (device buffers, stream-ordered). Digit split (kernels/modslice_digit.cpp with
+ * sparse_fix.h): the residues of A (m x k, lda) split into the digits of each modulus, written as int8
+ * values to planes [nplane][mp][kp] (plane poff[s] + 0 = l, + 1 = h, + 2 = s; a one-digit modulus has its
+ * residue in plane poff[s]); B (k x n, ldb) transposed into [nplane][np][kp]. delta as from
+ * oztt_ii_scale_rows / _cols with the plan's shift. */
+int oztt_ii_digit_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
+                             const oztt_digit_plan* plan, int8_t* planes, uint64_t mp, uint64_t kp, void* stream,
+                             char* err, size_t errlen);
+int oztt_ii_digit_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
+                             const oztt_digit_plan* plan, int8_t* planes, uint64_t np, uint64_t kp, void* stream,
+                             char* err, size_t errlen);
 /* Digit products (the reference's GEMM stage on digit planes with compose.cpp): mode 0 writes every GEMM
  * output P_o as int32 [nout][mp][np]; mode 1 composes in the epilogue and writes the CRT digits
  * k_s = (sum_o coeff_o P_o) y_s mod m_s as uint16 [S][mp][np]. mp, np, kp multiples of 128, 256, 128. */
-int oztt_ii_fp8_digit_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp, uint64_t np, uint64_t kp,
-                           const oztt_fp8_plan* plan, int32_t mode, void* out, void* stream, char* err, size_t errlen);
+int oztt_ii_digit_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp, uint64_t np, uint64_t kp,
+                       const oztt_digit_plan* plan, int32_t mode, void* out, void* stream, char* err, size_t errlen);
 /* Reconstruction from uint16 CRT digits [S][mp][np] (as oztt_ii_recon). */
-int oztt_ii_fp8_recon(const uint16_t* k_digits, uint64_t mp, uint64_t np, const int32_t* delta_a,
-                      const int32_t* delta_b, const oztt_fp8_plan* plan, double* c, uint64_t m, uint64_t n,
-                      uint64_t ldc, void* stream, char* err, size_t errlen);
+int oztt_ii_digit_recon(const uint16_t* k_digits, uint64_t mp, uint64_t np, const int32_t* delta_a,
+                        const int32_t* delta_b, const oztt_digit_plan* plan, double* c, uint64_t m, uint64_t n,
+                        uint64_t ldc, void* stream, char* err, size_t errlen);
 
 /* Plan of one Scheme I call (src/ozaki1.cpp:192-210): the number of slices p, the last diagonal L = p-1
- * kept, and the format's slicing (src/backend/ozaki1/param.hpp:47-50): INT8 radix 254, digits +-127; FP8
- * radix 32, digits +-16; both normalised to 2^-1. */
+ * kept, and the format's slicing (src/backend/ozaki1/param.hpp:47-70): INT8 radix 254, digits +-127; FP8
+ * radix 32, digits +-16; BF16, FP16, TF32 radix 64, digits +-32; all normalised to 2^-1. */
 typedef struct oztt_i_plan {
     uint32_t M, N, K;  /* planning dimensions: m, n rounded up to 64, k to 32 */
     int32_t p;         /* number of slices (Info::slices) */
     int32_t auto_p;    /* 1 if p was chosen from the input (oz_fp64_p), 0 if requested */
-    int32_t format;    /* OZTT_FMT_INT8 or OZTT_FMT_FP8 */
-    int32_t radix;     /* 254 or 32 */
-    int32_t dmax;      /* 127 or 16 */
+    int32_t format;    /* OZTT_FMT_INT8, _FP8, _BF16, _FP16 or _TF32 */
+    int32_t radix;     /* 254, 32 or 64 */
+    int32_t dmax;      /* 127, 16 or 32 */
 } oztt_i_plan;
 
 /* ---- whole calls ---------------------------------------------------------------------------- */
@@ -208,10 +216,11 @@ int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* 
  * reference would throw (K blocking needed, Horner exponent budget exceeded). */
 int oztt_i_int8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
                      oztt_i_plan* plan, char* err, size_t errlen);
-/* Scheme I FP8 plan (the same with the FP8 constants: K blocking allowed, the pair loop folding the FP32
- * partial products into Int32, ozaki1/plan.hpp:141-226). */
-int oztt_i_fp8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
-                    oztt_i_plan* plan, char* err, size_t errlen);
+/* Scheme I plan of any built format (the same with the format's constants: for FP8, BF16, FP16 and TF32
+ * K blocking is allowed and the pair loop folds the FP32 partial products into Int32,
+ * ozaki1/plan.hpp:141-226). */
+int oztt_i_format_plan(int32_t format, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                       uint32_t slices, oztt_i_plan* plan, char* err, size_t errlen);
 /* Scheme II INT8 plan for operands already on the device (a: m x k, b: k x n, row-major): the input
  * statistics of the precision policy are measured by kernels on `stream` (bit-identical to the host
  * measurement of oztt_ii_int8_plan), the decisions made on the host. Synchronises `stream`. */

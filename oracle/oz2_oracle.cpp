@@ -1147,6 +1147,10 @@ bool odd_integer(float a) { return (f_to_bits(a + 8388608.0f) & 1u) != 0; }
 // Digits of one residue r of a modulus with splitting mode `mode` (modslice_digit.cpp:193-226,
 // sparse_fix.h:52-72); returns the number of digits (l, h[, s]).
 int split_residue(float r, int mode, float q, float qinv, float* dg) {
+    if (mode == OZTT_SPLIT_ONE) {  // one digit: the residue itself (modslice_digit.cpp:207-211)
+        dg[0] = r;
+        return 1;
+    }
     if (mode == OZTT_SPLIT_KAR) {
         // h = round((r + sign(r) (q/2 - 1/2)) / q), the sign from Ltz: +1 for r >= 0
         const float ltz = r < 0.0f ? 1.0f : 0.0f;
@@ -1200,8 +1204,8 @@ int ozo_crt_plan(const int32_t* m, int S, int b, int two_pass, ozo_plan* out) {
     return 0;
 }
 
-int ozo_fp8_split(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, const int32_t* delta,
-                  const ozo_plan* crt, const oztt_fp8_plan* fp, int8_t* planes) {
+int ozo_digit_split(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, const int32_t* delta,
+                  const ozo_plan* crt, const oztt_digit_plan* fp, int8_t* planes) {
     const int S = crt->S, nd = crt->nd;
     const uint64_t plane = rows * cols;
     float qinv[OZO_MAXS];
@@ -1221,7 +1225,7 @@ int ozo_fp8_split(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, in
                 float digit[3];
                 const int nd2 = split_residue(res, fp->mode[s], (float)fp->q[s], qinv[s], digit);
                 for (int j = 0; j < nd2; ++j) {
-                    if (!e4m3_integer(digit[j])) bad = 1;
+                    if (fp->format == OZTT_FMT_FP8 ? !e4m3_integer(digit[j]) : std::fabs(digit[j]) > 32.0f) bad = 1;
                     planes[(uint64_t)(fp->poff[s] + j) * plane + idx] = (int8_t)(int)digit[j];
                 }
             }
@@ -1229,7 +1233,7 @@ int ozo_fp8_split(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, in
     return bad;
 }
 
-int ozo_fp8_gemm(const int8_t* ap, const int8_t* bp, const oztt_fp8_plan* fp, uint64_t M, uint64_t N, uint64_t K,
+int ozo_digit_gemm(const int8_t* ap, const int8_t* bp, const oztt_digit_plan* fp, uint64_t M, uint64_t N, uint64_t K,
                  int32_t* out) {
     int bad = 0;
     const int64_t nout = fp->nout;
@@ -1249,7 +1253,7 @@ int ozo_fp8_gemm(const int8_t* ap, const int8_t* bp, const oztt_fp8_plan* fp, ui
     return bad;
 }
 
-int ozo_fp8_compose(const int32_t* P, const oztt_fp8_plan* fp, const ozo_plan* crt, uint64_t M, uint64_t N, float* r) {
+int ozo_digit_compose(const int32_t* P, const oztt_digit_plan* fp, const ozo_plan* crt, uint64_t M, uint64_t N, float* r) {
     const int S = crt->S;
     const uint64_t plane = M * N;
     for (int s = 0; s < S; ++s) {
@@ -1259,6 +1263,14 @@ int ozo_fp8_compose(const int32_t* P, const oztt_fp8_plan* fp, const ozo_plan* c
         for (int o = o0; o < o1; ++o) {
             lo[o] = (float)fp->coeff[o];                                   // c mod m (coeff_lo)
             hi[o] = (float)(((int64_t)fp->coeff[o] * 4096) % crt->m[s]);  // c 2^12 mod m (coeff_hi)
+        }
+        if (fp->mode[s] == OZTT_SPLIT_ONE) {
+            // a one-digit modulus bypasses the composition; the reconstruction reduces its product first
+            // (RAWMASK, recon_crt_proc.h:28-33)
+#pragma omp parallel for schedule(static)
+            for (int64_t e = 0; e < (int64_t)plane; ++e)
+                r[(uint64_t)s * plane + (uint64_t)e] = mod_round((float)P[(uint64_t)o0 * plane + (uint64_t)e], m, ri);
+            continue;
         }
 #pragma omp parallel for schedule(static)
         for (int64_t e = 0; e < (int64_t)plane; ++e) {
@@ -1281,8 +1293,8 @@ int ozo_fp8_compose(const int32_t* P, const oztt_fp8_plan* fp, const ozo_plan* c
     return 0;
 }
 
-int ozo_fp8_emulate(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
-                    const oztt_fp8_plan* fp, int exact, char* err, size_t errlen) {
+int ozo_digit_emulate(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                    const oztt_digit_plan* fp, int exact, char* err, size_t errlen) {
     auto pad = [](uint64_t v, uint64_t q) { return (v + q - 1) / q * q; };
     const uint64_t M = pad(m, 64), N = pad(n, 64), K = pad(k, 32);
     std::vector<double> ap(M * K, 0.0), bp(K * N, 0.0);
@@ -1303,18 +1315,18 @@ int ozo_fp8_emulate(const double* a, const double* b, double* c, uint64_t m, uin
     }
     const uint64_t NP = (uint64_t)fp->nplane;
     std::vector<int8_t> da(NP * M * K), db(NP * N * K);
-    if (ozo_fp8_split(ap.data(), M, K, K, 0, dA.data(), &crt, fp, da.data()) |
-        ozo_fp8_split(bp.data(), K, N, N, 1, dB.data(), &crt, fp, db.data())) {
-        set_err(err, errlen, "a digit outside the integers of e4m3");
+    if (ozo_digit_split(ap.data(), M, K, K, 0, dA.data(), &crt, fp, da.data()) |
+        ozo_digit_split(bp.data(), K, N, N, 1, dB.data(), &crt, fp, db.data())) {
+        set_err(err, errlen, "a digit outside the digit set of the format");
         return 1;
     }
     std::vector<int32_t> P((uint64_t)fp->nout * M * N);
-    if (ozo_fp8_gemm(da.data(), db.data(), fp, M, N, K, P.data())) {
+    if (ozo_digit_gemm(da.data(), db.data(), fp, M, N, K, P.data())) {
         set_err(err, errlen, "a digit product above 2^24");
         return 1;
     }
     std::vector<float> r((uint64_t)crt.S * M * N);
-    ozo_fp8_compose(P.data(), fp, &crt, M, N, r.data());
+    ozo_digit_compose(P.data(), fp, &crt, M, N, r.data());
     std::vector<double> cp(M * N);
     if (exact) {
         std::vector<int32_t> ri(r.size());
@@ -1367,12 +1379,17 @@ void tf_mul_r(float& x0, float& x1, float& x2, float r) {
     fast_two_sum(ec, G, x1, x2);
 }
 
-// Radix and digit bound of a scheme I format (ozaki1/param.hpp:47-50): INT8 254 / 127, FP8 32 / 16.
+// Radix and digit bound of a scheme I format (ozaki1/param.hpp:47-70): INT8 (5) 254 / 127, FP8 (4) 32 / 16,
+// BF16 (0), FP16 (1) and TF32 (2) 64 / 32.
 struct I1Fmt {
     float radix, dmax;
     bool pow2;  // radix multiplication by tfMulP2 (sfpu_tf.h:121-134)
 };
-I1Fmt i1_fmt(int format) { return format == 4 ? I1Fmt{32.0f, 16.0f, true} : I1Fmt{254.0f, 127.0f, false}; }
+I1Fmt i1_fmt(int format) {
+    if (format == 4) return I1Fmt{32.0f, 16.0f, true};
+    if (format == 0 || format == 1 || format == 2) return I1Fmt{64.0f, 32.0f, true};
+    return I1Fmt{254.0f, 127.0f, false};
+}
 
 // The p slices of one element (slice_tf_body.h): t *= radix; d = clamp(Rnd(t0), +-dmax); t0 -= d.
 void make_slices(double x, int32_t d, int p, const I1Fmt& f, int8_t* out, uint64_t stride) {
@@ -1692,7 +1709,7 @@ int ozo_i_emulate_fmt(const double* a, const double* b, double* c, uint64_t m, u
     for (uint64_t i = 0; i < k; ++i) std::copy_n(b + i * n, n, bp.data() + i * N);
     std::vector<int32_t> dA(M), dB(N);
     uint32_t fa = 0, fb = 0;
-    const int ceil = format == 4 ? 0 : 1;  // OZ1_CEIL_MODE: FP8 truncates the maxima, INT8 rounds them up
+    const int ceil = format == 5 ? 1 : 0;  // OZ1_CEIL_MODE: INT8 rounds the maxima up, the FP formats truncate
     ozo_scale_mode(ap.data(), M, K, K, 0, -1, ceil, nullptr, dA.data(), &fa);
     ozo_scale_mode(bp.data(), K, N, N, 1, -1, ceil, nullptr, dB.data(), &fb);
     if (fa | fb) return 1;
@@ -1704,7 +1721,7 @@ int ozo_i_emulate_fmt(const double* a, const double* b, double* c, uint64_t m, u
     std::vector<double> cp(M * N);
     if (exact)
         ozo_i_recon_exact_fmt(pd.data(), p, format, M, N, dA.data(), dB.data(), cp.data(), N);
-    else if (format == 4)
+    else if (format != 5)
         ozo_i_recon_faithful_deferred(pd.data(), p, format, K, M, N, dA.data(), dB.data(), cp.data(), N);
     else
         ozo_i_recon_faithful(pd.data(), p, M, N, dA.data(), dB.data(), cp.data(), N);

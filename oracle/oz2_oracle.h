@@ -15,7 +15,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#include "oztt_cuda.h"  // the plain C struct oztt_fp8_plan (digit layout of one FP8 plan)
+#include "oztt_cuda.h"  // the plain C struct oztt_digit_plan (digit layout of one FP8 plan)
 
 #ifdef __cplusplus
 extern "C" {
@@ -146,9 +146,10 @@ int ozo_i_recon_exact(const int32_t* pd, int p, uint64_t M, uint64_t N, const in
 // Whole scheme I INT8 pipeline with p slices (p > 0) for unpadded inputs (padded like the reference).
 int ozo_i_emulate(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k, int p, int exact);
 
-// The same stages for a scheme I format (format: 5 INT8, 4 FP8; the OZTT_FMT_* values). FP8
-// (ozaki1/param.hpp:50, format.hpp): radix 32 multiplied by tfMulP2 (sfpu_tf.h:121-134), digits
-// clamped to +-16, row/column maxima truncated to BF16 (CEIL mode 0).
+// The same stages for a scheme I format (format: the OZTT_FMT_* value, 5 INT8, 4 FP8, 0 BF16, 1 FP16,
+// 2 TF32). FP8 (ozaki1/param.hpp:50, format.hpp): radix 32 multiplied by tfMulP2 (sfpu_tf.h:121-134),
+// digits clamped to +-16; BF16, FP16, TF32 (param.hpp:55-65): radix 64, digits +-32; the FP formats
+// truncate the row/column maxima to BF16 (CEIL mode 0).
 int ozo_scale_mode(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, int32_t shift, int ceil,
                    uint16_t* bf16_max, int32_t* delta, uint32_t* flags);
 int ozo_i_slice_fmt(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, const int32_t* delta,
@@ -163,35 +164,37 @@ int ozo_i_recon_exact_fmt(const int32_t* pd, int p, int format, uint64_t M, uint
 int ozo_i_emulate_fmt(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k, int p,
                       int format, int exact);
 
-// ---- Scheme II with FP8 (e4m3) digits (src/backend/ozaki2/kernels/modslice_digit.cpp, compose.cpp,
-// sparse_fix.h; the digit layout comes from an oztt_fp8_plan) ---------------------------------------
+// ---- Scheme II with digit formats: FP8 (e4m3), BF16, FP16, TF32 (src/backend/ozaki2/kernels/
+// modslice_digit.cpp, compose.cpp, sparse_fix.h; the digit layout comes from an oztt_digit_plan) -----------
 // CRT constants of a moduli set with integer width b (crt_constants of the INT8 path; nothing in them
 // depends on the route): yi, rinv, 2^20k mod m, the reciprocal fragments, W, qw, nd, shift.
 int ozo_crt_plan(const int32_t* m, int S, int b, int two_pass, ozo_plan* out);
 // Digit planes of every element: the residue r of A' modulo m (the INT8 path's oz2_residue) split per
-// modulus as modslice_digit.cpp:193-226 does (rounding to nearest for squares and wide moduli, the
-// sparse-digit fix of sparse_fix.h for SQS, radix-16 Karatsuba with rounding up for KAR); plane
-// poff[i]+0 = l, +1 = h, +2 = s. A: [nplane][rows][cols]; B (col_mode=1): [nplane][cols][rows].
-// Returns 1 if a digit is not an integer that e4m3 represents exactly, else 0.
-int ozo_fp8_split(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, const int32_t* delta,
-                  const ozo_plan* crt, const oztt_fp8_plan* fp, int8_t* planes);
+// modulus as modslice_digit.cpp:193-226 does (the residue itself for a one-digit modulus, rounding to
+// nearest for squares and wide moduli, the sparse-digit fix of sparse_fix.h for SQS, radix-16 Karatsuba
+// with rounding up for KAR); plane poff[i]+0 = l (or the residue), +1 = h, +2 = s. A: [nplane][rows][cols];
+// B (col_mode=1): [nplane][cols][rows]. Returns 1 if a digit is not an integer of the format's digit set
+// (e4m3's for FP8, |x| <= 32 otherwise), else 0.
+int ozo_digit_split(const double* x, uint64_t rows, uint64_t cols, uint64_t ld, int col_mode, const int32_t* delta,
+                  const ozo_plan* crt, const oztt_digit_plan* fp, int8_t* planes);
 // GEMM outputs P_o = sum_{t < out_g[o]} A_(out_a[o]+t) B_(out_b[o]-t)^T, int32 [nout][M][N]. Returns 1 if
 // some |P_o| exceeds 2^24 (the sums would not be exact in the reference's FP32 accumulation).
-int ozo_fp8_gemm(const int8_t* ap, const int8_t* bp, const oztt_fp8_plan* fp, uint64_t M, uint64_t N, uint64_t K,
+int ozo_digit_gemm(const int8_t* ap, const int8_t* bp, const oztt_digit_plan* fp, uint64_t M, uint64_t N, uint64_t K,
                  int32_t* out);
 // Composition (compose.cpp:118-146) in the reference's binary32 operations: per modulus the sum of its
-// outputs times their coefficients, reduced first (fold_first) or split at 2^12, then ModRound; the
-// symmetric residues r [S][M][N] as floats.
-int ozo_fp8_compose(const int32_t* P, const oztt_fp8_plan* fp, const ozo_plan* crt, uint64_t M, uint64_t N, float* r);
+// outputs times their coefficients, reduced first (fold_first) or split at 2^12, then ModRound; for a
+// one-digit modulus the ModRound of its product that the reconstruction applies (RAWMASK); the residues
+// r [S][M][N] as floats.
+int ozo_digit_compose(const int32_t* P, const oztt_digit_plan* fp, const ozo_plan* crt, uint64_t M, uint64_t N, float* r);
 // Reference reconstruction from residues given as binary32 values (recon_crt.cpp with IN_RESIDUE=1).
 int ozo_recon_faithful_residue(const float* r, uint64_t M, uint64_t N, const int32_t* dA, const int32_t* dB,
                                const ozo_plan* plan, double* c, uint64_t ldc);
-// Whole FP8 pipeline for unpadded m x k, k x n with the plan fp (made for the same inputs): pads like
+// Whole digit-format pipeline for unpadded m x k, k x n with the plan fp (made for the same inputs): pads like
 // context.cpp:103-117, scales with the plan's shift, splits, multiplies, composes and reconstructs
 // (exact: 0 the reference's triple-float reconstruction, 1 the exact one). Returns 0, or 1 with a
-// message (out-of-range maxima, a digit outside e4m3, a GEMM output above 2^24).
-int ozo_fp8_emulate(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
-                    const oztt_fp8_plan* fp, int exact, char* err, size_t errlen);
+// message (out-of-range maxima, a digit outside the format's set, a GEMM output above 2^24).
+int ozo_digit_emulate(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                    const oztt_digit_plan* fp, int exact, char* err, size_t errlen);
 
 #ifdef __cplusplus
 }

@@ -1,10 +1,11 @@
 // TEST INFRASTRUCTURE — checker only, never shipped.
 //
-// Compiles the reference's Scheme II planner headers in place for the FP8 format (-DOZ_FMT_FP8:
-// route OZ2_ROUTE_FP8 of src/backend/ozaki2/split.hpp, the moduli selection of moduli.hpp, the
-// precision policy of auto_precision.hpp) with the TT-Metalium name stub of ref_shim/, and fills the
-// project's plan structure (include/oztt_cuda.h) from its decisions, so that tests can compare the
-// product's FP8 planner field by field. The glue restates the few lines of choose_moduli_and_width
+// Compiles the reference's Scheme II planner headers in place for one digit format (-DOZ_FMT_FP8,
+// -DOZ_FMT_BF16, -DOZ_FMT_FP16 or -DOZ_FMT_FP32: the route of src/backend/ozaki2/split.hpp, the moduli
+// selection of moduli.hpp with the stage-time model of awe.hpp, the precision policy of
+// auto_precision.hpp) with the TT-Metalium name stub of ref_shim/, and fills the project's plan
+// structure (include/oztt_cuda.h) from its decisions, so that tests can compare the product's digit
+// planner field by field. The glue restates the few lines of choose_moduli_and_width
 // (src/backend/ozaki2/plan.hpp:258-306), whose header cannot be included without TT-Metalium.
 #include <cstring>
 #include <vector>
@@ -12,11 +13,22 @@
 #include "oztt_cuda.h"
 #include "ozaki2/auto_precision.hpp"
 
-namespace rp = ozTTgemm::detail::ozaki2_f8;
+namespace rp = ozTTgemm::detail::OZTTGEMM_BACKEND_NS;
+
+#if defined(OZ_FMT_FP8)
+constexpr int32_t kFormat = OZTT_FMT_FP8;
+#elif defined(OZ_FMT_BF16)
+constexpr int32_t kFormat = OZTT_FMT_BF16;
+#elif defined(OZ_FMT_FP16)
+constexpr int32_t kFormat = OZTT_FMT_FP16;
+#else
+constexpr int32_t kFormat = OZTT_FMT_TF32;
+#endif
 
 namespace {
-void fill(const rp::Ozaki2Moduli& mo, oztt_fp8_plan* out) {
+void fill(const rp::Ozaki2Moduli& mo, oztt_digit_plan* out) {
     oztt_ii_plan& b = out->base;
+    out->format = kFormat;
     b.S = mo.s;
     b.b = mo.b;
     out->nplane = mo.nplane;
@@ -55,19 +67,20 @@ void fill(const rp::Ozaki2Moduli& mo, oztt_fp8_plan* out) {
 
 extern "C" {
 
-// The moduli selection alone; returns ok (and acc_ok in *acc).
-int ozr_f8_choose(uint32_t K, int num_moduli, int b_cap, oztt_fp8_plan* out, int* acc) {
+// The moduli selection alone for output dimensions M x N (the stage-time model's DRAM estimate reads
+// them); returns ok (and acc_ok in *acc).
+int ozr_digit_choose(uint32_t M, uint32_t N, uint32_t K, int num_moduli, int b_cap, oztt_digit_plan* out, int* acc) {
     std::memset(out, 0, sizeof(*out));
-    const rp::Ozaki2Moduli mo = rp::ozaki2_choose_moduli(K, K, K, num_moduli, b_cap);
+    const rp::Ozaki2Moduli mo = rp::ozaki2_choose_moduli(M, N, K, num_moduli, b_cap);
     fill(mo, out);
     *acc = mo.acc_ok ? 1 : 0;
     return mo.ok ? 1 : 0;
 }
 
-// choose_moduli_and_width for padded row-major A (M x K) and B (K x N) with the FP8 route. Returns 1
+// choose_moduli_and_width for padded row-major A (M x K) and B (K x N) with the format's route. Returns 1
 // where the reference throws.
-int ozr_f8_plan(const double* a, const double* b, uint32_t M, uint32_t N, uint32_t K, uint32_t max_moduli,
-                int passes, int fixed_bits, oztt_fp8_plan* out) {
+int ozr_digit_plan(const double* a, const double* b, uint32_t M, uint32_t N, uint32_t K, uint32_t max_moduli,
+                int passes, int fixed_bits, oztt_digit_plan* out) {
     std::memset(out, 0, sizeof(*out));
     const std::vector<double> A(a, a + (size_t)M * K), B(b, b + (size_t)K * N);
     const bool b_fixed = fixed_bits > 0;

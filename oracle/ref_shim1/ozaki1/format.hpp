@@ -16,6 +16,13 @@ inline constexpr uint32_t OZ1_RADIX = 32;
 inline constexpr uint32_t OZ1_DMAX = 16;
 inline constexpr int32_t OZ1_NSHIFT = -1;
 inline constexpr uint32_t OZ1_CEIL_MODE = 0;
+#elif defined(OZ_FMT_BF16) || defined(OZ_FMT_FP16) || defined(OZ_FMT_FP32)
+// BF16, FP16, TF32 (param.hpp:55-65 radix 64; digit bound 32; target 2^-1; maxima truncated to BF16,
+// CEIL mode 0).
+inline constexpr uint32_t OZ1_RADIX = 64;
+inline constexpr uint32_t OZ1_DMAX = 32;
+inline constexpr int32_t OZ1_NSHIFT = -1;
+inline constexpr uint32_t OZ1_CEIL_MODE = 0;
 #else
 inline constexpr uint32_t OZ1_RADIX = 254;
 inline constexpr uint32_t OZ1_DMAX = 127;

@@ -116,13 +116,13 @@ class IIPlan(ctypes.Structure):
 
 
 MAXOUT = 96
-# Digit splitting methods of the FP8 plan (OZTT_SPLIT_* of include/oztt_cuda.h).
-SPLIT_SQ, SPLIT_KAR, SPLIT_WIDE, SPLIT_SQS = 0, 1, 2, 4
+# Digit splitting methods of a digit plan (OZTT_SPLIT_* of include/oztt_cuda.h).
+SPLIT_SQ, SPLIT_KAR, SPLIT_WIDE, SPLIT_SQS, SPLIT_ONE = 0, 1, 2, 4, 5
 
 
-class FP8Plan(ctypes.Structure):
-    """oztt_fp8_plan: the Scheme II FP8 digit plan (moduli, splitting, GEMM outputs, coefficients)."""
-    _fields_ = [("base", IIPlan), ("nplane", ctypes.c_int32), ("nprod", ctypes.c_int32), ("nout", ctypes.c_int32),
+class DigitPlan(ctypes.Structure):
+    """oztt_digit_plan: the Scheme II plan of a digit format (moduli, splitting, GEMM outputs, coefficients)."""
+    _fields_ = [("base", IIPlan), ("format", ctypes.c_int32), ("nplane", ctypes.c_int32), ("nprod", ctypes.c_int32), ("nout", ctypes.c_int32),
                 ("fold_first", ctypes.c_int32), ("q", ctypes.c_int32 * MAXS), ("mode", ctypes.c_int32 * MAXS),
                 ("poff", ctypes.c_int32 * MAXS), ("npl", ctypes.c_int32 * MAXS), ("oout", ctypes.c_int32 * (MAXS + 1)),
                 ("out_a", ctypes.c_int32 * MAXOUT), ("out_b", ctypes.c_int32 * MAXOUT),
@@ -171,20 +171,21 @@ _SIGNATURES = {
     "oztt_ii_int8_plan_from_stats": [_U64, _U64, _U64, ctypes.c_uint32, _I32, _I32, ctypes.c_double, ctypes.c_double,
                                      ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.POINTER(IIPlan), _ERR,
                                      _SZ],
-    "oztt_ii_fp8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, _I32, _I32, ctypes.POINTER(FP8Plan), _ERR, _SZ],
-    "oztt_ii_fp8_plan_device": [ctypes.c_int, _P, _P, _U64, _U64, _U64, ctypes.c_uint32, _I32, _I32,
-                                ctypes.POINTER(FP8Plan), _P, _ERR, _SZ],
-    "oztt_ii_fp8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(FP8Plan), _ERR, _SZ],
-    "oztt_ii_fp8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(FP8Plan), _P, _P, _ERR,
+    "oztt_ii_digit_plan": [_I32, _P, _P, _U64, _U64, _U64, ctypes.c_uint32, _I32, _I32, ctypes.POINTER(DigitPlan),
+                           _ERR, _SZ],
+    "oztt_ii_digit_plan_device": [ctypes.c_int, _I32, _P, _P, _U64, _U64, _U64, ctypes.c_uint32, _I32, _I32,
+                                  ctypes.POINTER(DigitPlan), _P, _ERR, _SZ],
+    "oztt_ii_digit_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(DigitPlan), _ERR, _SZ],
+    "oztt_ii_digit_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(DigitPlan), _P, _P, _ERR,
                                _SZ],
-    "oztt_ii_fp8_split_rows": [_P, _U64, _U64, _U64, _P, ctypes.POINTER(FP8Plan), _P, _U64, _U64, _P, _ERR, _SZ],
-    "oztt_ii_fp8_split_cols": [_P, _U64, _U64, _U64, _P, ctypes.POINTER(FP8Plan), _P, _U64, _U64, _P, _ERR, _SZ],
-    "oztt_ii_fp8_digit_gemm": [_P, _P, _U64, _U64, _U64, ctypes.POINTER(FP8Plan), _I32, _P, _P, _ERR, _SZ],
-    "oztt_ii_fp8_recon": [_P, _U64, _U64, _P, _P, ctypes.POINTER(FP8Plan), _P, _U64, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_ii_digit_split_rows": [_P, _U64, _U64, _U64, _P, ctypes.POINTER(DigitPlan), _P, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_ii_digit_split_cols": [_P, _U64, _U64, _U64, _P, ctypes.POINTER(DigitPlan), _P, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_ii_digit_gemm": [_P, _P, _U64, _U64, _U64, ctypes.POINTER(DigitPlan), _I32, _P, _P, _ERR, _SZ],
+    "oztt_ii_digit_recon": [_P, _U64, _U64, _P, _P, ctypes.POINTER(DigitPlan), _P, _U64, _U64, _U64, _P, _ERR, _SZ],
     "oztt_i_int8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _P, _P, _ERR, _SZ],
-    "oztt_i_fp8_plan": [_P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _ERR, _SZ],
+    "oztt_i_format_plan": [_I32, _P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_scale_rows": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _ERR, _SZ],
     "oztt_i_scale_cols": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _ERR, _SZ],
     "oztt_i_slice_rows": [_P, _U64, _U64, _U64, _P, _I32, _I32, _P, _U64, _U64, _P, _ERR, _SZ],
@@ -327,16 +328,17 @@ def ii_int8_plan_device(a_ptr: int, b_ptr: int, m: int, n: int, k: int, max_modu
     return plan
 
 
-def fp8_plan(a, b, m: int, n: int, k: int, max_moduli: int = 0, reconstruction: int = 0,
-             fixed_bits: int = 0) -> FP8Plan:
-    """Scheme II FP8 digit plan for row-major host matrices (oztt_ii_fp8_plan); a and b may be None with a
-    fixed width and a fixed number of passes."""
+def digit_plan(a, b, m: int, n: int, k: int, max_moduli: int = 0, reconstruction: int = 0,
+               fixed_bits: int = 0, fmt=Format.FP8) -> DigitPlan:
+    """Scheme II plan of a digit format (FP8, BF16, FP16, TF32) for row-major host matrices
+    (oztt_ii_digit_plan); a and b may be None with a fixed width and a fixed number of passes."""
     av = _as_f64(a, "a") if a is not None else None
     bv = _as_f64(b, "b") if b is not None else None
-    plan = FP8Plan()
+    plan = DigitPlan()
     err = _errbuf()
-    rc = _lib().oztt_ii_fp8_plan(av.ctypes.data if av is not None else None, bv.ctypes.data if bv is not None else None,
-                                 m, n, k, max_moduli, reconstruction, fixed_bits, ctypes.byref(plan), err, len(err))
+    rc = _lib().oztt_ii_digit_plan(int(fmt), av.ctypes.data if av is not None else None,
+                                   bv.ctypes.data if bv is not None else None, m, n, k, max_moduli, reconstruction,
+                                   fixed_bits, ctypes.byref(plan), err, len(err))
     if rc != OK:
         _raise(rc, err.value)
     return plan
@@ -397,41 +399,41 @@ def ii_int8_run_device_timed(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int,
     return list(ms)
 
 
-def fp8_plan_device(a_ptr: int, b_ptr: int, m: int, n: int, k: int, max_moduli: int = 0, reconstruction: int = 0,
-                    fixed_bits: int = 0, stream: int = 0, device_id: int = 0) -> FP8Plan:
-    """Scheme II FP8 plan for device-resident operands, the statistics measured on the device
-    (oztt_ii_fp8_plan_device)."""
-    plan = FP8Plan()
+def digit_plan_device(a_ptr: int, b_ptr: int, m: int, n: int, k: int, max_moduli: int = 0, reconstruction: int = 0,
+                      fixed_bits: int = 0, stream: int = 0, device_id: int = 0, fmt=Format.FP8) -> DigitPlan:
+    """Scheme II plan of a digit format for device-resident operands, the statistics measured on the device
+    (oztt_ii_digit_plan_device)."""
+    plan = DigitPlan()
     err = _errbuf()
-    rc = _lib().oztt_ii_fp8_plan_device(device_id, a_ptr, b_ptr, m, n, k, max_moduli, reconstruction, fixed_bits,
-                                        ctypes.byref(plan), stream, err, len(err))
+    rc = _lib().oztt_ii_digit_plan_device(device_id, int(fmt), a_ptr, b_ptr, m, n, k, max_moduli, reconstruction,
+                                          fixed_bits, ctypes.byref(plan), stream, err, len(err))
     if rc != OK:
         _raise(rc, err.value)
     return plan
 
 
-def fp8_run(a, b, m: int, n: int, k: int, plan: FP8Plan, device_id: int = 0) -> np.ndarray:
-    """The Scheme II FP8 pipeline on host matrices with a given plan (oztt_ii_fp8_run)."""
+def digit_run(a, b, m: int, n: int, k: int, plan: DigitPlan, device_id: int = 0) -> np.ndarray:
+    """The Scheme II digit-format pipeline on host matrices with a given plan (oztt_ii_digit_run)."""
     av, bv = _as_f64(a, "a"), _as_f64(b, "b")
     if av.size != m * k or bv.size != k * n:
         raise ValueError("matrix span sizes do not match m, n, k")
     c = np.empty(m * n, dtype=np.float64)
     err = _errbuf()
-    rc = _lib().oztt_ii_fp8_run(device_id, av.ctypes.data, bv.ctypes.data, c.ctypes.data, m, n, k, ctypes.byref(plan),
+    rc = _lib().oztt_ii_digit_run(device_id, av.ctypes.data, bv.ctypes.data, c.ctypes.data, m, n, k, ctypes.byref(plan),
                                 err, len(err))
     if rc != OK:
         _raise(rc, err.value)
     return c
 
 
-def fp8_run_device(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, plan: FP8Plan, stream: int = 0,
+def digit_run_device(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, plan: DigitPlan, stream: int = 0,
                    device_id: int = 0, timed: bool = False) -> list[float] | None:
-    """The FP8 pipeline on device pointers (oztt_ii_fp8_run_device); synchronises `stream`. With timed=True
+    """The digit-format pipeline on device pointers (oztt_ii_digit_run_device); synchronises `stream`. With timed=True
     returns the device milliseconds of scale rows, scale columns, split rows, split columns, digit GEMM and
     reconstruction."""
     ms = (ctypes.c_double * 6)()
     err = _errbuf()
-    rc = _lib().oztt_ii_fp8_run_device(device_id, a_ptr, b_ptr, c_ptr, m, n, k, ctypes.byref(plan), stream,
+    rc = _lib().oztt_ii_digit_run_device(device_id, a_ptr, b_ptr, c_ptr, m, n, k, ctypes.byref(plan), stream,
                                        ms if timed else None, err, len(err))
     if rc != OK:
         _raise(rc, err.value)
@@ -439,15 +441,19 @@ def fp8_run_device(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, p
 
 
 def i_int8_plan(a, b, m: int, n: int, k: int, slices: int = 0, fmt=None) -> IPlan:
-    """Scheme I plan (oztt_i_int8_plan, or oztt_i_fp8_plan for fmt=Format.FP8): slices > 0 fixes p, 0
-    selects it from the input."""
+    """Scheme I plan (oztt_i_int8_plan, or oztt_i_format_plan for another format fmt): slices > 0 fixes p,
+    0 selects it from the input."""
     av, bv = _as_f64(a, "a"), _as_f64(b, "b")
     if av.size != m * k or bv.size != k * n:
         raise ValueError("matrix span sizes do not match m, n, k")
     plan = IPlan()
     err = _errbuf()
-    fn = _lib().oztt_i_fp8_plan if fmt is not None and int(fmt) == Format.FP8 else _lib().oztt_i_int8_plan
-    rc = fn(av.ctypes.data, bv.ctypes.data, m, n, k, slices, ctypes.byref(plan), err, len(err))
+    if fmt is None or int(fmt) == Format.INT8:
+        rc = _lib().oztt_i_int8_plan(av.ctypes.data, bv.ctypes.data, m, n, k, slices, ctypes.byref(plan), err,
+                                     len(err))
+    else:
+        rc = _lib().oztt_i_format_plan(int(fmt), av.ctypes.data, bv.ctypes.data, m, n, k, slices, ctypes.byref(plan),
+                                       err, len(err))
     if rc != OK:
         _raise(rc, err.value)
     return plan

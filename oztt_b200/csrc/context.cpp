@@ -9,9 +9,8 @@
 //   * one process-wide mutex serialises the calls of all contexts (:19, :152);
 //   * the device is opened on the first valid call; Info reports the padded dimensions (:176-180);
 //   * all input is consumed before C is written, so C may overlap A or B.
-// Dispatch (src/dispatch.cpp:18-50): INT8 and FP8 (e4m3 digits) are built, both schemes;
-// the Tenstorrent block formats BFP8/BFP4/BFP2 are not available on this hardware, and BF16, FP16 and
-// TF32 are not built yet.
+// Dispatch (src/dispatch.cpp:18-50): INT8, FP8 (e4m3 digits), BF16, FP16 and TF32 are built, both schemes;
+// the Tenstorrent block formats BFP8/BFP4/BFP2 are not available on this hardware.
 #include <ozTTgemm/ozTTgemm.hpp>
 
 #include <algorithm>
@@ -29,8 +28,9 @@
 namespace oztt {
 int run_ii_int8_planned(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
                         uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_ii_plan& p, std::string& err);
-int run_ii_fp8_planned(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
-                       uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_fp8_plan& p, std::string& err);
+int run_ii_digit_planned(int device_id, int32_t format, const double* a, const double* b, double* c, uint64_t m,
+                         uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_digit_plan& p,
+                         std::string& err);
 }  // namespace oztt
 
 namespace ozTTgemm {
@@ -137,7 +137,10 @@ int32_t recon_code(Reconstruction r) {
 
 }  // namespace
 
-bool is_available(Format format) noexcept { return format == Format::INT8 || format == Format::FP8; }
+bool is_available(Format format) noexcept {
+    return format == Format::INT8 || format == Format::FP8 || format == Format::BF16 || format == Format::FP16 ||
+           format == Format::TF32;
+}
 
 const char* format_name(Format format) noexcept {
     switch (format) {
@@ -169,11 +172,11 @@ Context::~Context() = default;
 Info Context::Impl::execute(std::span<const double> a, std::span<const double> b, std::span<double> c, std::size_t m,
                             std::size_t n, std::size_t k, const Options& opt, const Checked& v) {
     std::lock_guard lock(runtime_mutex);
-    if (opt.format == Format::FP8 && opt.scheme == Scheme::II) {
-        oztt_fp8_plan plan;
+    if (opt.format != Format::INT8 && opt.scheme == Scheme::II) {  // the digit formats
+        oztt_digit_plan plan;
         std::string msg;
-        const int rc = oztt::run_ii_fp8_planned(options.device_id, a.data(), b.data(), c.data(), m, n, k,
-                                                opt.max_moduli, recon_code(opt.reconstruction), plan, msg);
+        const int rc = oztt::run_ii_digit_planned(options.device_id, (int32_t)opt.format, a.data(), b.data(), c.data(),
+                                                  m, n, k, opt.max_moduli, recon_code(opt.reconstruction), plan, msg);
         if (rc != OZTT_OK) rethrow(rc, msg);
         opened = true;
         Info info{Scheme::II, opt.format};
@@ -188,8 +191,8 @@ Info Context::Impl::execute(std::span<const double> a, std::span<const double> b
     if (opt.scheme == Scheme::I) {
         oztt_i_plan plan;
         std::string msg;
-        int rc = oztt::plan_i(a.data(), b.data(), m, n, k, opt.slices,
-                              opt.format == Format::FP8 ? oztt::kI1Fp8 : oztt::kI1Int8, plan, msg);
+        int rc = oztt::plan_i(a.data(), b.data(), m, n, k, opt.slices, *oztt::i1_format((int32_t)opt.format), plan,
+                              msg);
         if (rc != OZTT_OK) rethrow(rc, msg);
         char err[512] = {0};
         rc = oztt_i_int8_run(options.device_id, a.data(), b.data(), c.data(), m, n, k, &plan, err, sizeof err);

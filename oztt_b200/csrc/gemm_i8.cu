@@ -879,7 +879,7 @@ void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t 
 // epilogue, the CRT digits k_s = (sum_u c_u P_u) y_s mod m_s as uint16 [S][mp][np] (compose.cpp and the
 // term_k of recon_crt_proc.h, as one exact integer computation).
 void launch_digit_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
-                       const oztt_fp8_plan& fp, int mode, void* out, int* err_word, cudaStream_t st) {
+                       const oztt_digit_plan& fp, int mode, void* out, int* err_word, cudaStream_t st) {
     using namespace gemm;
     if (mp % BM || np % BN || kp % BK || mp == 0 || np == 0 || kp == 0)
         throw Error(OZTT_EINVAL, "digit_gemm: mp, np, kp must be positive multiples of 128, 256 and 128");

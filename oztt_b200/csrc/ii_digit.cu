@@ -1,17 +1,21 @@
 // SPDX-License-Identifier: Apache-2.0
 //
-// Scheme II with FP8 (e4m3) digits on one B200, and the C-ABI entry points of its stages.
+// Scheme II with digit formats (FP8 e4m3, BF16, FP16, TF32) on one B200, and the C-ABI entry points of
+// its stages.
 //
-// The reference's FP8 backend (the ozaki2 backend compiled with OZ_FMT_FP8: src/ozaki2.cpp:439-478 with
-// the digit stages of src/backend/ozaki2/stages.hpp) scales, splits every residue into two or three
-// e4m3 digits (kernels/modslice_digit.cpp), multiplies the digit planes with FP32 accumulation
-// (concatenating products of equal weight along K), composes the products of each modulus into its
-// residue (kernels/compose.cpp) and reconstructs (kernels/recon_crt.cpp, IN_RESIDUE=1). Here one call is
-// six launches on one stream:
+// The reference's digit backends (the ozaki2 backend compiled with OZ_FMT_FP8 / _BF16 / _FP16 / _FP32:
+// src/ozaki2.cpp:439-478 with the digit stages of src/backend/ozaki2/stages.hpp) scale, split every residue
+// into one to three small digits (kernels/modslice_digit.cpp), multiply the digit planes with FP32
+// accumulation (concatenating products of equal weight along K), compose the products of each modulus
+// into its residue (kernels/compose.cpp; a one-digit modulus skips it and the reconstruction reduces its
+// product, RAWMASK) and reconstruct (kernels/recon_crt.cpp, IN_RESIDUE=1). Here one call is six launches
+// on one stream:
 //     scale_rows(A) -> scale_cols(B) -> digit_split_rows(A) -> digit_split_cols(B)
 //     -> digit_gemm (every output of every modulus, composition fused into the epilogue) -> recon (uint16)
-// Digit planes [nplane][mp][kp] / [nplane][np][kp] int8 (every e4m3 digit is an integer in [-32, 32]),
-// CRT digits [S][mp][np] uint16.
+// Digit planes [nplane][mp][kp] / [nplane][np][kp] int8 (every digit of every format is an integer in
+// [-32, 32]), CRT digits [S][mp][np] uint16. The four formats differ only in their plans (moduli, splitting,
+// concatenation): on the reference's device they also differ in the transport type of the digits, which
+// carries the same integers.
 //
 // The digit products are integers the reference's planner keeps below 2^24, so its FP32 sums are exact;
 // the s32 tensor-core sums here are exact as well, and so the composed residue classes are the
@@ -32,38 +36,40 @@ void launch_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, in
 void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
                        uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax, cudaStream_t st);
 void launch_digit_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
-                             const oztt_fp8_plan& fp, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st);
+                             const oztt_digit_plan& fp, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st);
 void launch_digit_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
-                             const oztt_fp8_plan& fp, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st);
+                             const oztt_digit_plan& fp, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st);
 void launch_digit_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
-                       const oztt_fp8_plan& fp, int mode, void* out, int* err_word, cudaStream_t st);
+                       const oztt_digit_plan& fp, int mode, void* out, int* err_word, cudaStream_t st);
 void launch_recon_u16(const uint16_t* kp, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB,
                       const oztt_ii_plan& p, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st);
 PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
                                 cudaStream_t st);
 
 // Consistency of a digit plan (its own fields only; the GEMM launcher checks the output table).
-void check_fp8_plan(const oztt_fp8_plan& fp) {
+void check_digit_plan(const oztt_digit_plan& fp) {
     const oztt_ii_plan& p = fp.base;
     if (p.S < 1 || p.S > OZTT_MAXS) throw Error(OZTT_EINVAL, "plan: the number of moduli must be 1..24");
     if (p.nd < 3 || p.nd > 5) throw Error(OZTT_EINVAL, "plan: the number of digits must be 3..5");
-    if (fp.nplane < 2 || fp.nplane > 3 * OZTT_MAXS) throw Error(OZTT_EINVAL, "plan: bad number of digit planes");
+    if (fp.nplane < 1 || fp.nplane > 3 * OZTT_MAXS) throw Error(OZTT_EINVAL, "plan: bad number of digit planes");
     for (int s = 0; s < p.S; ++s) {
         const int m = p.moduli[s], mode = fp.mode[s];
-        if (m < 3 || m > 4096) throw Error(OZTT_EINVAL, "plan: FP8 moduli must be in 3..4096");
-        if (mode != OZTT_SPLIT_SQ && mode != OZTT_SPLIT_KAR && mode != OZTT_SPLIT_WIDE && mode != OZTT_SPLIT_SQS)
+        if (m < 2 || m > 4096) throw Error(OZTT_EINVAL, "plan: digit-format moduli must be in 2..4096");
+        if (mode != OZTT_SPLIT_SQ && mode != OZTT_SPLIT_KAR && mode != OZTT_SPLIT_WIDE && mode != OZTT_SPLIT_SQS &&
+            mode != OZTT_SPLIT_ONE)
             throw Error(OZTT_EINVAL, "plan: unknown splitting method");
-        const int npl = mode == OZTT_SPLIT_KAR ? 3 : 2;
-        if (fp.npl[s] != npl || fp.poff[s] < 0 || fp.poff[s] + npl > fp.nplane || fp.q[s] < 2 || fp.q[s] > 64)
+        const int npl = mode == OZTT_SPLIT_KAR ? 3 : (mode == OZTT_SPLIT_ONE ? 1 : 2);
+        const bool q_ok = mode == OZTT_SPLIT_ONE ? fp.q[s] == 1 : (fp.q[s] >= 2 && fp.q[s] <= 65);
+        if (fp.npl[s] != npl || fp.poff[s] < 0 || fp.poff[s] + npl > fp.nplane || !q_ok)
             throw Error(OZTT_EINVAL, "plan: bad digit layout of modulus " + std::to_string(s));
     }
 }
 
 // The device pipeline on device buffers (row-major, lda = k, ldb = n, ldc = n). stage_ms (optional, 6
 // entries): scale rows, scale cols, digit split rows, digit split cols, digit GEMM, reconstruction.
-void run_ii_fp8_device(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
-                       const oztt_fp8_plan& fp, cudaStream_t st, double* stage_ms = nullptr) {
-    check_fp8_plan(fp);
+void run_ii_digit_device(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                       const oztt_digit_plan& fp, cudaStream_t st, double* stage_ms = nullptr) {
+    check_digit_plan(fp);
     const oztt_ii_plan& p = fp.base;
     const uint64_t S = (uint64_t)p.S, NP = (uint64_t)fp.nplane;
     const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
@@ -113,10 +119,12 @@ void run_ii_fp8_device(const double* a, const double* b, double* c, uint64_t m, 
 }
 
 // Plan from device-resident operands (the precision policy's statistics measured on the device).
-int plan_fp8_device(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
-                    int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan& p, std::string& err, cudaStream_t st) {
-    return plan_fp8_with([&](uint32_t N, uint32_t) { return device_policy_stats(a, b, m, n, k, N, st); }, m, n, k,
-                         max_moduli, reconstruction, fixed_bits, p, err);
+int plan_digit_device(int32_t format, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                      uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_digit_plan& p,
+                      std::string& err, cudaStream_t st) {
+    return plan_digit_with(
+        format, [&](uint32_t N, uint32_t) { return device_policy_stats(a, b, m, n, k, N, st); }, m, n, k, max_moduli,
+        reconstruction, fixed_bits, p, err);
 }
 
 static void with_stream(int device_id, const std::function<void(cudaStream_t)>& f) {
@@ -135,8 +143,9 @@ static void with_stream(int device_id, const std::function<void(cudaStream_t)>& 
 
 // The whole call as Context::gemm makes it: A and B to the device, the plan from device statistics, the
 // pipeline, C back. Returns OZTT_OK, or an error code with its message (C is then untouched).
-int run_ii_fp8_planned(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
-                       uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_fp8_plan& p, std::string& err) {
+int run_ii_digit_planned(int device_id, int32_t format, const double* a, const double* b, double* c, uint64_t m,
+                         uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_digit_plan& p,
+                         std::string& err) {
     char buf[1024];
     int inner = OZTT_OK;
     const int rc = guarded(buf, sizeof buf, [&] {
@@ -144,11 +153,11 @@ int run_ii_fp8_planned(int device_id, const double* a, const double* b, double* 
             DevBuf da(st, m * k * 8), db(st, k * n * 8);
             OZTT_CUDA(cudaMemcpyAsync(da.p, a, m * k * 8, cudaMemcpyHostToDevice, st));
             OZTT_CUDA(cudaMemcpyAsync(db.p, b, k * n * 8, cudaMemcpyHostToDevice, st));
-            inner = plan_fp8_device(da.as<double>(), db.as<double>(), m, n, k, max_moduli, reconstruction, 0, p, err,
-                                    st);
+            inner = plan_digit_device(format, da.as<double>(), db.as<double>(), m, n, k, max_moduli, reconstruction, 0,
+                                      p, err, st);
             if (inner != OZTT_OK) return;
             DevBuf dc(st, m * n * 8);
-            run_ii_fp8_device(da.as<double>(), db.as<double>(), dc.as<double>(), m, n, k, p, st);
+            run_ii_digit_device(da.as<double>(), db.as<double>(), dc.as<double>(), m, n, k, p, st);
             OZTT_CUDA(cudaMemcpyAsync(c, dc.p, m * n * 8, cudaMemcpyDeviceToHost, st));
             OZTT_CUDA(cudaStreamSynchronize(st));
         });
@@ -164,21 +173,22 @@ using oztt::guarded;
 
 extern "C" {
 
-int oztt_ii_fp8_plan_device(int device_id, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
-                            uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan* plan,
-                            void* stream, char* err, size_t errlen) {
+int oztt_ii_digit_plan_device(int device_id, int32_t format, const double* a, const double* b, uint64_t m,
+                              uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits,
+                              oztt_digit_plan* plan, void* stream, char* err, size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!a || !b || !plan) throw Error(OZTT_EINVAL, "null argument");
         oztt::open_device(device_id);
         std::string msg;
-        const int rc = oztt::plan_fp8_device(a, b, m, n, k, max_moduli, reconstruction, fixed_bits, *plan, msg,
+        const int rc = oztt::plan_digit_device(format, a, b, m, n, k, max_moduli, reconstruction, fixed_bits, *plan,
+                                               msg,
                                              reinterpret_cast<cudaStream_t>(stream));
         if (rc != OZTT_OK) throw Error(rc, msg);
     });
 }
 
-int oztt_ii_fp8_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
-                    const oztt_fp8_plan* plan, char* err, size_t errlen) {
+int oztt_ii_digit_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                    const oztt_digit_plan* plan, char* err, size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!a || !b || !c || !plan) throw Error(OZTT_EINVAL, "null argument");
         if (!m || !n || !k) throw Error(OZTT_EINVAL, "matrix dimensions are zero");
@@ -186,53 +196,53 @@ int oztt_ii_fp8_run(int device_id, const double* a, const double* b, double* c, 
             oztt::DevBuf da(st, m * k * 8), db(st, k * n * 8), dc(st, m * n * 8);
             OZTT_CUDA(cudaMemcpyAsync(da.p, a, m * k * 8, cudaMemcpyHostToDevice, st));
             OZTT_CUDA(cudaMemcpyAsync(db.p, b, k * n * 8, cudaMemcpyHostToDevice, st));
-            oztt::run_ii_fp8_device(da.as<double>(), db.as<double>(), dc.as<double>(), m, n, k, *plan, st);
+            oztt::run_ii_digit_device(da.as<double>(), db.as<double>(), dc.as<double>(), m, n, k, *plan, st);
             OZTT_CUDA(cudaMemcpyAsync(c, dc.p, m * n * 8, cudaMemcpyDeviceToHost, st));
             OZTT_CUDA(cudaStreamSynchronize(st));
         });
     });
 }
 
-int oztt_ii_fp8_run_device(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
-                           uint64_t k, const oztt_fp8_plan* plan, void* stream, double* stage_ms, char* err,
+int oztt_ii_digit_run_device(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                           uint64_t k, const oztt_digit_plan* plan, void* stream, double* stage_ms, char* err,
                            size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!a || !b || !c || !plan) throw Error(OZTT_EINVAL, "null argument");
         if (!m || !n || !k) throw Error(OZTT_EINVAL, "matrix dimensions are zero");
         oztt::open_device(device_id);
-        oztt::run_ii_fp8_device(a, b, c, m, n, k, *plan, reinterpret_cast<cudaStream_t>(stream), stage_ms);
+        oztt::run_ii_digit_device(a, b, c, m, n, k, *plan, reinterpret_cast<cudaStream_t>(stream), stage_ms);
     });
 }
 
-int oztt_ii_fp8_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
-                           const oztt_fp8_plan* plan, int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err,
+int oztt_ii_digit_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
+                           const oztt_digit_plan* plan, int8_t* planes, uint64_t mp, uint64_t kp, void* stream, char* err,
                            size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!a || !delta || !plan || !planes || lda < k || mp < m || kp < k)
-            throw Error(OZTT_EINVAL, "fp8_split_rows: bad arguments");
-        oztt::check_fp8_plan(*plan);
+            throw Error(OZTT_EINVAL, "digit_split_rows: bad arguments");
+        oztt::check_digit_plan(*plan);
         oztt::launch_digit_split_rows(a, m, k, lda, delta, *plan, planes, mp, kp,
                                       reinterpret_cast<cudaStream_t>(stream));
     });
 }
 
-int oztt_ii_fp8_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
-                           const oztt_fp8_plan* plan, int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err,
+int oztt_ii_digit_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
+                           const oztt_digit_plan* plan, int8_t* planes, uint64_t np, uint64_t kp, void* stream, char* err,
                            size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!b || !delta || !plan || !planes || ldb < n || np < n || kp < k)
-            throw Error(OZTT_EINVAL, "fp8_split_cols: bad arguments");
-        oztt::check_fp8_plan(*plan);
+            throw Error(OZTT_EINVAL, "digit_split_cols: bad arguments");
+        oztt::check_digit_plan(*plan);
         oztt::launch_digit_split_cols(b, k, n, ldb, delta, *plan, planes, np, kp,
                                       reinterpret_cast<cudaStream_t>(stream));
     });
 }
 
-int oztt_ii_fp8_digit_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp, uint64_t np, uint64_t kp,
-                           const oztt_fp8_plan* plan, int32_t mode, void* out, void* stream, char* err, size_t errlen) {
+int oztt_ii_digit_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp, uint64_t np, uint64_t kp,
+                           const oztt_digit_plan* plan, int32_t mode, void* out, void* stream, char* err, size_t errlen) {
     return guarded(err, errlen, [&] {
-        if (!a_planes || !b_planes || !plan || !out) throw Error(OZTT_EINVAL, "fp8_digit_gemm: null argument");
-        oztt::check_fp8_plan(*plan);
+        if (!a_planes || !b_planes || !plan || !out) throw Error(OZTT_EINVAL, "digit_gemm: null argument");
+        oztt::check_digit_plan(*plan);
         cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
         oztt::DevBuf word(st, 16);
         OZTT_CUDA(cudaMemsetAsync(word.p, 0, 16, st));
@@ -244,13 +254,13 @@ int oztt_ii_fp8_digit_gemm(const int8_t* a_planes, const int8_t* b_planes, uint6
     });
 }
 
-int oztt_ii_fp8_recon(const uint16_t* k_digits, uint64_t mp, uint64_t np, const int32_t* delta_a,
-                      const int32_t* delta_b, const oztt_fp8_plan* plan, double* c, uint64_t m, uint64_t n,
+int oztt_ii_digit_recon(const uint16_t* k_digits, uint64_t mp, uint64_t np, const int32_t* delta_a,
+                      const int32_t* delta_b, const oztt_digit_plan* plan, double* c, uint64_t m, uint64_t n,
                       uint64_t ldc, void* stream, char* err, size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!k_digits || !delta_a || !delta_b || !plan || !c || ldc < n)
-            throw Error(OZTT_EINVAL, "fp8_recon: bad arguments");
-        oztt::check_fp8_plan(*plan);
+            throw Error(OZTT_EINVAL, "digit_recon: bad arguments");
+        oztt::check_digit_plan(*plan);
         oztt::launch_recon_u16(k_digits, mp, np, delta_a, delta_b, plan->base, c, m, n, ldc,
                                reinterpret_cast<cudaStream_t>(stream));
     });

@@ -69,15 +69,17 @@ int plan_ii_int8_with(const std::function<PolicyStats(uint32_t, uint32_t)>& stat
                       uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan& p,
                       std::string& err);
 
-// Scheme II FP8 digits (planner_digit.cpp).
-int plan_fp8_with(const std::function<PolicyStats(uint32_t, uint32_t)>& stats, uint64_t m, uint64_t n, uint64_t k,
-                  uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan& p, std::string& err);
-int plan_fp8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
-             int32_t reconstruction, int32_t fixed_bits, oztt_fp8_plan& p, std::string& err);
+// Scheme II digit formats: FP8, BF16, FP16, TF32 (planner_digit.cpp); format is an OZTT_FMT_* value.
+int plan_digit_with(int32_t format, const std::function<PolicyStats(uint32_t, uint32_t)>& stats, uint64_t m,
+                    uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits,
+                    oztt_digit_plan& p, std::string& err);
+int plan_digit(int32_t format, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+               uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_digit_plan& p, std::string& err);
 
-// Scheme I format constants (ozaki1/param.hpp, ozaki1/format.hpp): radix, digit bound, normalization
-// target 2^nshift, BF16 rounding of the maxima (1 up, 0 truncate), exact accumulator bits, Int32 partial
-// products.
+// Scheme I format constants (ozaki1/param.hpp:47-70, ozaki1/format.hpp:32-97): radix, digit bound,
+// normalization target 2^nshift, BF16 rounding of the maxima (1 up, 0 truncate), exact accumulator bits,
+// Int32 partial products. BF16, FP16 and TF32 share radix 64 and digits +-32 (only their transport
+// formats differ on the reference's device).
 struct I1Format {
     int32_t format;  // OZTT_FMT_*
     double radix, dmax;
@@ -87,6 +89,20 @@ struct I1Format {
 };
 inline constexpr I1Format kI1Int8{OZTT_FMT_INT8, 254.0, 127.0, -1, 1u, 31u, true};
 inline constexpr I1Format kI1Fp8{OZTT_FMT_FP8, 32.0, 16.0, -1, 0u, 24u, false};
+inline constexpr I1Format kI1Bf16{OZTT_FMT_BF16, 64.0, 32.0, -1, 0u, 24u, false};
+inline constexpr I1Format kI1Fp16{OZTT_FMT_FP16, 64.0, 32.0, -1, 0u, 24u, false};
+inline constexpr I1Format kI1Tf32{OZTT_FMT_TF32, 64.0, 32.0, -1, 0u, 24u, false};
+// The constants of a built format (INT8, FP8, BF16, FP16, TF32), or null.
+inline const I1Format* i1_format(int32_t format) {
+    switch (format) {
+    case OZTT_FMT_INT8: return &kI1Int8;
+    case OZTT_FMT_FP8: return &kI1Fp8;
+    case OZTT_FMT_BF16: return &kI1Bf16;
+    case OZTT_FMT_FP16: return &kI1Fp16;
+    case OZTT_FMT_TF32: return &kI1Tf32;
+    default: return nullptr;
+    }
+}
 // Scheme I (planner1.cpp): the slice count oz_fp64_p selects for row-major a (m x k), b (k x n) with padded
 // planning dimensions M, N, K; and the whole plan (slices > 0 fixes p).
 int select_slices(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,

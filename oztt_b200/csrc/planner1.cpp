@@ -591,7 +591,12 @@ extern "C" int oztt_i_int8_plan(const double* a, const double* b, uint64_t m, ui
     return plan_i_c(a, b, m, n, k, slices, oztt::kI1Int8, plan, err, errlen);
 }
 
-extern "C" int oztt_i_fp8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
-                               uint32_t slices, oztt_i_plan* plan, char* err, size_t errlen) {
-    return plan_i_c(a, b, m, n, k, slices, oztt::kI1Fp8, plan, err, errlen);
+extern "C" int oztt_i_format_plan(int32_t format, const double* a, const double* b, uint64_t m, uint64_t n,
+                                  uint64_t k, uint32_t slices, oztt_i_plan* plan, char* err, size_t errlen) {
+    const oztt::I1Format* f = oztt::i1_format(format);
+    if (!f) {
+        if (err && errlen) std::snprintf(err, errlen, "%s", "format is unknown or was not built");
+        return OZTT_EINVAL;
+    }
+    return plan_i_c(a, b, m, n, k, slices, *f, plan, err, errlen);
 }

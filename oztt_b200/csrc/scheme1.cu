@@ -1,14 +1,15 @@
 // SPDX-License-Identifier: Apache-2.0
 //
-// Ozaki scheme I with INT8 or FP8 slices on sm_100a (reference: src/ozaki1.cpp:192-282).
+// Ozaki scheme I with INT8, FP8, BF16, FP16 or TF32 slices on sm_100a (reference: src/ozaki1.cpp:192-282).
 //
 //   scale        the scheme II scaling kernels with the scheme I target: delta = -1 - e
 //                (OZ1_NSHIFT = -1; the maxima rounded up to BF16 for INT8, CEIL mode 1, truncated for
-//                FP8, CEIL mode 0: ozaki1/format.hpp:79-97)
+//                FP8, BF16, FP16 and TF32, CEIL mode 0: ozaki1/format.hpp:79-97)
 //   slice        p slices per element: INT8 radix 254, digits in [-127, 127], t *= 254 by the
 //                Dekker-split triple-float product (tfMulR of sfpu_tf_proc.h:108-133); FP8 radix 32,
-//                digits in [-16, 16] (integers e4m3 holds; stored as int8), t *= 32 by tfMulP2
-//                (sfpu_tf_proc.h:160-169); then d = clamp(rint(t0)), t0 -= d (slice_tf_body.h). The
+//                digits in [-16, 16], and BF16/FP16/TF32 radix 64, digits in [-32, 32] (integers the
+//                formats hold; stored as int8), t *= radix by tfMulP2 (sfpu_tf_proc.h:160-169); then
+//                d = clamp(rint(t0)), t0 -= d (slice_tf_body.h). The
 //                binary32 operation sequence is the reference's, with round-to-nearest-even and
 //                flush-to-zero, two elements per packed-FP32 instruction, so the slices are
 //                bit-identical. Layout: A [p][mp][kp], B transposed [p][np][kp].
@@ -122,13 +123,13 @@ __device__ __forceinline__ void tf_load1(double xv, int32_t d, float& x0, float&
     x2 = f32_mul(f32_mul(f32_add(__uint_as_float(craw), -8388608.0f), sc), 0.0078125f);
 }
 
-// One slice of two elements: t *= radix (P2: 32 by tfMulP2; else 254 by tfMulR), d = clamp(rint(t0),
+// One slice of two elements: t *= radix (P2: 32 or 64 by tfMulP2; else 254 by tfMulR), d = clamp(rint(t0),
 // +-dmax), t0 -= d. |t0| <= radix here, inside the range of rint2 (the 1.5*2^23 rounding, whose values
 // equal cvt.rni's).
 template <bool P2>
-__device__ __forceinline__ f32x2 next_digit2(f32x2& x0, f32x2& x1, f32x2& x2, float dmax, f32x2 nz) {
+__device__ __forceinline__ f32x2 next_digit2(f32x2& x0, f32x2& x1, f32x2& x2, float radix, float dmax, f32x2 nz) {
     if constexpr (P2)
-        tf_mul_p2(x0, x1, x2, splat2(32.0f), nz);
+        tf_mul_p2(x0, x1, x2, splat2(radix), nz);
     else
         tf_mul_254(x0, x1, x2, nz);
     float da, db;
@@ -153,8 +154,8 @@ __device__ __forceinline__ uint32_t pack_digits4(f32x2 d01, f32x2 d23) {
 
 // 16 elements -> p slices of 16 bytes each; element states stay in registers across the slices.
 template <bool P2>
-__device__ __forceinline__ void slice16(const double (&x)[16], int32_t d, int p, float dmax, float nzf, int8_t* dst,
-                                        uint64_t plane) {
+__device__ __forceinline__ void slice16(const double (&x)[16], int32_t d, int p, float radix, float dmax, float nzf,
+                                        int8_t* dst, uint64_t plane) {
     const f32x2 nz = splat2(nzf);
     f32x2 s0[8], s1[8], s2[8];
 #pragma unroll
@@ -169,7 +170,7 @@ __device__ __forceinline__ void slice16(const double (&x)[16], int32_t d, int p,
     for (int i = 0; i < p; ++i) {
         f32x2 dg[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) dg[e] = next_digit2<P2>(s0[e], s1[e], s2[e], dmax, nz);
+        for (int e = 0; e < 8; ++e) dg[e] = next_digit2<P2>(s0[e], s1[e], s2[e], radix, dmax, nz);
         *reinterpret_cast<uint4*>(dst + (uint64_t)i * plane) =
             make_uint4(pack_digits4(dg[0], dg[1]), pack_digits4(dg[2], dg[3]), pack_digits4(dg[4], dg[5]),
                        pack_digits4(dg[6], dg[7]));
@@ -179,8 +180,8 @@ __device__ __forceinline__ void slice16(const double (&x)[16], int32_t d, int p,
 template <bool P2>
 __global__ void __launch_bounds__(256) slice_rows_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
                                                          uint64_t lda, const int32_t* __restrict__ delta, int p,
-                                                         float dmax, float nz, int8_t* __restrict__ planes,
-                                                         uint64_t mp, uint64_t kp) {
+                                                         float radix, float dmax, float nz,
+                                                         int8_t* __restrict__ planes, uint64_t mp, uint64_t kp) {
     const uint64_t chunks = kp >> 4, total = mp * chunks, plane = mp * kp;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
          t += (uint64_t)gridDim.x * blockDim.x) {
@@ -199,15 +200,15 @@ __global__ void __launch_bounds__(256) slice_rows_kernel(const double* __restric
 #pragma unroll
             for (int e = 0; e < 16; ++e) x[e] = (in_row && k0 + e < k) ? __ldg(src + e) : 0.0;
         }
-        slice16<P2>(x, in_row ? __ldg(delta + row) : 0, p, dmax, nz, planes + row * kp + k0, plane);
+        slice16<P2>(x, in_row ? __ldg(delta + row) : 0, p, radix, dmax, nz, planes + row * kp + k0, plane);
     }
 }
 
 template <bool P2>
 __global__ void __launch_bounds__(256) slice_cols_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
                                                          uint64_t ldb, const int32_t* __restrict__ delta, int p,
-                                                         float dmax, float nz, int8_t* __restrict__ planes,
-                                                         uint64_t np, uint64_t kp) {
+                                                         float radix, float dmax, float nz,
+                                                         int8_t* __restrict__ planes, uint64_t np, uint64_t kp) {
     const int lane = threadIdx.x & 31;
     const uint64_t col_groups = np >> 4, total = col_groups * (kp >> 5), plane = np * kp;
     for (uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total;
@@ -218,13 +219,13 @@ __global__ void __launch_bounds__(256) slice_cols_kernel(const double* __restric
         double x[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) x[e] = (in_col && r0 + e < k) ? __ldg(b + (r0 + e) * ldb + col) : 0.0;
-        slice16<P2>(x, in_col ? __ldg(delta + col) : 0, p, dmax, nz, planes + col * kp + r0, plane);
+        slice16<P2>(x, in_col ? __ldg(delta + col) : 0, p, radix, dmax, nz, planes + col * kp + r0, plane);
     }
 }
 
 // ---- exact Horner reconstruction ------------------------------------------------------------
 constexpr int HW = 6;  // 192-bit two's complement: |S| < 2^32 r^(p-1): < 2^152 for r = 254, p <= 16,
-                       // < 2^187 for r = 32, p <= 32
+                       // < 2^187 for r = 32, p <= 32, < 2^188 for r = 64, p <= 27
 
 struct HornerConst {
     int32_t p;
@@ -342,7 +343,7 @@ int sm_count() {
 }  // namespace
 
 // 64-bit significand and exponent of radix^-(L+2), from the long double quotient as the reference
-// forms it (exact for radix 32).
+// forms it (exact for the power-of-two radices 32 and 64).
 void scheme1_radix_scale(int p, uint32_t radix, uint64_t& W, int32_t& qw) {
     long double w = 1.0L;
     for (int i = 0; i < p + 1; ++i) w /= (long double)radix;
@@ -363,7 +364,9 @@ struct I1Dev {
 I1Dev i1_dev(int format) {
     if (format == OZTT_FMT_FP8) return {32u, 16.0f, 0u, 32};
     if (format == OZTT_FMT_INT8) return {254u, 127.0f, 1u, 16};
-    throw Error(OZTT_EINVAL, "scheme I: the format must be INT8 or FP8");
+    // BF16, FP16, TF32: radix 64, digits +-32 (|S| < 2^32 64^26 < 2^188 for p <= 27)
+    if (format == OZTT_FMT_BF16 || format == OZTT_FMT_FP16 || format == OZTT_FMT_TF32) return {64u, 32.0f, 0u, 27};
+    throw Error(OZTT_EINVAL, "scheme I: the format must be INT8, FP8, BF16, FP16 or TF32");
 }
 
 void launch_slice_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int p, int format,
@@ -373,10 +376,12 @@ void launch_slice_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, co
     const uint64_t total = mp * (kp / 16);
     if (!total) return;
     const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 32);
-    if (f.radix == 32u)
-        slice_rows_kernel<true><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, p, f.dmax, -0.0f, planes, mp, kp);
+    if (f.radix != 254u)
+        slice_rows_kernel<true><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, p, (float)f.radix, f.dmax, -0.0f, planes,
+                                                        mp, kp);
     else
-        slice_rows_kernel<false><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, p, f.dmax, -0.0f, planes, mp, kp);
+        slice_rows_kernel<false><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, p, (float)f.radix, f.dmax, -0.0f, planes,
+                                                         mp, kp);
     OZTT_CUDA(cudaGetLastError());
 }
 
@@ -387,10 +392,12 @@ void launch_slice_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, co
     const uint64_t warps = (np / 16) * (kp / 32);
     if (!warps) return;
     const unsigned blocks = (unsigned)std::min<uint64_t>((warps + 7) / 8, (uint64_t)sm_count() * 32);
-    if (f.radix == 32u)
-        slice_cols_kernel<true><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, p, f.dmax, -0.0f, planes, np, kp);
+    if (f.radix != 254u)
+        slice_cols_kernel<true><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, p, (float)f.radix, f.dmax, -0.0f, planes,
+                                                        np, kp);
     else
-        slice_cols_kernel<false><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, p, f.dmax, -0.0f, planes, np, kp);
+        slice_cols_kernel<false><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, p, (float)f.radix, f.dmax, -0.0f, planes,
+                                                         np, kp);
     OZTT_CUDA(cudaGetLastError());
 }
 
@@ -430,12 +437,12 @@ void run_i_device(const double* a, const double* b, double* c, uint64_t m, uint6
     const int p = plan.p, format = plan.format;
     const I1Dev f = i1_dev(format);
     if (p < 1 || p > f.pmax)
-        throw Error(OZTT_EINVAL, "scheme I: the number of slices must be 1.." + std::to_string(f.pmax) + " for " +
-                                     (format == OZTT_FMT_FP8 ? "FP8" : "INT8"));
+        throw Error(OZTT_EINVAL, "scheme I: the number of slices must be 1.." + std::to_string(f.pmax) +
+                                     " for radix " + std::to_string(f.radix));
     if (plan.radix != (int32_t)f.radix || plan.dmax != (int32_t)f.dmax)
         throw Error(OZTT_EINVAL, "scheme I: the plan's radix and digit bound do not match its format");
     // The diagonal sums are exact in the s32 accumulators while (L+1) K dmax^2 <= 2^31 - 1 (the planner
-    // guarantees it for INT8; FP8 inputs beyond it would need the reference's FP32 K blocks).
+    // guarantees it for INT8; FP inputs beyond it would need the reference's FP32 K blocks).
     const uint64_t d2 = (uint64_t)f.dmax * (uint64_t)f.dmax;
     if ((uint64_t)p * round_up(k, 32) > (uint64_t)INT32_MAX / d2)
         throw Error(OZTT_ERUNTIME, "Ozaki scheme I: k*slices is too large for exact 32-bit diagonal sums in this "

@@ -25,11 +25,12 @@
 // contiguous). B is read row-major (k x n, ldb) and written transposed, [S][np][kp] int8, so that
 // both GEMM operands are K-major for the tensor cores. Padding rows/columns are written as zeros.
 //
-// FP8 digits (the DIG variants): the same residues are then split into the two or three e4m3 digits of
-// their modulus (modslice_digit.cpp:193-226 with sparse_fix.h:52-72) and written as nplane digit planes
-// [nplane][mp][kp] / [nplane][np][kp], plane poff_s + 0 = l, + 1 = h, + 2 = s. Every digit is an integer
-// in [-32, 32] that e4m3 represents exactly; the planes hold it as an int8, the operand type of the
-// tensor-core products (which are then exact in s32 for any K).
+// Digit formats (the DIG variants; FP8, BF16, FP16, TF32): the same residues are then split into the one to
+// three digits of their modulus (modslice_digit.cpp:193-226 with sparse_fix.h:52-72) and written as nplane
+// digit planes [nplane][mp][kp] / [nplane][np][kp], plane poff_s + 0 = l (or the residue of a one-digit
+// modulus), + 1 = h, + 2 = s. Every digit is an integer in [-32, 32] that the format represents exactly; the
+// planes hold it as an int8, the operand type of the tensor-core products (which are then exact in s32 for
+// any K).
 #include <algorithm>
 
 #include "oztt_common.cuh"
@@ -304,6 +305,7 @@ __device__ __forceinline__ void sqs_fix(float& l, float& h, float q) {
 }
 
 // Writes the digit planes of 16 elements (8 pairs x ND digits of A') for every modulus.
+//   one digit (ONE): the residue r itself (|r| <= 32)
 //   rounding to nearest (SQ, WIDE, SQS): h = rint(fl(r * qinv)), l = r - q h (exact); SQS then sqs_fix
 //   Karatsuba (KAR): h = rint((r + sgn(r) (q/2 - 1/2)) * qinv), l = r - q h, s = h + l, sgn(+-0) = +1
 // The products r*qinv are single roundings like the reference's MulS; everything else is exact.
@@ -322,7 +324,9 @@ __device__ __forceinline__ void store_digits(const f32x2 (&dg)[8][ND], const Spl
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const f32x2 r = residue2<ND>(dg[e], negm, ri, c0, c1, c2, c3, nz);
-            if (mode == OZTT_SPLIT_KAR) {
+            if (mode == OZTT_SPLIT_ONE) {
+                l[e] = r;
+            } else if (mode == OZTT_SPLIT_KAR) {
                 float r0, r1;
                 unpk2(r, r0, r1);
                 const float half = q * 0.5f - 0.5f;
@@ -347,6 +351,7 @@ __device__ __forceinline__ void store_digits(const f32x2 (&dg)[8][ND], const Spl
         int8_t* p = dst + (uint64_t)sc.poff[s] * plane;
         *reinterpret_cast<uint4*>(p) =
             make_uint4(pack4(l[0], l[1]), pack4(l[2], l[3]), pack4(l[4], l[5]), pack4(l[6], l[7]));
+        if (mode == OZTT_SPLIT_ONE) continue;
         *reinterpret_cast<uint4*>(p + plane) =
             make_uint4(pack4(h[0], h[1]), pack4(h[2], h[3]), pack4(h[4], h[5]), pack4(h[6], h[7]));
         if (mode == OZTT_SPLIT_KAR)
@@ -523,7 +528,7 @@ void launch_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, co
     split_cols_any<false>(b, k, n, ldb, delta, p.nd, split_const(p), planes, np, kp, st);
 }
 
-static SplitConst digit_const(const oztt_fp8_plan& fp) {
+static SplitConst digit_const(const oztt_digit_plan& fp) {
     SplitConst sc = split_const(fp.base);
     for (int s = 0; s < fp.base.S; ++s) {
         sc.q[s] = (float)fp.q[s];
@@ -534,14 +539,14 @@ static SplitConst digit_const(const oztt_fp8_plan& fp) {
     return sc;
 }
 
-// FP8 digit planes of A ([nplane][mp][kp]) and of B transposed ([nplane][np][kp]).
+// Digit planes of A ([nplane][mp][kp]) and of B transposed ([nplane][np][kp]).
 void launch_digit_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
-                             const oztt_fp8_plan& fp, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
+                             const oztt_digit_plan& fp, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
     split_rows_any<true>(a, m, k, lda, delta, fp.base.nd, digit_const(fp), planes, mp, kp, st);
 }
 
 void launch_digit_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
-                             const oztt_fp8_plan& fp, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
+                             const oztt_digit_plan& fp, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
     split_cols_any<true>(b, k, n, ldb, delta, fp.base.nd, digit_const(fp), planes, np, kp, st);
 }
 

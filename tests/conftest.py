@@ -16,7 +16,7 @@ for p in (str(ROOT), str(ROOT / "tests")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
-from oracle_lib import Oracle, RefEmu, RefPlan, RefPlan1, RefPlanF8  # noqa: E402
+from oracle_lib import Oracle, RefEmu, RefPlan, RefPlan1, RefPlanDigit  # noqa: E402
 
 
 def pytest_configure(config):
@@ -45,6 +45,14 @@ def ref_plan1():
 
 
 @pytest.fixture(scope="session")
+def ref_plan1_r64():
+    try:
+        return RefPlan1(r64=True)
+    except FileNotFoundError:
+        pytest.skip("oracle/_ref was not built on this machine (needs the reference tree)")
+
+
+@pytest.fixture(scope="session")
 def ref_plan1_f8():
     try:
         return RefPlan1(fp8=True)
@@ -53,9 +61,25 @@ def ref_plan1_f8():
 
 
 @pytest.fixture(scope="session")
+def ref_plan_digit():
+    """ref_plan_digit(fmt): the reference's planner compiled for that digit format (skips without it)."""
+    cache = {}
+
+    def get(fmt):
+        if fmt not in cache:
+            try:
+                cache[fmt] = RefPlanDigit(fmt)
+            except FileNotFoundError:
+                pytest.skip("oracle/_ref was not built on this machine (needs the reference tree)")
+        return cache[fmt]
+
+    return get
+
+
+@pytest.fixture(scope="session")
 def ref_plan_f8():
     try:
-        return RefPlanF8()
+        return RefPlanDigit(4)
     except FileNotFoundError:
         pytest.skip("oracle/_ref was not built on this machine (needs the reference tree)")
 

@@ -206,6 +206,12 @@ int main(int argc, char** argv) {
             o.reconstruction = ozTTgemm::Reconstruction::TwoPass;
             check(ctx, o, 64, 64, 64, Pattern::Uniform);
         }
+        if (ozTTgemm::is_available(ozTTgemm::Format::BF16)) {
+            ozTTgemm::Options o;
+            o.scheme = ozTTgemm::Scheme::I;
+            o.format = ozTTgemm::Format::BF16;
+            check(ctx, o, 64, 64, 32768, Pattern::Nonnegative);  // beyond the reference's exact FP32 K block
+        }
         ozTTgemm::Options o;
         o.format = first;
         std::vector<double> overlap{1, 2, 3, 4};

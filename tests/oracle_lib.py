@@ -18,7 +18,6 @@ ORACLE_SO = ROOT / "oracle" / "liboz2oracle.so"
 REF_PLAN_SO = ROOT / "oracle" / "_ref" / "libozref_plan.so"
 REF_EMU_SO = ROOT / "oracle" / "_ref" / "libozref_emu.so"
 REF_PLAN1_SO = ROOT / "oracle" / "_ref" / "libozref_plan1.so"
-REF_PLAN_F8_SO = ROOT / "oracle" / "_ref" / "libozref_plan_f8.so"
 REF_PLAN1_F8_SO = ROOT / "oracle" / "_ref" / "libozref_plan1_f8.so"
 
 MAXS, MAXRP = 24, 5
@@ -88,11 +87,11 @@ class Oracle:
         L.ozo_i_recon_exact_fmt.argtypes = [P, ctypes.c_int, ctypes.c_int, u64, u64, P, P, P, u64]
         L.ozo_i_emulate_fmt.argtypes = [P, P, P, u64, u64, u64, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         L.ozo_crt_plan.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(OzoPlan)]
-        L.ozo_fp8_split.argtypes = [P, u64, u64, u64, ctypes.c_int, P, ctypes.POINTER(OzoPlan), P, P]
-        L.ozo_fp8_gemm.argtypes = [P, P, P, u64, u64, u64, P]
-        L.ozo_fp8_compose.argtypes = [P, P, ctypes.POINTER(OzoPlan), u64, u64, P]
+        L.ozo_digit_split.argtypes = [P, u64, u64, u64, ctypes.c_int, P, ctypes.POINTER(OzoPlan), P, P]
+        L.ozo_digit_gemm.argtypes = [P, P, P, u64, u64, u64, P]
+        L.ozo_digit_compose.argtypes = [P, P, ctypes.POINTER(OzoPlan), u64, u64, P]
         L.ozo_recon_faithful_residue.argtypes = [P, u64, u64, P, P, ctypes.POINTER(OzoPlan), P, u64]
-        L.ozo_fp8_emulate.argtypes = [P, P, P, u64, u64, u64, P, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
+        L.ozo_digit_emulate.argtypes = [P, P, P, u64, u64, u64, P, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
 
     # -- generators ---------------------------------------------------------------------------
     def gen_inputs(self, m: int, n: int, k: int, phi: float, seed: int) -> tuple[np.ndarray, np.ndarray]:
@@ -161,7 +160,7 @@ class Oracle:
         return rc, c, p, err.value.decode()
 
     # -- Scheme I ------------------------------------------------------------------------------
-    # fmt: the OZTT_FMT_* value, 5 INT8 (radix 254), 4 FP8 (radix 32).
+    # fmt: the OZTT_FMT_* value, 5 INT8 (radix 254), 4 FP8 (radix 32), 0/1/2 BF16/FP16/TF32 (radix 64).
     def i_slice(self, x: np.ndarray, rows: int, cols: int, col_mode: int, delta: np.ndarray, p: int,
                 fmt: int = 5) -> np.ndarray:
         out = np.zeros(p * rows * cols, dtype=np.int8)
@@ -180,7 +179,7 @@ class Oracle:
         c = np.zeros(M * N)
         if exact:
             self.lib.ozo_i_recon_exact_fmt(ptr(pd), p, fmt, M, N, ptr(dA), ptr(dB), ptr(c), N)
-        elif fmt == 4:
+        elif fmt != 5:
             self.lib.ozo_i_recon_faithful_deferred(ptr(pd), p, fmt, K, M, N, ptr(dA), ptr(dB), ptr(c), N)
         else:
             self.lib.ozo_i_recon_faithful(ptr(pd), p, M, N, ptr(dA), ptr(dB), ptr(c), N)
@@ -192,28 +191,28 @@ class Oracle:
         return c
 
     # -- Scheme II FP8 digits ---------------------------------------------------------------
-    # `fp` is an oztt_fp8_plan ctypes structure (the product's FP8Plan or the reference planner's).
+    # `fp` is an oztt_digit_plan ctypes structure (the product's DigitPlan or the reference planner's).
     def crt_plan(self, moduli, b: int, two_pass: int) -> OzoPlan:
         m = np.asarray(moduli, dtype=np.int32)
         p = OzoPlan()
         assert self.lib.ozo_crt_plan(ptr(m), len(m), b, two_pass, ctypes.byref(p)) == 0
         return p
 
-    def fp8_split(self, x: np.ndarray, rows: int, cols: int, col_mode: int, delta: np.ndarray, crt: OzoPlan,
+    def digit_split(self, x: np.ndarray, rows: int, cols: int, col_mode: int, delta: np.ndarray, crt: OzoPlan,
                   fp) -> tuple[int, np.ndarray]:
         out = np.zeros(fp.nplane * rows * cols, dtype=np.int8)
-        bad = self.lib.ozo_fp8_split(ptr(x), rows, cols, cols, col_mode, ptr(delta), ctypes.byref(crt),
+        bad = self.lib.ozo_digit_split(ptr(x), rows, cols, cols, col_mode, ptr(delta), ctypes.byref(crt),
                                      ctypes.byref(fp), ptr(out))
         return bad, out
 
-    def fp8_gemm(self, da: np.ndarray, db: np.ndarray, fp, M: int, N: int, K: int) -> tuple[int, np.ndarray]:
+    def digit_gemm(self, da: np.ndarray, db: np.ndarray, fp, M: int, N: int, K: int) -> tuple[int, np.ndarray]:
         out = np.zeros(fp.nout * M * N, dtype=np.int32)
-        bad = self.lib.ozo_fp8_gemm(ptr(da), ptr(db), ctypes.byref(fp), M, N, K, ptr(out))
+        bad = self.lib.ozo_digit_gemm(ptr(da), ptr(db), ctypes.byref(fp), M, N, K, ptr(out))
         return bad, out
 
-    def fp8_compose(self, P_: np.ndarray, fp, crt: OzoPlan, M: int, N: int) -> np.ndarray:
+    def digit_compose(self, P_: np.ndarray, fp, crt: OzoPlan, M: int, N: int) -> np.ndarray:
         r = np.zeros(crt.S * M * N, dtype=np.float32)
-        self.lib.ozo_fp8_compose(ptr(P_), ctypes.byref(fp), ctypes.byref(crt), M, N, ptr(r))
+        self.lib.ozo_digit_compose(ptr(P_), ctypes.byref(fp), ctypes.byref(crt), M, N, ptr(r))
         return r
 
     def recon_residue(self, r: np.ndarray, M: int, N: int, dA: np.ndarray, dB: np.ndarray, crt: OzoPlan) -> np.ndarray:
@@ -221,10 +220,10 @@ class Oracle:
         self.lib.ozo_recon_faithful_residue(ptr(r), M, N, ptr(dA), ptr(dB), ctypes.byref(crt), ptr(c), N)
         return c
 
-    def fp8_emulate(self, a, b, m, n, k, fp, exact=False) -> tuple[int, np.ndarray, str]:
+    def digit_emulate(self, a, b, m, n, k, fp, exact=False) -> tuple[int, np.ndarray, str]:
         c = np.zeros(m * n)
         err = ctypes.create_string_buffer(512)
-        rc = self.lib.ozo_fp8_emulate(ptr(a), ptr(b), ptr(c), m, n, k, ctypes.byref(fp), 1 if exact else 0, err, 512)
+        rc = self.lib.ozo_digit_emulate(ptr(a), ptr(b), ptr(c), m, n, k, ctypes.byref(fp), 1 if exact else 0, err, 512)
         return rc, c, err.value.decode()
 
     # -- metrics ------------------------------------------------------------------------------
@@ -292,36 +291,43 @@ class RefEmu:
         return s, c, [int(x) for x in mods[:max(s, 0)]]
 
 
-class RefPlanF8:
-    """The reference's Scheme II planner headers compiled for FP8 (oracle/ref_plan_f8.cpp)."""
+class RefPlanDigit:
+    """The reference's Scheme II planner headers compiled for one digit format (oracle/ref_plan_digit.cpp);
+    fmt is the OZTT_FMT_* value (4 FP8, 0 BF16, 1 FP16, 2 TF32)."""
 
-    def __init__(self, path: Path = REF_PLAN_F8_SO):
+    LIBS = {4: "libozref_plan_f8.so", 0: "libozref_plan_bf16.so", 1: "libozref_plan_fp16.so", 2: "libozref_plan_tf32.so"}
+
+    def __init__(self, fmt: int = 4):
+        path = ROOT / "oracle" / "_ref" / self.LIBS[fmt]
         if not path.exists():
             raise FileNotFoundError(str(path))
         self.lib = ctypes.CDLL(str(path))
-        self.lib.ozr_f8_choose.argtypes = [ctypes.c_uint32, ctypes.c_int, ctypes.c_int, P, P]
-        self.lib.ozr_f8_plan.argtypes = [P, P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
-                                         ctypes.c_int, ctypes.c_int, P]
+        self.lib.ozr_digit_choose.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int,
+                                              ctypes.c_int, P, P]
+        self.lib.ozr_digit_plan.argtypes = [P, P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                            ctypes.c_int, ctypes.c_int, P]
 
-    def choose(self, K: int, num_moduli: int, b_cap: int, plan_type):
+    def choose(self, K: int, num_moduli: int, b_cap: int, plan_type, M: int = 0, N: int = 0):
         out = plan_type()
         acc = ctypes.c_int()
-        ok = self.lib.ozr_f8_choose(K, num_moduli, b_cap, ctypes.byref(out), ctypes.byref(acc))
+        ok = self.lib.ozr_digit_choose(M or K, N or K, K, num_moduli, b_cap, ctypes.byref(out), ctypes.byref(acc))
         return ok, acc.value, out
 
     def plan(self, ap, bp, M, N, K, plan_type, max_moduli=0, passes=0, fixed_bits=0):
         out = plan_type()
-        rc = self.lib.ozr_f8_plan(ptr(ap), ptr(bp), M, N, K, max_moduli, passes, fixed_bits, ctypes.byref(out))
+        rc = self.lib.ozr_digit_plan(ptr(ap), ptr(bp), M, N, K, max_moduli, passes, fixed_bits, ctypes.byref(out))
         return rc, out
 
 
 class RefPlan1:
     """The reference's Scheme I slice-count selection compiled in place (oracle/ref_plan1.cpp); the FP8
-    build when fp8 is set."""
+    build when fp8 is set, the radix-64 build (BF16, FP16, TF32) when r64 is set."""
 
-    def __init__(self, path: Path = REF_PLAN1_SO, fp8: bool = False):
+    def __init__(self, path: Path = REF_PLAN1_SO, fp8: bool = False, r64: bool = False):
         if fp8:
             path = REF_PLAN1_F8_SO
+        if r64:
+            path = ROOT / "oracle" / "_ref" / "libozref_plan1_r64.so"
         if not path.exists():
             raise FileNotFoundError(str(path))
         self.lib = ctypes.CDLL(str(path))

@@ -1,15 +1,16 @@
-"""Scheme II with FP8 (e4m3) digits on the B200, stage by stage and end to end, against the oracle.
+"""Scheme II with the digit formats (FP8 e4m3, BF16, FP16, TF32) on the B200, stage by stage and end to end,
+against the oracle.
 
 Every call goes through the C ABI of liboztt.so. Bars:
-  * digit planes (every splitting method: SQ, KAR, WIDE, SQS) and the GEMM outputs P_o (int32): bit-exact
-    against the oracle's restatement of modslice_digit.cpp / sparse_fix.h and of the digit products;
+  * digit planes (every splitting method: ONE, SQ, KAR, WIDE, SQS) and the GEMM outputs P_o (int32):
+    bit-exact against the oracle's restatement of modslice_digit.cpp / sparse_fix.h and of the digit products;
   * the CRT digits of the fused composition: equal to (sum_o coeff_o P_o) y_s mod m_s computed on the host
     from the oracle's P_o, and in the same residue class as the oracle's restatement of compose.cpp;
   * the FP64 output: bit-exact against the oracle's exact CRT from residues, and within the faithful
     tolerance of the reference's own (triple-float) reconstruction;
-  * the published FP8 device hash (tools/validated/quick.csv:11, n=128) through the GPU digit planes and
-    products with the reference's composition and reconstruction restated on the host, and the
-    acceptance cases of the reference's tests/correctness.cpp through the public API.
+  * the published device hashes at n=128 (tools/validated/quick.csv:3,5,7,11) through the GPU digit planes
+    and products with the reference's composition and reconstruction restated on the host, and the
+    acceptance cases of the reference's tests/correctness.cpp through the public API for every format.
 """
 
 import numpy as np
@@ -29,8 +30,12 @@ def stream():
     return torch.cuda.current_stream().cuda_stream
 
 
+FP8, BF16, FP16, TF32 = 4, 0, 1, 2  # OZTT_FMT_* values
+FORMATS = [FP8, BF16, FP16, TF32]
+
+
 def plan_and_crt(oztt, oracle, a, b, m, n, k, **kw):
-    fp = oztt.fp8_plan(a.reshape(m, k), b.reshape(k, n), m, n, k, **kw)
+    fp = oztt.digit_plan(a.reshape(m, k), b.reshape(k, n), m, n, k, **kw)
     crt = oracle.crt_plan([fp.base.moduli[i] for i in range(fp.base.S)], fp.base.b, fp.base.two_pass)
     return fp, crt
 
@@ -49,12 +54,12 @@ def gpu_digits(oztt, X, rows, cols, col_mode, delta, fp):
     if col_mode:
         npad, kpad = round_up(cols, 256), round_up(rows, 128)
         out = torch.full((fp.nplane * npad * kpad,), 77, dtype=torch.int8, device="cuda")
-        oztt.call("oztt_ii_fp8_split_cols", X.data_ptr(), rows, cols, cols, delta.data_ptr(), fp, out.data_ptr(), npad,
+        oztt.call("oztt_ii_digit_split_cols", X.data_ptr(), rows, cols, cols, delta.data_ptr(), fp, out.data_ptr(), npad,
                   kpad, stream())
         return out, npad, kpad
     mpad, kpad = round_up(rows, 128), round_up(cols, 128)
     out = torch.full((fp.nplane * mpad * kpad,), 77, dtype=torch.int8, device="cuda")
-    oztt.call("oztt_ii_fp8_split_rows", X.data_ptr(), rows, cols, cols, delta.data_ptr(), fp, out.data_ptr(), mpad, kpad,
+    oztt.call("oztt_ii_digit_split_rows", X.data_ptr(), rows, cols, cols, delta.data_ptr(), fp, out.data_ptr(), mpad, kpad,
               stream())
     return out, mpad, kpad
 
@@ -86,10 +91,14 @@ SPLIT_CASES = [
 ]
 
 
+@pytest.mark.parametrize("fmt", [FP8, BF16, TF32])
 @pytest.mark.parametrize("m,n,k,phi,seed,kw", SPLIT_CASES)
-def test_digit_split_matches_oracle(oztt, oracle, cuda, m, n, k, phi, seed, kw):
+def test_digit_split_matches_oracle(oztt, oracle, cuda, m, n, k, phi, seed, kw, fmt):
     a, b = oracle.gen_inputs(m, n, k, phi, seed)
-    fp, crt = plan_and_crt(oztt, oracle, a, b, m, n, k, **kw)
+    if fmt != FP8 and k >= 16384:
+        k = 8192  # the 32-digit routes need K * 32^2 <= 2^24
+    fp, crt = plan_and_crt(oztt, oracle, a[:m * k], b[:k * n], m, n, k, fmt=fmt, **kw)
+    a, b = a[:m * k], b[:k * n]
     A, B = dev(a), dev(b)
     dA = gpu_scale(oztt, A, m, k, 0, fp.base.shift)
     dB = gpu_scale(oztt, B, k, n, 1, fp.base.shift)
@@ -99,9 +108,9 @@ def test_digit_split_matches_oracle(oztt, oracle, cuda, m, n, k, phi, seed, kw):
     ga, mp, kp = gpu_digits(oztt, A, m, k, 0, dA, fp)
     gb, np_, kp2 = gpu_digits(oztt, B, k, n, 1, dB, fp)
     torch.cuda.synchronize()
-    bad, ra = oracle.fp8_split(a, m, k, 0, oda, crt, fp)
+    bad, ra = oracle.digit_split(a, m, k, 0, oda, crt, fp)
     assert bad == 0
-    bad, rb = oracle.fp8_split(b, k, n, 1, odb, crt, fp)
+    bad, rb = oracle.digit_split(b, k, n, 1, odb, crt, fp)
     assert bad == 0
     ga = ga.view(fp.nplane, mp, kp).cpu().numpy()
     gb = gb.view(fp.nplane, np_, kp2).cpu().numpy()
@@ -114,16 +123,19 @@ def test_digit_split_matches_oracle(oztt, oracle, cuda, m, n, k, phi, seed, kw):
 
 def test_split_cases_cover_every_method(oztt, oracle):
     seen = set()
-    for m, n, k, phi, seed, kw in SPLIT_CASES:
-        fp = oztt.fp8_plan(None, None, m, n, k, **kw) if kw.get("fixed_bits") else None
-        if fp is not None:
-            seen |= modes_of(fp)
-    assert seen == {oztt.SPLIT_SQ, oztt.SPLIT_KAR, oztt.SPLIT_WIDE, oztt.SPLIT_SQS}
+    for fmt in (FP8, BF16):
+        for m, n, k, phi, seed, kw in SPLIT_CASES:
+            if fmt != FP8 and k >= 16384:
+                k = 8192
+            fp = oztt.digit_plan(None, None, m, n, k, fmt=fmt, **kw) if kw.get("fixed_bits") else None
+            if fp is not None:
+                seen |= modes_of(fp)
+    assert seen == {oztt.SPLIT_SQ, oztt.SPLIT_KAR, oztt.SPLIT_WIDE, oztt.SPLIT_SQS, oztt.SPLIT_ONE}
 
 
-def digit_case(oztt, oracle, m, n, k, phi, seed, kw):
+def digit_case(oztt, oracle, m, n, k, phi, seed, kw, fmt=FP8):
     a, b = oracle.gen_inputs(m, n, k, phi, seed)
-    fp, crt = plan_and_crt(oztt, oracle, a, b, m, n, k, **kw)
+    fp, crt = plan_and_crt(oztt, oracle, a, b, m, n, k, fmt=fmt, **kw)
     A, B = dev(a), dev(b)
     dA = gpu_scale(oztt, A, m, k, 0, fp.base.shift)
     dB = gpu_scale(oztt, B, k, n, 1, fp.base.shift)
@@ -138,25 +150,26 @@ GEMM_CASES = [(128, 256, 128, -1.0, 7, dict(reconstruction=1, fixed_bits=54)),
               (128, 256, 2048, 1.0, 8, dict())]
 
 
+@pytest.mark.parametrize("fmt", [FP8, BF16, TF32])
 @pytest.mark.parametrize("m,n,k,phi,seed,kw", GEMM_CASES)
-def test_digit_gemm_matches_oracle(oztt, oracle, cuda, m, n, k, phi, seed, kw):
-    a, b, fp, crt, dA, dB, ga, gb, mp, np_, kp = digit_case(oztt, oracle, m, n, k, phi, seed, kw)
+def test_digit_gemm_matches_oracle(oztt, oracle, cuda, m, n, k, phi, seed, kw, fmt):
+    a, b, fp, crt, dA, dB, ga, gb, mp, np_, kp = digit_case(oztt, oracle, m, n, k, phi, seed, kw, fmt)
     P = torch.empty(fp.nout * mp * np_, dtype=torch.int32, device="cuda")
-    oztt.call("oztt_ii_fp8_digit_gemm", ga.data_ptr(), gb.data_ptr(), mp, np_, kp, fp, 0, P.data_ptr(), stream())
+    oztt.call("oztt_ii_digit_gemm", ga.data_ptr(), gb.data_ptr(), mp, np_, kp, fp, 0, P.data_ptr(), stream())
     KD = torch.empty(fp.base.S * mp * np_, dtype=torch.int16, device="cuda")
-    oztt.call("oztt_ii_fp8_digit_gemm", ga.data_ptr(), gb.data_ptr(), mp, np_, kp, fp, 1, KD.data_ptr(), stream())
+    oztt.call("oztt_ii_digit_gemm", ga.data_ptr(), gb.data_ptr(), mp, np_, kp, fp, 1, KD.data_ptr(), stream())
     torch.cuda.synchronize()
     # oracle products over the padded planes (the padding digits are zero)
     ha = ga.view(fp.nplane, mp, kp).cpu().numpy()
     hb = gb.view(fp.nplane, np_, kp).cpu().numpy()
-    bad, op = oracle.fp8_gemm(np.ascontiguousarray(ha).reshape(-1), np.ascontiguousarray(hb).reshape(-1), fp, mp, np_,
+    bad, op = oracle.digit_gemm(np.ascontiguousarray(ha).reshape(-1), np.ascontiguousarray(hb).reshape(-1), fp, mp, np_,
                               kp)
     assert bad == 0
     assert np.array_equal(P.cpu().numpy(), op)
     # the fused composition: k_s = (sum_o coeff_o P_o) y_s mod m_s
     op = op.reshape(fp.nout, mp, np_).astype(np.int64)
     kd = KD.cpu().numpy().view(np.uint16).reshape(fp.base.S, mp, np_)
-    r = oracle.fp8_compose(np.ascontiguousarray(op.astype(np.int32)).reshape(-1), fp, crt, mp, np_).reshape(
+    r = oracle.digit_compose(np.ascontiguousarray(op.astype(np.int32)).reshape(-1), fp, crt, mp, np_).reshape(
         fp.base.S, mp, np_)
     for s in range(fp.base.S):
         mod = fp.base.moduli[s]
@@ -176,15 +189,16 @@ RUN_CASES = [(128, 128, 128, -1.0, 7, dict(reconstruction=1, fixed_bits=54)),
              (96, 96, 600, 1.0, 12, dict(reconstruction=1, fixed_bits=99, max_moduli=24))]
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("m,n,k,phi,seed,kw", RUN_CASES)
-def test_pipeline_matches_oracle(oztt, oracle, cuda, m, n, k, phi, seed, kw):
+def test_pipeline_matches_oracle(oztt, oracle, cuda, m, n, k, phi, seed, kw, fmt):
     a, b = oracle.gen_inputs(m, n, k, phi, seed)
-    fp, crt = plan_and_crt(oztt, oracle, a, b, m, n, k, **kw)
-    c = oztt.fp8_run(a, b, m, n, k, fp)
-    rc, ce, err = oracle.fp8_emulate(a, b, m, n, k, fp, exact=True)
+    fp, crt = plan_and_crt(oztt, oracle, a, b, m, n, k, fmt=fmt, **kw)
+    c = oztt.digit_run(a, b, m, n, k, fp)
+    rc, ce, err = oracle.digit_emulate(a, b, m, n, k, fp, exact=True)
     assert rc == 0, err
     assert np.array_equal(c.view(np.uint64), ce.view(np.uint64))
-    rc, cf, err = oracle.fp8_emulate(a, b, m, n, k, fp)
+    rc, cf, err = oracle.digit_emulate(a, b, m, n, k, fp)
     assert rc == 0, err
     assert np.all(np.abs(c - cf).reshape(m, n) <= faithful_bound(oracle, a, b, m, n, k, crt, cf))
     hi, lo = oracle.dot2(a, b, m, n, k)
@@ -192,19 +206,24 @@ def test_pipeline_matches_oracle(oztt, oracle, cuda, m, n, k, phi, seed, kw):
     assert rel < 1e-15
 
 
-def test_published_fp8_hash_on_gpu(oztt, oracle, cuda):
-    """tools/validated/quick.csv:11: the GPU digit planes and products with the reference's composition and
-    triple-float reconstruction restated on the host give every output bit of the reference device."""
+PUBLISHED_128 = {FP8: "20046e5bb3816cbb", BF16: "13abe4ac7f292f42", FP16: "1811cf560959e61d",
+                 TF32: "9a8f2780d4b9976b"}
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_published_hash_on_gpu(oztt, oracle, cuda, fmt):
+    """tools/validated/quick.csv:3,5,7,11: the GPU digit planes and products with the reference's composition
+    and triple-float reconstruction restated on the host give every output bit of the reference device."""
     n = 128
     a, b, fp, crt, dA, dB, ga, gb, mp, np_, kp = digit_case(oztt, oracle, n, n, n, -1.0, 7,
-                                                           dict(reconstruction=1, fixed_bits=54))
+                                                           dict(reconstruction=1, fixed_bits=54), fmt)
     P = torch.empty(fp.nout * mp * np_, dtype=torch.int32, device="cuda")
-    oztt.call("oztt_ii_fp8_digit_gemm", ga.data_ptr(), gb.data_ptr(), mp, np_, kp, fp, 0, P.data_ptr(), stream())
+    oztt.call("oztt_ii_digit_gemm", ga.data_ptr(), gb.data_ptr(), mp, np_, kp, fp, 0, P.data_ptr(), stream())
     torch.cuda.synchronize()
     p = np.ascontiguousarray(P.view(fp.nout, mp, np_)[:, :n, :n].cpu().numpy())
-    r = oracle.fp8_compose(p.reshape(-1), fp, crt, n, n)
+    r = oracle.digit_compose(p.reshape(-1), fp, crt, n, n)
     c = oracle.recon_residue(r, n, n, dA.cpu().numpy(), dB.cpu().numpy(), crt)
-    assert oracle.output_hash(c) == "20046e5bb3816cbb"
+    assert oracle.output_hash(c) == PUBLISHED_128[fmt]
 
 
 PATTERNS = {"uniform": 0, "zero-A": 1, "nonnegative": 2, "scaled": 3, "cancellation": 4, "zero-row-column": 5,
@@ -214,40 +233,42 @@ CHECKS = [(64, 64, 64, "uniform", 0), (3, 5, 7, "nonnegative", 0), (65, 67, 97, 
           (1, 1, 1, "largest-maximum", 0), (5056, 64, 32, "uniform", 0), (64, 64, 64, "uniform", 2)]
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("m,n,k,pattern,recon", CHECKS)
-def test_correctness_cases(oztt, oracle, cuda, m, n, k, pattern, recon):
-    """The acceptance cases of the reference's tests/correctness.cpp with format FP8 (relative Frobenius error
-    <= 8 eps against the compensated reference)."""
+def test_correctness_cases(oztt, oracle, cuda, m, n, k, pattern, recon, fmt):
+    """The acceptance cases of the reference's tests/correctness.cpp with each digit format (relative Frobenius
+    error <= 8 eps against the compensated reference)."""
     a, b = oracle.gen_pattern(m, n, k, PATTERNS[pattern])
     c = np.full(m * n, 123.0)
-    info = oztt.Context().gemm(a, b, c, m, n, k, oztt.Options(format=oztt.Format.FP8, reconstruction=recon))
+    info = oztt.Context().gemm(a, b, c, m, n, k, oztt.Options(format=fmt, reconstruction=recon))
     assert np.all(np.isfinite(c))
     hi, lo = oracle.dot2(a, b, m, n, k)
     rel, _ = oracle.accuracy(c, hi, lo)
     assert rel <= 8 * np.finfo(float).eps, rel
-    assert info.format == oztt.Format.FP8 and info.scheme == oztt.Scheme.II
+    assert info.format == fmt and info.scheme == oztt.Scheme.II
     assert info.padded_m == round_up(m, 64) and info.padded_n == round_up(n, 64) and info.padded_k == round_up(k, 32)
     assert info.moduli >= 2 and info.integer_bits >= 53
     if recon == 2:
         assert info.reconstruction_passes == 2
 
 
-def test_context_matches_planned_run(oztt, oracle, cuda):
-    """Context::gemm with FP8 plans on the device (statistics measured there) and gives the bits of the
-    stage pipeline run with the host plan."""
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_context_matches_planned_run(oztt, oracle, cuda, fmt):
+    """Context::gemm with a digit format plans on the device (statistics measured there) and gives the bits
+    of the stage pipeline run with the host plan."""
     m, n, k = 300, 200, 500
     a, b = oracle.gen_inputs(m, n, k, 0.5, 21)
-    fp = oztt.fp8_plan(a, b, m, n, k)
+    fp = oztt.digit_plan(a, b, m, n, k, fmt=fmt)
     c = np.empty(m * n)
-    info = oztt.Context().gemm(a, b, c, m, n, k, oztt.Options(format=oztt.Format.FP8))
+    info = oztt.Context().gemm(a, b, c, m, n, k, oztt.Options(format=fmt))
     assert info.moduli == fp.base.S and info.integer_bits == fp.base.b
-    c2 = oztt.fp8_run(a, b, m, n, k, fp)
+    c2 = oztt.digit_run(a, b, m, n, k, fp)
     assert np.array_equal(c.view(np.uint64), c2.view(np.uint64))
     A, B = dev(a), dev(b)
-    fpd = oztt.fp8_plan_device(A.data_ptr(), B.data_ptr(), m, n, k, stream=stream())
+    fpd = oztt.digit_plan_device(A.data_ptr(), B.data_ptr(), m, n, k, stream=stream(), fmt=fmt)
     assert bytes(fpd) == bytes(fp)
     C = torch.empty(m * n, dtype=torch.float64, device="cuda")
-    ms = oztt.fp8_run_device(A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, fp, stream(), timed=True)
+    ms = oztt.digit_run_device(A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, fp, stream(), timed=True)
     assert len(ms) == 6 and all(x >= 0 for x in ms)
     assert np.array_equal(C.cpu().numpy().view(np.uint64), c.view(np.uint64))
 

@@ -19,7 +19,7 @@ from oracle_lib import pad, round_up
 
 pytestmark = pytest.mark.gpu
 
-INT8, FP8 = 5, 4  # OZTT_FMT_* values
+INT8, FP8, BF16, TF32 = 5, 4, 0, 2  # OZTT_FMT_* values
 PUBLISHED = {3520: {"II": "a7bb9bd6f452e753", "I": "3ec48d5faecdf98f"},
              7040: {"II": "a2a3d9c61f79b001", "I": "316f280769f1f880"}}
 
@@ -102,7 +102,7 @@ def test_scheme_ii_fp8_published(oztt, oracle, cuda, n):
     """GPU scaling, digit split and digit products (raw int32 outputs); the reference's composition
     (compose.cpp) and triple-float reconstruction restated on the host must give the published bits."""
     a, b = oracle.gen_inputs(n, n, n, -1.0, 7)
-    fp = oztt.fp8_plan(a, b, n, n, n, reconstruction=1, fixed_bits=54)
+    fp = oztt.digit_plan(a, b, n, n, n, reconstruction=1, fixed_bits=54)
     assert fp.base.S == 12 and fp.nprod == 36
     crt = oracle.crt_plan([fp.base.moduli[i] for i in range(fp.base.S)], fp.base.b, fp.base.two_pass)
     M = round_up(n, 64)
@@ -111,16 +111,16 @@ def test_scheme_ii_fp8_published(oztt, oracle, cuda, n):
     dA, dB = scale(oztt, A, n, n, 0, fp.base.shift), scale(oztt, B, n, n, 1, fp.base.shift)
     da_ = torch.zeros(fp.nplane * mp * kp, dtype=torch.int8, device="cuda")
     db_ = torch.zeros(fp.nplane * np_ * kp, dtype=torch.int8, device="cuda")
-    oztt.call("oztt_ii_fp8_split_rows", A.data_ptr(), n, n, n, dA.data_ptr(), fp, da_.data_ptr(), mp, kp, stream())
-    oztt.call("oztt_ii_fp8_split_cols", B.data_ptr(), n, n, n, dB.data_ptr(), fp, db_.data_ptr(), np_, kp, stream())
+    oztt.call("oztt_ii_digit_split_rows", A.data_ptr(), n, n, n, dA.data_ptr(), fp, da_.data_ptr(), mp, kp, stream())
+    oztt.call("oztt_ii_digit_split_cols", B.data_ptr(), n, n, n, dB.data_ptr(), fp, db_.data_ptr(), np_, kp, stream())
     del A, B
     P = torch.empty(fp.nout * mp * np_, dtype=torch.int32, device="cuda")
-    oztt.call("oztt_ii_fp8_digit_gemm", da_.data_ptr(), db_.data_ptr(), mp, np_, kp, fp, 0, P.data_ptr(), stream())
+    oztt.call("oztt_ii_digit_gemm", da_.data_ptr(), db_.data_ptr(), mp, np_, kp, fp, 0, P.data_ptr(), stream())
     torch.cuda.synchronize()
     del da_, db_
     host = np.ascontiguousarray(P.view(fp.nout, mp, np_)[:, :M, :M].cpu().numpy())
     del P
-    r = oracle.fp8_compose(host.reshape(-1), fp, crt, M, M)
+    r = oracle.digit_compose(host.reshape(-1), fp, crt, M, M)
     del host
     da = np.zeros(M, dtype=np.int32)
     db = np.zeros(M, dtype=np.int32)
@@ -165,3 +165,74 @@ def test_scheme_i_fp8_published(oztt, oracle, cuda, n):
     da[:n], db[:n] = dA.cpu().numpy(), dB.cpu().numpy()
     c = oracle.i_recon(host.reshape(-1), p, M, M, da, db, exact=False, fmt=FP8, K=M).reshape(M, M)[:n, :n]
     assert int(oracle.output_hash(np.ascontiguousarray(c).reshape(-1)), 16) == PUBLISHED_I_FP8[n]
+
+
+# Scheme II BF16 and TF32 (tools/validated/all.csv:3,7,19,23; FP16 publishes the same hashes as BF16 at these
+# sizes) and Scheme I with radix 64 (all.csv:2,18; BF16, FP16 and TF32 share it).
+PUBLISHED_II_DIGIT = {(BF16, 3520): 0x93b166fd9cdcea08, (BF16, 7040): 0xbab997b36b74c8e8,
+                      (TF32, 3520): 0x09fd289ad78b89a4, (TF32, 7040): 0x9bbf8b8aa484cdff}
+PUBLISHED_I_R64 = {3520: 0x0cb21e8470017933, 7040: 0x096204765d925a85}
+
+
+def digit_published_hash(oztt, oracle, n, fmt):
+    a, b = oracle.gen_inputs(n, n, n, -1.0, 7)
+    fp = oztt.digit_plan(a, b, n, n, n, reconstruction=1, fixed_bits=54, fmt=fmt)
+    crt = oracle.crt_plan([fp.base.moduli[i] for i in range(fp.base.S)], fp.base.b, fp.base.two_pass)
+    M = round_up(n, 64)
+    mp, np_, kp = round_up(n, 128), round_up(n, 256), round_up(n, 128)
+    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    dA, dB = scale(oztt, A, n, n, 0, fp.base.shift), scale(oztt, B, n, n, 1, fp.base.shift)
+    da_ = torch.zeros(fp.nplane * mp * kp, dtype=torch.int8, device="cuda")
+    db_ = torch.zeros(fp.nplane * np_ * kp, dtype=torch.int8, device="cuda")
+    oztt.call("oztt_ii_digit_split_rows", A.data_ptr(), n, n, n, dA.data_ptr(), fp, da_.data_ptr(), mp, kp, stream())
+    oztt.call("oztt_ii_digit_split_cols", B.data_ptr(), n, n, n, dB.data_ptr(), fp, db_.data_ptr(), np_, kp, stream())
+    del A, B
+    P = torch.empty(fp.nout * mp * np_, dtype=torch.int32, device="cuda")
+    oztt.call("oztt_ii_digit_gemm", da_.data_ptr(), db_.data_ptr(), mp, np_, kp, fp, 0, P.data_ptr(), stream())
+    torch.cuda.synchronize()
+    del da_, db_
+    host = np.ascontiguousarray(P.view(fp.nout, mp, np_)[:, :M, :M].cpu().numpy())
+    del P
+    r = oracle.digit_compose(host.reshape(-1), fp, crt, M, M)
+    del host
+    da = np.zeros(M, dtype=np.int32)
+    db = np.zeros(M, dtype=np.int32)
+    da[:n], db[:n] = dA.cpu().numpy(), dB.cpu().numpy()
+    c = oracle.recon_residue(r, M, M, da, db, crt).reshape(M, M)[:n, :n]
+    return int(oracle.output_hash(np.ascontiguousarray(c).reshape(-1)), 16)
+
+
+@pytest.mark.parametrize("fmt,n", list(PUBLISHED_II_DIGIT))
+def test_scheme_ii_digit_published(oztt, oracle, cuda, fmt, n):
+    assert digit_published_hash(oztt, oracle, n, fmt) == PUBLISHED_II_DIGIT[(fmt, n)]
+
+
+@pytest.mark.parametrize("n", [3520, 7040])
+def test_scheme_i_radix64_published(oztt, oracle, cuda, n):
+    a, b = oracle.gen_inputs(n, n, n, -1.0, 7)
+    p = 10
+    M = round_up(n, 64)
+    mp, np_, kp = round_up(n, 128), round_up(n, 256), round_up(n, 128)
+    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    dA = torch.zeros(n, dtype=torch.int32, device="cuda")
+    dB = torch.zeros(n, dtype=torch.int32, device="cuda")
+    flags = torch.zeros(1, dtype=torch.int32, device="cuda")
+    oztt.call("oztt_i_scale_rows", A.data_ptr(), n, n, n, BF16, dA.data_ptr(), flags.data_ptr(), stream())
+    oztt.call("oztt_i_scale_cols", B.data_ptr(), n, n, n, BF16, dB.data_ptr(), flags.data_ptr(), stream())
+    sa = torch.zeros(p * mp * kp, dtype=torch.int8, device="cuda")
+    sb = torch.zeros(p * np_ * kp, dtype=torch.int8, device="cuda")
+    oztt.call("oztt_i_slice_rows", A.data_ptr(), n, n, n, dA.data_ptr(), p, BF16, sa.data_ptr(), mp, kp, stream())
+    oztt.call("oztt_i_slice_cols", B.data_ptr(), n, n, n, dB.data_ptr(), p, BF16, sb.data_ptr(), np_, kp, stream())
+    del A, B
+    pd = torch.empty(p * mp * np_, dtype=torch.int32, device="cuda")
+    oztt.call("oztt_i_diag_gemm", sa.data_ptr(), sb.data_ptr(), mp, np_, kp, p, pd.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert int(flags.cpu()[0]) == 0
+    del sa, sb
+    host = np.ascontiguousarray(pd.view(p, mp, np_)[:, :M, :M].cpu().numpy())
+    del pd
+    da = np.zeros(M, dtype=np.int32)
+    db = np.zeros(M, dtype=np.int32)
+    da[:n], db[:n] = dA.cpu().numpy(), dB.cpu().numpy()
+    c = oracle.i_recon(host.reshape(-1), p, M, M, da, db, exact=False, fmt=BF16, K=M).reshape(M, M)[:n, :n]
+    assert int(oracle.output_hash(np.ascontiguousarray(c).reshape(-1)), 16) == PUBLISHED_I_R64[n]

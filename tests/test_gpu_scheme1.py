@@ -27,9 +27,9 @@ def stream():
     return torch.cuda.current_stream().cuda_stream
 
 
-INT8, FP8 = 5, 4  # OZTT_FMT_* values
-FORMATS = [INT8, FP8]
-CEIL = {INT8: 1, FP8: 0}  # BF16 rounding of the maxima: up for INT8, truncated for FP8
+INT8, FP8, BF16 = 5, 4, 0  # OZTT_FMT_* values (BF16 stands for the radix-64 formats BF16, FP16, TF32)
+FORMATS = [INT8, FP8, BF16]
+CEIL = {INT8: 1, FP8: 0, BF16: 0}  # BF16 rounding of the maxima: up for INT8, truncated for the FP formats
 
 
 def gpu_deltas(oztt, x, rows, cols, col_mode, fmt=INT8):
@@ -141,7 +141,7 @@ def test_recon_matches_oracle(oztt, oracle, cuda, m, n, p, fmt):
     rng = np.random.default_rng(m * n + p)
     mp, np_ = round_up(m, 128), round_up(n, 256)
     K = 2048
-    radix, dmax = (254, 127) if fmt == INT8 else (32, 16)
+    radix, dmax = {INT8: (254, 127), FP8: (32, 16), BF16: (64, 32)}[fmt]
     bound = np.array([(d + 1) * K * dmax * dmax for d in range(p)], dtype=np.int64)
     pd = (rng.uniform(-1, 1, (p, mp, np_)) * bound[:, None, None] * rng.uniform(0, 1, (p, 1, 1))).astype(np.int32)
     pd[:, 0, 0] = 0                     # zero result
@@ -184,7 +184,7 @@ PIPE_CASES = [("uniform", 128, 128, 128, -1.0, 8), ("phi1", 100, 70, 45, 1.0, 0)
 @pytest.mark.parametrize("name,m,n,k,phi,p", PIPE_CASES)
 def test_pipeline_matches_oracle(oztt, oracle, cuda, name, m, n, k, phi, p, fmt):
     a, b = oracle.gen_inputs(m, n, k, phi, 17)
-    p = p if fmt == INT8 or p == 0 else p + 4  # radix 32 carries 5 bits a slice, 254 about 8
+    p = p if fmt == INT8 or p == 0 else p + {FP8: 4, BF16: 2}[fmt]  # radix 32/64 carry 5/6 bits a slice, 254 ~8
     c, plan = run_gpu(oztt, a, b, m, n, k, p, fmt)
     assert p == 0 or plan.p == p
     exact = oracle.i_emulate(a, b, m, n, k, plan.p, exact=True, fmt=fmt)

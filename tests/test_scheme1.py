@@ -183,3 +183,26 @@ def test_fp8_plan_feasibility(oztt):
     # K blocking is allowed for FP8 (no INT8-style rejection)
     k = 16416
     assert oztt.i_int8_plan(np.ones(k), np.ones(k), 1, 1, k, slices=8, fmt=oztt.Format.FP8).p == 8
+
+
+# ---- Scheme I with BF16, FP16 and TF32 digits (radix 64, digits +-32) ---------------------------------
+# tools/validated/quick.csv:2,4,6: the three formats share radix and digits, so their device outputs are
+# identical: 10 slices, hash be6558fa9f435fa0, relative Frobenius error 4.69364573273e-17.
+@pytest.mark.parametrize("fmt", [0, 1, 2])
+def test_oracle_reproduces_published_radix64_output(oracle, fmt):
+    n = 128
+    a, b = oracle.gen_inputs(n, n, n, -1.0, 7)
+    c = oracle.i_emulate(a, b, n, n, n, 10, exact=False, fmt=fmt)
+    assert oracle.output_hash(c) == "be6558fa9f435fa0"
+    hi, lo = oracle.dot2(a, b, n, n, n)
+    assert oracle.accuracy(c, hi, lo)[0] == pytest.approx(4.69364573273e-17, rel=1e-10)
+
+
+def test_radix64_slice_selection_matches_reference(oracle, oztt, ref_plan1_r64):
+    for name, a, b, m, n, k in _selection_cases(oracle):
+        M, N, K = round_up(m, 64), round_up(n, 64), round_up(k, 32)
+        want = ref_plan1_r64.slices(pad(a, m, k, M, K), pad(b, k, n, K, N), M, N, K)
+        for fmt in (oztt.Format.BF16, oztt.Format.FP16, oztt.Format.TF32):
+            plan = oztt.i_int8_plan(a, b, m, n, k, fmt=fmt)
+            assert plan.p == want, (name, fmt)
+            assert (plan.radix, plan.dmax) == (64, 32)
