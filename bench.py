@@ -4,8 +4,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl oztt|reference]
     python bench.py --scheme I [--slices 0,4,8,12] [--format FP8]
                                    (Scheme I INT8 or FP8, 8192^3, phi=1: one line per p)
-    python bench.py --format FP8 [--moduli 12,16,20,24] [--passes 1,2]
-                                   (Scheme II FP8 digits, 8192 x 8192 x 16384, phi=4: one line per setting)
+    python bench.py --format FP8|BF16|FP16|TF32 [--moduli 12,16,20,24] [--passes 1,2]
+                                   (Scheme II digit formats, 8192 x 8192 x 16384, phi=4: one line per setting)
 
 One step is one pass of the Scheme II INT8 pipeline (scale -> split -> residue GEMM on the tensor
 cores -> exact CRT reconstruction) over one m x n x k problem with FP64 operands already resident in
@@ -58,9 +58,10 @@ def parse_args():
     ap.add_argument("--scheme", choices=["II", "I"], default="II",
                     help="I: the Scheme I INT8 workload (default 8192^3, phi=1.0), one JSON line per slice count")
     ap.add_argument("--slices", default="0", help="Scheme I: comma-separated slice counts, 0 = selected from the input")
-    ap.add_argument("--format", choices=["INT8", "FP8"], default="INT8", help="digit format (both schemes)")
-    ap.add_argument("--moduli", default="12,16,20,24", help="FP8: comma-separated max_moduli settings")
-    ap.add_argument("--passes", default="1,2", help="FP8: reconstruction passes to run (1 OnePass, 2 TwoPass)")
+    ap.add_argument("--format", choices=["INT8", "FP8", "BF16", "FP16", "TF32"], default="INT8",
+                    help="format of the low-precision products (both schemes)")
+    ap.add_argument("--moduli", default="12,16,20,24", help="digit formats: comma-separated max_moduli settings")
+    ap.add_argument("--passes", default="1,2", help="digit formats: reconstruction passes (1 OnePass, 2 TwoPass)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -69,7 +70,7 @@ def parse_args():
     if args.size is None:
         args.size = DEFAULT_SIZE if args.scheme == "II" and args.format == "INT8" else 8192
     if args.phi is None:
-        args.phi = 1.0 if args.scheme == "I" else (4.0 if args.format == "FP8" else 0.5)
+        args.phi = 1.0 if args.scheme == "I" else (0.5 if args.format == "INT8" else 4.0)
     return args
 
 
@@ -264,7 +265,7 @@ def run_scheme_i(args) -> None:
     C = torch.empty(m * n, dtype=torch.float64, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
     peaks = measured_peaks()
-    fmt = oz.Format.FP8 if args.format == "FP8" else oz.Format.INT8
+    fmt = getattr(oz.Format, args.format)
     for req in [int(x) for x in args.slices.split(",")]:
         t_plan = time.perf_counter()
         plan = oz.i_int8_plan(a, b, m, n, k, slices=req, fmt=fmt)
@@ -313,11 +314,11 @@ def run_scheme_i(args) -> None:
         print(json.dumps(line), flush=True)
 
 
-def run_fp8(args) -> None:
-    """One step = one pass of the Scheme II FP8 pipeline (scale -> digit split -> digit products on the
-    tensor cores with the composition in the epilogue -> exact CRT reconstruction) with the operands
-    resident in HBM, for each max_moduli and reconstruction setting of the configuration; a setting the
-    planner rejects prints its message instead of a number."""
+def run_digit(args) -> None:
+    """One step = one pass of the Scheme II pipeline of a digit format (FP8, BF16, FP16, TF32: scale -> digit
+    split -> digit products on the tensor cores with the composition in the epilogue -> exact CRT
+    reconstruction) with the operands resident in HBM, for each max_moduli and reconstruction setting of the
+    configuration; a setting the planner rejects prints its message instead of a number."""
     import torch
 
     import oztt_b200 as oz
@@ -331,15 +332,16 @@ def run_fp8(args) -> None:
     stream = torch.cuda.current_stream().cuda_stream
     peaks = measured_peaks()
     int8_peak = 2.0 * peaks["bf16_tflops_sustained"]
-    workload = f"Scheme II FP8 (e4m3 digits) {m}x{n}x{k}, phi={args.phi}"
+    fmt = getattr(oz.Format, args.format)
+    workload = f"Scheme II {args.format} digits {m}x{n}x{k}, phi={args.phi}"
     for S_req in [int(x) for x in args.moduli.split(",")]:
         for passes in [int(x) for x in args.passes.split(",")]:
-            base = {"metric": f"Ozaki-II FP8 effective FP64 TFLOPS at m=n={m}, k={k}", "unit": "TFLOPS",
+            base = {"metric": f"Ozaki-II {args.format} effective FP64 TFLOPS at m=n={m}, k={k}", "unit": "TFLOPS",
                     "n_gpus": 1, "config": {"workload": workload, "max_moduli": S_req, "reconstruction_passes": passes}}
             t_plan = time.perf_counter()
             try:
                 plan = oz.digit_plan_device(A.data_ptr(), B.data_ptr(), m, n, k, max_moduli=S_req,
-                                          reconstruction=passes, stream=stream)
+                                            reconstruction=passes, stream=stream, fmt=fmt)
             except (RuntimeError, ValueError) as exc:
                 print(json.dumps({**base, "value": None, "rejected": str(exc)}), flush=True)
                 continue
@@ -367,7 +369,7 @@ def run_fp8(args) -> None:
             gemm_tops = gemm_ops / (st[4] * 1e-3) / 1e12
             line = {**base, "value": 2.0 * m * n * k / (ms * 1e-3) / 1e12, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                    "vs_baseline": None, "dtype": "f64 (int8-held e4m3 digit products, s32 accumulate)",
+                    "vs_baseline": None, "dtype": f"f64 (int8-held {args.format} digit products, s32 accumulate)",
                     "data": f"synthetic: evaluation/numerics.hpp generator, phi={args.phi}, mt19937 seed {args.seed}",
                     "config": {**base["config"], "moduli": plan.base.S, "integer_bits": plan.base.b,
                                "passes_planned": 2 if plan.base.two_pass else 1, "digit_planes": plan.nplane,
@@ -412,8 +414,8 @@ def main() -> None:
     if args.scheme == "I":
         run_scheme_i(args)
         return
-    if args.format == "FP8":
-        run_fp8(args)
+    if args.format != "INT8":
+        run_digit(args)
         return
     import torch
     import torch.distributed as dist

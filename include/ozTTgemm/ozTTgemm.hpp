@@ -8,8 +8,7 @@
 // the tensor cores, and the FP64 result is reconstructed on the GPU.
 //
 // Differences a caller can observe (the declarations are identical):
-//   * Format::INT8 and Format::FP8 (e4m3 digits) are built, both schemes; BF16, FP16 and TF32 are not
-//     built yet (is_available() is false).
+//   * Format::INT8, FP8 (e4m3 digits), BF16, FP16 and TF32 are built, both schemes.
 //   * Format::BFP8, BFP4 and BFP2 are Tenstorrent block formats; is_available() is false for them, so a
 //     default-constructed Options (format BFP8) is rejected with std::invalid_argument, exactly as the
 //     reference rejects a format left out of its build.
