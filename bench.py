@@ -582,10 +582,14 @@ def main() -> None:
             t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_s = float(t[0])
+        phases = oz.ii_int8_last_phases()
         result["e2e"] = {"value": flops / e2e_s / 1e12, "unit": "TFLOPS", "s_per_step": e2e_s,
+                         "phases_ms_last_call": {key: round(v, 2) if isinstance(v, float) else v
+                                                 for key, v in phases.items()},
                          "h2d_bytes_per_step": 8 * (m * k + k * n), "d2h_bytes_per_step": 8 * m * n,
-                         "path": "ozTTgemm::Context::gemm via oztt_gemm (host validation, pinned H2D, device-measured plan statistics, "
-                                 "GPU pipeline, D2H)"}
+                         "path": "ozTTgemm::Context::gemm via oztt_gemm: chunked pinned H2D with the device-measured "
+                                 "plan statistics and the host value checks overlapped, plan, GPU pipeline in row bands "
+                                 "with each band's D2H overlapped"}
     # ---- CPU baseline (rank 0 at N=1) ------------------------------------------------------------------
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = time_cpu_dot2(a, b, n, k, target_s=12.0)

@@ -211,6 +211,12 @@ int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* 
                                   uint64_t n, uint64_t k, const oztt_ii_plan* plan, void* stream, double* stage_ms,
                                   char* err, size_t errlen);
 
+/* Host wall-clock phases (ms) of the last INT8 Scheme II call made through oztt_gemm / Context::gemm in
+ * this process, out[0..count-1] of: upload (to the end of the last host-to-device copy), statistics
+ * read-back after it, value checks from the measured maxima, plan, pipeline with the banded read-back of C,
+ * total, number of row bands. Zeros before the first such call. */
+int oztt_ii_int8_last_phases(double* out, int32_t count);
+
 /* Scheme I INT8 plan (plan_issue and the slice count of src/backend/ozaki1/plan.hpp:128-250 and
  * auto_precision.hpp:506): slices > 0 fixes p, 0 chooses it from the input. OZTT_ERUNTIME when the
  * reference would throw (K blocking needed, Horner exponent budget exceeded). */

@@ -168,6 +168,7 @@ _SIGNATURES = {
     "oztt_stats_sumsq": [_P, _U64, _U64, _I32, ctypes.c_double, _P, _P, _ERR, _SZ],
     "oztt_stats_sketch": [_P, _U64, _U64, ctypes.c_double, _P, _U64, _P, _U64, _P, _ERR, _SZ],
     "oztt_policy_vectors": [ctypes.c_uint32, _P],
+    "oztt_ii_int8_last_phases": [_P, _I32],
     "oztt_ii_int8_plan_from_stats": [_U64, _U64, _U64, ctypes.c_uint32, _I32, _I32, ctypes.c_double, ctypes.c_double,
                                      ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.POINTER(IIPlan), _ERR,
                                      _SZ],
@@ -349,6 +350,18 @@ def policy_vectors(N: int) -> np.ndarray:
     out = np.empty((8, N), dtype=np.float64)
     _lib().oztt_policy_vectors(N, out.ctypes.data)
     return out
+
+
+def ii_int8_last_phases() -> dict:
+    """Host wall-clock phases (ms) of the last INT8 Scheme II call through Context.gemm in this process
+    (oztt_ii_int8_last_phases): upload, statistics read-back, value checks from the measured maxima, plan,
+    pipeline with the banded read-back of C, total, and the number of row bands."""
+    out = np.zeros(7, dtype=np.float64)
+    _lib().oztt_ii_int8_last_phases(out.ctypes.data, 7)
+    keys = ("upload_ms", "stats_ms", "check_ms", "plan_ms", "pipeline_ms", "total_ms")
+    d = {key: float(v) for key, v in zip(keys, out[:6])}
+    d["bands"] = int(out[6])
+    return d
 
 
 def ii_int8_plan_from_stats(m: int, n: int, k: int, TA: float, TB: float, nA: float, nB: float, nC: float,

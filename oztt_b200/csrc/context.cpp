@@ -9,6 +9,8 @@
 //   * one process-wide mutex serialises the calls of all contexts (:19, :152);
 //   * the device is opened on the first valid call; Info reports the padded dimensions (:176-180);
 //   * all input is consumed before C is written, so C may overlap A or B.
+// For INT8 Scheme II the finiteness and range checks are made from the device-measured row and column
+// maxima once A and B are uploaded, before the plan is made and C is written.
 // Dispatch (src/dispatch.cpp:18-50): INT8, FP8 (e4m3 digits), BF16, FP16 and TF32 are built, both schemes;
 // the Tenstorrent block formats BFP8/BFP4/BFP2 are not available on this hardware.
 #include <ozTTgemm/ozTTgemm.hpp>
@@ -26,8 +28,6 @@
 #include "planner.hpp"
 
 namespace oztt {
-int run_ii_int8_planned(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
-                        uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_ii_plan& p, std::string& err);
 int run_ii_digit_planned(int device_id, int32_t format, const double* a, const double* b, double* c, uint64_t m,
                          uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_digit_plan& p,
                          std::string& err);
@@ -51,49 +51,64 @@ std::uint32_t padded(std::size_t value, std::size_t quantum) {
 }
 // Finiteness and the range of every nonzero row maximum of A and column maximum of B, with the
 // reference's order of reports (context.cpp:37-62): A's rows in order (a row's NaN/Inf before its
-// maximum), then any NaN/Inf in B, then B's column maxima. The scans run on all host threads; each
-// thread records per row (per column block) what it found, and the reports are made in order after.
-void check_values(std::span<const double> a, std::span<const double> b, std::size_t m, std::size_t n, std::size_t k) {
+// maximum), then any NaN/Inf in B, then B's column maxima. The scans run on the process's host
+// threads; each records per row (per column block) what it found, and the reports are made in order
+// after. One unsigned maximum of the magnitude patterns (the sign bit cleared) gives both answers:
+// nonnegative doubles order like their bit patterns, and a pattern at or above that of +Inf is an Inf
+// or a NaN.
+constexpr std::uint64_t kMagnitude = 0x7FFFFFFFFFFFFFFFull, kInfPattern = 0x7FF0000000000000ull;
+
+std::uint64_t max_pattern(const std::uint64_t* p, std::size_t count) {
+    std::uint64_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
+    std::size_t j = 0;
+    for (; j + 4 <= count; j += 4) {
+        m0 = std::max(m0, p[j] & kMagnitude);
+        m1 = std::max(m1, p[j + 1] & kMagnitude);
+        m2 = std::max(m2, p[j + 2] & kMagnitude);
+        m3 = std::max(m3, p[j + 3] & kMagnitude);
+    }
+    for (; j < count; ++j) m0 = std::max(m0, p[j] & kMagnitude);
+    return std::max(std::max(m0, m1), std::max(m2, m3));
+}
+
+double pattern_value(std::uint64_t u) {
+    double x;
+    std::memcpy(&x, &u, sizeof x);
+    return x;
+}
+
+// The reports from the magnitude-pattern maxima of A's rows and B's columns, in the reference's order.
+void report_maxima(const std::uint64_t* row_max, std::size_t m, const std::uint64_t* col_max, std::size_t n) {
     constexpr double maximum = 0x1.fep127;
     constexpr double minimum = 0x1p-126;
     const auto out_of_range = [&](double x) { return x != 0 && (x < minimum || x > maximum); };
     const char* range_msg = "each nonzero row maximum of A and column maximum of B must be in [2^-126, max_BF16]";
-    std::vector<double> row_max(m);
-    std::vector<unsigned char> row_bad(m, 0);
-    oztt::parallel_ranges(m, [&](std::uint64_t r0, std::uint64_t r1) {
-        for (std::uint64_t i = r0; i < r1; ++i) {
-            double mx = 0;
-            bool bad = false;
-            const double* p = a.data() + i * k;
-            for (std::size_t j = 0; j < k; ++j) {
-                const double x = p[j];
-                bad |= !std::isfinite(x);
-                mx = std::max(mx, std::abs(x));
-            }
-            row_max[i] = mx;
-            row_bad[i] = bad;
-        }
-    });
     for (std::size_t i = 0; i < m; ++i) {
-        if (row_bad[i]) throw std::invalid_argument("A contains NaN or infinity");
-        if (out_of_range(row_max[i])) throw std::invalid_argument(range_msg);
+        if (row_max[i] >= kInfPattern) throw std::invalid_argument("A contains NaN or infinity");
+        if (out_of_range(pattern_value(row_max[i]))) throw std::invalid_argument(range_msg);
     }
-    std::vector<double> maxima(n, 0);
-    std::vector<unsigned char> col_bad(n, 0);
+    for (std::size_t j = 0; j < n; ++j)
+        if (col_max[j] >= kInfPattern) throw std::invalid_argument("B contains NaN or infinity");
+    for (std::size_t j = 0; j < n; ++j)
+        if (out_of_range(pattern_value(col_max[j]))) throw std::invalid_argument(range_msg);
+}
+
+void check_values(std::span<const double> a, std::span<const double> b, std::size_t m, std::size_t n, std::size_t k) {
+    const auto* pa = reinterpret_cast<const std::uint64_t*>(a.data());
+    const auto* pb = reinterpret_cast<const std::uint64_t*>(b.data());
+    std::vector<std::uint64_t> row_max(m);
+    oztt::parallel_ranges(m, [&](std::uint64_t r0, std::uint64_t r1) {
+        for (std::uint64_t i = r0; i < r1; ++i) row_max[i] = max_pattern(pa + i * k, k);
+    });
+    std::vector<std::uint64_t> col_max(n, 0);
     oztt::parallel_ranges(n, [&](std::uint64_t c0, std::uint64_t c1) {
+        std::uint64_t* mx = col_max.data();
         for (std::size_t i = 0; i < k; ++i) {
-            const double* p = b.data() + i * n;
-            for (std::uint64_t j = c0; j < c1; ++j) {
-                const double x = p[j];
-                col_bad[j] |= !std::isfinite(x);
-                maxima[j] = std::max(maxima[j], std::abs(x));
-            }
+            const std::uint64_t* p = pb + i * n;
+            for (std::uint64_t j = c0; j < c1; ++j) mx[j] = std::max(mx[j], p[j] & kMagnitude);
         }
     });
-    for (std::size_t j = 0; j < n; ++j)
-        if (col_bad[j]) throw std::invalid_argument("B contains NaN or infinity");
-    for (double x : maxima)
-        if (out_of_range(x)) throw std::invalid_argument(range_msg);
+    report_maxima(row_max.data(), m, col_max.data(), n);
 }
 void check_options(const Options& o) {
     if (o.scheme != Scheme::I && o.scheme != Scheme::II) throw std::invalid_argument("unknown Ozaki scheme");
@@ -111,6 +126,13 @@ struct Checked {
     std::uint32_t mp, np, kp;
     std::size_t c_size;
 };
+// The Scheme II INT8 path makes the value checks from the row and column maxima that the device
+// measures for the precision policy (the same magnitude patterns, so the same reports in the same
+// order), before the plan and before C is written; should the device fail before that, the host
+// checks run after all, so that an invalid input is still the error reported. The other paths run
+// the host checks here, before the device is touched.
+bool checks_during_upload(const Options& o) { return o.scheme == Scheme::II && o.format == Format::INT8; }
+
 Checked validate(const Options& options, std::span<const double> a, std::span<const double> b,
                  std::optional<std::size_t> c_size, std::size_t m, std::size_t n, std::size_t k) {
     check_options(options);
@@ -123,7 +145,7 @@ Checked validate(const Options& options, std::span<const double> a, std::span<co
                        std::uint64_t(v.mp / 32) * (v.np / 32)})
         if (count > std::numeric_limits<std::uint32_t>::max() / 4096u)
             throw std::invalid_argument("matrix is too large for the device's 32-bit offsets");
-    check_values(a, b, m, n, k);
+    if (!checks_during_upload(options)) check_values(a, b, m, n, k);
     return v;
 }
 int32_t recon_code(Reconstruction r) {
@@ -205,13 +227,22 @@ Info Context::Impl::execute(std::span<const double> a, std::span<const double> b
         info.padded_k = v.kp;
         return info;
     }
-    // A and B go to the device first; the precision policy measures them there (bit-identical to the
-    // host measurement) and the host makes the decisions; C is written only after the pipeline ran.
+    // A and B go to the device in chunks; the precision policy measures them there (bit-identical to the
+    // host measurement), the values are checked from the measured maxima and the host makes the
+    // decisions; C is written only after that.
+    bool checked = false;
+    const auto check_maxima = [&](const std::uint64_t* row_max, const std::uint64_t* col_max) {
+        checked = true;
+        report_maxima(row_max, m, col_max, n);
+    };
     oztt_ii_plan plan;
     std::string msg;
-    const int rc = oztt::run_ii_int8_planned(options.device_id, a.data(), b.data(), c.data(), m, n, k, opt.max_moduli,
-                                             recon_code(opt.reconstruction), plan, msg);
-    if (rc != OZTT_OK) rethrow(rc, msg);
+    const int rc = oztt::run_ii_int8_streamed(options.device_id, a.data(), b.data(), c.data(), m, n, k, opt.max_moduli,
+                                              recon_code(opt.reconstruction), check_maxima, plan, msg);
+    if (rc != OZTT_OK) {
+        if (!checked) check_values(a, b, m, n, k);
+        rethrow(rc, msg);
+    }
     opened = true;
     Info info{Scheme::II, opt.format};
     info.moduli = (std::uint32_t)plan.S;
@@ -292,4 +323,13 @@ extern "C" int oztt_gemm(int device_id, const double* a, uint64_t a_len, const d
         put(e.what());
         return OZTT_ERUNTIME;
     }
+}
+
+extern "C" int oztt_ii_int8_last_phases(double* out, int32_t count) {
+    if (!out || count < 1) return OZTT_EINVAL;
+    const oztt::StreamedPhases ph = oztt::last_streamed_phases();
+    const double v[7] = {ph.upload_ms, ph.stats_ms, ph.check_ms, ph.plan_ms, ph.pipeline_ms, ph.total_ms,
+                         (double)ph.bands};
+    for (int32_t i = 0; i < count && i < 7; ++i) out[i] = v[i];
+    return OZTT_OK;
 }

@@ -68,136 +68,98 @@ OZTT_HD double double_of(uint64_t u) {
 
 OZTT_HD Ext zero() { return Ext{0, 0, 0}; }
 
+// x >> s and x << s for s in [0, 64], 0 at s = 64 (C++ leaves a 64-bit shift by 64 undefined).
+OZTT_HD uint64_t shr64(uint64_t x, uint32_t s) { return s < 64 ? x >> s : 0; }
+OZTT_HD uint64_t shl64(uint64_t x, uint32_t s) { return s < 64 ? x << s : 0; }
+
+// The operations below are written without data-dependent branches (every case is computed and the
+// result selected), so that the lanes of a warp, which hold different operands, never diverge.
+
 // Exact conversion of a finite double.
 OZTT_HD Ext from_double(double x) {
     const uint64_t u = bits_of(x);
+    const int32_t E = (int32_t)((u >> 52) & 0x7FF);
+    const uint64_t f = u & 0xFFFFFFFFFFFFFull;
+    const int lz = clz64(f);  // subnormal: value = f * 2^-1074
     Ext r;
     r.neg = (uint32_t)(u >> 63);
-    const int32_t E = (int32_t)((u >> 52) & 0x7FF);
-    uint64_t f = u & 0xFFFFFFFFFFFFFull;
-    if (E == 0) {
-        if (f == 0) {
-            r.m = 0;
-            r.e = 0;
-            return r;
-        }
-        const int lz = clz64(f);  // subnormal: value = f * 2^-1074
-        r.m = f << lz;
-        r.e = -1074 + 63 - lz;
-        return r;
-    }
-    r.m = (f | 0x10000000000000ull) << 11;
-    r.e = E - 1023;
+    r.m = E ? (f | 0x10000000000000ull) << 11 : shl64(f, (uint32_t)lz);
+    r.e = E ? E - 1023 : (f ? -1074 + 63 - lz : 0);
     return r;
 }
 
 // Rounds the 128-bit magnitude (hi:lo, bit 127 set) to 64 bits, ties to even; `sticky` says that
 // nonzero bits lie below lo. Returns the significand and adds the carry of the rounding to e.
 OZTT_HD uint64_t round128(uint64_t hi, uint64_t lo, bool sticky, int32_t& e) {
-    const bool guard = (lo >> 63) != 0;
-    const bool rest = (lo << 1) != 0 || sticky;
-    if (guard && (rest || (hi & 1))) {
-        ++hi;
-        if (hi == 0) {  // carried out of 64 bits: the significand becomes 2^63 with a larger exponent
-            hi = 0x8000000000000000ull;
-            ++e;
-        }
-    }
-    return hi;
+    const uint64_t guard = lo >> 63;
+    const uint64_t rest = ((lo << 1) != 0 || sticky) ? 1u : 0u;
+    const uint64_t inc = guard & (rest | (hi & 1));
+    const uint64_t r = hi + inc;
+    const bool wrap = r == 0 && inc;  // carried out of 64 bits: the significand becomes 2^63
+    e += wrap ? 1 : 0;
+    return wrap ? 0x8000000000000000ull : r;
 }
 
 // a * b rounded once to 64 significand bits (a, b from doubles or any Ext values).
 OZTT_HD Ext mul(const Ext& a, const Ext& b) {
+    const bool zero = a.m == 0 || b.m == 0;
+    const uint64_t hi = mulhi64(a.m, b.m), lo = a.m * b.m;
+    // a.m * b.m in [2^126, 2^128): value = (hi:lo) * 2^(ea + eb - 126)
+    const bool top = (hi >> 63) != 0;
+    int32_t e = a.e + b.e + (top ? 1 : 0);
+    const uint64_t h = top ? hi : (hi << 1) | (lo >> 63);
+    const uint64_t l = top ? lo : lo << 1;
     Ext r;
     r.neg = a.neg ^ b.neg;
-    if (a.m == 0 || b.m == 0) {
-        r.m = 0;
-        r.e = 0;
-        return r;
-    }
-    uint64_t hi = mulhi64(a.m, b.m), lo = a.m * b.m;
-    // a.m * b.m in [2^126, 2^128): value = (hi:lo) * 2^(ea + eb - 126)
-    int32_t e = a.e + b.e + 1;
-    if (!(hi >> 63)) {
-        hi = (hi << 1) | (lo >> 63);
-        lo <<= 1;
-        e -= 1;
-    }
-    r.m = round128(hi, lo, false, e);
-    r.e = e;
+    r.m = round128(h, l, false, e);
+    r.m = zero ? 0 : r.m;
+    r.e = zero ? 0 : e;
     return r;
 }
 
-// a + b rounded once to 64 significand bits.
+// a + b rounded once to 64 significand bits. Zeros keep the IEEE signs: -0 + -0 = -0, any other sum
+// of zeros and an exact cancellation give +0.
 OZTT_HD Ext add(const Ext& a, const Ext& b) {
-    if (b.m == 0) {
-        if (a.m == 0) return Ext{0, 0, a.neg & b.neg};  // -0 + -0 = -0, otherwise +0
-        return a;
-    }
-    if (a.m == 0) return b;
-    // x: the operand of larger magnitude.
-    const bool a_big = a.e > b.e || (a.e == b.e && a.m >= b.m);
-    const Ext& x = a_big ? a : b;
-    const Ext& y = a_big ? b : a;
-    const uint32_t d = (uint32_t)(x.e - y.e);
-    // X = x.m * 2^64, Y = y.m * 2^(64 - d), both as 128-bit fixed point, with the bits of Y that fall
-    // below the window kept as a sticky flag.
-    uint64_t yh, yl;
-    bool sticky = false;
-    if (d == 0) {
-        yh = y.m;
-        yl = 0;
-    } else if (d < 64) {
-        yh = y.m >> d;
-        yl = y.m << (64 - d);
-    } else if (d == 64) {
-        yh = 0;
-        yl = y.m;
-    } else if (d < 128) {
-        yh = 0;
-        yl = y.m >> (d - 64);
-        sticky = (y.m << (128 - d)) != 0;
-    } else {
-        yh = 0;
-        yl = 0;
-        sticky = true;
-    }
-    int32_t e = x.e;
-    uint64_t hi, lo;
-    if (x.neg == y.neg) {
-        lo = yl;  // x's low half is zero
-        hi = x.m + yh;
-        if (hi < x.m) {  // carry out of bit 127: shift right by one
-            sticky = sticky || (lo & 1);
-            lo = (lo >> 1) | (hi << 63);
-            hi = (hi >> 1) | 0x8000000000000000ull;
-            ++e;
-        }
-    } else {
-        // X - Y - (sticky ? 1 : 0): with discarded bits of Y, the exact difference lies strictly between
-        // this value and the next, which the sticky flag records.
-        const uint64_t sub = yl + (sticky ? 1u : 0u);  // wraps to 0 only when yl = 2^64 - 1 and sticky
-        lo = 0 - sub;
-        const uint64_t borrow = (yl != 0 || sticky) ? 1u : 0u;
-        hi = x.m - yh - borrow;
-        if (hi == 0 && lo == 0) return Ext{0, 0, 0};  // exact cancellation (sticky is then false): +0
-        // normalize: shift left until bit 127 is set
-        if (hi == 0) {
-            hi = lo;
-            lo = 0;
-            e -= 64;
-        }
-        const int lz = clz64(hi);
-        if (lz) {
-            hi = (hi << lz) | (lo >> (64 - lz));
-            lo <<= lz;
-            e -= lz;
-        }
-    }
+    const bool az = a.m == 0, bz = b.m == 0;
+    // x: the operand of larger magnitude (a zero is the smaller)
+    const bool a_big = bz || (!az && (a.e > b.e || (a.e == b.e && a.m >= b.m)));
+    const uint64_t xm = a_big ? a.m : b.m, ym = a_big ? b.m : a.m;
+    const int32_t xe = a_big ? a.e : b.e, ye = a_big ? b.e : a.e;
+    const uint32_t xn = a_big ? a.neg : b.neg, yn = a_big ? b.neg : a.neg;
+    // Y = y.m * 2^(64 - d) beside X = x.m * 2^64 as 128-bit fixed point; the bits of Y below the window
+    // become the sticky flag. d = 128 stands for "entirely below" (and for a zero y).
+    const int64_t dd = (int64_t)xe - (int64_t)ye;
+    const uint32_t d = (ym == 0 || dd >= 128) ? 128u : (uint32_t)dd;
+    const uint64_t yh = shr64(ym, d);
+    const uint64_t yl = d == 0 ? 0 : (d <= 64 ? shl64(ym, 64 - d) : shr64(ym, d - 64));
+    const bool sticky = d > 64 && (d < 128 ? shl64(ym, 128 - d) != 0 : ym != 0);
+    // same signs: X + Y, then one right shift on a carry out of bit 127
+    const uint64_t sh = xm + yh;
+    const bool carry = sh < xm;
+    const uint64_t add_hi = carry ? (sh >> 1) | 0x8000000000000000ull : sh;
+    const uint64_t add_lo = carry ? (yl >> 1) | (sh << 63) : yl;
+    const bool add_sticky = sticky || (carry && (yl & 1));
+    const int32_t add_e = xe + (carry ? 1 : 0);
+    // opposite signs: X - Y - (sticky ? 1 : 0) -- with discarded bits of Y the exact difference lies
+    // strictly between this value and the next, which the sticky flag records -- then normalised
+    const uint64_t sub = yl + (sticky ? 1u : 0u);  // wraps to 0 only when yl = 2^64 - 1 and sticky
+    const uint64_t d_lo = 0 - sub;
+    const uint64_t d_hi = xm - yh - ((yl != 0 || sticky) ? 1u : 0u);
+    const bool cancel = d_hi == 0 && d_lo == 0;  // exact (sticky is then false)
+    const bool hz = d_hi == 0;
+    const uint64_t h1 = hz ? d_lo : d_hi, l1 = hz ? 0 : d_lo;
+    const uint32_t lz = cancel ? 0u : (uint32_t)clz64(h1);
+    const uint64_t sub_hi = shl64(h1, lz) | (lz ? shr64(l1, 64 - lz) : 0);
+    const uint64_t sub_lo = shl64(l1, lz);
+    const int32_t sub_e = xe - (hz ? 64 : 0) - (int32_t)lz;
+    const bool same = xn == yn;
+    int32_t e = same ? add_e : sub_e;
+    const uint64_t m = round128(same ? add_hi : sub_hi, same ? add_lo : sub_lo, same ? add_sticky : sticky, e);
+    const bool zero = xm == 0 || (!same && cancel);
     Ext r;
-    r.neg = x.neg;
-    r.m = round128(hi, lo, sticky, e);
-    r.e = e;
+    r.m = zero ? 0 : m;
+    r.e = zero ? 0 : e;
+    r.neg = zero ? (xm == 0 ? (a.neg & b.neg) : 0u) : xn;
     return r;
 }
 

@@ -741,11 +741,13 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 3-D map over S planes of rows x kp int8 (K innermost), box BK x box_rows x 1, 128-byte swizzle.
-static CUtensorMap make_plane_map(const int8_t* base, uint64_t rows, uint64_t kp, uint64_t S, uint32_t box_rows) {
+// 3-D map over S planes of rows x kp int8 (K innermost), box BK x box_rows x 1, 128-byte swizzle. The
+// planes lie plane_rows x kp apart (plane_rows >= rows; a band of rows of taller planes), or rows x kp.
+static CUtensorMap make_plane_map(const int8_t* base, uint64_t rows, uint64_t kp, uint64_t S, uint32_t box_rows,
+                                  uint64_t plane_rows = 0) {
     CUtensorMap map;
     const cuuint64_t dims[3] = {kp, rows, S};
-    const cuuint64_t strides[2] = {kp, rows * kp};
+    const cuuint64_t strides[2] = {kp, (plane_rows ? plane_rows : rows) * kp};
     const cuuint32_t box[3] = {BK, box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(base), dims, strides,
@@ -825,11 +827,15 @@ void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* out, uint64
 
 }  // namespace
 
+// a_plane_rows: when nonzero, ap points at row r0 of A planes that are a_plane_rows tall, and the
+// GEMM covers the band of mp rows from there (output planes [S][mp][np] of the band).
 void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
-                         const oztt_ii_plan& p, int mode, void* out, int* err_word, cudaStream_t st) {
+                         const oztt_ii_plan& p, int mode, void* out, int* err_word, cudaStream_t st,
+                         uint64_t a_plane_rows) {
     using namespace gemm;
     if (mp % BM || np % BN || kp % BK || mp == 0 || np == 0 || kp == 0)
         throw Error(OZTT_EINVAL, "residue_gemm: mp, np, kp must be positive multiples of 128, 256 and 128");
+    if (a_plane_rows && a_plane_rows < mp) throw Error(OZTT_EINVAL, "residue_gemm: band taller than its planes");
     if (p.S < 1 || p.S > OZTT_MAXS) throw Error(OZTT_EINVAL, "residue_gemm: bad number of moduli");
     if ((reinterpret_cast<uintptr_t>(ap) | reinterpret_cast<uintptr_t>(bp)) & 15)
         throw Error(OZTT_EINVAL, "residue_gemm: planes must be 16-byte aligned");
@@ -844,7 +850,7 @@ void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64
         udiv_magic(ec.m[s], ec.magic[s], ec.shift[s]);
     }
     const bool pairs = use_pairs();
-    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p.S, pairs ? pair::BM : BM);
+    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p.S, pairs ? pair::BM : BM, a_plane_rows);
     const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p.S, pairs ? pair::BNH : BN);
     if (mode == 0)
         launch_gemm<0>(ta, tb, out, mp, np, kp, (uint32_t)p.S, ec, err_word, st);

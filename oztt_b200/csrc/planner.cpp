@@ -13,6 +13,8 @@
 // per-column quantities are computed in parallel, their totals sequentially, so the results are bit
 // for bit those of the single-threaded reference (x86 80-bit long double where the reference uses it;
 // this file is compiled without floating-point contraction).
+#include <sched.h>
+
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -164,8 +166,20 @@ ModuliChoice choose_moduli_int8(uint32_t K, int num_moduli, int b_cap) {
     return o;
 }
 
+unsigned host_threads() {
+    static const unsigned n = [] {
+        cpu_set_t set;
+        CPU_ZERO(&set);
+        if (sched_getaffinity(0, sizeof set, &set) == 0) {
+            const int c = CPU_COUNT(&set);
+            if (c > 0) return (unsigned)c;
+        }
+        return std::max(1u, std::thread::hardware_concurrency());
+    }();
+    return n;
+}
+
 double pow2_normalizer(const double* v, uint64_t rows, uint64_t cols, uint64_t ld) {
-    std::vector<double> part(std::max<unsigned>(1, std::thread::hardware_concurrency()) + 1, 0.0);
     std::vector<double> row_max(rows, 0.0);
     parallel_ranges(rows, [&](uint64_t b, uint64_t e) {
         for (uint64_t i = b; i < e; ++i) {

@@ -12,10 +12,14 @@
 
 namespace oztt {
 
-// Runs f(begin, end) over [0, n) on up to hardware_concurrency threads.
+// The host threads this process may run on: the CPUs of its affinity mask (a container's share of
+// the machine), else hardware_concurrency. Defined in planner.cpp.
+unsigned host_threads();
+
+// Runs f(begin, end) over [0, n) on up to host_threads() threads.
 template <class F>
 void parallel_ranges(uint64_t n, F&& f) {
-    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const unsigned hw = host_threads();
     const uint64_t nt = std::min<uint64_t>(hw, std::max<uint64_t>(1, n / 64));
     if (nt <= 1) {
         f(0, n);
@@ -113,5 +117,26 @@ int select_slices_int8(const double* a, const double* b, uint64_t m, uint64_t n,
                        uint32_t K);
 int plan_i_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
                 oztt_i_plan& p, std::string& err);
+
+// Scheme II INT8 from host buffers with the transfers overlapped (ii_int8.cu): A and B are uploaded in
+// chunks while the device measures the policy statistics; check(row_max, col_max) receives the
+// magnitude patterns (sign bit cleared) of the maxima of A's m rows and B's n columns once the upload
+// ends, and an exception from it ends the call (as its error code) before the plan and before C is
+// written; then the pipeline runs in row bands with each band of C read back during the next.
+int run_ii_int8_streamed(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                         uint64_t k, uint32_t max_moduli, int32_t reconstruction,
+                         const std::function<void(const uint64_t*, const uint64_t*)>& check, oztt_ii_plan& p,
+                         std::string& err);
+// Host wall-clock phases of the last completed call of run_ii_int8_streamed in this process.
+struct StreamedPhases {
+    double upload_ms = 0;      // from the call to the end of the last host-to-device copy
+    double stats_ms = 0;       // then until the statistics were read back
+    double check_ms = 0;       // then the value checks from the maxima
+    double plan_ms = 0;        // the plan
+    double pipeline_ms = 0;    // scale, split, banded GEMM and reconstruction, C read back
+    double total_ms = 0;
+    int bands = 0;
+};
+StreamedPhases last_streamed_phases();
 
 }  // namespace oztt

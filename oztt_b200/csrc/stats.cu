@@ -16,6 +16,8 @@
 // below): the sums over M and N terms are cheap, and doing them there keeps their order exact.
 #include <algorithm>
 #include <cmath>
+#include <memory>
+#include <mutex>
 #include <random>
 #include <vector>
 
@@ -30,16 +32,18 @@ constexpr int kVectors = 8;
 
 namespace {
 
-// One warp per row: the largest |a| as the 63-bit pattern (nonnegative doubles order like integers).
-__global__ void __launch_bounds__(256) row_absmax_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
-                                                         unsigned long long* __restrict__ out) {
+// One warp per row: the largest |a| over `cols` columns of rows lda apart, as the 63-bit pattern
+// (nonnegative doubles order like integers); with `carry` also over out[row] (earlier columns).
+__global__ void __launch_bounds__(256) row_absmax_kernel(const double* __restrict__ a, uint64_t m, uint64_t cols,
+                                                         uint64_t lda, unsigned long long* __restrict__ out,
+                                                         int carry) {
     const int lane = threadIdx.x & 31;
     const uint64_t nwarps = (uint64_t)gridDim.x * (blockDim.x >> 5);
     const unsigned long long* pu = reinterpret_cast<const unsigned long long*>(a);
     for (uint64_t row = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < m; row += nwarps) {
-        unsigned long long mx = 0;
-        for (uint64_t j = lane; j < k; j += 32) {
-            const unsigned long long v = __ldg(pu + row * k + j) & 0x7FFFFFFFFFFFFFFFull;
+        unsigned long long mx = (carry && lane == 0) ? out[row] : 0ull;
+        for (uint64_t j = lane; j < cols; j += 32) {
+            const unsigned long long v = __ldg(pu + row * lda + j) & 0x7FFFFFFFFFFFFFFFull;
             mx = v > mx ? v : mx;
         }
 #pragma unroll
@@ -66,123 +70,389 @@ __global__ void __launch_bounds__(256) col_absmax_kernel(const double* __restric
     if (mx) atomicMax(out + col, mx);
 }
 
-// sum_c (a[i][c]*rg)^2 for each row i, c ascending, one rounding per operation.
-__global__ void __launch_bounds__(128) row_sumsq_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
-                                                        double rg, double* __restrict__ out) {
-    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= m) return;
-    const double* p = a + i * k;
-    double sq = 0.0;
-    for (uint64_t c = 0; c < k; ++c) {
-        const double v = __dmul_rn(__ldg(p + c), rg);
-        sq = __dadd_rn(sq, __dmul_rn(v, v));
+// Nonzero magnitudes below 2^-383 are the only inputs (with row and column maxima in the validated
+// range, so that the scale rg lies in [2^-128, 2^125]) for which the sums of squares and sketches taken
+// on the unscaled values, scaled by rg afterwards, could differ from the reference's scale-first sums:
+// above that bound x*rg, x^2 and (x*rg)^2 are all normal doubles, so scaling by a power of two commutes
+// with every rounding. The chunked path raises a matrix's `tiny` word when it meets one, and the matrix
+// is then measured again scale-first once its scale is known.
+constexpr double kTinyBound = 0x1p-383;
+
+__device__ __forceinline__ bool is_tiny(double x) { return x != 0.0 && fabs(x) < kTinyBound; }
+
+// Each of the sequential sums below runs as one dependent chain per thread, so its speed is set by
+// the latency of a step, not by bandwidth: the loads of a batch of kBatch steps are issued together
+// (and those of the next batch before the current one is summed), so that a step waits for the
+// arithmetic only.
+constexpr int kBatch = 16;
+constexpr int kSketchBatch = 8;  // the sketch's steps hold more registers
+constexpr int kSketchThreads = 128;
+
+// sum over `len` terms at stride `stride` from p of (x*rg)^2, continuing from sq; raises `small` for a
+// tiny element.
+__device__ __forceinline__ double sumsq_chain(const double* __restrict__ p, uint64_t len, uint64_t stride, double rg,
+                                              double sq, bool& small) {
+    double cur[kBatch], nxt[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) cur[u] = (uint64_t)u < len ? __ldg(p + (uint64_t)u * stride) : 0.0;
+    for (uint64_t j0 = 0; j0 < len; j0 += kBatch) {
+        const uint64_t j1 = j0 + kBatch;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) nxt[u] = j1 + u < len ? __ldg(p + (j1 + u) * stride) : 0.0;
+        const int cnt = len - j0 < (uint64_t)kBatch ? (int)(len - j0) : kBatch;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            if (u < cnt) {
+                small |= is_tiny(cur[u]);
+                const double v = __dmul_rn(cur[u], rg);
+                sq = __dadd_rn(sq, __dmul_rn(v, v));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) cur[u] = nxt[u];
     }
-    out[i] = sq;
+    return sq;
 }
 
-// sum_r (b[r][j]*rg)^2 for each column j, r ascending.
-__global__ void __launch_bounds__(128) col_sumsq_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
-                                                        double rg, double* __restrict__ out) {
+// sum_c (a[i][c]*rg)^2 over `cols` columns of each row i (rows lda apart), c ascending, one rounding
+// per operation; with `carry` the sum continues from out[i] (earlier columns). The scale is rg, or
+// *rgp when rgp is set; gate, when set, skips the kernel unless *gate is nonzero; tiny, when set,
+// receives 1 if a row holds a tiny element.
+__global__ void __launch_bounds__(128) row_sumsq_kernel(const double* __restrict__ a, uint64_t m, uint64_t cols,
+                                                        uint64_t lda, double rg, const double* __restrict__ rgp,
+                                                        double* __restrict__ out, int carry,
+                                                        uint32_t* __restrict__ tiny,
+                                                        const uint32_t* __restrict__ gate) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= m || (gate && *gate == 0u)) return;
+    if (rgp) rg = *rgp;
+    bool small = false;
+    out[i] = sumsq_chain(a + i * lda, cols, 1, rg, carry ? out[i] : 0.0, small);
+    if (tiny && small) atomicOr(tiny, 1u);
+}
+
+// sum_r (b[r][j]*rg)^2 for each column j, r ascending over the `rows` rows given; with `carry` the sum
+// continues from out[j] (the rows of an earlier chunk).
+__global__ void __launch_bounds__(128) col_sumsq_kernel(const double* __restrict__ b, uint64_t rows, uint64_t n,
+                                                        double rg, const double* __restrict__ rgp,
+                                                        double* __restrict__ out, int carry,
+                                                        uint32_t* __restrict__ tiny,
+                                                        const uint32_t* __restrict__ gate) {
     const uint64_t j = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= n) return;
-    double sq = 0.0;
-    for (uint64_t r = 0; r < k; ++r) {
-        const double v = __dmul_rn(__ldg(b + r * n + j), rg);
-        sq = __dadd_rn(sq, __dmul_rn(v, v));
-    }
-    out[j] = sq;
+    if (j >= n || (gate && *gate == 0u)) return;
+    if (rgp) rg = *rgp;
+    bool small = false;
+    out[j] = sumsq_chain(b + j, rows, n, rg, carry ? out[j] : 0.0, small);
+    if (tiny && small) atomicOr(tiny, 1u);
 }
 
 // out[l][r] = (double) sum_{j < cols} ext((x[r][j]*rg)) * ext(v[l][j]), the sum in 64-bit-significand
 // arithmetic, j ascending. Thread t handles row t / 8 and vector t % 8, so a warp reads 4 rows and
-// the 8 vectors; the rows stay in L1 while the warp walks them.
-__global__ void __launch_bounds__(256) sketch_kernel(const double* __restrict__ x, uint64_t rows, uint64_t cols,
-                                                     double rg, const double* __restrict__ v, uint64_t vstride,
-                                                     double* __restrict__ out, uint64_t ostride) {
+// the 8 vectors. The products are independent of the running sum, so only the additions form the
+// chain. UNSCALED: the elements enter as they are and the
+// extended-precision sums are stored (eout) for scaling later.
+// Rows of x lie ldx apart; the sum runs over `cols` columns and, UNSCALED with `carry`, continues from
+// eout (earlier columns).
+template <bool UNSCALED>
+__global__ void __launch_bounds__(128) sketch_kernel(const double* __restrict__ x, uint64_t rows, uint64_t cols,
+                                                     uint64_t ldx, double rg, const double* __restrict__ rgp,
+                                                     const double* __restrict__ v, uint64_t vstride,
+                                                     double* __restrict__ out, ext80::Ext* __restrict__ eout,
+                                                     uint64_t ostride, int carry, const uint32_t* __restrict__ gate) {
     const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t r = t / kVectors, l = t % kVectors;
-    if (r >= rows) return;
-    const double* xr = x + r * cols;
+    if (r >= rows || (gate && *gate == 0u)) return;
+    if (rgp) rg = *rgp;
+    const double* xr = x + r * ldx;
     const double* vl = v + l * vstride;
-    ext80::Ext acc = ext80::zero();
-    for (uint64_t j = 0; j < cols; ++j) {
-        const double xs = __dmul_rn(__ldg(xr + j), rg);
-        acc = ext80::add(acc, ext80::mul(ext80::from_double(xs), ext80::from_double(__ldg(vl + j))));
+    ext80::Ext acc = (UNSCALED && carry) ? eout[l * ostride + r] : ext80::zero();
+    constexpr int B = kSketchBatch;
+    double cx[B], cv[B], nx[B], nv[B];
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+        cx[u] = (uint64_t)u < cols ? __ldg(xr + u) : 0.0;
+        cv[u] = (uint64_t)u < cols ? __ldg(vl + u) : 0.0;
     }
-    out[l * ostride + r] = ext80::to_double(acc);
+    for (uint64_t j0 = 0; j0 < cols; j0 += B) {
+        const uint64_t j1 = j0 + B;
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+            nx[u] = j1 + u < cols ? __ldg(xr + j1 + u) : 0.0;
+            nv[u] = j1 + u < cols ? __ldg(vl + j1 + u) : 0.0;
+        }
+        const int cnt = cols - j0 < (uint64_t)B ? (int)(cols - j0) : B;
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+            const double xs = UNSCALED ? cx[u] : __dmul_rn(cx[u], rg);
+            const ext80::Ext prod = ext80::mul(ext80::from_double(xs), ext80::from_double(cv[u]));
+            if (u < cnt) acc = ext80::add(acc, prod);
+        }
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+            cx[u] = nx[u];
+            cv[u] = nv[u];
+        }
+    }
+    if constexpr (UNSCALED)
+        eout[l * ostride + r] = acc;
+    else
+        out[l * ostride + r] = ext80::to_double(acc);
+}
+
+inline unsigned sketch_blocks(uint64_t rows) {
+    return (unsigned)((rows * kVectors + kSketchThreads - 1) / kSketchThreads);
+}
+
+// The exponent s of a scale rg = 2^s.
+__device__ __forceinline__ int pow2_exponent(double rg) {
+    return (int)((__double_as_longlong(rg) >> 52) & 0x7FF) - 1023;
+}
+
+// Unscaled sums of squares -> scaled: s * rg * rg, both products exact (the results are normal
+// doubles when the matrix held no tiny element). Skipped when *tiny is set.
+__global__ void __launch_bounds__(256) finish_sumsq_kernel(double* __restrict__ s, uint64_t count,
+                                                           const double* __restrict__ rgp,
+                                                           const uint32_t* __restrict__ tiny) {
+    if (*tiny) return;
+    const double rg = *rgp;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x)
+        s[i] = __dmul_rn(__dmul_rn(s[i], rg), rg);
+}
+
+// Unscaled extended sums -> the scaled sums rounded to double: the scale is an exact shift of the
+// exponent. Skipped when *tiny is set.
+__global__ void __launch_bounds__(256) finish_sketch_kernel(const ext80::Ext* __restrict__ e, uint64_t count,
+                                                            const double* __restrict__ rgp,
+                                                            const uint32_t* __restrict__ tiny,
+                                                            double* __restrict__ out) {
+    if (*tiny) return;
+    const int sh = pow2_exponent(*rgp);
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        ext80::Ext t = e[i];
+        if (t.m) t.e += sh;
+        out[i] = ext80::to_double(t);
+    }
+}
+
+// rg = 1 / 2^e for the exponent e of the largest of `count` magnitude patterns, e clamped to
+// [-1000, 1000], and 1 when that largest is zero or infinite (oz_pow2_scale,
+// src/backend/common/norm_estimate.hpp:20-28). NaN patterns are passed over, as the host's std::max
+// over the maxima passes them over. One block.
+__global__ void __launch_bounds__(1024) pow2_scale_kernel(const unsigned long long* __restrict__ maxima,
+                                                          uint64_t count, double* __restrict__ rg) {
+    __shared__ unsigned long long part[32];
+    constexpr unsigned long long kInf = 0x7FF0000000000000ull;
+    unsigned long long mx = 0;
+    for (uint64_t i = threadIdx.x; i < count; i += blockDim.x) {
+        const unsigned long long v = maxima[i];
+        if (v <= kInf && v > mx) mx = v;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+        mx = t > mx ? t : mx;
+    }
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
+    mx = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0ull;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+        mx = t > mx ? t : mx;
+    }
+    if (threadIdx.x == 0) {
+        double r = 1.0;
+        if (mx != 0 && mx < kInf) {
+            int e;
+            frexp(__longlong_as_double((long long)mx), &e);
+            e = min(max(e, -1000), 1000);
+            r = __longlong_as_double((long long)(1023 - e) << 52);  // 2^-e, exact
+        }
+        *rg = r;
+    }
 }
 
 double pattern_to_double(unsigned long long u) { return ext80::double_of(u); }
 
-// 1 / (2^e) for the exponent e of the largest magnitude, e clamped to [-1000, 1000] (oz_pow2_scale).
-double inverse_pow2_scale(double mx) {
-    if (!(mx > 0) || !std::isfinite(mx)) return 1.0;
-    int e;
-    std::frexp(mx, &e);
-    e = std::min(std::max(e, -1000), 1000);
-    return 1.0 / std::ldexp(1.0, e);
+// The 8 Gaussian vectors of length N from mt19937(12345), in the reference's draw order, kept for the
+// last few N of the process (drawing them costs milliseconds at N = 16384).
+std::shared_ptr<const std::vector<double>> policy_vectors(uint32_t N) {
+    static std::mutex mu;
+    static std::vector<std::pair<uint32_t, std::shared_ptr<const std::vector<double>>>> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto& e : cache)
+        if (e.first == N) return e.second;
+    auto g = std::make_shared<std::vector<double>>((size_t)kVectors * N);
+    std::mt19937 rng(12345);
+    std::normal_distribution<double> normal(0.0, 1.0);
+    for (int l = 0; l < kVectors; ++l)
+        for (uint32_t j = 0; j < N; ++j) (*g)[(size_t)l * N + j] = normal(rng);
+    if (cache.size() >= 4) cache.erase(cache.begin());
+    cache.emplace_back(N, g);
+    return g;
 }
 
 }  // namespace
 
-PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
-                                cudaStream_t st) {
-    PolicyStats ps;
-    int dev = 0, sms = 148;
+// The statistics in stages on stream st (and `side` extra streams for the row-local stages of the
+// chunks, so that the chunks' latency-bound sums overlap one another), every stage stream-ordered;
+// collect() is the one synchronisation. Chunk stages measure unscaled values; the finishing stage of
+// each matrix scales them once its scale is known (or, after a tiny element, recomputes scale-first).
+struct PolicyStatsRun::Bufs {
+    Bufs(cudaStream_t st, uint64_t m, uint64_t n, uint64_t k, uint32_t N)
+        : rmax(st, m * 8), cmax(st, n * 8), rg(st, 16), words(st, 16), s2r(st, m * 8), s2c(st, n * 8),
+          dg(st, (uint64_t)kVectors * N * 8), dy(st, (uint64_t)kVectors * k * 8), ds(st, (uint64_t)kVectors * m * 8),
+          ey(st, (uint64_t)kVectors * k * sizeof(ext80::Ext)), es(st, (uint64_t)kVectors * m * sizeof(ext80::Ext)) {}
+    DevBuf rmax, cmax, rg, words, s2r, s2c, dg, dy, ds, ey, es;
+    uint32_t* tiny_a() { return words.as<uint32_t>(); }
+    uint32_t* tiny_b() { return words.as<uint32_t>() + 1; }
+};
+
+PolicyStatsRun::PolicyStatsRun(uint64_t m, uint64_t n, uint64_t k, uint32_t N, cudaStream_t st, int side)
+    : m_(m), n_(n), k_(k), N_(N), st_(st) {
+    int dev = 0;
     OZTT_CUDA(cudaGetDevice(&dev));
-    OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    // maxima
-    DevBuf rmax(st, m * 8), cmax(st, n * 8);
-    OZTT_CUDA(cudaMemsetAsync(cmax.p, 0, n * 8, st));
-    row_absmax_kernel<<<(unsigned)std::min<uint64_t>((m + 7) / 8, (uint64_t)sms * 32), 256, 0, st>>>(
-        a, m, k, rmax.as<unsigned long long>());
-    OZTT_CUDA(cudaGetLastError());
-    {
-        const uint64_t col_blocks = (n + 255) / 256;
-        const uint64_t want = std::max<uint64_t>(1, (uint64_t)sms * 8 / std::max<uint64_t>(col_blocks, 1));
-        const uint64_t chunks = std::min<uint64_t>(std::min<uint64_t>(want, k), 65535);
-        const uint64_t rpc = (k + chunks - 1) / chunks;
-        col_absmax_kernel<<<dim3((unsigned)col_blocks, (unsigned)((k + rpc - 1) / rpc)), 256, 0, st>>>(
-            b, k, n, rpc, cmax.as<unsigned long long>());
-        OZTT_CUDA(cudaGetLastError());
+    OZTT_CUDA(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, dev));
+    for (int i = 0; i < side; ++i) {
+        cudaStream_t x;
+        OZTT_CUDA(cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking));
+        side_.push_back(x);
     }
+    bufs_ = std::make_unique<Bufs>(st, m, n, k, N);
+    OZTT_CUDA(cudaMemsetAsync(bufs_->cmax.p, 0, n * 8, st));
+    OZTT_CUDA(cudaMemsetAsync(bufs_->words.p, 0, 16, st));
+    g_ = policy_vectors(N);
+    OZTT_CUDA(cudaMemcpyAsync(bufs_->dg.p, g_->data(), g_->size() * 8, cudaMemcpyHostToDevice, st));
+}
+
+PolicyStatsRun::~PolicyStatsRun() {
+    for (cudaStream_t x : side_) cudaStreamSynchronize(x);
+    bufs_.reset();  // freed on st, after all side work
+    for (cudaEvent_t e : events_) cudaEventDestroy(e);
+    for (cudaStream_t x : side_) cudaStreamDestroy(x);
+}
+
+void PolicyStatsRun::order(cudaStream_t from, cudaStream_t to) {
+    cudaEvent_t e;
+    OZTT_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    events_.push_back(e);
+    OZTT_CUDA(cudaEventRecord(e, from));
+    OZTT_CUDA(cudaStreamWaitEvent(to, e, 0));
+}
+
+// The stream of the next row-local chunk stage, ordered after everything issued on st so far.
+cudaStream_t PolicyStatsRun::next_side() {
+    if (side_.empty()) return st_;
+    cudaStream_t x = side_[next_++ % side_.size()];
+    order(st_, x);
+    return x;
+}
+
+void PolicyStatsRun::join_sides() {
+    for (cudaStream_t x : side_) order(x, st_);
+}
+
+void PolicyStatsRun::b_rows(const double* b_chunk, uint64_t row0, uint64_t rows) {
+    if (!rows) return;
+    const uint64_t col_blocks = (n_ + 255) / 256;
+    const uint64_t want = std::max<uint64_t>(1, (uint64_t)sms_ * 8 / std::max<uint64_t>(col_blocks, 1));
+    const uint64_t chunks = std::min<uint64_t>(std::min<uint64_t>(want, rows), 65535);
+    const uint64_t rpc = (rows + chunks - 1) / chunks;
+    col_absmax_kernel<<<dim3((unsigned)col_blocks, (unsigned)((rows + rpc - 1) / rpc)), 256, 0, st_>>>(
+        b_chunk, rows, n_, rpc, bufs_->cmax.as<unsigned long long>());
+    OZTT_CUDA(cudaGetLastError());
+    // the column sums continue from the previous chunk: kept in order on st
+    col_sumsq_kernel<<<(unsigned)((n_ + 127) / 128), 128, 0, st_>>>(b_chunk, rows, n_, 1.0, nullptr,
+                                                                    bufs_->s2c.as<double>(), row0 > 0 ? 1 : 0,
+                                                                    bufs_->tiny_b(), nullptr);
+    OZTT_CUDA(cudaGetLastError());
+    // y_l = B g_l for these rows of B (the padded columns add exact zeros), unscaled
+    cudaStream_t x = next_side();
+    sketch_kernel<true><<<sketch_blocks(rows), kSketchThreads, 0, x>>>(b_chunk, rows, n_, n_, 1.0, nullptr,
+                                                                      bufs_->dg.as<double>(), N_, nullptr,
+                                                                      bufs_->ey.as<ext80::Ext>() + row0, k_, 0, nullptr);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void PolicyStatsRun::b_done(const double* b) {
+    join_sides();
+    double* rgB = bufs_->rg.as<double>() + 1;
+    const uint32_t* tiny = bufs_->tiny_b();
+    pow2_scale_kernel<<<1, 1024, 0, st_>>>(bufs_->cmax.as<unsigned long long>(), n_, rgB);
+    OZTT_CUDA(cudaGetLastError());
+    finish_sumsq_kernel<<<(unsigned)std::min<uint64_t>((n_ + 255) / 256, 1024), 256, 0, st_>>>(bufs_->s2c.as<double>(),
+                                                                                               n_, rgB, tiny);
+    OZTT_CUDA(cudaGetLastError());
+    const uint64_t ny = (uint64_t)kVectors * k_;
+    finish_sketch_kernel<<<(unsigned)std::min<uint64_t>((ny + 255) / 256, 1024), 256, 0, st_>>>(
+        bufs_->ey.as<ext80::Ext>(), ny, rgB, tiny, bufs_->dy.as<double>());
+    OZTT_CUDA(cudaGetLastError());
+    // after a tiny element: B again, scale first
+    col_sumsq_kernel<<<(unsigned)((n_ + 127) / 128), 128, 0, st_>>>(b, k_, n_, 0.0, rgB, bufs_->s2c.as<double>(), 0,
+                                                                    nullptr, tiny);
+    OZTT_CUDA(cudaGetLastError());
+    sketch_kernel<false><<<sketch_blocks(k_), kSketchThreads, 0, st_>>>(
+        b, k_, n_, n_, 0.0, rgB, bufs_->dg.as<double>(), N_, bufs_->dy.as<double>(), nullptr, k_, 0, tiny);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void PolicyStatsRun::a_cols(const double* a, uint64_t c0, uint64_t c1) {
+    if (c1 <= c0) return;
+    const uint64_t w = c1 - c0;
+    const int carry = c0 > 0 ? 1 : 0;
+    row_absmax_kernel<<<(unsigned)std::min<uint64_t>((m_ + 7) / 8, (uint64_t)sms_ * 32), 256, 0, st_>>>(
+        a + c0, m_, w, k_, bufs_->rmax.as<unsigned long long>(), carry);
+    OZTT_CUDA(cudaGetLastError());
+    row_sumsq_kernel<<<(unsigned)((m_ + 127) / 128), 128, 0, st_>>>(a + c0, m_, w, k_, 1.0, nullptr,
+                                                                    bufs_->s2r.as<double>(), carry, bufs_->tiny_a(),
+                                                                    nullptr);
+    OZTT_CUDA(cudaGetLastError());
+    // s_l = A y_l over these columns, unscaled, continuing the sums of the earlier columns
+    sketch_kernel<true><<<sketch_blocks(m_), kSketchThreads, 0, st_>>>(a + c0, m_, w, k_, 1.0, nullptr,
+                                                                      bufs_->dy.as<double>() + c0, k_, nullptr,
+                                                                      bufs_->es.as<ext80::Ext>(), m_, carry, nullptr);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void PolicyStatsRun::a_done(const double* a) {
+    join_sides();
+    double* rgA = bufs_->rg.as<double>();
+    const uint32_t* tiny = bufs_->tiny_a();
+    pow2_scale_kernel<<<1, 1024, 0, st_>>>(bufs_->rmax.as<unsigned long long>(), m_, rgA);
+    OZTT_CUDA(cudaGetLastError());
+    finish_sumsq_kernel<<<(unsigned)std::min<uint64_t>((m_ + 255) / 256, 1024), 256, 0, st_>>>(bufs_->s2r.as<double>(),
+                                                                                               m_, rgA, tiny);
+    OZTT_CUDA(cudaGetLastError());
+    const uint64_t ns = (uint64_t)kVectors * m_;
+    finish_sketch_kernel<<<(unsigned)std::min<uint64_t>((ns + 255) / 256, 1024), 256, 0, st_>>>(
+        bufs_->es.as<ext80::Ext>(), ns, rgA, tiny, bufs_->ds.as<double>());
+    OZTT_CUDA(cudaGetLastError());
+    // after a tiny element: A again, scale first
+    row_sumsq_kernel<<<(unsigned)((m_ + 127) / 128), 128, 0, st_>>>(a, m_, k_, k_, 0.0, rgA, bufs_->s2r.as<double>(),
+                                                                    0, nullptr, tiny);
+    OZTT_CUDA(cudaGetLastError());
+    sketch_kernel<false><<<sketch_blocks(m_), kSketchThreads, 0, st_>>>(
+        a, m_, k_, k_, 0.0, rgA, bufs_->dy.as<double>(), k_, bufs_->ds.as<double>(), nullptr, m_, 0, tiny);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+PolicyStats PolicyStatsRun::collect(std::vector<uint64_t>* row_max, std::vector<uint64_t>* col_max) {
+    const uint64_t m = m_, n = n_;
     std::vector<unsigned long long> hr(m), hc(n);
-    OZTT_CUDA(cudaMemcpyAsync(hr.data(), rmax.p, m * 8, cudaMemcpyDeviceToHost, st));
-    OZTT_CUDA(cudaMemcpyAsync(hc.data(), cmax.p, n * 8, cudaMemcpyDeviceToHost, st));
-    OZTT_CUDA(cudaStreamSynchronize(st));
-    double gA = 0, gB = 0;
-    for (auto u : hr) gA = std::max(gA, pattern_to_double(u));
-    for (auto u : hc) gB = std::max(gB, pattern_to_double(u));
-    const double rgA = inverse_pow2_scale(gA), rgB = inverse_pow2_scale(gB);
-    // sums of squares per row / column on the device
-    DevBuf s2r(st, m * 8), s2c(st, n * 8);
-    row_sumsq_kernel<<<(unsigned)((m + 127) / 128), 128, 0, st>>>(a, m, k, rgA, s2r.as<double>());
-    OZTT_CUDA(cudaGetLastError());
-    col_sumsq_kernel<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(b, k, n, rgB, s2c.as<double>());
-    OZTT_CUDA(cudaGetLastError());
-    // the 8 Gaussian vectors of length N from mt19937(12345), in the reference's draw order
-    std::vector<double> g((size_t)kVectors * N);
-    {
-        std::mt19937 rng(12345);
-        std::normal_distribution<double> normal(0.0, 1.0);
-        for (int l = 0; l < kVectors; ++l)
-            for (uint32_t j = 0; j < N; ++j) g[(size_t)l * N + j] = normal(rng);
-    }
-    DevBuf dg(st, g.size() * 8), dy(st, (uint64_t)kVectors * k * 8), ds(st, (uint64_t)kVectors * m * 8);
-    OZTT_CUDA(cudaMemcpyAsync(dg.p, g.data(), g.size() * 8, cudaMemcpyHostToDevice, st));
-    // y_l = B g_l over the real columns (the padded ones add exact zeros), then s_l = A y_l
-    sketch_kernel<<<(unsigned)((k * kVectors + 255) / 256), 256, 0, st>>>(b, k, n, rgB, dg.as<double>(), N,
-                                                                          dy.as<double>(), k);
-    OZTT_CUDA(cudaGetLastError());
-    sketch_kernel<<<(unsigned)((m * kVectors + 255) / 256), 256, 0, st>>>(a, m, k, rgA, dy.as<double>(), k,
-                                                                          ds.as<double>(), m);
-    OZTT_CUDA(cudaGetLastError());
     std::vector<double> h2r(m), h2c(n), hs((size_t)kVectors * m);
-    OZTT_CUDA(cudaMemcpyAsync(h2r.data(), s2r.p, m * 8, cudaMemcpyDeviceToHost, st));
-    OZTT_CUDA(cudaMemcpyAsync(h2c.data(), s2c.p, n * 8, cudaMemcpyDeviceToHost, st));
-    OZTT_CUDA(cudaMemcpyAsync(hs.data(), ds.p, hs.size() * 8, cudaMemcpyDeviceToHost, st));
-    OZTT_CUDA(cudaStreamSynchronize(st));
+    double rg[2] = {0, 0};
+    OZTT_CUDA(cudaMemcpyAsync(hr.data(), bufs_->rmax.p, m * 8, cudaMemcpyDeviceToHost, st_));
+    OZTT_CUDA(cudaMemcpyAsync(hc.data(), bufs_->cmax.p, n * 8, cudaMemcpyDeviceToHost, st_));
+    OZTT_CUDA(cudaMemcpyAsync(rg, bufs_->rg.p, 16, cudaMemcpyDeviceToHost, st_));
+    OZTT_CUDA(cudaMemcpyAsync(h2r.data(), bufs_->s2r.p, m * 8, cudaMemcpyDeviceToHost, st_));
+    OZTT_CUDA(cudaMemcpyAsync(h2c.data(), bufs_->s2c.p, n * 8, cudaMemcpyDeviceToHost, st_));
+    OZTT_CUDA(cudaMemcpyAsync(hs.data(), bufs_->ds.p, hs.size() * 8, cudaMemcpyDeviceToHost, st_));
+    OZTT_CUDA(cudaStreamSynchronize(st_));
+    const double rgA = rg[0], rgB = rg[1];
     // the host's part, in the reference's order
+    PolicyStats ps;
     for (uint64_t r = 0; r < m; ++r) {
         const double mx = pattern_to_double(hr[r]) * rgA;
         if (mx > 0) {
@@ -202,14 +472,26 @@ PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, ui
     double cs2 = 0, cmx = 0;
     for (int l = 0; l < kVectors; ++l) {
         double q = 0;
-        const double* s = hs.data() + (size_t)l * m;
-        for (uint64_t i = 0; i < m; ++i) q += s[i] * s[i];
+        const double* sv = hs.data() + (size_t)l * m;
+        for (uint64_t i = 0; i < m; ++i) q += sv[i] * sv[i];
         cs2 += q;
         cmx = std::max(cmx, q);
     }
     ps.nC = (cs2 - cmx) / (kVectors - 1) / (1.0 + 2.0 * std::sqrt(2.0 / (double)kVectors));
     ps.measured = true;
+    if (row_max) row_max->assign(hr.begin(), hr.end());
+    if (col_max) col_max->assign(hc.begin(), hc.end());
     return ps;
+}
+
+PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
+                                cudaStream_t st) {
+    PolicyStatsRun run(m, n, k, N, st, 0);
+    run.b_rows(b, 0, k);
+    run.b_done(b);
+    run.a_cols(a, 0, k);
+    run.a_done(a);
+    return run.collect();
 }
 
 }  // namespace oztt
@@ -232,7 +514,7 @@ int oztt_stats_absmax(const double* x, uint64_t rows, uint64_t cols, int32_t mod
         auto* o = reinterpret_cast<unsigned long long*>(out);  // nonnegative doubles order like their patterns
         if (mode == 0) {
             oztt::row_absmax_kernel<<<(unsigned)std::min<uint64_t>((rows + 7) / 8, (uint64_t)sms * 32), 256, 0, st>>>(
-                x, rows, cols, o);
+                x, rows, cols, cols, o, 0);
         } else {
             OZTT_CUDA(cudaMemsetAsync(out, 0, cols * 8, st));
             const uint64_t col_blocks = (cols + 255) / 256;
@@ -253,9 +535,11 @@ int oztt_stats_sumsq(const double* x, uint64_t rows, uint64_t cols, int32_t mode
         if (!rows || !cols) return;
         cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
         if (mode == 0)
-            oztt::row_sumsq_kernel<<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(x, rows, cols, rg, out);
+            oztt::row_sumsq_kernel<<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(x, rows, cols, cols, rg, nullptr,
+                                                                                  out, 0, nullptr, nullptr);
         else
-            oztt::col_sumsq_kernel<<<(unsigned)((cols + 127) / 128), 128, 0, st>>>(x, rows, cols, rg, out);
+            oztt::col_sumsq_kernel<<<(unsigned)((cols + 127) / 128), 128, 0, st>>>(x, rows, cols, rg, nullptr, out, 0,
+                                                                                  nullptr, nullptr);
         OZTT_CUDA(cudaGetLastError());
     });
 }
@@ -266,8 +550,8 @@ int oztt_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double rg, 
         if (!x || !v || !out || vstride < cols || ostride < rows) throw Error(OZTT_EINVAL, "stats_sketch: bad arguments");
         if (!rows) return;
         cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-        oztt::sketch_kernel<<<(unsigned)((rows * oztt::kVectors + 255) / 256), 256, 0, st>>>(x, rows, cols, rg, v,
-                                                                                             vstride, out, ostride);
+        oztt::sketch_kernel<false><<<oztt::sketch_blocks(rows), oztt::kSketchThreads, 0, st>>>(
+            x, rows, cols, cols, rg, nullptr, v, vstride, out, nullptr, ostride, 0, nullptr);
         OZTT_CUDA(cudaGetLastError());
     });
 }

@@ -44,3 +44,36 @@ def test_ext80_dot_matches_long_double(oztt, case):
     got = oztt.lib.oztt_test_ext80_dot(x.ctypes.data, g.ctypes.data, n, rg)
     want = reference_dot(x, g, rg)
     assert np.float64(got).view(np.uint64) == np.float64(want).view(np.uint64)
+
+
+def _mixed_case(seed, n=1500):
+    """Sums whose additions hit every alignment of the 64-bit window: exponent gaps around 0, 64 and
+    128 and beyond, carries out of the top bit, exact and near cancellations, full significands."""
+    rng = np.random.default_rng(1000 + seed)
+    style = seed % 4
+    sign = np.where(rng.random(n) < 0.5, -1.0, 1.0)
+    frac = 1.0 + rng.integers(0, 2 ** 52, n) * 2.0 ** -52
+    if style == 0:  # exponent gaps spread over [0, 160]
+        x = sign * frac * np.exp2(rng.integers(-80, 81, n).astype(float))
+        g = frac[::-1] * np.exp2(rng.integers(-80, 81, n).astype(float))
+    elif style == 1:  # gaps clustered at 63, 64, 65 and 127, 128, 129 bits
+        gap = rng.choice([0, 1, 62, 63, 64, 65, 66, 126, 127, 128, 129, 130], n).astype(float)
+        x = sign * frac * np.exp2(-gap)
+        g = 1.0 + rng.integers(0, 2 ** 52, n) * 2.0 ** -52
+    elif style == 2:  # near cancellations: each term undoes most of the previous one
+        base = rng.standard_normal(n)
+        x = base.copy()
+        x[1::2] = -base[:-1:2] * (1.0 + np.exp2(-rng.integers(1, 70, n // 2).astype(float)))
+        g = np.ones(n)
+    else:  # significands full of ones, products rounding at the 64-bit boundary, mixed signs
+        x = sign * (2.0 - np.exp2(-rng.integers(40, 53, n).astype(float)))
+        g = (2.0 - np.exp2(-rng.integers(1, 53, n).astype(float))) * np.exp2(rng.integers(-70, 71, n).astype(float))
+    return x, g
+
+
+@pytest.mark.parametrize("seed", range(16))
+def test_ext80_dot_mixed_alignments(oztt, seed):
+    x, g = _mixed_case(seed)
+    got = oztt.lib.oztt_test_ext80_dot(x.ctypes.data, g.ctypes.data, len(x), 1.0)
+    want = reference_dot(x, g, 1.0)
+    assert np.float64(got).view(np.uint64) == np.float64(want).view(np.uint64), seed

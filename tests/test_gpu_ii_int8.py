@@ -301,3 +301,58 @@ def test_device_run_matches_host_run(oztt, oracle, cuda):
     # repeated calls give the same bits
     oztt.ii_int8_run_device(A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, plan, stream())
     assert np.array_equal(C.cpu().numpy().view(np.uint64), c_host.view(np.uint64))
+
+
+# ---- Context.gemm's streamed path: chunked upload, statistics as chunks land, banded read-back ----------
+# Sizes: B in 64 MiB chunks of rows, A in blocks of max(512, 64 MiB / 8m) columns, row bands of about
+# 2048 rows (up to 8). (9000, 256, 256): one piece each, 4 bands, a ragged last band; (4500, 4608, 2048):
+# B in two chunks, A in two column blocks (the last one ragged), 2 bands.
+# (3000, 2048, 4608): two chunks of B and two column blocks of A, with tiny elements (below 2^-383) in
+# both operands.
+@pytest.mark.parametrize("m,n,k,phi,seed", [(9000, 256, 256, 0.5, 31), (4500, 4608, 2048, 1.0, 32),
+                                            (3000, 2048, 4608, 1.0, 33)])
+def test_context_streamed_matches_planned_run(oztt, oracle, cuda, m, n, k, phi, seed):
+    a, b = oracle.gen_inputs(m, n, k, phi, seed)
+    if seed == 33:
+        a[7], a[m * k // 2] = 2.0 ** -600, -5e-324
+        b[k * n - 5] = 2.0 ** -450
+    plan = plan_for(oztt, a, b, m, n, k)  # host statistics
+    c_ref = oztt.ii_int8_run(a, b, m, n, k, plan)
+    c = np.full(m * n, 123.0)
+    info = oztt.Context().gemm(a, b, c, m, n, k, oztt.Options(format=oztt.Format.INT8))
+    assert info.moduli == plan.S and info.integer_bits == plan.b
+    assert info.reconstruction_passes == (2 if plan.two_pass else 1)
+    assert np.array_equal(c.view(np.uint64), c_ref.view(np.uint64))
+    ph = oztt.ii_int8_last_phases()
+    assert ph["bands"] == expected_bands(m)
+    assert ph["total_ms"] > 0 and ph["upload_ms"] > 0
+
+
+def expected_bands(m):
+    mp = round_up(m, 128)
+    bm = round_up(-(-mp // min(8, max(1, mp // 2048))), 128)
+    return -(-mp // bm)
+
+
+def test_context_streamed_reports_check_errors_first(oztt, cuda):
+    """A value error found by the host checks that run during the upload is the error reported, and C
+    stays untouched, also when the plan would fail (max_moduli = 2)."""
+    ctx = oztt.Context()
+    m = n = k = 300
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal(m * k)
+    b = rng.standard_normal(k * n)
+    a[m * k - 1] = np.nan
+    c = np.full(m * n, 123.0)
+    for opt in (oztt.Options(format=oztt.Format.INT8), oztt.Options(format=oztt.Format.INT8, max_moduli=2)):
+        with pytest.raises(ValueError, match="A contains NaN or infinity"):
+            ctx.gemm(a, b, c, m, n, k, opt)
+    a[m * k - 1] = 1.0
+    b[5] = 2.0 ** 130
+    with pytest.raises(ValueError, match="must be in"):
+        ctx.gemm(a, b, c, m, n, k, oztt.Options(format=oztt.Format.INT8))
+    assert np.all(c == 123.0)
+    # a valid call afterwards runs normally
+    b[5] = 1.0
+    ctx.gemm(a, b, c, m, n, k, oztt.Options(format=oztt.Format.INT8))
+    assert np.all(np.isfinite(c))

@@ -15,7 +15,9 @@ def _stream():
 
 CASES = [("uniform", 128, 128, 128, -1.0, {}), ("phi0.5", 300, 200, 500, 0.5, {}), ("phi4", 97, 131, 77, 4.0, {}),
          ("ragged", 1, 70, 1000, 1.0, {}), ("two-pass", 256, 256, 256, 2.0, {"reconstruction": 2}),
-         ("max16", 200, 100, 300, 0.5, {"max_moduli": 16}), ("fixed-auto", 64, 64, 64, 1.0, {"fixed_bits": 58})]
+         ("max16", 200, 100, 300, 0.5, {"max_moduli": 16}), ("fixed-auto", 64, 64, 64, 1.0, {"fixed_bits": 58}),
+         ("tiny-a", 150, 90, 260, 1.0, {}), ("tiny-b", 70, 180, 333, 1.0, {}), ("near-bound", 129, 65, 200, 1.0, {}),
+         ("large-scale", 100, 100, 100, 1.0, {})]
 
 
 @pytest.mark.parametrize("name,m,n,k,phi,kw", CASES)
@@ -24,6 +26,20 @@ def test_device_plan_equals_host_plan(oztt, oracle, cuda, name, m, n, k, phi, kw
     if name == "ragged":
         a[: k // 3] = 0.0  # a run of zeros and a row scale far from the others
         b[::7] *= 2.0 ** -40
+    # Nonzero magnitudes below 2^-383 send the device statistics to their scale-first recomputation;
+    # at and above it the unscaled sums, scaled afterwards, must give the same bits.
+    if name == "tiny-a":
+        a[5], a[17], a[k + 3] = 2.0 ** -500, 5e-324, -(2.0 ** -384)
+    if name == "tiny-b":
+        b[3], b[n + 1] = -(2.0 ** -700), 2.0 ** -1000
+    if name == "near-bound":
+        a[::11] = 2.0 ** -383
+        b[::13] = -(2.0 ** -383)
+    if name == "large-scale":
+        a *= 2.0 ** 100
+        b *= 2.0 ** -100
+        a[::9] = 2.0 ** -280
+        b[::5] = 2.0 ** -380
     host = oztt.ii_int8_plan(a, b, m, n, k, **kw)
     A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
     dev = oztt.ii_int8_plan_device(A.data_ptr(), B.data_ptr(), m, n, k, stream=_stream(), **kw)
