@@ -43,7 +43,7 @@ CXX_FLAGS_BY_SOURCE = {"planner.cpp": ["-O3", "-march=x86-64-v3"], "planner1.cpp
                        "planner_digit.cpp": ["-O3", "-march=x86-64-v3"]}
 
 CU_SOURCES = ["split.cu", "gemm_i8.cu", "recon.cu", "ii_int8.cu", "ii_digit.cu", "noalloc.cu", "scheme1.cu",
-              "stats.cu"]
+              "stats.cu", "profile.cu"]
 CPP_SOURCES = ["planner.cpp", "planner1.cpp", "planner_digit.cpp", "context.cpp", "evaluation.cpp"]
 
 
@@ -63,7 +63,8 @@ def _stale(target: Path, deps: list[Path]) -> bool:
 def build_library(force: bool = False) -> Path:
     OUT.mkdir(parents=True, exist_ok=True)
     headers = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.hpp")) + [ROOT / "include" / "oztt_cuda.h",
-                                                                      ROOT / "include" / "ozTTgemm" / "ozTTgemm.hpp"]
+                                                                      ROOT / "include" / "ozTTgemm" / "ozTTgemm.hpp",
+                                                                      ROOT / "include" / "evaluation_hooks.hpp"]
     objs = []
     for src in CU_SOURCES:
         s, o = CSRC / src, OUT / (src + ".o")
@@ -96,11 +97,14 @@ def build_programs(force: bool = False) -> None:
 
 def build_oracle() -> None:
     """The CPU checker libraries (test infrastructure): oracle/liboz2oracle.so always, and
-    oracle/_ref/*.so when the reference tree is present on this machine."""
+    oracle/_ref/*.so and the reference's caller programs when the reference tree is present on this
+    machine."""
     make = shutil.which("make") or "make"
     _run([make, "-s", "-C", str(ROOT / "oracle"), "all"])
     if Path("/root/reference/src/backend").is_dir():
         _run([make, "-s", "-C", str(ROOT / "oracle"), "ref"])
+        # the reference's own callers of the public API, compiled unchanged against liboztt.so
+        _run([make, "-s", "-C", str(ROOT / "oracle"), "callers"])
 
 
 def build(force: bool = False) -> None:

@@ -11,9 +11,13 @@
 //   * all input is consumed before C is written, so C may overlap A or B.
 // For INT8 Scheme II the finiteness and range checks are made from the device-measured row and column
 // maxima once A and B are uploaded, before the plan is made and C is written.
+// Under an evaluation Scope (include/evaluation_hooks.hpp, the reference's src/evaluation_hooks.hpp) a
+// call runs its device pipeline through the evaluator's phase timing and whole-pass check, with the
+// Ozaki II width the Scope fixes (src/ozaki2.cpp:447).
 // Dispatch (src/dispatch.cpp:18-50): INT8, FP8 (e4m3 digits), BF16, FP16 and TF32 are built, both schemes;
 // the Tenstorrent block formats BFP8/BFP4/BFP2 are not available on this hardware.
 #include <ozTTgemm/ozTTgemm.hpp>
+#include <evaluation_hooks.hpp>
 
 #include <algorithm>
 #include <cmath>
@@ -29,12 +33,14 @@
 
 namespace oztt {
 int run_ii_digit_planned(int device_id, int32_t format, const double* a, const double* b, double* c, uint64_t m,
-                         uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_digit_plan& p,
-                         std::string& err);
+                         uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits,
+                         oztt_digit_plan& p, std::string& err);
 }  // namespace oztt
 
 namespace ozTTgemm {
 namespace {
+
+namespace ev = detail::evaluation;
 
 std::mutex runtime_mutex;
 
@@ -131,7 +137,9 @@ struct Checked {
 // order), before the plan and before C is written; should the device fail before that, the host
 // checks run after all, so that an invalid input is still the error reported. The other paths run
 // the host checks here, before the device is touched.
-bool checks_during_upload(const Options& o) { return o.scheme == Scheme::II && o.format == Format::INT8; }
+bool checks_during_upload(const Options& o) {
+    return o.scheme == Scheme::II && o.format == Format::INT8 && ev::active == nullptr;
+}
 
 Checked validate(const Options& options, std::span<const double> a, std::span<const double> b,
                  std::optional<std::size_t> c_size, std::size_t m, std::size_t n, std::size_t k) {
@@ -148,6 +156,18 @@ Checked validate(const Options& options, std::span<const double> a, std::span<co
     if (!checks_during_upload(options)) check_values(a, b, m, n, k);
     return v;
 }
+Info ii_info(const oztt_ii_plan& plan, const Options& opt, const Checked& v) {
+    Info info{Scheme::II, opt.format};
+    info.moduli = (std::uint32_t)plan.S;
+    info.integer_bits = (std::uint32_t)plan.b;
+    info.reconstruction_passes = plan.two_pass ? 2u : 1u;
+    info.padded_m = v.mp;
+    info.padded_n = v.np;
+    info.padded_k = v.kp;
+    return info;
+}
+// The Ozaki II width an evaluation Scope open on this thread fixes (0: none).
+std::int32_t evaluation_fixed_bits() { return ev::active ? (std::int32_t)ev::active->fixed_bits : 0; }
 int32_t recon_code(Reconstruction r) {
     return r == Reconstruction::OnePass ? OZTT_RECON_ONE : (r == Reconstruction::TwoPass ? OZTT_RECON_TWO : OZTT_RECON_AUTO);
 }
@@ -198,7 +218,8 @@ Info Context::Impl::execute(std::span<const double> a, std::span<const double> b
         oztt_digit_plan plan;
         std::string msg;
         const int rc = oztt::run_ii_digit_planned(options.device_id, (int32_t)opt.format, a.data(), b.data(), c.data(),
-                                                  m, n, k, opt.max_moduli, recon_code(opt.reconstruction), plan, msg);
+                                                  m, n, k, opt.max_moduli, recon_code(opt.reconstruction),
+                                                  evaluation_fixed_bits(), plan, msg);
         if (rc != OZTT_OK) rethrow(rc, msg);
         opened = true;
         Info info{Scheme::II, opt.format};
@@ -227,6 +248,18 @@ Info Context::Impl::execute(std::span<const double> a, std::span<const double> b
         info.padded_k = v.kp;
         return info;
     }
+    if (ev::active) {
+        // a profiled call of the evaluator (its values were checked on the host in validate): the plain
+        // upload and the pipeline under the Scope's phase timing and whole-pass check
+        oztt_ii_plan plan;
+        std::string msg;
+        const int rc = oztt::run_ii_int8_uploaded(options.device_id, a.data(), b.data(), c.data(), m, n, k,
+                                                  opt.max_moduli, recon_code(opt.reconstruction),
+                                                  evaluation_fixed_bits(), plan, msg);
+        if (rc != OZTT_OK) rethrow(rc, msg);
+        opened = true;
+        return ii_info(plan, opt, v);
+    }
     // A and B go to the device in chunks; the precision policy measures them there (bit-identical to the
     // host measurement), the values are checked from the measured maxima and the host makes the
     // decisions; C is written only after that.
@@ -244,14 +277,7 @@ Info Context::Impl::execute(std::span<const double> a, std::span<const double> b
         rethrow(rc, msg);
     }
     opened = true;
-    Info info{Scheme::II, opt.format};
-    info.moduli = (std::uint32_t)plan.S;
-    info.integer_bits = (std::uint32_t)plan.b;
-    info.reconstruction_passes = plan.two_pass ? 2u : 1u;
-    info.padded_m = v.mp;
-    info.padded_n = v.np;
-    info.padded_k = v.kp;
-    return info;
+    return ii_info(plan, opt, v);
 }
 
 Info Context::gemm(std::span<const double> a, std::span<const double> b, std::span<double> c, std::size_t m,

@@ -78,43 +78,40 @@ void run_ii_digit_device(const double* a, const double* b, double* c, uint64_t m
     OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
-    cudaEvent_t ev[7] = {};
-    struct Events {
-        cudaEvent_t* e;
-        bool on;
-        ~Events() {
-            if (on)
-                for (int i = 0; i < 7; ++i)
-                    if (e[i]) cudaEventDestroy(e[i]);
-        }
-    } events{ev, stage_ms != nullptr};
-    auto mark = [&](int i) {
-        if (stage_ms) OZTT_CUDA(cudaEventRecord(ev[i], st));
-    };
-    if (stage_ms)
-        for (auto& e : ev) OZTT_CUDA(cudaEventCreate(&e));
-    mark(0);
-    launch_scale_rows(a, m, k, k, p.shift, dA.as<int32_t>(), nullptr, flags, st);
-    mark(1);
-    launch_scale_cols(b, k, n, n, p.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
-    mark(2);
-    launch_digit_split_rows(a, m, k, k, dA.as<int32_t>(), fp, da.as<int8_t>(), mp, kp, st);
-    mark(3);
-    launch_digit_split_cols(b, k, n, n, dB.as<int32_t>(), fp, db.as<int8_t>(), np, kp, st);
-    mark(4);
-    launch_digit_gemm(da.as<int8_t>(), db.as<int8_t>(), mp, np, kp, fp, 1, kd.p, gemm_err, st);
-    mark(5);
-    launch_recon_u16(kd.as<uint16_t>(), mp, np, dA.as<int32_t>(), dB.as<int32_t>(), p, c, m, n, n, st);
-    mark(6);
+    // the stages as the evaluator sees them (the composition is fused into the GEMM epilogue)
+    Pipeline pl;
+    pl.add(kScale, kHead, 0, [&] { launch_scale_rows(a, m, k, k, p.shift, dA.as<int32_t>(), nullptr, flags, st); });
+    pl.add(kScale, kHead, 1, [&] {
+        launch_scale_cols(b, k, n, n, p.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
+    });
+    pl.add(kSlice, kHead, 2,
+           [&] { launch_digit_split_rows(a, m, k, k, dA.as<int32_t>(), fp, da.as<int8_t>(), mp, kp, st); });
+    pl.add(kSlice, kHead, 3,
+           [&] { launch_digit_split_cols(b, k, n, n, dB.as<int32_t>(), fp, db.as<int8_t>(), np, kp, st); });
+    pl.add(kGemm, kGemmStep, 4,
+           [&] { launch_digit_gemm(da.as<int8_t>(), db.as<int8_t>(), mp, np, kp, fp, 1, kd.p, gemm_err, st); });
+    // under an evaluation Scope a two-pass plan's reconstruction is timed as two launches (row halves)
+    const uint64_t halves = (evaluation_active() && p.two_pass && m > 1) ? 2 : 1;
+    for (uint64_t h = 0; h < halves; ++h) {
+        const uint64_t r0 = m * h / halves, rows = m * (h + 1) / halves - r0;
+        pl.add(kRecon, kReconStep, 5, [&, r0, rows] {
+            launch_recon_u16(kd.as<uint16_t>() + r0 * np, mp, np, dA.as<int32_t>() + r0, dB.as<int32_t>(), p,
+                             c + r0 * n, rows, n, n, st);
+        }, true);
+    }
+    pl.writes(dA.p, mp * 4);
+    pl.writes(dB.p, np * 4);
+    pl.writes(da.p, NP * mp * kp);
+    pl.writes(db.p, NP * np * kp);
+    pl.writes(kd.p, S * mp * np * 2);
+    pl.writes(c, m * n * 8);
+    pl.out = c;
+    pl.out_bytes = m * n * 8;
+    pl.partial_products = (unsigned)fp.nprod;
+    if (!run_profiled(pl, st)) pl.run(st, stage_ms, 6);
     uint32_t host_words[2] = {0, 0};
     OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
     OZTT_CUDA(cudaStreamSynchronize(st));
-    if (stage_ms)
-        for (int i = 0; i < 6; ++i) {
-            float ms = 0;
-            OZTT_CUDA(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
-            stage_ms[i] = ms;
-        }
     check_flags(host_words[0], (int)host_words[1]);
 }
 
@@ -141,11 +138,12 @@ static void with_stream(int device_id, const std::function<void(cudaStream_t)>& 
     f(st);
 }
 
-// The whole call as Context::gemm makes it: A and B to the device, the plan from device statistics, the
-// pipeline, C back. Returns OZTT_OK, or an error code with its message (C is then untouched).
+// The whole call as Context::gemm makes it: A and B to the device, the plan from device statistics (the
+// width fixed to fixed_bits when nonzero), the pipeline, C back. Returns OZTT_OK, or an error code with
+// its message (C is then untouched).
 int run_ii_digit_planned(int device_id, int32_t format, const double* a, const double* b, double* c, uint64_t m,
-                         uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction, oztt_digit_plan& p,
-                         std::string& err) {
+                         uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits,
+                         oztt_digit_plan& p, std::string& err) {
     char buf[1024];
     int inner = OZTT_OK;
     const int rc = guarded(buf, sizeof buf, [&] {
@@ -153,8 +151,8 @@ int run_ii_digit_planned(int device_id, int32_t format, const double* a, const d
             DevBuf da(st, m * k * 8), db(st, k * n * 8);
             OZTT_CUDA(cudaMemcpyAsync(da.p, a, m * k * 8, cudaMemcpyHostToDevice, st));
             OZTT_CUDA(cudaMemcpyAsync(db.p, b, k * n * 8, cudaMemcpyHostToDevice, st));
-            inner = plan_digit_device(format, da.as<double>(), db.as<double>(), m, n, k, max_moduli, reconstruction, 0,
-                                      p, err, st);
+            inner = plan_digit_device(format, da.as<double>(), db.as<double>(), m, n, k, max_moduli, reconstruction,
+                                      fixed_bits, p, err, st);
             if (inner != OZTT_OK) return;
             DevBuf dc(st, m * n * 8);
             run_ii_digit_device(da.as<double>(), db.as<double>(), dc.as<double>(), m, n, k, p, st);

@@ -85,7 +85,10 @@ void check_flags(uint32_t flags, int gemm_err) {
 
 // The device pipeline on device buffers (row-major, lda = k, ldb = n, ldc = n).
 // stage_ms (optional, 6 entries): device time of scale rows, scale cols, split rows, split cols, residue
-// GEMM and reconstruction, from CUDA events recorded on `st` between the launches.
+// GEMM and reconstruction, from CUDA events recorded on `st` between the launches. Under an evaluation
+// Scope the launches run through the evaluator's phase timing and whole-pass check instead
+// (run_profiled); a two-pass plan's reconstruction is then timed as two launches, one per half of the
+// rows, so that the evaluator sees one reconstruction interval per pass.
 void run_ii_int8_device(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
                         const oztt_ii_plan& p, cudaStream_t st, double* stage_ms = nullptr) {
     check_plan(p);
@@ -96,43 +99,36 @@ void run_ii_int8_device(const double* a, const double* b, double* c, uint64_t m,
     OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
-    cudaEvent_t ev[7] = {};
-    struct Events {
-        cudaEvent_t* e;
-        bool on;
-        ~Events() {
-            if (on)
-                for (int i = 0; i < 7; ++i)
-                    if (e[i]) cudaEventDestroy(e[i]);
-        }
-    } events{ev, stage_ms != nullptr};
-    auto mark = [&](int i) {
-        if (stage_ms) OZTT_CUDA(cudaEventRecord(ev[i], st));
-    };
-    if (stage_ms)
-        for (auto& e : ev) OZTT_CUDA(cudaEventCreate(&e));
-    mark(0);
-    launch_scale_rows(a, m, k, k, p.shift, dA.as<int32_t>(), nullptr, flags, st);
-    mark(1);
-    launch_scale_cols(b, k, n, n, p.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
-    mark(2);
-    launch_split_rows(a, m, k, k, dA.as<int32_t>(), p, ra.as<int8_t>(), mp, kp, st);
-    mark(3);
-    launch_split_cols(b, k, n, n, dB.as<int32_t>(), p, rb.as<int8_t>(), np, kp, st);
-    mark(4);
-    launch_residue_gemm(ra.as<int8_t>(), rb.as<int8_t>(), mp, np, kp, p, 1, kpl.p, gemm_err, st);
-    mark(5);
-    launch_recon(kpl.as<uint8_t>(), mp, np, dA.as<int32_t>(), dB.as<int32_t>(), p, c, m, n, n, st);
-    mark(6);
+    Pipeline pl;
+    pl.add(kScale, kHead, 0, [&] { launch_scale_rows(a, m, k, k, p.shift, dA.as<int32_t>(), nullptr, flags, st); });
+    pl.add(kScale, kHead, 1, [&] {
+        launch_scale_cols(b, k, n, n, p.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
+    });
+    pl.add(kSlice, kHead, 2, [&] { launch_split_rows(a, m, k, k, dA.as<int32_t>(), p, ra.as<int8_t>(), mp, kp, st); });
+    pl.add(kSlice, kHead, 3, [&] { launch_split_cols(b, k, n, n, dB.as<int32_t>(), p, rb.as<int8_t>(), np, kp, st); });
+    pl.add(kGemm, kGemmStep, 4,
+           [&] { launch_residue_gemm(ra.as<int8_t>(), rb.as<int8_t>(), mp, np, kp, p, 1, kpl.p, gemm_err, st); });
+    const uint64_t halves = (evaluation_active() && p.two_pass && m > 1) ? 2 : 1;
+    for (uint64_t h = 0; h < halves; ++h) {
+        const uint64_t r0 = m * h / halves, rows = m * (h + 1) / halves - r0;
+        pl.add(kRecon, kReconStep, 5, [&, r0, rows] {
+            launch_recon(kpl.as<uint8_t>() + r0 * np, mp, np, dA.as<int32_t>() + r0, dB.as<int32_t>(), p, c + r0 * n,
+                         rows, n, n, st);
+        }, true);
+    }
+    pl.writes(dA.p, mp * 4);
+    pl.writes(dB.p, np * 4);
+    pl.writes(ra.p, S * mp * kp);
+    pl.writes(rb.p, S * np * kp);
+    pl.writes(kpl.p, S * mp * np);
+    pl.writes(c, m * n * 8);
+    pl.out = c;
+    pl.out_bytes = m * n * 8;
+    pl.partial_products = (unsigned)S;
+    if (!run_profiled(pl, st)) pl.run(st, stage_ms, 6);
     uint32_t host_words[2] = {0, 0};
     OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
     OZTT_CUDA(cudaStreamSynchronize(st));
-    if (stage_ms)
-        for (int i = 0; i < 6; ++i) {
-            float ms = 0;
-            OZTT_CUDA(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
-            stage_ms[i] = ms;
-        }
     check_flags(host_words[0], (int)host_words[1]);
 }
 
@@ -168,6 +164,40 @@ int plan_ii_int8_device(const double* a, const double* b, uint64_t m, uint64_t n
                         cudaStream_t st) {
     return plan_ii_int8_with([&](uint32_t N, uint32_t) { return device_policy_stats(a, b, m, n, k, N, st); }, m, n,
                              k, max_moduli, reconstruction, fixed_bits, p, err);
+}
+
+// The call from host buffers without overlap, as the evaluator's profiled calls make it: A and B to the
+// device, the plan from device statistics (the width fixed to fixed_bits when nonzero), the pipeline
+// (under the evaluation Scope), C back. Returns OZTT_OK, or an error code with its message.
+int run_ii_int8_uploaded(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                         uint64_t k, uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan& p,
+                         std::string& err) {
+    char buf[1024];
+    int inner = OZTT_OK;
+    const int rc = guarded(buf, sizeof buf, [&] {
+        open_device(device_id);
+        cudaStream_t st;
+        OZTT_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+        struct StreamGuard {
+            cudaStream_t s;
+            ~StreamGuard() {
+                cudaStreamSynchronize(s);
+                cudaStreamDestroy(s);
+            }
+        } guard{st};
+        DevBuf da(st, m * k * 8), db(st, k * n * 8);
+        OZTT_CUDA(cudaMemcpyAsync(da.p, a, m * k * 8, cudaMemcpyHostToDevice, st));
+        OZTT_CUDA(cudaMemcpyAsync(db.p, b, k * n * 8, cudaMemcpyHostToDevice, st));
+        inner = plan_ii_int8_device(da.as<double>(), db.as<double>(), m, n, k, max_moduli, reconstruction, fixed_bits,
+                                    p, err, st);
+        if (inner != OZTT_OK) return;
+        DevBuf dc(st, m * n * 8);
+        run_ii_int8_device(da.as<double>(), db.as<double>(), dc.as<double>(), m, n, k, p, st);
+        OZTT_CUDA(cudaMemcpyAsync(c, dc.p, m * n * 8, cudaMemcpyDeviceToHost, st));
+        OZTT_CUDA(cudaStreamSynchronize(st));
+    });
+    if (rc != OZTT_OK) err = buf;
+    return rc != OZTT_OK ? rc : inner;
 }
 
 // ---- the call from host buffers, transfers overlapped ----------------------------------------------

@@ -3,8 +3,10 @@
 // the read-back checks of the range flags and the GEMM wait-timeout word.
 #pragma once
 #include <algorithm>
+#include <functional>
 #include <memory>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "oztt_common.cuh"
@@ -42,6 +44,43 @@ struct DevBuf {
     DevBuf(const DevBuf&) = delete;
     DevBuf& operator=(const DevBuf&) = delete;
 };
+
+// One device pipeline as an ordered list of launches on one stream. Each launch belongs to a stage of
+// the evaluator hooks (include/evaluation_hooks.hpp: kScale .. kRecon), is a kind of device step
+// (kHead .. kComposeStep) and fills one slot of the caller's per-stage timings; consecutive launches
+// of one stage form one timed phase unless a launch opens a new one.
+enum EvStage { kScale = 0, kSlice = 1, kGemm = 2, kCompose = 3, kRecon = 4 };
+enum EvStep { kHead = 0, kGemmStep = 1, kReconStep = 2, kComposeStep = 3 };
+
+struct Pipeline {
+    struct Launch {
+        int stage, step, slot, phase;
+        std::function<void()> issue;
+    };
+    std::vector<Launch> launches;
+    std::vector<std::pair<void*, size_t>> written;  // buffers the pass writes (whole-pass sentinel fill)
+    void* out = nullptr;                            // the output the whole-pass check compares
+    size_t out_bytes = 0;
+    unsigned partial_products = 0;                  // products the GEMM stage forms
+    void add(int stage, int step, int slot, std::function<void()> issue, bool new_phase = false) {
+        const bool next = launches.empty() || new_phase || launches.back().stage != stage;
+        const int phase = launches.empty() ? 0 : launches.back().phase + (next ? 1 : 0);
+        launches.push_back({stage, step, slot, phase, std::move(issue)});
+    }
+    void writes(void* p, size_t bytes) { written.push_back({p, bytes}); }
+    // Issues every launch in order; stage_ms (optional, `slots` entries) receives the device time of
+    // each slot from CUDA events recorded between them.
+    void run(cudaStream_t st, double* stage_ms = nullptr, int slots = 0) const;
+};
+
+// Under an evaluation Scope open on this thread (evaluation_hooks.hpp): runs the pipeline with the
+// evaluator's phase timing and, when asked, its whole-pass check and timing, and reports the GEMM's
+// partial products and grid; returns false, running nothing, when no Scope is open.
+bool run_profiled(const Pipeline& pl, cudaStream_t st);
+// The scaled-integer width of Ozaki II that the open Scope fixes (0: none, or no Scope).
+unsigned evaluation_fixed_bits();
+// True while a Scope is open on this thread.
+bool evaluation_active();
 
 struct PolicyStats;
 

@@ -454,41 +454,37 @@ void run_i_device(const double* a, const double* b, double* c, uint64_t m, uint6
     OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
-    cudaEvent_t ev[6] = {};
-    struct Events {
-        cudaEvent_t* e;
-        ~Events() {
-            for (int i = 0; i < 6; ++i)
-                if (e[i]) cudaEventDestroy(e[i]);
-        }
-    } events{ev};
-    if (stage_ms)
-        for (auto& e : ev) OZTT_CUDA(cudaEventCreate(&e));
-    auto mark = [&](int i) {
-        if (stage_ms) OZTT_CUDA(cudaEventRecord(ev[i], st));
-    };
-    mark(0);
-    launch_scale_rows_mode(a, m, k, k, -1, f.ceil, dA.as<int32_t>(), nullptr, flags, st);
-    mark(1);
-    launch_scale_cols_mode(b, k, n, n, -1, f.ceil, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(),
-                           st);
-    mark(2);
-    launch_slice_rows(a, m, k, k, dA.as<int32_t>(), p, format, sa.as<int8_t>(), mp, kp, st);
-    launch_slice_cols(b, k, n, n, dB.as<int32_t>(), p, format, sb.as<int8_t>(), np, kp, st);
-    mark(3);
-    launch_diag_gemm(sa.as<int8_t>(), sb.as<int8_t>(), mp, np, kp, p, pd.as<int32_t>(), gemm_err, st);
-    mark(4);
-    launch_horner(pd.as<int32_t>(), mp, np, dA.as<int32_t>(), dB.as<int32_t>(), p, format, c, m, n, n, st);
-    mark(5);
+    // The evaluator's Scheme I has no scale stage: the scaling belongs to the slice stage, as in the
+    // reference's slicing programs (src/ozaki1.cpp:113-118).
+    Pipeline pl;
+    pl.add(kSlice, kHead, 0,
+           [&] { launch_scale_rows_mode(a, m, k, k, -1, f.ceil, dA.as<int32_t>(), nullptr, flags, st); });
+    pl.add(kSlice, kHead, 1, [&] {
+        launch_scale_cols_mode(b, k, n, n, -1, f.ceil, dB.as<int32_t>(), nullptr, flags,
+                               colmax.as<unsigned long long>(), st);
+    });
+    pl.add(kSlice, kHead, 2,
+           [&] { launch_slice_rows(a, m, k, k, dA.as<int32_t>(), p, format, sa.as<int8_t>(), mp, kp, st); });
+    pl.add(kSlice, kHead, 2,
+           [&] { launch_slice_cols(b, k, n, n, dB.as<int32_t>(), p, format, sb.as<int8_t>(), np, kp, st); });
+    pl.add(kGemm, kGemmStep, 3,
+           [&] { launch_diag_gemm(sa.as<int8_t>(), sb.as<int8_t>(), mp, np, kp, p, pd.as<int32_t>(), gemm_err, st); });
+    pl.add(kRecon, kReconStep, 4, [&] {
+        launch_horner(pd.as<int32_t>(), mp, np, dA.as<int32_t>(), dB.as<int32_t>(), p, format, c, m, n, n, st);
+    });
+    pl.writes(dA.p, mp * 4);
+    pl.writes(dB.p, np * 4);
+    pl.writes(sa.p, P * mp * kp);
+    pl.writes(sb.p, P * np * kp);
+    pl.writes(pd.p, P * mp * np * 4);
+    pl.writes(c, m * n * 8);
+    pl.out = c;
+    pl.out_bytes = m * n * 8;
+    pl.partial_products = (unsigned)(P * (P + 1) / 2);
+    if (!run_profiled(pl, st)) pl.run(st, stage_ms, 5);
     uint32_t host_words[2] = {0, 0};
     OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
     OZTT_CUDA(cudaStreamSynchronize(st));
-    if (stage_ms)
-        for (int i = 0; i < 5; ++i) {
-            float ms = 0;
-            OZTT_CUDA(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
-            stage_ms[i] = ms;
-        }
     check_flags(host_words[0], (int)host_words[1]);
 }
 
