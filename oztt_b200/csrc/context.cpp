@@ -9,8 +9,8 @@
 //   * one process-wide mutex serialises the calls of all contexts (:19, :152);
 //   * the device is opened on the first valid call; Info reports the padded dimensions (:176-180);
 //   * all input is consumed before C is written, so C may overlap A or B.
-// For INT8 Scheme II the finiteness and range checks are made from the device-measured row and column
-// maxima once A and B are uploaded, before the plan is made and C is written.
+// For Scheme II the finiteness and range checks are made from the device-measured row and column maxima
+// once A and B are uploaded, before the plan is made and C is written.
 // Under an evaluation Scope (include/evaluation_hooks.hpp, the reference's src/evaluation_hooks.hpp) a
 // call runs its device pipeline through the evaluator's phase timing and whole-pass check, with the
 // Ozaki II width the Scope fixes (src/ozaki2.cpp:447).
@@ -132,14 +132,12 @@ struct Checked {
     std::uint32_t mp, np, kp;
     std::size_t c_size;
 };
-// The Scheme II INT8 path makes the value checks from the row and column maxima that the device
-// measures for the precision policy (the same magnitude patterns, so the same reports in the same
-// order), before the plan and before C is written; should the device fail before that, the host
-// checks run after all, so that an invalid input is still the error reported. The other paths run
-// the host checks here, before the device is touched.
-bool checks_during_upload(const Options& o) {
-    return o.scheme == Scheme::II && o.format == Format::INT8 && ev::active == nullptr;
-}
+// An ordinary Scheme II call (any format) makes the value checks from the row and column maxima that
+// the device measures for the precision policy (the same magnitude patterns, so the same reports in the
+// same order), before the plan and before C is written; should the device fail before that, the host
+// checks run after all, so that an invalid input is still the error reported. Scheme I and profiled
+// calls run the host checks here, before the device is touched.
+bool checks_during_upload(const Options& o) { return o.scheme == Scheme::II && ev::active == nullptr; }
 
 Checked validate(const Options& options, std::span<const double> a, std::span<const double> b,
                  std::optional<std::size_t> c_size, std::size_t m, std::size_t n, std::size_t k) {
@@ -214,22 +212,30 @@ Context::~Context() = default;
 Info Context::Impl::execute(std::span<const double> a, std::span<const double> b, std::span<double> c, std::size_t m,
                             std::size_t n, std::size_t k, const Options& opt, const Checked& v) {
     std::lock_guard lock(runtime_mutex);
+    // The value checks of an ordinary Scheme II call are made from the maxima the device measures while
+    // A and B are uploaded; should the device fail first, the host checks run after all.
+    bool checked = false;
+    const auto check_maxima = [&](const std::uint64_t* row_max, const std::uint64_t* col_max) {
+        checked = true;
+        report_maxima(row_max, m, col_max, n);
+    };
+    const auto fail = [&](int rc, const std::string& msg) {
+        if (!checked && checks_during_upload(opt)) check_values(a, b, m, n, k);
+        rethrow(rc, msg);
+    };
     if (opt.format != Format::INT8 && opt.scheme == Scheme::II) {  // the digit formats
         oztt_digit_plan plan;
         std::string msg;
-        const int rc = oztt::run_ii_digit_planned(options.device_id, (int32_t)opt.format, a.data(), b.data(), c.data(),
-                                                  m, n, k, opt.max_moduli, recon_code(opt.reconstruction),
-                                                  evaluation_fixed_bits(), plan, msg);
-        if (rc != OZTT_OK) rethrow(rc, msg);
+        const int rc =
+            ev::active ? oztt::run_ii_digit_planned(options.device_id, (int32_t)opt.format, a.data(), b.data(),
+                                                    c.data(), m, n, k, opt.max_moduli, recon_code(opt.reconstruction),
+                                                    evaluation_fixed_bits(), plan, msg)
+                       : oztt::run_ii_digit_streamed(options.device_id, (int32_t)opt.format, a.data(), b.data(),
+                                                     c.data(), m, n, k, opt.max_moduli, recon_code(opt.reconstruction),
+                                                     check_maxima, plan, msg);
+        if (rc != OZTT_OK) fail(rc, msg);
         opened = true;
-        Info info{Scheme::II, opt.format};
-        info.moduli = (std::uint32_t)plan.base.S;
-        info.integer_bits = (std::uint32_t)plan.base.b;
-        info.reconstruction_passes = plan.base.two_pass ? 2u : 1u;
-        info.padded_m = v.mp;
-        info.padded_n = v.np;
-        info.padded_k = v.kp;
-        return info;
+        return ii_info(plan.base, opt, v);
     }
     if (opt.scheme == Scheme::I) {
         oztt_i_plan plan;
@@ -263,19 +269,11 @@ Info Context::Impl::execute(std::span<const double> a, std::span<const double> b
     // A and B go to the device in chunks; the precision policy measures them there (bit-identical to the
     // host measurement), the values are checked from the measured maxima and the host makes the
     // decisions; C is written only after that.
-    bool checked = false;
-    const auto check_maxima = [&](const std::uint64_t* row_max, const std::uint64_t* col_max) {
-        checked = true;
-        report_maxima(row_max, m, col_max, n);
-    };
     oztt_ii_plan plan;
     std::string msg;
     const int rc = oztt::run_ii_int8_streamed(options.device_id, a.data(), b.data(), c.data(), m, n, k, opt.max_moduli,
                                               recon_code(opt.reconstruction), check_maxima, plan, msg);
-    if (rc != OZTT_OK) {
-        if (!checked) check_values(a, b, m, n, k);
-        rethrow(rc, msg);
-    }
+    if (rc != OZTT_OK) fail(rc, msg);
     opened = true;
     return ii_info(plan, opt, v);
 }

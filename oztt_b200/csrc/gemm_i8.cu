@@ -884,11 +884,15 @@ void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t 
 // digits, exact s32 sums). mode 0: P_u as int32 [nout][mp][np]; mode 1: the composition fused into the
 // epilogue, the CRT digits k_s = (sum_u c_u P_u) y_s mod m_s as uint16 [S][mp][np] (compose.cpp and the
 // term_k of recon_crt_proc.h, as one exact integer computation).
+// a_plane_rows: when nonzero, ap points at row r0 of A digit planes that are a_plane_rows tall, and the
+// GEMM covers the band of mp rows from there (outputs [S or nout][mp][np] of the band).
 void launch_digit_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
-                       const oztt_digit_plan& fp, int mode, void* out, int* err_word, cudaStream_t st) {
+                       const oztt_digit_plan& fp, int mode, void* out, int* err_word, cudaStream_t st,
+                       uint64_t a_plane_rows) {
     using namespace gemm;
     if (mp % BM || np % BN || kp % BK || mp == 0 || np == 0 || kp == 0)
         throw Error(OZTT_EINVAL, "digit_gemm: mp, np, kp must be positive multiples of 128, 256 and 128");
+    if (a_plane_rows && a_plane_rows < mp) throw Error(OZTT_EINVAL, "digit_gemm: band taller than its planes");
     const int S = fp.base.S;
     if (S < 1 || S > OZTT_MAXS) throw Error(OZTT_EINVAL, "digit_gemm: bad number of moduli");
     if (fp.nout < 1 || fp.nout > OZTT_MAXOUT || fp.nplane < 1 || fp.nplane > 255 || fp.oout[0] != 0 ||
@@ -926,7 +930,7 @@ void launch_digit_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t
     if ((uint64_t)kp * (uint64_t)max_g * 1024ull >= (1ull << 31))
         throw Error(OZTT_EINVAL, "digit_gemm: K too large for exact 32-bit digit sums");
     if (mp / BM * (np / BN) * (uint64_t)S >= (1ull << 31)) throw Error(OZTT_EINVAL, "digit_gemm: problem too large");
-    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)fp.nplane, BM);
+    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)fp.nplane, BM, a_plane_rows);
     const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)fp.nplane, BN);
     if (mode == 0)
         launch_gemm<4>(ta, tb, out, mp, np, kp, (uint32_t)S, ec, err_word, st);

@@ -23,7 +23,9 @@
 // sequence gives the same class, it only picks a representative), and the reconstruction is the exact
 // CRT of this library (recon.cu).
 #include <algorithm>
+#include <functional>
 #include <string>
+#include <vector>
 
 #include "oztt_common.cuh"
 #include "planner.hpp"
@@ -40,7 +42,8 @@ void launch_digit_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t l
 void launch_digit_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
                              const oztt_digit_plan& fp, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st);
 void launch_digit_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
-                       const oztt_digit_plan& fp, int mode, void* out, int* err_word, cudaStream_t st);
+                       const oztt_digit_plan& fp, int mode, void* out, int* err_word, cudaStream_t st,
+                       uint64_t a_plane_rows = 0);
 void launch_recon_u16(const uint16_t* kp, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB,
                       const oztt_ii_plan& p, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st);
 PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
@@ -159,6 +162,77 @@ int run_ii_digit_planned(int device_id, int32_t format, const double* a, const d
             OZTT_CUDA(cudaMemcpyAsync(c, dc.p, m * n * 8, cudaMemcpyDeviceToHost, st));
             OZTT_CUDA(cudaStreamSynchronize(st));
         });
+    });
+    if (rc != OZTT_OK) err = buf;
+    return rc != OZTT_OK ? rc : inner;
+}
+
+// Context::gemm's path for a digit format (StreamedCall, streamed.cu): the upload with the statistics
+// measured on the way, the caller's value checks from the measured maxima, the format's plan, scale and
+// digit split, then the digit GEMM (the composition in its epilogue) and the reconstruction in bands of
+// about 2048 rows (up to 8), each band of C read back while the next is computed.
+static int run_ii_digit_streamed_impl(int device_id, int32_t format, const double* a, const double* b, double* c,
+                                      uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
+                                      int32_t reconstruction,
+                                      const std::function<void(const uint64_t*, const uint64_t*)>& check,
+                                      oztt_digit_plan& fp, std::string& err) {
+    StreamedCall call(device_id, a, b, m, n, k);
+    StreamedPhases& ph = call.phases();
+    cudaStream_t st = call.work();
+    std::vector<uint64_t> row_max, col_max;
+    const PolicyStats ps = call.upload(row_max, col_max);
+    double t = call.ms_since_start();
+    check(row_max.data(), col_max.data());
+    ph.check_ms = call.ms_since_start() - t;
+    t = call.ms_since_start();
+    const int rc = plan_digit_with(format, [&](uint32_t, uint32_t) { return ps; }, m, n, k, max_moduli,
+                                   reconstruction, 0, fp, err);
+    if (rc != OZTT_OK) return rc;
+    ph.plan_ms = call.ms_since_start() - t;
+    t = call.ms_since_start();
+    check_digit_plan(fp);
+    const oztt_ii_plan& p = fp.base;
+    const uint64_t S = (uint64_t)p.S, NP = (uint64_t)fp.nplane;
+    const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
+    const uint64_t bands = std::min<uint64_t>(8, std::max<uint64_t>(1, mp / 2048));
+    const uint64_t bm = round_up((mp + bands - 1) / bands, 128);
+    const double *da = call.a_dev(), *db = call.b_dev();
+    double* dc = call.c_dev();
+    DevBuf dA(st, mp * 4), dB(st, np * 4), colmax(st, n * 8), words(st, 16);
+    DevBuf pa(st, NP * mp * kp), pb(st, NP * np * kp), kd(st, S * bm * np * 2);
+    OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
+    uint32_t* flags = words.as<uint32_t>();
+    int* gemm_err = words.as<int>() + 1;
+    launch_scale_rows(da, m, k, k, p.shift, dA.as<int32_t>(), nullptr, flags, st);
+    launch_scale_cols(db, k, n, n, p.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
+    launch_digit_split_rows(da, m, k, k, dA.as<int32_t>(), fp, pa.as<int8_t>(), mp, kp, st);
+    launch_digit_split_cols(db, k, n, n, dB.as<int32_t>(), fp, pb.as<int8_t>(), np, kp, st);
+    for (uint64_t r0 = 0; r0 < mp; r0 += bm) {
+        const uint64_t rows_p = std::min(bm, mp - r0);
+        launch_digit_gemm(pa.as<int8_t>() + r0 * kp, pb.as<int8_t>(), rows_p, np, kp, fp, 1, kd.p, gemm_err, st, mp);
+        if (r0 >= m) continue;
+        const uint64_t rows = std::min(m, r0 + rows_p) - r0;
+        launch_recon_u16(kd.as<uint16_t>(), rows_p, np, dA.as<int32_t>() + r0, dB.as<int32_t>(), p, dc + r0 * n, rows,
+                         n, n, st);
+        call.band_done(r0, rows);
+    }
+    call.read_back(c);
+    uint32_t host_words[2] = {0, 0};
+    OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
+    call.finish(t);
+    check_flags(host_words[0], (int)host_words[1]);
+    return OZTT_OK;
+}
+
+int run_ii_digit_streamed(int device_id, int32_t format, const double* a, const double* b, double* c, uint64_t m,
+                          uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction,
+                          const std::function<void(const uint64_t*, const uint64_t*)>& check, oztt_digit_plan& p,
+                          std::string& err) {
+    char buf[1024];
+    int inner = OZTT_OK;
+    const int rc = guarded(buf, sizeof buf, [&] {
+        inner = run_ii_digit_streamed_impl(device_id, format, a, b, c, m, n, k, max_moduli, reconstruction, check, p,
+                                           err);
     });
     if (rc != OZTT_OK) err = buf;
     return rc != OZTT_OK ? rc : inner;

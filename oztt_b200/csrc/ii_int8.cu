@@ -202,171 +202,61 @@ int run_ii_int8_uploaded(int device_id, const double* a, const double* b, double
 
 // ---- the call from host buffers, transfers overlapped ----------------------------------------------
 //
-// Context::gemm's path for INT8 Scheme II. B goes up in chunks of rows and then A in blocks of columns
-// on a copy stream; the work stream measures the precision-policy statistics of each piece as it lands
-// (B's column maxima and sums and its sketch rows, then B's scale while A is in flight, then A's row
-// maxima, sums and sketch advanced block by block), so that the plan can be made as soon as the upload
-// ends. The caller checks the input values from the measured row and column
-// maxima before the plan is made and before C is written. The pipeline then runs the
-// residue GEMM and the reconstruction in bands of rows, and each band of C goes down on a second copy
-// stream while the next band is computed. The range flags and the GEMM's wait-timeout word are read
+// Context::gemm's path for INT8 Scheme II (StreamedCall, streamed.cu): the upload with the statistics
+// measured on the way, the caller's value checks from the measured maxima, the plan, then scale and
+// split, and the residue GEMM and the reconstruction in bands of about 2048 rows (up to 8), each band of
+// C read back while the next is computed. The range flags and the GEMM's wait-timeout word are read
 // after C, as the reference reads its flags after C (src/ozaki2.cpp:469-472).
-
 namespace {
-
-StreamedPhases g_last_phases;
-std::mutex g_phases_mu;
-
-struct Streams {
-    cudaStream_t work = nullptr, up = nullptr, down = nullptr;
-    std::vector<cudaEvent_t> events;
-    Streams() {
-        OZTT_CUDA(cudaStreamCreateWithFlags(&work, cudaStreamNonBlocking));
-        OZTT_CUDA(cudaStreamCreateWithFlags(&up, cudaStreamNonBlocking));
-        OZTT_CUDA(cudaStreamCreateWithFlags(&down, cudaStreamNonBlocking));
-    }
-    ~Streams() {
-        for (cudaStream_t s : {up, down, work})
-            if (s) cudaStreamSynchronize(s);
-        for (cudaEvent_t e : events) cudaEventDestroy(e);
-        for (cudaStream_t s : {up, down, work})
-            if (s) cudaStreamDestroy(s);
-    }
-    // An event marking everything issued on `s` so far.
-    cudaEvent_t mark(cudaStream_t s) {
-        cudaEvent_t e;
-        OZTT_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-        events.push_back(e);
-        OZTT_CUDA(cudaEventRecord(e, s));
-        return e;
-    }
-    // `to` waits for everything issued on `from` so far.
-    cudaEvent_t order(cudaStream_t from, cudaStream_t to) {
-        cudaEvent_t e = mark(from);
-        OZTT_CUDA(cudaStreamWaitEvent(to, e, 0));
-        return e;
-    }
-    Streams(const Streams&) = delete;
-    Streams& operator=(const Streams&) = delete;
-};
-
-// Waits for all three streams when it leaves scope, so that no copy still in flight outlives the
-// stream-ordered buffers declared before it (they are freed on the work stream after this runs).
-struct DrainGuard {
-    Streams& s;
-    ~DrainGuard() {
-        for (cudaStream_t x : {s.up, s.down, s.work}) cudaStreamSynchronize(x);
-    }
-};
-
-constexpr uint64_t kUploadChunkBytes = 64ull << 20;
 
 int run_ii_int8_streamed_impl(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
                               uint64_t k, uint32_t max_moduli, int32_t reconstruction,
                               const std::function<void(const uint64_t*, const uint64_t*)>& check,
                               oztt_ii_plan& p, std::string& err) {
-    using clock = std::chrono::steady_clock;
-    const auto t0 = clock::now();
-    auto ms_since = [](clock::time_point t) { return std::chrono::duration<double, std::milli>(clock::now() - t).count(); };
-    StreamedPhases ph;
-    open_device(device_id);
-    Streams ss;
-    cudaStream_t st = ss.work;
-    const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
-    const uint32_t N = (uint32_t)round_up(n, 64);  // the planner's padded width (plan_ii_int8_with)
-    DevBuf da(st, m * k * 8), db(st, k * n * 8);
-    PolicyStatsRun stats(m, n, k, N, st, 8);
-    DevBuf dA(st), dB(st), colmax(st), words(st), ra(st), rb(st), kpl(st), dc(st);
-    DrainGuard drain{ss};
-    ss.order(st, ss.up);  // the allocations before the first copy
-    // B, then A, in chunks of rows; the statistics of each chunk follow it on the work stream
-    const uint64_t rows_b = std::max<uint64_t>(1, kUploadChunkBytes / (8 * n));
-    for (uint64_t r0 = 0; r0 < k; r0 += rows_b) {
-        const uint64_t rows = std::min(rows_b, k - r0);
-        OZTT_CUDA(cudaMemcpyAsync(db.as<double>() + r0 * n, b + r0 * n, rows * n * 8, cudaMemcpyHostToDevice, ss.up));
-        ss.order(ss.up, st);
-        stats.b_rows(db.as<double>() + r0 * n, r0, rows);
-    }
-    stats.b_done(db.as<double>());
-    // A in blocks of columns (2-D copies of all rows), so that the rows' sequential sums advance block by
-    // block; blocks of at least 512 columns keep the copies at full speed
-    const uint64_t cols_a = std::min<uint64_t>(k, std::max<uint64_t>(512, kUploadChunkBytes / (8 * m)));
-    cudaEvent_t uploaded = nullptr;
-    for (uint64_t c0 = 0; c0 < k; c0 += cols_a) {
-        const uint64_t w = std::min(cols_a, k - c0);
-        OZTT_CUDA(cudaMemcpy2DAsync(da.as<double>() + c0, k * 8, a + c0, k * 8, w * 8, m, cudaMemcpyHostToDevice,
-                                    ss.up));
-        uploaded = ss.order(ss.up, st);
-        stats.a_cols(da.as<double>(), c0, c0 + w);
-    }
-    stats.a_done(da.as<double>());
-    OZTT_CUDA(cudaEventSynchronize(uploaded));
-    ph.upload_ms = ms_since(t0);
+    StreamedCall call(device_id, a, b, m, n, k);
+    StreamedPhases& ph = call.phases();
+    cudaStream_t st = call.work();
     std::vector<uint64_t> row_max, col_max;
-    const PolicyStats ps = stats.collect(&row_max, &col_max);
-    ph.stats_ms = ms_since(t0) - ph.upload_ms;
+    const PolicyStats ps = call.upload(row_max, col_max);
     // every input value checked before the plan and before C is written
-    const auto t1 = clock::now();
+    double t = call.ms_since_start();
     check(row_max.data(), col_max.data());
-    ph.check_ms = ms_since(t1);
-    const auto t2 = clock::now();
+    ph.check_ms = call.ms_since_start() - t;
+    t = call.ms_since_start();
     const int rc = plan_ii_int8_with([&](uint32_t, uint32_t) { return ps; }, m, n, k, max_moduli, reconstruction, 0, p,
                                      err);
     if (rc != OZTT_OK) return rc;
-    ph.plan_ms = ms_since(t2);
-    const auto t3 = clock::now();
+    ph.plan_ms = call.ms_since_start() - t;
+    t = call.ms_since_start();
     check_plan(p);
     const uint64_t S = (uint64_t)p.S;
+    const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
     const uint64_t bands = std::min<uint64_t>(8, std::max<uint64_t>(1, mp / 2048));
     const uint64_t bm = round_up((mp + bands - 1) / bands, 128);
-    dA.alloc(mp * 4);
-    dB.alloc(np * 4);
-    colmax.alloc(n * 8);
-    words.alloc(16);
-    ra.alloc(S * mp * kp);
-    rb.alloc(S * np * kp);
-    kpl.alloc(S * bm * np);
-    dc.alloc(m * n * 8);
+    const double *da = call.a_dev(), *db = call.b_dev();
+    double* dc = call.c_dev();
+    DevBuf dA(st, mp * 4), dB(st, np * 4), colmax(st, n * 8), words(st, 16);
+    DevBuf ra(st, S * mp * kp), rb(st, S * np * kp), kpl(st, S * bm * np);
     OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
-    launch_scale_rows(da.as<double>(), m, k, k, p.shift, dA.as<int32_t>(), nullptr, flags, st);
-    launch_scale_cols(db.as<double>(), k, n, n, p.shift, dB.as<int32_t>(), nullptr, flags,
-                      colmax.as<unsigned long long>(), st);
-    launch_split_rows(da.as<double>(), m, k, k, dA.as<int32_t>(), p, ra.as<int8_t>(), mp, kp, st);
-    launch_split_cols(db.as<double>(), k, n, n, dB.as<int32_t>(), p, rb.as<int8_t>(), np, kp, st);
-    // all bands are queued before the first read-back is issued: a read-back into pageable memory
-    // returns only when it is done, and the GPU keeps computing meanwhile
-    struct Band {
-        uint64_t r0, rows;
-        cudaEvent_t done;
-    };
-    std::vector<Band> done_bands;
+    launch_scale_rows(da, m, k, k, p.shift, dA.as<int32_t>(), nullptr, flags, st);
+    launch_scale_cols(db, k, n, n, p.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
+    launch_split_rows(da, m, k, k, dA.as<int32_t>(), p, ra.as<int8_t>(), mp, kp, st);
+    launch_split_cols(db, k, n, n, dB.as<int32_t>(), p, rb.as<int8_t>(), np, kp, st);
     for (uint64_t r0 = 0; r0 < mp; r0 += bm) {
         const uint64_t rows_p = std::min(bm, mp - r0);
         launch_residue_gemm(ra.as<int8_t>() + r0 * kp, rb.as<int8_t>(), rows_p, np, kp, p, 1, kpl.p, gemm_err, st, mp);
         if (r0 >= m) continue;
         const uint64_t rows = std::min(m, r0 + rows_p) - r0;
-        launch_recon(kpl.as<uint8_t>(), rows_p, np, dA.as<int32_t>() + r0, dB.as<int32_t>(), p, dc.as<double>() + r0 * n,
-                     rows, n, n, st);
-        done_bands.push_back({r0, rows, ss.mark(st)});
+        launch_recon(kpl.as<uint8_t>(), rows_p, np, dA.as<int32_t>() + r0, dB.as<int32_t>(), p, dc + r0 * n, rows, n,
+                     n, st);
+        call.band_done(r0, rows);
     }
-    for (const Band& band : done_bands) {
-        OZTT_CUDA(cudaStreamWaitEvent(ss.down, band.done, 0));
-        OZTT_CUDA(cudaMemcpyAsync(c + band.r0 * n, dc.as<double>() + band.r0 * n, band.rows * n * 8,
-                                  cudaMemcpyDeviceToHost, ss.down));
-    }
+    call.read_back(c);
     uint32_t host_words[2] = {0, 0};
     OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
-    ss.order(ss.down, st);
-    OZTT_CUDA(cudaStreamSynchronize(st));
-    ph.pipeline_ms = ms_since(t3);
-    ph.total_ms = ms_since(t0);
-    ph.bands = (int)((mp + bm - 1) / bm);
-    {
-        std::lock_guard<std::mutex> lock(g_phases_mu);
-        g_last_phases = ph;
-    }
+    call.finish(t);
     check_flags(host_words[0], (int)host_words[1]);
     return OZTT_OK;
 }
@@ -384,11 +274,6 @@ int run_ii_int8_streamed(int device_id, const double* a, const double* b, double
     });
     if (rc != OZTT_OK) err = buf;
     return rc != OZTT_OK ? rc : inner;
-}
-
-StreamedPhases last_streamed_phases() {
-    std::lock_guard<std::mutex> lock(g_phases_mu);
-    return g_last_phases;
 }
 
 void open_device_checked(int device_id) { open_device(device_id); }

@@ -127,12 +127,17 @@ int run_ii_int8_streamed(int device_id, const double* a, const double* b, double
                          uint64_t k, uint32_t max_moduli, int32_t reconstruction,
                          const std::function<void(const uint64_t*, const uint64_t*)>& check, oztt_ii_plan& p,
                          std::string& err);
+// The same for a digit format (ii_digit.cu).
+int run_ii_digit_streamed(int device_id, int32_t format, const double* a, const double* b, double* c, uint64_t m,
+                          uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction,
+                          const std::function<void(const uint64_t*, const uint64_t*)>& check, oztt_digit_plan& p,
+                          std::string& err);
 // Scheme II INT8 from host buffers without overlap (whole upload, device statistics, pipeline, C back),
 // the width fixed to fixed_bits when nonzero: the path of the evaluator's profiled calls.
 int run_ii_int8_uploaded(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
                          uint64_t k, uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan& p,
                          std::string& err);
-// Host wall-clock phases of the last completed call of run_ii_int8_streamed in this process.
+// Host wall-clock phases of the last completed streamed call (INT8 or a digit format) in this process.
 struct StreamedPhases {
     double upload_ms = 0;      // from the call to the end of the last host-to-device copy
     double stats_ms = 0;       // then until the statistics were read back

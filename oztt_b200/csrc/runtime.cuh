@@ -3,6 +3,7 @@
 // the read-back checks of the range flags and the GEMM wait-timeout word.
 #pragma once
 #include <algorithm>
+#include <chrono>
 #include <functional>
 #include <memory>
 #include <string>
@@ -10,6 +11,7 @@
 #include <vector>
 
 #include "oztt_common.cuh"
+#include "planner.hpp"
 
 namespace oztt {
 
@@ -120,6 +122,51 @@ private:
     size_t next_ = 0;
     std::unique_ptr<Bufs> bufs_;
     std::shared_ptr<const std::vector<double>> g_;
+};
+
+// Context::gemm from host buffers with the transfers overlapped (streamed.cu): A and B uploaded in
+// pieces while the device measures the precision-policy statistics, then the caller's pipeline on the
+// work stream, marking each finished band of rows of C, which goes back on a copy stream while the next
+// band is computed. Every stream is drained before the buffers are released.
+class StreamedCall {
+public:
+    StreamedCall(int device_id, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k);
+    ~StreamedCall();
+    // B in chunks of rows, then A in blocks of columns, with the statistics measured as they land;
+    // returns them, with the magnitude patterns of A's row maxima and B's column maxima.
+    PolicyStats upload(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max);
+    const double* a_dev() const { return da_->as<double>(); }
+    const double* b_dev() const { return db_->as<double>(); }
+    double* c_dev();
+    cudaStream_t work() const { return work_; }
+    // rows [r0, r0 + rows) of the device C are complete once the work issued so far has run
+    void band_done(uint64_t r0, uint64_t rows);
+    // issues the read-back of every completed band into c, in order
+    void read_back(double* c);
+    // waits for everything (the read-back included) and records the phases of the call, the pipeline
+    // counted from pipeline_start_ms (ms_since_start when it was issued)
+    void finish(double pipeline_start_ms);
+    StreamedPhases& phases() { return phases_; }
+    double ms_since_start() const;
+    StreamedCall(const StreamedCall&) = delete;
+    StreamedCall& operator=(const StreamedCall&) = delete;
+
+private:
+    cudaEvent_t mark(cudaStream_t s);
+    cudaEvent_t order(cudaStream_t from, cudaStream_t to);
+    struct Band {
+        uint64_t r0, rows;
+        cudaEvent_t done;
+    };
+    const double *a_, *b_;
+    uint64_t m_, n_, k_;
+    std::chrono::steady_clock::time_point t0_;
+    cudaStream_t work_ = nullptr, up_ = nullptr, down_ = nullptr;
+    std::vector<cudaEvent_t> events_;
+    std::vector<Band> bands_;
+    std::unique_ptr<DevBuf> da_, db_, dc_;
+    std::unique_ptr<PolicyStatsRun> stats_;
+    StreamedPhases phases_;
 };
 
 }  // namespace oztt

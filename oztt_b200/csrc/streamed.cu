@@ -1,0 +1,135 @@
+// SPDX-License-Identifier: Apache-2.0
+//
+// Context::gemm from host buffers with the transfers overlapped (StreamedCall, runtime.cuh), shared by
+// the INT8 and digit-format Scheme II paths.
+//
+//   copy-up stream   B in 64 MiB chunks of rows, then A in blocks of columns (2-D copies of all rows)
+//   work stream      the precision-policy statistics of each piece as it lands (PolicyStatsRun), then
+//                    the caller's pipeline, which marks each finished band of rows of C
+//   copy-down stream each finished band of C read back while the next is computed
+//
+// The statistics left after the upload are those of the last block of A, so the plan can be made as
+// soon as the upload ends; the values are checked from the measured maxima before that.
+#include <chrono>
+#include <mutex>
+
+#include "oztt_common.cuh"
+#include "planner.hpp"
+#include "runtime.cuh"
+
+namespace oztt {
+
+namespace {
+StreamedPhases g_last_phases;
+std::mutex g_phases_mu;
+constexpr uint64_t kUploadChunkBytes = 64ull << 20;
+}  // namespace
+
+StreamedPhases last_streamed_phases() {
+    std::lock_guard<std::mutex> lock(g_phases_mu);
+    return g_last_phases;
+}
+
+StreamedCall::StreamedCall(int device_id, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k)
+    : a_(a), b_(b), m_(m), n_(n), k_(k), t0_(std::chrono::steady_clock::now()) {
+    open_device(device_id);
+    for (cudaStream_t* s : {&work_, &up_, &down_}) OZTT_CUDA(cudaStreamCreateWithFlags(s, cudaStreamNonBlocking));
+    da_ = std::make_unique<DevBuf>(work_, m * k * 8);
+    db_ = std::make_unique<DevBuf>(work_, k * n * 8);
+}
+
+StreamedCall::~StreamedCall() {
+    for (cudaStream_t s : {up_, down_, work_})
+        if (s) cudaStreamSynchronize(s);
+    // the buffers go back to the pool on the work stream, after everything that used them
+    stats_.reset();
+    dc_.reset();
+    da_.reset();
+    db_.reset();
+    for (cudaEvent_t e : events_) cudaEventDestroy(e);
+    for (cudaStream_t s : {up_, down_, work_})
+        if (s) {
+            cudaStreamSynchronize(s);
+            cudaStreamDestroy(s);
+        }
+}
+
+double StreamedCall::ms_since_start() const {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0_).count();
+}
+
+cudaEvent_t StreamedCall::mark(cudaStream_t s) {
+    cudaEvent_t e;
+    OZTT_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    events_.push_back(e);
+    OZTT_CUDA(cudaEventRecord(e, s));
+    return e;
+}
+
+cudaEvent_t StreamedCall::order(cudaStream_t from, cudaStream_t to) {
+    cudaEvent_t e = mark(from);
+    OZTT_CUDA(cudaStreamWaitEvent(to, e, 0));
+    return e;
+}
+
+PolicyStats StreamedCall::upload(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max) {
+    const uint64_t m = m_, n = n_, k = k_;
+    const uint32_t N = (uint32_t)round_up(n, 64);  // the planners' padded width
+    stats_ = std::make_unique<PolicyStatsRun>(m, n, k, N, work_, 8);
+    order(work_, up_);  // the allocations before the first copy
+    double* db = db_->as<double>();
+    double* da = da_->as<double>();
+    const uint64_t rows_b = std::max<uint64_t>(1, kUploadChunkBytes / (8 * n));
+    for (uint64_t r0 = 0; r0 < k; r0 += rows_b) {
+        const uint64_t rows = std::min(rows_b, k - r0);
+        OZTT_CUDA(cudaMemcpyAsync(db + r0 * n, b_ + r0 * n, rows * n * 8, cudaMemcpyHostToDevice, up_));
+        order(up_, work_);
+        stats_->b_rows(db + r0 * n, r0, rows);
+    }
+    stats_->b_done(db);
+    // blocks of at least 512 columns keep the 2-D copies at full speed
+    const uint64_t cols_a = std::min<uint64_t>(k, std::max<uint64_t>(512, kUploadChunkBytes / (8 * m)));
+    cudaEvent_t uploaded = nullptr;
+    for (uint64_t c0 = 0; c0 < k; c0 += cols_a) {
+        const uint64_t w = std::min(cols_a, k - c0);
+        OZTT_CUDA(cudaMemcpy2DAsync(da + c0, k * 8, a_ + c0, k * 8, w * 8, m, cudaMemcpyHostToDevice, up_));
+        uploaded = order(up_, work_);
+        stats_->a_cols(da, c0, c0 + w);
+    }
+    stats_->a_done(da);
+    OZTT_CUDA(cudaEventSynchronize(uploaded));
+    phases_.upload_ms = ms_since_start();
+    const PolicyStats ps = stats_->collect(&row_max, &col_max);
+    phases_.stats_ms = ms_since_start() - phases_.upload_ms;
+    return ps;
+}
+
+double* StreamedCall::c_dev() {
+    if (!dc_) dc_ = std::make_unique<DevBuf>(work_, m_ * n_ * 8);
+    return dc_->as<double>();
+}
+
+void StreamedCall::band_done(uint64_t r0, uint64_t rows) { bands_.push_back({r0, rows, mark(work_)}); }
+
+void StreamedCall::read_back(double* c) {
+    // all bands are queued before the first read-back is issued: a read-back into pageable memory
+    // returns only when it is done, and the GPU keeps computing meanwhile
+    const double* dc = c_dev();
+    for (const Band& band : bands_) {
+        OZTT_CUDA(cudaStreamWaitEvent(down_, band.done, 0));
+        OZTT_CUDA(cudaMemcpyAsync(c + band.r0 * n_, dc + band.r0 * n_, band.rows * n_ * 8, cudaMemcpyDeviceToHost,
+                                  down_));
+    }
+    order(down_, work_);
+}
+
+void StreamedCall::finish(double pipeline_start_ms) {
+    OZTT_CUDA(cudaStreamSynchronize(work_));
+    phases_.total_ms = ms_since_start();
+    phases_.pipeline_ms = phases_.total_ms - pipeline_start_ms;
+    phases_.bands = (int)bands_.size();
+    std::lock_guard<std::mutex> lock(g_phases_mu);
+    g_last_phases = phases_;
+}
+
+}  // namespace oztt

@@ -273,6 +273,42 @@ def test_context_matches_planned_run(oztt, oracle, cuda, fmt):
     assert np.array_equal(C.cpu().numpy().view(np.uint64), c.view(np.uint64))
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_context_streamed_bands(oztt, oracle, cuda, fmt):
+    """Context::gemm's streamed path with a digit format: B in two chunks of rows, A in three blocks of
+    columns (the last one ragged), two row bands (the last one ragged), tiny elements in both operands (the
+    statistics' scale-first recomputation); the bits of the stage pipeline run with the host plan."""
+    m, n, k = 4500, 2048, 4608
+    a, b = oracle.gen_inputs(m, n, k, 1.0, 23)
+    a[11], b[k * n - 3] = 2.0 ** -500, -(2.0 ** -420)
+    fp = oztt.digit_plan(a, b, m, n, k, fmt=fmt)
+    c = np.full(m * n, 123.0)
+    info = oztt.Context().gemm(a, b, c, m, n, k, oztt.Options(format=fmt))
+    assert info.moduli == fp.base.S and info.integer_bits == fp.base.b
+    c2 = oztt.digit_run(a, b, m, n, k, fp)
+    assert np.array_equal(c.view(np.uint64), c2.view(np.uint64))
+    assert oztt.ii_int8_last_phases()["bands"] == 2
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_context_streamed_check_errors(oztt, cuda, fmt):
+    """A value error is reported from the measured maxima in the reference's order, before any plan
+    error, with C untouched."""
+    ctx = oztt.Context()
+    m = n = k = 200
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal(m * k)
+    b = rng.standard_normal(k * n)
+    c = np.full(m * n, 123.0)
+    b[7] = np.inf
+    with pytest.raises(ValueError, match="B contains NaN or infinity"):
+        ctx.gemm(a, b, c, m, n, k, oztt.Options(format=fmt, max_moduli=2))
+    b[7] = 1.0
+    with pytest.raises(ValueError, match="must be in"):  # a row of A whose maximum is below 2^-126
+        ctx.gemm(np.full(k, 2.0 ** -140), b, c[:n], 1, n, k, oztt.Options(format=fmt))
+    assert np.all(c == 123.0)
+
+
 def test_rejections(oztt, cuda):
     ctx = oztt.Context()
     a = np.ones(64 * 64)
