@@ -227,6 +227,19 @@ int oztt_i_int8_plan(const double* a, const double* b, uint64_t m, uint64_t n, u
  * ozaki1/plan.hpp:141-226). */
 int oztt_i_format_plan(int32_t format, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
                        uint32_t slices, oztt_i_plan* plan, char* err, size_t errlen);
+/* Scheme I plan of a built format for operands on the device (row-major a_dev: m x k, b_dev: k x n), the
+ * slice count (slices = 0) selected from statistics measured there (oz_fp64_p,
+ * src/backend/ozaki1/auto_precision.hpp:65-526). Bit-identical to oztt_i_format_plan on the same finite
+ * values. Synchronises `stream`. */
+int oztt_i_format_plan_device(int32_t format, const double* a_dev, const double* b_dev, uint64_t m, uint64_t n,
+                              uint64_t k, uint32_t slices, oztt_i_plan* plan, void* stream, char* err,
+                              size_t errlen);
+/* The Scheme I slice selection's model (1) errors (out[q] for q = 2..count-1) and the estimate of
+ * ||C||_F^2 (out[0]), measured on the host from a, b (a_dev NULL) or on the device from a_dev, b_dev:
+ * for checking the two against each other. */
+int oztt_i_model1_errors(int32_t format, const double* a, const double* b, const double* a_dev, const double* b_dev,
+                         uint64_t m, uint64_t n, uint64_t k, double* out, int32_t count, void* stream, char* err,
+                         size_t errlen);
 /* Scheme II INT8 plan for operands already on the device (a: m x k, b: k x n, row-major): the input
  * statistics of the precision policy are measured by kernels on `stream` (bit-identical to the host
  * measurement of oztt_ii_int8_plan), the decisions made on the host. Synchronises `stream`. */

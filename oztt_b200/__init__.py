@@ -187,6 +187,9 @@ _SIGNATURES = {
     "oztt_i_int8_run": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _ERR, _SZ],
     "oztt_i_int8_run_device": [ctypes.c_int, _P, _P, _P, _U64, _U64, _U64, ctypes.POINTER(IPlan), _P, _P, _ERR, _SZ],
     "oztt_i_format_plan": [_I32, _P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _ERR, _SZ],
+    "oztt_i_format_plan_device": [_I32, _P, _P, _U64, _U64, _U64, ctypes.c_uint32, ctypes.POINTER(IPlan), _P, _ERR,
+                                  _SZ],
+    "oztt_i_model1_errors": [_I32, _P, _P, _P, _P, _U64, _U64, _U64, _P, _I32, _P, _ERR, _SZ],
     "oztt_i_scale_rows": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _ERR, _SZ],
     "oztt_i_scale_cols": [_P, _U64, _U64, _U64, _I32, _P, _P, _P, _ERR, _SZ],
     "oztt_i_slice_rows": [_P, _U64, _U64, _U64, _P, _I32, _I32, _P, _U64, _U64, _P, _ERR, _SZ],
@@ -470,6 +473,35 @@ def i_int8_plan(a, b, m: int, n: int, k: int, slices: int = 0, fmt=None) -> IPla
     if rc != OK:
         _raise(rc, err.value)
     return plan
+
+
+def i_plan_device(a_dev: int, b_dev: int, m: int, n: int, k: int, slices: int = 0, fmt=Format.INT8,
+                  stream: int = 0) -> IPlan:
+    """Scheme I plan for device pointers a_dev (m x k), b_dev (k x n), the slice count selected from
+    statistics measured on the device (oztt_i_format_plan_device)."""
+    plan = IPlan()
+    err = _errbuf()
+    rc = _lib().oztt_i_format_plan_device(int(fmt), a_dev, b_dev, m, n, k, slices, ctypes.byref(plan), stream, err,
+                                          len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return plan
+
+
+def i_model1_errors(a, b, m: int, n: int, k: int, fmt=Format.INT8, a_dev: int = 0, b_dev: int = 0,
+                    stream: int = 0, count: int = 40) -> np.ndarray:
+    """Scheme I slice selection's model (1) errors (entries 2..) and its ||C||_F^2 estimate (entry 0),
+    measured on the host (a_dev 0) or on the device (oztt_i_model1_errors)."""
+    av = _as_f64(a, "a") if a is not None else None
+    bv = _as_f64(b, "b") if b is not None else None
+    out = np.zeros(count)
+    err = _errbuf()
+    rc = _lib().oztt_i_model1_errors(int(fmt), av.ctypes.data if av is not None else None,
+                                     bv.ctypes.data if bv is not None else None, a_dev or None, b_dev or None, m, n, k,
+                                     out.ctypes.data, count, stream, err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return out
 
 
 def i_int8_run(a, b, m: int, n: int, k: int, plan: IPlan, device_id: int = 0) -> np.ndarray:

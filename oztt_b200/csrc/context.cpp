@@ -238,14 +238,17 @@ Info Context::Impl::execute(std::span<const double> a, std::span<const double> b
         return ii_info(plan.base, opt, v);
     }
     if (opt.scheme == Scheme::I) {
+        const oztt::I1Format& fmt = *oztt::i1_format((int32_t)opt.format);
         oztt_i_plan plan;
         std::string msg;
-        int rc = oztt::plan_i(a.data(), b.data(), m, n, k, opt.slices, *oztt::i1_format((int32_t)opt.format), plan,
-                              msg);
+        if (opt.slices) {  // a fixed slice count: the feasibility checks before any device work, as the reference
+            const int rc = oztt::plan_i(a.data(), b.data(), m, n, k, opt.slices, fmt, plan, msg);
+            if (rc != OZTT_OK) rethrow(rc, msg);
+        }
+        // one upload; the slice count (when not fixed) selected from statistics measured on the device
+        const int rc = oztt::run_i_uploaded(options.device_id, a.data(), b.data(), c.data(), m, n, k, opt.slices, fmt,
+                                            plan, msg);
         if (rc != OZTT_OK) rethrow(rc, msg);
-        char err[512] = {0};
-        rc = oztt_i_int8_run(options.device_id, a.data(), b.data(), c.data(), m, n, k, &plan, err, sizeof err);
-        if (rc != OZTT_OK) rethrow(rc, err);
         opened = true;
         Info info{Scheme::I, opt.format};
         info.slices = (std::uint32_t)plan.p;

@@ -107,12 +107,58 @@ inline const I1Format* i1_format(int32_t format) {
     default: return nullptr;
     }
 }
+// Scheme I slice selection in parts, so that the per-element statistics can be measured on the device
+// (plan1_dev.cu) and the rest done here with the same arithmetic:
+//   I1Normalization  the global scales rg, per row of A / column of B the device exponent e, the scaled
+//                    divisor s = rg 2^(e - nshift) (0: not counted) and the squared norm sum (x rg)^2;
+//   I1Terms          model (1)'s per-k sums: S[i][k], R[q][k] (slice and residual contributions of A and
+//                    of B, q = 1..pmax, index i*k + c) and the column norms N[k].
+struct I1Normalization {
+    double rgA = 1.0, rgB = 1.0;
+    std::vector<int> eA, eB;
+    std::vector<double> sA, sB, nrA, nrB;
+};
+struct I1Terms {
+    std::vector<double> SA, RA, SB, RB, NA, NB;
+};
+// The largest slice count the search considers (ceil(160 / log2 radix) + 1).
+int i1_pmax(const I1Format& f);
+// The normalization from the magnitude patterns of the row and column maxima and the squared norms.
+I1Normalization i1_normalization(double rgA, double rgB, const uint64_t* row_max, const uint64_t* col_max,
+                                 const double* nrA, const double* nrB, uint64_t m, uint64_t n, const I1Format& f);
+// Model (2) in parts, for an evaluation of its sums elsewhere (the device): the sampled rows of A and
+// columns of B with their weights (the largest norms, then a seeded uniform draw), ||C||_F^2's
+// denominator from the sample's C (Ch + Cl, the compensated products of the pairs) and nC, the error for
+// one q from the chunk partial sums part[ch][s][u] of the dropped terms (nch chunks of the padded K), and
+// the search over q with model (1)'s terms.
+struct I1SamplePick {
+    std::vector<uint32_t> rows, cols;
+    std::vector<double> wr, wc;
+};
+constexpr uint32_t kI1Chunks = 64;
+I1SamplePick i1_pick(const I1Normalization& nm);
+double i1_sample_norm2(const I1SamplePick& sp, const std::vector<double>& Ch, double nC);
+double i1_model2_finish(const double* part, uint32_t nch, const I1SamplePick& sp, const std::vector<double>& Ch,
+                        const std::vector<double>& Cl, const I1Normalization& nm, double norm2);
+int i1_select_with(const I1Terms& terms, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N, uint32_t K,
+                   const I1Format& f, double nC, const std::function<double(int)>& model2);
+// Model (1)'s error for q = 0..pmax (entries below 2 unused): from the given terms, or measured on the
+// host from a and b (with the given normalization, or the host's own).
+std::vector<double> i1_model1_errors(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                                     const I1Format& f, const I1Terms* terms, const I1Normalization* nm);
 // Scheme I (planner1.cpp): the slice count oz_fp64_p selects for row-major a (m x k), b (k x n) with padded
 // planning dimensions M, N, K; and the whole plan (slices > 0 fixes p).
 int select_slices(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,
                   uint32_t K, const I1Format& f);
 int plan_i(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices, const I1Format& f,
            oztt_i_plan& p, std::string& err);
+// Context::gemm's Scheme I call (plan1_dev.cu): one upload, the slice count from statistics measured on
+// the device, the pipeline on the resident operands.
+int run_i_uploaded(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
+                   uint32_t slices, const I1Format& f, oztt_i_plan& p, std::string& err);
+// The same with the slice count from select(M, N, K) when slices is 0 (e.g. measured on the device).
+int plan_i_with(const std::function<int(uint32_t, uint32_t, uint32_t)>& select, uint64_t m, uint64_t n, uint64_t k,
+                uint32_t slices, const I1Format& f, oztt_i_plan& p, std::string& err);
 int select_slices_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,
                        uint32_t K);
 int plan_i_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,

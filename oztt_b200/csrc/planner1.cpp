@@ -24,6 +24,7 @@
 #include <cstdio>
 #include <cstring>
 #include <exception>
+#include <functional>
 #include <random>
 #include <string>
 #include <vector>
@@ -99,11 +100,17 @@ struct Dims {
     }
 };
 
-struct Normalization {
-    double rgA = 1.0, rgB = 1.0;
-    std::vector<int> eA, eB;
-    std::vector<double> sA, sB, nrA, nrB;  // scaled divisors (0: row/column not counted), squared norms
-};
+using Normalization = I1Normalization;
+
+// The exponent and scaled divisor of a row (column) from its largest magnitude.
+void row_scale(double mx, double rg, const Dims& d, int& e_out, double& s_out) {
+    bool ok = false;
+    const int e = device_exponent(mx, d.f.ceil_mode, ok);
+    if (mx > 0 && ok) {
+        e_out = e;
+        s_out = std::ldexp(rg, e - d.f.nshift);
+    }
+}
 
 Normalization normalize(const double* a, const double* b, const Dims& d) {
     Normalization nm;
@@ -123,12 +130,7 @@ Normalization normalize(const double* a, const double* b, const Dims& d) {
                 mx = std::max(mx, std::fabs(v));
                 nr += (v * nm.rgA) * (v * nm.rgA);
             }
-            bool ok = false;
-            const int e = device_exponent(mx, d.f.ceil_mode, ok);
-            if (mx > 0 && ok) {
-                nm.eA[i] = e;
-                nm.sA[i] = std::ldexp(nm.rgA, e - d.f.nshift);
-            }
+            row_scale(mx, nm.rgA, d, nm.eA[i], nm.sA[i]);
             nm.nrA[i] = nr;
         }
     });
@@ -142,24 +144,27 @@ Normalization normalize(const double* a, const double* b, const Dims& d) {
             }
         }
         for (uint64_t c = c0; c < c1; ++c) {
-            bool ok = false;
-            const int e = device_exponent(mx[c], d.f.ceil_mode, ok);
-            if (mx[c] > 0 && ok) {
-                nm.eB[c] = e;
-                nm.sB[c] = std::ldexp(nm.rgB, e - d.f.nshift);
-            }
+            row_scale(mx[c], nm.rgB, d, nm.eB[c], nm.sB[c]);
         }
     });
     return nm;
 }
 
 // Model (1): err2[q] = expected ||E||_F^2 for q slices with independent signs (q = 2..pmax), scaled
-// units of the normalization.
-std::vector<double> independent_error(const double* a, const double* b, const Dims& d, const Normalization& nm) {
+// units of the normalization. First the per-k terms (independent_terms; the device computes the same
+// arrays, plan1_dev.cu), then their combination (combine_terms).
+I1Terms independent_terms(const double* a, const double* b, const Dims& d, const Normalization& nm) {
     const int pmax = d.pmax;
     const size_t P1 = (size_t)pmax + 1, K = d.k;
     // Per k: slice contributions S[i][k], residual contributions R[q][k], column norms N[k].
-    std::vector<double> SA(P1 * K, 0.0), RA(P1 * K, 0.0), SB(P1 * K, 0.0), RB(P1 * K, 0.0), NA(K, 0.0), NB(K, 0.0);
+    I1Terms terms;
+    terms.SA.assign(P1 * K, 0.0);
+    terms.RA.assign(P1 * K, 0.0);
+    terms.SB.assign(P1 * K, 0.0);
+    terms.RB.assign(P1 * K, 0.0);
+    terms.NA.assign(K, 0.0);
+    terms.NB.assign(K, 0.0);
+    std::vector<double>&SA = terms.SA, &RA = terms.RA, &SB = terms.SB, &RB = terms.RB, &NA = terms.NA, &NB = terms.NB;
     // Expands up to four elements of different k side by side (their chains are independent, so they
     // overlap in the pipeline); each element adds its slice and residual terms to its own column k, in
     // the order of its own steps, and stops once its residual is exactly zero.
@@ -243,6 +248,14 @@ std::vector<double> independent_error(const double* a, const double* b, const Di
             for (int l = 0; l < nl; ++l) NB[c0 + l] = nb[l];
         }
     });
+    return terms;
+}
+
+std::vector<double> combine_terms(const I1Terms& terms, const Dims& d) {
+    const int pmax = d.pmax;
+    const size_t P1 = (size_t)pmax + 1, K = d.k;
+    const std::vector<double>&SA = terms.SA, &RA = terms.RA, &SB = terms.SB, &RB = terms.RB, &NA = terms.NA,
+                             &NB = terms.NB;
     // G[i][j] = sum_k SA_i[k] SB_j[k]: the pairs the device drops.
     std::vector<double> G((size_t)pmax * pmax, 0.0);
     parallel_ranges((uint64_t)pmax * pmax, [&](uint64_t t0, uint64_t t1) {
@@ -264,6 +277,38 @@ std::vector<double> independent_error(const double* a, const double* b, const Di
     return err2;
 }
 
+// Model (2)'s last step for one q: E = the per-pair sums of the dropped terms (chunk partial sums
+// part[ch][s][u], combined in chunk order), and the simulated rounding of C - E against C.
+double model2_finish(const double* part, uint32_t nch, const std::vector<uint32_t>& rows,
+                     const std::vector<uint32_t>& cols, const std::vector<double>& wr, const std::vector<double>& wc,
+                     const std::vector<double>& Ch, const std::vector<double>& Cl, const Normalization& nm,
+                     double norm2) {
+    const size_t na = rows.size(), nb = cols.size();
+    double e2 = 0;
+    for (size_t s = 0; s < na; ++s)
+        for (size_t u = 0; u < nb; ++u) {
+            double E = 0;
+            for (uint32_t ch = 0; ch < nch; ++ch) E += part[((size_t)ch * na + s) * nb + u];
+            // The device's 64-bit assembly window can move a value by about 2^-60 relative before
+            // its rounding: within 2^-59 of a rounding midpoint the side farther from C is taken.
+            const size_t su = s * nb + u;
+            double h, r;
+            two_sum(Ch[su], Cl[su] - nm.sA[rows[s]] * nm.sB[cols[u]] * E, h, r);
+            double out = h;
+            if (h != 0) {
+                const double h2 = std::nextafter(h, r >= 0 ? INFINITY : -INFINITY);
+                const double gap = 0.5 * std::fabs(h2 - h) - std::fabs(r);
+                if (gap <= std::ldexp(1.0, std::ilogb(h) - 59)) {
+                    const double d1 = (h - Ch[su]) - Cl[su], d2 = (h2 - Ch[su]) - Cl[su];
+                    if (std::fabs(d2) > std::fabs(d1)) out = h2;
+                }
+            }
+            const double dv = (out - Ch[su]) - Cl[su];
+            e2 += wr[s] * wc[u] * dv * dv;
+        }
+    return norm2 > 0 ? e2 / norm2 : (e2 > 0 ? INFINITY : 0.0);
+}
+
 // Model (2): the sampled rows and columns with their products in double-double.
 struct Sample {
     const Dims* d = nullptr;
@@ -280,7 +325,7 @@ struct Sample {
         const size_t na = rows.size(), nb = cols.size();
         if (na == 0 || nb == 0) return 0.0;
         const uint64_t K = d->K, kreal = d->k;
-        constexpr uint32_t NCH = 64;
+        constexpr uint32_t NCH = kI1Chunks;
         std::vector<double> part((size_t)NCH * na * nb, 0.0);
         parallel_ranges(NCH, [&](uint64_t c0, uint64_t c1) {
             std::vector<double> D(na * q), RX(na), RY(nb * (q + 1)), Yk(nb);
@@ -318,29 +363,7 @@ struct Sample {
                 }
             }
         });
-        double e2 = 0;
-        for (size_t s = 0; s < na; ++s)
-            for (size_t u = 0; u < nb; ++u) {
-                double E = 0;
-                for (uint32_t ch = 0; ch < NCH; ++ch) E += part[((size_t)ch * na + s) * nb + u];
-                // The device's 64-bit assembly window can move a value by about 2^-60 relative before
-                // its rounding: within 2^-59 of a rounding midpoint the side farther from C is taken.
-                const size_t su = s * nb + u;
-                double h, r;
-                two_sum(Ch[su], Cl[su] - nm->sA[rows[s]] * nm->sB[cols[u]] * E, h, r);
-                double out = h;
-                if (h != 0) {
-                    const double h2 = std::nextafter(h, r >= 0 ? INFINITY : -INFINITY);
-                    const double gap = 0.5 * std::fabs(h2 - h) - std::fabs(r);
-                    if (gap <= std::ldexp(1.0, std::ilogb(h) - 59)) {
-                        const double d1 = (h - Ch[su]) - Cl[su], d2 = (h2 - Ch[su]) - Cl[su];
-                        if (std::fabs(d2) > std::fabs(d1)) out = h2;
-                    }
-                }
-                const double dv = (out - Ch[su]) - Cl[su];
-                e2 += wr[s] * wc[u] * dv * dv;
-            }
-        return norm2 > 0 ? e2 / norm2 : (e2 > 0 ? INFINITY : 0.0);
+        return model2_finish(part.data(), NCH, rows, cols, wr, wc, Ch, Cl, *nm, norm2);
     }
 };
 
@@ -413,10 +436,10 @@ Sample sample(const double* a, const double* b, const Dims& d, const Normalizati
 
 // Starts at the smallest q that model (1) accepts; if model (2) rejects it, doubles the step upward
 // until a q passes both, then bisects. pmax when the target is not reached.
-int search(const std::vector<double>& r1, const Sample& sm, int pmax, double tgt) {
+int search(const std::vector<double>& r1, const std::function<double(int)>& model2, int pmax, double tgt) {
     std::vector<double> cache((size_t)pmax + 1, -1.0);
     auto f = [&](int q) {
-        if (cache[q] < 0) cache[q] = sm.err2(q);
+        if (cache[q] < 0) cache[q] = model2(q);
         return std::max(r1[q], cache[q]);
     };
     int q0 = pmax;
@@ -463,20 +486,95 @@ uint32_t block_k(uint32_t K, int L, const I1Format& f) {
     return best;
 }
 
-}  // namespace
-
-int select_slices(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,
-                  uint32_t K, const I1Format& f) {
-    Dims d{m, n, k, M, N, K, 0, f};
-    d.pmax = (int)std::ceil(160.0 / std::log2(f.radix)) + 1;
-    const Normalization nm = normalize(a, b, d);
-    const std::vector<double> err2 = independent_error(a, b, d, nm);
-    const double nC = product_norm_estimate(a, b, m, n, k, N, nm.rgA, nm.rgB);
-    const Sample sm = sample(a, b, d, nm, nC);
+// The slice count from model (1)'s terms, nC and model (2) (model2(q): its error for q slices).
+int select_with(const I1Terms& terms, const Dims& d, double nC, const std::function<double(int)>& model2) {
+    const std::vector<double> err2 = combine_terms(terms, d);
     const double tgt = std::ldexp(1.0, -106);
     std::vector<double> r1((size_t)d.pmax + 1, INFINITY);
     for (int q = 2; q <= d.pmax; ++q) r1[q] = nC > 0 ? err2[q] / nC : (err2[q] > 0 ? INFINITY : 0.0);
-    return search(r1, sm, d.pmax, tgt);
+    return search(r1, model2, d.pmax, tgt);
+}
+
+// The slice count from the normalization, the per-k terms of model (1) and nC, however measured.
+int select_from(const double* a, const double* b, const Dims& d, const Normalization& nm, const I1Terms& terms,
+                double nC) {
+    const Sample sm = sample(a, b, d, nm, nC);
+    return select_with(terms, d, nC, [&](int q) { return sm.err2(q); });
+}
+
+Dims make_dims(uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N, uint32_t K, const I1Format& f) {
+    Dims d{m, n, k, M, N, K, 0, f};
+    d.pmax = i1_pmax(f);
+    return d;
+}
+
+}  // namespace
+
+int i1_pmax(const I1Format& f) { return (int)std::ceil(160.0 / std::log2(f.radix)) + 1; }
+
+I1Normalization i1_normalization(double rgA, double rgB, const uint64_t* row_max, const uint64_t* col_max,
+                                 const double* nrA, const double* nrB, uint64_t m, uint64_t n, const I1Format& f) {
+    const Dims d = make_dims(m, n, 1, 64, 64, 32, f);
+    Normalization nm;
+    nm.rgA = rgA;
+    nm.rgB = rgB;
+    nm.eA.assign(m, 0);
+    nm.sA.assign(m, 0.0);
+    nm.eB.assign(n, 0);
+    nm.sB.assign(n, 0.0);
+    nm.nrA.assign(nrA, nrA + m);
+    nm.nrB.assign(nrB, nrB + n);
+    const auto value = [](uint64_t u) {
+        double x;
+        std::memcpy(&x, &u, 8);
+        return x;
+    };
+    for (uint64_t i = 0; i < m; ++i) row_scale(value(row_max[i]), rgA, d, nm.eA[i], nm.sA[i]);
+    for (uint64_t j = 0; j < n; ++j) row_scale(value(col_max[j]), rgB, d, nm.eB[j], nm.sB[j]);
+    return nm;
+}
+
+I1SamplePick i1_pick(const I1Normalization& nm) {
+    I1SamplePick sp;
+    pick(nm.nrA, nm.sA, kSeedRows, sp.rows, sp.wr);
+    pick(nm.nrB, nm.sB, kSeedCols, sp.cols, sp.wc);
+    return sp;
+}
+
+double i1_sample_norm2(const I1SamplePick& sp, const std::vector<double>& Ch, double nC) {
+    const size_t na = sp.rows.size(), nb = sp.cols.size();
+    double ns = 0;
+    for (size_t s = 0; s < na; ++s)
+        for (size_t u = 0; u < nb; ++u) ns += sp.wr[s] * sp.wc[u] * Ch[s * nb + u] * Ch[s * nb + u];
+    return std::max(nC, ns);
+}
+
+double i1_model2_finish(const double* part, uint32_t nch, const I1SamplePick& sp, const std::vector<double>& Ch,
+                        const std::vector<double>& Cl, const I1Normalization& nm, double norm2) {
+    if (sp.rows.empty() || sp.cols.empty()) return 0.0;
+    return model2_finish(part, nch, sp.rows, sp.cols, sp.wr, sp.wc, Ch, Cl, nm, norm2);
+}
+
+int i1_select_with(const I1Terms& terms, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N, uint32_t K,
+                   const I1Format& f, double nC, const std::function<double(int)>& model2) {
+    return select_with(terms, make_dims(m, n, k, M, N, K, f), nC, model2);
+}
+
+std::vector<double> i1_model1_errors(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                                     const I1Format& f, const I1Terms* terms, const I1Normalization* nm_in) {
+    const Dims d = make_dims(m, n, k, 64, 64, 32, f);
+    if (terms) return combine_terms(*terms, d);
+    const Normalization nm = nm_in ? *nm_in : normalize(a, b, d);
+    return combine_terms(independent_terms(a, b, d, nm), d);
+}
+
+int select_slices(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,
+                  uint32_t K, const I1Format& f) {
+    const Dims d = make_dims(m, n, k, M, N, K, f);
+    const Normalization nm = normalize(a, b, d);
+    const I1Terms terms = independent_terms(a, b, d, nm);
+    const double nC = product_norm_estimate(a, b, m, n, k, N, nm.rgA, nm.rgB);
+    return select_from(a, b, d, nm, terms, nC);
 }
 
 int select_slices_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t M, uint32_t N,
@@ -486,6 +584,12 @@ int select_slices_int8(const double* a, const double* b, uint64_t m, uint64_t n,
 
 int plan_i(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices, const I1Format& f,
            oztt_i_plan& p, std::string& err) {
+    return plan_i_with([&](uint32_t M, uint32_t N, uint32_t K) { return select_slices(a, b, m, n, k, M, N, K, f); },
+                       m, n, k, slices, f, p, err);
+}
+
+int plan_i_with(const std::function<int(uint32_t, uint32_t, uint32_t)>& select, uint64_t m, uint64_t n, uint64_t k,
+                uint32_t slices, const I1Format& f, oztt_i_plan& p, std::string& err) {
     auto pad = [](uint64_t v, uint64_t q) { return (v + q - 1) / q * q; };
     std::memset(&p, 0, sizeof p);
     if (!m || !n || !k) {
@@ -507,7 +611,7 @@ int plan_i(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
     p.format = f.format;
     p.radix = (int32_t)f.radix;
     p.dmax = (int32_t)f.dmax;
-    p.p = slices ? (int32_t)slices : select_slices(a, b, m, n, k, p.M, p.N, p.K, f);
+    p.p = slices ? (int32_t)slices : select(p.M, p.N, p.K);
     const int L = p.p - 1;
     char msg[512];
     // The issue the reference plans (plan_issue, ozaki1/plan.hpp:141-226): the pair loop or the pairwise

@@ -105,8 +105,11 @@ public:
     // order), after b_done
     void a_cols(const double* a, uint64_t c0, uint64_t c1);
     void a_done(const double* a);
-    // row_max / col_max, when given, receive the magnitude patterns of A's row and B's column maxima
-    PolicyStats collect(std::vector<uint64_t>* row_max = nullptr, std::vector<uint64_t>* col_max = nullptr);
+    // row_max / col_max, when given, receive the magnitude patterns of A's row and B's column maxima;
+    // row_sumsq / col_sumsq the scaled squared norms of A's rows and B's columns; rg the scales of A and B
+    PolicyStats collect(std::vector<uint64_t>* row_max = nullptr, std::vector<uint64_t>* col_max = nullptr,
+                        std::vector<double>* row_sumsq = nullptr, std::vector<double>* col_sumsq = nullptr,
+                        double* rg = nullptr);
 
 private:
     struct Bufs;

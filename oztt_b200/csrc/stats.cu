@@ -438,7 +438,8 @@ void PolicyStatsRun::a_done(const double* a) {
     OZTT_CUDA(cudaGetLastError());
 }
 
-PolicyStats PolicyStatsRun::collect(std::vector<uint64_t>* row_max, std::vector<uint64_t>* col_max) {
+PolicyStats PolicyStatsRun::collect(std::vector<uint64_t>* row_max, std::vector<uint64_t>* col_max,
+                                    std::vector<double>* row_sumsq, std::vector<double>* col_sumsq, double* rg_out) {
     const uint64_t m = m_, n = n_;
     std::vector<unsigned long long> hr(m), hc(n);
     std::vector<double> h2r(m), h2c(n), hs((size_t)kVectors * m);
@@ -481,6 +482,12 @@ PolicyStats PolicyStatsRun::collect(std::vector<uint64_t>* row_max, std::vector<
     ps.measured = true;
     if (row_max) row_max->assign(hr.begin(), hr.end());
     if (col_max) col_max->assign(hc.begin(), hc.end());
+    if (row_sumsq) *row_sumsq = h2r;
+    if (col_sumsq) *col_sumsq = h2c;
+    if (rg_out) {
+        rg_out[0] = rgA;
+        rg_out[1] = rgB;
+    }
     return ps;
 }
 

@@ -276,3 +276,44 @@ def test_context_scheme_i_fp8(oztt, oracle, cuda):
     # the fixed slice count of the reference's test for FP8 (tests/correctness.cpp:280)
     c12 = ctx.multiply(a, b, m, n, k, oztt.Options(scheme=oztt.Scheme.I, format=oztt.Format.FP8, slices=12))
     assert np.array_equal(c12.view(np.uint64), oracle.i_emulate(a, b, m, n, k, 12, exact=True, fmt=FP8).view(np.uint64))
+
+
+# ---- slice selection with the per-element statistics measured on the device (plan1_dev.cu) --------------
+SELECT_CASES = [(5, 150, 90, 260, 0.5, 41, None), (5, 129, 65, 200, 4.0, 42, "tiny"), (4, 97, 131, 77, 1.0, 43, None),
+                (0, 200, 72, 256, 2.0, 44, "zeros"), (5, 300, 280, 1000, 8.0, 45, None), (2, 64, 64, 64, -1.0, 46, None),
+                (4, 1, 70, 1000, 1.0, 47, "zeros"), (0, 513, 257, 129, 0.5, 48, "tiny")]
+
+
+@pytest.mark.parametrize("fmt,m,n,k,phi,seed,extra", SELECT_CASES)
+def test_device_selection_equals_host(oztt, oracle, cuda, fmt, m, n, k, phi, seed, extra):
+    """Model (1)'s error vector and the ||C||_F^2 estimate measured on the device equal the host planner's to
+    the bit, and so does the plan (zero rows and columns, elements below 2^-383 that send the device
+    statistics to their scale-first recomputation, every radix)."""
+    a, b = oracle.gen_inputs(m, n, k, phi, seed)
+    if extra == "zeros":
+        a[: k] = 0.0
+        b[::5] = 0.0
+    if extra == "tiny":
+        a[3], b[7] = 2.0 ** -500, -(2.0 ** -450)
+    A, B = dev(a), dev(b)
+    host = oztt.i_model1_errors(a, b, m, n, k, fmt=fmt)
+    devv = oztt.i_model1_errors(None, None, m, n, k, fmt=fmt, a_dev=A.data_ptr(), b_dev=B.data_ptr(),
+                                stream=stream())
+    assert np.array_equal(host.view(np.uint64), devv.view(np.uint64))
+    hp = oztt.i_int8_plan(a, b, m, n, k, fmt=fmt)
+    dp = oztt.i_plan_device(A.data_ptr(), B.data_ptr(), m, n, k, fmt=fmt, stream=stream())
+    assert bytes(hp) == bytes(dp)
+
+
+@pytest.mark.parametrize("fmt", [5, 4, 0])
+def test_context_scheme_i_device_selection(oztt, oracle, cuda, fmt):
+    """Context::gemm's Scheme I call selects the slice count on the device and runs on the resident operands:
+    the host plan's p and the bits of the host-planned run."""
+    m, n, k = 333, 222, 444
+    a, b = oracle.gen_inputs(m, n, k, 1.0, 49)
+    plan = oztt.i_int8_plan(a, b, m, n, k, fmt=fmt)
+    c = np.empty(m * n)
+    info = oztt.Context().gemm(a, b, c, m, n, k, oztt.Options(scheme=oztt.Scheme.I, format=fmt))
+    assert info.slices == plan.p
+    ref = oztt.i_int8_run(a, b, m, n, k, plan)
+    assert np.array_equal(c.view(np.uint64), ref.view(np.uint64))
