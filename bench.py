@@ -17,8 +17,10 @@ collective on the data path (weak scaling; at N=4 the global problem is 32768 x 
 
 Printed (rank 0, one JSON line): value = 2*m*n*k*N / (max over ranks of the device time of one step),
 e2e = the same metric through the public API (ozTTgemm::Context::gemm via the C ABI) from pinned host
-buffers including the host planning, the copies in and the copy of C back, the roofline of the residue
-GEMM (int8 tensor ops per launch / its CUDA-event duration against the B200 dense int8 peak), the
+buffers including the copies in (with the device-measured plan statistics and value checks overlapped),
+the plan and the banded pipeline with the copy of C back overlapped, the roofline of the residue GEMM
+(int8 tensor ops per launch / its CUDA-event duration against the measured sustained int8 rate), the
+effective rate the selected moduli allow at that rate (moduli_roofline), the ratio to the B200 FP64 peak, the
 reference's host FP64 GEMM (Dot2, compiled from the reference sources in oracle/_ref) timed on a sample
 of rows as the CPU baseline, cuBLAS DGEMM on the same GPU for comparison, and the maximum relative error
 of sampled rows against a binary128 reference.
@@ -44,6 +46,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 DEFAULT_SIZE = 16384
+FP64_PEAK_TFLOPS = 40.0
 METRIC = "Ozaki-II INT8 effective FP64 TFLOPS at m=n=k=16384; max rel err vs binary128"
 
 
@@ -475,8 +478,9 @@ def main() -> None:
     A = torch.from_numpy(a).cuda()
     B = torch.from_numpy(b).cuda()
     t_plan = time.perf_counter()
-    if world == 1:
-        plan = oz.ii_int8_plan(a, b, m, n, k)
+    if world == 1:  # as Context::gemm plans: the policy statistics measured on the device
+        plan = oz.ii_int8_plan_device(A.data_ptr(), B.data_ptr(), m, n, k,
+                                      stream=torch.cuda.current_stream().cuda_stream)
     else:  # the precision decision of the global problem: panel statistics all-reduced over NCCL
         from oztt_b200.distributed import Grid, plan_ii_int8_tiled
 
@@ -539,8 +543,14 @@ def main() -> None:
                          "moduli": S, "integer_bits": plan.b, "reconstruction_passes": 2 if plan.two_pass else 1,
                          "l2": "inputs (2.1 GB each) larger than the 126 MB L2; no flush",
                          "planning_s": round(t_plan, 3),
-                         "planning": "host (reference arithmetic)" if world == 1 else
+                         "planning": "device-measured statistics" if world == 1 else
                                      "global statistics from the panels of all ranks (NCCL all-reduce)"},
+              "moduli_roofline": {
+                  "tflops": int8_peak / S, "frac": value / (int8_peak / S),
+                  "meaning": "effective FP64 TFLOPS the sustained int8 tensor rate allows with S moduli "
+                             "(2mnk FP64 flops cost 2mnk*S int8 ops); frac = value / that"},
+              "vs_fp64_peak": {"fp64_peak_tflops": FP64_PEAK_TFLOPS, "ratio": value / FP64_PEAK_TFLOPS,
+                               "source": "B200 nominal dense FP64 (vector and tensor core), NVIDIA datasheet"},
               "stage_ms": {"scale_rows": stage_ms[0], "scale_cols": stage_ms[1], "split_rows": stage_ms[2],
                            "split_cols": stage_ms[3], "residue_gemm": stage_ms[4], "recon": stage_ms[5]},
               "roofline": {"bound": "tensor", "kernel": "residue_gemm_kernel<1> (tcgen05 kind::i8)",
