@@ -12,8 +12,8 @@
 // combining the terms, picking the sample, the rounding simulation, the search). The result is
 // bit-identical to the host planner's.
 //
-// terms_kernel runs one thread per column c of A (rows in ascending order) or per row r of B (columns in
-// ascending order), as the host sums them. Each element x (scaled by 2^(nshift - e) of its row or column)
+// terms_kernel runs one thread per column c of A (rows in ascending order) and per row r of B (columns in
+// ascending order), as the host sums them, in one launch. Each element x (scaled by 2^(nshift - e) of its row or column)
 // is expanded as the reference's device slicer does -- u = radix t (FMA-exact product, TwoSum), digit
 // d = clamp(rint(fl32(u_hi)), +-dmax), t = u - d in two doubles -- until its residual is zero, adding
 // (s d w)^2 to S[i] and (s t w)^2 to R[i+1] with w = radix^-(i+1) formed by repeated division. Every
@@ -39,42 +39,39 @@ __device__ __forceinline__ void two_sum_d(double a, double b, double& s, double&
 // 2^e for |e| <= 1022.
 __device__ __forceinline__ double pow2d(int e) { return __longlong_as_double((long long)(1023 + e) << 52); }
 
-template <int PMAX>
-__device__ __forceinline__ void expand_add(double x, double s, double radix, double dmax, double (&S)[PMAX],
-                                           double (&R)[PMAX + 1]) {
-    double th = x, tl = 0.0, w = 1.0;
-    bool live = true;
-#pragma unroll
-    for (int i = 0; i < PMAX; ++i) {
-        if (live) {
-            w = __ddiv_rn(w, radix);
-            const double ph = __dmul_rn(radix, th);
-            const double pe = __fma_rn(radix, th, -ph);
-            double uh, ul;
-            two_sum_d(ph, __dadd_rn(pe, __dmul_rn(radix, tl)), uh, ul);
-            const double r = rint((double)__double2float_rn(uh));
-            const double dg = fmin(dmax, fmax(-dmax, r));
-            two_sum_d(__dsub_rn(uh, dg), ul, th, tl);
-            const double c = __dmul_rn(__dmul_rn(s, dg), w);
-            S[i] = __dadd_rn(S[i], __dmul_rn(c, c));
-            const double rr = __dmul_rn(__dmul_rn(s, __dadd_rn(th, tl)), w);
-            R[i + 1] = __dadd_rn(R[i + 1], __dmul_rn(rr, rr));
-            live = th != 0.0;
-        }
-    }
+// One step of the expansion t = th + tl: u = radix t, digit d = clamp(rint(fl32(u_hi)), +-dmax), t = u - d.
+__device__ __forceinline__ double expand_step(double& th, double& tl, double radix, double dmax) {
+    const double ph = __dmul_rn(radix, th);
+    const double pe = __fma_rn(radix, th, -ph);
+    double uh, ul;
+    two_sum_d(ph, __dadd_rn(pe, __dmul_rn(radix, tl)), uh, ul);
+    const double dg = fmin(dmax, fmax(-dmax, rint((double)__double2float_rn(uh))));
+    two_sum_d(__dsub_rn(uh, dg), ul, th, tl);
+    return dg;
 }
 
-// Thread t walks `len` elements from x + t*thread_stride, elem_stride apart: for A, column c (elements
-// i*k + c: thread stride 1, element stride k); for B, row r (elements r*n + j: thread stride n, element
-// stride 1). s[e] and sh[e] are the divisor and the exponent shift of element e's row of A (column of B);
-// the sums go to S_out[i][t], R_out[q][t] and N_out[t].
+// The sums of one side (A or B) of model (1).
+struct TermsSide {
+    const double* x;                 // thread t walks len elements from x + t*thread_stride, elem_stride apart
+    uint64_t len, thread_stride, elem_stride;
+    const double* s;                 // divisor of element e's row of A (column of B); 0: not counted
+    const int32_t* sh;               // its exponent shift nshift - e
+    double rg;
+    double *S, *R, *N;               // S[i][t], R[q][t], N[t]
+};
+
+// Thread t of side A (blocks below a_blocks) or B: the element chains of kLanes consecutive elements
+// advance together, and at each step their contributions join the sums in element order, so every sum
+// receives its terms in the host's order while the chains overlap. A lane whose residual is exactly zero
+// adds +0 from then on (the sums are never -0, so +0 changes nothing), as the host stops adding.
+constexpr int kLanes = 4;
+
 template <int PMAX>
-__global__ void __launch_bounds__(128) terms_kernel(const double* __restrict__ x, uint64_t threads, uint64_t len,
-                                                    uint64_t thread_stride, uint64_t elem_stride,
-                                                    const double* __restrict__ s, const int32_t* __restrict__ sh,
-                                                    double rg, double radix, double dmax, double* __restrict__ S_out,
-                                                    double* __restrict__ R_out, double* __restrict__ N_out) {
-    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(64) terms_kernel(TermsSide A, TermsSide B, uint64_t threads, uint32_t a_blocks,
+                                                   double radix, double dmax) {
+    const bool side_b = blockIdx.x >= a_blocks;
+    const TermsSide& sd = side_b ? B : A;
+    const uint64_t t = (uint64_t)(blockIdx.x - (side_b ? a_blocks : 0)) * blockDim.x + threadIdx.x;
     if (t >= threads) return;
     double S[PMAX], R[PMAX + 1];
 #pragma unroll
@@ -82,37 +79,75 @@ __global__ void __launch_bounds__(128) terms_kernel(const double* __restrict__ x
 #pragma unroll
     for (int i = 0; i <= PMAX; ++i) R[i] = 0.0;
     double nrm = 0.0;
-    const double* p = x + t * thread_stride;
-    for (uint64_t e = 0; e < len; ++e) {
-        const double v = __ldg(p + e * elem_stride);
-        const double vr = __dmul_rn(v, rg);
-        nrm = __dadd_rn(nrm, __dmul_rn(vr, vr));
-        const double se = __ldg(s + e);
-        if (v != 0.0 && se > 0.0) expand_add<PMAX>(__dmul_rn(v, pow2d(__ldg(sh + e))), se, radix, dmax, S, R);
+    const double* p = sd.x + t * sd.thread_stride;
+    for (uint64_t e0 = 0; e0 < sd.len; e0 += kLanes) {
+        double th[kLanes], tl[kLanes], sc[kLanes];
+        bool live[kLanes];
+#pragma unroll
+        for (int l = 0; l < kLanes; ++l) {
+            const uint64_t e = e0 + l;
+            th[l] = tl[l] = sc[l] = 0.0;
+            live[l] = false;
+            if (e < sd.len) {
+                const double v = __ldg(p + e * sd.elem_stride);
+                const double vr = __dmul_rn(v, sd.rg);
+                nrm = __dadd_rn(nrm, __dmul_rn(vr, vr));
+                const double se = __ldg(sd.s + e);
+                if (v != 0.0 && se > 0.0) {
+                    live[l] = true;
+                    th[l] = __dmul_rn(v, pow2d(__ldg(sd.sh + e)));
+                    sc[l] = se;
+                }
+            }
+        }
+        double w = 1.0;
+#pragma unroll
+        for (int i = 0; i < PMAX; ++i) {
+            bool any = false;
+#pragma unroll
+            for (int l = 0; l < kLanes; ++l) any |= live[l];
+            if (!any) break;
+            w = __ddiv_rn(w, radix);
+            double cs[kLanes], cr[kLanes];
+#pragma unroll
+            for (int l = 0; l < kLanes; ++l) {
+                cs[l] = cr[l] = 0.0;
+                if (live[l]) {
+                    const double dg = expand_step(th[l], tl[l], radix, dmax);
+                    const double c = __dmul_rn(__dmul_rn(sc[l], dg), w);
+                    cs[l] = __dmul_rn(c, c);
+                    const double r = __dmul_rn(__dmul_rn(sc[l], __dadd_rn(th[l], tl[l])), w);
+                    cr[l] = __dmul_rn(r, r);
+                    live[l] = th[l] != 0.0;
+                }
+            }
+#pragma unroll
+            for (int l = 0; l < kLanes; ++l) {
+                S[i] = __dadd_rn(S[i], cs[l]);
+                R[i + 1] = __dadd_rn(R[i + 1], cr[l]);
+            }
+        }
     }
 #pragma unroll
-    for (int i = 0; i < PMAX; ++i) S_out[(uint64_t)i * threads + t] = S[i];
+    for (int i = 0; i < PMAX; ++i) sd.S[(uint64_t)i * threads + t] = S[i];
 #pragma unroll
-    for (int i = 0; i <= PMAX; ++i) R_out[(uint64_t)i * threads + t] = R[i];
-    N_out[t] = nrm;
+    for (int i = 0; i <= PMAX; ++i) sd.R[(uint64_t)i * threads + t] = R[i];
+    sd.N[t] = nrm;
 }
 
 template <int PMAX>
-void launch_terms(const double* x, uint64_t threads, uint64_t len, uint64_t thread_stride, uint64_t elem_stride,
-                  const double* s, const int32_t* sh, double rg, const I1Format& f, double* S, double* R, double* N,
-                  cudaStream_t st) {
-    terms_kernel<PMAX><<<(unsigned)((threads + 127) / 128), 128, 0, st>>>(
-        x, threads, len, thread_stride, elem_stride, s, sh, rg, f.radix, f.dmax, S, R, N);
+void launch_terms(const TermsSide& A, const TermsSide& B, uint64_t threads, const I1Format& f, cudaStream_t st) {
+    const uint32_t blocks = (uint32_t)((threads + 63) / 64);
+    terms_kernel<PMAX><<<2 * blocks, 64, 0, st>>>(A, B, threads, blocks, f.radix, f.dmax);
     OZTT_CUDA(cudaGetLastError());
 }
 
-void launch_terms_any(int pmax, const double* x, uint64_t threads, uint64_t len, uint64_t thread_stride,
-                      uint64_t elem_stride, const double* s, const int32_t* sh, double rg, const I1Format& f, double* S,
-                      double* R, double* N, cudaStream_t st) {
+void launch_terms_any(int pmax, const TermsSide& A, const TermsSide& B, uint64_t threads, const I1Format& f,
+                      cudaStream_t st) {
     switch (pmax) {
-    case 22: launch_terms<22>(x, threads, len, thread_stride, elem_stride, s, sh, rg, f, S, R, N, st); break;
-    case 28: launch_terms<28>(x, threads, len, thread_stride, elem_stride, s, sh, rg, f, S, R, N, st); break;
-    case 33: launch_terms<33>(x, threads, len, thread_stride, elem_stride, s, sh, rg, f, S, R, N, st); break;
+    case 22: launch_terms<22>(A, B, threads, f, st); break;
+    case 28: launch_terms<28>(A, B, threads, f, st); break;
+    case 33: launch_terms<33>(A, B, threads, f, st); break;
     default: throw Error(OZTT_EINVAL, "scheme I: no device slice-selection kernel for this radix");
     }
 }
@@ -179,12 +214,7 @@ __global__ void __launch_bounds__(128) sample_err_kernel(const double* __restric
 #pragma unroll
         for (int i = 0; i < PMAX; ++i) {
             if (i < q) {
-                const double ph = __dmul_rn(radix, th);
-                const double pe = __fma_rn(radix, th, -ph);
-                double uh, ul;
-                two_sum_d(ph, __dadd_rn(pe, __dmul_rn(radix, tl)), uh, ul);
-                const double dg = fmin(dmax, fmax(-dmax, rint((double)__double2float_rn(uh))));
-                two_sum_d(__dsub_rn(uh, dg), ul, th, tl);
+                const double dg = expand_step(th, tl, radix, dmax);
                 w = __ddiv_rn(w, radix);
                 D[i] = __dmul_rn(dg, w);
             }
@@ -197,12 +227,7 @@ __global__ void __launch_bounds__(128) sample_err_kernel(const double* __restric
 #pragma unroll
         for (int r = 1; r <= PMAX; ++r) {
             if (r <= q) {
-                const double ph = __dmul_rn(radix, th);
-                const double pe = __fma_rn(radix, th, -ph);
-                double uh, ul;
-                two_sum_d(ph, __dadd_rn(pe, __dmul_rn(radix, tl)), uh, ul);
-                const double dg = fmin(dmax, fmax(-dmax, rint((double)__double2float_rn(uh))));
-                two_sum_d(__dsub_rn(uh, dg), ul, th, tl);
+                (void)expand_step(th, tl, radix, dmax);
                 w = __ddiv_rn(w, radix);
                 RY[r] = __dmul_rn(__dadd_rn(th, tl), w);
             }
@@ -329,11 +354,12 @@ void measure_i1_device(const double* a, const double* b, uint64_t m, uint64_t n,
     OZTT_CUDA(cudaMemcpyAsync(dshB.p, shB.data(), n * 4, cudaMemcpyHostToDevice, st));
     OZTT_CUDA(cudaMemsetAsync(SA.p, 0, P1 * k * 8, st));  // row pmax of S stays zero
     OZTT_CUDA(cudaMemsetAsync(SB.p, 0, P1 * k * 8, st));
-    // A: thread c walks rows i (elements i*k + c); B: thread r walks columns j (elements r*n + j)
-    launch_terms_any(pmax, a, k, m, 1, k, dsA.as<double>(), dshA.as<int32_t>(), nm.rgA, f, SA.as<double>(),
-                     RA.as<double>(), NA.as<double>(), st);
-    launch_terms_any(pmax, b, k, n, n, 1, dsB.as<double>(), dshB.as<int32_t>(), nm.rgB, f, SB.as<double>(),
-                     RB.as<double>(), NB.as<double>(), st);
+    // A: thread c walks rows i (elements i*k + c); B: thread r walks columns j (elements r*n + j); one launch
+    const TermsSide sa{a, m, 1, k, dsA.as<double>(), dshA.as<int32_t>(), nm.rgA, SA.as<double>(), RA.as<double>(),
+                       NA.as<double>()};
+    const TermsSide sb{b, n, n, 1, dsB.as<double>(), dshB.as<int32_t>(), nm.rgB, SB.as<double>(), RB.as<double>(),
+                       NB.as<double>()};
+    launch_terms_any(pmax, sa, sb, k, f, st);
     terms.SA.resize(P1 * k);
     terms.RA.resize(P1 * k);
     terms.SB.resize(P1 * k);
