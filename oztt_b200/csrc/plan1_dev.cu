@@ -331,8 +331,8 @@ void measure_i1_device(const double* a, const double* b, uint64_t m, uint64_t n,
     std::vector<double> nrA, nrB;
     double rg[2] = {1.0, 1.0};
     {
-        PolicyStatsRun run(m, n, k, N, st, 0);
-        run.b_rows(b, 0, k);
+        PolicyStatsRun run(m, n, k, N, st);
+        run.b_cols(b, 0, n);
         run.b_done(b);
         run.a_cols(a, 0, k);
         run.a_done(a);

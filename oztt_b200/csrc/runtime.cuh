@@ -86,23 +86,21 @@ bool evaluation_active();
 
 struct PolicyStats;
 
-// The input statistics of the Scheme II precision policy measured on the device in stages: B's rows in
-// any chunks, then B's own stages, then A's rows, then A's; collect() reads back (synchronising the
-// stream) and finishes the reductions on the host in the reference's order. The result is bit-identical
-// to the host measurement for the padded planning width N.
-// `side` extra streams carry the sketches of B's row chunks (0: everything on st). The caller orders
-// each chunk's arrival before st ahead of the chunk's call; b_done rejoins the side streams into st.
-// A comes in blocks of columns (all rows), so that every row's sequential sums advance as each block
-// lands and only the last block's share is left when the upload ends.
+// The input statistics of the Scheme II precision policy measured on the device in stages: B's blocks,
+// then B's own stages, then A's blocks, then A's; collect() reads back (synchronising the stream) and
+// finishes the reductions on the host in the reference's order. The result is bit-identical to the host
+// measurement for the padded planning width N. Operands come in blocks of columns (all rows), B first and then A, so that every row's and column's
+// sequential sums advance as each block lands and only the last block's share is left when the upload
+// ends. The caller orders each block's arrival before st ahead of the block's call.
 class PolicyStatsRun {
 public:
-    PolicyStatsRun(uint64_t m, uint64_t n, uint64_t k, uint32_t N, cudaStream_t st, int side);
+    PolicyStatsRun(uint64_t m, uint64_t n, uint64_t k, uint32_t N, cudaStream_t st);
     ~PolicyStatsRun();
-    // maxima, sums of squares and sketch of rows row0 .. row0+rows-1 of B (chunks in row order)
-    void b_rows(const double* b_chunk, uint64_t row0, uint64_t rows);
+    // maxima, sums of squares and sketch over columns c0 .. c1-1 of B (b: the whole row-major B; blocks in
+    // column order)
+    void b_cols(const double* b, uint64_t c0, uint64_t c1);
     void b_done(const double* b);  // B's scale, then its sums and y = B g scaled
-    // the same for columns c0 .. c1-1 of all rows of A (a: the whole row-major A; blocks in column
-    // order), after b_done
+    // the same for columns c0 .. c1-1 of all rows of A (a: the whole row-major A), after b_done
     void a_cols(const double* a, uint64_t c0, uint64_t c1);
     void a_done(const double* a);
     // row_max / col_max, when given, receive the magnitude patterns of A's row and B's column maxima;
@@ -113,29 +111,21 @@ public:
 
 private:
     struct Bufs;
-    void order(cudaStream_t from, cudaStream_t to);
-    cudaStream_t next_side();
-    void join_sides();
     uint64_t m_, n_, k_;
     uint32_t N_;
     cudaStream_t st_;
+    cudaStream_t cols_st_ = nullptr;  // B's per-column stages, rejoined into st by b_done
+    cudaEvent_t landed_ = nullptr, cols_done_ = nullptr;
     int sms_ = 148;
-    std::vector<cudaStream_t> side_;
-    std::vector<cudaEvent_t> events_;
-    size_t next_ = 0;
     std::unique_ptr<Bufs> bufs_;
     std::shared_ptr<const std::vector<double>> g_;
 };
 
-// Context::gemm from host buffers with the transfers overlapped (streamed.cu): A and B uploaded in
-// pieces while the device measures the precision-policy statistics, then the caller's pipeline on the
-// work stream, marking each finished band of rows of C, which goes back on a copy stream while the next
-// band is computed. Every stream is drained before the buffers are released.
 class StreamedCall {
 public:
     StreamedCall(int device_id, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k);
     ~StreamedCall();
-    // B in chunks of rows, then A in blocks of columns, with the statistics measured as they land;
+    // B, then A, in blocks of columns, with the statistics measured as they land;
     // returns them, with the magnitude patterns of A's row maxima and B's column maxima.
     PolicyStats upload(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max);
     const double* a_dev() const { return da_->as<double>(); }

@@ -55,16 +55,18 @@ __global__ void __launch_bounds__(256) row_absmax_kernel(const double* __restric
     }
 }
 
-// Column maxima: a thread per column over a chunk of rows, combined with atomicMax.
+// Column maxima of n columns of rows ldb apart: a thread per column over a chunk of rows, combined with
+// atomicMax.
 __global__ void __launch_bounds__(256) col_absmax_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
-                                                         uint64_t rows_per_chunk, unsigned long long* __restrict__ out) {
+                                                         uint64_t ldb, uint64_t rows_per_chunk,
+                                                         unsigned long long* __restrict__ out) {
     const uint64_t col = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (col >= n) return;
     const uint64_t r0 = (uint64_t)blockIdx.y * rows_per_chunk, r1 = min(k, r0 + rows_per_chunk);
     const unsigned long long* pu = reinterpret_cast<const unsigned long long*>(b);
     unsigned long long mx = 0;
     for (uint64_t r = r0; r < r1; ++r) {
-        const unsigned long long v = __ldg(pu + r * n + col) & 0x7FFFFFFFFFFFFFFFull;
+        const unsigned long long v = __ldg(pu + r * ldb + col) & 0x7FFFFFFFFFFFFFFFull;
         mx = v > mx ? v : mx;
     }
     if (mx) atomicMax(out + col, mx);
@@ -90,18 +92,21 @@ constexpr int kSketchThreads = 128;
 
 // sum over `len` terms at stride `stride` from p of (x*rg)^2, continuing from sq; raises `small` for a
 // tiny element.
+// B is the batch; a column chain (stride of a whole row) waits on DRAM for every batch, so it takes a
+// larger one.
+template <int B = kBatch>
 __device__ __forceinline__ double sumsq_chain(const double* __restrict__ p, uint64_t len, uint64_t stride, double rg,
                                               double sq, bool& small) {
-    double cur[kBatch], nxt[kBatch];
+    double cur[B], nxt[B];
 #pragma unroll
-    for (int u = 0; u < kBatch; ++u) cur[u] = (uint64_t)u < len ? __ldg(p + (uint64_t)u * stride) : 0.0;
-    for (uint64_t j0 = 0; j0 < len; j0 += kBatch) {
-        const uint64_t j1 = j0 + kBatch;
+    for (int u = 0; u < B; ++u) cur[u] = (uint64_t)u < len ? __ldg(p + (uint64_t)u * stride) : 0.0;
+    for (uint64_t j0 = 0; j0 < len; j0 += B) {
+        const uint64_t j1 = j0 + B;
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) nxt[u] = j1 + u < len ? __ldg(p + (j1 + u) * stride) : 0.0;
-        const int cnt = len - j0 < (uint64_t)kBatch ? (int)(len - j0) : kBatch;
+        for (int u = 0; u < B; ++u) nxt[u] = j1 + u < len ? __ldg(p + (j1 + u) * stride) : 0.0;
+        const int cnt = len - j0 < (uint64_t)B ? (int)(len - j0) : B;
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
+        for (int u = 0; u < B; ++u) {
             if (u < cnt) {
                 small |= is_tiny(cur[u]);
                 const double v = __dmul_rn(cur[u], rg);
@@ -109,7 +114,7 @@ __device__ __forceinline__ double sumsq_chain(const double* __restrict__ p, uint
             }
         }
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) cur[u] = nxt[u];
+        for (int u = 0; u < B; ++u) cur[u] = nxt[u];
     }
     return sq;
 }
@@ -127,14 +132,14 @@ __global__ void __launch_bounds__(128) row_sumsq_kernel(const double* __restrict
     if (i >= m || (gate && *gate == 0u)) return;
     if (rgp) rg = *rgp;
     bool small = false;
-    out[i] = sumsq_chain(a + i * lda, cols, 1, rg, carry ? out[i] : 0.0, small);
+    out[i] = sumsq_chain<>(a + i * lda, cols, 1, rg, carry ? out[i] : 0.0, small);
     if (tiny && small) atomicOr(tiny, 1u);
 }
 
-// sum_r (b[r][j]*rg)^2 for each column j, r ascending over the `rows` rows given; with `carry` the sum
-// continues from out[j] (the rows of an earlier chunk).
+// sum_r (b[r][j]*rg)^2 for each of n columns j (rows ldb apart), r ascending over the `rows` rows given;
+// with `carry` the sum continues from out[j] (the rows of an earlier chunk).
 __global__ void __launch_bounds__(128) col_sumsq_kernel(const double* __restrict__ b, uint64_t rows, uint64_t n,
-                                                        double rg, const double* __restrict__ rgp,
+                                                        uint64_t ldb, double rg, const double* __restrict__ rgp,
                                                         double* __restrict__ out, int carry,
                                                         uint32_t* __restrict__ tiny,
                                                         const uint32_t* __restrict__ gate) {
@@ -142,7 +147,7 @@ __global__ void __launch_bounds__(128) col_sumsq_kernel(const double* __restrict
     if (j >= n || (gate && *gate == 0u)) return;
     if (rgp) rg = *rgp;
     bool small = false;
-    out[j] = sumsq_chain(b + j, rows, n, rg, carry ? out[j] : 0.0, small);
+    out[j] = sumsq_chain<32>(b + j, rows, ldb, rg, carry ? out[j] : 0.0, small);
     if (tiny && small) atomicOr(tiny, 1u);
 }
 
@@ -296,9 +301,8 @@ std::shared_ptr<const std::vector<double>> policy_vectors(uint32_t N) {
 
 }  // namespace
 
-// The statistics in stages on stream st (and `side` extra streams for the row-local stages of the
-// chunks, so that the chunks' latency-bound sums overlap one another), every stage stream-ordered;
-// collect() is the one synchronisation. Chunk stages measure unscaled values; the finishing stage of
+// The statistics in stages on stream st, every stage stream-ordered; collect() is the one
+// synchronisation. Chunk stages measure unscaled values; the finishing stage of
 // each matrix scales them once its scale is known (or, after a tiny element, recomputes scale-first).
 struct PolicyStatsRun::Bufs {
     Bufs(cudaStream_t st, uint64_t m, uint64_t n, uint64_t k, uint32_t N)
@@ -310,16 +314,13 @@ struct PolicyStatsRun::Bufs {
     uint32_t* tiny_b() { return words.as<uint32_t>() + 1; }
 };
 
-PolicyStatsRun::PolicyStatsRun(uint64_t m, uint64_t n, uint64_t k, uint32_t N, cudaStream_t st, int side)
+PolicyStatsRun::PolicyStatsRun(uint64_t m, uint64_t n, uint64_t k, uint32_t N, cudaStream_t st)
     : m_(m), n_(n), k_(k), N_(N), st_(st) {
     int dev = 0;
     OZTT_CUDA(cudaGetDevice(&dev));
     OZTT_CUDA(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, dev));
-    for (int i = 0; i < side; ++i) {
-        cudaStream_t x;
-        OZTT_CUDA(cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking));
-        side_.push_back(x);
-    }
+    OZTT_CUDA(cudaStreamCreateWithFlags(&cols_st_, cudaStreamNonBlocking));
+    for (cudaEvent_t* e : {&landed_, &cols_done_}) OZTT_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
     bufs_ = std::make_unique<Bufs>(st, m, n, k, N);
     OZTT_CUDA(cudaMemsetAsync(bufs_->cmax.p, 0, n * 8, st));
     OZTT_CUDA(cudaMemsetAsync(bufs_->words.p, 0, 16, st));
@@ -328,56 +329,44 @@ PolicyStatsRun::PolicyStatsRun(uint64_t m, uint64_t n, uint64_t k, uint32_t N, c
 }
 
 PolicyStatsRun::~PolicyStatsRun() {
-    for (cudaStream_t x : side_) cudaStreamSynchronize(x);
-    bufs_.reset();  // freed on st, after all side work
-    for (cudaEvent_t e : events_) cudaEventDestroy(e);
-    for (cudaStream_t x : side_) cudaStreamDestroy(x);
+    if (cols_st_) cudaStreamSynchronize(cols_st_);
+    bufs_.reset();  // freed on st, after the column stages
+    for (cudaEvent_t e : {landed_, cols_done_})
+        if (e) cudaEventDestroy(e);
+    if (cols_st_) cudaStreamDestroy(cols_st_);
 }
 
-void PolicyStatsRun::order(cudaStream_t from, cudaStream_t to) {
-    cudaEvent_t e;
-    OZTT_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-    events_.push_back(e);
-    OZTT_CUDA(cudaEventRecord(e, from));
-    OZTT_CUDA(cudaStreamWaitEvent(to, e, 0));
-}
-
-// The stream of the next row-local chunk stage, ordered after everything issued on st so far.
-cudaStream_t PolicyStatsRun::next_side() {
-    if (side_.empty()) return st_;
-    cudaStream_t x = side_[next_++ % side_.size()];
-    order(st_, x);
-    return x;
-}
-
-void PolicyStatsRun::join_sides() {
-    for (cudaStream_t x : side_) order(x, st_);
-}
-
-void PolicyStatsRun::b_rows(const double* b_chunk, uint64_t row0, uint64_t rows) {
-    if (!rows) return;
-    const uint64_t col_blocks = (n_ + 255) / 256;
+void PolicyStatsRun::b_cols(const double* b, uint64_t c0, uint64_t c1) {
+    if (c1 <= c0) return;
+    const uint64_t w = c1 - c0;
+    // Each column of the block is complete, so its maximum and its sum of squares (a chain over all k
+    // rows, latency-bound for a narrow block) depend on no other block: they run on their own stream,
+    // beside the sketch sums, which continue from block to block on st.
+    OZTT_CUDA(cudaEventRecord(landed_, st_));
+    OZTT_CUDA(cudaStreamWaitEvent(cols_st_, landed_, 0));
+    const uint64_t col_blocks = (w + 255) / 256;
     const uint64_t want = std::max<uint64_t>(1, (uint64_t)sms_ * 8 / std::max<uint64_t>(col_blocks, 1));
-    const uint64_t chunks = std::min<uint64_t>(std::min<uint64_t>(want, rows), 65535);
-    const uint64_t rpc = (rows + chunks - 1) / chunks;
-    col_absmax_kernel<<<dim3((unsigned)col_blocks, (unsigned)((rows + rpc - 1) / rpc)), 256, 0, st_>>>(
-        b_chunk, rows, n_, rpc, bufs_->cmax.as<unsigned long long>());
+    const uint64_t chunks = std::min<uint64_t>(std::min<uint64_t>(want, k_), 65535);
+    const uint64_t rpc = (k_ + chunks - 1) / chunks;
+    col_absmax_kernel<<<dim3((unsigned)col_blocks, (unsigned)((k_ + rpc - 1) / rpc)), 256, 0, cols_st_>>>(
+        b + c0, k_, w, n_, rpc, bufs_->cmax.as<unsigned long long>() + c0);
     OZTT_CUDA(cudaGetLastError());
-    // the column sums continue from the previous chunk: kept in order on st
-    col_sumsq_kernel<<<(unsigned)((n_ + 127) / 128), 128, 0, st_>>>(b_chunk, rows, n_, 1.0, nullptr,
-                                                                    bufs_->s2c.as<double>(), row0 > 0 ? 1 : 0,
-                                                                    bufs_->tiny_b(), nullptr);
+    col_sumsq_kernel<<<(unsigned)((w + 127) / 128), 128, 0, cols_st_>>>(b + c0, k_, w, n_, 1.0, nullptr,
+                                                                       bufs_->s2c.as<double>() + c0, 0,
+                                                                       bufs_->tiny_b(), nullptr);
     OZTT_CUDA(cudaGetLastError());
-    // y_l = B g_l for these rows of B (the padded columns add exact zeros), unscaled
-    cudaStream_t x = next_side();
-    sketch_kernel<true><<<sketch_blocks(rows), kSketchThreads, 0, x>>>(b_chunk, rows, n_, n_, 1.0, nullptr,
-                                                                      bufs_->dg.as<double>(), N_, nullptr,
-                                                                      bufs_->ey.as<ext80::Ext>() + row0, k_, 0, nullptr);
+    // y_l = B g_l over these columns (the padded ones add exact zeros), unscaled, continuing the sums of
+    // the earlier columns
+    sketch_kernel<true><<<sketch_blocks(k_), kSketchThreads, 0, st_>>>(b + c0, k_, w, n_, 1.0, nullptr,
+                                                                      bufs_->dg.as<double>() + c0, N_, nullptr,
+                                                                      bufs_->ey.as<ext80::Ext>(), k_, c0 > 0 ? 1 : 0,
+                                                                      nullptr);
     OZTT_CUDA(cudaGetLastError());
 }
 
 void PolicyStatsRun::b_done(const double* b) {
-    join_sides();
+    OZTT_CUDA(cudaEventRecord(cols_done_, cols_st_));
+    OZTT_CUDA(cudaStreamWaitEvent(st_, cols_done_, 0));
     double* rgB = bufs_->rg.as<double>() + 1;
     const uint32_t* tiny = bufs_->tiny_b();
     pow2_scale_kernel<<<1, 1024, 0, st_>>>(bufs_->cmax.as<unsigned long long>(), n_, rgB);
@@ -390,8 +379,8 @@ void PolicyStatsRun::b_done(const double* b) {
         bufs_->ey.as<ext80::Ext>(), ny, rgB, tiny, bufs_->dy.as<double>());
     OZTT_CUDA(cudaGetLastError());
     // after a tiny element: B again, scale first
-    col_sumsq_kernel<<<(unsigned)((n_ + 127) / 128), 128, 0, st_>>>(b, k_, n_, 0.0, rgB, bufs_->s2c.as<double>(), 0,
-                                                                    nullptr, tiny);
+    col_sumsq_kernel<<<(unsigned)((n_ + 127) / 128), 128, 0, st_>>>(b, k_, n_, n_, 0.0, rgB, bufs_->s2c.as<double>(),
+                                                                    0, nullptr, tiny);
     OZTT_CUDA(cudaGetLastError());
     sketch_kernel<false><<<sketch_blocks(k_), kSketchThreads, 0, st_>>>(
         b, k_, n_, n_, 0.0, rgB, bufs_->dg.as<double>(), N_, bufs_->dy.as<double>(), nullptr, k_, 0, tiny);
@@ -417,7 +406,6 @@ void PolicyStatsRun::a_cols(const double* a, uint64_t c0, uint64_t c1) {
 }
 
 void PolicyStatsRun::a_done(const double* a) {
-    join_sides();
     double* rgA = bufs_->rg.as<double>();
     const uint32_t* tiny = bufs_->tiny_a();
     pow2_scale_kernel<<<1, 1024, 0, st_>>>(bufs_->rmax.as<unsigned long long>(), m_, rgA);
@@ -493,8 +481,8 @@ PolicyStats PolicyStatsRun::collect(std::vector<uint64_t>* row_max, std::vector<
 
 PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
                                 cudaStream_t st) {
-    PolicyStatsRun run(m, n, k, N, st, 0);
-    run.b_rows(b, 0, k);
+    PolicyStatsRun run(m, n, k, N, st);
+    run.b_cols(b, 0, n);
     run.b_done(b);
     run.a_cols(a, 0, k);
     run.a_done(a);
@@ -529,7 +517,7 @@ int oztt_stats_absmax(const double* x, uint64_t rows, uint64_t cols, int32_t mod
             const uint64_t chunks = std::min<uint64_t>(std::min<uint64_t>(want, rows), 65535);
             const uint64_t rpc = (rows + chunks - 1) / chunks;
             oztt::col_absmax_kernel<<<dim3((unsigned)col_blocks, (unsigned)((rows + rpc - 1) / rpc)), 256, 0, st>>>(
-                x, rows, cols, rpc, o);
+                x, rows, cols, cols, rpc, o);
         }
         OZTT_CUDA(cudaGetLastError());
     });
@@ -545,8 +533,8 @@ int oztt_stats_sumsq(const double* x, uint64_t rows, uint64_t cols, int32_t mode
             oztt::row_sumsq_kernel<<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(x, rows, cols, cols, rg, nullptr,
                                                                                   out, 0, nullptr, nullptr);
         else
-            oztt::col_sumsq_kernel<<<(unsigned)((cols + 127) / 128), 128, 0, st>>>(x, rows, cols, rg, nullptr, out, 0,
-                                                                                  nullptr, nullptr);
+            oztt::col_sumsq_kernel<<<(unsigned)((cols + 127) / 128), 128, 0, st>>>(x, rows, cols, cols, rg, nullptr,
+                                                                                  out, 0, nullptr, nullptr);
         OZTT_CUDA(cudaGetLastError());
     });
 }

@@ -3,7 +3,7 @@
 // Context::gemm from host buffers with the transfers overlapped (StreamedCall, runtime.cuh), shared by
 // the INT8 and digit-format Scheme II paths.
 //
-//   copy-up stream   B in 64 MiB chunks of rows, then A in blocks of columns (2-D copies of all rows)
+//   copy-up stream   B, then A, in blocks of columns of about 64 MiB (2-D copies of all rows)
 //   work stream      the precision-policy statistics of each piece as it lands (PolicyStatsRun), then
 //                    the caller's pipeline, which marks each finished band of rows of C
 //   copy-down stream each finished band of C read back while the next is computed
@@ -75,19 +75,20 @@ cudaEvent_t StreamedCall::order(cudaStream_t from, cudaStream_t to) {
 PolicyStats StreamedCall::upload(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max) {
     const uint64_t m = m_, n = n_, k = k_;
     const uint32_t N = (uint32_t)round_up(n, 64);  // the planners' padded width
-    stats_ = std::make_unique<PolicyStatsRun>(m, n, k, N, work_, 8);
+    stats_ = std::make_unique<PolicyStatsRun>(m, n, k, N, work_);
     order(work_, up_);  // the allocations before the first copy
     double* db = db_->as<double>();
     double* da = da_->as<double>();
-    const uint64_t rows_b = std::max<uint64_t>(1, kUploadChunkBytes / (8 * n));
-    for (uint64_t r0 = 0; r0 < k; r0 += rows_b) {
-        const uint64_t rows = std::min(rows_b, k - r0);
-        OZTT_CUDA(cudaMemcpyAsync(db + r0 * n, b_ + r0 * n, rows * n * 8, cudaMemcpyHostToDevice, up_));
+    // both operands in blocks of columns (2-D copies of all rows; blocks of at least 512 columns keep them
+    // at full speed), B first
+    const uint64_t cols_b = std::min<uint64_t>(n, std::max<uint64_t>(512, kUploadChunkBytes / (8 * k)));
+    for (uint64_t c0 = 0; c0 < n; c0 += cols_b) {
+        const uint64_t w = std::min(cols_b, n - c0);
+        OZTT_CUDA(cudaMemcpy2DAsync(db + c0, n * 8, b_ + c0, n * 8, w * 8, k, cudaMemcpyHostToDevice, up_));
         order(up_, work_);
-        stats_->b_rows(db + r0 * n, r0, rows);
+        stats_->b_cols(db, c0, c0 + w);
     }
     stats_->b_done(db);
-    // blocks of at least 512 columns keep the 2-D copies at full speed
     const uint64_t cols_a = std::min<uint64_t>(k, std::max<uint64_t>(512, kUploadChunkBytes / (8 * m)));
     cudaEvent_t uploaded = nullptr;
     for (uint64_t c0 = 0; c0 < k; c0 += cols_a) {

@@ -275,7 +275,7 @@ def test_context_matches_planned_run(oztt, oracle, cuda, fmt):
 
 @pytest.mark.parametrize("fmt", FORMATS)
 def test_context_streamed_bands(oztt, oracle, cuda, fmt):
-    """Context::gemm's streamed path with a digit format: B in two chunks of rows, A in three blocks of
+    """Context::gemm's streamed path with a digit format: B in two blocks of columns, A in three blocks of
     columns (the last one ragged), two row bands (the last one ragged), tiny elements in both operands (the
     statistics' scale-first recomputation); the bits of the stage pipeline run with the host plan."""
     m, n, k = 4500, 2048, 4608

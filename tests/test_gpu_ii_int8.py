@@ -304,10 +304,10 @@ def test_device_run_matches_host_run(oztt, oracle, cuda):
 
 
 # ---- Context.gemm's streamed path: chunked upload, statistics as chunks land, banded read-back ----------
-# Sizes: B in 64 MiB chunks of rows, A in blocks of max(512, 64 MiB / 8m) columns, row bands of about
+# Sizes: B and A in blocks of max(512, 64 MiB / 8k) and max(512, 64 MiB / 8m) columns, row bands of about
 # 2048 rows (up to 8). (9000, 256, 256): one piece each, 4 bands, a ragged last band; (4500, 4608, 2048):
-# B in two chunks, A in two column blocks (the last one ragged), 2 bands.
-# (3000, 2048, 4608): two chunks of B and two column blocks of A, with tiny elements (below 2^-383) in
+# B in two column blocks, A in two column blocks (the last ones ragged), 2 bands.
+# (3000, 2048, 4608): two column blocks of B and of A, with tiny elements (below 2^-383) in
 # both operands.
 @pytest.mark.parametrize("m,n,k,phi,seed", [(9000, 256, 256, 0.5, 31), (4500, 4608, 2048, 1.0, 32),
                                             (3000, 2048, 4608, 1.0, 33)])
