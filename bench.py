@@ -322,6 +322,29 @@ def run_scheme_i(args) -> None:
                                             "the diagonal GEMM runs inside steps of tens of ms, back to back",
                              "algorithmic": f"2*m*n*k*p(p+1)/2 = {gemm_ops:.4g} int8 ops per launch"},
                 "gpu_launches": 7 * args.steps, "clocks": clocks.summary()}
+        if args.e2e_steps > 0:
+            # the same request through the public API from pinned host buffers (the slice count selected
+            # on the device when not fixed)
+            ha = torch.from_numpy(a).pin_memory().numpy()
+            hb = torch.from_numpy(b).pin_memory().numpy()
+            hc = torch.empty(m * n, dtype=torch.float64).pin_memory().numpy()
+            ctx = oz.Context(oz.DeviceOptions(device_id=0))
+            opt = oz.Options(scheme=oz.Scheme.I, format=fmt, slices=req)
+            ctx.gemm(ha, hb, hc, m, n, k, opt)  # warm-up
+            times = []
+            for _ in range(args.e2e_steps):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                ctx.gemm(ha, hb, hc, m, n, k, opt)
+                times.append(time.perf_counter() - t0)
+            e2e_s = statistics.median(times)
+            phases = oz.ii_int8_last_phases()
+            line["e2e"] = {"value": 2.0 * m * n * k / e2e_s / 1e12, "unit": "TFLOPS", "s_per_step": e2e_s,
+                           "h2d_bytes_per_step": 8 * (m * k + k * n), "d2h_bytes_per_step": 8 * m * n,
+                           "phases_ms_last_call": {key: round(v, 2) if isinstance(v, float) else v
+                                                   for key, v in phases.items()},
+                           "path": "ozTTgemm::Context::gemm via oztt_gemm"}
+            del ha, hb, hc
         print(json.dumps(line), flush=True)
 
 

@@ -9,8 +9,8 @@
 //   * one process-wide mutex serialises the calls of all contexts (:19, :152);
 //   * the device is opened on the first valid call; Info reports the padded dimensions (:176-180);
 //   * all input is consumed before C is written, so C may overlap A or B.
-// For Scheme II the finiteness and range checks are made from the device-measured row and column maxima
-// once A and B are uploaded, before the plan is made and C is written.
+// The finiteness and range checks are made from the device-measured row and column maxima once A and B
+// are uploaded, before the plan is made and C is written.
 // Under an evaluation Scope (include/evaluation_hooks.hpp, the reference's src/evaluation_hooks.hpp) a
 // call runs its device pipeline through the evaluator's phase timing and whole-pass check, with the
 // Ozaki II width the Scope fixes (src/ozaki2.cpp:447).
@@ -132,12 +132,12 @@ struct Checked {
     std::uint32_t mp, np, kp;
     std::size_t c_size;
 };
-// An ordinary Scheme II call (any format) makes the value checks from the row and column maxima that
-// the device measures for the precision policy (the same magnitude patterns, so the same reports in the
-// same order), before the plan and before C is written; should the device fail before that, the host
-// checks run after all, so that an invalid input is still the error reported. Scheme I and profiled
-// calls run the host checks here, before the device is touched.
-bool checks_during_upload(const Options& o) { return o.scheme == Scheme::II && ev::active == nullptr; }
+// An ordinary call (either scheme, any format) makes the value checks from the row and column maxima
+// that the device measures for the plan statistics (the same magnitude patterns, so the same reports in
+// the same order), before the plan and before C is written; should the device or a fixed-slice plan fail
+// before that, the host checks run after all, so that an invalid input is still the error reported.
+// Profiled calls (an evaluation Scope) run the host checks here, before the device is touched.
+bool checks_during_upload(const Options&) { return ev::active == nullptr; }
 
 Checked validate(const Options& options, std::span<const double> a, std::span<const double> b,
                  std::optional<std::size_t> c_size, std::size_t m, std::size_t n, std::size_t k) {
@@ -212,8 +212,8 @@ Context::~Context() = default;
 Info Context::Impl::execute(std::span<const double> a, std::span<const double> b, std::span<double> c, std::size_t m,
                             std::size_t n, std::size_t k, const Options& opt, const Checked& v) {
     std::lock_guard lock(runtime_mutex);
-    // The value checks of an ordinary Scheme II call are made from the maxima the device measures while
-    // A and B are uploaded; should the device fail first, the host checks run after all.
+    // The value checks of an ordinary call are made from the maxima the device measures while A and B are
+    // uploaded; should the device (or a fixed-slice plan) fail first, the host checks run after all.
     bool checked = false;
     const auto check_maxima = [&](const std::uint64_t* row_max, const std::uint64_t* col_max) {
         checked = true;
@@ -241,14 +241,19 @@ Info Context::Impl::execute(std::span<const double> a, std::span<const double> b
         const oztt::I1Format& fmt = *oztt::i1_format((int32_t)opt.format);
         oztt_i_plan plan;
         std::string msg;
-        if (opt.slices) {  // a fixed slice count: the feasibility checks before any device work, as the reference
+        if (opt.slices) {
+            // a fixed slice count: the feasibility checks before any device work, as the reference (an invalid
+            // value is still the error reported first)
             const int rc = oztt::plan_i(a.data(), b.data(), m, n, k, opt.slices, fmt, plan, msg);
-            if (rc != OZTT_OK) rethrow(rc, msg);
+            if (rc != OZTT_OK) fail(rc, msg);
         }
-        // one upload; the slice count (when not fixed) selected from statistics measured on the device
-        const int rc = oztt::run_i_uploaded(options.device_id, a.data(), b.data(), c.data(), m, n, k, opt.slices, fmt,
-                                            plan, msg);
-        if (rc != OZTT_OK) rethrow(rc, msg);
+        // the slice count (when not fixed) selected from statistics measured on the device: during the
+        // streamed upload, or after one plain upload under an evaluation Scope
+        const int rc = ev::active ? oztt::run_i_uploaded(options.device_id, a.data(), b.data(), c.data(), m, n, k,
+                                                         opt.slices, fmt, plan, msg)
+                                  : oztt::run_i_streamed(options.device_id, (int32_t)opt.format, a.data(), b.data(),
+                                                         c.data(), m, n, k, opt.slices, check_maxima, plan, msg);
+        if (rc != OZTT_OK) fail(rc, msg);
         opened = true;
         Info info{Scheme::I, opt.format};
         info.slices = (std::uint32_t)plan.p;

@@ -861,11 +861,14 @@ void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64
 // Scheme I diagonal products P_d = sum_{i=0..d} A_i B_{d-i}^T, d = 0..p-1, int32 [p][mp][np], from
 // slice planes A [p][mp][kp] and B [p][np][kp] (tcgen05 kind::i8, s32 accumulation over the
 // concatenated K of (d+1)*kp).
+// a_plane_rows: when nonzero, ap points at row r0 of A slice planes that are a_plane_rows tall, and the
+// GEMM covers the band of mp rows from there (diagonals [p][mp][np] of the band).
 void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp, int p,
-                      int32_t* out, int* err_word, cudaStream_t st) {
+                      int32_t* out, int* err_word, cudaStream_t st, uint64_t a_plane_rows) {
     using namespace gemm;
     if (mp % BM || np % BN || kp % BK || mp == 0 || np == 0 || kp == 0)
         throw Error(OZTT_EINVAL, "diag_gemm: mp, np, kp must be positive multiples of 128, 256 and 128");
+    if (a_plane_rows && a_plane_rows < mp) throw Error(OZTT_EINVAL, "diag_gemm: band taller than its planes");
     if (p < 1 || p > 64) throw Error(OZTT_EINVAL, "diag_gemm: the number of slices must be 1..64");
     if ((reinterpret_cast<uintptr_t>(ap) | reinterpret_cast<uintptr_t>(bp)) & 15)
         throw Error(OZTT_EINVAL, "diag_gemm: planes must be 16-byte aligned");
@@ -874,7 +877,7 @@ void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t 
     EpiConst ec{};
     ec.S = (uint32_t)p;
     const bool pairs = use_pairs();
-    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p, pairs ? pair::BM : BM);
+    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p, pairs ? pair::BM : BM, a_plane_rows);
     const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p, pairs ? pair::BNH : BN);
     launch_gemm<2>(ta, tb, out, mp, np, kp, (uint32_t)p, ec, err_word, st);
 }

@@ -12,8 +12,8 @@
 // combining the terms, picking the sample, the rounding simulation, the search). The result is
 // bit-identical to the host planner's.
 //
-// terms_kernel runs one thread per column c of A (rows in ascending order) and per row r of B (columns in
-// ascending order), as the host sums them, in one launch. Each element x (scaled by 2^(nshift - e) of its row or column)
+// terms_kernel sums per column c of A (rows in ascending order) and per row r of B (columns in ascending
+// order), as the host sums them, both operands in one launch. Each element x (scaled by 2^(nshift - e) of its row or column)
 // is expanded as the reference's device slicer does -- u = radix t (FMA-exact product, TwoSum), digit
 // d = clamp(rint(fl32(u_hi)), +-dmax), t = u - d in two doubles -- until its residual is zero, adding
 // (s d w)^2 to S[i] and (s t w)^2 to R[i+1] with w = radix^-(i+1) formed by repeated division. Every
@@ -36,6 +36,20 @@ __device__ __forceinline__ void two_sum_d(double a, double b, double& s, double&
     e = __dadd_rn(__dsub_rn(a, __dsub_rn(s, bb)), __dsub_rn(b, bb));
 }
 
+// w_i = radix^-(i+1) formed by repeated division, w_0 = 1/radix, w_(i+1) = w_i / radix, exactly as the
+// host planner forms it in its loops; passed to the kernels by value.
+constexpr int kMaxSteps = 40;
+struct Weights {
+    double w[kMaxSteps];
+};
+
+Weights weights_of(double radix) {
+    Weights t;
+    double x = 1.0;
+    for (int i = 0; i < kMaxSteps; ++i) t.w[i] = x = x / radix;
+    return t;
+}
+
 // 2^e for |e| <= 1022.
 __device__ __forceinline__ double pow2d(int e) { return __longlong_as_double((long long)(1023 + e) << 52); }
 
@@ -50,104 +64,132 @@ __device__ __forceinline__ double expand_step(double& th, double& tl, double rad
     return dg;
 }
 
-// The sums of one side (A or B) of model (1).
+// The sums of one side (A or B) of model (1): `chains` sequential sums (a column of A over its rows, a row
+// of B over its columns) of `len` elements each; element e of chain q sits at x + q*chain_stride +
+// e*elem_stride.
 struct TermsSide {
-    const double* x;                 // thread t walks len elements from x + t*thread_stride, elem_stride apart
-    uint64_t len, thread_stride, elem_stride;
-    const double* s;                 // divisor of element e's row of A (column of B); 0: not counted
-    const int32_t* sh;               // its exponent shift nshift - e
+    const double* x;
+    uint64_t chains, len, chain_stride, elem_stride;
+    const double* s;    // divisor of element e's row of A (column of B); 0: not counted
+    const int32_t* sh;  // its exponent shift nshift - e
     double rg;
-    double *S, *R, *N;               // S[i][t], R[q][t], N[t]
+    double *S, *R, *N;  // S[i][q], R[r][q], N[q]
 };
 
-// Thread t of side A (blocks below a_blocks) or B: the element chains of kLanes consecutive elements
-// advance together, and at each step their contributions join the sums in element order, so every sum
-// receives its terms in the host's order while the chains overlap. A lane whose residual is exactly zero
-// adds +0 from then on (the sums are never -0, so +0 changes nothing), as the host stops adding.
-constexpr int kLanes = 4;
+// A block owns kChains adjacent chains. It takes their elements kSpan at a time: every thread expands one
+// element (the expansions are independent of one another and of the sums) and leaves its per-step
+// contributions in shared memory, then the owners of the sums -- one thread per (chain, sum) -- add the
+// kSpan contributions in element order, so each sum receives its terms in the host's order. A step after
+// an element's residual reached exactly zero contributes +0, which leaves a sum unchanged (the sums are
+// never -0), as the host adds nothing. For A (element stride = a row) the kChains adjacent columns make a
+// warp's loads cover whole 32-byte sectors; for B (element stride 1) a warp reads kSpan consecutive
+// elements of one row.
+constexpr int kChains = 4, kSpan = 32, kTermsThreads = kChains * kSpan;
 
 template <int PMAX>
-__global__ void __launch_bounds__(64) terms_kernel(TermsSide A, TermsSide B, uint64_t threads, uint32_t a_blocks,
-                                                   double radix, double dmax) {
+__global__ void __launch_bounds__(kTermsThreads) terms_kernel(TermsSide A, TermsSide B, uint32_t a_blocks,
+                                                              double radix, double dmax, const Weights wt) {
+    extern __shared__ double contrib[];  // [2 PMAX + 1][kTermsThreads]: S steps, R steps 1..PMAX, N
+    constexpr int NS = 2 * PMAX + 1;
     const bool side_b = blockIdx.x >= a_blocks;
     const TermsSide& sd = side_b ? B : A;
-    const uint64_t t = (uint64_t)(blockIdx.x - (side_b ? a_blocks : 0)) * blockDim.x + threadIdx.x;
-    if (t >= threads) return;
-    double S[PMAX], R[PMAX + 1];
+    const uint64_t q0 = (uint64_t)(blockIdx.x - (side_b ? a_blocks : 0)) * kChains;
+    const int t = threadIdx.x;
+    // the element slot of this thread: chain fastest for A (adjacent columns), element fastest for B
+    const int cq = side_b ? t / kSpan : t % kChains, ce = side_b ? t % kSpan : t / kChains;
+    const uint64_t q = q0 + cq;
+    // the sums this thread owns: indices t, t + 128, ... of [kChains][NS]
+    double acc[(kChains * NS + kTermsThreads - 1) / kTermsThreads];
 #pragma unroll
-    for (int i = 0; i < PMAX; ++i) S[i] = 0.0;
-#pragma unroll
-    for (int i = 0; i <= PMAX; ++i) R[i] = 0.0;
-    double nrm = 0.0;
-    const double* p = sd.x + t * sd.thread_stride;
-    for (uint64_t e0 = 0; e0 < sd.len; e0 += kLanes) {
-        double th[kLanes], tl[kLanes], sc[kLanes];
-        bool live[kLanes];
-#pragma unroll
-        for (int l = 0; l < kLanes; ++l) {
-            const uint64_t e = e0 + l;
-            th[l] = tl[l] = sc[l] = 0.0;
-            live[l] = false;
-            if (e < sd.len) {
-                const double v = __ldg(p + e * sd.elem_stride);
-                const double vr = __dmul_rn(v, sd.rg);
-                nrm = __dadd_rn(nrm, __dmul_rn(vr, vr));
-                const double se = __ldg(sd.s + e);
-                if (v != 0.0 && se > 0.0) {
-                    live[l] = true;
-                    th[l] = __dmul_rn(v, pow2d(__ldg(sd.sh + e)));
-                    sc[l] = se;
-                }
+    for (int j = 0; j < (kChains * NS + kTermsThreads - 1) / kTermsThreads; ++j) acc[j] = 0.0;
+    for (uint64_t e0 = 0; e0 < sd.len; e0 += kSpan) {
+        // expand this thread's element
+        double* col = contrib + t;  // contrib[i * kTermsThreads + t]
+        const uint64_t e = e0 + ce;
+        double th = 0.0, tl = 0.0, sc = 0.0, vr2 = 0.0;
+        bool live = false;
+        if (q < sd.chains && e < sd.len) {
+            const double v = __ldg(sd.x + q * sd.chain_stride + e * sd.elem_stride);
+            const double vr = __dmul_rn(v, sd.rg);
+            vr2 = __dmul_rn(vr, vr);
+            const double se = __ldg(sd.s + e);
+            if (v != 0.0 && se > 0.0) {
+                live = true;
+                th = __dmul_rn(v, pow2d(__ldg(sd.sh + e)));
+                sc = se;
             }
         }
-        double w = 1.0;
-#pragma unroll
+#pragma unroll 1
         for (int i = 0; i < PMAX; ++i) {
-            bool any = false;
-#pragma unroll
-            for (int l = 0; l < kLanes; ++l) any |= live[l];
-            if (!any) break;
-            w = __ddiv_rn(w, radix);
-            double cs[kLanes], cr[kLanes];
-#pragma unroll
-            for (int l = 0; l < kLanes; ++l) {
-                cs[l] = cr[l] = 0.0;
-                if (live[l]) {
-                    const double dg = expand_step(th[l], tl[l], radix, dmax);
-                    const double c = __dmul_rn(__dmul_rn(sc[l], dg), w);
-                    cs[l] = __dmul_rn(c, c);
-                    const double r = __dmul_rn(__dmul_rn(sc[l], __dadd_rn(th[l], tl[l])), w);
-                    cr[l] = __dmul_rn(r, r);
-                    live[l] = th[l] != 0.0;
-                }
+            double cs = 0.0, cr = 0.0;
+            if (live) {
+                const double w = wt.w[i];
+                const double dg = expand_step(th, tl, radix, dmax);
+                const double c = __dmul_rn(__dmul_rn(sc, dg), w);
+                cs = __dmul_rn(c, c);
+                const double r = __dmul_rn(__dmul_rn(sc, __dadd_rn(th, tl)), w);
+                cr = __dmul_rn(r, r);
+                live = th != 0.0;
             }
+            col[i * kTermsThreads] = cs;
+            col[(PMAX + i) * kTermsThreads] = cr;
+        }
+        col[2 * PMAX * kTermsThreads] = vr2;
+        __syncthreads();
+        // add the kSpan contributions of each owned sum in element order
+        const int n_el = sd.len - e0 < (uint64_t)kSpan ? (int)(sd.len - e0) : kSpan;
 #pragma unroll
-            for (int l = 0; l < kLanes; ++l) {
-                S[i] = __dadd_rn(S[i], cs[l]);
-                R[i + 1] = __dadd_rn(R[i + 1], cr[l]);
+        for (int j = 0; j < (kChains * NS + kTermsThreads - 1) / kTermsThreads; ++j) {
+            const int idx = t + j * kTermsThreads;
+            if (idx < kChains * NS) {
+                const int oq = idx / NS, oi = idx % NS;
+                const double* src = contrib + oi * kTermsThreads;
+                double a = acc[j];
+                for (int el = 0; el < n_el; ++el) {
+                    const int slot = side_b ? oq * kSpan + el : el * kChains + oq;
+                    a = __dadd_rn(a, src[slot]);
+                }
+                acc[j] = a;
+            }
+        }
+        __syncthreads();
+    }
+    // S[i][q] (i < PMAX), R[i + 1][q], N[q]; R[0][q] = 0
+#pragma unroll
+    for (int j = 0; j < (kChains * NS + kTermsThreads - 1) / kTermsThreads; ++j) {
+        const int idx = t + j * kTermsThreads;
+        if (idx < kChains * NS) {
+            const int oq = idx / NS, oi = idx % NS;
+            const uint64_t qq = q0 + oq;
+            if (qq < sd.chains) {
+                if (oi < PMAX)
+                    sd.S[(uint64_t)oi * sd.chains + qq] = acc[j];
+                else if (oi < 2 * PMAX)
+                    sd.R[(uint64_t)(oi - PMAX + 1) * sd.chains + qq] = acc[j];
+                else
+                    sd.N[qq] = acc[j];
             }
         }
     }
-#pragma unroll
-    for (int i = 0; i < PMAX; ++i) sd.S[(uint64_t)i * threads + t] = S[i];
-#pragma unroll
-    for (int i = 0; i <= PMAX; ++i) sd.R[(uint64_t)i * threads + t] = R[i];
-    sd.N[t] = nrm;
+    if (t < kChains && q0 + t < sd.chains) sd.R[q0 + t] = 0.0;
 }
 
 template <int PMAX>
-void launch_terms(const TermsSide& A, const TermsSide& B, uint64_t threads, const I1Format& f, cudaStream_t st) {
-    const uint32_t blocks = (uint32_t)((threads + 63) / 64);
-    terms_kernel<PMAX><<<2 * blocks, 64, 0, st>>>(A, B, threads, blocks, f.radix, f.dmax);
+void launch_terms(const TermsSide& A, const TermsSide& B, const I1Format& f, cudaStream_t st) {
+    const uint32_t a_blocks = (uint32_t)((A.chains + kChains - 1) / kChains);
+    const uint32_t b_blocks = (uint32_t)((B.chains + kChains - 1) / kChains);
+    const size_t smem = (size_t)(2 * PMAX + 1) * kTermsThreads * sizeof(double);
+    OZTT_CUDA(cudaFuncSetAttribute(terms_kernel<PMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    terms_kernel<PMAX><<<a_blocks + b_blocks, kTermsThreads, smem, st>>>(A, B, a_blocks, f.radix, f.dmax,
+                                                                        weights_of(f.radix));
     OZTT_CUDA(cudaGetLastError());
 }
 
-void launch_terms_any(int pmax, const TermsSide& A, const TermsSide& B, uint64_t threads, const I1Format& f,
-                      cudaStream_t st) {
+void launch_terms_any(int pmax, const TermsSide& A, const TermsSide& B, const I1Format& f, cudaStream_t st) {
     switch (pmax) {
-    case 22: launch_terms<22>(A, B, threads, f, st); break;
-    case 28: launch_terms<28>(A, B, threads, f, st); break;
-    case 33: launch_terms<33>(A, B, threads, f, st); break;
+    case 22: launch_terms<22>(A, B, f, st); break;
+    case 28: launch_terms<28>(A, B, f, st); break;
+    case 33: launch_terms<33>(A, B, f, st); break;
     default: throw Error(OZTT_EINVAL, "scheme I: no device slice-selection kernel for this radix");
     }
 }
@@ -200,7 +242,8 @@ __global__ void __launch_bounds__(128) sample_err_kernel(const double* __restric
                                                          uint32_t na, uint32_t nb, uint64_t k, uint64_t K,
                                                          const int32_t* __restrict__ shx,
                                                          const int32_t* __restrict__ shy, int q, double radix,
-                                                         double dmax, double* __restrict__ part) {
+                                                         double dmax, const Weights wt,
+                                                         double* __restrict__ part) {
     const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t pairs = (uint64_t)na * nb;
     if (t >= pairs * kI1Chunks) return;
@@ -210,26 +253,23 @@ __global__ void __launch_bounds__(128) sample_err_kernel(const double* __restric
     double acc = 0.0;
     for (uint64_t c = k0; c < k1; ++c) {
         double D[PMAX], RY[PMAX + 1];
-        double th = __dmul_rn(__ldg(XA + s * k + c), px), tl = 0.0, w = 1.0;
+        double th = __dmul_rn(__ldg(XA + s * k + c), px), tl = 0.0;
 #pragma unroll
         for (int i = 0; i < PMAX; ++i) {
             if (i < q) {
                 const double dg = expand_step(th, tl, radix, dmax);
-                w = __ddiv_rn(w, radix);
-                D[i] = __dmul_rn(dg, w);
+                D[i] = __dmul_rn(dg, wt.w[i]);
             }
         }
-        const double rx = __dmul_rn(__dadd_rn(th, tl), w);
+        const double rx = __dmul_rn(__dadd_rn(th, tl), wt.w[q - 1]);
         const double yk = __dmul_rn(__ldg(YB + u * k + c), py);
         th = yk;
         tl = 0.0;
-        w = 1.0;
 #pragma unroll
         for (int r = 1; r <= PMAX; ++r) {
             if (r <= q) {
                 (void)expand_step(th, tl, radix, dmax);
-                w = __ddiv_rn(w, radix);
-                RY[r] = __dmul_rn(__dadd_rn(th, tl), w);
+                RY[r] = __dmul_rn(__dadd_rn(th, tl), wt.w[r - 1]);
             }
         }
         double e = __dmul_rn(rx, yk);
@@ -247,7 +287,8 @@ void launch_sample_err(const double* XA, const double* YB, uint32_t na, uint32_t
                        cudaStream_t st) {
     const uint64_t threads = (uint64_t)na * nb * kI1Chunks;
     sample_err_kernel<PMAX><<<(unsigned)((threads + 127) / 128), 128, 0, st>>>(XA, YB, na, nb, k, K, shx, shy, q,
-                                                                               f.radix, f.dmax, part);
+                                                                               f.radix, f.dmax, weights_of(f.radix),
+                                                                               part);
     OZTT_CUDA(cudaGetLastError());
 }
 
@@ -321,12 +362,13 @@ private:
     double norm2_ = 0;
 };
 
+I1Terms measure_i1_terms(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                         const I1Normalization& nm, const I1Format& f, cudaStream_t st);
+
 // The normalization and model (1)'s terms of device-resident a (m x k) and b (k x n), with nC; the stream
 // is synchronised.
 void measure_i1_device(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
                        const I1Format& f, cudaStream_t st, I1Normalization& nm, I1Terms& terms, double& nC) {
-    const int pmax = i1_pmax(f);
-    const uint64_t P1 = (uint64_t)pmax + 1;
     std::vector<uint64_t> row_max, col_max;
     std::vector<double> nrA, nrB;
     double rg[2] = {1.0, 1.0};
@@ -339,6 +381,15 @@ void measure_i1_device(const double* a, const double* b, uint64_t m, uint64_t n,
         nC = run.collect(&row_max, &col_max, &nrA, &nrB, rg).nC;
     }
     nm = i1_normalization(rg[0], rg[1], row_max.data(), col_max.data(), nrA.data(), nrB.data(), m, n, f);
+    terms = measure_i1_terms(a, b, m, n, k, nm, f, st);
+}
+
+// Model (1)'s per-k sums of device-resident a, b with a given normalization; the stream is synchronised.
+I1Terms measure_i1_terms(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,
+                         const I1Normalization& nm, const I1Format& f, cudaStream_t st) {
+    const int pmax = i1_pmax(f);
+    const uint64_t P1 = (uint64_t)pmax + 1;
+    I1Terms terms;
     // per row of A / column of B: the divisor and the shift nshift - e (0 where the row is not counted)
     std::vector<int32_t> shA(m, 0), shB(n, 0);
     for (uint64_t i = 0; i < m; ++i)
@@ -355,11 +406,11 @@ void measure_i1_device(const double* a, const double* b, uint64_t m, uint64_t n,
     OZTT_CUDA(cudaMemsetAsync(SA.p, 0, P1 * k * 8, st));  // row pmax of S stays zero
     OZTT_CUDA(cudaMemsetAsync(SB.p, 0, P1 * k * 8, st));
     // A: thread c walks rows i (elements i*k + c); B: thread r walks columns j (elements r*n + j); one launch
-    const TermsSide sa{a, m, 1, k, dsA.as<double>(), dshA.as<int32_t>(), nm.rgA, SA.as<double>(), RA.as<double>(),
+    const TermsSide sa{a, k, m, 1, k, dsA.as<double>(), dshA.as<int32_t>(), nm.rgA, SA.as<double>(), RA.as<double>(),
                        NA.as<double>()};
-    const TermsSide sb{b, n, n, 1, dsB.as<double>(), dshB.as<int32_t>(), nm.rgB, SB.as<double>(), RB.as<double>(),
+    const TermsSide sb{b, k, n, n, 1, dsB.as<double>(), dshB.as<int32_t>(), nm.rgB, SB.as<double>(), RB.as<double>(),
                        NB.as<double>()};
-    launch_terms_any(pmax, sa, sb, k, f, st);
+    launch_terms_any(pmax, sa, sb, f, st);
     terms.SA.resize(P1 * k);
     terms.RA.resize(P1 * k);
     terms.SB.resize(P1 * k);
@@ -373,6 +424,21 @@ void measure_i1_device(const double* a, const double* b, uint64_t m, uint64_t n,
     OZTT_CUDA(cudaMemcpyAsync(terms.NA.data(), NA.p, k * 8, cudaMemcpyDeviceToHost, st));
     OZTT_CUDA(cudaMemcpyAsync(terms.NB.data(), NB.p, k * 8, cudaMemcpyDeviceToHost, st));
     OZTT_CUDA(cudaStreamSynchronize(st));
+    return terms;
+}
+
+// The same with the normalization and nC already measured (the streamed upload measures them on the way).
+int plan_i_measured(const double* a_dev, const double* b_dev, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
+                    const I1Format& f, const I1Normalization& nm, double nC, oztt_i_plan& p, std::string& err,
+                    cudaStream_t st) {
+    return plan_i_with(
+        [&](uint32_t M, uint32_t N, uint32_t K) {
+            (void)N;
+            const I1Terms terms = measure_i1_terms(a_dev, b_dev, m, n, k, nm, f, st);
+            DeviceSample sample(a_dev, b_dev, m, n, k, K, f, nm, nC, st);
+            return i1_select_with(terms, m, n, k, M, N, K, f, nC, [&](int q) { return sample.err2(q); });
+        },
+        m, n, k, slices, f, p, err);
 }
 
 // The Scheme I plan with the slice count selected from statistics measured on the device (a_dev, b_dev),

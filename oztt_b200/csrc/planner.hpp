@@ -152,8 +152,15 @@ int select_slices(const double* a, const double* b, uint64_t m, uint64_t n, uint
                   uint32_t K, const I1Format& f);
 int plan_i(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t slices, const I1Format& f,
            oztt_i_plan& p, std::string& err);
-// Context::gemm's Scheme I call (plan1_dev.cu): one upload, the slice count from statistics measured on
-// the device, the pipeline on the resident operands.
+// Context::gemm's Scheme I call from host buffers with the transfers overlapped (scheme1.cu): the streamed
+// upload with the statistics, check(row_max, col_max) as for Scheme II, the slice count (slices 0) from
+// the measured statistics, the banded pipeline with the read-back overlapped.
+int run_i_streamed(int device_id, int32_t format, const double* a, const double* b, double* c, uint64_t m,
+                   uint64_t n, uint64_t k, uint32_t slices,
+                   const std::function<void(const uint64_t*, const uint64_t*)>& check, oztt_i_plan& plan,
+                   std::string& err);
+// Context::gemm's Scheme I call under an evaluation Scope (plan1_dev.cu): one upload, the slice count from
+// statistics measured on the device, the pipeline on the resident operands.
 int run_i_uploaded(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
                    uint32_t slices, const I1Format& f, oztt_i_plan& p, std::string& err);
 // The same with the slice count from select(M, N, K) when slices is 0 (e.g. measured on the device).

@@ -126,8 +126,11 @@ public:
     StreamedCall(int device_id, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k);
     ~StreamedCall();
     // B, then A, in blocks of columns, with the statistics measured as they land;
-    // returns them, with the magnitude patterns of A's row maxima and B's column maxima.
-    PolicyStats upload(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max);
+    // returns them, with the magnitude patterns of A's row maxima and B's column maxima (and, when asked,
+    // the scaled squared norms of A's rows and B's columns and the two scales).
+    PolicyStats upload(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max,
+                       std::vector<double>* row_sumsq = nullptr, std::vector<double>* col_sumsq = nullptr,
+                       double* rg = nullptr);
     const double* a_dev() const { return da_->as<double>(); }
     const double* b_dev() const { return db_->as<double>(); }
     double* c_dev();

@@ -25,6 +25,9 @@
 //                assembles in a 64-bit window (assemble_tf_f64); the B200 result is within that
 //                error of the reference's.
 #include <algorithm>
+#include <functional>
+#include <string>
+#include <vector>
 
 #include "oztt_common.cuh"
 
@@ -430,7 +433,7 @@ void launch_scale_cols_mode(const double* b, uint64_t k, uint64_t n, uint64_t ld
                             int32_t* delta, uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax,
                             cudaStream_t st);
 void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp, int p,
-                      int32_t* out, int* err_word, cudaStream_t st);
+                      int32_t* out, int* err_word, cudaStream_t st, uint64_t a_plane_rows = 0);
 
 void run_i_device(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
                   const oztt_i_plan& plan, cudaStream_t st, double* stage_ms) {
@@ -604,3 +607,95 @@ int oztt_i_recon(const int32_t* diag, uint64_t mp, uint64_t np, const int32_t* d
 }
 
 }  // extern "C"
+
+// ---- Context::gemm's Scheme I call from host buffers, transfers overlapped ---------------------------
+namespace oztt {
+
+int plan_i_measured(const double* a_dev, const double* b_dev, uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
+                    const I1Format& f, const I1Normalization& nm, double nC, oztt_i_plan& p, std::string& err,
+                    cudaStream_t st);
+
+// The upload with the statistics measured on the way (StreamedCall), the caller's value checks from the
+// measured maxima, the slice count (when not fixed) selected from those statistics and the device's model
+// sums, then scale and slice, and the diagonal GEMM and the Horner evaluation in bands of about 2048 rows
+// (up to 8), each band of C read back while the next is computed.
+static int run_i_streamed_impl(int device_id, int32_t format, const double* a, const double* b, double* c,
+                               uint64_t m, uint64_t n, uint64_t k, uint32_t slices,
+                               const std::function<void(const uint64_t*, const uint64_t*)>& check, oztt_i_plan& plan,
+                               std::string& err) {
+    const I1Format* fp = i1_format(format);
+    if (!fp) throw Error(OZTT_EINVAL, "format is unknown or was not built");
+    const I1Format& fmt = *fp;
+    StreamedCall call(device_id, a, b, m, n, k);
+    StreamedPhases& ph = call.phases();
+    cudaStream_t st = call.work();
+    std::vector<uint64_t> row_max, col_max;
+    std::vector<double> nrA, nrB;
+    double rg[2] = {1.0, 1.0};
+    const PolicyStats ps = call.upload(row_max, col_max, &nrA, &nrB, rg);
+    double t = call.ms_since_start();
+    check(row_max.data(), col_max.data());
+    ph.check_ms = call.ms_since_start() - t;
+    t = call.ms_since_start();
+    const I1Normalization nm =
+        i1_normalization(rg[0], rg[1], row_max.data(), col_max.data(), nrA.data(), nrB.data(), m, n, fmt);
+    const int rc = plan_i_measured(call.a_dev(), call.b_dev(), m, n, k, slices, fmt, nm, ps.nC, plan, err, st);
+    if (rc != OZTT_OK) return rc;
+    ph.plan_ms = call.ms_since_start() - t;
+    t = call.ms_since_start();
+    const int p = plan.p;
+    const I1Dev f = i1_dev(format);
+    if (p < 1 || p > f.pmax)
+        throw Error(OZTT_EINVAL, "scheme I: the number of slices must be 1.." + std::to_string(f.pmax) +
+                                     " for radix " + std::to_string(f.radix));
+    const uint64_t d2 = (uint64_t)f.dmax * (uint64_t)f.dmax;
+    if ((uint64_t)p * round_up(k, 32) > (uint64_t)INT32_MAX / d2)
+        throw Error(OZTT_ERUNTIME, "Ozaki scheme I: k*slices is too large for exact 32-bit diagonal sums in this "
+                                   "build (k=" + std::to_string(k) + ", " + std::to_string(p) + " slices)");
+    const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128), P = (uint64_t)p;
+    const uint64_t bands = std::min<uint64_t>(8, std::max<uint64_t>(1, mp / 2048));
+    const uint64_t bm = round_up((mp + bands - 1) / bands, 128);
+    const double *da = call.a_dev(), *db = call.b_dev();
+    double* dc = call.c_dev();
+    DevBuf dA(st, mp * 4), dB(st, np * 4), colmax(st, n * 8), words(st, 16);
+    DevBuf sa(st, P * mp * kp), sb(st, P * np * kp), pd(st, P * bm * np * 4);
+    OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
+    uint32_t* flags = words.as<uint32_t>();
+    int* gemm_err = words.as<int>() + 1;
+    launch_scale_rows_mode(da, m, k, k, -1, f.ceil, dA.as<int32_t>(), nullptr, flags, st);
+    launch_scale_cols_mode(db, k, n, n, -1, f.ceil, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(),
+                           st);
+    launch_slice_rows(da, m, k, k, dA.as<int32_t>(), p, format, sa.as<int8_t>(), mp, kp, st);
+    launch_slice_cols(db, k, n, n, dB.as<int32_t>(), p, format, sb.as<int8_t>(), np, kp, st);
+    for (uint64_t r0 = 0; r0 < mp; r0 += bm) {
+        const uint64_t rows_p = std::min(bm, mp - r0);
+        launch_diag_gemm(sa.as<int8_t>() + r0 * kp, sb.as<int8_t>(), rows_p, np, kp, p, pd.as<int32_t>(), gemm_err,
+                         st, mp);
+        if (r0 >= m) continue;
+        const uint64_t rows = std::min(m, r0 + rows_p) - r0;
+        launch_horner(pd.as<int32_t>(), rows_p, np, dA.as<int32_t>() + r0, dB.as<int32_t>(), p, format, dc + r0 * n,
+                      rows, n, n, st);
+        call.band_done(r0, rows);
+    }
+    call.read_back(c);
+    uint32_t host_words[2] = {0, 0};
+    OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
+    call.finish(t);
+    check_flags(host_words[0], (int)host_words[1]);
+    return OZTT_OK;
+}
+
+int run_i_streamed(int device_id, int32_t format, const double* a, const double* b, double* c, uint64_t m,
+                   uint64_t n, uint64_t k, uint32_t slices,
+                   const std::function<void(const uint64_t*, const uint64_t*)>& check, oztt_i_plan& plan,
+                   std::string& err) {
+    char buf[1024];
+    int inner = OZTT_OK;
+    const int rc = guarded(buf, sizeof buf, [&] {
+        inner = run_i_streamed_impl(device_id, format, a, b, c, m, n, k, slices, check, plan, err);
+    });
+    if (rc != OZTT_OK) err = buf;
+    return rc != OZTT_OK ? rc : inner;
+}
+
+}  // namespace oztt

@@ -72,7 +72,8 @@ cudaEvent_t StreamedCall::order(cudaStream_t from, cudaStream_t to) {
     return e;
 }
 
-PolicyStats StreamedCall::upload(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max) {
+PolicyStats StreamedCall::upload(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max,
+                                 std::vector<double>* row_sumsq, std::vector<double>* col_sumsq, double* rg) {
     const uint64_t m = m_, n = n_, k = k_;
     const uint32_t N = (uint32_t)round_up(n, 64);  // the planners' padded width
     stats_ = std::make_unique<PolicyStatsRun>(m, n, k, N, work_);
@@ -100,7 +101,7 @@ PolicyStats StreamedCall::upload(std::vector<uint64_t>& row_max, std::vector<uin
     stats_->a_done(da);
     OZTT_CUDA(cudaEventSynchronize(uploaded));
     phases_.upload_ms = ms_since_start();
-    const PolicyStats ps = stats_->collect(&row_max, &col_max);
+    const PolicyStats ps = stats_->collect(&row_max, &col_max, row_sumsq, col_sumsq, rg);
     phases_.stats_ms = ms_since_start() - phases_.upload_ms;
     return ps;
 }

@@ -317,3 +317,28 @@ def test_context_scheme_i_device_selection(oztt, oracle, cuda, fmt):
     assert info.slices == plan.p
     ref = oztt.i_int8_run(a, b, m, n, k, plan)
     assert np.array_equal(c.view(np.uint64), ref.view(np.uint64))
+
+
+@pytest.mark.parametrize("fmt", [5, 0])
+def test_context_scheme_i_streamed_bands(oztt, oracle, cuda, fmt):
+    """Context::gemm's streamed Scheme I call over several column blocks of both operands and two row bands
+    (the last ragged): the host plan's p and the bits of the host-planned run; value errors come from the
+    measured maxima in the reference's order, before a fixed-slice feasibility error."""
+    m, n, k = 4500, 2048, 4608
+    a, b = oracle.gen_inputs(m, n, k, 0.5, 51)
+    plan = oztt.i_int8_plan(a, b, m, n, k, fmt=fmt)
+    c = np.full(m * n, 123.0)
+    ctx = oztt.Context()
+    info = ctx.gemm(a, b, c, m, n, k, oztt.Options(scheme=oztt.Scheme.I, format=fmt))
+    assert info.slices == plan.p
+    ref = oztt.i_int8_run(a, b, m, n, k, plan)
+    assert np.array_equal(c.view(np.uint64), ref.view(np.uint64))
+    assert oztt.ii_int8_last_phases()["bands"] == 2
+    a[17] = np.nan
+    c2 = np.full(64 * 64, 123.0)
+    small_a, small_b = a[: 64 * 64].copy(), b[: 64 * 64].copy()
+    with pytest.raises(ValueError, match="A contains NaN or infinity"):
+        ctx.gemm(small_a, small_b, c2, 64, 64, 64, oztt.Options(scheme=oztt.Scheme.I, format=fmt))
+    with pytest.raises(ValueError, match="A contains NaN or infinity"):  # before the infeasible 255 slices
+        ctx.gemm(small_a, small_b, c2, 64, 64, 64, oztt.Options(scheme=oztt.Scheme.I, format=fmt, slices=255))
+    assert np.all(c2 == 123.0)
