@@ -77,20 +77,24 @@ struct TermsSide {
 };
 
 // A block owns kChains adjacent chains. It takes their elements kSpan at a time: every thread expands one
-// element (the expansions are independent of one another and of the sums) and leaves its per-step
-// contributions in shared memory, then the owners of the sums -- one thread per (chain, sum) -- add the
-// kSpan contributions in element order, so each sum receives its terms in the host's order. A step after
-// an element's residual reached exactly zero contributes +0, which leaves a sum unchanged (the sums are
-// never -0), as the host adds nothing. For A (element stride = a row) the kChains adjacent columns make a
-// warp's loads cover whole 32-byte sectors; for B (element stride 1) a warp reads kSpan consecutive
-// elements of one row.
-constexpr int kChains = 4, kSpan = 32, kTermsThreads = kChains * kSpan;
+// element (the expansions are independent of one another and of the sums), kGroup steps at a time, and
+// leaves the group's per-step contributions in shared memory; then the owners of the group's sums -- one
+// thread per (chain, sum) -- add the kSpan contributions in element order, so each sum receives its terms
+// in the host's order. A step after an element's residual reached exactly zero contributes +0, which
+// leaves a sum unchanged (the sums are never -0), as the host adds nothing; once every element of the
+// block is exhausted the remaining groups are skipped. Holding one group at a time keeps the shared
+// memory per thread small, so that more warps hide the latency of the dependent FP64 chains. For A
+// (element stride = a row) the kChains adjacent columns make a warp's loads cover whole 32-byte sectors;
+// for B (element stride 1) a warp reads kSpan consecutive elements of one row.
+constexpr int kChains = 4, kSpan = 32, kTermsThreads = kChains * kSpan, kGroup = 8;
+// contributions of one group: [2 kGroup + 1][kTermsThreads] (S steps, R steps, N)
+constexpr int kGroupRows = 2 * kGroup + 1;
 
 template <int PMAX>
 __global__ void __launch_bounds__(kTermsThreads) terms_kernel(TermsSide A, TermsSide B, uint32_t a_blocks,
                                                               double radix, double dmax, const Weights wt) {
-    extern __shared__ double contrib[];  // [2 PMAX + 1][kTermsThreads]: S steps, R steps 1..PMAX, N
-    constexpr int NS = 2 * PMAX + 1;
+    __shared__ double contrib[kGroupRows * kTermsThreads];
+    constexpr int NG = (PMAX + kGroup - 1) / kGroup;
     const bool side_b = blockIdx.x >= a_blocks;
     const TermsSide& sd = side_b ? B : A;
     const uint64_t q0 = (uint64_t)(blockIdx.x - (side_b ? a_blocks : 0)) * kChains;
@@ -98,13 +102,15 @@ __global__ void __launch_bounds__(kTermsThreads) terms_kernel(TermsSide A, Terms
     // the element slot of this thread: chain fastest for A (adjacent columns), element fastest for B
     const int cq = side_b ? t / kSpan : t % kChains, ce = side_b ? t % kSpan : t / kChains;
     const uint64_t q = q0 + cq;
-    // the sums this thread owns: indices t, t + 128, ... of [kChains][NS]
-    double acc[(kChains * NS + kTermsThreads - 1) / kTermsThreads];
+    // the sum this thread owns in every group (kChains * kGroupRows <= kTermsThreads): chain oq, row oi of
+    // the group's contributions; the S and R sums of all groups and N stay in registers
+    const int oq = t / kGroupRows, oi = t % kGroupRows;
+    const bool owner = t < kChains * kGroupRows;
+    double accS[NG], accR[NG], accN = 0.0;
 #pragma unroll
-    for (int j = 0; j < (kChains * NS + kTermsThreads - 1) / kTermsThreads; ++j) acc[j] = 0.0;
+    for (int g = 0; g < NG; ++g) accS[g] = accR[g] = 0.0;
+    double* col = contrib + t;
     for (uint64_t e0 = 0; e0 < sd.len; e0 += kSpan) {
-        // expand this thread's element
-        double* col = contrib + t;  // contrib[i * kTermsThreads + t]
         const uint64_t e = e0 + ce;
         double th = 0.0, tl = 0.0, sc = 0.0, vr2 = 0.0;
         bool live = false;
@@ -119,56 +125,63 @@ __global__ void __launch_bounds__(kTermsThreads) terms_kernel(TermsSide A, Terms
                 sc = se;
             }
         }
-#pragma unroll 1
-        for (int i = 0; i < PMAX; ++i) {
-            double cs = 0.0, cr = 0.0;
-            if (live) {
-                const double w = wt.w[i];
-                const double dg = expand_step(th, tl, radix, dmax);
-                const double c = __dmul_rn(__dmul_rn(sc, dg), w);
-                cs = __dmul_rn(c, c);
-                const double r = __dmul_rn(__dmul_rn(sc, __dadd_rn(th, tl)), w);
-                cr = __dmul_rn(r, r);
-                live = th != 0.0;
-            }
-            col[i * kTermsThreads] = cs;
-            col[(PMAX + i) * kTermsThreads] = cr;
-        }
-        col[2 * PMAX * kTermsThreads] = vr2;
-        __syncthreads();
-        // add the kSpan contributions of each owned sum in element order
         const int n_el = sd.len - e0 < (uint64_t)kSpan ? (int)(sd.len - e0) : kSpan;
+        const int slot = side_b ? oq * kSpan : oq;         // first element's slot of the owned chain
+        const int slot_step = side_b ? 1 : kChains;        // slot distance of consecutive elements
 #pragma unroll
-        for (int j = 0; j < (kChains * NS + kTermsThreads - 1) / kTermsThreads; ++j) {
-            const int idx = t + j * kTermsThreads;
-            if (idx < kChains * NS) {
-                const int oq = idx / NS, oi = idx % NS;
-                const double* src = contrib + oi * kTermsThreads;
-                double a = acc[j];
-                for (int el = 0; el < n_el; ++el) {
-                    const int slot = side_b ? oq * kSpan + el : el * kChains + oq;
-                    a = __dadd_rn(a, src[slot]);
+        for (int g = 0; g < NG; ++g) {
+            // the block stops at the first group in which no element is still being expanded
+            if (!__syncthreads_or(live) && g > 0) break;
+#pragma unroll
+            for (int j = 0; j < kGroup; ++j) {
+                const int i = g * kGroup + j;
+                double cs = 0.0, cr = 0.0;
+                if (i < PMAX && live) {
+                    const double w = wt.w[i];
+                    const double dg = expand_step(th, tl, radix, dmax);
+                    const double c = __dmul_rn(__dmul_rn(sc, dg), w);
+                    cs = __dmul_rn(c, c);
+                    const double r = __dmul_rn(__dmul_rn(sc, __dadd_rn(th, tl)), w);
+                    cr = __dmul_rn(r, r);
+                    live = th != 0.0;
                 }
-                acc[j] = a;
+                col[j * kTermsThreads] = cs;
+                col[(kGroup + j) * kTermsThreads] = cr;
+            }
+            col[2 * kGroup * kTermsThreads] = vr2;
+            __syncthreads();
+            if (owner) {
+                const double* src = contrib + oi * kTermsThreads + slot;
+                double a = oi < kGroup ? accS[g] : (oi < 2 * kGroup ? accR[g] : accN);
+                const bool skip = oi == 2 * kGroup && g > 0;  // N is summed once, with group 0
+                if (!skip)
+                    for (int el = 0; el < n_el; ++el) a = __dadd_rn(a, src[el * slot_step]);
+                if (oi < kGroup)
+                    accS[g] = a;
+                else if (oi < 2 * kGroup)
+                    accR[g] = a;
+                else
+                    accN = a;
             }
         }
         __syncthreads();
     }
-    // S[i][q] (i < PMAX), R[i + 1][q], N[q]; R[0][q] = 0
+    // S[i][q] (i < PMAX) and R[i + 1][q] for i = g kGroup + (oi mod kGroup); N[q]; R[0][q] = 0. Groups the
+    // block skipped left their sums at +0.
+    if (owner) {
+        const uint64_t qq = q0 + oq;
+        if (qq < sd.chains) {
 #pragma unroll
-    for (int j = 0; j < (kChains * NS + kTermsThreads - 1) / kTermsThreads; ++j) {
-        const int idx = t + j * kTermsThreads;
-        if (idx < kChains * NS) {
-            const int oq = idx / NS, oi = idx % NS;
-            const uint64_t qq = q0 + oq;
-            if (qq < sd.chains) {
-                if (oi < PMAX)
-                    sd.S[(uint64_t)oi * sd.chains + qq] = acc[j];
-                else if (oi < 2 * PMAX)
-                    sd.R[(uint64_t)(oi - PMAX + 1) * sd.chains + qq] = acc[j];
-                else
-                    sd.N[qq] = acc[j];
+            for (int g = 0; g < NG; ++g) {
+                if (oi < kGroup) {
+                    const int i = g * kGroup + oi;
+                    if (i < PMAX) sd.S[(uint64_t)i * sd.chains + qq] = accS[g];
+                } else if (oi < 2 * kGroup) {
+                    const int i = g * kGroup + oi - kGroup;
+                    if (i < PMAX) sd.R[(uint64_t)(i + 1) * sd.chains + qq] = accR[g];
+                }
             }
+            if (oi == 2 * kGroup) sd.N[qq] = accN;
         }
     }
     if (t < kChains && q0 + t < sd.chains) sd.R[q0 + t] = 0.0;
@@ -178,10 +191,8 @@ template <int PMAX>
 void launch_terms(const TermsSide& A, const TermsSide& B, const I1Format& f, cudaStream_t st) {
     const uint32_t a_blocks = (uint32_t)((A.chains + kChains - 1) / kChains);
     const uint32_t b_blocks = (uint32_t)((B.chains + kChains - 1) / kChains);
-    const size_t smem = (size_t)(2 * PMAX + 1) * kTermsThreads * sizeof(double);
-    OZTT_CUDA(cudaFuncSetAttribute(terms_kernel<PMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    terms_kernel<PMAX><<<a_blocks + b_blocks, kTermsThreads, smem, st>>>(A, B, a_blocks, f.radix, f.dmax,
-                                                                        weights_of(f.radix));
+    terms_kernel<PMAX><<<a_blocks + b_blocks, kTermsThreads, 0, st>>>(A, B, a_blocks, f.radix, f.dmax,
+                                                                     weights_of(f.radix));
     OZTT_CUDA(cudaGetLastError());
 }
 
