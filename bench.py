@@ -569,11 +569,13 @@ def main() -> None:
                          "planning": "device-measured statistics" if world == 1 else
                                      "global statistics from the panels of all ranks (NCCL all-reduce)"},
               "moduli_roofline": {
-                  "tflops": int8_peak / S, "frac": value / (int8_peak / S),
-                  "meaning": "effective FP64 TFLOPS the sustained int8 tensor rate allows with S moduli "
-                             "(2mnk FP64 flops cost 2mnk*S int8 ops); frac = value / that"},
-              "vs_fp64_peak": {"fp64_peak_tflops": FP64_PEAK_TFLOPS, "ratio": value / FP64_PEAK_TFLOPS,
-                               "source": "B200 nominal dense FP64 (vector and tensor core), NVIDIA datasheet"},
+                  "tflops": int8_peak * world / S, "frac": value / (int8_peak * world / S),
+                  "meaning": "whole-job effective FP64 TFLOPS the sustained int8 tensor rate of the N GPUs "
+                             "allows with S moduli (2mnk FP64 flops cost 2mnk*S int8 ops); frac = value / that"},
+              "vs_fp64_peak": {"fp64_peak_tflops": FP64_PEAK_TFLOPS * world,
+                               "ratio": value / (FP64_PEAK_TFLOPS * world),
+                               "source": "B200 nominal dense FP64 (vector and tensor core), NVIDIA datasheet, "
+                                         "times the N GPUs"},
               "stage_ms": {"scale_rows": stage_ms[0], "scale_cols": stage_ms[1], "split_rows": stage_ms[2],
                            "split_cols": stage_ms[3], "residue_gemm": stage_ms[4], "recon": stage_ms[5]},
               "roofline": {"bound": "tensor", "kernel": "residue_gemm_kernel<1> (tcgen05 kind::i8)",
