@@ -86,17 +86,25 @@ struct TermsSide {
 // memory per thread small, so that more warps hide the latency of the dependent FP64 chains. For A
 // (element stride = a row) the kChains adjacent columns make a warp's loads cover whole 32-byte sectors;
 // for B (element stride 1) a warp reads kSpan consecutive elements of one row.
-// Groups of 3 steps stop a block within 3 steps of its longest expansion. Measured at 8192^2 per operand
-// (INT8 / BF16 digits, ms per launch): groups of 8 24.9 / 17.1, of 4 21.4 / 11.3, of 3 20.9 / 11.0, of 2
-// 21.6 / 12.7 (more owner passes, more registers for the sums).
-constexpr int kChains = 4, kSpan = 32, kTermsThreads = kChains * kSpan, kGroup = 3;
-// contributions of one group: [2 kGroup + 1][kTermsThreads] (S steps, R steps, N)
+// Groups of 5 steps stop a block within 5 steps of its longest expansion. Measured at 8192^2 per operand
+// (INT8 / BF16 digits, ms per launch) with the padded layout below and the owners' loads issued 8 at a
+// time: groups of 2 15.2 / 8.9, of 3 11.3 / 6.1, of 4 10.9 / 5.9, of 5 10.1 / 6.0; with an unpadded layout
+// and one load per add, groups of 3 took 20.9 / 11.0 and groups of 8 24.9 / 17.1.
+constexpr int kChains = 4, kSpan = 32, kTermsThreads = kChains * kSpan, kGroup = 5;
+// contributions of one group: [2 kGroup + 1][kRowStride] (S steps, R steps, N)
 constexpr int kGroupRows = 2 * kGroup + 1;
+// Layout of the contributions: thread t writes slot t + (t / kSpan) (one pad per 32 slots) of every row,
+// rows kRowStride apart. kRowStride = 4 (mod 16) and chains 33 slots apart give owner (row i, chain q)
+// the 8-byte bank 4 i + q + const (mod 16): at most 3 of a warp's owners share a bank, so a load takes
+// at most 3 wavefronts (2 is the minimum for 32 doubles; unpadded, the owners of B's chains all read one
+// bank).
+constexpr int kChainPad = 1, kRowStride = kTermsThreads + 4;
+static_assert(kTermsThreads - 1 + (kTermsThreads - 1) / kSpan * kChainPad < kRowStride, "slots fit a row");
 
 template <int PMAX>
 __global__ void __launch_bounds__(kTermsThreads) terms_kernel(TermsSide A, TermsSide B, uint32_t a_blocks,
                                                               double radix, double dmax, const Weights wt) {
-    __shared__ double contrib[kGroupRows * kTermsThreads];
+    __shared__ double contrib[kGroupRows * kRowStride];
     constexpr int NG = (PMAX + kGroup - 1) / kGroup;
     const bool side_b = blockIdx.x >= a_blocks;
     const TermsSide& sd = side_b ? B : A;
@@ -112,7 +120,7 @@ __global__ void __launch_bounds__(kTermsThreads) terms_kernel(TermsSide A, Terms
     double accS[NG], accR[NG], accN = 0.0;
 #pragma unroll
     for (int g = 0; g < NG; ++g) accS[g] = accR[g] = 0.0;
-    double* col = contrib + t;
+    double* col = contrib + t + t / kSpan * kChainPad;
     for (uint64_t e0 = 0; e0 < sd.len; e0 += kSpan) {
         const uint64_t e = e0 + ce;
         double th = 0.0, tl = 0.0, sc = 0.0, vr2 = 0.0;
@@ -129,8 +137,9 @@ __global__ void __launch_bounds__(kTermsThreads) terms_kernel(TermsSide A, Terms
             }
         }
         const int n_el = sd.len - e0 < (uint64_t)kSpan ? (int)(sd.len - e0) : kSpan;
-        const int slot = side_b ? oq * kSpan : oq;         // first element's slot of the owned chain
-        const int slot_step = side_b ? 1 : kChains;        // slot distance of consecutive elements
+        // first element's slot of the owned chain; element el is el slots further on B's side and
+        // 4 el + el / 8 further on A's side (4 chains interleaved, one pad per 32 slots)
+        const int slot = side_b ? oq * (kSpan + kChainPad) : oq;
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
             // the block stops at the first group in which no element is still being expanded
@@ -148,17 +157,21 @@ __global__ void __launch_bounds__(kTermsThreads) terms_kernel(TermsSide A, Terms
                     cr = __dmul_rn(r, r);
                     live = th != 0.0;
                 }
-                col[j * kTermsThreads] = cs;
-                col[(kGroup + j) * kTermsThreads] = cr;
+                col[j * kRowStride] = cs;
+                col[(kGroup + j) * kRowStride] = cr;
             }
-            col[2 * kGroup * kTermsThreads] = vr2;
+            col[2 * kGroup * kRowStride] = vr2;
             __syncthreads();
             if (owner) {
-                const double* src = contrib + oi * kTermsThreads + slot;
+                const double* src = contrib + oi * kRowStride + slot;
                 double a = oi < kGroup ? accS[g] : (oi < 2 * kGroup ? accR[g] : accN);
                 const bool skip = oi == 2 * kGroup && g > 0;  // N is summed once, with group 0
-                if (!skip)
-                    for (int el = 0; el < n_el; ++el) a = __dadd_rn(a, src[el * slot_step]);
+                if (!skip && n_el == kSpan) {
+#pragma unroll 8
+                    for (int el = 0; el < kSpan; ++el) a = __dadd_rn(a, src[side_b ? el : 4 * el + (el >> 3)]);
+                } else if (!skip) {
+                    for (int el = 0; el < n_el; ++el) a = __dadd_rn(a, src[side_b ? el : 4 * el + (el >> 3)]);
+                }
                 if (oi < kGroup)
                     accS[g] = a;
                 else if (oi < 2 * kGroup)
