@@ -85,20 +85,23 @@ struct TermsSide {
 // block is exhausted the remaining groups are skipped. Holding one group at a time keeps the shared
 // memory per thread small, so that more warps hide the latency of the dependent FP64 chains. For A
 // (element stride = a row) the kChains adjacent columns make a warp's loads cover whole 32-byte sectors;
-// for B (element stride 1) a warp reads kSpan consecutive elements of one row.
+// for B (element stride 1) a warp reads runs of kSpan consecutive elements of a row.
 // Groups of 5 steps stop a block within 5 steps of its longest expansion. Measured at 8192^2 per operand
 // (INT8 / BF16 digits, ms per launch) with the padded layout below and the owners' loads issued 8 at a
-// time: groups of 2 15.2 / 8.9, of 3 11.3 / 6.1, of 4 10.9 / 5.9, of 5 10.1 / 6.0; with an unpadded layout
-// and one load per add, groups of 3 took 20.9 / 11.0 and groups of 8 24.9 / 17.1.
-constexpr int kChains = 4, kSpan = 32, kTermsThreads = kChains * kSpan, kGroup = 5;
+// time, 4 chains of 32 elements: groups of 2 15.2 / 8.9, of 3 11.3 / 6.1, of 4 10.9 / 5.9, of 5 10.1 / 6.0;
+// 8 chains of 16 elements (shorter serial sums, A's loads two sectors wide) with groups of 5: 9.97 / 5.77.
+// With an unpadded layout and one load per add, groups of 3 took 20.9 / 11.0 and groups of 8 24.9 / 17.1.
+constexpr int kChains = 8, kSpan = 16, kTermsThreads = kChains * kSpan, kGroup = 5;
 // contributions of one group: [2 kGroup + 1][kRowStride] (S steps, R steps, N)
 constexpr int kGroupRows = 2 * kGroup + 1;
-// Layout of the contributions: thread t writes slot t + (t / kSpan) (one pad per 32 slots) of every row,
-// rows kRowStride apart. kRowStride = 4 (mod 16) and chains 33 slots apart give owner (row i, chain q)
-// the 8-byte bank 4 i + q + const (mod 16): at most 3 of a warp's owners share a bank, so a load takes
-// at most 3 wavefronts (2 is the minimum for 32 doubles; unpadded, the owners of B's chains all read one
-// bank).
-constexpr int kChainPad = 1, kRowStride = kTermsThreads + 4;
+// Layout of the contributions: thread t writes slot t + (t / kSpan) (one pad per kSpan slots) of every
+// row, rows kRowStride apart. kRowStride = 4 (mod 16) and B's chains kSpan + 1 slots apart (A's chains
+// adjacent) give owner (row i, chain q) the 8-byte bank 4 i + q + const (mod 16): at most 3 of a warp's
+// owners share a bank, so a load takes at most 3 wavefronts (2 is the minimum for 32 doubles; unpadded,
+// the owners of B's chains all read one bank).
+constexpr int kChainPad = 1, kSlots = kTermsThreads + kTermsThreads / kSpan * kChainPad;
+constexpr int kRowStride = kSlots + ((4 - kSlots) % 16 + 16) % 16;
+static_assert(kRowStride % 16 == 4 && kSpan % kChains == 0 && kChains * kGroupRows <= kTermsThreads, "layout");
 static_assert(kTermsThreads - 1 + (kTermsThreads - 1) / kSpan * kChainPad < kRowStride, "slots fit a row");
 
 template <int PMAX>
@@ -138,7 +141,7 @@ __global__ void __launch_bounds__(kTermsThreads) terms_kernel(TermsSide A, Terms
         }
         const int n_el = sd.len - e0 < (uint64_t)kSpan ? (int)(sd.len - e0) : kSpan;
         // first element's slot of the owned chain; element el is el slots further on B's side and
-        // 4 el + el / 8 further on A's side (4 chains interleaved, one pad per 32 slots)
+        // kChains el + el / (kSpan / kChains) further on A's side (chains interleaved, one pad per kSpan)
         const int slot = side_b ? oq * (kSpan + kChainPad) : oq;
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
@@ -168,9 +171,9 @@ __global__ void __launch_bounds__(kTermsThreads) terms_kernel(TermsSide A, Terms
                 const bool skip = oi == 2 * kGroup && g > 0;  // N is summed once, with group 0
                 if (!skip && n_el == kSpan) {
 #pragma unroll 8
-                    for (int el = 0; el < kSpan; ++el) a = __dadd_rn(a, src[side_b ? el : 4 * el + (el >> 3)]);
+                    for (int el = 0; el < kSpan; ++el) a = __dadd_rn(a, src[side_b ? el : el * kChains + el / (kSpan / kChains)]);
                 } else if (!skip) {
-                    for (int el = 0; el < n_el; ++el) a = __dadd_rn(a, src[side_b ? el : 4 * el + (el >> 3)]);
+                    for (int el = 0; el < n_el; ++el) a = __dadd_rn(a, src[side_b ? el : el * kChains + el / (kSpan / kChains)]);
                 }
                 if (oi < kGroup)
                     accS[g] = a;
