@@ -209,25 +209,31 @@ def time_cpu_dot2(a: np.ndarray, b: np.ndarray, n: int, k: int, target_s: float)
                       f"({rows}x{n}x{k}), {t:.2f} s"}
 
 
+def headline_config(args, world: int = 1) -> dict:
+    """The workload of the headline line; both arms (this library and --impl reference) print this same
+    object, so their numbers are quoted on one configuration."""
+    m = n = k = args.size
+    return {"workload": f"Scheme II INT8, {m}x{n}x{k}, phi={args.phi}, seed {args.seed}, auto precision",
+            "l2": "inputs (2.1 GB each) larger than the 126 MB L2; no flush"}
+
+
 def run_reference(args) -> None:
-    """--impl reference: the reference's own CPU FP64 GEMM on the box's host cores, per step a bounded
-    row sample of the same workload; rank 0 only."""
+    """--impl reference: the reference's own CPU FP64 GEMM (paper_eval::reference_gemm, Dot2 with OpenMP,
+    compiled from the reference sources into oracle/_ref) on the box's host cores, per step a bounded row
+    sample of the same workload; rank 0 only. The inputs come from the oracle's restatement of the
+    evaluator's generator (oracle/liboz2oracle.so), so this process maps no library of the product."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     n = k = args.size
-    sys.path.insert(0, str(ROOT))
-    import oztt_b200 as oz
+    sys.path.insert(0, str(ROOT / "tests"))
+    from oracle_lib import Oracle  # noqa: E402  (generator and, without oracle/_ref, the Dot2 port)
 
-    a, b = oz.eval_inputs(n, n, k, args.phi, args.seed)
+    orc = Oracle()
+    a, b = orc.gen_inputs(n, n, k, args.phi, args.seed)
     threads = cpu_threads()
     lib, kind = cpu_dot2_library()
     if lib is None:
-        sys.path.insert(0, str(ROOT / "tests"))
-        from oracle_lib import Oracle  # noqa: E402
-
-        orc = Oracle()
-
         def run(rows):
             return orc.lib.ozo_time_dot2_rows(a.ctypes.data, b.ctypes.data, rows, n, k, threads)
     else:
@@ -242,15 +248,81 @@ def run_reference(args) -> None:
         times.append(run(rows))
     t = statistics.median(times)
     value = 2.0 * rows * n * k / t / 1e12
+    sample = (f"Dot2 reference_gemm (evaluation/numerics.hpp:58-93) on the first {rows} rows of C per step "
+              f"({rows}x{n}x{k}, {2.0 * rows * n * k:.3g} FP64 flops), median of {args.steps} steps")
     line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "TFLOPS", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": f"II INT8 {n}x{n}x{k} phi={args.phi} seed={args.seed}; reference CPU FP64 GEMM "
-                                   f"on a {rows}-row sample per step"},
-            "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": kind,
-                             "sample": f"first {rows} rows of C per step"},
+            "config": headline_config(args),
+            "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def time_int8_cublaslt(m: int, n: int, k: int, gpu_index: int, seconds: float = 1.5) -> dict:
+    """cuBLASLt's int8 GEMM (torch._int_mm, int8 x int8 -> int32, A row-major times B column-major) on one
+    modulus-sized product m x n x k, run back to back for about `seconds` like the residue GEMM inside the
+    timed steps, with the SM clock sampled meanwhile: the library's int8 rate on this GPU, the bar for
+    the residue GEMM."""
+    import torch
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    a8 = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda", generator=g)
+    b8 = torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda", generator=g).t()
+    for _ in range(3):
+        c32 = torch._int_mm(a8, b8)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    c32 = torch._int_mm(a8, b8)
+    e1.record()
+    torch.cuda.synchronize()
+    reps = max(3, int(seconds / max(e0.elapsed_time(e1) * 1e-3, 1e-4)))
+    with ClockSampler(gpu_index) as clocks:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            c32 = torch._int_mm(a8, b8)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del a8, b8, c32
+    clk = clocks.summary()
+    return {"tops": 2.0 * m * n * k / (ms * 1e-3) / 1e12, "ms": ms, "reps": reps, "sm_mhz": clk.get("sm_mhz"),
+            "reasons": clk.get("reasons"), "shape": f"{m}x{n}x{k} int8 -> int32 (torch._int_mm, cuBLASLt)"}
+
+
+def reference_faithful_rows(oz, orc, A, B, m: int, n: int, k: int, plan, rows: np.ndarray) -> np.ndarray:
+    """The reference device's result on the listed rows of C, for the accuracy comparison: this library's
+    scaling, residues and exact int32 residue products (bit-identical to the reference's, pinned by the
+    published device hashes) on the GPU, then the oracle's restatement of the reference's triple-float CRT
+    reconstruction (recon_crt_proc.h, f64_tf.h) on the host. Checker only; outside the timed steps."""
+    import torch
+
+    r = len(rows)
+    st = torch.cuda.current_stream().cuda_stream
+    idx = torch.as_tensor(rows.astype(np.int64), device=A.device)
+    Ar = A.view(m, k).index_select(0, idx).contiguous()
+    mp, np_, kp = oz.padded_dims(r, n, k)
+    S = plan.S
+    dA = torch.zeros(mp, dtype=torch.int32, device="cuda")
+    dB = torch.zeros(np_, dtype=torch.int32, device="cuda")
+    flags = torch.zeros(2, dtype=torch.int32, device="cuda")
+    oz.call("oztt_ii_scale_rows", Ar.data_ptr(), r, k, k, plan.shift, dA.data_ptr(), None, flags.data_ptr(), st)
+    oz.call("oztt_ii_scale_cols", B.data_ptr(), k, n, n, plan.shift, dB.data_ptr(), None, flags[1:].data_ptr(), st)
+    ra = torch.zeros(S * mp * kp, dtype=torch.int8, device="cuda")
+    rb = torch.zeros(S * np_ * kp, dtype=torch.int8, device="cuda")
+    oz.call("oztt_ii_split_rows", Ar.data_ptr(), r, k, k, dA.data_ptr(), plan, ra.data_ptr(), mp, kp, st)
+    oz.call("oztt_ii_split_cols", B.data_ptr(), k, n, n, dB.data_ptr(), plan, rb.data_ptr(), np_, kp, st)
+    cs = torch.empty(S * mp * np_, dtype=torch.int32, device="cuda")
+    oz.call("oztt_ii_residue_gemm", ra.data_ptr(), rb.data_ptr(), mp, np_, kp, plan, 0, cs.data_ptr(), st)
+    torch.cuda.synchronize()
+    del ra, rb
+    host = np.ascontiguousarray(cs.view(S, mp, np_)[:, :r, :n].cpu().numpy()).reshape(-1)
+    del cs
+    oplan = orc.crt_plan(plan.moduli_list, plan.b, plan.two_pass)
+    return orc.recon(host, r, n, dA[:r].cpu().numpy(), dB[:n].cpu().numpy(), oplan, exact=False)
 
 
 # ---- Scheme I INT8 (a separate workload, one GPU) -------------------------------------------------------
@@ -560,14 +632,14 @@ def main() -> None:
               "vs_baseline": None, "dtype": "f64 (int8 residue products, s32 accumulate)",
               "data": "synthetic: evaluation/numerics.hpp generator (u-0.5)*exp(phi*z), mt19937 seed "
                       f"{args.seed}" + ("" if world == 1 else " per panel"),
-              "config": {"workload": f"Scheme II INT8, {m}x{n}x{k} per GPU" +
-                                     ("" if world == 1 else f" ({P}x{Q} tiles: global {P * m}x{Q * n}x{k})") +
-                                     f", phi={args.phi}, auto precision",
-                         "moduli": S, "integer_bits": plan.b, "reconstruction_passes": 2 if plan.two_pass else 1,
-                         "l2": "inputs (2.1 GB each) larger than the 126 MB L2; no flush",
-                         "planning_s": round(t_plan, 3),
-                         "planning": "device-measured statistics" if world == 1 else
-                                     "global statistics from the panels of all ranks (NCCL all-reduce)"},
+              "config": headline_config(args, world) if world == 1 else
+                        {"workload": f"Scheme II INT8, {m}x{n}x{k} per GPU ({P}x{Q} tiles: global {P * m}x{Q * n}x{k}), "
+                                     f"phi={args.phi}, auto precision",
+                         "l2": "inputs (2.1 GB each) larger than the 126 MB L2; no flush"},
+              "plan": {"moduli": S, "moduli_set": plan.moduli_list, "integer_bits": plan.b,
+                       "reconstruction_passes": 2 if plan.two_pass else 1, "planning_s": round(t_plan, 3),
+                       "planning": "device-measured statistics" if world == 1 else
+                                   "global statistics from the panels of all ranks (NCCL all-reduce)"},
               "moduli_roofline": {
                   "tflops": int8_peak * world / S, "frac": value / (int8_peak * world / S),
                   "meaning": "whole-job effective FP64 TFLOPS the sustained int8 tensor rate of the N GPUs "
@@ -585,8 +657,8 @@ def main() -> None:
                                           f"burst 2 x bf16_tflops = {int8_burst:.1f}",
                            "traffic": gemm_traffic(m, n, k, S),
                            "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of residue_gemm_kernel<1> "
-                                             "captured at 4096^3 with S = 16 (537.35 MB + 246.64 MB, profiles/"
-                                             "residue_gemm_4096.md), scaled by S*(mk + nk + mn) to this launch",
+                                             "captured by ncu at 4096^3 with S = 16 (537.35 MB + 246.64 MB), scaled "
+                                             "by S*(mk + nk + mn) to this launch",
                            "algorithmic": f"2*m*n*k*S = {gemm_ops:.4g} int8 ops per launch"},
               "hbm_stages": {
                   "split_GBps": (split_bytes / ((stage_ms[2] + stage_ms[3]) * 1e-3)) / 1e9,
@@ -616,16 +688,38 @@ def main() -> None:
                 from oracle_lib import Oracle  # checker only
 
                 orc = Oracle()
-                rows = np.linspace(0, m - 1, 8).astype(np.uint64)
-                c_oz = C.cpu().numpy()
-                c_dg = D.reshape(-1).cpu().numpy()
-                result["max_rel_err"] = orc.maxrel_f128(a, b, c_oz, m, n, k, rows=rows)
-                result["cublas_dgemm"]["max_rel_err"] = orc.maxrel_f128(a, b, c_dg, m, n, k, rows=rows)
-                result["accuracy_sample"] = "8 rows of C (all columns) vs a binary128 reference"
+                rows = np.linspace(0, m - 1, 8).astype(np.int64)
+                idx = torch.as_tensor(rows, device="cuda")
+                c_oz = C.view(m, n).index_select(0, idx).cpu().numpy()
+                c_dg = D.index_select(0, idx).cpu().numpy()
+                del D
+                c_ref = reference_faithful_rows(oz, orc, A, B, m, n, k, plan, rows)
+                e_oz, e_dg, e_ref = orc.maxrel_f128_rows(a, b, [c_oz, c_dg, c_ref], m, n, k, rows)
+                result["max_rel_err"] = e_oz
+                result["cublas_dgemm"]["max_rel_err"] = e_dg
+                result["max_rel_err_reference"] = e_ref
+                result["max_rel_err_ratio_to_reference"] = e_oz / e_ref if e_ref > 0 else None
+                result["accuracy_sample"] = (
+                    "8 rows of C (all columns) vs a binary128 reference; max_rel_err_reference is the reference "
+                    "device's result on the same rows (its integer stages are this library's, bit-identical; its "
+                    "triple-float CRT reconstruction restated on the host)")
             except Exception as exc:  # noqa: BLE001
                 result["max_rel_err"] = None
                 result["accuracy_error"] = str(exc)
-        del D
+        if "D" in locals():
+            del D
+        torch.cuda.empty_cache()
+        # cuBLASLt's int8 GEMM on one modulus's product, back to back for about the length of the timed
+        # steps: the library rate the residue GEMM (all S moduli per launch) is compared with, clock for clock
+        lt = time_int8_cublaslt(m, n, k, local, seconds=max(1.0, ms * args.steps * 1e-3))
+        result["int8_cublaslt_tops"] = lt["tops"]
+        result["int8_cublaslt"] = lt
+        result["roofline"]["vs_int8_cublaslt"] = {
+            "residue_gemm_tops": gemm_tops, "residue_gemm_sm_mhz": clk.get("sm_mhz"),
+            "cublaslt_tops": lt["tops"], "cublaslt_sm_mhz": lt["sm_mhz"],
+            "ratio": gemm_tops / lt["tops"],
+            "ratio_per_clock": (gemm_tops / clk["sm_mhz"]) / (lt["tops"] / lt["sm_mhz"])
+            if clk.get("sm_mhz") and lt.get("sm_mhz") else None}
 
     # ---- end to end through the public API --------------------------------------------------------
     if args.e2e_steps > 0:

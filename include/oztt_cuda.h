@@ -302,7 +302,8 @@ int oztt_ii_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, in
  * front, or latency-critical paths where an allocation may synchronise or fail). Its scratch is a
  * fixed static device array that every GPU loading the library keeps until exit; n is limited to
  * OZTT_NOALLOC_MAX_COLS (larger n: OZTT_EINVAL). The first call on a device looks up the array's
- * address with that device current; make it before any stream capture. Calls on one device share the
+ * address with that device current; make it before any stream capture (after a cudaDeviceReset the next
+ * call looks it up again, so make that one before any capture too). Calls on one device share the
  * array (each clears the part it uses first); calls that overlap on the GPU race. */
 int oztt_ii_scale_cols_noalloc(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
                                uint16_t* bf16max, uint32_t* flags, void* stream, char* err, size_t errlen);
@@ -363,6 +364,21 @@ int oztt_i_diag_gemm(const int8_t* a_planes, const int8_t* b_planes, uint64_t mp
 int oztt_i_recon(const int32_t* diag, uint64_t mp, uint64_t np, const int32_t* delta_a, const int32_t* delta_b,
                  int32_t p, int32_t format, double* c, uint64_t m, uint64_t n, uint64_t ldc, void* stream, char* err,
                  size_t errlen);
+
+/* ---- kernel variants ------------------------------------------------------------------------------
+ * No counterpart in the reference (it has one kernel per stage and reads no environment). Process-wide
+ * switches between kernels that give identical results; the defaults (0) are the faster ones on a B200
+ * under its 1 kW power cap. A change applies to launches issued after it returns.
+ *   OZTT_OPT_GEMM_CTA_PAIRS  1: the INT8 residue GEMMs and Scheme I diagonal GEMMs on CTA pairs
+ *                            (tcgen05 cta_group::2, M = 256 per pair); 0: one CTA per tile.
+ *   OZTT_OPT_RECON_INT       1: the Scheme II INT8 reconstruction on the integer pipe (32-bit words);
+ *                            0: the FP64-pipe kernel (radix-2^39 limbs). */
+#define OZTT_OPT_GEMM_CTA_PAIRS 1
+#define OZTT_OPT_RECON_INT 2
+/* Sets an option to 0 or 1 (OZTT_EINVAL for an unknown option or value). */
+int oztt_set_option(int32_t option, int32_t value, char* err, size_t errlen);
+/* Reads an option's current value into *value. */
+int oztt_get_option(int32_t option, int32_t* value);
 
 /* Number of SMs and compute capability of a device (0 on success). */
 int oztt_device_info(int device_id, int32_t* sm_count, int32_t* cc_major, int32_t* cc_minor);

@@ -1114,6 +1114,43 @@ int ozo_maxrel_f128(const double* a, const double* b, const double* c, uint64_t 
     return 0;
 }
 
+int ozo_maxrel_f128_rows(const double* a, const double* b, const double* const* cs, int nc, uint64_t m, uint64_t n,
+                         uint64_t k, const uint64_t* rows, uint64_t nrows, double* maxrel) {
+    if (nc < 1 || nc > 16) return 1;
+    for (uint64_t t = 0; t < nrows; ++t)
+        if (rows[t] >= m) return 1;
+    double worst[16] = {};
+    // rows in parallel, and each row's columns in chunks, so that a handful of rows still fills the cores
+    const uint64_t chunk = 512, nchunk = (n + chunk - 1) / chunk;
+#pragma omp parallel
+    {
+        double mine[16] = {};
+#pragma omp for schedule(dynamic) collapse(2)
+        for (int64_t t = 0; t < (int64_t)nrows; ++t)
+            for (int64_t q = 0; q < (int64_t)nchunk; ++q) {
+                const uint64_t i = rows[t], j0 = (uint64_t)q * chunk, j1 = std::min(n, j0 + chunk);
+                std::vector<__float128> acc(j1 - j0, 0);
+                for (uint64_t l = 0; l < k; ++l) {
+                    const __float128 av = a[i * k + l];
+                    const double* br = b + l * n;
+                    for (uint64_t j = j0; j < j1; ++j) acc[j - j0] += av * (__float128)br[j];
+                }
+                for (int r = 0; r < nc; ++r)
+                    for (uint64_t j = j0; j < j1; ++j) {
+                        const __float128 ref = acc[j - j0];
+                        const __float128 d = (__float128)cs[r][(uint64_t)t * n + j] - ref;
+                        const double ad = (double)(d < 0 ? -d : d);
+                        const double ar = (double)(ref < 0 ? -ref : ref);
+                        mine[r] = std::max(mine[r], ar > 0 ? ad / ar : ad);
+                    }
+            }
+#pragma omp critical
+        for (int r = 0; r < nc; ++r) worst[r] = std::max(worst[r], mine[r]);
+    }
+    for (int r = 0; r < nc; ++r) maxrel[r] = worst[r];
+    return 0;
+}
+
 double ozo_time_dot2_rows(const double* a, const double* b, uint64_t rows, uint64_t n, uint64_t k, int threads) {
 #ifdef _OPENMP
     if (threads > 0) omp_set_num_threads(threads);

@@ -121,6 +121,11 @@ uint64_t ozo_output_hash(const double* c, uint64_t count);
 // rows if rows == NULL) and all columns. Elements whose reference is 0 count as absolute errors.
 int ozo_maxrel_f128(const double* a, const double* b, const double* c, uint64_t m, uint64_t n, uint64_t k,
                     const uint64_t* rows, uint64_t nrows, double* maxrel);
+// The same for nc results at once, each given only on the listed rows: cs[t] points at nrows x n values
+// (row r of cs[t] is row rows[r] of that result); maxrel[t] receives its error. One binary128 product per
+// row serves all of them.
+int ozo_maxrel_f128_rows(const double* a, const double* b, const double* const* cs, int nc, uint64_t m, uint64_t n,
+                         uint64_t k, const uint64_t* rows, uint64_t nrows, double* maxrel);
 
 // Time the Dot2 reference GEMM on `threads` OpenMP threads for the first `rows` rows of C
 // (m x n x k problem); returns seconds.

@@ -196,6 +196,8 @@ _SIGNATURES = {
     "oztt_i_slice_cols": [_P, _U64, _U64, _U64, _P, _I32, _I32, _P, _U64, _U64, _P, _ERR, _SZ],
     "oztt_i_diag_gemm": [_P, _P, _U64, _U64, _U64, _I32, _P, _P, _ERR, _SZ],
     "oztt_i_recon": [_P, _U64, _U64, _P, _P, _I32, _I32, _P, _U64, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_set_option": [_I32, _I32, _ERR, _SZ],
+    "oztt_get_option": [_I32, ctypes.POINTER(_I32)],
     "oztt_is_available": [_I32],
     "oztt_format_name": [_I32],
     "oztt_test_udiv_small": [ctypes.c_uint32, ctypes.c_uint32],
@@ -547,6 +549,26 @@ def padded_dims(m: int, n: int, k: int) -> tuple[int, int, int]:
     mp, np_, kp = _U64(), _U64(), _U64()
     _lib().oztt_ii_padded_dims(m, n, k, ctypes.byref(mp), ctypes.byref(np_), ctypes.byref(kp))
     return mp.value, np_.value, kp.value
+
+
+# Kernel-variant options (OZTT_OPT_* of include/oztt_cuda.h): identical results, default 0.
+OPT_GEMM_CTA_PAIRS, OPT_RECON_INT = 1, 2
+
+
+def set_option(option: int, value: int) -> None:
+    """Select a kernel variant process-wide (oztt_set_option)."""
+    err = _errbuf()
+    rc = _lib().oztt_set_option(option, int(value), err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+
+
+def get_option(option: int) -> int:
+    v = _I32()
+    rc = _lib().oztt_get_option(option, ctypes.byref(v))
+    if rc != OK:
+        _raise(rc, "unknown option")
+    return v.value
 
 
 def call(name: str, *args) -> None:

@@ -95,16 +95,23 @@ def build_programs(force: bool = False) -> None:
                   f"-L{PKG}", "-loztt", f"-Wl,-rpath,{PKG}", "-pthread"])
 
 
+def reference_root() -> Path:
+    """Where the reference tree is looked for (test tooling only): the directory named by the environment
+    variable OZTT_REFERENCE_DIR, else a directory named `reference` beside the repository."""
+    return Path(os.environ.get("OZTT_REFERENCE_DIR", str(ROOT.parent / "reference"))).resolve()
+
+
 def build_oracle() -> None:
     """The CPU checker libraries (test infrastructure): oracle/liboz2oracle.so always, and
     oracle/_ref/*.so and the reference's caller programs when the reference tree is present on this
-    machine."""
+    machine (reference_root())."""
     make = shutil.which("make") or "make"
     _run([make, "-s", "-C", str(ROOT / "oracle"), "all"])
-    if Path("/root/reference/src/backend").is_dir():
-        _run([make, "-s", "-C", str(ROOT / "oracle"), "ref"])
+    ref = reference_root()
+    if (ref / "src" / "backend").is_dir():
+        _run([make, "-s", "-C", str(ROOT / "oracle"), "ref", f"REF={ref}"])
         # the reference's own callers of the public API, compiled unchanged against liboztt.so
-        _run([make, "-s", "-C", str(ROOT / "oracle"), "callers"])
+        _run([make, "-s", "-C", str(ROOT / "oracle"), "callers", f"REF={ref}"])
 
 
 def build(force: bool = False) -> None:

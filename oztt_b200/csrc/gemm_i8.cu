@@ -769,26 +769,25 @@ static void udiv_magic(uint32_t d, uint32_t& magic, uint32_t& shift) {
 
 namespace {
 
-// The single-CTA kernel is the default; OZTT_GEMM_CTA_PAIRS=1 selects the CTA-pair kernel. Both give
-// identical results. Measured on B200 at 16384^3 (S = 17, 20 steps): the pair kernel needs about 9 %
-// fewer SM cycles for the residue GEMM, but it draws more power per cycle, and under the 1 kW cap the
-// SM clock settles near 1130 MHz instead of 1500 MHz, so it takes 64 ms instead of 53 ms. In short
-// runs that stay below the cap (Scheme I at 8192^3) it is the faster of the two.
-bool use_pairs() {
-    const char* v = std::getenv("OZTT_GEMM_CTA_PAIRS");
-    return v && v[0] == '1';
-}
+// The single-CTA kernel is the default; oztt_set_option(OZTT_OPT_GEMM_CTA_PAIRS, 1) selects the CTA-pair
+// kernel for modes 0-2. Both give identical results. Measured on B200 at 16384^3 (S = 17, 20 steps): the
+// pair kernel needs about 9 % fewer SM cycles for the residue GEMM, but it draws more power per cycle,
+// and under the 1 kW cap the SM clock settles near 1130 MHz instead of 1500 MHz, so it takes 64 ms
+// instead of 53 ms. In short runs that stay below the cap (Scheme I at 8192^3) it is the faster of the
+// two. Read once per launch, so the tensor maps and the kernel of one launch always agree.
+bool use_pairs() { return option_value(OZTT_OPT_GEMM_CTA_PAIRS) == 1; }
 
-// Launches mode MODE of the GEMM over `planes` planes of tiles (a plane = a modulus or a diagonal).
+// Launches mode MODE of the GEMM over `planes` planes of tiles (a plane = a modulus or a diagonal), on
+// CTA pairs when `pairs` (modes 0-2 only; the tensor maps must have been made for the same choice).
 template <int MODE>
 void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* out, uint64_t mp, uint64_t np, uint64_t kp,
-                 uint32_t planes, const gemm::EpiConst& ec, int* err_word, cudaStream_t st) {
+                 uint32_t planes, const gemm::EpiConst& ec, int* err_word, cudaStream_t st, bool pairs = false) {
     using namespace gemm;
     int dev = 0, sms = 148;
     OZTT_CUDA(cudaGetDevice(&dev));
     OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const uint32_t tiles_n = (uint32_t)(np / BN), num_kb = (uint32_t)(kp / BK);
-    if (MODE < 3 && use_pairs()) {
+    if (MODE < 3 && pairs) {
         // the CTA-pair kernel covers modes 0-2
         const uint32_t tiles_m2 = (uint32_t)((mp / 128 + 1) / 2);
         const uint64_t num_tiles = (uint64_t)planes * tiles_m2 * tiles_n;
@@ -853,9 +852,9 @@ void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64
     const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p.S, pairs ? pair::BM : BM, a_plane_rows);
     const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p.S, pairs ? pair::BNH : BN);
     if (mode == 0)
-        launch_gemm<0>(ta, tb, out, mp, np, kp, (uint32_t)p.S, ec, err_word, st);
+        launch_gemm<0>(ta, tb, out, mp, np, kp, (uint32_t)p.S, ec, err_word, st, pairs);
     else
-        launch_gemm<1>(ta, tb, out, mp, np, kp, (uint32_t)p.S, ec, err_word, st);
+        launch_gemm<1>(ta, tb, out, mp, np, kp, (uint32_t)p.S, ec, err_word, st, pairs);
 }
 
 // Scheme I diagonal products P_d = sum_{i=0..d} A_i B_{d-i}^T, d = 0..p-1, int32 [p][mp][np], from
@@ -879,7 +878,7 @@ void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t 
     const bool pairs = use_pairs();
     const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p, pairs ? pair::BM : BM, a_plane_rows);
     const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p, pairs ? pair::BNH : BN);
-    launch_gemm<2>(ta, tb, out, mp, np, kp, (uint32_t)p, ec, err_word, st);
+    launch_gemm<2>(ta, tb, out, mp, np, kp, (uint32_t)p, ec, err_word, st, pairs);
 }
 
 // FP8 digit products on the tensor cores: for each GEMM output u of the plan, P_u = sum_t A_(out_a+t)

@@ -11,6 +11,7 @@
 // CRT digits) taken from the stream-ordered allocator and released at the end of the call (the pool
 // keeps them for the next call). The range flags of the scaling stage and the wait-timeout word of
 // the GEMM are read back after C, as the reference reads its flags after C (src/ozaki2.cpp:469-472).
+#include <atomic>
 #include <algorithm>
 #include <chrono>
 #include <functional>
@@ -278,12 +279,33 @@ int run_ii_int8_streamed(int device_id, const double* a, const double* b, double
 
 void open_device_checked(int device_id) { open_device(device_id); }
 
+namespace {
+std::atomic<int> g_options[3];  // indexed by OZTT_OPT_*; zero-initialised (the defaults)
+}
+
+int option_value(int option) { return option > 0 && option < 3 ? g_options[option].load() : 0; }
+
 }  // namespace oztt
 
 using oztt::Error;
 using oztt::guarded;
 
 extern "C" {
+
+int oztt_set_option(int32_t option, int32_t value, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (option != OZTT_OPT_GEMM_CTA_PAIRS && option != OZTT_OPT_RECON_INT)
+            throw Error(OZTT_EINVAL, "unknown option " + std::to_string(option));
+        if (value != 0 && value != 1) throw Error(OZTT_EINVAL, "option values are 0 or 1");
+        oztt::g_options[option].store(value);
+    });
+}
+
+int oztt_get_option(int32_t option, int32_t* value) {
+    if (!value || (option != OZTT_OPT_GEMM_CTA_PAIRS && option != OZTT_OPT_RECON_INT)) return OZTT_EINVAL;
+    *value = oztt::option_value(option);
+    return OZTT_OK;
+}
 
 int oztt_ii_int8_run(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
                      const oztt_ii_plan* plan, char* err, size_t errlen) {

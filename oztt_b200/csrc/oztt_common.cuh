@@ -56,6 +56,9 @@ int guarded(char* err, size_t errlen, F&& f) {
 
 inline uint64_t round_up(uint64_t v, uint64_t q) { return (v + q - 1) / q * q; }
 
+// Current value of a process-wide kernel-variant option (OZTT_OPT_*, set by oztt_set_option; 0 by default).
+int option_value(int option);
+
 // ---- binary32 with round-to-nearest-even and flush-to-zero, never contracted -----------------
 // Each is one PTX instruction with an explicit rounding modifier, so the compiler can neither fuse
 // nor reorder them; .ftz flushes subnormal inputs and results to signed zero.

@@ -311,7 +311,9 @@ void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA
     const uint64_t total = m * ((n + 3) / 4);
     if (total == 0) return;
     const unsigned blocks = recon_blocks(total);
-    const bool fp64 = !(std::getenv("OZTT_RECON_INT") && std::getenv("OZTT_RECON_INT")[0] == '1');
+    // the FP64-pipe kernel unless oztt_set_option(OZTT_OPT_RECON_INT, 1) asks for the integer-pipe one
+    // (identical results)
+    const bool fp64 = option_value(OZTT_OPT_RECON_INT) != 1;
     if (fp64) {
 #define OZTT_RECON_FP64(NW_, NL_) \
     recon_fp64_kernel<NW_, NL_><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc)

@@ -4,19 +4,22 @@ infrastructure).
 tools/validated/quick.csv is the reference evaluator's CSV (evaluation/evaluate.cpp --quick) from the
 reference's own device: the table suite at n = 128 (seed 7, uniform(-1, 1); Scheme I with the table's fixed
 slice counts, Scheme II with fixed_bits 54 and one reconstruction pass). This keeps its rows for the
-formats built on B200 (BF16, FP16, TF32, FP8, INT8): what the plan reported and the output hash. Run in
-the build container, where the reference tree exists; the GPU machine reads the fixture.
+formats built on B200 (BF16, FP16, TF32, FP8, INT8): what the plan reported and the output hash. Run
+where the reference tree exists (OZTT_REFERENCE_DIR, or a directory named `reference` beside the
+repository); the GPU machine reads the fixture.
 
-    python tests/golden/make_quick_table.py
+    OZTT_REFERENCE_DIR=<reference tree> python tests/golden/make_quick_table.py
 """
 
 from __future__ import annotations
 
 import csv
 import json
+import os
 from pathlib import Path
 
-SOURCE = Path("/root/reference/tools/validated/quick.csv")
+REPO = Path(__file__).resolve().parents[2]
+SOURCE = Path(os.environ.get("OZTT_REFERENCE_DIR", REPO.parent / "reference")) / "tools" / "validated" / "quick.csv"
 OUT = Path(__file__).resolve().parent / "quick_table_128.json"
 FORMATS = ("BF16", "FP16", "TF32", "FP8", "INT8")
 KEEP = ("scheme", "format", "slices", "integer_bits", "moduli", "passes", "partial_products", "output_hash",

@@ -76,6 +76,7 @@ class Oracle:
         L.ozo_dot2_gemm.argtypes = [P, P, u64, u64, u64, P, P]
         L.ozo_accuracy.argtypes = [P, P, P, u64, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
         L.ozo_maxrel_f128.argtypes = [P, P, P, u64, u64, u64, P, u64, ctypes.POINTER(ctypes.c_double)]
+        L.ozo_maxrel_f128_rows.argtypes = [P, P, P, ctypes.c_int, u64, u64, u64, P, u64, P]
         L.ozo_i_slice.argtypes = [P, u64, u64, u64, ctypes.c_int, P, ctypes.c_int, P]
         L.ozo_i_gemm.argtypes = [P, P, ctypes.c_int, u64, u64, u64, P]
         L.ozo_i_recon_faithful.argtypes = [P, ctypes.c_int, u64, u64, P, P, P, u64]
@@ -248,6 +249,20 @@ class Oracle:
             r = np.ascontiguousarray(rows, dtype=np.uint64)
             self.lib.ozo_maxrel_f128(ptr(a), ptr(b), ptr(c), m, n, k, ptr(r), r.size, ctypes.byref(out))
         return out.value
+
+
+    def maxrel_f128_rows(self, a, b, results, m, n, k, rows) -> list[float]:
+        """Maximum relative errors against binary128 of several results given on the listed rows only
+        (each result: len(rows) x n values, row r standing for row rows[r])."""
+        r = np.ascontiguousarray(rows, dtype=np.uint64)
+        cs = [np.ascontiguousarray(c, dtype=np.float64).reshape(-1) for c in results]
+        for c in cs:
+            assert c.size == r.size * n
+        ptrs = (ctypes.c_void_p * len(cs))(*[ptr(c) for c in cs])
+        out = np.zeros(len(cs))
+        rc = self.lib.ozo_maxrel_f128_rows(ptr(a), ptr(b), ptrs, len(cs), m, n, k, ptr(r), r.size, ptr(out))
+        assert rc == 0, "bad arguments to ozo_maxrel_f128_rows"
+        return [float(x) for x in out]
 
 
 class RefPlan:

@@ -1,8 +1,7 @@
 """The CTA-pair variant of the residue GEMM (tcgen05.mma.cta_group::2, selected with
-OZTT_GEMM_CTA_PAIRS=1) against torch's int8 matmul and the oracle, including row counts that leave the
-last pair tile half empty (mp an odd multiple of 128)."""
-
-import os
+oztt_set_option(OZTT_OPT_GEMM_CTA_PAIRS, 1)) against torch's int8 matmul and the oracle, including row
+counts that leave the last pair tile half empty (mp an odd multiple of 128); and the integer-pipe
+reconstruction (OZTT_OPT_RECON_INT) against the oracle."""
 
 import numpy as np
 import pytest
@@ -12,14 +11,11 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture()
-def pairs():
-    old = os.environ.get("OZTT_GEMM_CTA_PAIRS")
-    os.environ["OZTT_GEMM_CTA_PAIRS"] = "1"
+def pairs(oztt):
+    old = oztt.get_option(oztt.OPT_GEMM_CTA_PAIRS)
+    oztt.set_option(oztt.OPT_GEMM_CTA_PAIRS, 1)
     yield
-    if old is None:
-        del os.environ["OZTT_GEMM_CTA_PAIRS"]
-    else:
-        os.environ["OZTT_GEMM_CTA_PAIRS"] = old
+    oztt.set_option(oztt.OPT_GEMM_CTA_PAIRS, old)
 
 
 def _stream():
@@ -52,3 +48,18 @@ def test_pair_pipeline_and_diagonals(oztt, oracle, cuda, pairs):
     ci = oztt.i_int8_run(a, b, m, n, k, iplan)
     refi = oracle.i_emulate(a, b, m, n, k, 7, exact=True)
     assert np.array_equal(ci.view(np.uint64), refi.view(np.uint64))
+
+
+def test_integer_pipe_reconstruction(oztt, oracle, cuda):
+    m, n, k = 260, 300, 400
+    a, b = oracle.gen_inputs(m, n, k, 1.0, 12)
+    plan = oztt.ii_int8_plan(a, b, m, n, k)
+    rc, ref, _, _ = oracle.emulate(a, b, m, n, k, exact=True)
+    assert rc == 0
+    old = oztt.get_option(oztt.OPT_RECON_INT)
+    oztt.set_option(oztt.OPT_RECON_INT, 1)
+    try:
+        c = oztt.ii_int8_run(a, b, m, n, k, plan)
+    finally:
+        oztt.set_option(oztt.OPT_RECON_INT, old)
+    assert np.array_equal(c.view(np.uint64), ref.view(np.uint64))
