@@ -3,9 +3,10 @@
 // Public C++ API (include/ozTTgemm/ozTTgemm.hpp) on top of the CUDA backend, and its C-ABI form
 // oztt_gemm. Front-end semantics follow the reference's src/context.cpp:
 //   * the same checks in the same order, before the device is touched and before C is written
-//     (check_options :82-93, span sizes, padding to 64/64/32 with the 32-bit tile-offset limit
-//     :103-117, finiteness and the [2^-126, largest BF16] range of every nonzero row maximum of A and
-//     column maximum of B :37-62), with the same exception types and messages;
+//     (the options :82-93, span sizes and padding to 64/64/32 :103-110, finiteness and the
+//     [2^-126, largest BF16] range of every nonzero row maximum of A and column maximum of B :37-62),
+//     with the same exception types and messages; the Tensix tile-offset bound (:111-114) is a limit of
+//     that device and is not applied;
 //   * one process-wide mutex serialises the calls of all contexts (:19, :152);
 //   * the device is opened on the first valid call; Info reports the padded dimensions (:176-180);
 //   * all input is consumed before C is written, so C may overlap A or B.
@@ -44,17 +45,8 @@ namespace ev = detail::evaluation;
 
 std::mutex runtime_mutex;
 
-std::size_t checked_product(std::size_t a, std::size_t b) {
-    if (a == 0 || b == 0 || a > std::numeric_limits<std::size_t>::max() / sizeof(double) / b)
-        throw std::invalid_argument("matrix dimensions are zero or overflow the address space");
-    return a * b;
-}
-std::uint32_t padded(std::size_t value, std::size_t quantum) {
-    constexpr std::size_t limit = std::numeric_limits<std::int32_t>::max();
-    if (value == 0 || value > limit - quantum)
-        throw std::invalid_argument("matrix dimension exceeds the supported device index range");
-    return static_cast<std::uint32_t>((value + quantum - 1) / quantum * quantum);
-}
+std::size_t round_up_to(std::size_t v, std::size_t q) { return (v + q - 1) / q * q; }
+
 // Finiteness and the range of every nonzero row maximum of A and column maximum of B, with the
 // reference's order of reports (context.cpp:37-62): A's rows in order (a row's NaN/Inf before its
 // maximum), then any NaN/Inf in B, then B's column maxima. The scans run on the process's host
@@ -116,17 +108,48 @@ void check_values(std::span<const double> a, std::span<const double> b, std::siz
     });
     report_maxima(row_max.data(), m, col_max.data(), n);
 }
+// The option rules in the order the reference examines them (src/context.cpp:79-93); the first one that
+// holds is reported. The enum values are range-checked because a caller can cast any integer to them.
+using OptionRule = std::pair<bool (*)(const Options&), const char*>;
+const OptionRule kOptionRules[] = {
+    {[](const Options& o) { return o.scheme != Scheme::I && o.scheme != Scheme::II; }, "unknown Ozaki scheme"},
+    {[](const Options& o) { return !is_available(o.format); }, "format is unknown or was not built"},
+    {[](const Options& o) {
+         return o.reconstruction != Reconstruction::Automatic && o.reconstruction != Reconstruction::OnePass &&
+                o.reconstruction != Reconstruction::TwoPass;
+     },
+     "unknown reconstruction mode"},
+    {[](const Options& o) { return o.slices > 256; }, "slices must be zero (automatic) or at most 256"},
+    {[](const Options& o) { return o.max_moduli > 24; }, "max_moduli exceeds the supported bound of 24"},
+    {[](const Options& o) {
+         return o.scheme == Scheme::I && (o.max_moduli != 0 || o.reconstruction != Reconstruction::Automatic);
+     },
+     "max_moduli and reconstruction apply only to Ozaki II"},
+    {[](const Options& o) { return o.scheme == Scheme::II && o.slices != 0; }, "slices applies only to Ozaki I"},
+};
+
 void check_options(const Options& o) {
-    if (o.scheme != Scheme::I && o.scheme != Scheme::II) throw std::invalid_argument("unknown Ozaki scheme");
-    if (!is_available(o.format)) throw std::invalid_argument("format is unknown or was not built");
-    if (o.reconstruction != Reconstruction::Automatic && o.reconstruction != Reconstruction::OnePass &&
-        o.reconstruction != Reconstruction::TwoPass)
-        throw std::invalid_argument("unknown reconstruction mode");
-    if (o.slices > 256) throw std::invalid_argument("slices must be zero (automatic) or at most 256");
-    if (o.max_moduli > 24) throw std::invalid_argument("max_moduli exceeds the supported bound of 24");
-    if (o.scheme == Scheme::I && (o.max_moduli != 0 || o.reconstruction != Reconstruction::Automatic))
-        throw std::invalid_argument("max_moduli and reconstruction apply only to Ozaki II");
-    if (o.scheme == Scheme::II && o.slices != 0) throw std::invalid_argument("slices applies only to Ozaki I");
+    for (const auto& [broken, message] : kOptionRules)
+        if (broken(o)) throw std::invalid_argument(message);
+}
+
+// The size rules (src/context.cpp:103-110), in the reference's order: A's span, then B's, then C's; a zero
+// dimension or an element count whose byte size overflows size_t is reported where the reference computes
+// that count, so a wrong span of A is reported before a zero n. Then each padded dimension must stay in
+// the signed 32-bit index range that the planner's dimensions use.
+constexpr const char* kBadDims = "matrix dimensions are zero or overflow the address space";
+constexpr const char* kBadSpans = "matrix span sizes do not match m, n, k";
+
+std::size_t elements_or_throw(std::size_t rows, std::size_t cols) {
+    const bool bad = rows == 0 || cols == 0 || rows > std::numeric_limits<std::size_t>::max() / sizeof(double) / cols;
+    if (bad) throw std::invalid_argument(kBadDims);
+    return rows * cols;
+}
+
+std::uint32_t padded_dim(std::size_t value, std::size_t quantum) {
+    const std::size_t top = (std::size_t)std::numeric_limits<std::int32_t>::max() - quantum;
+    if (value == 0 || value > top) throw std::invalid_argument("matrix dimension exceeds the supported device index range");
+    return (std::uint32_t)round_up_to(value, quantum);
 }
 struct Checked {
     std::uint32_t mp, np, kp;
@@ -142,15 +165,17 @@ bool checks_during_upload(const Options&) { return ev::active == nullptr; }
 Checked validate(const Options& options, std::span<const double> a, std::span<const double> b,
                  std::optional<std::size_t> c_size, std::size_t m, std::size_t n, std::size_t k) {
     check_options(options);
-    if (a.size() != checked_product(m, k) || b.size() != checked_product(k, n))
-        throw std::invalid_argument("matrix span sizes do not match m, n, k");
-    const std::size_t mn = checked_product(m, n);
-    if (c_size && *c_size != mn) throw std::invalid_argument("matrix span sizes do not match m, n, k");
-    const Checked v{padded(m, 64), padded(n, 64), padded(k, 32), mn};
-    for (auto count : {std::uint64_t(v.mp / 32) * (v.kp / 32), std::uint64_t(v.kp / 32) * (v.np / 32),
-                       std::uint64_t(v.mp / 32) * (v.np / 32)})
-        if (count > std::numeric_limits<std::uint32_t>::max() / 4096u)
-            throw std::invalid_argument("matrix is too large for the device's 32-bit offsets");
+    if (a.size() != elements_or_throw(m, k)) throw std::invalid_argument(kBadSpans);
+    if (b.size() != elements_or_throw(k, n)) throw std::invalid_argument(kBadSpans);
+    const std::size_t mn = elements_or_throw(m, n);
+    if (c_size && *c_size != mn) throw std::invalid_argument(kBadSpans);
+    Checked v{};
+    v.mp = padded_dim(m, 64);
+    v.np = padded_dim(n, 64);
+    v.kp = padded_dim(k, 32);
+    v.c_size = mn;
+    // (The reference also bounds the Tensix tile offsets of the padded matrices, src/context.cpp:111-114; the
+    // B200 kernels index HBM with 64-bit offsets, so that device limit does not apply here.)
     if (!checks_during_upload(options)) check_values(a, b, m, n, k);
     return v;
 }

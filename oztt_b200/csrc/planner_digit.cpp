@@ -22,9 +22,11 @@
 #include <cmath>
 #include <cstring>
 #include <functional>
+#include <map>
 #include <mutex>
 #include <numeric>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "oztt_cuda.h"
@@ -332,316 +334,453 @@ double compose_planes(bool composes, uint32_t mx) {
     return chunk < max_nout ? chunk + (max_nout + chunk - 1) / chunk : max_nout;
 }
 
-struct AweCand {
-    int m;
-    double bits;
-};
-struct AweClass {
+// The model search chooses the moduli of the BF16 and FP16 routes (awe.hpp, oz2_awe_choose): the set whose
+// modelled stage time is least among those covering the CRT window. Its decisions are the reference's, so
+// the specification below fixes not only what is minimised but also the traversal orders and cutoffs that
+// decide which set comes out when several cost the same or a cutoff is reached.
+//
+//  1. Families. Every usable modulus, taken from mod_cap down to 2, whose GEMM outputs stay exact binary32
+//     integers (largest group bound + mod_cap <= 2^24) and whose composition sum sum|c| (m/2 + 2) stays
+//     below 2^22, joins the family of moduli with the same (products, outputs, digit planes, slicer
+//     operations, one-digit) signature; the signature fixes the family's modelled cost per modulus. A
+//     family keeps its members in descending order; reach[t] is the number of bits of its first t members
+//     that are pairwise coprime, taken greedily in that order. Families are ranked by cost per bit of their
+//     largest member (ties: by cost).
+//  2. Bound. All members of all families, in ascending cost per bit (stable: family rank, then member
+//     order), are taken greedily when coprime to those taken, until the window is covered or the slots are
+//     used up; a member whose bits, with every remaining slot holding log2(mod_cap) bits, could no longer
+//     cover the window is passed over. If the window is covered the bound is 1.05 (cost + reconstruction)
+//     + 1e-9, with no total budget for the assignments when nothing was passed over; else there is no bound.
+//  3. Count vectors. Depth first over the families in rank order, the count of a family rising from 0 to
+//     the smaller of its reach table's length - 1 and the slots left. A complete vector is kept when its reach
+//     covers the window, it has a modulus, and its time (cost + reconstruction) is below the bound -- unless
+//     the DRAM condition applies and fails, which drops it and records the drop. A family is not entered
+//     when the cost so far plus the cheapest completion (missing bits x the least cost per bit of this and
+//     later families) reaches the bound; its counting stops at the first count whose cost + reconstruction
+//     reaches the bound, and after a count whose reach is 16 bits past the window; a count above zero is
+//     passed over when its cost plus the cheapest completion by later families reaches the bound. At most
+//     200000 vectors are kept; they are tried in ascending time (ties in the order kept).
+//  4. Assignment of one vector. Families in ascending member count (ties: rank). A family's members are
+//     chosen as ascending index combinations, each member coprime to all chosen before it. Trying index j
+//     with `left` members still to choose: if the bits so far, the next `left` members from j and the most
+//     the later families can add fall short of the window, no later index can do better (members descend)
+//     and the choices at this depth end; for the family's last member, one whose bits and the least the
+//     later families add overshoot the window by more than tol is passed over. A complete choice with an
+//     excess over the window in [0, tol], below the best so far, becomes the best. Every state -- a member
+//     chosen, the move to the next family, a complete choice, and the start -- counts one; the assignment
+//     stops once more than 400000 states were counted or an excess of at most 1e-4 was found.
+//  5. The first vector, in order, that has an assignment gives the set (sorted descending); with a total
+//     budget, no further vector is started once the states counted exceed it. If no set was found and the
+//     DRAM condition dropped some vector, the search runs again without the condition, with the budget 10^7.
+struct ModelFamily {
     int nprod, nout, npl, ops;
     bool one;
-    double cost;
-    std::vector<AweCand> v;
-    std::vector<double> est;
+    double cost;                // modelled cost of one member
+    std::vector<int> members;   // descending
+    std::vector<double> bits;   // log2 of each member
+    std::vector<double> reach;  // reach[t]: bits of the first t pairwise coprime members
 };
 
-// Usable moduli sorted into classes of equal cost, each with its greedy coprime bit estimate; classes
-// ordered by cost per bit of their largest member (ties by cost).
-std::vector<AweClass> awe_classes(uint32_t K, const AweCoef& C, const Path& p, int smax) {
-    std::vector<AweClass> ks;
+bool coprime_to_all(const std::vector<int>& set, int m) {
+    return std::all_of(set.begin(), set.end(), [m](int x) { return std::gcd(x, m) == 1; });
+}
+
+std::vector<ModelFamily> model_families(uint32_t K, const AweCoef& C, const Path& p, int smax) {
+    std::vector<ModelFamily> fam;
     const int mod_cap = p.mod_cap;
     for (int m = mod_cap; m >= 2; --m) {
         if (!usable(m, p, smax)) continue;
-        const int mg = maxg_for(m, K, mod_cap, p, smax);
-        const int pl = planes_of(m, p);
-        const int np = (int)product_terms(m, p).size();
-        const std::vector<Group> gr = product_groups(m, p, mg);
-        const int no = (int)gr.size(), op = awe_ops(m, p, smax);
-        const bool one = split_mode(m, p, smax) == OZTT_SPLIT_ONE;
-        double csum = 0, gmax = 0;
+        const std::vector<Group> gr = product_groups(m, p, maxg_for(m, K, mod_cap, p, smax));
+        if (gr.empty()) continue;
+        double coeff_sum = 0, worst = 0;
         for (const Group& g : gr) {
-            csum += std::fabs((double)g.coeff);
-            gmax = std::max(gmax, group_bound(m, g, (double)K, p, smax));
+            coeff_sum += std::fabs((double)g.coeff);
+            worst = std::max(worst, group_bound(m, g, (double)K, p, smax));
         }
-        if (gr.empty() || gmax + mod_cap > kTwo24 || csum * (m / 2.0 + 2.0) >= kTwo22) continue;
-        AweClass* k = nullptr;
-        for (AweClass& x : ks)
-            if (x.nprod == np && x.nout == no && x.npl == pl && x.ops == op && x.one == one) {
-                k = &x;
+        if (worst + mod_cap > kTwo24 || coeff_sum * (m / 2.0 + 2.0) >= kTwo22) continue;
+        const int nprod = (int)product_terms(m, p).size(), nout = (int)gr.size(), npl = planes_of(m, p);
+        const int ops = awe_ops(m, p, smax);
+        const bool one = split_mode(m, p, smax) == OZTT_SPLIT_ONE;
+        auto same = [&](const ModelFamily& f) {
+            return f.nprod == nprod && f.nout == nout && f.npl == npl && f.ops == ops && f.one == one;
+        };
+        auto it = std::find_if(fam.begin(), fam.end(), same);
+        if (it == fam.end()) {
+            // GEMM products and outputs, the composition, the slicer's operations and planes (summed in
+            // this order: the costs are compared exactly); a one-digit modulus skips the composition and
+            // costs one more ModRound in the reconstruction instead
+            const double cost = one ? C.gp * nprod + C.go * nout + C.sop * (19 + ops) + C.spl * npl + kAweOneRecon * C.rb
+                                    : C.gp * nprod + (C.go + C.co) * nout + C.cs + C.sop * (19 + ops) + C.spl * npl;
+            fam.push_back({nprod, nout, npl, ops, one, cost, {}, {}, {}});
+            it = fam.end() - 1;
+        }
+        it->members.push_back(m);
+        it->bits.push_back(std::log2((double)m));
+    }
+    for (ModelFamily& f : fam) {
+        std::vector<int> taken;
+        f.reach.assign(1, 0.0);
+        for (size_t j = 0; j < f.members.size(); ++j)
+            if (coprime_to_all(taken, f.members[j])) {
+                taken.push_back(f.members[j]);
+                f.reach.push_back(f.reach.back() + f.bits[j]);
+            }
+    }
+    std::sort(fam.begin(), fam.end(), [](const ModelFamily& x, const ModelFamily& y) {
+        const double rx = x.cost / x.bits[0], ry = y.cost / y.bits[0];
+        if (rx != ry) return rx < ry;
+        return x.cost < y.cost;
+    });
+    return fam;
+}
+
+// The search's fixed data: the families, the window `need` and tolerance, the slots (max_moduli), the least
+// cost per bit from each family on, and the byte counts of the DRAM estimate.
+struct ModelProblem {
+    std::vector<ModelFamily> fam;
+    AweCoef C;
+    double need, tol;
+    int slots;
+    std::vector<double> cheapest;  // cheapest[f]: least cost per bit among families f.. (1e300 past the end)
+    double plane_bytes, out_bytes, free_bytes;
+    double recon(int S) const { return awe_recon(C, S); }
+    // S moduli with npl digit planes (largest composed output count mxo, 0: none) fit the model's free DRAM
+    // without output bands.
+    bool fits_dram(int S, int npl, int mxo) const {
+        const double q = (compose_planes(mxo > 0, (uint32_t)mxo) + S) * out_bytes;
+        return npl * plane_bytes + std::max(0.0, q - free_bytes) + kDramMargin <= kAweDramFree;
+    }
+};
+
+struct CountVector {
+    double time;
+    std::vector<int> n;
+};
+
+// Step 3: the count vectors under `bound`; returns whether the DRAM condition dropped one.
+bool count_vectors(const ModelProblem& P, double bound, bool dram, std::vector<CountVector>& kept) {
+    const int F = (int)P.fam.size();
+    struct Level {
+        int t = -1, tmax = 0, S = 0, npl = 0, mxo = 0;
+        double cost = 0, reach = 0;
+        bool visited = false;  // the current count t was descended into
+    };
+    std::vector<Level> path;
+    std::vector<int> n(F, 0);
+    bool dropped = false, full = false;
+    // Visits the node of family f (f == F: a complete vector); pushes a level when family f's counts are
+    // to be tried.
+    auto visit = [&](int f, int S, double cost, double reach, int npl, int mxo) {
+        if (kept.size() >= kAweVecMax) {
+            full = true;
+            return;
+        }
+        if (f == F) {
+            if (reach < P.need || S == 0) return;
+            const double T = cost + P.recon(S);
+            if (T >= bound) return;
+            if (dram && !P.fits_dram(S, npl, mxo))
+                dropped = true;
+            else
+                kept.push_back({T, n});
+            return;
+        }
+        if (cost + std::max(0.0, P.need - reach) * P.cheapest[f] + P.recon(S) >= bound) return;
+        Level lv;
+        lv.tmax = std::min((int)P.fam[f].reach.size() - 1, P.slots - S);
+        lv.S = S;
+        lv.npl = npl;
+        lv.mxo = mxo;
+        lv.cost = cost;
+        lv.reach = reach;
+        path.push_back(lv);
+    };
+    visit(0, 0, 0.0, 0.0, 0, 0);
+    while (!path.empty() && !full) {
+        const int f = (int)path.size() - 1;
+        const ModelFamily& g = P.fam[f];
+        Level& lv = path.back();
+        if (lv.visited && lv.reach + g.reach[lv.t] >= P.need + kAweOverNeedBits) lv.t = lv.tmax;  // counting ends
+        lv.visited = false;
+        if (++lv.t > lv.tmax) {
+            n[f] = 0;
+            path.pop_back();
+            continue;
+        }
+        const int t = lv.t;
+        n[f] = t;
+        const double cost = lv.cost + t * g.cost, reach = lv.reach + g.reach[t];
+        if (cost + P.recon(lv.S + t) >= bound) {
+            lv.t = lv.tmax;  // no larger count can be cheaper
+            continue;
+        }
+        if (t > 0 && cost + std::max(0.0, P.need - reach) * P.cheapest[f + 1] + P.recon(lv.S + t) >= bound) continue;
+        lv.visited = true;
+        const Level at = lv;  // visit() may grow `path`
+        visit(f + 1, at.S + t, cost, reach, at.npl + t * g.npl, (t && !g.one) ? std::max(at.mxo, g.nout) : at.mxo);
+    }
+    return dropped;
+}
+
+// Step 4: the moduli for one count vector (empty if none); `states` receives the states counted.
+std::vector<int> assign_moduli(const ModelProblem& P, const std::vector<int>& order, const std::vector<int>& counts,
+                               long& states) {
+    const int F = (int)P.fam.size();
+    std::vector<int> want(F);
+    std::vector<double> most(F + 1, 0.0), least(F + 1, 0.0);  // bits the families at positions i.. can add
+    for (int i = 0; i < F; ++i) want[i] = counts[order[i]];
+    for (int i = F - 1; i >= 0; --i) {
+        const std::vector<double>& b = P.fam[order[i]].bits;
+        const int use = std::min<int>(want[i], (int)b.size());
+        double hi = 0, lo = 0;
+        for (int j = 0; j < use; ++j) {
+            hi += b[j];
+            lo += b[b.size() - 1 - j];
+        }
+        most[i] = most[i + 1] + hi;
+        least[i] = least[i + 1] + lo;
+    }
+    struct Choosing {
+        int pos, next, left;
+        double bits;
+        bool rooted;  // entered by choosing a member (every frame but the first)
+    };
+    std::vector<Choosing> frames;
+    std::vector<int> chosen, best;
+    double best_excess = 1e300;
+    bool stop = false;
+    states = 0;
+    auto finished = [&] { return states > kAweNodeMax || best_excess <= 1e-4; };
+    // Enters a state: counts it, evaluates a complete choice, passes through family moves, and pushes a
+    // frame when members are to be chosen.
+    auto enter = [&](int pos, int next, int left, double bits, bool rooted) {
+        for (;;) {
+            ++states;
+            if (finished()) {
+                stop = true;
+                return;
+            }
+            if (pos == F) {
+                const double excess = bits - P.need;
+                if (excess >= 0 && excess <= P.tol && excess < best_excess) {
+                    best_excess = excess;
+                    best = chosen;
+                }
+                return;
+            }
+            if (left > 0) break;
+            ++pos;  // the move to the next family is a state of its own
+            next = 0;
+            left = pos < F ? want[pos] : 0;
+        }
+        frames.push_back({pos, next, left, bits, rooted});
+    };
+    enter(0, 0, F ? want[0] : 0, 0.0, false);
+    while (!stop && !frames.empty()) {
+        Choosing& fr = frames.back();
+        const ModelFamily& g = P.fam[order[fr.pos]];
+        const int size = (int)g.members.size();
+        bool pushed = false;
+        while (!stop && fr.next + fr.left <= size) {
+            const int j = fr.next++;
+            double upper = 0;
+            for (int t = 0; t < fr.left; ++t) upper += g.bits[j + t];
+            if (fr.bits + upper + most[fr.pos + 1] < P.need) {
+                fr.next = size;  // nothing from j on can reach the window
                 break;
             }
-        if (!k) {
-            const double cost = one ? C.gp * np + C.go * no + C.sop * (19 + op) + C.spl * pl + kAweOneRecon * C.rb
-                                    : C.gp * np + (C.go + C.co) * no + C.cs + C.sop * (19 + op) + C.spl * pl;
-            ks.push_back({np, no, pl, op, one, cost, {}, {}});
-            k = &ks.back();
-        }
-        k->v.push_back({m, std::log2((double)m)});
-    }
-    for (AweClass& k : ks) {
-        std::vector<int> got;
-        k.est.assign(1, 0.0);
-        for (const AweCand& c : k.v) {
-            bool ok = true;
-            for (int g : got)
-                if (std::gcd(g, c.m) != 1) {
-                    ok = false;
-                    break;
-                }
-            if (ok) {
-                got.push_back(c.m);
-                k.est.push_back(k.est.back() + c.bits);
+            if (fr.left == 1 && fr.bits + g.bits[j] + least[fr.pos + 1] > P.need + P.tol) continue;
+            if (!coprime_to_all(chosen, g.members[j])) continue;
+            chosen.push_back(g.members[j]);
+            const Choosing here = fr;  // enter() may grow `frames`
+            const size_t depth = frames.size();
+            enter(here.pos, j + 1, here.left - 1, here.bits + g.bits[j], true);
+            if (stop) break;
+            if (frames.size() > depth) {
+                pushed = true;
+                break;
             }
+            chosen.pop_back();
+            if (finished()) stop = true;
+        }
+        if (stop || pushed) continue;
+        const bool rooted = frames.back().rooted;
+        frames.pop_back();
+        if (rooted) {
+            chosen.pop_back();
+            if (finished()) stop = true;
         }
     }
-    std::sort(ks.begin(), ks.end(), [](const AweClass& a, const AweClass& b) {
-        const double ra = a.cost / a.v[0].bits, rb = b.cost / b.v[0].bits;
-        return ra != rb ? ra < rb : a.cost < b.cost;
-    });
-    return ks;
+    return best;
 }
 
-struct AweSearch {
-    const std::vector<AweClass>& ks;
-    const AweCoef& C;
-    double need, tol;
-    int max_moduli;
-    std::vector<double> minrate;
-    double P, out, F;
-    // S moduli with npl digit planes fit the model's free DRAM without output bands.
-    bool dram_ok(int S, int npl, int mxo) const {
-        const double Q = (compose_planes(mxo > 0, (uint32_t)mxo) + S) * out;
-        return npl * P + (Q > F ? Q - F : 0.0) + kDramMargin <= kAweDramFree;
-    }
-};
-struct AweVec {
-    double T;
-    std::vector<int> n;
-};
-
-// Count vectors below `incumbent` whose bit estimate reaches the window (pruned depth-first traversal).
-struct AweEnum {
-    const AweSearch& s;
-    double incumbent;
-    bool dram;
-    bool& dram_cut;
-    std::vector<AweVec>& vecs;
-    std::vector<int> n;
-    void rec(int c, int S, double cost, double est, int npl, int mxo) {
-        const int NC = (int)s.ks.size();
-        if (vecs.size() >= kAweVecMax) return;
-        if (c == NC) {
-            if (est >= s.need && S > 0) {
-                const double T = cost + awe_recon(s.C, S);
-                if (T < incumbent) {
-                    if (!dram || s.dram_ok(S, npl, mxo))
-                        vecs.push_back({T, n});
-                    else
-                        dram_cut = true;
-                }
-            }
-            return;
-        }
-        const double rem = std::max(0.0, s.need - est);
-        if (cost + rem * s.minrate[c] + awe_recon(s.C, S) >= incumbent) return;
-        const AweClass& k = s.ks[c];
-        const int maxn = std::min<int>((int)k.est.size() - 1, s.max_moduli - S);
-        for (int t = 0; t <= maxn; ++t) {
-            n[c] = t;
-            const double e2 = est + k.est[t];
-            if (cost + t * k.cost + awe_recon(s.C, S + t) >= incumbent) break;
-            if (t > 0 &&
-                cost + t * k.cost + std::max(0.0, s.need - e2) * s.minrate[c + 1] + awe_recon(s.C, S + t) >= incumbent)
-                continue;
-            rec(c + 1, S + t, cost + t * k.cost, e2, npl + t * k.npl, (t && !k.one) ? std::max(mxo, k.nout) : mxo);
-            if (e2 >= s.need + kAweOverNeedBits) break;
-        }
-        n[c] = 0;
-    }
-};
-
-// Pairwise coprime moduli for one count vector with bits in [need, need + tol], least excess first.
-struct AweAssign {
-    const AweSearch& s;
-    const std::vector<int>& ord;
-    std::vector<int> cnt;
-    std::vector<double> ubrest, lbrest;
-    std::vector<int> pick, best;
-    double bestex = 1e300;
-    long nodes = 0;
-    void dfs(int i, int start, int left, double bits) {
-        const int NC = (int)s.ks.size();
-        if (++nodes > kAweNodeMax || bestex <= 1e-4) return;
-        if (i == NC) {
-            const double ex = bits - s.need;
-            if (ex >= 0 && ex <= s.tol && ex < bestex) {
-                bestex = ex;
-                best = pick;
-            }
-            return;
-        }
-        if (left == 0) {
-            dfs(i + 1, 0, i + 1 < NC ? cnt[i + 1] : 0, bits);
-            return;
-        }
-        const std::vector<AweCand>& v = s.ks[ord[i]].v;
-        for (int j = start; j + left <= (int)v.size(); ++j) {
-            double ubc = 0;
-            for (int t = 0; t < left; ++t) ubc += v[j + t].bits;
-            if (bits + ubc + ubrest[i + 1] < s.need) return;
-            if (bits + v[j].bits + lbrest[i + 1] > s.need + s.tol && left == 1) continue;
-            bool ok = true;
-            for (int x : pick)
-                if (std::gcd(x, v[j].m) != 1) {
-                    ok = false;
-                    break;
-                }
-            if (!ok) continue;
-            pick.push_back(v[j].m);
-            dfs(i, j + 1, left - 1, bits + v[j].bits);
-            pick.pop_back();
-            if (nodes > kAweNodeMax || bestex <= 1e-4) return;
-        }
-    }
-};
-
-std::vector<int> awe_assign(const AweSearch& s, const std::vector<int>& ord, const AweVec& vec, long& nodes) {
-    const int NC = (int)s.ks.size();
-    AweAssign a{s, ord, std::vector<int>(NC), std::vector<double>(NC + 1, 0.0), std::vector<double>(NC + 1, 0.0),
-                {}, {}};
-    for (int i = 0; i < NC; ++i) a.cnt[i] = vec.n[ord[i]];
-    for (int i = NC - 1; i >= 0; --i) {
-        const std::vector<AweCand>& v = s.ks[ord[i]].v;
-        const int t = a.cnt[i];
-        double ubs = 0, lbs = 0;
-        for (int j = 0; j < t && j < (int)v.size(); ++j) {
-            ubs += v[j].bits;
-            lbs += v[v.size() - 1 - j].bits;
-        }
-        a.ubrest[i] = a.ubrest[i + 1] + ubs;
-        a.lbrest[i] = a.lbrest[i + 1] + lbs;
-    }
-    a.dfs(0, 0, NC ? a.cnt[0] : 0, 0.0);
-    nodes = a.nodes;
-    return a.best;
-}
-
-std::vector<int> awe_search(const AweSearch& s, double ub, bool dram, bool& dram_cut, long budget) {
-    const int NC = (int)s.ks.size();
-    std::vector<AweVec> vecs;
-    AweEnum e{s, ub, dram, dram_cut, vecs, std::vector<int>(NC, 0)};
-    e.rec(0, 0, 0.0, 0.0, 0, 0);
-    std::stable_sort(vecs.begin(), vecs.end(), [](const AweVec& a, const AweVec& b) { return a.T < b.T; });
-    std::vector<int> ord(NC);
-    for (int c = 0; c < NC; ++c) ord[c] = c;
-    std::stable_sort(ord.begin(), ord.end(), [&](int a, int b) { return s.ks[a].v.size() < s.ks[b].v.size(); });
+// Step 5 for one bound: the first assignable vector's moduli, descending (empty if none).
+std::vector<int> model_search(const ModelProblem& P, double bound, bool dram, bool& dropped, long budget) {
+    std::vector<CountVector> vecs;
+    dropped = count_vectors(P, bound, dram, vecs) || dropped;
+    std::stable_sort(vecs.begin(), vecs.end(), [](const CountVector& x, const CountVector& y) { return x.time < y.time; });
+    std::vector<int> order(P.fam.size());
+    for (size_t f = 0; f < order.size(); ++f) order[f] = (int)f;
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int x, int y) { return P.fam[x].members.size() < P.fam[y].members.size(); });
     long spent = 0;
-    for (const AweVec& vec : vecs) {
+    for (const CountVector& v : vecs) {
         if (budget > 0 && spent > budget) break;
-        long nodes = 0;
-        std::vector<int> best = awe_assign(s, ord, vec, nodes);
-        spent += nodes;
-        if (!best.empty()) {
-            std::sort(best.begin(), best.end(), std::greater<int>());
-            return best;
+        long states = 0;
+        std::vector<int> set = assign_moduli(P, order, v.n, states);
+        spent += states;
+        if (!set.empty()) {
+            std::sort(set.begin(), set.end(), std::greater<int>());
+            return set;
         }
     }
     return {};
 }
 
-// The greedy solution by cost per bit (with a look-ahead that keeps the window reachable within the
-// limit) times the slack; `unbounded` when the plain greedy solution reached the window.
-double awe_upper_bound(const AweSearch& s, int mod_cap, bool& unbounded) {
-    double ub = 1e300;
-    std::vector<std::pair<double, std::pair<int, double>>> all;
-    for (const AweClass& k : s.ks)
-        for (const AweCand& c : k.v) all.push_back({k.cost / c.bits, {c.m, k.cost}});
-    std::stable_sort(all.begin(), all.end(), [](const auto& a, const auto& b) { return a.first < b.first; });
-    const double maxbits = std::log2((double)mod_cap);
-    std::vector<int> got;
+// Step 2: the cost bound; `unbounded` when the plain greedy set covered the window.
+double model_bound(const ModelProblem& P, int mod_cap, bool& unbounded) {
+    struct Item {
+        double rate, cost;
+        int m;
+    };
+    std::vector<Item> items;
+    for (const ModelFamily& f : P.fam)
+        for (size_t j = 0; j < f.members.size(); ++j) items.push_back({f.cost / f.bits[j], f.cost, f.members[j]});
+    std::stable_sort(items.begin(), items.end(), [](const Item& x, const Item& y) { return x.rate < y.rate; });
+    const double widest = std::log2((double)mod_cap);
+    std::vector<int> taken;
     double bits = 0, cost = 0;
-    bool skipped = false;
-    for (const auto& a : all) {
-        if (bits >= s.need || (int)got.size() >= s.max_moduli) break;
-        bool ok = true;
-        for (int g : got)
-            if (std::gcd(g, a.second.first) != 1) {
-                ok = false;
-                break;
-            }
-        if (!ok) continue;
-        const double lb = std::log2((double)a.second.first);
-        if (bits + lb + (s.max_moduli - (int)got.size() - 1) * maxbits < s.need) {
-            skipped = true;
+    bool passed_over = false;
+    for (const Item& it : items) {
+        if (bits >= P.need || (int)taken.size() >= P.slots) break;
+        if (!coprime_to_all(taken, it.m)) continue;
+        const double b = std::log2((double)it.m);
+        const int open_slots = P.slots - (int)taken.size() - 1;
+        if (bits + b + open_slots * widest < P.need) {
+            passed_over = true;
             continue;
         }
-        got.push_back(a.second.first);
-        bits += lb;
-        cost += a.second.second;
+        taken.push_back(it.m);
+        bits += b;
+        cost += it.cost;
     }
-    if (bits >= s.need) ub = (cost + awe_recon(s.C, (int)got.size())) * kAweUbSlack + 1e-9;
-    unbounded = bits >= s.need && !skipped;
-    return ub;
+    unbounded = bits >= P.need && !passed_over;
+    return bits >= P.need ? (cost + P.recon((int)taken.size())) * kAweUbSlack + 1e-9 : 1e300;
 }
 
-// The moduli set (descending) of the stage-time model for the window `need`, or empty. The search is
-// deterministic in its arguments and can take seconds for large K, so its results are kept for the process.
-std::vector<int> awe_search_set(int awe, const Path& p, int smax, double need, double tol, int max_moduli, uint32_t M,
-                                uint32_t N, double slice_tile);
-std::vector<int> awe_choose(int awe, const Path& p, int smax, double need, double tol, int max_moduli, uint32_t M,
-                            uint32_t N, double slice_tile) {
-    struct Key {
-        int awe, mod_cap, dmax, smax, max_moduli;
-        bool one;
-        uint32_t K, M, N;
-        double need, tol, slice_tile;
-        bool operator==(const Key& o) const {
-            return awe == o.awe && mod_cap == o.mod_cap && dmax == o.dmax && smax == o.smax &&
-                   max_moduli == o.max_moduli && one == o.one && K == o.K && M == o.M && N == o.N && need == o.need &&
-                   tol == o.tol && slice_tile == o.slice_tile;
-        }
-    };
-    static std::mutex mu;
-    static std::vector<std::pair<Key, std::vector<int>>> memo;
-    const Key key{awe, p.mod_cap, p.dmax, smax, max_moduli, p.one, p.K, M, N, need, tol, slice_tile};
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        for (const auto& e : memo)
-            if (e.first == key) return e.second;
+std::vector<int> model_set_uncached(int awe, const Path& p, int smax, double need, double tol, int max_moduli, uint32_t M,
+                                    uint32_t N, double slice_tile) {
+    const uint32_t K = p.K;
+    ModelProblem P;
+    P.C = awe_coef(awe, K);
+    P.fam = model_families(K, P.C, p, smax);
+    if (P.fam.empty()) return {};
+    P.need = need;
+    P.tol = tol;
+    P.slots = max_moduli;
+    const int F = (int)P.fam.size();
+    P.cheapest.assign(F + 1, 1e300);
+    for (int f = F - 1; f >= 0; --f) P.cheapest[f] = std::min(P.cheapest[f + 1], P.fam[f].cost / P.fam[f].bits[0]);
+    const double operand_elems = (double)M * K + (double)K * N;
+    P.plane_bytes = operand_elems / 1024.0 * slice_tile;
+    P.out_bytes = (double)M * N * 4.0;
+    P.free_bytes = operand_elems * 8.0;
+    bool unbounded = false;
+    const double bound = model_bound(P, p.mod_cap, unbounded);
+    bool dropped = false;
+    std::vector<int> set = model_search(P, bound, true, dropped, unbounded ? 0 : kAweNodeBudget);
+    if (set.empty() && dropped) {
+        bool ignored = false;
+        set = model_search(P, bound, false, ignored, kAweNodeBudget);
     }
-    std::vector<int> set = awe_search_set(awe, p, smax, need, tol, max_moduli, M, N, slice_tile);
-    std::lock_guard<std::mutex> lock(mu);
-    if (memo.size() >= 256) memo.erase(memo.begin());
-    memo.push_back({key, set});
     return set;
 }
 
-std::vector<int> awe_search_set(int awe, const Path& p, int smax, double need, double tol, int max_moduli, uint32_t M,
-                                uint32_t N, double slice_tile) {
-    const uint32_t K = p.K;
-    const AweCoef C = awe_coef(awe, K);
-    const std::vector<AweClass> ks = awe_classes(K, C, p, smax);
-    if (ks.empty()) return {};
-    const int NC = (int)ks.size();
-    const double Md = M, Nd = N;
-    AweSearch s{ks,
-                C,
-                need,
-                tol,
-                max_moduli,
-                std::vector<double>(NC + 1, 1e300),
-                (Md * K + (double)K * Nd) / 1024.0 * slice_tile,
-                Md * Nd * 4.0,
-                (Md * K + (double)K * Nd) * 8.0};
-    for (int c = NC - 1; c >= 0; --c) s.minrate[c] = std::min(s.minrate[c + 1], ks[c].cost / ks[c].v[0].bits);
-    bool unbounded = false;
-    const double ub = awe_upper_bound(s, p.mod_cap, unbounded);
-    bool dram_cut = false;
-    std::vector<int> best = awe_search(s, ub, true, dram_cut, unbounded ? 0 : kAweNodeBudget);
-    if (best.empty() && dram_cut) {
-        bool unused = false;
-        best = awe_search(s, ub, false, unused, kAweNodeBudget);
+// The model's moduli set (descending) for the window `need`, or empty. The search is deterministic in its
+// arguments and can take seconds for large K, so its results are kept for the process.
+std::vector<int> awe_choose(int awe, const Path& p, int smax, double need, double tol, int max_moduli, uint32_t M,
+                            uint32_t N, double slice_tile) {
+    using Key = std::tuple<int, int, int, int, int, bool, uint32_t, uint32_t, uint32_t, double, double, double>;
+    static std::mutex mu;
+    static std::map<Key, std::vector<int>> memo;
+    const Key key{awe, p.mod_cap, p.dmax, smax, max_moduli, p.one, p.K, M, N, need, tol, slice_tile};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        const auto it = memo.find(key);
+        if (it != memo.end()) return it->second;
     }
-    return best;
+    std::vector<int> set = model_set_uncached(awe, p, smax, need, tol, max_moduli, M, N, slice_tile);
+    std::lock_guard<std::mutex> lock(mu);
+    if (memo.size() >= 256) memo.clear();
+    memo.emplace(key, set);
+    return set;
+}
+
+// Tail reselection (oz2_reselect_tail, moduli.hpp:365-451). The table's moduli step by several bits, so
+// the last two of a set often overshoot the window; the excess buys no accuracy (the reconstruction solves
+// C'/M to a fixed absolute accuracy) but costs products. Specification: keep the head (all but the last two
+// moduli) and choose, as the new tail, one modulus a or a pair a < b -- usable, at most mod_cap, coprime to
+// the head and to each other -- whose product with the head covers the window, minimising the key
+//   (matrix products of the tail, 1 if the excess exceeds kTailTol, 1000 x GEMM outputs + digit planes of
+//    the tail, log2 of the whole set)
+// lexicographically. The current tail is the starting incumbent and only a strictly smaller key replaces
+// it; candidates are met in the order a = 3, 4, ... (only odd a and b when the head has an even member),
+// a alone before the pairs (a, b) with b ascending, so among equal keys the first met wins.
+void reselect_tail(std::vector<int>& m, double& logM, double need, const Path& p, int smax, int mod_cap, uint32_t K) {
+    if (m.size() < 2 || !(logM > need)) return;
+    const std::vector<int> head(m.begin(), m.end() - 2);
+    double base = 0;
+    for (int x : head) base += std::log2((double)x);
+    // per-modulus products and layout cost; `open`: usable and coprime to the head
+    std::vector<int> products(mod_cap + 1, 0), layout(mod_cap + 1, 0);
+    std::vector<char> open(mod_cap + 1, 0);
+    for (int x = 3; x <= mod_cap; ++x)
+        if (usable(x, p, smax)) {
+            products[x] = (int)product_terms(x, p).size();
+            layout[x] = 1000 * (int)product_groups(x, p, maxg_for(x, K, mod_cap, p, smax)).size() + planes_of(x, p);
+            open[x] = coprime_to_all(head, x);
+        }
+    struct Key {
+        int products, over, layout;
+        double log2m;
+        bool operator<(const Key& o) const {
+            return std::tie(products, over, layout, log2m) < std::tie(o.products, o.over, o.layout, o.log2m);
+        }
+    };
+    auto key = [&](int nprod, int lay, double l) { return Key{nprod, (l - need) > kTailTol ? 1 : 0, lay, l}; };
+    auto cost_of = [&](int x) { return x >= 0 && x <= mod_cap ? products[x] : 0; };
+    auto layout_of = [&](int x) { return x >= 0 && x <= mod_cap ? layout[x] : 0; };
+    int ta = m[m.size() - 2], tb = m.back();
+    Key best = key(cost_of(ta) + cost_of(tb), layout_of(ta) + layout_of(tb), logM);
+    const bool head_even = std::any_of(head.begin(), head.end(), [](int x) { return x % 2 == 0; });
+    const int step = head_even ? 2 : 1;
+    for (int a = 3; a <= mod_cap; a += step) {
+        if (!open[a]) continue;
+        const double la = base + std::log2((double)a);
+        if (la >= need) {
+            const Key k = key(products[a], layout[a], la);
+            if (k < best) {
+                best = k;
+                ta = a;
+                tb = 0;
+            }
+        }
+        for (int b = a + step; b <= mod_cap; b += step) {
+            if (!open[b] || std::gcd(a, b) != 1) continue;
+            const double lab = la + std::log2((double)b);
+            if (lab < need) continue;
+            const Key k = key(products[a] + products[b], layout[a] + layout[b], lab);
+            if (k < best) {
+                best = k;
+                ta = a;
+                tb = b;
+            }
+        }
+    }
+    m = head;
+    m.push_back(ta);
+    if (tb) m.push_back(tb);
+    logM = best.log2m;
 }
 
 // ---- moduli selection (ozaki2_choose_moduli, moduli.hpp:700-770) ---------------------------------
@@ -704,66 +843,7 @@ Choice choose(const Route& rt, uint32_t M, uint32_t N, uint32_t K, int num_modul
             o.m.pop_back();
             logM -= l2;
         }
-        // reselect the last two (moduli.hpp:357-453)
-        if (o.m.size() >= 2 && logM > need) {
-            std::vector<int> head(o.m.begin(), o.m.end() - 2);
-            double base = 0;
-            for (int x : head) base += std::log2((double)x);
-            auto cop_head = [&](int mm) {
-                for (int x : head)
-                    if (std::gcd(mm, x) != 1) return false;
-                return true;
-            };
-            std::vector<char> use_c(mod_cap + 1, 0);
-            std::vector<int> np_c(mod_cap + 1, 0), lay_c(mod_cap + 1, 0);
-            for (int mm = 3; mm <= mod_cap; ++mm)
-                if (usable(mm, p, smax)) {
-                    use_c[mm] = 1;
-                    np_c[mm] = (int)product_terms(mm, p).size();
-                    lay_c[mm] =
-                        1000 * (int)product_groups(mm, p, maxg_for(mm, K, mod_cap, p, smax)).size() + planes_of(mm, p);
-                }
-            auto ok_c = [&](int mm) { return mm >= 3 && mm <= mod_cap && use_c[mm]; };
-            auto over = [&](double l) { return (l - need) > kTailTol ? 1 : 0; };
-            double best = logM;
-            int bp = o.m[o.m.size() - 2], bq = o.m.back();
-            int bcost = np_c[bp] + np_c[bq], blay = lay_c[bp] + lay_c[bq];
-            auto better = [&](int c, int lay, double l) {
-                if (c != bcost) return c < bcost;
-                if (over(l) != over(best)) return over(l) < over(best);
-                return lay < blay || (lay == blay && l < best);
-            };
-            bool head_even = false;
-            for (int x : head) head_even = head_even || (x % 2 == 0);
-            const int step = head_even ? 2 : 1;
-            for (int p2 = 3; p2 <= mod_cap; p2 += step) {
-                if (!ok_c(p2) || !cop_head(p2)) continue;
-                const double lp = base + std::log2((double)p2);
-                if (lp >= need && better(np_c[p2], lay_c[p2], lp)) {
-                    best = lp;
-                    bp = p2;
-                    bq = 0;
-                    bcost = np_c[p2];
-                    blay = lay_c[p2];
-                }
-                for (int q = p2 + step; q <= mod_cap; q += step) {
-                    if (!ok_c(q) || std::gcd(p2, q) != 1 || !cop_head(q)) continue;
-                    const double lq = lp + std::log2((double)q);
-                    const int c = np_c[p2] + np_c[q], lay = lay_c[p2] + lay_c[q];
-                    if (lq >= need && better(c, lay, lq)) {
-                        best = lq;
-                        bp = p2;
-                        bq = q;
-                        bcost = c;
-                        blay = lay;
-                    }
-                }
-            }
-            o.m = head;
-            o.m.push_back(bp);
-            if (bq) o.m.push_back(bq);
-            logM = best;
-        }
+        reselect_tail(o.m, logM, need, p, smax, mod_cap, K);
     }
     const int S = (int)o.m.size();
     o.ok = logM >= need && S > 0 && S <= kMaxS && S <= num_moduli && o.b > 0;
