@@ -261,6 +261,25 @@ int oztt_stats_sumsq(const double* x, uint64_t rows, uint64_t cols, int32_t mode
                      void* stream, char* err, size_t errlen);
 int oztt_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double rg, const double* v, uint64_t vstride,
                       double* out, uint64_t ostride, void* stream, char* err, size_t errlen);
+/* The sketch y_l = B g_l over a stretch of columns, for B split into column panels over several devices
+ * (no counterpart in the reference, which is single-device; it continues the sums of estimate_product_norm,
+ * src/backend/common/norm_estimate.hpp:48-73, across panels): state holds 8 x rows extended-precision sums
+ * of 16 bytes each (state[l*rows + r]); x is rows x cols with rows ldx apart, v the vectors' entries for
+ * these columns (8 rows, vstride apart). carry = 0 starts the sums, 1 continues them from state (e.g. a
+ * state received from the device holding the earlier columns). The terms are (x*rg) * v in the
+ * reference's long-double arithmetic, columns ascending. */
+int oztt_stats_sketch_chain(const double* x, uint64_t rows, uint64_t cols, uint64_t ldx, double rg, const double* v,
+                            uint64_t vstride, void* state, int32_t carry, void* stream, char* err, size_t errlen);
+/* out[i] = the extended sum state[i] rounded to double, i < count (the end of a chain). */
+int oztt_stats_sketch_round(const void* state, uint64_t count, double* out, void* stream, char* err, size_t errlen);
+/* The five statistics (TA, TB, nA, nB, nC into out5) from the per-row and per-column measurements of the
+ * whole problem, summed on the host in the reference's order (choose_precision_policy and
+ * estimate_product_norm, src/backend/ozaki2/auto_precision.hpp:24-80, common/norm_estimate.hpp:48-73):
+ * row_max / col_max the |maxima| of A's m rows and B's n columns, row_sumsq / col_sumsq their sums of
+ * (x*rg)^2, sketch_s the 8 x m sketches s_l = A y_l; rgA, rgB the power-of-two scales. Host memory. */
+int oztt_policy_stats_combine(const double* row_max, uint64_t m, const double* col_max, uint64_t n,
+                              const double* row_sumsq, const double* col_sumsq, const double* sketch_s, double rgA,
+                              double rgB, double* out5, char* err, size_t errlen);
 /* The 8 x N Gaussian vectors of the norm estimate (mt19937 seeded 12345, the reference's draw order). */
 void oztt_policy_vectors(uint32_t N, double* out);
 /* Scheme II INT8 plan from the five input statistics of the precision policy (TA, TB: sums of squared

@@ -168,6 +168,9 @@ _SIGNATURES = {
     "oztt_stats_sumsq": [_P, _U64, _U64, _I32, ctypes.c_double, _P, _P, _ERR, _SZ],
     "oztt_stats_sketch": [_P, _U64, _U64, ctypes.c_double, _P, _U64, _P, _U64, _P, _ERR, _SZ],
     "oztt_policy_vectors": [ctypes.c_uint32, _P],
+    "oztt_stats_sketch_chain": [_P, _U64, _U64, _U64, ctypes.c_double, _P, _U64, _P, _I32, _P, _ERR, _SZ],
+    "oztt_stats_sketch_round": [_P, _U64, _P, _P, _ERR, _SZ],
+    "oztt_policy_stats_combine": [_P, _U64, _P, _U64, _P, _P, _P, ctypes.c_double, ctypes.c_double, _P, _ERR, _SZ],
     "oztt_ii_int8_last_phases": [_P, _I32],
     "oztt_ii_int8_plan_from_stats": [_U64, _U64, _U64, ctypes.c_uint32, _I32, _I32, ctypes.c_double, ctypes.c_double,
                                      ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.POINTER(IIPlan), _ERR,
@@ -367,6 +370,25 @@ def ii_int8_last_phases() -> dict:
     d = {key: float(v) for key, v in zip(keys, out[:6])}
     d["bands"] = int(out[6])
     return d
+
+
+def policy_stats_combine(row_max, col_max, row_sumsq, col_sumsq, sketch_s, rgA: float,
+                         rgB: float) -> tuple[float, float, float, float, float]:
+    """(TA, TB, nA, nB, nC) from the whole problem's per-row and per-column measurements, summed in the
+    reference's order (oztt_policy_stats_combine); sketch_s is 8 x m."""
+    rm, cm = np.ascontiguousarray(row_max, np.float64), np.ascontiguousarray(col_max, np.float64)
+    r2, c2 = np.ascontiguousarray(row_sumsq, np.float64), np.ascontiguousarray(col_sumsq, np.float64)
+    sk = np.ascontiguousarray(sketch_s, np.float64)
+    m, n = rm.size, cm.size
+    if r2.size != m or c2.size != n or sk.size != 8 * m:
+        raise ValueError("policy_stats_combine: sizes do not match")
+    out = np.zeros(5)
+    err = _errbuf()
+    rc = _lib().oztt_policy_stats_combine(rm.ctypes.data, m, cm.ctypes.data, n, r2.ctypes.data, c2.ctypes.data,
+                                          sk.ctypes.data, rgA, rgB, out.ctypes.data, err, len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return tuple(float(x) for x in out)
 
 
 def ii_int8_plan_from_stats(m: int, n: int, k: int, TA: float, TB: float, nA: float, nB: float, nC: float,

@@ -154,11 +154,12 @@ __global__ void __launch_bounds__(128) col_sumsq_kernel(const double* __restrict
 // out[l][r] = (double) sum_{j < cols} ext((x[r][j]*rg)) * ext(v[l][j]), the sum in 64-bit-significand
 // arithmetic, j ascending. Thread t handles row t / 8 and vector t % 8, so a warp reads 4 rows and
 // the 8 vectors. The products are independent of the running sum, so only the additions form the
-// chain. UNSCALED: the elements enter as they are and the
-// extended-precision sums are stored (eout) for scaling later.
-// Rows of x lie ldx apart; the sum runs over `cols` columns and, UNSCALED with `carry`, continues from
+// chain. UNSCALED: the elements enter as they are. EXT_OUT: the extended-precision sums are stored
+// (eout) instead of their rounding to double -- for scaling later (UNSCALED) or for a later stretch of
+// columns, on this device or another (the tiled statistics).
+// Rows of x lie ldx apart; the sum runs over `cols` columns and, EXT_OUT with `carry`, continues from
 // eout (earlier columns).
-template <bool UNSCALED>
+template <bool UNSCALED, bool EXT_OUT = UNSCALED>
 __global__ void __launch_bounds__(128) sketch_kernel(const double* __restrict__ x, uint64_t rows, uint64_t cols,
                                                      uint64_t ldx, double rg, const double* __restrict__ rgp,
                                                      const double* __restrict__ v, uint64_t vstride,
@@ -170,7 +171,7 @@ __global__ void __launch_bounds__(128) sketch_kernel(const double* __restrict__ 
     if (rgp) rg = *rgp;
     const double* xr = x + r * ldx;
     const double* vl = v + l * vstride;
-    ext80::Ext acc = (UNSCALED && carry) ? eout[l * ostride + r] : ext80::zero();
+    ext80::Ext acc = (EXT_OUT && carry) ? eout[l * ostride + r] : ext80::zero();
     constexpr int B = kSketchBatch;
     double cx[B], cv[B], nx[B], nv[B];
 #pragma unroll
@@ -198,10 +199,17 @@ __global__ void __launch_bounds__(128) sketch_kernel(const double* __restrict__ 
             cv[u] = nv[u];
         }
     }
-    if constexpr (UNSCALED)
+    if constexpr (EXT_OUT)
         eout[l * ostride + r] = acc;
     else
         out[l * ostride + r] = ext80::to_double(acc);
+}
+
+// out[i] = the extended sum e[i] rounded to double (the end of a chain of sketch stretches).
+__global__ void __launch_bounds__(256) round_ext_kernel(const ext80::Ext* __restrict__ e, uint64_t count,
+                                                        double* __restrict__ out) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x)
+        out[i] = ext80::to_double(e[i]);
 }
 
 inline unsigned sketch_blocks(uint64_t rows) {
@@ -300,6 +308,44 @@ std::shared_ptr<const std::vector<double>> policy_vectors(uint32_t N) {
 }
 
 }  // namespace
+
+// The host's part of the statistics, in the reference's order (choose_precision_policy and
+// estimate_product_norm): TA, nA over the rows of A and TB, nB over the columns of B, each a sequential
+// sum; ||C||_F^2 from the eight sketches s_l (8 x m, l-th row at sstride*l) -- each ||s_l||^2 a
+// sequential sum -- dropping the largest, over 7, divided by 1 + 2 sqrt(2/8). The maxima are |values|
+// (their bit patterns are the ones the absmax stages write).
+PolicyStats combine_policy_stats(const double* row_max, uint64_t m, const double* col_max, uint64_t n,
+                                 const double* row_sumsq, const double* col_sumsq, const double* s, uint64_t sstride,
+                                 double rgA, double rgB) {
+    PolicyStats ps;
+    for (uint64_t r = 0; r < m; ++r) {
+        const double mx = row_max[r] * rgA;
+        if (mx > 0) {
+            const double t = std::exp2(std::ceil(std::log2(mx)));
+            ps.TA += t * t;
+        }
+        ps.nA += row_sumsq[r];
+    }
+    for (uint64_t c = 0; c < n; ++c) {
+        const double mx = col_max[c] * rgB;
+        if (mx > 0) {
+            const double t = std::exp2(std::ceil(std::log2(mx)));
+            ps.TB += t * t;
+        }
+        ps.nB += col_sumsq[c];
+    }
+    double cs2 = 0, cmx = 0;
+    for (int l = 0; l < kVectors; ++l) {
+        double q = 0;
+        const double* sv = s + (size_t)l * sstride;
+        for (uint64_t i = 0; i < m; ++i) q += sv[i] * sv[i];
+        cs2 += q;
+        cmx = std::max(cmx, q);
+    }
+    ps.nC = (cs2 - cmx) / (kVectors - 1) / (1.0 + 2.0 * std::sqrt(2.0 / (double)kVectors));
+    ps.measured = true;
+    return ps;
+}
 
 // The statistics in stages on stream st, every stage stream-ordered; collect() is the one
 // synchronisation. Chunk stages measure unscaled values; the finishing stage of
@@ -440,34 +486,9 @@ PolicyStats PolicyStatsRun::collect(std::vector<uint64_t>* row_max, std::vector<
     OZTT_CUDA(cudaMemcpyAsync(hs.data(), bufs_->ds.p, hs.size() * 8, cudaMemcpyDeviceToHost, st_));
     OZTT_CUDA(cudaStreamSynchronize(st_));
     const double rgA = rg[0], rgB = rg[1];
-    // the host's part, in the reference's order
-    PolicyStats ps;
-    for (uint64_t r = 0; r < m; ++r) {
-        const double mx = pattern_to_double(hr[r]) * rgA;
-        if (mx > 0) {
-            const double t = std::exp2(std::ceil(std::log2(mx)));
-            ps.TA += t * t;
-        }
-        ps.nA += h2r[r];
-    }
-    for (uint64_t c = 0; c < n; ++c) {
-        const double mx = pattern_to_double(hc[c]) * rgB;
-        if (mx > 0) {
-            const double t = std::exp2(std::ceil(std::log2(mx)));
-            ps.TB += t * t;
-        }
-        ps.nB += h2c[c];
-    }
-    double cs2 = 0, cmx = 0;
-    for (int l = 0; l < kVectors; ++l) {
-        double q = 0;
-        const double* sv = hs.data() + (size_t)l * m;
-        for (uint64_t i = 0; i < m; ++i) q += sv[i] * sv[i];
-        cs2 += q;
-        cmx = std::max(cmx, q);
-    }
-    ps.nC = (cs2 - cmx) / (kVectors - 1) / (1.0 + 2.0 * std::sqrt(2.0 / (double)kVectors));
-    ps.measured = true;
+    PolicyStats ps = combine_policy_stats(reinterpret_cast<const double*>(hr.data()), m,
+                                          reinterpret_cast<const double*>(hc.data()), n, h2r.data(), h2c.data(),
+                                          hs.data(), m, rgA, rgB);
     if (row_max) row_max->assign(hr.begin(), hr.end());
     if (col_max) col_max->assign(hc.begin(), hc.end());
     if (row_sumsq) *row_sumsq = h2r;
@@ -548,6 +569,50 @@ int oztt_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double rg, 
         oztt::sketch_kernel<false><<<oztt::sketch_blocks(rows), oztt::kSketchThreads, 0, st>>>(
             x, rows, cols, cols, rg, nullptr, v, vstride, out, nullptr, ostride, 0, nullptr);
         OZTT_CUDA(cudaGetLastError());
+    });
+}
+
+int oztt_stats_sketch_chain(const double* x, uint64_t rows, uint64_t cols, uint64_t ldx, double rg, const double* v,
+                            uint64_t vstride, void* state, int32_t carry, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!x || !v || !state || vstride < cols || ldx < cols) throw Error(OZTT_EINVAL, "stats_sketch_chain: bad arguments");
+        if (!rows) return;
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        auto* e = reinterpret_cast<oztt::ext80::Ext*>(state);
+        if (!cols) {
+            if (!carry) OZTT_CUDA(cudaMemsetAsync(state, 0, rows * oztt::kVectors * sizeof(oztt::ext80::Ext), st));
+            return;
+        }
+        oztt::sketch_kernel<false, true><<<oztt::sketch_blocks(rows), oztt::kSketchThreads, 0, st>>>(
+            x, rows, cols, ldx, rg, nullptr, v, vstride, nullptr, e, rows, carry ? 1 : 0, nullptr);
+        OZTT_CUDA(cudaGetLastError());
+    });
+}
+
+int oztt_stats_sketch_round(const void* state, uint64_t count, double* out, void* stream, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!state || !out) throw Error(OZTT_EINVAL, "stats_sketch_round: bad arguments");
+        if (!count) return;
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        oztt::round_ext_kernel<<<(unsigned)std::min<uint64_t>((count + 255) / 256, 1024), 256, 0, st>>>(
+            reinterpret_cast<const oztt::ext80::Ext*>(state), count, out);
+        OZTT_CUDA(cudaGetLastError());
+    });
+}
+
+int oztt_policy_stats_combine(const double* row_max, uint64_t m, const double* col_max, uint64_t n,
+                              const double* row_sumsq, const double* col_sumsq, const double* sketch_s, double rgA,
+                              double rgB, double* out5, char* err, size_t errlen) {
+    return guarded(err, errlen, [&] {
+        if (!row_max || !col_max || !row_sumsq || !col_sumsq || !sketch_s || !out5)
+            throw Error(OZTT_EINVAL, "policy_stats_combine: null argument");
+        const oztt::PolicyStats ps =
+            oztt::combine_policy_stats(row_max, m, col_max, n, row_sumsq, col_sumsq, sketch_s, m, rgA, rgB);
+        out5[0] = ps.TA;
+        out5[1] = ps.TB;
+        out5[2] = ps.nA;
+        out5[3] = ps.nB;
+        out5[4] = ps.nC;
     });
 }
 

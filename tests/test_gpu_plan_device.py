@@ -61,10 +61,12 @@ def test_context_uses_the_same_plan(oztt, oracle, cuda):
 
 
 def test_tiled_plan_on_one_rank_equals_host_plan(oztt, oracle, cuda):
-    from oztt_b200.distributed import Grid, plan_ii_int8_tiled
+    """The tiled statistics (panel measurements, the sketch chain, the host combination) on a 1 x 1 grid,
+    without torch.distributed: the plan of the host planner, byte for byte."""
+    from oztt_b200.distributed import DeviceStats, Grid, GridComm, plan_ii_int8_tiled
 
-    m, n, k = 200, 300, 160
-    a, b = oracle.gen_inputs(m, n, k, 1.0, 13)
-    A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
-    plan = plan_ii_int8_tiled(A.view(m, k), B.view(k, n), m, n, k, Grid(1, 1, 0, 0), stream=_stream())
-    assert bytes(plan) == bytes(oztt.ii_int8_plan(a, b, m, n, k))
+    for (m, n, k, phi) in [(200, 300, 160, 1.0), (77, 65, 513, 4.0)]:
+        a, b = oracle.gen_inputs(m, n, k, phi, 13)
+        A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+        plan = plan_ii_int8_tiled(GridComm(Grid(1, 1, 0, 0)), A, B, m, n, k, stats=DeviceStats(_stream()))
+        assert bytes(plan) == bytes(oztt.ii_int8_plan(a, b, m, n, k))
