@@ -384,6 +384,32 @@ int oztt_i_recon(const int32_t* diag, uint64_t mp, uint64_t np, const int32_t* d
                  int32_t p, int32_t format, double* c, uint64_t m, uint64_t n, uint64_t ldc, void* stream, char* err,
                  size_t errlen);
 
+/* ---- resident operands ----------------------------------------------------------------------------
+ * No counterpart in the reference: it rebuilds its buffers and programs on every call and keeps no operand
+ * on the device (README.md:81-85), as Context::gemm does here. For callers that multiply by the same matrix
+ * many times, a resident operand is uploaded once and keeps in HBM what the Scheme II INT8 pipeline derives
+ * from it alone: its precision-policy measurements (row or column maxima, scale, sums of squares, and for B
+ * the sketch y = B g of estimate_product_norm) and the exponent deltas and residue planes of the last two
+ * plans it was used with. A product of two resident operands makes the plan Context::gemm makes for the same
+ * values (byte for byte) and returns the same C, bit for bit; with an unchanged plan it starts at the
+ * residue GEMM. Scheme II with INT8 products only. Products on one process are serialised. */
+#define OZTT_ROLE_A 0 /* left operand, m x k */
+#define OZTT_ROLE_B 1 /* right operand, k x n */
+typedef struct oztt_resident oztt_resident;
+/* Uploads x (rows x cols, row-major; host memory, or device memory of device_id when x_on_device) as a
+ * left (OZTT_ROLE_A) or right (OZTT_ROLE_B) operand and measures it. The values are checked as the front
+ * end checks them (finiteness, the range of the nonzero row maxima of A / column maxima of B), with the
+ * same messages. */
+int oztt_resident_create(int device_id, int32_t role, const double* x, uint64_t rows, uint64_t cols,
+                         int32_t x_on_device, oztt_resident** out, char* err, size_t errlen);
+/* Frees the operand's device memory. NULL is allowed. */
+int oztt_resident_destroy(oztt_resident* r);
+/* C = A B for resident A (m x k) and B (k x n) on one device; c is m x n row-major, in host memory or (when
+ * c_on_device) device memory of that device. opt must name Scheme II and INT8 (max_moduli and
+ * reconstruction as in oztt_gemm); info (may be NULL) receives what Context::gemm reports. */
+int oztt_resident_gemm(oztt_resident* a, oztt_resident* b, double* c, int32_t c_on_device, const oztt_options* opt,
+                       oztt_info* info, char* err, size_t errlen);
+
 /* ---- kernel variants ------------------------------------------------------------------------------
  * No counterpart in the reference (it has one kernel per stage and reads no environment). Process-wide
  * switches between kernels that give identical results; the defaults (0) are the faster ones on a B200

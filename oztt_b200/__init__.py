@@ -199,15 +199,20 @@ _SIGNATURES = {
     "oztt_i_slice_cols": [_P, _U64, _U64, _U64, _P, _I32, _I32, _P, _U64, _U64, _P, _ERR, _SZ],
     "oztt_i_diag_gemm": [_P, _P, _U64, _U64, _U64, _I32, _P, _P, _ERR, _SZ],
     "oztt_i_recon": [_P, _U64, _U64, _P, _P, _I32, _I32, _P, _U64, _U64, _U64, _P, _ERR, _SZ],
+    "oztt_resident_create": [ctypes.c_int, _I32, _P, _U64, _U64, _I32, ctypes.POINTER(_P), _ERR, _SZ],
+    "oztt_resident_destroy": [_P],
+    "oztt_resident_gemm": [_P, _P, _P, _I32, ctypes.POINTER(_COptions), ctypes.POINTER(_CInfo), _ERR, _SZ],
     "oztt_set_option": [_I32, _I32, _ERR, _SZ],
     "oztt_get_option": [_I32, ctypes.POINTER(_I32)],
     "oztt_is_available": [_I32],
     "oztt_format_name": [_I32],
     "oztt_test_udiv_small": [ctypes.c_uint32, ctypes.c_uint32],
     "oztt_test_ext80_dot": [_P, _P, _U64, ctypes.c_double],
+    "oztt_test_gemm_wait_timeout": [_U64, _P, _P, _ERR, _SZ],
+    "oztt_test_scheme1_kblock": [_U64],
 }
 
-_RESTYPES = {"oztt_format_name": ctypes.c_char_p, "oztt_policy_vectors": None, "oztt_test_udiv_small": ctypes.c_uint32, "oztt_test_ext80_dot": ctypes.c_double, "oztt_ii_padded_dims": None, "oztt_eval_inputs": None,
+_RESTYPES = {"oztt_test_scheme1_kblock": None, "oztt_format_name": ctypes.c_char_p, "oztt_policy_vectors": None, "oztt_test_udiv_small": ctypes.c_uint32, "oztt_test_ext80_dot": ctypes.c_double, "oztt_ii_padded_dims": None, "oztt_eval_inputs": None,
              "oztt_eval_output_hash": ctypes.c_uint64}
 
 # Symbols declared in include/oztt_cuda.h (the tests check that the library exports each of them).
@@ -571,6 +576,73 @@ def padded_dims(m: int, n: int, k: int) -> tuple[int, int, int]:
     mp, np_, kp = _U64(), _U64(), _U64()
     _lib().oztt_ii_padded_dims(m, n, k, ctypes.byref(mp), ctypes.byref(np_), ctypes.byref(kp))
     return mp.value, np_.value, kp.value
+
+
+class ResidentMatrix:
+    """A matrix kept in HBM as the left ("A", m x k) or right ("B", k x n) operand of Scheme II INT8 products,
+    with its precision-policy measurements and the residue planes of its last two plans cached
+    (oztt_resident_*). x: row-major float64, a numpy array (host) or a CUDA tensor (device, device_id's)."""
+
+    def __init__(self, x, rows: int, cols: int, role: str = "A", device_id: int = 0):
+        self._h = None
+        if role not in ("A", "B"):
+            raise ValueError("role must be 'A' or 'B'")
+        self.role, self.rows, self.cols, self.device_id = role, rows, cols, device_id
+        on_device = hasattr(x, "data_ptr") and getattr(x, "is_cuda", False)
+        if on_device:
+            if x.numel() != rows * cols:
+                raise ValueError("matrix span sizes do not match m, n, k")
+            ptr = x.data_ptr()
+        else:
+            xv = _as_f64(x, "x")
+            if xv.size != rows * cols:
+                raise ValueError("matrix span sizes do not match m, n, k")
+            ptr = xv.ctypes.data
+        h = _P()
+        err = _errbuf()
+        rc = _lib().oztt_resident_create(device_id, 0 if role == "A" else 1, ptr, rows, cols, 1 if on_device else 0,
+                                         ctypes.byref(h), err, len(err))
+        if rc != OK:
+            _raise(rc, err.value)
+        self._h = h
+
+    def close(self) -> None:
+        if self._h is not None and _LIB is not None:
+            _LIB.oztt_resident_destroy(self._h)
+        self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def __matmul__(self, other: "ResidentMatrix") -> np.ndarray:
+        return resident_gemm(self, other)[0]
+
+
+def resident_gemm(a: ResidentMatrix, b: ResidentMatrix, c=None, options: Options | None = None):
+    """C = A B of two resident operands (Scheme II INT8; oztt_resident_gemm): returns (C, Info). c: None (a new
+    host array), a writable float64 host array of m*n, or a CUDA tensor of m*n doubles on the operands' device."""
+    opt = options or Options(format=Format.INT8)
+    m, n = a.rows, b.cols
+    on_device = c is not None and hasattr(c, "data_ptr") and getattr(c, "is_cuda", False)
+    if c is None:
+        c = np.empty(m * n, dtype=np.float64)
+    if on_device:
+        if c.numel() != m * n:
+            raise ValueError("matrix span sizes do not match m, n, k")
+        ptr = c.data_ptr()
+    else:
+        if not (isinstance(c, np.ndarray) and c.dtype == np.float64 and c.flags.c_contiguous and c.size == m * n):
+            raise ValueError("c must be a writable C-contiguous float64 array of m*n")
+        ptr = c.ctypes.data
+    co = _COptions(int(opt.scheme), int(opt.format), int(opt.slices), int(opt.max_moduli), int(opt.reconstruction))
+    ci = _CInfo()
+    err = _errbuf()
+    rc = _lib().oztt_resident_gemm(a._h, b._h, ptr, 1 if on_device else 0, ctypes.byref(co), ctypes.byref(ci), err,
+                                   len(err))
+    if rc != OK:
+        _raise(rc, err.value)
+    return c, Info(Scheme(ci.scheme), Format(ci.format), ci.slices, ci.moduli, ci.integer_bits,
+                   ci.reconstruction_passes, ci.padded_m, ci.padded_n, ci.padded_k)
 
 
 # Kernel-variant options (OZTT_OPT_* of include/oztt_cuda.h): identical results, default 0.

@@ -43,7 +43,7 @@ CXX_FLAGS_BY_SOURCE = {"planner.cpp": ["-O3", "-march=x86-64-v3"], "planner1.cpp
                        "planner_digit.cpp": ["-O3", "-march=x86-64-v3"]}
 
 CU_SOURCES = ["split.cu", "gemm_i8.cu", "recon.cu", "ii_int8.cu", "ii_digit.cu", "noalloc.cu", "scheme1.cu",
-              "stats.cu", "profile.cu", "streamed.cu", "plan1_dev.cu"]
+              "stats.cu", "profile.cu", "streamed.cu", "plan1_dev.cu", "resident.cu"]
 CPP_SOURCES = ["planner.cpp", "planner1.cpp", "planner_digit.cpp", "context.cpp", "evaluation.cpp"]
 
 

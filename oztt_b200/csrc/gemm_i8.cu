@@ -88,16 +88,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 // Waits for the phase of `parity` to complete. Gives up when another role raised the abort flag or
-// after TIMEOUT_NS (then records `code` and raises the flag). Returns true when the phase completed.
+// after limit_ns (then records `code` and raises the flag). Returns true when the phase completed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
-                                          int code) {
+                                          int code, uint64_t limit_ns = TIMEOUT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63) == 0) {
             if (*abort_flag) return false;
-            if (global_timer_ns() - t0 > TIMEOUT_NS) {
+            if (global_timer_ns() - t0 > limit_ns) {
                 atomicOr(err, code);
                 *abort_flag = 1;
                 return false;
@@ -722,6 +722,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::NUM_THREADS, 1
     }
 }
 
+// Test of the bounded wait: one CTA waits, through the GEMM's own mbar_wait, on an mbarrier that nothing
+// arrives at, with no TMA load or MMA issued, and gives up after limit_ns; the code the GEMM's epilogue
+// would record lands in *err_word. A second thread then waits (bounded) on the same barrier with the abort
+// flag raised, as the GEMM's other roles do, and must leave at once.
+__global__ void __launch_bounds__(64) wait_probe_kernel(int* err_word, uint64_t limit_ns, int* left_on_abort) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, err_word, ERR_WAIT_EPILOGUE, limit_ns);
+    __syncthreads();
+    if (threadIdx.x == 32) {
+        const bool done = mbar_wait(&bar, 0, &abort_flag, err_word, ERR_WAIT_PRODUCER, limit_ns);
+        if (!done && abort_flag) atomicAdd(left_on_abort, 1);
+    }
+}
+
 // ---- host side -------------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -742,12 +763,14 @@ static EncodeTiledFn encode_fn() {
 }
 
 // 3-D map over S planes of rows x kp int8 (K innermost), box BK x box_rows x 1, 128-byte swizzle. The
-// planes lie plane_rows x kp apart (plane_rows >= rows; a band of rows of taller planes), or rows x kp.
+// planes lie plane_rows x pitch apart (plane_rows >= rows; a band of rows of taller planes), or rows x pitch;
+// rows lie pitch apart (pitch >= kp; a window of kp columns of wider rows), or kp.
 static CUtensorMap make_plane_map(const int8_t* base, uint64_t rows, uint64_t kp, uint64_t S, uint32_t box_rows,
-                                  uint64_t plane_rows = 0) {
+                                  uint64_t plane_rows = 0, uint64_t pitch = 0) {
     CUtensorMap map;
+    const uint64_t rp = pitch ? pitch : kp;
     const cuuint64_t dims[3] = {kp, rows, S};
-    const cuuint64_t strides[2] = {kp, (plane_rows ? plane_rows : rows) * kp};
+    const cuuint64_t strides[2] = {rp, (plane_rows ? plane_rows : rows) * rp};
     const cuuint32_t box[3] = {BK, box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(base), dims, strides,
@@ -862,11 +885,18 @@ void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64
 // concatenated K of (d+1)*kp).
 // a_plane_rows: when nonzero, ap points at row r0 of A slice planes that are a_plane_rows tall, and the
 // GEMM covers the band of mp rows from there (diagonals [p][mp][np] of the band).
+// k0, kw: when kw is nonzero, the products run over the K window [k0, k0 + kw) of planes whose rows are kp
+// long (a K block of a sum too long for exact 32-bit diagonal sums); k0 and kw multiples of 128.
 void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp, int p,
-                      int32_t* out, int* err_word, cudaStream_t st, uint64_t a_plane_rows) {
+                      int32_t* out, int* err_word, cudaStream_t st, uint64_t a_plane_rows, uint64_t k0, uint64_t kw) {
     using namespace gemm;
     if (mp % BM || np % BN || kp % BK || mp == 0 || np == 0 || kp == 0)
         throw Error(OZTT_EINVAL, "diag_gemm: mp, np, kp must be positive multiples of 128, 256 and 128");
+    if (kw) {
+        if (k0 % BK || kw % BK || k0 + kw > kp) throw Error(OZTT_EINVAL, "diag_gemm: bad K window");
+        ap += k0;
+        bp += k0;
+    }
     if (a_plane_rows && a_plane_rows < mp) throw Error(OZTT_EINVAL, "diag_gemm: band taller than its planes");
     if (p < 1 || p > 64) throw Error(OZTT_EINVAL, "diag_gemm: the number of slices must be 1..64");
     if ((reinterpret_cast<uintptr_t>(ap) | reinterpret_cast<uintptr_t>(bp)) & 15)
@@ -876,9 +906,10 @@ void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t 
     EpiConst ec{};
     ec.S = (uint32_t)p;
     const bool pairs = use_pairs();
-    const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p, pairs ? pair::BM : BM, a_plane_rows);
-    const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p, pairs ? pair::BNH : BN);
-    launch_gemm<2>(ta, tb, out, mp, np, kp, (uint32_t)p, ec, err_word, st, pairs);
+    const uint64_t kext = kw ? kw : kp;
+    const CUtensorMap ta = make_plane_map(ap, mp, kext, (uint64_t)p, pairs ? pair::BM : BM, a_plane_rows, kp);
+    const CUtensorMap tb = make_plane_map(bp, np, kext, (uint64_t)p, pairs ? pair::BNH : BN, 0, kp);
+    launch_gemm<2>(ta, tb, out, mp, np, kext, (uint32_t)p, ec, err_word, st, pairs);
 }
 
 // FP8 digit products on the tensor cores: for each GEMM output u of the plan, P_u = sum_t A_(out_a+t)
@@ -939,6 +970,36 @@ void launch_digit_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t
     else
         launch_gemm<3>(ta, tb, out, mp, np, kp, (uint32_t)S, ec, err_word, st);
 }
+
+// Runs wait_probe_kernel with a limit of limit_ns and reports its outcome as the GEMM pipelines do: the
+// recorded code becomes a runtime error through check_flags.
+void check_flags(uint32_t flags, int gemm_err);
+
+}  // namespace oztt
+
+extern "C" int oztt_test_gemm_wait_timeout(uint64_t limit_ns, int32_t* code_out, void* stream, char* err,
+                                           size_t errlen) {
+    return oztt::guarded(err, errlen, [&] {
+        if (limit_ns == 0 || limit_ns > 1000000000ull) throw oztt::Error(OZTT_EINVAL, "limit must be in (0, 1 s]");
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        int* words = nullptr;
+        OZTT_CUDA(cudaMallocAsync(&words, 2 * sizeof(int), st));
+        OZTT_CUDA(cudaMemsetAsync(words, 0, 2 * sizeof(int), st));
+        oztt::gemm::wait_probe_kernel<<<1, 64, 0, st>>>(words, limit_ns, words + 1);
+        OZTT_CUDA(cudaGetLastError());
+        int host[2] = {0, 0};
+        OZTT_CUDA(cudaMemcpyAsync(host, words, sizeof host, cudaMemcpyDeviceToHost, st));
+        OZTT_CUDA(cudaFreeAsync(words, st));
+        OZTT_CUDA(cudaStreamSynchronize(st));
+        if (code_out) {
+            code_out[0] = host[0];
+            code_out[1] = host[1];
+        }
+        oztt::check_flags(0, host[0]);
+    });
+}
+
+namespace oztt {
 
 // Host model of the epilogue's division, for the CPU tests of the C ABI.
 extern "C" uint32_t oztt_test_udiv_small(uint32_t a, uint32_t d) {

@@ -237,14 +237,17 @@ struct HornerConst {
     int32_t qw;      // its exponent
 };
 
-__device__ __forceinline__ double horner_element(const int32_t* pd, uint64_t plane, const HornerConst& hc,
-                                                 int32_t g) {
+// T: int32_t diagonals (one K block), or int64_t diagonals summed over K blocks; NW words of two's
+// complement (HW = 6, or 7 for the K-blocked sums: |S| < 2^45 r^(p-1) < 2^204 for every format).
+template <typename T = int32_t, int NW = HW>
+__device__ __forceinline__ double horner_element(const T* pd, uint64_t plane, const HornerConst& hc, int32_t g) {
+    constexpr int HW = NW;
     uint32_t s[HW];
 #pragma unroll
     for (int w = 0; w < HW; ++w) s[w] = 0;
     for (int d = 0; d < hc.p; ++d) {
-        // s = s * radix + P_d  (mod 2^192)
-        const int32_t v = __ldg(pd + (uint64_t)d * plane);
+        // s = s * radix + P_d  (mod 2^(32 NW))
+        const int64_t v = (int64_t)__ldg(pd + (uint64_t)d * plane);
         uint64_t carry = 0;
 #pragma unroll
         for (int w = 0; w < HW; ++w) {
@@ -323,7 +326,8 @@ __device__ __forceinline__ double horner_element(const int32_t* pd, uint64_t pla
     return neg ? -r : r;
 }
 
-__global__ void __launch_bounds__(256) horner_kernel(const int32_t* __restrict__ pd, uint64_t mp, uint64_t np,
+template <typename T = int32_t, int NW = HW>
+__global__ void __launch_bounds__(256) horner_kernel(const T* __restrict__ pd, uint64_t mp, uint64_t np,
                                                      const int32_t* __restrict__ dA, const int32_t* __restrict__ dB,
                                                      double* __restrict__ c, uint64_t m, uint64_t n, uint64_t ldc,
                                                      const HornerConst hc) {
@@ -332,7 +336,24 @@ __global__ void __launch_bounds__(256) horner_kernel(const int32_t* __restrict__
          t += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t i = t / n, j = t - i * n;
         const int32_t g = -(__ldg(dA + i) + __ldg(dB + j));
-        c[i * ldc + j] = horner_element(pd + i * np + j, plane, hc, g);
+        c[i * ldc + j] = horner_element<T, NW>(pd + i * np + j, plane, hc, g);
+    }
+}
+
+// acc[i] += part[i] (the diagonals of one K block into their running 64-bit sums), four at a time.
+__global__ void __launch_bounds__(256) accumulate_kernel(const int32_t* __restrict__ part, int64_t* __restrict__ acc,
+                                                         uint64_t count4) {
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < count4;
+         t += (uint64_t)gridDim.x * blockDim.x) {
+        const int4 v = __ldg(reinterpret_cast<const int4*>(part) + t);
+        longlong2* a = reinterpret_cast<longlong2*>(acc) + 2 * t;
+        longlong2 lo = a[0], hi = a[1];
+        lo.x += v.x;
+        lo.y += v.y;
+        hi.x += v.z;
+        hi.y += v.w;
+        a[0] = lo;
+        a[1] = hi;
     }
 }
 
@@ -404,8 +425,10 @@ void launch_slice_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, co
     OZTT_CUDA(cudaGetLastError());
 }
 
+// pd: int32 diagonals [p][mp][np]; pd64 (instead, when not NULL): their int64 sums over K blocks.
 void launch_horner(const int32_t* pd, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB, int p,
-                   int format, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st) {
+                   int format, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st,
+                   const int64_t* pd64 = nullptr) {
     const I1Dev f = i1_dev(format);
     if (p < 1 || p > f.pmax)
         throw Error(OZTT_EINVAL, "horner: the number of slices must be 1.." + std::to_string(f.pmax));
@@ -415,9 +438,36 @@ void launch_horner(const int32_t* pd, uint64_t mp, uint64_t np, const int32_t* d
     scheme1_radix_scale(p, f.radix, hc.W, hc.qw);
     const uint64_t total = m * n;
     if (!total) return;
-    horner_kernel<<<(unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 16), 256, 0, st>>>(
-        pd, mp, np, dA, dB, c, m, n, ldc, hc);
+    const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 16);
+    if (pd64)
+        horner_kernel<int64_t, HW + 1><<<blocks, 256, 0, st>>>(pd64, mp, np, dA, dB, c, m, n, ldc, hc);
+    else
+        horner_kernel<<<blocks, 256, 0, st>>>(pd, mp, np, dA, dB, c, m, n, ldc, hc);
     OZTT_CUDA(cudaGetLastError());
+}
+
+void launch_accumulate(const int32_t* part, int64_t* acc, uint64_t count, cudaStream_t st) {
+    if (count % 4) throw Error(OZTT_EINVAL, "accumulate: count must be a multiple of 4");
+    const uint64_t c4 = count / 4;
+    if (!c4) return;
+    accumulate_kernel<<<(unsigned)std::min<uint64_t>((c4 + 255) / 256, (uint64_t)sm_count() * 16), 256, 0, st>>>(
+        part, acc, c4);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+namespace {
+uint64_t g_kblock_cap = 0;  // test hook: the largest K block (0: as exactness allows)
+}
+
+// K blocks of the diagonal products: one block over all of kp when (L+1) K dmax^2 fits the s32
+// accumulators (K the reference's padded k, to 32: the further zero columns add nothing); else blocks of
+// kb columns, a multiple of 128 with p kb dmax^2 <= 2^31 - 1, whose int32 diagonals are summed in int64.
+uint64_t scheme1_kblock(int p, uint64_t k, uint64_t kp, uint64_t d2) {
+    uint64_t kb = kp;
+    if ((uint64_t)p * round_up(k, 32) > (uint64_t)INT32_MAX / d2)
+        kb = std::max<uint64_t>(128, ((uint64_t)INT32_MAX / ((uint64_t)p * d2)) / 128 * 128);
+    if (g_kblock_cap) kb = std::min(kb, std::max<uint64_t>(128, g_kblock_cap / 128 * 128));
+    return std::min(kb, kp);
 }
 
 }  // namespace oztt
@@ -433,7 +483,24 @@ void launch_scale_cols_mode(const double* b, uint64_t k, uint64_t n, uint64_t ld
                             int32_t* delta, uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax,
                             cudaStream_t st);
 void launch_diag_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp, int p,
-                      int32_t* out, int* err_word, cudaStream_t st, uint64_t a_plane_rows = 0);
+                      int32_t* out, int* err_word, cudaStream_t st, uint64_t a_plane_rows = 0, uint64_t k0 = 0,
+                      uint64_t kw = 0);
+
+// The exact diagonal products of a band of rows_p rows (planes rows kp long; A planes a_plane_rows tall when
+// nonzero): into pd (int32) in one launch, or, K blocked, block by block into pd (int32) summed into pd64.
+void diag_products(const int8_t* ap, const int8_t* bp, uint64_t rows_p, uint64_t np, uint64_t kp, uint64_t kb,
+                   int p, int32_t* pd, int64_t* pd64, int* err_word, cudaStream_t st, uint64_t a_plane_rows) {
+    if (kb >= kp) {
+        launch_diag_gemm(ap, bp, rows_p, np, kp, p, pd, err_word, st, a_plane_rows);
+        return;
+    }
+    const uint64_t count = (uint64_t)p * rows_p * np;
+    OZTT_CUDA(cudaMemsetAsync(pd64, 0, count * 8, st));
+    for (uint64_t k0 = 0; k0 < kp; k0 += kb) {
+        launch_diag_gemm(ap, bp, rows_p, np, kp, p, pd, err_word, st, a_plane_rows, k0, std::min(kb, kp - k0));
+        launch_accumulate(pd, pd64, count, st);
+    }
+}
 
 void run_i_device(const double* a, const double* b, double* c, uint64_t m, uint64_t n, uint64_t k,
                   const oztt_i_plan& plan, cudaStream_t st, double* stage_ms) {
@@ -445,15 +512,15 @@ void run_i_device(const double* a, const double* b, double* c, uint64_t m, uint6
     if (plan.radix != (int32_t)f.radix || plan.dmax != (int32_t)f.dmax)
         throw Error(OZTT_EINVAL, "scheme I: the plan's radix and digit bound do not match its format");
     // The diagonal sums are exact in the s32 accumulators while (L+1) K dmax^2 <= 2^31 - 1 (the planner
-    // guarantees it for INT8; FP inputs beyond it would need the reference's FP32 K blocks).
+    // guarantees it for INT8, whose K blocking the reference rejects); beyond it (FP8, BF16, FP16, TF32 with
+    // a long K) the products run in K blocks summed exactly in int64, where the reference sums FP32 partial
+    // products block by block (src/ozaki1.cpp:238-262).
     const uint64_t d2 = (uint64_t)f.dmax * (uint64_t)f.dmax;
-    if ((uint64_t)p * round_up(k, 32) > (uint64_t)INT32_MAX / d2)
-        throw Error(OZTT_ERUNTIME, "Ozaki scheme I: k*slices is too large for exact 32-bit diagonal sums in this "
-                                   "build (k=" + std::to_string(k) + ", " + std::to_string(p) + " slices)");
     const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
+    const uint64_t kb = scheme1_kblock(p, k, kp, d2);
     const uint64_t P = (uint64_t)p;
     DevBuf dA(st, mp * 4), dB(st, np * 4), colmax(st, n * 8), words(st, 16);
-    DevBuf sa(st, P * mp * kp), sb(st, P * np * kp), pd(st, P * mp * np * 4);
+    DevBuf sa(st, P * mp * kp), sb(st, P * np * kp), pd(st, P * mp * np * 4), pd64(st, kb < kp ? P * mp * np * 8 : 8);
     OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
@@ -470,20 +537,23 @@ void run_i_device(const double* a, const double* b, double* c, uint64_t m, uint6
            [&] { launch_slice_rows(a, m, k, k, dA.as<int32_t>(), p, format, sa.as<int8_t>(), mp, kp, st); });
     pl.add(kSlice, kHead, 2,
            [&] { launch_slice_cols(b, k, n, n, dB.as<int32_t>(), p, format, sb.as<int8_t>(), np, kp, st); });
-    pl.add(kGemm, kGemmStep, 3,
-           [&] { launch_diag_gemm(sa.as<int8_t>(), sb.as<int8_t>(), mp, np, kp, p, pd.as<int32_t>(), gemm_err, st); });
+    int64_t* wide = kb < kp ? pd64.as<int64_t>() : nullptr;
+    pl.add(kGemm, kGemmStep, 3, [&] {
+        diag_products(sa.as<int8_t>(), sb.as<int8_t>(), mp, np, kp, kb, p, pd.as<int32_t>(), wide, gemm_err, st, 0);
+    });
     pl.add(kRecon, kReconStep, 4, [&] {
-        launch_horner(pd.as<int32_t>(), mp, np, dA.as<int32_t>(), dB.as<int32_t>(), p, format, c, m, n, n, st);
+        launch_horner(pd.as<int32_t>(), mp, np, dA.as<int32_t>(), dB.as<int32_t>(), p, format, c, m, n, n, st, wide);
     });
     pl.writes(dA.p, mp * 4);
     pl.writes(dB.p, np * 4);
     pl.writes(sa.p, P * mp * kp);
     pl.writes(sb.p, P * np * kp);
     pl.writes(pd.p, P * mp * np * 4);
+    if (wide) pl.writes(pd64.p, P * mp * np * 8);
     pl.writes(c, m * n * 8);
     pl.out = c;
     pl.out_bytes = m * n * 8;
-    pl.partial_products = (unsigned)(P * (P + 1) / 2);
+    pl.partial_products = (unsigned)(P * (P + 1) / 2 * ((kp + kb - 1) / kb));
     if (!run_profiled(pl, st)) pl.run(st, stage_ms, 5);
     uint32_t host_words[2] = {0, 0};
     OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
@@ -515,6 +585,10 @@ void run_i_host(int device_id, const double* a, const double* b, double* c, uint
 
 using oztt::Error;
 using oztt::guarded;
+
+// Test hook: caps the K blocks of the Scheme I diagonal products at kb columns (0: only as exactness
+// requires), so that the blocked path can be checked against the unblocked one at small sizes.
+extern "C" void oztt_test_scheme1_kblock(uint64_t kb) { oztt::g_kblock_cap = kb; }
 
 extern "C" {
 
@@ -649,16 +723,15 @@ static int run_i_streamed_impl(int device_id, int32_t format, const double* a, c
         throw Error(OZTT_EINVAL, "scheme I: the number of slices must be 1.." + std::to_string(f.pmax) +
                                      " for radix " + std::to_string(f.radix));
     const uint64_t d2 = (uint64_t)f.dmax * (uint64_t)f.dmax;
-    if ((uint64_t)p * round_up(k, 32) > (uint64_t)INT32_MAX / d2)
-        throw Error(OZTT_ERUNTIME, "Ozaki scheme I: k*slices is too large for exact 32-bit diagonal sums in this "
-                                   "build (k=" + std::to_string(k) + ", " + std::to_string(p) + " slices)");
     const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128), P = (uint64_t)p;
+    const uint64_t kb = scheme1_kblock(p, k, kp, d2);
     const uint64_t bands = std::min<uint64_t>(8, std::max<uint64_t>(1, mp / 2048));
     const uint64_t bm = round_up((mp + bands - 1) / bands, 128);
     const double *da = call.a_dev(), *db = call.b_dev();
     double* dc = call.c_dev();
     DevBuf dA(st, mp * 4), dB(st, np * 4), colmax(st, n * 8), words(st, 16);
-    DevBuf sa(st, P * mp * kp), sb(st, P * np * kp), pd(st, P * bm * np * 4);
+    DevBuf sa(st, P * mp * kp), sb(st, P * np * kp), pd(st, P * bm * np * 4), pd64(st, kb < kp ? P * bm * np * 8 : 8);
+    int64_t* wide = kb < kp ? pd64.as<int64_t>() : nullptr;
     OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
@@ -669,12 +742,12 @@ static int run_i_streamed_impl(int device_id, int32_t format, const double* a, c
     launch_slice_cols(db, k, n, n, dB.as<int32_t>(), p, format, sb.as<int8_t>(), np, kp, st);
     for (uint64_t r0 = 0; r0 < mp; r0 += bm) {
         const uint64_t rows_p = std::min(bm, mp - r0);
-        launch_diag_gemm(sa.as<int8_t>() + r0 * kp, sb.as<int8_t>(), rows_p, np, kp, p, pd.as<int32_t>(), gemm_err,
-                         st, mp);
+        diag_products(sa.as<int8_t>() + r0 * kp, sb.as<int8_t>(), rows_p, np, kp, kb, p, pd.as<int32_t>(), wide,
+                      gemm_err, st, mp);
         if (r0 >= m) continue;
         const uint64_t rows = std::min(m, r0 + rows_p) - r0;
         launch_horner(pd.as<int32_t>(), rows_p, np, dA.as<int32_t>() + r0, dB.as<int32_t>(), p, format, dc + r0 * n,
-                      rows, n, n, st);
+                      rows, n, n, st, wide);
         call.band_done(r0, rows);
     }
     call.read_back(c);

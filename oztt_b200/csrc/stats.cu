@@ -500,6 +500,51 @@ PolicyStats PolicyStatsRun::collect(std::vector<uint64_t>* row_max, std::vector<
     return ps;
 }
 
+// The statistics stages on one whole matrix (x: rows x cols, row-major), as the C ABI and the resident
+// operands use them: |maxima| per row (mode 0) or column (mode 1), scaled sums of squares, the sketch.
+void launch_stats_absmax(const double* x, uint64_t rows, uint64_t cols, int mode, double* out, cudaStream_t st) {
+    if (!rows || !cols) return;
+    int dev = 0, sms = 148;
+    OZTT_CUDA(cudaGetDevice(&dev));
+    OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    auto* o = reinterpret_cast<unsigned long long*>(out);  // nonnegative doubles order like their patterns
+    if (mode == 0) {
+        row_absmax_kernel<<<(unsigned)std::min<uint64_t>((rows + 7) / 8, (uint64_t)sms * 32), 256, 0, st>>>(
+            x, rows, cols, cols, o, 0);
+    } else {
+        OZTT_CUDA(cudaMemsetAsync(out, 0, cols * 8, st));
+        const uint64_t col_blocks = (cols + 255) / 256;
+        const uint64_t want = std::max<uint64_t>(1, (uint64_t)sms * 8 / std::max<uint64_t>(col_blocks, 1));
+        const uint64_t chunks = std::min<uint64_t>(std::min<uint64_t>(want, rows), 65535);
+        const uint64_t rpc = (rows + chunks - 1) / chunks;
+        col_absmax_kernel<<<dim3((unsigned)col_blocks, (unsigned)((rows + rpc - 1) / rpc)), 256, 0, st>>>(
+            x, rows, cols, cols, rpc, o);
+    }
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void launch_stats_sumsq(const double* x, uint64_t rows, uint64_t cols, int mode, double rg, double* out,
+                        cudaStream_t st) {
+    if (!rows || !cols) return;
+    if (mode == 0)
+        row_sumsq_kernel<<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(x, rows, cols, cols, rg, nullptr, out, 0,
+                                                                         nullptr, nullptr);
+    else
+        col_sumsq_kernel<<<(unsigned)((cols + 127) / 128), 128, 0, st>>>(x, rows, cols, cols, rg, nullptr, out, 0,
+                                                                         nullptr, nullptr);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void launch_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double rg, const double* v, uint64_t vstride,
+                         double* out, uint64_t ostride, cudaStream_t st) {
+    if (!rows) return;
+    sketch_kernel<false><<<sketch_blocks(rows), kSketchThreads, 0, st>>>(x, rows, cols, cols, rg, nullptr, v, vstride,
+                                                                        out, nullptr, ostride, 0, nullptr);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+std::vector<double> policy_vectors_host(uint32_t N) { return *policy_vectors(N); }
+
 PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
                                 cudaStream_t st) {
     PolicyStatsRun run(m, n, k, N, st);
@@ -522,25 +567,7 @@ int oztt_stats_absmax(const double* x, uint64_t rows, uint64_t cols, int32_t mod
                       char* err, size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!x || !out || (mode != 0 && mode != 1)) throw Error(OZTT_EINVAL, "stats_absmax: bad arguments");
-        if (!rows || !cols) return;
-        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-        int dev = 0, sms = 148;
-        OZTT_CUDA(cudaGetDevice(&dev));
-        OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        auto* o = reinterpret_cast<unsigned long long*>(out);  // nonnegative doubles order like their patterns
-        if (mode == 0) {
-            oztt::row_absmax_kernel<<<(unsigned)std::min<uint64_t>((rows + 7) / 8, (uint64_t)sms * 32), 256, 0, st>>>(
-                x, rows, cols, cols, o, 0);
-        } else {
-            OZTT_CUDA(cudaMemsetAsync(out, 0, cols * 8, st));
-            const uint64_t col_blocks = (cols + 255) / 256;
-            const uint64_t want = std::max<uint64_t>(1, (uint64_t)sms * 8 / std::max<uint64_t>(col_blocks, 1));
-            const uint64_t chunks = std::min<uint64_t>(std::min<uint64_t>(want, rows), 65535);
-            const uint64_t rpc = (rows + chunks - 1) / chunks;
-            oztt::col_absmax_kernel<<<dim3((unsigned)col_blocks, (unsigned)((rows + rpc - 1) / rpc)), 256, 0, st>>>(
-                x, rows, cols, cols, rpc, o);
-        }
-        OZTT_CUDA(cudaGetLastError());
+        oztt::launch_stats_absmax(x, rows, cols, mode, out, reinterpret_cast<cudaStream_t>(stream));
     });
 }
 
@@ -548,15 +575,7 @@ int oztt_stats_sumsq(const double* x, uint64_t rows, uint64_t cols, int32_t mode
                      void* stream, char* err, size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!x || !out || (mode != 0 && mode != 1)) throw Error(OZTT_EINVAL, "stats_sumsq: bad arguments");
-        if (!rows || !cols) return;
-        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-        if (mode == 0)
-            oztt::row_sumsq_kernel<<<(unsigned)((rows + 127) / 128), 128, 0, st>>>(x, rows, cols, cols, rg, nullptr,
-                                                                                  out, 0, nullptr, nullptr);
-        else
-            oztt::col_sumsq_kernel<<<(unsigned)((cols + 127) / 128), 128, 0, st>>>(x, rows, cols, cols, rg, nullptr,
-                                                                                  out, 0, nullptr, nullptr);
-        OZTT_CUDA(cudaGetLastError());
+        oztt::launch_stats_sumsq(x, rows, cols, mode, rg, out, reinterpret_cast<cudaStream_t>(stream));
     });
 }
 
@@ -564,11 +583,7 @@ int oztt_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double rg, 
                       double* out, uint64_t ostride, void* stream, char* err, size_t errlen) {
     return guarded(err, errlen, [&] {
         if (!x || !v || !out || vstride < cols || ostride < rows) throw Error(OZTT_EINVAL, "stats_sketch: bad arguments");
-        if (!rows) return;
-        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-        oztt::sketch_kernel<false><<<oztt::sketch_blocks(rows), oztt::kSketchThreads, 0, st>>>(
-            x, rows, cols, cols, rg, nullptr, v, vstride, out, nullptr, ostride, 0, nullptr);
-        OZTT_CUDA(cudaGetLastError());
+        oztt::launch_stats_sketch(x, rows, cols, rg, v, vstride, out, ostride, reinterpret_cast<cudaStream_t>(stream));
     });
 }
 
