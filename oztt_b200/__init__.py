@@ -368,12 +368,15 @@ def policy_vectors(N: int) -> np.ndarray:
 def ii_int8_last_phases() -> dict:
     """Host wall-clock phases (ms) of the last INT8 Scheme II call through Context.gemm in this process
     (oztt_ii_int8_last_phases): upload, statistics read-back, value checks from the measured maxima, plan,
-    pipeline with the banded read-back of C, total, and the number of row bands."""
-    out = np.zeros(7, dtype=np.float64)
-    _lib().oztt_ii_int8_last_phases(out.ctypes.data, 7)
+    pipeline with the banded read-back of C, total, the number of row bands, and, on the path that overlaps
+    the GEMM with A's upload, when the first plan was made and whether the complete statistics replanned."""
+    out = np.zeros(9, dtype=np.float64)
+    _lib().oztt_ii_int8_last_phases(out.ctypes.data, 9)
     keys = ("upload_ms", "stats_ms", "check_ms", "plan_ms", "pipeline_ms", "total_ms")
     d = {key: float(v) for key, v in zip(keys, out[:6])}
     d["bands"] = int(out[6])
+    d["first_plan_ms"] = float(out[7])
+    d["replanned"] = int(out[8])
     return d
 
 

@@ -262,6 +262,100 @@ int run_ii_int8_streamed_impl(int device_id, const double* a, const double* b, d
     return OZTT_OK;
 }
 
+// ---- the call from host buffers with the GEMM overlapping A's upload --------------------------------------
+//
+// B goes up first in blocks of columns, its statistics measured as each block lands (as before); A then goes
+// up in bands of rows. The plan needs statistics of the whole A, which exist only after its last band, so
+// the pipeline starts on a plan made from B's statistics and A's first band (the precision decision depends
+// on ratios of the statistics -- sqrt((TA nB + TB nA) / 12 nC) -- which a band of rows estimates closely),
+// each band's GEMM and reconstruction following its arrival. When A has landed, its statistics are finished,
+// the values are checked, and the reference's plan is made from the complete statistics; if its moduli and
+// width equal the first plan's, C is already the result of the reference's plan and is read back band by
+// band; otherwise the pipeline runs again with it. Nothing is written to the caller's C before every value
+// has been checked, so C may alias A or B and an invalid input leaves C untouched, as the front end requires.
+int run_ii_int8_overlapped(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
+                           uint64_t k, uint32_t max_moduli, int32_t reconstruction,
+                           const std::function<void(const uint64_t*, const uint64_t*)>& check, oztt_ii_plan& p,
+                           std::string& err) {
+    StreamedCall call(device_id, a, b, m, n, k);
+    StreamedPhases& ph = call.phases();
+    cudaStream_t st = call.work();
+    const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
+    const uint64_t bands = std::min<uint64_t>(8, std::max<uint64_t>(1, mp / 2048));
+    const uint64_t bm = round_up((mp + bands - 1) / bands, 128);
+    // uploads: B by column blocks with its statistics, then A by bands of rows with theirs
+    call.upload_b();
+    const std::vector<cudaEvent_t> landed = call.upload_a_rows(bm);
+    // the first plan: B's statistics and those of A's first band
+    const uint64_t m0 = std::min(bm, m);
+    PolicyStats first = call.band_stats(0, m0, landed[0]);
+    ph.first_plan_ms = call.ms_since_start();
+    oztt_ii_plan p0{};
+    std::string err0;
+    const int rc0 = plan_ii_int8_with([&](uint32_t, uint32_t) { return first; }, m, n, k, max_moduli, reconstruction, 0,
+                                      p0, err0);
+    const double *da = call.a_dev(), *db = call.b_dev();
+    double* dc = call.c_dev();
+    DevBuf dA(st, mp * 4), dB(st, np * 4), colmax(st, n * 8), words(st, 16);
+    OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
+    uint32_t* flags = words.as<uint32_t>();
+    int* gemm_err = words.as<int>() + 1;
+    std::unique_ptr<DevBuf> rb, ra, kpl;
+    auto pipeline = [&](const oztt_ii_plan& q, bool wait_bands) {
+        const uint64_t S = (uint64_t)q.S;
+        rb = std::make_unique<DevBuf>(st, S * np * kp);
+        ra = std::make_unique<DevBuf>(st, S * bm * kp);
+        kpl = std::make_unique<DevBuf>(st, S * bm * np);
+        launch_scale_cols(db, k, n, n, q.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
+        launch_split_cols(db, k, n, n, dB.as<int32_t>(), q, rb->as<int8_t>(), np, kp, st);
+        for (uint64_t bi = 0, r0 = 0; r0 < mp; ++bi, r0 += bm) {
+            const uint64_t rows_p = std::min(bm, mp - r0);
+            const uint64_t rows = r0 < m ? std::min(m, r0 + rows_p) - r0 : 0;
+            if (wait_bands && bi < landed.size()) OZTT_CUDA(cudaStreamWaitEvent(st, landed[bi], 0));
+            if (rows) {
+                launch_scale_rows(da + r0 * k, rows, k, k, q.shift, dA.as<int32_t>() + r0, nullptr, flags, st);
+                launch_split_rows(da + r0 * k, rows, k, k, dA.as<int32_t>() + r0, q, ra->as<int8_t>(), rows_p, kp, st);
+            } else {
+                OZTT_CUDA(cudaMemsetAsync(ra->p, 0, S * rows_p * kp, st));
+            }
+            launch_residue_gemm(ra->as<int8_t>(), rb->as<int8_t>(), rows_p, np, kp, q, 1, kpl->p, gemm_err, st, 0);
+            if (!rows) continue;
+            launch_recon(kpl->as<uint8_t>(), rows_p, np, dA.as<int32_t>() + r0, dB.as<int32_t>(), q, dc + r0 * n, rows,
+                         n, n, st);
+            call.band_done(r0, rows);
+        }
+    };
+    if (rc0 == OZTT_OK) {
+        check_plan(p0);
+        pipeline(p0, true);
+    }
+    // the complete statistics, the checks of every value, the reference's plan
+    std::vector<uint64_t> row_max, col_max;
+    const PolicyStats ps = call.finish_stats(row_max, col_max);
+    double t = call.ms_since_start();
+    check(row_max.data(), col_max.data());
+    ph.check_ms = call.ms_since_start() - t;
+    t = call.ms_since_start();
+    const int rc = plan_ii_int8_with([&](uint32_t, uint32_t) { return ps; }, m, n, k, max_moduli, reconstruction, 0, p,
+                                     err);
+    if (rc != OZTT_OK) return rc;
+    ph.plan_ms = call.ms_since_start() - t;
+    const bool same = rc0 == OZTT_OK && p0.S == p.S && p0.b == p.b && p0.nd == p.nd && p0.shift == p.shift &&
+                      std::equal(p0.moduli, p0.moduli + p0.S, p.moduli);
+    ph.replanned = same ? 0 : 1;
+    if (!same) {  // the first plan was not the reference's: again, with the reference's plan
+        call.discard_bands();
+        check_plan(p);
+        pipeline(p, false);
+    }
+    call.read_back(c);
+    uint32_t host_words[2] = {0, 0};
+    OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
+    call.finish(ph.first_plan_ms);
+    check_flags(host_words[0], (int)host_words[1]);
+    return OZTT_OK;
+}
+
 }  // namespace
 
 int run_ii_int8_streamed(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
@@ -271,7 +365,12 @@ int run_ii_int8_streamed(int device_id, const double* a, const double* b, double
     char buf[1024];
     int inner = OZTT_OK;
     const int rc = guarded(buf, sizeof buf, [&] {
-        inner = run_ii_int8_streamed_impl(device_id, a, b, c, m, n, k, max_moduli, reconstruction, check, p, err);
+        // at least two bands of A's rows: the GEMM overlaps A's upload (a first plan from B and A's first band,
+        // confirmed by the complete statistics); smaller calls upload everything first
+        if (round_up(m, 128) >= 4096)
+            inner = run_ii_int8_overlapped(device_id, a, b, c, m, n, k, max_moduli, reconstruction, check, p, err);
+        else
+            inner = run_ii_int8_streamed_impl(device_id, a, b, c, m, n, k, max_moduli, reconstruction, check, p, err);
     });
     if (rc != OZTT_OK) err = buf;
     return rc != OZTT_OK ? rc : inner;

@@ -199,6 +199,8 @@ struct StreamedPhases {
     double pipeline_ms = 0;    // scale, split, banded GEMM and reconstruction, C read back
     double total_ms = 0;
     int bands = 0;
+    double first_plan_ms = 0;  // overlapped INT8 path: when the first plan (B and A's first band) was made
+    int replanned = 0;         // 1 if the complete statistics gave another plan and the pipeline ran again
 };
 StreamedPhases last_streamed_phases();
 

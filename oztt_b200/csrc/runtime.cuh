@@ -102,7 +102,18 @@ public:
     void b_done(const double* b);  // B's scale, then its sums and y = B g scaled
     // the same for columns c0 .. c1-1 of all rows of A (a: the whole row-major A), after b_done
     void a_cols(const double* a, uint64_t c0, uint64_t c1);
+    // or for rows r0 .. r1-1 of A, whole rows (bands in any order, together covering every row), after b_done
+    void a_rows(const double* a, uint64_t r0, uint64_t r1);
     void a_done(const double* a);
+    // B's finished parts on the device, valid on st after b_done: the magnitude patterns of its column
+    // maxima, its scaled column sums of squares, its scale (one double) and the sketch y (8 x k doubles)
+    struct BParts {
+        const unsigned long long* col_max;
+        const double* col_sumsq;
+        const double* rgB;
+        const double* y;
+    };
+    BParts b_parts() const;
     // row_max / col_max, when given, receive the magnitude patterns of A's row and B's column maxima;
     // row_sumsq / col_sumsq the scaled squared norms of A's rows and B's columns; rg the scales of A and B
     PolicyStats collect(std::vector<uint64_t>* row_max = nullptr, std::vector<uint64_t>* col_max = nullptr,
@@ -142,6 +153,18 @@ public:
     // waits for everything (the read-back included) and records the phases of the call, the pipeline
     // counted from pipeline_start_ms (ms_since_start when it was issued)
     void finish(double pipeline_start_ms);
+    // The upload in two parts, for the INT8 path that overlaps the GEMM with A's upload: B in blocks of
+    // columns with its statistics, then A in bands of band_rows rows, each band's statistics measured as it
+    // lands (on a statistics stream of their own); returns the events that mark each band's arrival.
+    void upload_b();
+    std::vector<cudaEvent_t> upload_a_rows(uint64_t band_rows);
+    // The statistics of the problem with A's rows r0 .. r1-1 standing for the whole A (B's complete), once
+    // that band has landed (`landed`): the estimate a first plan is made from. Synchronises the work stream.
+    PolicyStats band_stats(uint64_t r0, uint64_t r1, cudaEvent_t landed);
+    // after upload_a_rows: A's finishing stages; the complete statistics and the maxima, as upload() returns
+    PolicyStats finish_stats(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max);
+    // forgets the bands marked so far (their C is recomputed)
+    void discard_bands() { bands_.clear(); }
     StreamedPhases& phases() { return phases_; }
     double ms_since_start() const;
     StreamedCall(const StreamedCall&) = delete;
@@ -157,7 +180,8 @@ private:
     const double *a_, *b_;
     uint64_t m_, n_, k_;
     std::chrono::steady_clock::time_point t0_;
-    cudaStream_t work_ = nullptr, up_ = nullptr, down_ = nullptr;
+    cudaStream_t work_ = nullptr, up_ = nullptr, down_ = nullptr, stat_ = nullptr;
+    cudaEvent_t b_ready_ = nullptr, a_last_ = nullptr;
     std::vector<cudaEvent_t> events_;
     std::vector<Band> bands_;
     std::unique_ptr<DevBuf> da_, db_, dc_;

@@ -451,6 +451,31 @@ void PolicyStatsRun::a_cols(const double* a, uint64_t c0, uint64_t c1) {
     OZTT_CUDA(cudaGetLastError());
 }
 
+void PolicyStatsRun::a_rows(const double* a, uint64_t r0, uint64_t r1) {
+    if (r1 <= r0) return;
+    const uint64_t rows = r1 - r0;
+    const double* ab = a + r0 * k_;
+    // whole rows: the maxima, the unscaled sums of squares and the unscaled sketch sums of these rows are
+    // complete in one pass each (the same sequential sums as a_cols over all column blocks)
+    row_absmax_kernel<<<(unsigned)std::min<uint64_t>((rows + 7) / 8, (uint64_t)sms_ * 32), 256, 0, st_>>>(
+        ab, rows, k_, k_, bufs_->rmax.as<unsigned long long>() + r0, 0);
+    OZTT_CUDA(cudaGetLastError());
+    row_sumsq_kernel<<<(unsigned)((rows + 127) / 128), 128, 0, st_>>>(ab, rows, k_, k_, 1.0, nullptr,
+                                                                     bufs_->s2r.as<double>() + r0, 0, bufs_->tiny_a(),
+                                                                     nullptr);
+    OZTT_CUDA(cudaGetLastError());
+    sketch_kernel<true><<<sketch_blocks(rows), kSketchThreads, 0, st_>>>(ab, rows, k_, k_, 1.0, nullptr,
+                                                                        bufs_->dy.as<double>(), k_, nullptr,
+                                                                        bufs_->es.as<ext80::Ext>() + r0, m_, 0,
+                                                                        nullptr);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+PolicyStatsRun::BParts PolicyStatsRun::b_parts() const {
+    return {bufs_->cmax.as<unsigned long long>(), bufs_->s2c.as<double>(), bufs_->rg.as<double>() + 1,
+            bufs_->dy.as<double>()};
+}
+
 void PolicyStatsRun::a_done(const double* a) {
     double* rgA = bufs_->rg.as<double>();
     const uint32_t* tiny = bufs_->tiny_a();

@@ -11,6 +11,7 @@
 // The statistics left after the upload are those of the last block of A, so the plan can be made as
 // soon as the upload ends; the values are checked from the measured maxima before that.
 #include <chrono>
+#include <cmath>
 #include <mutex>
 
 #include "oztt_common.cuh"
@@ -18,6 +19,15 @@
 #include "runtime.cuh"
 
 namespace oztt {
+
+void launch_stats_absmax(const double* x, uint64_t rows, uint64_t cols, int mode, double* out, cudaStream_t st);
+void launch_stats_sumsq(const double* x, uint64_t rows, uint64_t cols, int mode, double rg, double* out,
+                        cudaStream_t st);
+void launch_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double rg, const double* v, uint64_t vstride,
+                         double* out, uint64_t ostride, cudaStream_t st);
+PolicyStats combine_policy_stats(const double* row_max, uint64_t m, const double* col_max, uint64_t n,
+                                 const double* row_sumsq, const double* col_sumsq, const double* s, uint64_t sstride,
+                                 double rgA, double rgB);
 
 namespace {
 StreamedPhases g_last_phases;
@@ -39,7 +49,7 @@ StreamedCall::StreamedCall(int device_id, const double* a, const double* b, uint
 }
 
 StreamedCall::~StreamedCall() {
-    for (cudaStream_t s : {up_, down_, work_})
+    for (cudaStream_t s : {up_, down_, stat_, work_})
         if (s) cudaStreamSynchronize(s);
     // the buffers go back to the pool on the work stream, after everything that used them
     stats_.reset();
@@ -47,7 +57,7 @@ StreamedCall::~StreamedCall() {
     da_.reset();
     db_.reset();
     for (cudaEvent_t e : events_) cudaEventDestroy(e);
-    for (cudaStream_t s : {up_, down_, work_})
+    for (cudaStream_t s : {up_, down_, stat_, work_})
         if (s) {
             cudaStreamSynchronize(s);
             cudaStreamDestroy(s);
@@ -102,6 +112,78 @@ PolicyStats StreamedCall::upload(std::vector<uint64_t>& row_max, std::vector<uin
     OZTT_CUDA(cudaEventSynchronize(uploaded));
     phases_.upload_ms = ms_since_start();
     const PolicyStats ps = stats_->collect(&row_max, &col_max, row_sumsq, col_sumsq, rg);
+    phases_.stats_ms = ms_since_start() - phases_.upload_ms;
+    return ps;
+}
+
+void StreamedCall::upload_b() {
+    const uint32_t N = (uint32_t)round_up(n_, 64);  // the planners' padded width
+    OZTT_CUDA(cudaStreamCreateWithFlags(&stat_, cudaStreamNonBlocking));
+    order(work_, stat_);  // the operand buffers before the statistics buffers and stages
+    stats_ = std::make_unique<PolicyStatsRun>(m_, n_, k_, N, stat_);
+    order(stat_, up_);  // every allocation before the first copy
+    double* db = db_->as<double>();
+    const uint64_t cols_b = std::min<uint64_t>(n_, std::max<uint64_t>(512, kUploadChunkBytes / (8 * k_)));
+    for (uint64_t c0 = 0; c0 < n_; c0 += cols_b) {
+        const uint64_t w = std::min(cols_b, n_ - c0);
+        OZTT_CUDA(cudaMemcpy2DAsync(db + c0, n_ * 8, b_ + c0, n_ * 8, w * 8, k_, cudaMemcpyHostToDevice, up_));
+        order(up_, stat_);
+        stats_->b_cols(db, c0, c0 + w);
+    }
+    stats_->b_done(db);
+    b_ready_ = mark(stat_);
+}
+
+std::vector<cudaEvent_t> StreamedCall::upload_a_rows(uint64_t band_rows) {
+    std::vector<cudaEvent_t> landed;
+    double* da = da_->as<double>();
+    for (uint64_t r0 = 0; r0 < m_; r0 += band_rows) {
+        const uint64_t rows = std::min(band_rows, m_ - r0);
+        OZTT_CUDA(cudaMemcpyAsync(da + r0 * k_, a_ + r0 * k_, rows * k_ * 8, cudaMemcpyHostToDevice, up_));
+        landed.push_back(order(up_, stat_));
+        stats_->a_rows(da, r0, r0 + rows);
+    }
+    a_last_ = landed.back();
+    return landed;
+}
+
+PolicyStats StreamedCall::band_stats(uint64_t r0, uint64_t r1, cudaEvent_t landed) {
+    OZTT_CUDA(cudaStreamWaitEvent(work_, b_ready_, 0));
+    OZTT_CUDA(cudaStreamWaitEvent(work_, landed, 0));
+    const uint64_t rows = r1 - r0;
+    const double* ab = da_->as<double>() + r0 * k_;
+    const PolicyStatsRun::BParts bp = stats_->b_parts();
+    DevBuf mx(work_, rows * 8), s2(work_, rows * 8), sk(work_, 8 * rows * 8);
+    std::vector<double> hmax(rows), hs2(rows), hsk(8 * rows), cmax(n_), cs2(n_);
+    double rgB = 1.0;
+    launch_stats_absmax(ab, rows, k_, 0, mx.as<double>(), work_);
+    OZTT_CUDA(cudaMemcpyAsync(hmax.data(), mx.p, rows * 8, cudaMemcpyDeviceToHost, work_));
+    OZTT_CUDA(cudaMemcpyAsync(cmax.data(), bp.col_max, n_ * 8, cudaMemcpyDeviceToHost, work_));
+    OZTT_CUDA(cudaMemcpyAsync(cs2.data(), bp.col_sumsq, n_ * 8, cudaMemcpyDeviceToHost, work_));
+    OZTT_CUDA(cudaMemcpyAsync(&rgB, bp.rgB, 8, cudaMemcpyDeviceToHost, work_));
+    OZTT_CUDA(cudaStreamSynchronize(work_));
+    double top = 0;
+    for (double v : hmax) top = std::max(top, v);
+    double rgA = 1.0;
+    if (top > 0 && std::isfinite(top)) {
+        int e = 0;
+        std::frexp(top, &e);
+        rgA = std::ldexp(1.0, -std::min(std::max(e, -1000), 1000));
+    }
+    launch_stats_sumsq(ab, rows, k_, 0, rgA, s2.as<double>(), work_);
+    launch_stats_sketch(ab, rows, k_, rgA, bp.y, k_, sk.as<double>(), rows, work_);
+    OZTT_CUDA(cudaMemcpyAsync(hs2.data(), s2.p, rows * 8, cudaMemcpyDeviceToHost, work_));
+    OZTT_CUDA(cudaMemcpyAsync(hsk.data(), sk.p, hsk.size() * 8, cudaMemcpyDeviceToHost, work_));
+    OZTT_CUDA(cudaStreamSynchronize(work_));
+    return combine_policy_stats(hmax.data(), rows, cmax.data(), n_, hs2.data(), cs2.data(), hsk.data(), rows, rgA,
+                                rgB);
+}
+
+PolicyStats StreamedCall::finish_stats(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max) {
+    stats_->a_done(da_->as<double>());
+    OZTT_CUDA(cudaEventSynchronize(a_last_));
+    phases_.upload_ms = ms_since_start();
+    const PolicyStats ps = stats_->collect(&row_max, &col_max);
     phases_.stats_ms = ms_since_start() - phases_.upload_ms;
     return ps;
 }
