@@ -215,8 +215,8 @@ int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* 
  * this process, out[0..count-1] of: upload (to the end of the last host-to-device copy), statistics
  * read-back after it, value checks from the measured maxima, plan, pipeline with the banded read-back of C,
  * total, number of row bands, and (calls of at least 4096 rows, whose GEMM overlaps A's upload) the time
- * the first plan was made and 1 if the complete statistics gave another plan. Zeros before the first
- * such call. */
+ * the first plan was made, 1 if the complete statistics gave another plan, and 1 if the bounds of the
+ * statistics left a decision open so that A's exact sums were computed. Zeros before the first such call. */
 int oztt_ii_int8_last_phases(double* out, int32_t count);
 
 /* Scheme I INT8 plan (plan_issue and the slice count of src/backend/ozaki1/plan.hpp:128-250 and

@@ -264,15 +264,20 @@ int run_ii_int8_streamed_impl(int device_id, const double* a, const double* b, d
 
 // ---- the call from host buffers with the GEMM overlapping A's upload --------------------------------------
 //
-// B goes up first in blocks of columns, its statistics measured as each block lands (as before); A then goes
-// up in bands of rows. The plan needs statistics of the whole A, which exist only after its last band, so
-// the pipeline starts on a plan made from B's statistics and A's first band (the precision decision depends
-// on ratios of the statistics -- sqrt((TA nB + TB nA) / 12 nC) -- which a band of rows estimates closely),
-// each band's GEMM and reconstruction following its arrival. When A has landed, its statistics are finished,
-// the values are checked, and the reference's plan is made from the complete statistics; if its moduli and
-// width equal the first plan's, C is already the result of the reference's plan and is read back band by
-// band; otherwise the pipeline runs again with it. Nothing is written to the caller's C before every value
-// has been checked, so C may alias A or B and an invalid input leaves C untouched, as the front end requires.
+// B goes up first in blocks of columns, its exact statistics measured as each block lands; A then goes up in
+// bands of 1024 rows. The plan depends on statistics of the whole A, so the pipeline starts on a first plan
+// made from B's statistics and an estimate from A's first band (the decision depends on ratios of the
+// statistics -- sqrt((TA nB + TB nA) / 12 nC) -- which a band of rows estimates closely), each band's scaling,
+// split, GEMM and reconstruction following its arrival. Each band's rows are also measured, as they land, by
+// one fast pass that yields bounds of the reference's statistics (its maxima exact; its sums of squares and
+// sketch values with error bounds that contain the reference's sequential long-double sums). When A has
+// landed, the values are checked and the reference's plan is decided from the bounds: the width cap and the
+// number of passes are step functions of the statistics, so when they are the same everywhere inside the
+// bounds they are the reference's decisions; only when a decision lies within the bounds are A's exact
+// long-double sums computed (a pass whose chains are 16384 steps long). If the plan equals the first one, C
+// is already its result and is read back band by band; otherwise the pipeline runs again with it. Nothing is
+// written to the caller's C before every value has been checked, so C may alias A or B and an invalid input
+// leaves C untouched, as the front end requires.
 int run_ii_int8_overlapped(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
                            uint64_t k, uint32_t max_moduli, int32_t reconstruction,
                            const std::function<void(const uint64_t*, const uint64_t*)>& check, oztt_ii_plan& p,
@@ -281,19 +286,17 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     StreamedPhases& ph = call.phases();
     cudaStream_t st = call.work();
     const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
-    const uint64_t bands = std::min<uint64_t>(8, std::max<uint64_t>(1, mp / 2048));
-    const uint64_t bm = round_up((mp + bands - 1) / bands, 128);
-    // uploads: B by column blocks with its statistics, then A by bands of rows with theirs
+    const uint64_t bm = 1024;
+    // uploads: B by column blocks with its statistics, then A by bands of rows with their bounded statistics
     call.upload_b();
     const std::vector<cudaEvent_t> landed = call.upload_a_rows(bm);
-    // the first plan: B's statistics and those of A's first band
-    const uint64_t m0 = std::min(bm, m);
-    PolicyStats first = call.band_stats(0, m0, landed[0]);
-    ph.first_plan_ms = call.ms_since_start();
+    // the first plan: B's statistics and an estimate from A's first band
+    const PolicyStats first = call.band_stats(0, std::min(bm, m));
     oztt_ii_plan p0{};
     std::string err0;
     const int rc0 = plan_ii_int8_with([&](uint32_t, uint32_t) { return first; }, m, n, k, max_moduli, reconstruction, 0,
                                       p0, err0);
+    ph.first_plan_ms = call.ms_since_start();
     const double *da = call.a_dev(), *db = call.b_dev();
     double* dc = call.c_dev();
     DevBuf dA(st, mp * 4), dB(st, np * 4), colmax(st, n * 8), words(st, 16);
@@ -311,15 +314,11 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
         for (uint64_t bi = 0, r0 = 0; r0 < mp; ++bi, r0 += bm) {
             const uint64_t rows_p = std::min(bm, mp - r0);
             const uint64_t rows = r0 < m ? std::min(m, r0 + rows_p) - r0 : 0;
+            if (!rows) break;
             if (wait_bands && bi < landed.size()) OZTT_CUDA(cudaStreamWaitEvent(st, landed[bi], 0));
-            if (rows) {
-                launch_scale_rows(da + r0 * k, rows, k, k, q.shift, dA.as<int32_t>() + r0, nullptr, flags, st);
-                launch_split_rows(da + r0 * k, rows, k, k, dA.as<int32_t>() + r0, q, ra->as<int8_t>(), rows_p, kp, st);
-            } else {
-                OZTT_CUDA(cudaMemsetAsync(ra->p, 0, S * rows_p * kp, st));
-            }
+            launch_scale_rows(da + r0 * k, rows, k, k, q.shift, dA.as<int32_t>() + r0, nullptr, flags, st);
+            launch_split_rows(da + r0 * k, rows, k, k, dA.as<int32_t>() + r0, q, ra->as<int8_t>(), rows_p, kp, st);
             launch_residue_gemm(ra->as<int8_t>(), rb->as<int8_t>(), rows_p, np, kp, q, 1, kpl->p, gemm_err, st, 0);
-            if (!rows) continue;
             launch_recon(kpl->as<uint8_t>(), rows_p, np, dA.as<int32_t>() + r0, dB.as<int32_t>(), q, dc + r0 * n, rows,
                          n, n, st);
             call.band_done(r0, rows);
@@ -329,15 +328,19 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
         check_plan(p0);
         pipeline(p0, true);
     }
-    // the complete statistics, the checks of every value, the reference's plan
+    // every value checked, then the reference's plan: decided by the bounds, or from the exact sums
     std::vector<uint64_t> row_max, col_max;
-    const PolicyStats ps = call.finish_stats(row_max, col_max);
+    const PolicyBounds bounds = call.certified_bounds(row_max, col_max);
     double t = call.ms_since_start();
     check(row_max.data(), col_max.data());
     ph.check_ms = call.ms_since_start() - t;
     t = call.ms_since_start();
-    const int rc = plan_ii_int8_with([&](uint32_t, uint32_t) { return ps; }, m, n, k, max_moduli, reconstruction, 0, p,
-                                     err);
+    bool decided = false;
+    int rc = plan_ii_int8_certified(bounds, m, n, k, max_moduli, reconstruction, p, err, decided);
+    if (rc == OZTT_OK && !decided) {
+        const PolicyStats ps = call.exact_stats();
+        rc = plan_ii_int8_with([&](uint32_t, uint32_t) { return ps; }, m, n, k, max_moduli, reconstruction, 0, p, err);
+    }
     if (rc != OZTT_OK) return rc;
     ph.plan_ms = call.ms_since_start() - t;
     const bool same = rc0 == OZTT_OK && p0.S == p.S && p0.b == p.b && p0.nd == p.nd && p0.shift == p.shift &&

@@ -421,6 +421,41 @@ int plan_ii_int8_with(const std::function<PolicyStats(uint32_t, uint32_t)>& stat
     return OZTT_OK;
 }
 
+// The width cap grows with nA and falls with nC, the one-pass error estimate falls with nC; both are
+// evaluated at the corners of the bounds, each a relative 1e-12 beyond them, so that the few roundings of
+// the decision formulas cannot tip a case the bounds call decided.
+int plan_ii_int8_certified(const PolicyBounds& bounds, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
+                           int32_t reconstruction, oztt_ii_plan& p, std::string& err, bool& decided) {
+    decided = false;
+    if (!bounds.usable) return OZTT_OK;
+    PolicyStats low = bounds.lo, high = bounds.hi;  // k2 at its least and at its greatest
+    low.nC = bounds.hi.nC * (1 + 1e-12);
+    low.nA = bounds.lo.nA * (1 - 1e-12);
+    high.nC = bounds.lo.nC * (1 - 1e-12);
+    high.nA = bounds.hi.nA * (1 + 1e-12);
+    for (const PolicyStats* q : {&low, &high})
+        if (!(q->nC > 0) || !(q->nA >= 0) || !std::isfinite(q->nC) || !std::isfinite(q->nA)) return OZTT_OK;
+    const int b_cap = policy_width_cap(low);
+    if (policy_width_cap(high) != b_cap) return OZTT_OK;
+    // plan at the middle of the bounds: its width cap is the decided one
+    PolicyStats mid = bounds.lo;
+    mid.nA = 0.5 * (bounds.lo.nA + bounds.hi.nA);
+    mid.nC = 0.5 * (bounds.lo.nC + bounds.hi.nC);
+    mid.measured = true;
+    const int rc = plan_ii_int8_with([&](uint32_t, uint32_t) { return mid; }, m, n, k, max_moduli, reconstruction, 0,
+                                     p, err);
+    if (rc != OZTT_OK || p.b_cap != b_cap) return rc;
+    if (reconstruction == OZTT_RECON_AUTO) {
+        std::vector<int> mods(p.moduli, p.moduli + p.S);
+        const double r_lo = one_pass_error_log2(mods, p.b, high), r_hi = one_pass_error_log2(mods, p.b, low);
+        // the estimate falls as nC grows: r_lo at the largest nC, r_hi at the smallest
+        const bool two_lo = !(r_lo + 1e-9 <= kRecon1Thr), two_hi = !(r_hi - 1e-9 <= kRecon1Thr);
+        if (two_lo != two_hi || two_lo != (p.two_pass != 0)) return OZTT_OK;
+    }
+    decided = true;
+    return OZTT_OK;
+}
+
 }  // namespace oztt
 
 extern "C" int oztt_ii_int8_plan(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k,

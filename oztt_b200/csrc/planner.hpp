@@ -61,6 +61,17 @@ ModuliChoice choose_moduli_int8(uint32_t K, int num_moduli, int b_cap);
 PolicyStats measure_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
                                  uint32_t K);
 int policy_width_cap(const PolicyStats& st);
+// Bounds of the five statistics: TA, TB, nB known exactly, nA and nC in [lo, hi] (the reference's values,
+// which come from sequential sums in its own rounding, lie inside).
+struct PolicyBounds {
+    PolicyStats lo, hi;  // lo: nA and nC at their lower bounds; hi: at their upper bounds
+    bool usable = false;
+};
+// The Scheme II INT8 plan when the bounds decide it: the width cap (and, for Automatic, the number of
+// passes) is the same everywhere in the bounds, so it is the reference's decision; decided = false (and
+// nothing planned) otherwise. Returns an OZTT_* code.
+int plan_ii_int8_certified(const PolicyBounds& bounds, uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli,
+                           int32_t reconstruction, oztt_ii_plan& p, std::string& err, bool& decided);
 double one_pass_error_log2(const std::vector<int>& mods, int b, const PolicyStats& st);
 void fill_crt_constants(const std::vector<int>& mods, oztt_ii_plan& p);
 // The whole plan; returns an OZTT_* code and a message.
@@ -201,6 +212,7 @@ struct StreamedPhases {
     int bands = 0;
     double first_plan_ms = 0;  // overlapped INT8 path: when the first plan (B and A's first band) was made
     int replanned = 0;         // 1 if the complete statistics gave another plan and the pipeline ran again
+    int exact_stats = 0;       // 1 if the bounds left the decision open and A's exact sums were computed
 };
 StreamedPhases last_streamed_phases();
 

@@ -154,15 +154,20 @@ public:
     // counted from pipeline_start_ms (ms_since_start when it was issued)
     void finish(double pipeline_start_ms);
     // The upload in two parts, for the INT8 path that overlaps the GEMM with A's upload: B in blocks of
-    // columns with its statistics, then A in bands of band_rows rows, each band's statistics measured as it
-    // lands (on a statistics stream of their own); returns the events that mark each band's arrival.
+    // columns with its exact statistics (on a statistics stream), then A in bands of band_rows rows, each
+    // band's bounded statistics measured as it lands (on a high-priority stream, so that they run between
+    // the GEMM's launches); returns the events that mark each band's arrival.
     void upload_b();
     std::vector<cudaEvent_t> upload_a_rows(uint64_t band_rows);
-    // The statistics of the problem with A's rows r0 .. r1-1 standing for the whole A (B's complete), once
-    // that band has landed (`landed`): the estimate a first plan is made from. Synchronises the work stream.
-    PolicyStats band_stats(uint64_t r0, uint64_t r1, cudaEvent_t landed);
-    // after upload_a_rows: A's finishing stages; the complete statistics and the maxima, as upload() returns
-    PolicyStats finish_stats(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max);
+    // An estimate of the statistics with A's rows r0 .. r1-1 (a band) standing for the whole A and B's
+    // complete: what a first plan is made from. Waits for that band's measurements.
+    PolicyStats band_stats(uint64_t r0, uint64_t r1);
+    // After upload_a_rows: bounds of the statistics that contain the reference's values, and the magnitude
+    // patterns of A's row maxima and B's column maxima (for the value checks). Waits for every band.
+    PolicyBounds certified_bounds(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max);
+    // The reference's exact statistics of the whole A and B (A's long-double sums over all of A, after the
+    // work issued so far on the statistics stream), for the rare call whose bounds leave a decision open.
+    PolicyStats exact_stats();
     // forgets the bands marked so far (their C is recomputed)
     void discard_bands() { bands_.clear(); }
     StreamedPhases& phases() { return phases_; }
@@ -180,8 +185,10 @@ private:
     const double *a_, *b_;
     uint64_t m_, n_, k_;
     std::chrono::steady_clock::time_point t0_;
-    cudaStream_t work_ = nullptr, up_ = nullptr, down_ = nullptr, stat_ = nullptr;
+    cudaStream_t work_ = nullptr, up_ = nullptr, down_ = nullptr, stat_ = nullptr, cert_ = nullptr;
     cudaEvent_t b_ready_ = nullptr, a_last_ = nullptr;
+    std::unique_ptr<DevBuf> cert_buf_, cert_flags_;
+    std::vector<cudaEvent_t> certified_;  // per band: its bounded statistics are written
     std::vector<cudaEvent_t> events_;
     std::vector<Band> bands_;
     std::unique_ptr<DevBuf> da_, db_, dc_;

@@ -205,6 +205,63 @@ __global__ void __launch_bounds__(128) sketch_kernel(const double* __restrict__ 
         out[l * ostride + r] = ext80::to_double(acc);
 }
 
+// Bounded statistics of rows of A (x: rows x k, row-major; one warp per row, the lanes striding the row),
+// for deciding the plan without the reference's sequential long-double sums: per row, into out[r*kCertW ..]:
+//   [0]          the largest magnitude as its bit pattern (NaN and Inf patterns order above every number)
+//   [1]          sum x^2            [2 .. 9]   sum x * y_l            [10 .. 17]  sum |x * y_l|
+// all unscaled, in FP64 (fused multiply-adds, the warp's order); the host turns them into bounds that
+// contain the reference's values. y: the 8 x k sketch y_l = B g_l of the reference (scaled). flags |= 1
+// when a nonzero element below 2^-383 makes the scaled squares leave the normal range (no bounds then).
+constexpr int kCertW = 18;
+__global__ void __launch_bounds__(256) band_certify_kernel(const double* __restrict__ x, uint64_t rows, uint64_t k,
+                                                           const double* __restrict__ y, double* __restrict__ out,
+                                                           uint32_t* __restrict__ flags) {
+    const uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const double* xr = x + r * k;
+    unsigned long long mx = 0;
+    bool tiny = false;
+    double s2 = 0.0, sl[kVectors], al[kVectors];
+#pragma unroll
+    for (int l = 0; l < kVectors; ++l) sl[l] = al[l] = 0.0;
+    for (uint64_t j = lane; j < k; j += 32) {
+        const double v = __ldg(xr + j);
+        const unsigned long long pat = (unsigned long long)__double_as_longlong(v) & 0x7FFFFFFFFFFFFFFFull;
+        mx = pat > mx ? pat : mx;
+        tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);  // 0 < |v| < 2^-383
+        s2 = fma(v, v, s2);
+#pragma unroll
+        for (int l = 0; l < kVectors; ++l) {
+            const double t = v * __ldg(y + (uint64_t)l * k + j);
+            sl[l] += t;
+            al[l] += fabs(t);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long om = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+        mx = om > mx ? om : mx;
+        s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
+#pragma unroll
+        for (int l = 0; l < kVectors; ++l) {
+            sl[l] += __shfl_xor_sync(0xFFFFFFFFu, sl[l], o);
+            al[l] += __shfl_xor_sync(0xFFFFFFFFu, al[l], o);
+        }
+    }
+    if (__any_sync(0xFFFFFFFFu, tiny) && lane == 0) atomicOr(flags, 1u);
+    if (lane == 0) {
+        double* o = out + r * kCertW;
+        o[0] = __longlong_as_double((long long)mx);
+        o[1] = s2;
+#pragma unroll
+        for (int l = 0; l < kVectors; ++l) {
+            o[2 + l] = sl[l];
+            o[2 + kVectors + l] = al[l];
+        }
+    }
+}
+
 // out[i] = the extended sum e[i] rounded to double (the end of a chain of sketch stretches).
 __global__ void __launch_bounds__(256) round_ext_kernel(const ext80::Ext* __restrict__ e, uint64_t count,
                                                         double* __restrict__ out) {
@@ -362,6 +419,17 @@ struct PolicyStatsRun::Bufs {
 
 PolicyStatsRun::PolicyStatsRun(uint64_t m, uint64_t n, uint64_t k, uint32_t N, cudaStream_t st)
     : m_(m), n_(n), k_(k), N_(N), st_(st) {
+    // The row stages of A's bands run beside the persistent residue GEMM, whose CTAs hold most of each SM's
+    // shared memory: ask for the same carveout, so that their blocks can share the SMs instead of waiting
+    // for the GEMM to end (they use no shared memory themselves).
+    static std::once_flag carveout;
+    std::call_once(carveout, [] {
+        const int shared = cudaSharedmemCarveoutMaxShared;
+        cudaFuncSetAttribute(row_absmax_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, shared);
+        cudaFuncSetAttribute(row_sumsq_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, shared);
+        cudaFuncSetAttribute(sketch_kernel<true, true>, cudaFuncAttributePreferredSharedMemoryCarveout, shared);
+        cudaGetLastError();
+    });
     int dev = 0;
     OZTT_CUDA(cudaGetDevice(&dev));
     OZTT_CUDA(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, dev));
@@ -570,6 +638,81 @@ void launch_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double r
 
 std::vector<double> policy_vectors_host(uint32_t N) { return *policy_vectors(N); }
 
+void launch_band_certify(const double* x, uint64_t rows, uint64_t k, const double* y, double* out, uint32_t* flags,
+                         cudaStream_t st) {
+    if (!rows) return;
+    band_certify_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(x, rows, k, y, out, flags);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+// Bounds of nA and nC around the reference's values from the rows' bounded statistics (cert: m x kCertW as
+// band_certify_kernel writes them) and B's exact parts; TA, TB, nB exact. Error terms, with gamma(n, u) =
+// n u / (1 - n u), u = 2^-53 for binary64 and 2^-64 for the reference's long double:
+//   a row's sum of squares: each side (the reference's sequential one, this warp-order one) is within
+//     gamma(k+1, u) of the exact sum of positive terms;
+//   a sketch value s_l[r]: the reference's long-double sum is within gamma(k+1, 2^-64) sum |t| of the exact
+//     sum and is rounded once to double, this one within gamma(k+1, u) sum |t|;
+//   the sums over rows (nA, each ||s_l||^2) gain gamma(m+1, u) on each side; nC's last few operations
+//     16 u. The bounds are widened by these, so the reference's values lie inside.
+PolicyBounds certified_policy_bounds(const double* cert, uint64_t m, uint64_t k, const double* col_max, uint64_t n,
+                                     const double* col_sumsq, double rgB) {
+    PolicyBounds pb;
+    auto gamma = [](double cnt, double u) { return cnt * u / (1.0 - cnt * u); };
+    const double u = 0x1p-53, ue = 0x1p-64;
+    unsigned long long top = 0;
+    for (uint64_t r = 0; r < m; ++r) {
+        unsigned long long pat;
+        std::memcpy(&pat, cert + r * kCertW, 8);
+        if (pat >= 0x7FF0000000000000ull) return pb;  // NaN or Inf: the value checks report it
+        top = std::max(top, pat);
+    }
+    double topv;
+    std::memcpy(&topv, &top, 8);
+    double rgA = 1.0;
+    if (topv > 0) {
+        int e = 0;
+        std::frexp(topv, &e);
+        rgA = std::ldexp(1.0, -std::min(std::max(e, -1000), 1000));
+    }
+    // TA, TB, nB exactly as the reference sums them (combine_policy_stats with zero placeholders for nA, nC)
+    std::vector<double> row_max(m), zeros(m, 0.0), zs(8 * m, 0.0);
+    for (uint64_t r = 0; r < m; ++r) row_max[r] = cert[r * kCertW];
+    const PolicyStats exact = combine_policy_stats(row_max.data(), m, col_max, n, zeros.data(), col_sumsq, zs.data(), m,
+                                                   rgA, rgB);
+    const double g_row = gamma((double)k + 1, u), g_rowe = gamma((double)k + 1, ue), g_sum = gamma((double)m + 1, u);
+    long double nA = 0, q_lo[8] = {}, q_hi[8] = {};
+    const double s2scale = rgA * rgA;
+    for (uint64_t r = 0; r < m; ++r) {
+        const double* c = cert + r * kCertW;
+        nA += (long double)(c[1] * s2scale);
+        for (int l = 0; l < 8; ++l) {
+            const double sv = c[2 + l] * rgA, av = c[10 + l] * rgA;
+            const double d = (g_row * (1 + u) + g_rowe) * av + u * std::fabs(sv) + 0x1p-1000;
+            const double lo = std::max(0.0, std::fabs(sv) - d), hi = std::fabs(sv) + d;
+            q_lo[l] += (long double)lo * lo;
+            q_hi[l] += (long double)hi * hi;
+        }
+    }
+    const double e_nA = 2 * g_row + g_sum + 4 * u;
+    auto nc_of = [](const long double* q) {
+        long double cs2 = 0, cmx = 0;
+        for (int l = 0; l < 8; ++l) {
+            cs2 += q[l];
+            cmx = std::max(cmx, q[l]);
+        }
+        return (double)((cs2 - cmx) / 7 / (1.0L + 2.0L * std::sqrt(2.0L / 8)));
+    };
+    pb.lo = pb.hi = exact;
+    pb.lo.measured = pb.hi.measured = true;
+    pb.lo.nA = (double)nA * (1 - e_nA);
+    pb.hi.nA = (double)nA * (1 + e_nA);
+    pb.lo.nC = nc_of(q_lo) * (1 - g_sum - 16 * u);
+    pb.hi.nC = nc_of(q_hi) * (1 + g_sum + 16 * u);
+    pb.usable = std::isfinite(pb.hi.nA) && std::isfinite(pb.hi.nC) && pb.lo.nC > 0 && rgA * topv < 2.0;
+    return pb;
+}
+
+
 PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
                                 cudaStream_t st) {
     PolicyStatsRun run(m, n, k, N, st);
@@ -581,6 +724,29 @@ PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, ui
 }
 
 }  // namespace oztt
+
+// Test hook: the certified decision from host copies of the bounded row statistics (m x 18, as
+// band_certify_kernel writes them) and B's exact parts; bounds5 (NULL or 4 doubles) receives nA lo/hi and nC
+// lo/hi, *decided whether the bounds decided the plan (which is then in *plan).
+extern "C" int oztt_test_certified_plan(const double* cert, uint64_t m, uint64_t n, uint64_t k, const double* col_max,
+                                        const double* col_sumsq, double rgB, uint32_t max_moduli, int32_t reconstruction,
+                                        oztt_ii_plan* plan, int32_t* decided, double* bounds4, char* err,
+                                        size_t errlen) {
+    return oztt::guarded(err, errlen, [&] {
+        const oztt::PolicyBounds pb = oztt::certified_policy_bounds(cert, m, k, col_max, n, col_sumsq, rgB);
+        if (bounds4) {
+            bounds4[0] = pb.lo.nA;
+            bounds4[1] = pb.hi.nA;
+            bounds4[2] = pb.lo.nC;
+            bounds4[3] = pb.hi.nC;
+        }
+        bool ok = false;
+        std::string msg;
+        const int rc = oztt::plan_ii_int8_certified(pb, m, n, k, max_moduli, reconstruction, *plan, msg, ok);
+        if (rc != OZTT_OK) throw oztt::Error(rc, msg);
+        *decided = ok ? 1 : 0;
+    });
+}
 
 // ---- C ABI: the statistics stages, for callers that hold panels of A and B on several devices ------
 using oztt::Error;

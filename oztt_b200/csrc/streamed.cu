@@ -28,6 +28,11 @@ void launch_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double r
 PolicyStats combine_policy_stats(const double* row_max, uint64_t m, const double* col_max, uint64_t n,
                                  const double* row_sumsq, const double* col_sumsq, const double* s, uint64_t sstride,
                                  double rgA, double rgB);
+void launch_band_certify(const double* x, uint64_t rows, uint64_t k, const double* y, double* out, uint32_t* flags,
+                         cudaStream_t st);
+PolicyBounds certified_policy_bounds(const double* cert, uint64_t m, uint64_t k, const double* col_max, uint64_t n,
+                                     const double* col_sumsq, double rgB);
+constexpr uint64_t kCertWidth = 18;  // doubles per row written by launch_band_certify
 
 namespace {
 StreamedPhases g_last_phases;
@@ -49,15 +54,17 @@ StreamedCall::StreamedCall(int device_id, const double* a, const double* b, uint
 }
 
 StreamedCall::~StreamedCall() {
-    for (cudaStream_t s : {up_, down_, stat_, work_})
+    for (cudaStream_t s : {up_, down_, stat_, cert_, work_})
         if (s) cudaStreamSynchronize(s);
     // the buffers go back to the pool on the work stream, after everything that used them
     stats_.reset();
+    cert_buf_.reset();
+    cert_flags_.reset();
     dc_.reset();
     da_.reset();
     db_.reset();
     for (cudaEvent_t e : events_) cudaEventDestroy(e);
-    for (cudaStream_t s : {up_, down_, stat_, work_})
+    for (cudaStream_t s : {up_, down_, stat_, cert_, work_})
         if (s) {
             cudaStreamSynchronize(s);
             cudaStreamDestroy(s);
@@ -135,56 +142,94 @@ void StreamedCall::upload_b() {
 }
 
 std::vector<cudaEvent_t> StreamedCall::upload_a_rows(uint64_t band_rows) {
+    int lo = 0, hi = 0;
+    OZTT_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+    OZTT_CUDA(cudaStreamCreateWithPriority(&cert_, cudaStreamNonBlocking, hi));
+    order(work_, cert_);
+    cert_buf_ = std::make_unique<DevBuf>(cert_, m_ * kCertWidth * 8);
+    cert_flags_ = std::make_unique<DevBuf>(cert_, 16);
+    OZTT_CUDA(cudaMemsetAsync(cert_flags_->p, 0, 16, cert_));
+    OZTT_CUDA(cudaStreamWaitEvent(cert_, b_ready_, 0));  // the sketch y of B
+    order(cert_, up_);
     std::vector<cudaEvent_t> landed;
     double* da = da_->as<double>();
+    const double* y = stats_->b_parts().y;
     for (uint64_t r0 = 0; r0 < m_; r0 += band_rows) {
         const uint64_t rows = std::min(band_rows, m_ - r0);
         OZTT_CUDA(cudaMemcpyAsync(da + r0 * k_, a_ + r0 * k_, rows * k_ * 8, cudaMemcpyHostToDevice, up_));
-        landed.push_back(order(up_, stat_));
-        stats_->a_rows(da, r0, r0 + rows);
+        landed.push_back(order(up_, cert_));
+        launch_band_certify(da + r0 * k_, rows, k_, y, cert_buf_->as<double>() + r0 * kCertWidth,
+                            cert_flags_->as<uint32_t>(), cert_);
+        certified_.push_back(mark(cert_));
     }
     a_last_ = landed.back();
     return landed;
 }
 
-PolicyStats StreamedCall::band_stats(uint64_t r0, uint64_t r1, cudaEvent_t landed) {
-    OZTT_CUDA(cudaStreamWaitEvent(work_, b_ready_, 0));
-    OZTT_CUDA(cudaStreamWaitEvent(work_, landed, 0));
+PolicyStats StreamedCall::band_stats(uint64_t r0, uint64_t r1) {
+    const uint64_t band = r0 / std::max<uint64_t>(1, r1 - r0);
+    OZTT_CUDA(cudaStreamWaitEvent(work_, certified_.at(std::min<uint64_t>(band, certified_.size() - 1)), 0));
     const uint64_t rows = r1 - r0;
-    const double* ab = da_->as<double>() + r0 * k_;
     const PolicyStatsRun::BParts bp = stats_->b_parts();
-    DevBuf mx(work_, rows * 8), s2(work_, rows * 8), sk(work_, 8 * rows * 8);
-    std::vector<double> hmax(rows), hs2(rows), hsk(8 * rows), cmax(n_), cs2(n_);
+    std::vector<double> he(rows * kCertWidth), cmax(n_), cs2(n_);
     double rgB = 1.0;
-    launch_stats_absmax(ab, rows, k_, 0, mx.as<double>(), work_);
-    OZTT_CUDA(cudaMemcpyAsync(hmax.data(), mx.p, rows * 8, cudaMemcpyDeviceToHost, work_));
+    OZTT_CUDA(cudaMemcpyAsync(he.data(), cert_buf_->as<double>() + r0 * kCertWidth, he.size() * 8,
+                              cudaMemcpyDeviceToHost, work_));
     OZTT_CUDA(cudaMemcpyAsync(cmax.data(), bp.col_max, n_ * 8, cudaMemcpyDeviceToHost, work_));
     OZTT_CUDA(cudaMemcpyAsync(cs2.data(), bp.col_sumsq, n_ * 8, cudaMemcpyDeviceToHost, work_));
     OZTT_CUDA(cudaMemcpyAsync(&rgB, bp.rgB, 8, cudaMemcpyDeviceToHost, work_));
     OZTT_CUDA(cudaStreamSynchronize(work_));
+    // the band's rows as if they were all of A: its own power-of-two scale, the sums scaled by it
     double top = 0;
-    for (double v : hmax) top = std::max(top, v);
+    for (uint64_t r = 0; r < rows; ++r) top = std::max(top, he[r * kCertWidth]);
     double rgA = 1.0;
     if (top > 0 && std::isfinite(top)) {
         int e = 0;
         std::frexp(top, &e);
         rgA = std::ldexp(1.0, -std::min(std::max(e, -1000), 1000));
     }
-    launch_stats_sumsq(ab, rows, k_, 0, rgA, s2.as<double>(), work_);
-    launch_stats_sketch(ab, rows, k_, rgA, bp.y, k_, sk.as<double>(), rows, work_);
-    OZTT_CUDA(cudaMemcpyAsync(hs2.data(), s2.p, rows * 8, cudaMemcpyDeviceToHost, work_));
-    OZTT_CUDA(cudaMemcpyAsync(hsk.data(), sk.p, hsk.size() * 8, cudaMemcpyDeviceToHost, work_));
-    OZTT_CUDA(cudaStreamSynchronize(work_));
+    std::vector<double> hmax(rows), hs2(rows), hsk(8 * rows);
+    for (uint64_t r = 0; r < rows; ++r) {
+        const double* c = he.data() + r * kCertWidth;
+        hmax[r] = c[0];
+        hs2[r] = c[1] * rgA * rgA;
+        for (int l = 0; l < 8; ++l) hsk[(uint64_t)l * rows + r] = c[2 + l] * rgA;
+    }
     return combine_policy_stats(hmax.data(), rows, cmax.data(), n_, hs2.data(), cs2.data(), hsk.data(), rows, rgA,
                                 rgB);
 }
 
-PolicyStats StreamedCall::finish_stats(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max) {
-    stats_->a_done(da_->as<double>());
+PolicyBounds StreamedCall::certified_bounds(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max) {
     OZTT_CUDA(cudaEventSynchronize(a_last_));
     phases_.upload_ms = ms_since_start();
-    const PolicyStats ps = stats_->collect(&row_max, &col_max);
+    const PolicyStatsRun::BParts bp = stats_->b_parts();
+    std::vector<double> cert(m_ * kCertWidth), cs2(n_);
+    col_max.assign(n_, 0);
+    double rgB = 1.0;
+    uint32_t flags = 0;
+    OZTT_CUDA(cudaStreamWaitEvent(cert_, b_ready_, 0));
+    OZTT_CUDA(cudaMemcpyAsync(cert.data(), cert_buf_->p, cert.size() * 8, cudaMemcpyDeviceToHost, cert_));
+    OZTT_CUDA(cudaMemcpyAsync(&flags, cert_flags_->p, 4, cudaMemcpyDeviceToHost, cert_));
+    OZTT_CUDA(cudaMemcpyAsync(col_max.data(), bp.col_max, n_ * 8, cudaMemcpyDeviceToHost, cert_));
+    OZTT_CUDA(cudaMemcpyAsync(cs2.data(), bp.col_sumsq, n_ * 8, cudaMemcpyDeviceToHost, cert_));
+    OZTT_CUDA(cudaMemcpyAsync(&rgB, bp.rgB, 8, cudaMemcpyDeviceToHost, cert_));
+    OZTT_CUDA(cudaStreamSynchronize(cert_));
+    row_max.resize(m_);
+    for (uint64_t r = 0; r < m_; ++r) std::memcpy(&row_max[r], &cert[r * kCertWidth], 8);
+    PolicyBounds pb = certified_policy_bounds(cert.data(), m_, k_, reinterpret_cast<const double*>(col_max.data()),
+                                              n_, cs2.data(), rgB);
+    if (flags) pb.usable = false;  // elements below 2^-383: the bounds do not hold
     phases_.stats_ms = ms_since_start() - phases_.upload_ms;
+    return pb;
+}
+
+PolicyStats StreamedCall::exact_stats() {
+    const double* da = da_->as<double>();
+    OZTT_CUDA(cudaStreamWaitEvent(stat_, a_last_, 0));
+    stats_->a_cols(da, 0, k_);
+    stats_->a_done(da);
+    const PolicyStats ps = stats_->collect();
+    phases_.exact_stats = 1;
     return ps;
 }
 
