@@ -213,10 +213,11 @@ int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* 
 
 /* Host wall-clock phases (ms) of the last INT8 Scheme II call made through oztt_gemm / Context::gemm in
  * this process, out[0..count-1] of: upload (to the end of the last host-to-device copy), statistics
- * read-back after it, value checks from the measured maxima, plan, pipeline with the banded read-back of C,
- * total, number of row bands, and (calls of at least 4096 rows, whose GEMM overlaps A's upload) the time
- * the first plan was made, 1 if the complete statistics gave another plan, and 1 if the bounds of the
- * statistics left a decision open so that A's exact sums were computed. Zeros before the first such call. */
+ * read-back after it, value checks, plan, pipeline with the banded read-back of C, total, number of row
+ * bands, and (calls of at least 4096 rows, which compute while their operands upload) the time the first
+ * plan was made, 1 if the complete statistics gave another plan, 1 if the bounds of the statistics left a
+ * decision open so that the exact sums were computed, and 1 if C's bands were read back as they finished,
+ * before the plan was confirmed. Zeros before the first such call. */
 int oztt_ii_int8_last_phases(double* out, int32_t count);
 
 /* Scheme I INT8 plan (plan_issue and the slice count of src/backend/ozaki1/plan.hpp:128-250 and

@@ -210,8 +210,9 @@ _SIGNATURES = {
     "oztt_test_ext80_dot": [_P, _P, _U64, ctypes.c_double],
     "oztt_test_gemm_wait_timeout": [_U64, _P, _P, _ERR, _SZ],
     "oztt_test_scheme1_kblock": [_U64],
-    "oztt_test_certified_plan": [_P, _U64, _U64, _U64, _P, _P, ctypes.c_double, ctypes.c_uint32, _I32,
-                                 ctypes.POINTER(IIPlan), ctypes.POINTER(_I32), _P, _ERR, _SZ],
+    "oztt_test_certified_plan": [_P, _U64, _U64, _U64, _P, ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                                 ctypes.c_uint32, _I32, ctypes.POINTER(IIPlan), ctypes.POINTER(_I32), _P, _ERR, _SZ],
+    "oztt_test_bounded_nb": [_P, _U64, _U64, ctypes.c_double, _P, _ERR, _SZ],
 }
 
 _RESTYPES = {"oztt_test_scheme1_kblock": None, "oztt_format_name": ctypes.c_char_p, "oztt_policy_vectors": None, "oztt_test_udiv_small": ctypes.c_uint32, "oztt_test_ext80_dot": ctypes.c_double, "oztt_ii_padded_dims": None, "oztt_eval_inputs": None,
@@ -369,18 +370,20 @@ def policy_vectors(N: int) -> np.ndarray:
 
 def ii_int8_last_phases() -> dict:
     """Host wall-clock phases (ms) of the last INT8 Scheme II call through Context.gemm in this process
-    (oztt_ii_int8_last_phases): upload, statistics read-back, value checks from the measured maxima, plan,
-    pipeline with the banded read-back of C, total, the number of row bands, and, on the path that overlaps
-    the GEMM with A's upload, when the first plan was made, whether the complete statistics replanned, and
-    whether the bounds left the decision open so that A's exact sums were computed."""
-    out = np.zeros(10, dtype=np.float64)
-    _lib().oztt_ii_int8_last_phases(out.ctypes.data, 10)
+    (oztt_ii_int8_last_phases): upload, statistics read-back, value checks, plan, pipeline with the banded
+    read-back of C, total, the number of row bands, and, on the path that computes while its operands
+    upload, when the first plan was made, whether the complete statistics replanned, whether the bounds
+    left the decision open so that the exact sums were computed, and whether C's bands were read back as
+    they finished (before the plan was confirmed)."""
+    out = np.zeros(11, dtype=np.float64)
+    _lib().oztt_ii_int8_last_phases(out.ctypes.data, 11)
     keys = ("upload_ms", "stats_ms", "check_ms", "plan_ms", "pipeline_ms", "total_ms")
     d = {key: float(v) for key, v in zip(keys, out[:6])}
     d["bands"] = int(out[6])
     d["first_plan_ms"] = float(out[7])
     d["replanned"] = int(out[8])
     d["exact_stats"] = int(out[9])
+    d["early_readback"] = int(out[10])
     return d
 
 

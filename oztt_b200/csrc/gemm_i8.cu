@@ -850,14 +850,16 @@ void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* out, uint64
 }  // namespace
 
 // a_plane_rows: when nonzero, ap points at row r0 of A planes that are a_plane_rows tall, and the
-// GEMM covers the band of mp rows from there (output planes [S][mp][np] of the band).
+// GEMM covers the band of mp rows from there (output planes [S][mp][np] of the band). b_plane_rows: the
+// same for B, whose planes hold a block of np of their b_plane_rows columns (output [S][mp][np] of the block).
 void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
                          const oztt_ii_plan& p, int mode, void* out, int* err_word, cudaStream_t st,
-                         uint64_t a_plane_rows) {
+                         uint64_t a_plane_rows, uint64_t b_plane_rows) {
     using namespace gemm;
     if (mp % BM || np % BN || kp % BK || mp == 0 || np == 0 || kp == 0)
         throw Error(OZTT_EINVAL, "residue_gemm: mp, np, kp must be positive multiples of 128, 256 and 128");
     if (a_plane_rows && a_plane_rows < mp) throw Error(OZTT_EINVAL, "residue_gemm: band taller than its planes");
+    if (b_plane_rows && b_plane_rows < np) throw Error(OZTT_EINVAL, "residue_gemm: block wider than its planes");
     if (p.S < 1 || p.S > OZTT_MAXS) throw Error(OZTT_EINVAL, "residue_gemm: bad number of moduli");
     if ((reinterpret_cast<uintptr_t>(ap) | reinterpret_cast<uintptr_t>(bp)) & 15)
         throw Error(OZTT_EINVAL, "residue_gemm: planes must be 16-byte aligned");
@@ -873,7 +875,7 @@ void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64
     }
     const bool pairs = use_pairs();
     const CUtensorMap ta = make_plane_map(ap, mp, kp, (uint64_t)p.S, pairs ? pair::BM : BM, a_plane_rows);
-    const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p.S, pairs ? pair::BNH : BN);
+    const CUtensorMap tb = make_plane_map(bp, np, kp, (uint64_t)p.S, pairs ? pair::BNH : BN, b_plane_rows);
     if (mode == 0)
         launch_gemm<0>(ta, tb, out, mp, np, kp, (uint32_t)p.S, ec, err_word, st, pairs);
     else

@@ -16,6 +16,7 @@
 #include <chrono>
 #include <functional>
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "oztt_common.cuh"
@@ -31,10 +32,11 @@ void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, in
 void launch_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
                        const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st);
 void launch_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
-                       const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st);
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st,
+                       uint64_t plane_rows = 0);
 void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
                          const oztt_ii_plan& p, int mode, void* out, int* err_word, cudaStream_t st,
-                         uint64_t a_plane_rows = 0);
+                         uint64_t a_plane_rows = 0, uint64_t b_plane_rows = 0);
 void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB,
                   const oztt_ii_plan& p, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st);
 
@@ -262,22 +264,59 @@ int run_ii_int8_streamed_impl(int device_id, const double* a, const double* b, d
     return OZTT_OK;
 }
 
-// ---- the call from host buffers with the GEMM overlapping A's upload --------------------------------------
+// ---- the call from host buffers, computing while the operands upload ------------------------------------------
 //
-// B goes up first in blocks of columns, its exact statistics measured as each block lands; A then goes up in
-// bands of 1024 rows. The plan depends on statistics of the whole A, so the pipeline starts on a first plan
-// made from B's statistics and an estimate from A's first band (the decision depends on ratios of the
-// statistics -- sqrt((TA nB + TB nA) / 12 nC) -- which a band of rows estimates closely), each band's scaling,
-// split, GEMM and reconstruction following its arrival. Each band's rows are also measured, as they land, by
-// one fast pass that yields bounds of the reference's statistics (its maxima exact; its sums of squares and
-// sketch values with error bounds that contain the reference's sequential long-double sums). When A has
-// landed, the values are checked and the reference's plan is decided from the bounds: the width cap and the
-// number of passes are step functions of the statistics, so when they are the same everywhere inside the
-// bounds they are the reference's decisions; only when a decision lies within the bounds are A's exact
-// long-double sums computed (a pass whose chains are 16384 steps long). If the plan equals the first one, C
-// is already its result and is read back band by band; otherwise the pipeline runs again with it. Nothing is
-// written to the caller's C before every value has been checked, so C may alias A or B and an invalid input
-// leaves C untouched, as the front end requires.
+// The magnitude patterns of A's row maxima and B's column maxima (the front end's value checks), measured by
+// the host's threads from the caller's buffers while the operands upload: known long before A has landed.
+class HostMaxima {
+public:
+    HostMaxima(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k)
+        : row_max(m), col_max(n, 0), th_([this, a, b, m, n, k] { measure(a, b, m, n, k); }) {}
+    ~HostMaxima() { wait(); }
+    void wait() {
+        if (th_.joinable()) th_.join();
+    }
+    std::vector<uint64_t> row_max, col_max;
+
+private:
+    void measure(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k) {
+        constexpr uint64_t kMag = 0x7FFFFFFFFFFFFFFFull;
+        const auto* pa = reinterpret_cast<const uint64_t*>(a);
+        const auto* pb = reinterpret_cast<const uint64_t*>(b);
+        parallel_ranges(m, [&](uint64_t r0, uint64_t r1) {
+            for (uint64_t i = r0; i < r1; ++i) {
+                uint64_t mx = 0;
+                for (uint64_t j = 0; j < k; ++j) mx = std::max(mx, pa[i * k + j] & kMag);
+                row_max[i] = mx;
+            }
+        });
+        parallel_ranges(n, [&](uint64_t c0, uint64_t c1) {
+            uint64_t* mx = col_max.data();
+            for (uint64_t i = 0; i < k; ++i)
+                for (uint64_t j = c0; j < c1; ++j) mx[j] = std::max(mx[j], pb[i * n + j] & kMag);
+        });
+    }
+    std::thread th_;  // after the vectors it fills
+};
+
+bool overlaps(const void* p, uint64_t pbytes, const void* q, uint64_t qbytes) {
+    const uintptr_t p0 = reinterpret_cast<uintptr_t>(p), q0 = reinterpret_cast<uintptr_t>(q);
+    return p0 < q0 + qbytes && q0 < p0 + pbytes;
+}
+
+// Context::gemm from host buffers, computing while the operands upload. The upload order is A's first half
+// (bands of 1024 rows), then B in eight blocks of columns, then the rest of A. The precision decision depends
+// on the statistics of the whole A and B, so the pipeline starts on a first plan made from an estimate: A's
+// first half and B's first block, each standing for its matrix (the decision depends on the size-free ratio
+// (TA nB + TB nA) / 12 nC, which such parts estimate closely). On that plan A's first half is split once and
+// multiplied by each block of B as the block lands; then each later band of A by the whole B as it lands.
+// Meanwhile the host measures the maxima of A and B from the caller's buffers, and once every value is
+// checked the bands of C are read back as they finish -- when that cannot change the outcome of the call:
+// no plan for these dimensions can fail, and C does not overlap A or B. When A has landed, the reference's
+// plan is decided from bounds of its statistics measured as the blocks and bands landed (only a decision
+// that lies within the bounds needs the exact long-double sums). If it equals the first plan, C is its
+// result; otherwise the pipeline runs again with it and C is read back again. An invalid input is reported
+// before anything is written to C, as the front end requires.
 int run_ii_int8_overlapped(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
                            uint64_t k, uint32_t max_moduli, int32_t reconstruction,
                            const std::function<void(const uint64_t*, const uint64_t*)>& check, oztt_ii_plan& p,
@@ -287,15 +326,20 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     cudaStream_t st = call.work();
     const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
     const uint64_t bm = 1024;
-    // uploads: B by column blocks with its statistics, then A by bands of rows with their bounded statistics
-    call.upload_b();
-    const std::vector<cudaEvent_t> landed = call.upload_a_rows(bm);
-    // the first plan: B's statistics and an estimate from A's first band
-    const PolicyStats first = call.band_stats(0, std::min(bm, m));
+    const uint64_t pre = std::min(round_up(m / 2, bm), m);  // A's first part: whole bands
+    const uint64_t pre_bands = (pre + bm - 1) / bm;
+    const uint64_t nb = round_up((n + 7) / 8, 256);  // B's blocks of columns
+    HostMaxima host(a, b, m, n, k);
+    std::vector<cudaEvent_t> b_landed;
+    const std::vector<cudaEvent_t> landed = call.upload_prefix_first(pre, bm, nb, b_landed);
+    // the first plan, from A's first part and B's first block
+    bool estimated = false;
+    const PolicyStats first = call.prefix_estimate(pre, nb, landed[pre_bands - 1], b_landed[0], estimated);
     oztt_ii_plan p0{};
     std::string err0;
-    const int rc0 = plan_ii_int8_with([&](uint32_t, uint32_t) { return first; }, m, n, k, max_moduli, reconstruction, 0,
-                                      p0, err0);
+    const int rc0 = estimated ? plan_ii_int8_with([&](uint32_t, uint32_t) { return first; }, m, n, k, max_moduli,
+                                                  reconstruction, 0, p0, err0)
+                              : OZTT_ERUNTIME;
     ph.first_plan_ms = call.ms_since_start();
     const double *da = call.a_dev(), *db = call.b_dev();
     double* dc = call.c_dev();
@@ -304,36 +348,72 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
     std::unique_ptr<DevBuf> rb, ra, kpl;
-    auto pipeline = [&](const oztt_ii_plan& q, bool wait_bands) {
+    const auto buffers = [&](const oztt_ii_plan& q, uint64_t a_rows) {
         const uint64_t S = (uint64_t)q.S;
         rb = std::make_unique<DevBuf>(st, S * np * kp);
-        ra = std::make_unique<DevBuf>(st, S * bm * kp);
-        kpl = std::make_unique<DevBuf>(st, S * bm * np);
+        ra = std::make_unique<DevBuf>(st, S * a_rows * kp);
+        kpl = std::make_unique<DevBuf>(st, S * std::max(a_rows * std::min(nb, np), bm * np));
+    };
+    // one band of A's rows against the whole B (B's planes complete)
+    const auto band = [&](const oztt_ii_plan& q, uint64_t r0) {
+        const uint64_t rows_p = std::min(bm, mp - r0), rows = std::min(m, r0 + rows_p) - r0;
+        launch_scale_rows(da + r0 * k, rows, k, k, q.shift, dA.as<int32_t>() + r0, nullptr, flags, st);
+        launch_split_rows(da + r0 * k, rows, k, k, dA.as<int32_t>() + r0, q, ra->as<int8_t>(), rows_p, kp, st);
+        launch_residue_gemm(ra->as<int8_t>(), rb->as<int8_t>(), rows_p, np, kp, q, 1, kpl->p, gemm_err, st, 0);
+        launch_recon(kpl->as<uint8_t>(), rows_p, np, dA.as<int32_t>() + r0, dB.as<int32_t>(), q, dc + r0 * n, rows, n,
+                     n, st);
+        call.band_done(r0, rows);
+    };
+    // on the first plan, following the upload: A's first part against each block of B, then the later bands
+    const auto following = [&](const oztt_ii_plan& q) {
+        buffers(q, pre);
+        OZTT_CUDA(cudaStreamWaitEvent(st, landed[pre_bands - 1], 0));
+        launch_scale_rows(da, pre, k, k, q.shift, dA.as<int32_t>(), nullptr, flags, st);
+        launch_split_rows(da, pre, k, k, dA.as<int32_t>(), q, ra->as<int8_t>(), pre, kp, st);
+        for (uint64_t j = 0, c0 = 0; c0 < n; ++j, c0 += nb) {
+            const uint64_t cols_p = std::min(nb, np - c0), cols = std::min(n, c0 + cols_p) - c0;
+            OZTT_CUDA(cudaStreamWaitEvent(st, b_landed.at(j), 0));
+            launch_scale_cols(db + c0, k, cols, n, q.shift, dB.as<int32_t>() + c0, nullptr, flags,
+                              colmax.as<unsigned long long>() + c0, st);
+            launch_split_cols(db + c0, k, cols, n, dB.as<int32_t>() + c0, q, rb->as<int8_t>() + c0 * kp, cols_p, kp,
+                              st, np);
+            launch_residue_gemm(ra->as<int8_t>(), rb->as<int8_t>() + c0 * kp, pre, cols_p, kp, q, 1, kpl->p, gemm_err,
+                                st, 0, np);
+            launch_recon(kpl->as<uint8_t>(), pre, cols_p, dA.as<int32_t>(), dB.as<int32_t>() + c0, q, dc + c0, pre,
+                         cols, n, st);
+        }
+        for (uint64_t r0 = 0; r0 < pre; r0 += bm) call.band_done(r0, std::min(bm, pre - r0));
+        for (uint64_t i = pre_bands, r0 = pre; r0 < m; ++i, r0 += bm) {
+            OZTT_CUDA(cudaStreamWaitEvent(st, landed[i], 0));
+            band(q, r0);
+        }
+    };
+    // after everything has landed: the whole pipeline on a plan
+    const auto whole = [&](const oztt_ii_plan& q) {
+        OZTT_CUDA(cudaStreamWaitEvent(st, landed.back(), 0));
+        OZTT_CUDA(cudaStreamWaitEvent(st, b_landed.back(), 0));
+        buffers(q, bm);
         launch_scale_cols(db, k, n, n, q.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
         launch_split_cols(db, k, n, n, dB.as<int32_t>(), q, rb->as<int8_t>(), np, kp, st);
-        for (uint64_t bi = 0, r0 = 0; r0 < mp; ++bi, r0 += bm) {
-            const uint64_t rows_p = std::min(bm, mp - r0);
-            const uint64_t rows = r0 < m ? std::min(m, r0 + rows_p) - r0 : 0;
-            if (!rows) break;
-            if (wait_bands && bi < landed.size()) OZTT_CUDA(cudaStreamWaitEvent(st, landed[bi], 0));
-            launch_scale_rows(da + r0 * k, rows, k, k, q.shift, dA.as<int32_t>() + r0, nullptr, flags, st);
-            launch_split_rows(da + r0 * k, rows, k, k, dA.as<int32_t>() + r0, q, ra->as<int8_t>(), rows_p, kp, st);
-            launch_residue_gemm(ra->as<int8_t>(), rb->as<int8_t>(), rows_p, np, kp, q, 1, kpl->p, gemm_err, st, 0);
-            launch_recon(kpl->as<uint8_t>(), rows_p, np, dA.as<int32_t>() + r0, dB.as<int32_t>(), q, dc + r0 * n, rows,
-                         n, n, st);
-            call.band_done(r0, rows);
-        }
+        for (uint64_t r0 = 0; r0 < m; r0 += bm) band(q, r0);
     };
     if (rc0 == OZTT_OK) {
         check_plan(p0);
-        pipeline(p0, true);
+        following(p0);
     }
-    // every value checked, then the reference's plan: decided by the bounds, or from the exact sums
+    // every value checked (from the host's maxima); then C is read back as its bands finish when writing it
+    // before the plan is confirmed cannot change the outcome of the call
+    host.wait();
+    double t = call.ms_since_start();
+    check(host.row_max.data(), host.col_max.data());
+    ph.check_ms = call.ms_since_start() - t;
+    const bool early = rc0 == OZTT_OK && plan_ii_int8_never_fails(m, n, k, max_moduli) &&
+                       !overlaps(c, m * n * 8, a, m * k * 8) && !overlaps(c, m * n * 8, b, k * n * 8);
+    if (early) call.read_back(c);
+    ph.early_readback = early ? 1 : 0;
+    // the reference's plan: decided by the bounds, or from the exact sums
     std::vector<uint64_t> row_max, col_max;
     const PolicyBounds bounds = call.certified_bounds(row_max, col_max);
-    double t = call.ms_since_start();
-    check(row_max.data(), col_max.data());
-    ph.check_ms = call.ms_since_start() - t;
     t = call.ms_since_start();
     bool decided = false;
     int rc = plan_ii_int8_certified(bounds, m, n, k, max_moduli, reconstruction, p, err, decided);
@@ -349,9 +429,11 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     if (!same) {  // the first plan was not the reference's: again, with the reference's plan
         call.discard_bands();
         check_plan(p);
-        pipeline(p, false);
+        whole(p);
+        call.read_back(c);
+    } else if (!early) {
+        call.read_back(c);
     }
-    call.read_back(c);
     uint32_t host_words[2] = {0, 0};
     OZTT_CUDA(cudaMemcpyAsync(host_words, words.p, 8, cudaMemcpyDeviceToHost, st));
     call.finish(ph.first_plan_ms);
@@ -368,8 +450,8 @@ int run_ii_int8_streamed(int device_id, const double* a, const double* b, double
     char buf[1024];
     int inner = OZTT_OK;
     const int rc = guarded(buf, sizeof buf, [&] {
-        // at least two bands of A's rows: the GEMM overlaps A's upload (a first plan from B and A's first band,
-        // confirmed by the complete statistics); smaller calls upload everything first
+        // calls of 4096 rows and more compute while their operands upload (a first plan estimated from A's first
+        // half and B's first block, confirmed by the complete statistics); smaller calls upload everything first
         if (round_up(m, 128) >= 4096)
             inner = run_ii_int8_overlapped(device_id, a, b, c, m, n, k, max_moduli, reconstruction, check, p, err);
         else

@@ -19,6 +19,8 @@
 #include <cfloat>
 #include <cmath>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <numeric>
 #include <random>
 #include <string>
@@ -295,6 +297,35 @@ int policy_width_cap(const PolicyStats& st) {
     return std::min(kMaxDigit * kDigitBits, kTargetBits + (int)std::ceil(std::log2(std::max(k2, 1.0))));
 }
 
+bool plan_ii_int8_never_fails(uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli) {
+    if (m == 0 || n == 0 || k == 0 || max_moduli > (uint32_t)kMaxS) return false;
+    // the outcome depends on the padded K and the limit only (choose_moduli_int8)
+    static std::mutex mu;
+    static std::map<std::pair<uint64_t, uint32_t>, bool> known;
+    const std::pair<uint64_t, uint32_t> key{(k + 31) / 32 * 32, max_moduli};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        const auto it = known.find(key);
+        if (it != known.end()) return it->second;
+    }
+    bool ok = true;
+    for (int b = kTargetBits; ok && b <= kMaxDigit * kDigitBits; ++b) {
+        // statistics whose k2 is exactly 2^(b - 53): the width cap b
+        PolicyStats st;
+        st.measured = true;
+        st.TA = 12.0 * std::ldexp(1.0, 2 * (b - kTargetBits));
+        st.nB = 1.0;
+        st.nC = 1.0;
+        oztt_ii_plan p;
+        std::string err;
+        ok = plan_ii_int8_with([&](uint32_t, uint32_t) { return st; }, m, n, k, max_moduli, OZTT_RECON_AUTO, 0, p,
+                               err) == OZTT_OK;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    known[key] = ok;
+    return ok;
+}
+
 double one_pass_error_log2(const std::vector<int>& mods, int b, const PolicyStats& st) {
     if (!st.measured || !(st.nC > 0) || !(st.TA > 0) || !(st.TB > 0)) return -INFINITY;
     double l2m = 0;
@@ -431,15 +462,20 @@ int plan_ii_int8_certified(const PolicyBounds& bounds, uint64_t m, uint64_t n, u
     PolicyStats low = bounds.lo, high = bounds.hi;  // k2 at its least and at its greatest
     low.nC = bounds.hi.nC * (1 + 1e-12);
     low.nA = bounds.lo.nA * (1 - 1e-12);
+    low.nB = bounds.lo.nB * (1 - 1e-12);
     high.nC = bounds.lo.nC * (1 - 1e-12);
     high.nA = bounds.hi.nA * (1 + 1e-12);
+    high.nB = bounds.hi.nB * (1 + 1e-12);
     for (const PolicyStats* q : {&low, &high})
-        if (!(q->nC > 0) || !(q->nA >= 0) || !std::isfinite(q->nC) || !std::isfinite(q->nA)) return OZTT_OK;
+        if (!(q->nC > 0) || !(q->nA >= 0) || !(q->nB >= 0) || !std::isfinite(q->nC) || !std::isfinite(q->nA) ||
+            !std::isfinite(q->nB))
+            return OZTT_OK;
     const int b_cap = policy_width_cap(low);
     if (policy_width_cap(high) != b_cap) return OZTT_OK;
     // plan at the middle of the bounds: its width cap is the decided one
     PolicyStats mid = bounds.lo;
     mid.nA = 0.5 * (bounds.lo.nA + bounds.hi.nA);
+    mid.nB = 0.5 * (bounds.lo.nB + bounds.hi.nB);
     mid.nC = 0.5 * (bounds.lo.nC + bounds.hi.nC);
     mid.measured = true;
     const int rc = plan_ii_int8_with([&](uint32_t, uint32_t) { return mid; }, m, n, k, max_moduli, reconstruction, 0,

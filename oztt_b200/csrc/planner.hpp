@@ -61,10 +61,10 @@ ModuliChoice choose_moduli_int8(uint32_t K, int num_moduli, int b_cap);
 PolicyStats measure_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
                                  uint32_t K);
 int policy_width_cap(const PolicyStats& st);
-// Bounds of the five statistics: TA, TB, nB known exactly, nA and nC in [lo, hi] (the reference's values,
+// Bounds of the five statistics: TA, TB known exactly, nA, nB and nC in [lo, hi] (the reference's values,
 // which come from sequential sums in its own rounding, lie inside).
 struct PolicyBounds {
-    PolicyStats lo, hi;  // lo: nA and nC at their lower bounds; hi: at their upper bounds
+    PolicyStats lo, hi;  // lo: nA, nB and nC at their lower bounds; hi: at their upper bounds
     bool usable = false;
 };
 // The Scheme II INT8 plan when the bounds decide it: the width cap (and, for Automatic, the number of
@@ -83,6 +83,11 @@ int plan_ii_int8(const double* a, const double* b, uint64_t m, uint64_t n, uint6
 int plan_ii_int8_with(const std::function<PolicyStats(uint32_t, uint32_t)>& stats, uint64_t m, uint64_t n, uint64_t k,
                       uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits, oztt_ii_plan& p,
                       std::string& err);
+
+// Whether the Scheme II INT8 plan for these dimensions and this limit succeeds whatever the statistics:
+// every width cap the statistics can set (53 .. 100 bits) finds its moduli. A call that writes C before its
+// statistics are complete relies on it: its plan cannot fail afterwards.
+bool plan_ii_int8_never_fails(uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli);
 
 // Scheme II digit formats: FP8, BF16, FP16, TF32 (planner_digit.cpp); format is an OZTT_FMT_* value.
 int plan_digit_with(int32_t format, const std::function<PolicyStats(uint32_t, uint32_t)>& stats, uint64_t m,
@@ -210,9 +215,10 @@ struct StreamedPhases {
     double pipeline_ms = 0;    // scale, split, banded GEMM and reconstruction, C read back
     double total_ms = 0;
     int bands = 0;
-    double first_plan_ms = 0;  // overlapped INT8 path: when the first plan (B and A's first band) was made
+    double first_plan_ms = 0;  // overlapped INT8 path: when the first plan (A's first half, B's first block) was made
     int replanned = 0;         // 1 if the complete statistics gave another plan and the pipeline ran again
-    int exact_stats = 0;       // 1 if the bounds left the decision open and A's exact sums were computed
+    int exact_stats = 0;       // 1 if the bounds left the decision open and the exact sums were computed
+    int early_readback = 0;    // 1 if C's bands were read back as they finished, before the plan was confirmed
 };
 StreamedPhases last_streamed_phases();
 

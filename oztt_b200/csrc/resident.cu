@@ -34,10 +34,11 @@ void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, in
 void launch_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
                        const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st);
 void launch_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
-                       const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st);
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st,
+                       uint64_t plane_rows = 0);
 void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
                          const oztt_ii_plan& p, int mode, void* out, int* err_word, cudaStream_t st,
-                         uint64_t a_plane_rows);
+                         uint64_t a_plane_rows, uint64_t b_plane_rows = 0);
 void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA, const int32_t* dB,
                   const oztt_ii_plan& p, double* c, uint64_t m, uint64_t n, uint64_t ldc, cudaStream_t st);
 void check_plan(const oztt_ii_plan& p);

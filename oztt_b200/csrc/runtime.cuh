@@ -153,20 +153,22 @@ public:
     // waits for everything (the read-back included) and records the phases of the call, the pipeline
     // counted from pipeline_start_ms (ms_since_start when it was issued)
     void finish(double pipeline_start_ms);
-    // The upload in two parts, for the INT8 path that overlaps the GEMM with A's upload: B in blocks of
-    // columns with its exact statistics (on a statistics stream), then A in bands of band_rows rows, each
-    // band's bounded statistics measured as it lands (on a high-priority stream, so that they run between
-    // the GEMM's launches); returns the events that mark each band's arrival.
-    void upload_b();
-    std::vector<cudaEvent_t> upload_a_rows(uint64_t band_rows);
-    // An estimate of the statistics with A's rows r0 .. r1-1 (a band) standing for the whole A and B's
-    // complete: what a first plan is made from. Waits for that band's measurements.
-    PolicyStats band_stats(uint64_t r0, uint64_t r1);
-    // After upload_a_rows: bounds of the statistics that contain the reference's values, and the magnitude
+    // The upload of the INT8 path that computes while its operands land: A's first pre_rows rows in bands of
+    // band_rows, then B in blocks of block_cols columns, then the rest of A in bands. Each block of B is
+    // measured as it lands and each band of A once B has landed (one fast pass each that bounds the
+    // reference's statistics, on a high-priority stream, so that it runs between the GEMM's launches).
+    // Returns the events that mark each band's arrival and fills b_landed with those of B's blocks.
+    std::vector<cudaEvent_t> upload_prefix_first(uint64_t pre_rows, uint64_t band_rows, uint64_t block_cols,
+                                                 std::vector<cudaEvent_t>& b_landed);
+    // After upload_prefix_first: the estimate of the statistics from A's first pre_rows rows and B's first
+    // block (estimate_policy_stats); waits for both. ok is false when no estimate could be made.
+    PolicyStats prefix_estimate(uint64_t pre_rows, uint64_t block_cols, cudaEvent_t a_landed, cudaEvent_t b_landed,
+                                bool& ok);
+    // After upload_prefix_first: bounds of the statistics that contain the reference's values, and the magnitude
     // patterns of A's row maxima and B's column maxima (for the value checks). Waits for every band.
     PolicyBounds certified_bounds(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max);
-    // The reference's exact statistics of the whole A and B (A's long-double sums over all of A, after the
-    // work issued so far on the statistics stream), for the rare call whose bounds leave a decision open.
+    // The reference's exact statistics of the whole A and B (its sequential long-double sums), for the rare
+    // call whose bounds leave a decision open.
     PolicyStats exact_stats();
     // forgets the bands marked so far (their C is recomputed)
     void discard_bands() { bands_.clear(); }
@@ -185,10 +187,18 @@ private:
     const double *a_, *b_;
     uint64_t m_, n_, k_;
     std::chrono::steady_clock::time_point t0_;
-    cudaStream_t work_ = nullptr, up_ = nullptr, down_ = nullptr, stat_ = nullptr, cert_ = nullptr;
-    cudaEvent_t b_ready_ = nullptr, a_last_ = nullptr;
+    cudaStream_t work_ = nullptr, up_ = nullptr, down_ = nullptr, stat_ = nullptr, cert_ = nullptr, est_ = nullptr;
+    cudaEvent_t a_last_ = nullptr, b_last_ = nullptr, g_ready_ = nullptr;
     std::unique_ptr<DevBuf> cert_buf_, cert_flags_;
-    std::vector<cudaEvent_t> certified_;  // per band: its bounded statistics are written
+    // B's bounded measurements (upload_prefix_first): per row of B 17 accumulators, the column maxima (n
+    // patterns), the scale, the scaled sketch (8 x k), its error bounds (k), the probe vectors (8 x N)
+    std::unique_ptr<DevBuf> bparts_;
+    double* b_acc() const { return bparts_->as<double>(); }
+    unsigned long long* b_colmax() const { return reinterpret_cast<unsigned long long*>(b_acc() + k_ * 17); }
+    double* b_rg() const { return b_acc() + k_ * 17 + n_; }
+    double* b_y() const { return b_rg() + 1; }
+    double* b_ew() const { return b_y() + 8 * k_; }
+    double* b_probe() const { return b_ew() + k_; }
     std::vector<cudaEvent_t> events_;
     std::vector<Band> bands_;
     std::unique_ptr<DevBuf> da_, db_, dc_;

@@ -42,6 +42,10 @@ struct SplitConst {
     float nz;  // -0.0, the run-time addend of the packed multiplies (mul2 in oztt_common.cuh)
     float m[OZTT_MAXS], rinv[OZTT_MAXS];
     float c[4][OZTT_MAXS];
+    // odd moduli (bit s): their residues from one exact sum of weighted digit terms (store_residues);
+    // w[j][s] = the symmetric residue of 2^e mod m_s for the j-th weighted term (split_const)
+    uint32_t odd;
+    float w[8][OZTT_MAXS];
     // FP8 digits: radix q, fl(1/q) (stages.hpp:222-223), splitting method, first digit plane
     float q[OZTT_MAXS], qinv[OZTT_MAXS];
     int32_t mode[OZTT_MAXS], poff[OZTT_MAXS];
@@ -265,23 +269,89 @@ __device__ __forceinline__ uint32_t pack4(f32x2 r01, f32x2 r23) {
 }
 
 // Writes the S residue planes of 16 elements whose digits are in dg (8 pairs x ND) to dst + s*plane.
-template <int ND>
-__device__ __forceinline__ void store_residues(const f32x2 (&dg)[8][ND], const SplitConst& sc, int8_t* dst,
-                                               uint64_t plane) {
+//
+// An even modulus follows the reference's chain (residue2), whose binary32 roundings decide the sign of a
+// residue of m/2. For an odd modulus the residue is the symmetric one, r in [-(m-1)/2, (m-1)/2], whatever the
+// chain; it is computed here with fewer operations, as one exact integer sum and one ModRound: A' = sum_i
+// d_i 2^(20 (ND-1-i)), and every digit whose product with a weight 2^e mod m (symmetric, |.| <= 127) could
+// leave the exact range of binary32 is first split into 10-bit halves (d = 1024 h + l, h = rint(d/1024),
+// both exact). The lower digits are below 2^19 + 1, so they are split; the top digit is below 2^shift and
+// is split only when shift > 16 (TOP): with it whole the sum is below 2^16 * 127 + 6 * 513 * 127 + 2^19 + 1
+// < 2^24, exact. ModRound of that exact integer gives the symmetric residue (x * fl(1/m) is within 1/(4m)
+// of x/m, and x/m is at least 1/(2m) from a half-integer when m is odd). The residues are the reference's,
+// bit for bit. The terms of a pair: the top digit or its halves, the halves of the middle digits, the last
+// digit (weight 1); NT of them carry a weight w[j][s] (split_const).
+template <int ND, bool TOP>
+struct ResidueTerms {
+    static constexpr int NT = TOP ? 2 * (ND - 1) : 2 * ND - 3;
+};
+
+// The terms of pairs E0 .. E0+NPAIR-1, then their residues: 2*NPAIR bytes per plane at dst + s*plane +
+// 2*E0. Rows of A store 8 bytes twice (fewer live registers); the transposed planes of B store 16 bytes
+// at once (a whole half sector per lane).
+template <int ND, bool TOP, int E0, int NPAIR>
+__device__ __forceinline__ void store_residues_part(const f32x2 (&dg)[8][ND], const SplitConst& sc, int8_t* dst,
+                                                    uint64_t plane) {
     const f32x2 nz = splat2(sc.nz);
+    constexpr int NT = ResidueTerms<ND, TOP>::NT;
+    constexpr int I0 = TOP ? 0 : 1;  // the first digit that is split
+    f32x2 t[NPAIR][NT + 1];
+    {
+        const f32x2 inv = splat2(0.0009765625f), neg = splat2(-1024.0f);
+#pragma unroll
+        for (int e = 0; e < NPAIR; ++e) {
+            if constexpr (!TOP) t[e][0] = dg[E0 + e][0];
+#pragma unroll
+            for (int i = I0; i < ND - 1; ++i) {
+                const f32x2 h = rint2(mul2(dg[E0 + e][i], inv, nz));
+                t[e][2 * i - I0] = h;
+                t[e][2 * i - I0 + 1] = fma2(h, neg, dg[E0 + e][i]);
+            }
+            t[e][NT] = dg[E0 + e][ND - 1];
+        }
+    }
+    const f32x2 k1024 = splat2(1024.0f);
     for (int s = 0; s < sc.S; ++s) {
         const f32x2 negm = splat2(-sc.m[s]), ri = splat2(sc.rinv[s]);
-        const f32x2 c0 = splat2(sc.c[0][s]), c1 = splat2(sc.c[1][s]), c2 = splat2(sc.c[2][s]),
-                    c3 = splat2(sc.c[3][s]);
-        f32x2 r[8];
+        f32x2 r[NPAIR];
+        if ((sc.odd >> s) & 1u) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) r[e] = residue2<ND>(dg[e], negm, ri, c0, c1, c2, c3, nz);
-        uint4 v;
-        v.x = pack4(r[0], r[1]);
-        v.y = pack4(r[2], r[3]);
-        v.z = pack4(r[4], r[5]);
-        v.w = pack4(r[6], r[7]);
-        *reinterpret_cast<uint4*>(dst + (uint64_t)s * plane) = v;
+            for (int e = 0; e < NPAIR; ++e) {
+                f32x2 acc = t[e][NT];
+#pragma unroll
+                for (int j = 0; j < NT; ++j) acc = fma2(t[e][j], splat2(sc.w[j][s]), acc);
+                r[e] = mod_round2(acc, negm, ri, nz);
+            }
+        } else {
+            const f32x2 c0 = splat2(sc.c[0][s]), c1 = splat2(sc.c[1][s]), c2 = splat2(sc.c[2][s]),
+                        c3 = splat2(sc.c[3][s]);
+#pragma unroll
+            for (int e = 0; e < NPAIR; ++e) {
+                f32x2 d[ND];
+                if constexpr (!TOP) d[0] = t[e][0];
+#pragma unroll
+                for (int i = I0; i < ND - 1; ++i) d[i] = fma2(t[e][2 * i - I0], k1024, t[e][2 * i - I0 + 1]);
+                d[ND - 1] = t[e][NT];
+                r[e] = residue2<ND>(d, negm, ri, c0, c1, c2, c3, nz);
+            }
+        }
+        int8_t* o = dst + (uint64_t)s * plane + 2 * E0;
+        if constexpr (NPAIR == 4)
+            *reinterpret_cast<uint2*>(o) = make_uint2(pack4(r[0], r[1]), pack4(r[2], r[3]));
+        else
+            *reinterpret_cast<uint4*>(o) =
+                make_uint4(pack4(r[0], r[1]), pack4(r[2], r[3]), pack4(r[4], r[5]), pack4(r[6], r[7]));
+    }
+}
+
+template <int ND, bool TOP, bool ROWS>
+__device__ __forceinline__ void store_residues(const f32x2 (&dg)[8][ND], const SplitConst& sc, int8_t* dst,
+                                               uint64_t plane) {
+    if constexpr (ROWS) {
+        store_residues_part<ND, TOP, 0, 4>(dg, sc, dst, plane);
+        store_residues_part<ND, TOP, 4, 4>(dg, sc, dst, plane);
+    } else {
+        store_residues_part<ND, TOP, 0, 8>(dg, sc, dst, plane);
     }
 }
 
@@ -360,18 +430,24 @@ __device__ __forceinline__ void store_digits(const f32x2 (&dg)[8][ND], const Spl
     }
 }
 
-template <int ND, bool DIG>
+// What a split kernel stores: residues with the top digit split (kTopSplit) or whole (kTopWhole), or the
+// digit planes of the digit formats (kDigits).
+constexpr int kTopSplit = 0, kTopWhole = 1, kDigits = 2;
+
+template <int ND, int MODE, bool ROWS>
 __device__ __forceinline__ void store_planes(const f32x2 (&dg)[8][ND], const SplitConst& sc, int8_t* dst,
                                              uint64_t plane) {
-    if constexpr (DIG)
+    if constexpr (MODE == kDigits)
         store_digits<ND>(dg, sc, dst, plane);
     else
-        store_residues<ND>(dg, sc, dst, plane);
+        store_residues<ND, MODE == kTopSplit, ROWS>(dg, sc, dst, plane);
 }
 
-// A: one thread = 16 consecutive elements of one row.
-template <int ND, bool DIG>
-__global__ void __launch_bounds__(256) split_rows_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
+// A: one thread = 16 consecutive elements of one row. (ND = 3 with the top digit whole, the widths of the
+// usual plans: at most 85 registers, so that three blocks share an SM -- measured 2.78 against 3.08 ms at
+// 16384^2 x 17 moduli with two.)
+template <int ND, int MODE>
+__global__ void __launch_bounds__(256, (ND == 3 && MODE == kTopWhole) ? 3 : 1) split_rows_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
                                                          uint64_t lda, const int32_t* __restrict__ delta,
                                                          int8_t* __restrict__ planes, uint64_t mp, uint64_t kp,
                                                          const SplitConst sc) {
@@ -397,20 +473,20 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const double* __restric
         f32x2 dg[8][ND];
 #pragma unroll
         for (int e = 0; e < 8; ++e) make_digits2<ND>(x[2 * e], x[2 * e + 1], d, splat2(sc.nz), dg[e]);
-        store_planes<ND, DIG>(dg, sc, planes + row * kp + k0, plane);
+        store_planes<ND, MODE, true>(dg, sc, planes + row * kp + k0, plane);
     }
 }
 
 // B: a warp covers 16 columns x 32 rows of B; lane l takes column (l & 15) and the 16 rows of half
-// (l >> 4), so lanes l and l+16 write the two halves of one 32-byte sector of the transposed plane.
-template <int ND, bool DIG>
+// (l >> 4), so lanes l and l+16 write the two halves of one 32-byte sector of the transposed plane. The
+// planes are `plane` bytes apart (np * kp, or more for a block of the columns of wider planes).
+template <int ND, int MODE>
 __global__ void __launch_bounds__(256) split_cols_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
                                                          uint64_t ldb, const int32_t* __restrict__ delta,
                                                          int8_t* __restrict__ planes, uint64_t np, uint64_t kp,
-                                                         const SplitConst sc) {
+                                                         uint64_t plane, const SplitConst sc) {
     const int lane = threadIdx.x & 31;
     const uint64_t col_groups = np >> 4, row_groups = kp >> 5, total = col_groups * row_groups;
-    const uint64_t plane = np * kp;
     for (uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total;
          w += ((uint64_t)gridDim.x * blockDim.x) >> 5) {
         const uint64_t cg = w % col_groups, rg = w / col_groups;
@@ -423,7 +499,7 @@ __global__ void __launch_bounds__(256) split_cols_kernel(const double* __restric
         f32x2 dg[8][ND];
 #pragma unroll
         for (int e = 0; e < 8; ++e) make_digits2<ND>(x[2 * e], x[2 * e + 1], d, splat2(sc.nz), dg[e]);
-        store_planes<ND, DIG>(dg, sc, planes + col * kp + r0, plane);
+        store_planes<ND, MODE, false>(dg, sc, planes + col * kp + r0, plane);
     }
 }
 
@@ -435,14 +511,38 @@ static int device_sms() {
     return sms;
 }
 
+// The residue mode of a plan: the top digit whole when it is below 2^16 (shift <= 16; store_residues).
+static int residue_mode(const oztt_ii_plan& p) { return p.shift <= 16 ? kTopWhole : kTopSplit; }
+
+// 2^e mod m as the symmetric residue in [-(m-1)/2, m/2].
+static float pow2_mod_symmetric(int e, int32_t m) {
+    int64_t r = 1 % m;
+    for (int t = 0; t < e; ++t) r = (r * 2) % m;
+    if (r > m / 2) r -= m;
+    return (float)r;
+}
+
 static SplitConst split_const(const oztt_ii_plan& p) {
     SplitConst sc{};
     sc.S = p.S;
     sc.nz = -0.0f;
+    const bool top_whole = residue_mode(p) == kTopWhole;
     for (int s = 0; s < p.S; ++s) {
         sc.m[s] = (float)p.moduli[s];
         sc.rinv[s] = p.rinv[s];
         for (int j = 0; j < 4; ++j) sc.c[j][s] = p.c[j][s];
+        const int32_t m = p.moduli[s];
+        if (m % 2 == 1 && p.nd >= 3 && p.nd <= 5) {
+            sc.odd |= 1u << s;
+            // the weighted terms of store_residues_part, top first: the top digit (exponent 20 (nd-1)) or
+            // its halves, then the halves of digits 1 .. nd-2 (exponents 20 (nd-1-i) + 10 and 20 (nd-1-i))
+            int j = 0;
+            if (top_whole) sc.w[j++][s] = pow2_mod_symmetric(20 * (p.nd - 1), m);
+            for (int i = top_whole ? 1 : 0; i < p.nd - 1; ++i) {
+                sc.w[j++][s] = pow2_mod_symmetric(20 * (p.nd - 1 - i) + 10, m);
+                sc.w[j++][s] = pow2_mod_symmetric(20 * (p.nd - 1 - i), m);
+            }
+        }
     }
     return sc;
 }
@@ -486,33 +586,36 @@ void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, in
     launch_scale_cols_mode(b, k, n, ldb, shift, 1u, delta, bfmax, flags, colmax, st);
 }
 
-template <bool DIG>
-static void split_rows_any(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int nd,
-                           const SplitConst& sc, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
+template <int MODE>
+static void split_rows_nd(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int nd,
+                          const SplitConst& sc, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
     if (mp % 16 || kp % 16) throw Error(OZTT_EINVAL, "split_rows: padded dimensions must be multiples of 16");
     const uint64_t total = mp * (kp / 16);
     const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)device_sms() * 32);
     if (total == 0) return;
     switch (nd) {
-    case 3: split_rows_kernel<3, DIG><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
-    case 4: split_rows_kernel<4, DIG><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
-    case 5: split_rows_kernel<5, DIG><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
+    case 3: split_rows_kernel<3, MODE><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
+    case 4: split_rows_kernel<4, MODE><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
+    case 5: split_rows_kernel<5, MODE><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
     default: throw Error(OZTT_EINVAL, "split: the number of digits must be 3, 4 or 5");
     }
     OZTT_CUDA(cudaGetLastError());
 }
 
-template <bool DIG>
-static void split_cols_any(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta, int nd,
-                           const SplitConst& sc, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
+template <int MODE>
+static void split_cols_nd(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta, int nd,
+                          const SplitConst& sc, int8_t* planes, uint64_t np, uint64_t kp, uint64_t plane_rows,
+                          cudaStream_t st) {
     if (np % 16 || kp % 32) throw Error(OZTT_EINVAL, "split_cols: np must be a multiple of 16 and kp of 32");
+    if (plane_rows < np) throw Error(OZTT_EINVAL, "split_cols: block wider than its planes");
     const uint64_t warps = (np / 16) * (kp / 32);
     if (warps == 0) return;
     const unsigned blocks = (unsigned)std::min<uint64_t>((warps + 7) / 8, (uint64_t)device_sms() * 32);
+    const uint64_t plane = plane_rows * kp;
     switch (nd) {
-    case 3: split_cols_kernel<3, DIG><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
-    case 4: split_cols_kernel<4, DIG><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
-    case 5: split_cols_kernel<5, DIG><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, sc); break;
+    case 3: split_cols_kernel<3, MODE><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, plane, sc); break;
+    case 4: split_cols_kernel<4, MODE><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, plane, sc); break;
+    case 5: split_cols_kernel<5, MODE><<<blocks, 256, 0, st>>>(b, k, n, ldb, delta, planes, np, kp, plane, sc); break;
     default: throw Error(OZTT_EINVAL, "split: the number of digits must be 3, 4 or 5");
     }
     OZTT_CUDA(cudaGetLastError());
@@ -520,12 +623,22 @@ static void split_cols_any(const double* b, uint64_t k, uint64_t n, uint64_t ldb
 
 void launch_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
                        const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
-    split_rows_any<false>(a, m, k, lda, delta, p.nd, split_const(p), planes, mp, kp, st);
+    if (residue_mode(p) == kTopWhole)
+        split_rows_nd<kTopWhole>(a, m, k, lda, delta, p.nd, split_const(p), planes, mp, kp, st);
+    else
+        split_rows_nd<kTopSplit>(a, m, k, lda, delta, p.nd, split_const(p), planes, mp, kp, st);
 }
 
+// plane_rows: when nonzero, planes points at row c0 of planes that are plane_rows tall (columns c0 ..
+// c0+np-1 of wider planes: a block of B's columns, split as it lands).
 void launch_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
-                       const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
-    split_cols_any<false>(b, k, n, ldb, delta, p.nd, split_const(p), planes, np, kp, st);
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st,
+                       uint64_t plane_rows) {
+    const uint64_t pr = plane_rows ? plane_rows : np;
+    if (residue_mode(p) == kTopWhole)
+        split_cols_nd<kTopWhole>(b, k, n, ldb, delta, p.nd, split_const(p), planes, np, kp, pr, st);
+    else
+        split_cols_nd<kTopSplit>(b, k, n, ldb, delta, p.nd, split_const(p), planes, np, kp, pr, st);
 }
 
 static SplitConst digit_const(const oztt_digit_plan& fp) {
@@ -542,12 +655,12 @@ static SplitConst digit_const(const oztt_digit_plan& fp) {
 // Digit planes of A ([nplane][mp][kp]) and of B transposed ([nplane][np][kp]).
 void launch_digit_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
                              const oztt_digit_plan& fp, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
-    split_rows_any<true>(a, m, k, lda, delta, fp.base.nd, digit_const(fp), planes, mp, kp, st);
+    split_rows_nd<kDigits>(a, m, k, lda, delta, fp.base.nd, digit_const(fp), planes, mp, kp, st);
 }
 
 void launch_digit_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
                              const oztt_digit_plan& fp, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st) {
-    split_cols_any<true>(b, k, n, ldb, delta, fp.base.nd, digit_const(fp), planes, np, kp, st);
+    split_cols_nd<kDigits>(b, k, n, ldb, delta, fp.base.nd, digit_const(fp), planes, np, kp, np, st);
 }
 
 }  // namespace oztt

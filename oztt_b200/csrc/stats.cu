@@ -209,12 +209,15 @@ __global__ void __launch_bounds__(128) sketch_kernel(const double* __restrict__ 
 // for deciding the plan without the reference's sequential long-double sums: per row, into out[r*kCertW ..]:
 //   [0]          the largest magnitude as its bit pattern (NaN and Inf patterns order above every number)
 //   [1]          sum x^2            [2 .. 9]   sum x * y_l            [10 .. 17]  sum |x * y_l|
+//   [18]         sum |x| * ew       (0 when ew is null)
 // all unscaled, in FP64 (fused multiply-adds, the warp's order); the host turns them into bounds that
-// contain the reference's values. y: the 8 x k sketch y_l = B g_l of the reference (scaled). flags |= 1
+// contain the reference's values. y: the 8 x k sketch y_l = B g_l (scaled), as the reference has it or as
+// bcert_finish_kernel bounds it (then ew[j] bounds |y_l[j] - the reference's y_l[j]| over l). flags |= 1
 // when a nonzero element below 2^-383 makes the scaled squares leave the normal range (no bounds then).
-constexpr int kCertW = 18;
+constexpr int kCertW = 19;
 __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restrict__ x, uint64_t rows, uint64_t k,
-                                                           const double* __restrict__ y, double* __restrict__ out,
+                                                           const double* __restrict__ y,
+                                                           const double* __restrict__ ew, double* __restrict__ out,
                                                            uint32_t* __restrict__ flags) {
     const uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -222,7 +225,7 @@ __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restr
     const double* xr = x + r * k;
     unsigned long long mx = 0;
     bool tiny = false;
-    double s2 = 0.0, sl[kVectors], al[kVectors];
+    double s2 = 0.0, se = 0.0, sl[kVectors], al[kVectors];
 #pragma unroll
     for (int l = 0; l < kVectors; ++l) sl[l] = al[l] = 0.0;
     for (uint64_t j = lane; j < k; j += 32) {
@@ -231,6 +234,7 @@ __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restr
         mx = pat > mx ? pat : mx;
         tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);  // 0 < |v| < 2^-383
         s2 = fma(v, v, s2);
+        if (ew) se = fma(fabs(v), __ldg(ew + j), se);
 #pragma unroll
         for (int l = 0; l < kVectors; ++l) {
             const double t = v * __ldg(y + (uint64_t)l * k + j);
@@ -243,6 +247,7 @@ __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restr
         const unsigned long long om = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
         mx = om > mx ? om : mx;
         s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
+        se += __shfl_xor_sync(0xFFFFFFFFu, se, o);
 #pragma unroll
         for (int l = 0; l < kVectors; ++l) {
             sl[l] += __shfl_xor_sync(0xFFFFFFFFu, sl[l], o);
@@ -259,6 +264,78 @@ __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restr
             o[2 + l] = sl[l];
             o[2 + kVectors + l] = al[l];
         }
+        o[18] = se;
+    }
+}
+
+// Bounded statistics of B, a block of columns at a time as the blocks land (b: k rows of w elements from the
+// block's first column, rows ldb apart; g: the probe vectors from the block's first column, gstride apart);
+// one warp per row r of B, accumulating into acc[r*kBCertW ..] (zeroed before the first block):
+//   [0 .. 7]  sum b g_l        [8 .. 15]  sum |b g_l|        [16]  sum b^2
+// unscaled, in FP64 (the warp's order, the blocks one after another). flags |= 1 when a nonzero element
+// below 2^-383 is met (the scaled values could leave the normal range: no bounds then).
+constexpr int kBCertW = 17;
+__global__ void __launch_bounds__(256) bcert_block_kernel(const double* __restrict__ b, uint64_t k, uint64_t w,
+                                                          uint64_t ldb, const double* __restrict__ g, uint64_t gstride,
+                                                          double* __restrict__ acc, uint32_t* __restrict__ flags) {
+    const uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= k) return;
+    const double* br = b + r * ldb;
+    bool tiny = false;
+    double s2 = 0.0, sl[kVectors], al[kVectors];
+#pragma unroll
+    for (int l = 0; l < kVectors; ++l) sl[l] = al[l] = 0.0;
+    for (uint64_t c = lane; c < w; c += 32) {
+        const double v = __ldg(br + c);
+        const unsigned long long pat = (unsigned long long)__double_as_longlong(v) & 0x7FFFFFFFFFFFFFFFull;
+        tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);
+        s2 = fma(v, v, s2);
+#pragma unroll
+        for (int l = 0; l < kVectors; ++l) {
+            const double t = v * __ldg(g + (uint64_t)l * gstride + c);
+            sl[l] += t;
+            al[l] += fabs(t);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
+#pragma unroll
+        for (int l = 0; l < kVectors; ++l) {
+            sl[l] += __shfl_xor_sync(0xFFFFFFFFu, sl[l], o);
+            al[l] += __shfl_xor_sync(0xFFFFFFFFu, al[l], o);
+        }
+    }
+    if (__any_sync(0xFFFFFFFFu, tiny) && lane == 0) atomicOr(flags, 1u);
+    if (lane == 0) {
+        double* o = acc + r * kBCertW;
+#pragma unroll
+        for (int l = 0; l < kVectors; ++l) {
+            o[l] += sl[l];
+            o[kVectors + l] += al[l];
+        }
+        o[16] += s2;
+    }
+}
+
+// After B's last block: the scaled sketch y_l[r] = acc_l[r] * rgB (8 x k, as band_certify_kernel reads it)
+// and ew[r], a bound of |y_l[r] - the reference's y_l[r]| over l: c1 * sum |b g_l| * rgB + u |y_l[r]|, with
+// c1 covering this FP64 sum and the reference's long-double one (bcert_error_factor).
+__global__ void __launch_bounds__(256) bcert_finish_kernel(const double* __restrict__ acc, uint64_t k,
+                                                           const double* __restrict__ rgp, double c1,
+                                                           double* __restrict__ y, double* __restrict__ ew) {
+    const double rg = *rgp;
+    for (uint64_t r = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; r < k; r += (uint64_t)gridDim.x * blockDim.x) {
+        const double* o = acc + r * kBCertW;
+        double e = 0.0;
+#pragma unroll
+        for (int l = 0; l < kVectors; ++l) {
+            const double v = o[l] * rg;
+            y[(uint64_t)l * k + r] = v;
+            e = fmax(e, c1 * (o[kVectors + l] * rg) + 0x1p-53 * fabs(v));
+        }
+        ew[r] = e;
     }
 }
 
@@ -638,24 +715,85 @@ void launch_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double r
 
 std::vector<double> policy_vectors_host(uint32_t N) { return *policy_vectors(N); }
 
-void launch_band_certify(const double* x, uint64_t rows, uint64_t k, const double* y, double* out, uint32_t* flags,
-                         cudaStream_t st) {
+void launch_band_certify(const double* x, uint64_t rows, uint64_t k, const double* y, const double* ew, double* out,
+                         uint32_t* flags, cudaStream_t st) {
     if (!rows) return;
-    band_certify_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(x, rows, k, y, out, flags);
+    band_certify_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(x, rows, k, y, ew, out, flags);
     OZTT_CUDA(cudaGetLastError());
 }
 
-// Bounds of nA and nC around the reference's values from the rows' bounded statistics (cert: m x kCertW as
-// band_certify_kernel writes them) and B's exact parts; TA, TB, nB exact. Error terms, with gamma(n, u) =
-// n u / (1 - n u), u = 2^-53 for binary64 and 2^-64 for the reference's long double:
+// Column maxima (magnitude patterns) of k rows of w columns, rows ldb apart, merged into out (atomic maxima:
+// out holds zeros or earlier maxima).
+void launch_col_absmax(const double* b, uint64_t k, uint64_t w, uint64_t ldb, unsigned long long* out,
+                       cudaStream_t st) {
+    if (!k || !w) return;
+    int dev = 0, sms = 148;
+    OZTT_CUDA(cudaGetDevice(&dev));
+    OZTT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const uint64_t col_blocks = (w + 255) / 256;
+    const uint64_t want = std::max<uint64_t>(1, (uint64_t)sms * 8 / col_blocks);
+    const uint64_t chunks = std::min<uint64_t>(std::min<uint64_t>(want, k), 65535);
+    const uint64_t rpc = (k + chunks - 1) / chunks;
+    col_absmax_kernel<<<dim3((unsigned)col_blocks, (unsigned)((k + rpc - 1) / rpc)), 256, 0, st>>>(b, k, w, ldb, rpc,
+                                                                                                 out);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void launch_bcert_block(const double* b, uint64_t k, uint64_t w, uint64_t ldb, const double* g, uint64_t gstride,
+                        double* acc, uint32_t* flags, cudaStream_t st) {
+    if (!k || !w) return;
+    bcert_block_kernel<<<(unsigned)((k * 32 + 255) / 256), 256, 0, st>>>(b, k, w, ldb, g, gstride, acc, flags);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+// B's scale from its column maxima (patterns, n of them) into *rgB, then the scaled sketch and the bounds of
+// its error (bcert_finish_kernel).
+void launch_bcert_finish(const unsigned long long* col_max, uint64_t n, const double* acc, uint64_t k, double c1,
+                         double* rgB, double* y, double* ew, cudaStream_t st) {
+    pow2_scale_kernel<<<1, 1024, 0, st>>>(col_max, n, rgB);
+    OZTT_CUDA(cudaGetLastError());
+    bcert_finish_kernel<<<(unsigned)std::min<uint64_t>((k + 255) / 256, 1024), 256, 0, st>>>(acc, k, rgB, c1, y, ew);
+    OZTT_CUDA(cudaGetLastError());
+}
+
+// c1 of bcert_finish_kernel for rows of n elements: this pass's FP64 sum (products and additions in a
+// lane, the warp's shuffles, the blocks' partial sums: fewer than n + 64 roundings on any term's path) and
+// the reference's long-double sum (n products and additions, gamma(n + 2, 2^-64)), with room for the final
+// rounding of the reference's sum to double.
+double bcert_error_factor(uint64_t n) {
+    auto gamma = [](double cnt, double u) { return cnt * u / (1.0 - cnt * u); };
+    const double u = 0x1p-53;
+    return (gamma((double)n + 64, u) + gamma((double)n + 2, 0x1p-64)) * (1 + 4 * u) + 2 * u;
+}
+
+// Bounds of the reference's nB (per column a sequential double sum of the scaled squares, then a sequential
+// sum over the columns) from the bounded pass: acc[r*kBCertW + 16] = the unscaled sum of row r's squares.
+// With T the exact sum, the reference's value is within (gamma(k+1) + gamma(n+1) + their product) T of
+// T, and the sum formed here (row sums in FP64, then over the rows) within gamma(n + k + 64) T.
+void bounded_nb(const double* acc, uint64_t k, uint64_t n, double rgB, double& lo, double& hi) {
+    auto gamma = [](double cnt, double u) { return cnt * u / (1.0 - cnt * u); };
+    const double u = 0x1p-53;
+    double t = 0;
+    for (uint64_t r = 0; r < k; ++r) t += acc[r * kBCertW + 16] * rgB * rgB;
+    const double gk = gamma((double)k + 1, u), gn = gamma((double)n + 1, u);
+    const double e = gk + gn + gk * gn + gamma((double)(n + k) + 64, u) + 4 * u;
+    lo = t * (1 - e);
+    hi = t * (1 + e);
+}
+
+// Bounds of nA, nB and nC around the reference's values from the rows' bounded statistics (cert: m x kCertW as
+// band_certify_kernel writes them), B's column maxima (exact) and bounds of B's nB; TA, TB exact. Error terms,
+// with gamma(n, u) = n u / (1 - n u), u = 2^-53 for binary64 and 2^-64 for the reference's long double:
 //   a row's sum of squares: each side (the reference's sequential one, this warp-order one) is within
 //     gamma(k+1, u) of the exact sum of positive terms;
 //   a sketch value s_l[r]: the reference's long-double sum is within gamma(k+1, 2^-64) sum |t| of the exact
-//     sum and is rounded once to double, this one within gamma(k+1, u) sum |t|;
+//     sum and is rounded once to double, this one within gamma(k+1, u) sum |t|; when y is this pass's bound
+//     of B's sketch rather than the reference's (cert[18] nonzero), the two sums differ by a further
+//     sum_j |x_j| ew_j at most;
 //   the sums over rows (nA, each ||s_l||^2) gain gamma(m+1, u) on each side; nC's last few operations
 //     16 u. The bounds are widened by these, so the reference's values lie inside.
 PolicyBounds certified_policy_bounds(const double* cert, uint64_t m, uint64_t k, const double* col_max, uint64_t n,
-                                     const double* col_sumsq, double rgB) {
+                                     double nB_lo, double nB_hi, double rgB) {
     PolicyBounds pb;
     auto gamma = [](double cnt, double u) { return cnt * u / (1.0 - cnt * u); };
     const double u = 0x1p-53, ue = 0x1p-64;
@@ -674,11 +812,11 @@ PolicyBounds certified_policy_bounds(const double* cert, uint64_t m, uint64_t k,
         std::frexp(topv, &e);
         rgA = std::ldexp(1.0, -std::min(std::max(e, -1000), 1000));
     }
-    // TA, TB, nB exactly as the reference sums them (combine_policy_stats with zero placeholders for nA, nC)
-    std::vector<double> row_max(m), zeros(m, 0.0), zs(8 * m, 0.0);
+    // TA and TB exactly as the reference sums them (combine_policy_stats with zero placeholders for the sums)
+    std::vector<double> row_max(m), zeros(std::max(m, n), 0.0), zs(8 * m, 0.0);
     for (uint64_t r = 0; r < m; ++r) row_max[r] = cert[r * kCertW];
-    const PolicyStats exact = combine_policy_stats(row_max.data(), m, col_max, n, zeros.data(), col_sumsq, zs.data(), m,
-                                                   rgA, rgB);
+    const PolicyStats exact = combine_policy_stats(row_max.data(), m, col_max, n, zeros.data(), zeros.data(),
+                                                   zs.data(), m, rgA, rgB);
     const double g_row = gamma((double)k + 1, u), g_rowe = gamma((double)k + 1, ue), g_sum = gamma((double)m + 1, u);
     long double nA = 0, q_lo[8] = {}, q_hi[8] = {};
     const double s2scale = rgA * rgA;
@@ -686,8 +824,8 @@ PolicyBounds certified_policy_bounds(const double* cert, uint64_t m, uint64_t k,
         const double* c = cert + r * kCertW;
         nA += (long double)(c[1] * s2scale);
         for (int l = 0; l < 8; ++l) {
-            const double sv = c[2 + l] * rgA, av = c[10 + l] * rgA;
-            const double d = (g_row * (1 + u) + g_rowe) * av + u * std::fabs(sv) + 0x1p-1000;
+            const double sv = c[2 + l] * rgA, av = c[10 + l] * rgA, ev = c[18] * rgA;
+            const double d = ((g_row * (1 + u) + g_rowe) * (av + ev) + ev + u * std::fabs(sv)) * (1 + 4 * u) + 0x1p-1000;
             const double lo = std::max(0.0, std::fabs(sv) - d), hi = std::fabs(sv) + d;
             q_lo[l] += (long double)lo * lo;
             q_hi[l] += (long double)hi * hi;
@@ -704,14 +842,106 @@ PolicyBounds certified_policy_bounds(const double* cert, uint64_t m, uint64_t k,
     };
     pb.lo = pb.hi = exact;
     pb.lo.measured = pb.hi.measured = true;
+    pb.lo.nB = nB_lo;
+    pb.hi.nB = nB_hi;
     pb.lo.nA = (double)nA * (1 - e_nA);
     pb.hi.nA = (double)nA * (1 + e_nA);
     pb.lo.nC = nc_of(q_lo) * (1 - g_sum - 16 * u);
     pb.hi.nC = nc_of(q_hi) * (1 + g_sum + 16 * u);
-    pb.usable = std::isfinite(pb.hi.nA) && std::isfinite(pb.hi.nC) && pb.lo.nC > 0 && rgA * topv < 2.0;
+    pb.usable = std::isfinite(pb.hi.nA) && std::isfinite(pb.hi.nC) && std::isfinite(nB_hi) && nB_lo >= 0 &&
+                pb.lo.nC > 0 && rgA * topv < 2.0;
     return pb;
 }
 
+
+// ---- a first estimate from parts of A and B ------------------------------------------------------------------
+// For a block of B's columns (k rows of w elements, rows ldb apart), one warp per row r: the row's sum of
+// squares over the block and y_l[r] = sum_c b[r][c] g_l[c] (the sketch of the block), unscaled, in FP64.
+__global__ void __launch_bounds__(256) block_rows_kernel(const double* __restrict__ b, uint64_t k, uint64_t w,
+                                                         uint64_t ldb, const double* __restrict__ g, uint64_t gstride,
+                                                         double* __restrict__ y, double* __restrict__ sq) {
+    const uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= k) return;
+    const double* br = b + r * ldb;
+    double s2 = 0.0, sl[kVectors];
+#pragma unroll
+    for (int l = 0; l < kVectors; ++l) sl[l] = 0.0;
+    for (uint64_t c = lane; c < w; c += 32) {
+        const double v = __ldg(br + c);
+        s2 = fma(v, v, s2);
+#pragma unroll
+        for (int l = 0; l < kVectors; ++l) sl[l] = fma(v, __ldg(g + (uint64_t)l * gstride + c), sl[l]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
+#pragma unroll
+        for (int l = 0; l < kVectors; ++l) sl[l] += __shfl_xor_sync(0xFFFFFFFFu, sl[l], o);
+    }
+    if (lane == 0) {
+        sq[r] = s2;
+#pragma unroll
+        for (int l = 0; l < kVectors; ++l) y[(uint64_t)l * k + r] = sl[l];
+    }
+}
+
+// An estimate of the precision policy's statistics with rows [0, rows_a) of A (row-major, k columns)
+// standing for the whole A and columns [0, cols_b) of B (rows ldb apart) for the whole B: each part is
+// measured as if it were the matrix (the statistics enter the width cap through the size-free ratio
+// (TA nB + TB nA) / nC). It is what the first plan of a call that computes while its operands are still
+// uploading is made from, and is then confirmed by the reference's statistics. g: the probe vectors on
+// the device (8 x N). ok is false when a part holds a value that is not finite or the estimate degenerates.
+PolicyStats estimate_policy_stats(const double* a, uint64_t rows_a, uint64_t k, const double* b, uint64_t cols_b,
+                                  uint64_t ldb, const double* g, uint64_t N, cudaStream_t st, bool& ok) {
+    ok = false;
+    if (!rows_a || !cols_b || !k) return {};
+    DevBuf cmax(st, cols_b * 8), y(st, (uint64_t)kVectors * k * 8), sq(st, k * 8), cert(st, rows_a * kCertW * 8),
+        flags(st, 16);
+    OZTT_CUDA(cudaMemsetAsync(cmax.p, 0, cols_b * 8, st));
+    OZTT_CUDA(cudaMemsetAsync(flags.p, 0, 16, st));
+    launch_col_absmax(b, k, cols_b, ldb, cmax.as<unsigned long long>(), st);
+    block_rows_kernel<<<(unsigned)((k * 32 + 255) / 256), 256, 0, st>>>(b, k, cols_b, ldb, g, N, y.as<double>(),
+                                                                        sq.as<double>());
+    OZTT_CUDA(cudaGetLastError());
+    band_certify_kernel<<<(unsigned)((rows_a * 32 + 255) / 256), 256, 0, st>>>(
+        a, rows_a, k, y.as<double>(), nullptr, cert.as<double>(), flags.as<uint32_t>());
+    OZTT_CUDA(cudaGetLastError());
+    std::vector<double> hcmax(cols_b), hsq(k), hcert(rows_a * kCertW);
+    OZTT_CUDA(cudaMemcpyAsync(hcmax.data(), cmax.p, cols_b * 8, cudaMemcpyDeviceToHost, st));
+    OZTT_CUDA(cudaMemcpyAsync(hsq.data(), sq.p, k * 8, cudaMemcpyDeviceToHost, st));
+    OZTT_CUDA(cudaMemcpyAsync(hcert.data(), cert.p, hcert.size() * 8, cudaMemcpyDeviceToHost, st));
+    OZTT_CUDA(cudaStreamSynchronize(st));
+    // the power-of-two scale of each part (the magnitude patterns order like the magnitudes)
+    const auto scale_of = [](double top) {
+        if (!(top > 0) || !std::isfinite(top)) return 1.0;
+        int e = 0;
+        std::frexp(top, &e);
+        return std::ldexp(1.0, -std::min(std::max(e, -1000), 1000));
+    };
+    double top_a = 0, top_b = 0;
+    for (uint64_t r = 0; r < rows_a; ++r) top_a = std::max(top_a, hcert[r * kCertW]);
+    for (uint64_t c = 0; c < cols_b; ++c) top_b = std::max(top_b, hcmax[c]);
+    if (!std::isfinite(top_a) || !std::isfinite(top_b)) return {};
+    const double rgA = scale_of(top_a), rgB = scale_of(top_b);
+    double nb = 0;
+    for (uint64_t r = 0; r < k; ++r) nb += hsq[r];
+    std::vector<double> hmax(rows_a), hs2(rows_a), hsk((uint64_t)kVectors * rows_a);
+    for (uint64_t r = 0; r < rows_a; ++r) {
+        const double* c = hcert.data() + r * kCertW;
+        hmax[r] = c[0];
+        hs2[r] = c[1] * rgA * rgA;
+        for (int l = 0; l < kVectors; ++l) hsk[(uint64_t)l * rows_a + r] = c[2 + l] * rgA * rgB;
+    }
+    std::vector<double> cs2(cols_b, 0.0);
+    cs2[0] = nb * rgB * rgB;  // only the sum over the block's columns enters the statistics
+    const PolicyStats ps =
+        combine_policy_stats(hmax.data(), rows_a, hcmax.data(), cols_b, hs2.data(), cs2.data(), hsk.data(), rows_a,
+                             rgA, rgB);
+    ok = std::isfinite(ps.TA) && std::isfinite(ps.TB) && std::isfinite(ps.nA) && std::isfinite(ps.nB) &&
+         std::isfinite(ps.nC) && ps.nC > 0;
+    return ps;
+}
 
 PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint32_t N,
                                 cudaStream_t st) {
@@ -729,22 +959,34 @@ PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, ui
 // band_certify_kernel writes them) and B's exact parts; bounds5 (NULL or 4 doubles) receives nA lo/hi and nC
 // lo/hi, *decided whether the bounds decided the plan (which is then in *plan).
 extern "C" int oztt_test_certified_plan(const double* cert, uint64_t m, uint64_t n, uint64_t k, const double* col_max,
-                                        const double* col_sumsq, double rgB, uint32_t max_moduli, int32_t reconstruction,
-                                        oztt_ii_plan* plan, int32_t* decided, double* bounds4, char* err,
-                                        size_t errlen) {
+                                        double nB_lo, double nB_hi, double rgB, uint32_t max_moduli,
+                                        int32_t reconstruction, oztt_ii_plan* plan, int32_t* decided, double* bounds6,
+                                        char* err, size_t errlen) {
     return oztt::guarded(err, errlen, [&] {
-        const oztt::PolicyBounds pb = oztt::certified_policy_bounds(cert, m, k, col_max, n, col_sumsq, rgB);
-        if (bounds4) {
-            bounds4[0] = pb.lo.nA;
-            bounds4[1] = pb.hi.nA;
-            bounds4[2] = pb.lo.nC;
-            bounds4[3] = pb.hi.nC;
+        const oztt::PolicyBounds pb = oztt::certified_policy_bounds(cert, m, k, col_max, n, nB_lo, nB_hi, rgB);
+        if (bounds6) {
+            bounds6[0] = pb.lo.nA;
+            bounds6[1] = pb.hi.nA;
+            bounds6[2] = pb.lo.nC;
+            bounds6[3] = pb.hi.nC;
+            bounds6[4] = pb.lo.nB;
+            bounds6[5] = pb.hi.nB;
         }
         bool ok = false;
         std::string msg;
         const int rc = oztt::plan_ii_int8_certified(pb, m, n, k, max_moduli, reconstruction, *plan, msg, ok);
         if (rc != OZTT_OK) throw oztt::Error(rc, msg);
         *decided = ok ? 1 : 0;
+    });
+}
+
+// Test hook: the bounds of nB and the error factor of the bounded pass over B, from its accumulators
+// (k x 17 as bcert_block_kernel leaves them); out3 = {nB low, nB high, c1}.
+extern "C" int oztt_test_bounded_nb(const double* acc, uint64_t k, uint64_t n, double rgB, double* out3, char* err,
+                                    size_t errlen) {
+    return oztt::guarded(err, errlen, [&] {
+        oztt::bounded_nb(acc, k, n, rgB, out3[0], out3[1]);
+        out3[2] = oztt::bcert_error_factor(n);
     });
 }
 

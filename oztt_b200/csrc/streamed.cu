@@ -3,7 +3,9 @@
 // Context::gemm from host buffers with the transfers overlapped (StreamedCall, runtime.cuh), shared by
 // the INT8 and digit-format Scheme II paths.
 //
-//   copy-up stream   B, then A, in blocks of columns of about 64 MiB (2-D copies of all rows)
+//   copy-up stream   B, then A, in blocks of columns of about 64 MiB (2-D copies of all rows); for the
+//                    INT8 path that computes while its operands land (upload_prefix_first): A's first
+//                    half in bands of rows, B in blocks of columns, the rest of A in bands
 //   work stream      the precision-policy statistics of each piece as it lands (PolicyStatsRun), then
 //                    the caller's pipeline, which marks each finished band of rows of C
 //   copy-down stream each finished band of C read back while the next is computed
@@ -28,11 +30,23 @@ void launch_stats_sketch(const double* x, uint64_t rows, uint64_t cols, double r
 PolicyStats combine_policy_stats(const double* row_max, uint64_t m, const double* col_max, uint64_t n,
                                  const double* row_sumsq, const double* col_sumsq, const double* s, uint64_t sstride,
                                  double rgA, double rgB);
-void launch_band_certify(const double* x, uint64_t rows, uint64_t k, const double* y, double* out, uint32_t* flags,
-                         cudaStream_t st);
+void launch_band_certify(const double* x, uint64_t rows, uint64_t k, const double* y, const double* ew, double* out,
+                         uint32_t* flags, cudaStream_t st);
+void launch_bcert_block(const double* b, uint64_t k, uint64_t w, uint64_t ldb, const double* g, uint64_t gstride,
+                        double* acc, uint32_t* flags, cudaStream_t st);
+void launch_bcert_finish(const unsigned long long* col_max, uint64_t n, const double* acc, uint64_t k, double c1,
+                         double* rgB, double* y, double* ew, cudaStream_t st);
+void launch_col_absmax(const double* b, uint64_t k, uint64_t w, uint64_t ldb, unsigned long long* out,
+                       cudaStream_t st);
+double bcert_error_factor(uint64_t n);
+void bounded_nb(const double* acc, uint64_t k, uint64_t n, double rgB, double& lo, double& hi);
+std::vector<double> policy_vectors_host(uint32_t N);
 PolicyBounds certified_policy_bounds(const double* cert, uint64_t m, uint64_t k, const double* col_max, uint64_t n,
-                                     const double* col_sumsq, double rgB);
-constexpr uint64_t kCertWidth = 18;  // doubles per row written by launch_band_certify
+                                     double nB_lo, double nB_hi, double rgB);
+PolicyStats estimate_policy_stats(const double* a, uint64_t rows_a, uint64_t k, const double* b, uint64_t cols_b,
+                                  uint64_t ldb, const double* g, uint64_t N, cudaStream_t st, bool& ok);
+constexpr uint64_t kCertWidth = 19;   // doubles per row of A written by launch_band_certify
+constexpr uint64_t kBCertWidth = 17;  // doubles per row of B accumulated by launch_bcert_block
 
 namespace {
 StreamedPhases g_last_phases;
@@ -54,17 +68,18 @@ StreamedCall::StreamedCall(int device_id, const double* a, const double* b, uint
 }
 
 StreamedCall::~StreamedCall() {
-    for (cudaStream_t s : {up_, down_, stat_, cert_, work_})
+    for (cudaStream_t s : {up_, down_, stat_, cert_, est_, work_})
         if (s) cudaStreamSynchronize(s);
     // the buffers go back to the pool on the work stream, after everything that used them
     stats_.reset();
     cert_buf_.reset();
+    bparts_.reset();
     cert_flags_.reset();
     dc_.reset();
     da_.reset();
     db_.reset();
     for (cudaEvent_t e : events_) cudaEventDestroy(e);
-    for (cudaStream_t s : {up_, down_, stat_, cert_, work_})
+    for (cudaStream_t s : {up_, down_, stat_, cert_, est_, work_})
         if (s) {
             cudaStreamSynchronize(s);
             cudaStreamDestroy(s);
@@ -123,109 +138,100 @@ PolicyStats StreamedCall::upload(std::vector<uint64_t>& row_max, std::vector<uin
     return ps;
 }
 
-void StreamedCall::upload_b() {
-    const uint32_t N = (uint32_t)round_up(n_, 64);  // the planners' padded width
-    OZTT_CUDA(cudaStreamCreateWithFlags(&stat_, cudaStreamNonBlocking));
-    order(work_, stat_);  // the operand buffers before the statistics buffers and stages
-    stats_ = std::make_unique<PolicyStatsRun>(m_, n_, k_, N, stat_);
-    order(stat_, up_);  // every allocation before the first copy
-    double* db = db_->as<double>();
-    const uint64_t cols_b = std::min<uint64_t>(n_, std::max<uint64_t>(512, kUploadChunkBytes / (8 * k_)));
-    for (uint64_t c0 = 0; c0 < n_; c0 += cols_b) {
-        const uint64_t w = std::min(cols_b, n_ - c0);
-        OZTT_CUDA(cudaMemcpy2DAsync(db + c0, n_ * 8, b_ + c0, n_ * 8, w * 8, k_, cudaMemcpyHostToDevice, up_));
-        order(up_, stat_);
-        stats_->b_cols(db, c0, c0 + w);
-    }
-    stats_->b_done(db);
-    b_ready_ = mark(stat_);
-}
-
-std::vector<cudaEvent_t> StreamedCall::upload_a_rows(uint64_t band_rows) {
+std::vector<cudaEvent_t> StreamedCall::upload_prefix_first(uint64_t pre_rows, uint64_t band_rows, uint64_t block_cols,
+                                                           std::vector<cudaEvent_t>& b_landed) {
+    const uint64_t N = round_up(n_, 64);  // the planners' padded width
     int lo = 0, hi = 0;
     OZTT_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
     OZTT_CUDA(cudaStreamCreateWithPriority(&cert_, cudaStreamNonBlocking, hi));
-    order(work_, cert_);
+    OZTT_CUDA(cudaStreamCreateWithPriority(&est_, cudaStreamNonBlocking, hi));
+    order(work_, cert_);  // the operand buffers before the measurement buffers
     cert_buf_ = std::make_unique<DevBuf>(cert_, m_ * kCertWidth * 8);
+    bparts_ = std::make_unique<DevBuf>(cert_, (k_ * kBCertWidth + n_ + 1 + 8 * k_ + k_ + 8 * N) * 8);
     cert_flags_ = std::make_unique<DevBuf>(cert_, 16);
     OZTT_CUDA(cudaMemsetAsync(cert_flags_->p, 0, 16, cert_));
-    OZTT_CUDA(cudaStreamWaitEvent(cert_, b_ready_, 0));  // the sketch y of B
-    order(cert_, up_);
-    std::vector<cudaEvent_t> landed;
+    OZTT_CUDA(cudaMemsetAsync(bparts_->p, 0, (k_ * kBCertWidth + n_) * 8, cert_));  // accumulators, maxima
+    const std::vector<double> g = policy_vectors_host((uint32_t)N);
+    OZTT_CUDA(cudaMemcpyAsync(b_probe(), g.data(), g.size() * 8, cudaMemcpyHostToDevice, cert_));
+    OZTT_CUDA(cudaStreamSynchronize(cert_));  // the probe vectors leave the host vector
+    g_ready_ = mark(cert_);
+    order(cert_, up_);  // every allocation before the first copy
     double* da = da_->as<double>();
-    const double* y = stats_->b_parts().y;
-    for (uint64_t r0 = 0; r0 < m_; r0 += band_rows) {
+    double* db = db_->as<double>();
+    std::vector<cudaEvent_t> landed;
+    const auto a_band = [&](uint64_t r0) {
         const uint64_t rows = std::min(band_rows, m_ - r0);
         OZTT_CUDA(cudaMemcpyAsync(da + r0 * k_, a_ + r0 * k_, rows * k_ * 8, cudaMemcpyHostToDevice, up_));
-        landed.push_back(order(up_, cert_));
-        launch_band_certify(da + r0 * k_, rows, k_, y, cert_buf_->as<double>() + r0 * kCertWidth,
+        landed.push_back(mark(up_));
+    };
+    for (uint64_t r0 = 0; r0 < pre_rows; r0 += band_rows) a_band(r0);
+    // B's blocks, each measured as it lands (its columns' maxima exactly, its rows' partial sketch sums bounded)
+    b_landed.clear();
+    for (uint64_t c0 = 0; c0 < n_; c0 += block_cols) {
+        const uint64_t w = std::min(block_cols, n_ - c0);
+        OZTT_CUDA(cudaMemcpy2DAsync(db + c0, n_ * 8, b_ + c0, n_ * 8, w * 8, k_, cudaMemcpyHostToDevice, up_));
+        b_landed.push_back(order(up_, cert_));
+        launch_col_absmax(db + c0, k_, w, n_, b_colmax() + c0, cert_);
+        launch_bcert_block(db + c0, k_, w, n_, b_probe() + c0, N, b_acc(), cert_flags_->as<uint32_t>() + 1, cert_);
+    }
+    launch_bcert_finish(b_colmax(), n_, b_acc(), k_, bcert_error_factor(n_), b_rg(), b_y(), b_ew(), cert_);
+    for (uint64_t r0 = pre_rows; r0 < m_; r0 += band_rows) a_band(r0);
+    // the bands' bounded statistics need B's sketch: all of them after B, each after its band
+    for (uint64_t r0 = 0, i = 0; r0 < m_; r0 += band_rows, ++i) {
+        const uint64_t rows = std::min(band_rows, m_ - r0);
+        OZTT_CUDA(cudaStreamWaitEvent(cert_, landed[i], 0));
+        launch_band_certify(da + r0 * k_, rows, k_, b_y(), b_ew(), cert_buf_->as<double>() + r0 * kCertWidth,
                             cert_flags_->as<uint32_t>(), cert_);
-        certified_.push_back(mark(cert_));
     }
     a_last_ = landed.back();
+    b_last_ = b_landed.back();
     return landed;
 }
 
-PolicyStats StreamedCall::band_stats(uint64_t r0, uint64_t r1) {
-    const uint64_t band = r0 / std::max<uint64_t>(1, r1 - r0);
-    OZTT_CUDA(cudaStreamWaitEvent(work_, certified_.at(std::min<uint64_t>(band, certified_.size() - 1)), 0));
-    const uint64_t rows = r1 - r0;
-    const PolicyStatsRun::BParts bp = stats_->b_parts();
-    std::vector<double> he(rows * kCertWidth), cmax(n_), cs2(n_);
-    double rgB = 1.0;
-    OZTT_CUDA(cudaMemcpyAsync(he.data(), cert_buf_->as<double>() + r0 * kCertWidth, he.size() * 8,
-                              cudaMemcpyDeviceToHost, work_));
-    OZTT_CUDA(cudaMemcpyAsync(cmax.data(), bp.col_max, n_ * 8, cudaMemcpyDeviceToHost, work_));
-    OZTT_CUDA(cudaMemcpyAsync(cs2.data(), bp.col_sumsq, n_ * 8, cudaMemcpyDeviceToHost, work_));
-    OZTT_CUDA(cudaMemcpyAsync(&rgB, bp.rgB, 8, cudaMemcpyDeviceToHost, work_));
-    OZTT_CUDA(cudaStreamSynchronize(work_));
-    // the band's rows as if they were all of A: its own power-of-two scale, the sums scaled by it
-    double top = 0;
-    for (uint64_t r = 0; r < rows; ++r) top = std::max(top, he[r * kCertWidth]);
-    double rgA = 1.0;
-    if (top > 0 && std::isfinite(top)) {
-        int e = 0;
-        std::frexp(top, &e);
-        rgA = std::ldexp(1.0, -std::min(std::max(e, -1000), 1000));
-    }
-    std::vector<double> hmax(rows), hs2(rows), hsk(8 * rows);
-    for (uint64_t r = 0; r < rows; ++r) {
-        const double* c = he.data() + r * kCertWidth;
-        hmax[r] = c[0];
-        hs2[r] = c[1] * rgA * rgA;
-        for (int l = 0; l < 8; ++l) hsk[(uint64_t)l * rows + r] = c[2 + l] * rgA;
-    }
-    return combine_policy_stats(hmax.data(), rows, cmax.data(), n_, hs2.data(), cs2.data(), hsk.data(), rows, rgA,
-                                rgB);
+PolicyStats StreamedCall::prefix_estimate(uint64_t pre_rows, uint64_t block_cols, cudaEvent_t a_landed,
+                                          cudaEvent_t b_landed, bool& ok) {
+    OZTT_CUDA(cudaStreamWaitEvent(est_, a_landed, 0));
+    OZTT_CUDA(cudaStreamWaitEvent(est_, b_landed, 0));
+    OZTT_CUDA(cudaStreamWaitEvent(est_, g_ready_, 0));
+    return estimate_policy_stats(da_->as<double>(), pre_rows, k_, db_->as<double>(), std::min(block_cols, n_), n_,
+                                 b_probe(), round_up(n_, 64), est_, ok);
 }
 
 PolicyBounds StreamedCall::certified_bounds(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max) {
     OZTT_CUDA(cudaEventSynchronize(a_last_));
     phases_.upload_ms = ms_since_start();
-    const PolicyStatsRun::BParts bp = stats_->b_parts();
-    std::vector<double> cert(m_ * kCertWidth), cs2(n_);
+    std::vector<double> cert(m_ * kCertWidth), acc(k_ * kBCertWidth);
     col_max.assign(n_, 0);
     double rgB = 1.0;
-    uint32_t flags = 0;
-    OZTT_CUDA(cudaStreamWaitEvent(cert_, b_ready_, 0));
+    uint32_t flags[2] = {0, 0};
     OZTT_CUDA(cudaMemcpyAsync(cert.data(), cert_buf_->p, cert.size() * 8, cudaMemcpyDeviceToHost, cert_));
-    OZTT_CUDA(cudaMemcpyAsync(&flags, cert_flags_->p, 4, cudaMemcpyDeviceToHost, cert_));
-    OZTT_CUDA(cudaMemcpyAsync(col_max.data(), bp.col_max, n_ * 8, cudaMemcpyDeviceToHost, cert_));
-    OZTT_CUDA(cudaMemcpyAsync(cs2.data(), bp.col_sumsq, n_ * 8, cudaMemcpyDeviceToHost, cert_));
-    OZTT_CUDA(cudaMemcpyAsync(&rgB, bp.rgB, 8, cudaMemcpyDeviceToHost, cert_));
+    OZTT_CUDA(cudaMemcpyAsync(flags, cert_flags_->p, 8, cudaMemcpyDeviceToHost, cert_));
+    OZTT_CUDA(cudaMemcpyAsync(col_max.data(), b_colmax(), n_ * 8, cudaMemcpyDeviceToHost, cert_));
+    OZTT_CUDA(cudaMemcpyAsync(acc.data(), b_acc(), acc.size() * 8, cudaMemcpyDeviceToHost, cert_));
+    OZTT_CUDA(cudaMemcpyAsync(&rgB, b_rg(), 8, cudaMemcpyDeviceToHost, cert_));
     OZTT_CUDA(cudaStreamSynchronize(cert_));
     row_max.resize(m_);
     for (uint64_t r = 0; r < m_; ++r) std::memcpy(&row_max[r], &cert[r * kCertWidth], 8);
+    double nb_lo = 0, nb_hi = 0;
+    bounded_nb(acc.data(), k_, n_, rgB, nb_lo, nb_hi);
     PolicyBounds pb = certified_policy_bounds(cert.data(), m_, k_, reinterpret_cast<const double*>(col_max.data()),
-                                              n_, cs2.data(), rgB);
-    if (flags) pb.usable = false;  // elements below 2^-383: the bounds do not hold
+                                              n_, nb_lo, nb_hi, rgB);
+    if (flags[0] || flags[1]) pb.usable = false;  // elements below 2^-383: the bounds do not hold
     phases_.stats_ms = ms_since_start() - phases_.upload_ms;
     return pb;
 }
 
 PolicyStats StreamedCall::exact_stats() {
+    // the reference's sequential sums over the whole A and B, for the rare call whose bounds leave a
+    // decision open
     const double* da = da_->as<double>();
+    const double* db = db_->as<double>();
+    if (!stat_) OZTT_CUDA(cudaStreamCreateWithFlags(&stat_, cudaStreamNonBlocking));
     OZTT_CUDA(cudaStreamWaitEvent(stat_, a_last_, 0));
+    OZTT_CUDA(cudaStreamWaitEvent(stat_, b_last_, 0));
+    stats_ = std::make_unique<PolicyStatsRun>(m_, n_, k_, (uint32_t)round_up(n_, 64), stat_);
+    stats_->b_cols(db, 0, n_);
+    stats_->b_done(db);
     stats_->a_cols(da, 0, k_);
     stats_->a_done(da);
     const PolicyStats ps = stats_->collect();
