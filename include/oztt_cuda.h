@@ -212,12 +212,18 @@ int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* 
                                   char* err, size_t errlen);
 
 /* Host wall-clock phases (ms) of the last INT8 Scheme II call made through oztt_gemm / Context::gemm in
- * this process, out[0..count-1] of: upload (to the end of the last host-to-device copy), statistics
- * read-back after it, value checks, plan, pipeline with the banded read-back of C, total, number of row
- * bands, and (calls of at least 4096 rows, which compute while their operands upload) the time the first
- * plan was made, 1 if the complete statistics gave another plan, 1 if the bounds of the statistics left a
- * decision open so that the exact sums were computed, and 1 if C's bands were read back as they finished,
- * before the plan was confirmed. Zeros before the first such call. */
+ * this process, out[0..count-1] of (16 values):
+ *   0 upload (to the end of the last host-to-device copy), 1 statistics read-back after it, 2 value checks,
+ *   3 plan, 4 pipeline with the read-back of C, 5 total, 6 the number of pieces of C read back (row bands,
+ *   or tiles);
+ * and for calls of at least 4096 rows, which compute while their operands upload:
+ *   7 when the first plan was made, 8 1 if the complete statistics gave another plan, 9 1 if the bounds of
+ *   the statistics left a decision open so that the exact sums were computed, 10 1 if C was read back as
+ *   its pieces finished (before the plan was confirmed); the device timeline in ms from the first copy:
+ *   11 A's first half done against every block of B, 12 the last reconstruction, 13 the end of the
+ *   read-back of C, 14 the last band's bounded statistics; 15 when the host's value checks were ready
+ *   (ms from the call).
+ * Zeros before the first such call. */
 int oztt_ii_int8_last_phases(double* out, int32_t count);
 
 /* Scheme I INT8 plan (plan_issue and the slice count of src/backend/ozaki1/plan.hpp:128-250 and

@@ -370,13 +370,15 @@ def policy_vectors(N: int) -> np.ndarray:
 
 def ii_int8_last_phases() -> dict:
     """Host wall-clock phases (ms) of the last INT8 Scheme II call through Context.gemm in this process
-    (oztt_ii_int8_last_phases): upload, statistics read-back, value checks, plan, pipeline with the banded
-    read-back of C, total, the number of row bands, and, on the path that computes while its operands
-    upload, when the first plan was made, whether the complete statistics replanned, whether the bounds
-    left the decision open so that the exact sums were computed, and whether C's bands were read back as
-    they finished (before the plan was confirmed)."""
-    out = np.zeros(11, dtype=np.float64)
-    _lib().oztt_ii_int8_last_phases(out.ctypes.data, 11)
+    (oztt_ii_int8_last_phases): upload, statistics read-back, value checks, plan, pipeline with the
+    read-back of C, total, the number of pieces of C read back (row bands or tiles); on the path that
+    computes while its operands upload also when the first plan was made, whether the complete statistics
+    replanned, whether the bounds left the decision open so that the exact sums were computed, whether C
+    was read back as its pieces finished (before the plan was confirmed), the device timeline (ms from the
+    first copy: A's first half done against every block of B, the last reconstruction, the end of C's
+    read-back, the last band's bounded statistics) and when the host's value checks were ready."""
+    out = np.zeros(16, dtype=np.float64)
+    _lib().oztt_ii_int8_last_phases(out.ctypes.data, 16)
     keys = ("upload_ms", "stats_ms", "check_ms", "plan_ms", "pipeline_ms", "total_ms")
     d = {key: float(v) for key, v in zip(keys, out[:6])}
     d["bands"] = int(out[6])
@@ -384,6 +386,11 @@ def ii_int8_last_phases() -> dict:
     d["replanned"] = int(out[8])
     d["exact_stats"] = int(out[9])
     d["early_readback"] = int(out[10])
+    d["gpu_prefix_ms"] = float(out[11])
+    d["gpu_compute_ms"] = float(out[12])
+    d["gpu_readback_ms"] = float(out[13])
+    d["gpu_bounds_ms"] = float(out[14])
+    d["host_checked_ms"] = float(out[15])
     return d
 
 

@@ -385,9 +385,11 @@ extern "C" int oztt_gemm(int device_id, const double* a, uint64_t a_len, const d
 extern "C" int oztt_ii_int8_last_phases(double* out, int32_t count) {
     if (!out || count < 1) return OZTT_EINVAL;
     const oztt::StreamedPhases ph = oztt::last_streamed_phases();
-    const double v[11] = {ph.upload_ms,   ph.stats_ms, ph.check_ms,       ph.plan_ms,
-                          ph.pipeline_ms, ph.total_ms, (double)ph.bands, ph.first_plan_ms,
-                          (double)ph.replanned, (double)ph.exact_stats, (double)ph.early_readback};
-    for (int32_t i = 0; i < count && i < 11; ++i) out[i] = v[i];
+    const double v[16] = {ph.upload_ms,       ph.stats_ms,         ph.check_ms,         ph.plan_ms,
+                          ph.pipeline_ms,     ph.total_ms,         (double)ph.bands,    ph.first_plan_ms,
+                          (double)ph.replanned, (double)ph.exact_stats, (double)ph.early_readback,
+                          ph.gpu_prefix_ms,   ph.gpu_compute_ms,   ph.gpu_readback_ms,  ph.gpu_bounds_ms,
+                          ph.host_checked_ms};
+    for (int32_t i = 0; i < count && i < 16; ++i) out[i] = v[i];
     return OZTT_OK;
 }

@@ -266,12 +266,16 @@ int run_ii_int8_streamed_impl(int device_id, const double* a, const double* b, d
 
 // ---- the call from host buffers, computing while the operands upload ------------------------------------------
 //
-// The magnitude patterns of A's row maxima and B's column maxima (the front end's value checks), measured by
-// the host's threads from the caller's buffers while the operands upload: known long before A has landed.
+// The magnitude patterns of A's row maxima and B's column maxima (the front end's value checks) for A's rows
+// from r_begin on and all of B, measured by the host's threads from the caller's buffers while the operands
+// upload: known long before A has landed. (The first r_begin rows' maxima come from the device, which measures
+// them for the first plan.)
 class HostMaxima {
 public:
-    HostMaxima(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k)
-        : row_max(m), col_max(n, 0), th_([this, a, b, m, n, k] { measure(a, b, m, n, k); }) {}
+    HostMaxima(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint64_t r_begin)
+        : row_max(m), col_max(n, 0), th_([this, a, b, m, n, k, r_begin] {
+              value_maxima(a + r_begin * k, b, m - r_begin, n, k, row_max.data() + r_begin, col_max.data());
+          }) {}
     ~HostMaxima() { wait(); }
     void wait() {
         if (th_.joinable()) th_.join();
@@ -279,23 +283,6 @@ public:
     std::vector<uint64_t> row_max, col_max;
 
 private:
-    void measure(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k) {
-        constexpr uint64_t kMag = 0x7FFFFFFFFFFFFFFFull;
-        const auto* pa = reinterpret_cast<const uint64_t*>(a);
-        const auto* pb = reinterpret_cast<const uint64_t*>(b);
-        parallel_ranges(m, [&](uint64_t r0, uint64_t r1) {
-            for (uint64_t i = r0; i < r1; ++i) {
-                uint64_t mx = 0;
-                for (uint64_t j = 0; j < k; ++j) mx = std::max(mx, pa[i * k + j] & kMag);
-                row_max[i] = mx;
-            }
-        });
-        parallel_ranges(n, [&](uint64_t c0, uint64_t c1) {
-            uint64_t* mx = col_max.data();
-            for (uint64_t i = 0; i < k; ++i)
-                for (uint64_t j = c0; j < c1; ++j) mx[j] = std::max(mx[j], pb[i * n + j] & kMag);
-        });
-    }
     std::thread th_;  // after the vectors it fills
 };
 
@@ -310,8 +297,10 @@ bool overlaps(const void* p, uint64_t pbytes, const void* q, uint64_t qbytes) {
 // first half and B's first block, each standing for its matrix (the decision depends on the size-free ratio
 // (TA nB + TB nA) / 12 nC, which such parts estimate closely). On that plan A's first half is split once and
 // multiplied by each block of B as the block lands; then each later band of A by the whole B as it lands.
-// Meanwhile the host measures the maxima of A and B from the caller's buffers, and once every value is
-// checked the bands of C are read back as they finish -- when that cannot change the outcome of the call:
+// The value checks need the maxima of every row of A and column of B: the device measures A's first half
+// for the first plan, the host's threads measure the rest of A and all of B from the caller's buffers
+// meanwhile. Once every value is checked, the pieces of C (A's first half against each block of B, then
+// the bands) are read back as they finish -- when that cannot change the outcome of the call:
 // no plan for these dimensions can fail, and C does not overlap A or B. When A has landed, the reference's
 // plan is decided from bounds of its statistics measured as the blocks and bands landed (only a decision
 // that lies within the bounds needs the exact long-double sums). If it equals the first plan, C is its
@@ -329,12 +318,13 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     const uint64_t pre = std::min(round_up(m / 2, bm), m);  // A's first part: whole bands
     const uint64_t pre_bands = (pre + bm - 1) / bm;
     const uint64_t nb = round_up((n + 7) / 8, 256);  // B's blocks of columns
-    HostMaxima host(a, b, m, n, k);
+    HostMaxima host(a, b, m, n, k, pre);
     std::vector<cudaEvent_t> b_landed;
     const std::vector<cudaEvent_t> landed = call.upload_prefix_first(pre, bm, nb, b_landed);
     // the first plan, from A's first part and B's first block
     bool estimated = false;
-    const PolicyStats first = call.prefix_estimate(pre, nb, landed[pre_bands - 1], b_landed[0], estimated);
+    std::vector<uint64_t> pre_max;
+    const PolicyStats first = call.prefix_estimate(pre, nb, landed[pre_bands - 1], b_landed[0], estimated, &pre_max);
     oztt_ii_plan p0{};
     std::string err0;
     const int rc0 = estimated ? plan_ii_int8_with([&](uint32_t, uint32_t) { return first; }, m, n, k, max_moduli,
@@ -354,9 +344,9 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
         ra = std::make_unique<DevBuf>(st, S * a_rows * kp);
         kpl = std::make_unique<DevBuf>(st, S * std::max(a_rows * std::min(nb, np), bm * np));
     };
-    // one band of A's rows against the whole B (B's planes complete)
-    const auto band = [&](const oztt_ii_plan& q, uint64_t r0) {
-        const uint64_t rows_p = std::min(bm, mp - r0), rows = std::min(m, r0 + rows_p) - r0;
+    // one band of A's rows (at most h) against the whole B (B's planes complete)
+    const auto band = [&](const oztt_ii_plan& q, uint64_t r0, uint64_t h = 1024) {
+        const uint64_t rows_p = std::min(h, mp - r0), rows = std::min(m, r0 + rows_p) - r0;
         launch_scale_rows(da + r0 * k, rows, k, k, q.shift, dA.as<int32_t>() + r0, nullptr, flags, st);
         launch_split_rows(da + r0 * k, rows, k, k, dA.as<int32_t>() + r0, q, ra->as<int8_t>(), rows_p, kp, st);
         launch_residue_gemm(ra->as<int8_t>(), rb->as<int8_t>(), rows_p, np, kp, q, 1, kpl->p, gemm_err, st, 0);
@@ -381,12 +371,19 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
                                 st, 0, np);
             launch_recon(kpl->as<uint8_t>(), pre, cols_p, dA.as<int32_t>(), dB.as<int32_t>() + c0, q, dc + c0, pre,
                          cols, n, st);
+            call.tile_done(0, pre, c0, cols);  // read back as soon as it is written (2-D copy)
         }
-        for (uint64_t r0 = 0; r0 < pre; r0 += bm) call.band_done(r0, std::min(bm, pre - r0));
+        call.timeline(st, 0);
         for (uint64_t i = pre_bands, r0 = pre; r0 < m; ++i, r0 += bm) {
             OZTT_CUDA(cudaStreamWaitEvent(st, landed[i], 0));
-            band(q, r0);
+            if (r0 + bm >= m && m - r0 > bm / 2) {  // the last band in two halves: the last read-back is shorter
+                band(q, r0, bm / 2);
+                band(q, r0 + bm / 2, bm / 2);
+            } else {
+                band(q, r0);
+            }
         }
+        call.timeline(st, 1);
     };
     // after everything has landed: the whole pipeline on a plan
     const auto whole = [&](const oztt_ii_plan& q) {
@@ -396,6 +393,7 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
         launch_scale_cols(db, k, n, n, q.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
         launch_split_cols(db, k, n, n, dB.as<int32_t>(), q, rb->as<int8_t>(), np, kp, st);
         for (uint64_t r0 = 0; r0 < m; r0 += bm) band(q, r0);
+        call.timeline(st, 1);
     };
     if (rc0 == OZTT_OK) {
         check_plan(p0);
@@ -404,6 +402,11 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     // every value checked (from the host's maxima); then C is read back as its bands finish when writing it
     // before the plan is confirmed cannot change the outcome of the call
     host.wait();
+    if (pre_max.size() == pre)
+        std::copy(pre_max.begin(), pre_max.end(), host.row_max.begin());
+    else  // (no device measurement of the first part: the host measures it too)
+        value_maxima(a, b, pre, 0, k, host.row_max.data(), nullptr);
+    ph.host_checked_ms = call.ms_since_start();
     double t = call.ms_since_start();
     check(host.row_max.data(), host.col_max.data());
     ph.check_ms = call.ms_since_start() - t;
@@ -412,8 +415,7 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     if (early) call.read_back(c);
     ph.early_readback = early ? 1 : 0;
     // the reference's plan: decided by the bounds, or from the exact sums
-    std::vector<uint64_t> row_max, col_max;
-    const PolicyBounds bounds = call.certified_bounds(row_max, col_max);
+    const PolicyBounds bounds = call.certified_bounds();
     t = call.ms_since_start();
     bool decided = false;
     int rc = plan_ii_int8_certified(bounds, m, n, k, max_moduli, reconstruction, p, err, decided);

@@ -16,6 +16,7 @@
 #include <sched.h>
 
 #include <algorithm>
+#include <bit>
 #include <cfloat>
 #include <cmath>
 #include <cstring>
@@ -179,6 +180,29 @@ unsigned host_threads() {
         return std::max(1u, std::thread::hardware_concurrency());
     }();
     return n;
+}
+
+void value_maxima(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint64_t* row_max,
+                  uint64_t* col_max) {
+    // magnitude patterns as signed 64-bit integers (the sign bit cleared, so they order like the unsigned
+    // patterns): maxima that the compiler vectorises (this file is built for x86-64-v3)
+    constexpr int64_t kMag = 0x7FFFFFFFFFFFFFFFll;
+    parallel_ranges(m, [&](uint64_t r0, uint64_t r1) {
+        for (uint64_t i = r0; i < r1; ++i) {
+            const double* p = a + i * k;
+            int64_t mx = 0;
+            for (uint64_t j = 0; j < k; ++j) mx = std::max(mx, std::bit_cast<int64_t>(p[j]) & kMag);
+            row_max[i] = (uint64_t)mx;
+        }
+    });
+    parallel_ranges(n, [&](uint64_t c0, uint64_t c1) {
+        std::vector<int64_t> mx(c1 - c0, 0);
+        for (uint64_t i = 0; i < k; ++i) {
+            const double* p = b + i * n + c0;
+            for (uint64_t j = 0; j < c1 - c0; ++j) mx[j] = std::max(mx[j], std::bit_cast<int64_t>(p[j]) & kMag);
+        }
+        for (uint64_t j = c0; j < c1; ++j) col_max[j] = (uint64_t)mx[j - c0];
+    });
 }
 
 double pow2_normalizer(const double* v, uint64_t rows, uint64_t cols, uint64_t ld) {

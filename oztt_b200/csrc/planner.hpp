@@ -89,6 +89,11 @@ int plan_ii_int8_with(const std::function<PolicyStats(uint32_t, uint32_t)>& stat
 // statistics are complete relies on it: its plan cannot fail afterwards.
 bool plan_ii_int8_never_fails(uint64_t m, uint64_t n, uint64_t k, uint32_t max_moduli);
 
+// The magnitude patterns (sign bit cleared) of the largest element of each row of row-major a (m x k) and of
+// each column of row-major b (k x n), on the host's threads: what the front end's value checks read.
+void value_maxima(const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k, uint64_t* row_max,
+                  uint64_t* col_max);
+
 // Scheme II digit formats: FP8, BF16, FP16, TF32 (planner_digit.cpp); format is an OZTT_FMT_* value.
 int plan_digit_with(int32_t format, const std::function<PolicyStats(uint32_t, uint32_t)>& stats, uint64_t m,
                     uint64_t n, uint64_t k, uint32_t max_moduli, int32_t reconstruction, int32_t fixed_bits,
@@ -219,6 +224,10 @@ struct StreamedPhases {
     int replanned = 0;         // 1 if the complete statistics gave another plan and the pipeline ran again
     int exact_stats = 0;       // 1 if the bounds left the decision open and the exact sums were computed
     int early_readback = 0;    // 1 if C's bands were read back as they finished, before the plan was confirmed
+    // device timeline of that path, ms from the first copy: A's first part done against all of B, the last
+    // reconstruction, the end of the last read-back of C, the last band's bounded statistics
+    double gpu_prefix_ms = 0, gpu_compute_ms = 0, gpu_readback_ms = 0, gpu_bounds_ms = 0;
+    double host_checked_ms = 0;  // that path: when the host's maxima of A and B were ready (ms from the call)
 };
 StreamedPhases last_streamed_phases();
 

@@ -148,6 +148,8 @@ public:
     cudaStream_t work() const { return work_; }
     // rows [r0, r0 + rows) of the device C are complete once the work issued so far has run
     void band_done(uint64_t r0, uint64_t rows);
+    // the same for the tile of rows [r0, r0 + rows) and columns [c0, c0 + cols)
+    void tile_done(uint64_t r0, uint64_t rows, uint64_t c0, uint64_t cols);
     // issues the read-back of every completed band into c, in order
     void read_back(double* c);
     // waits for everything (the read-back included) and records the phases of the call, the pipeline
@@ -161,17 +163,23 @@ public:
     std::vector<cudaEvent_t> upload_prefix_first(uint64_t pre_rows, uint64_t band_rows, uint64_t block_cols,
                                                  std::vector<cudaEvent_t>& b_landed);
     // After upload_prefix_first: the estimate of the statistics from A's first pre_rows rows and B's first
-    // block (estimate_policy_stats); waits for both. ok is false when no estimate could be made.
+    // block (estimate_policy_stats); waits for both. ok is false when no estimate could be made; row_max
+    // receives the magnitude patterns of those rows' maxima.
     PolicyStats prefix_estimate(uint64_t pre_rows, uint64_t block_cols, cudaEvent_t a_landed, cudaEvent_t b_landed,
-                                bool& ok);
-    // After upload_prefix_first: bounds of the statistics that contain the reference's values, and the magnitude
-    // patterns of A's row maxima and B's column maxima (for the value checks). Waits for every band.
-    PolicyBounds certified_bounds(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max);
+                                bool& ok, std::vector<uint64_t>* row_max);
+    // After upload_prefix_first: bounds of the statistics that contain the reference's values. Waits for
+    // every band's measurements.
+    PolicyBounds certified_bounds();
     // The reference's exact statistics of the whole A and B (its sequential long-double sums), for the rare
     // call whose bounds leave a decision open.
     PolicyStats exact_stats();
     // forgets the bands marked so far (their C is recomputed)
     void discard_bands() { bands_.clear(); }
+    // The device timeline of the computing-while-uploading path: slot 0 when A's first part has met every
+    // block of B, slot 1 when the last band's reconstruction has run (marked on stream s), slot 2 when the
+    // last read-back of C has ended, slot 3 when the bounded statistics of the last band are written;
+    // finish() reports them in milliseconds from the call's first copy.
+    void timeline(cudaStream_t s, int slot);
     StreamedPhases& phases() { return phases_; }
     double ms_since_start() const;
     StreamedCall(const StreamedCall&) = delete;
@@ -181,7 +189,7 @@ private:
     cudaEvent_t mark(cudaStream_t s);
     cudaEvent_t order(cudaStream_t from, cudaStream_t to);
     struct Band {
-        uint64_t r0, rows;
+        uint64_t r0, rows, c0, cols;  // a tile of C: rows r0.., columns c0.. (cols = n: whole rows)
         cudaEvent_t done;
     };
     const double *a_, *b_;
@@ -193,6 +201,8 @@ private:
     // B's bounded measurements (upload_prefix_first): per row of B 17 accumulators, the column maxima (n
     // patterns), the scale, the scaled sketch (8 x k), its error bounds (k), the probe vectors (8 x N)
     std::unique_ptr<DevBuf> bparts_;
+    double* stage_ = nullptr;  // pinned: the measurements of A's bands and B, copied back as they are written
+    bool stage_shared_ = false;
     double* b_acc() const { return bparts_->as<double>(); }
     unsigned long long* b_colmax() const { return reinterpret_cast<unsigned long long*>(b_acc() + k_ * 17); }
     double* b_rg() const { return b_acc() + k_ * 17 + n_; }
@@ -200,6 +210,7 @@ private:
     double* b_ew() const { return b_y() + 8 * k_; }
     double* b_probe() const { return b_ew() + k_; }
     std::vector<cudaEvent_t> events_;
+    cudaEvent_t tl_start_ = nullptr, tl_[4] = {nullptr, nullptr, nullptr, nullptr};
     std::vector<Band> bands_;
     std::unique_ptr<DevBuf> da_, db_, dc_;
     std::unique_ptr<PolicyStatsRun> stats_;

@@ -892,8 +892,10 @@ __global__ void __launch_bounds__(256) block_rows_kernel(const double* __restric
 // (TA nB + TB nA) / nC). It is what the first plan of a call that computes while its operands are still
 // uploading is made from, and is then confirmed by the reference's statistics. g: the probe vectors on
 // the device (8 x N). ok is false when a part holds a value that is not finite or the estimate degenerates.
+// row_max, when given, receives the magnitude patterns of the maxima of A's rows_a rows (for the value checks).
 PolicyStats estimate_policy_stats(const double* a, uint64_t rows_a, uint64_t k, const double* b, uint64_t cols_b,
-                                  uint64_t ldb, const double* g, uint64_t N, cudaStream_t st, bool& ok) {
+                                  uint64_t ldb, const double* g, uint64_t N, cudaStream_t st, bool& ok,
+                                  std::vector<uint64_t>* row_max) {
     ok = false;
     if (!rows_a || !cols_b || !k) return {};
     DevBuf cmax(st, cols_b * 8), y(st, (uint64_t)kVectors * k * 8), sq(st, k * 8), cert(st, rows_a * kCertW * 8),
@@ -912,6 +914,10 @@ PolicyStats estimate_policy_stats(const double* a, uint64_t rows_a, uint64_t k, 
     OZTT_CUDA(cudaMemcpyAsync(hsq.data(), sq.p, k * 8, cudaMemcpyDeviceToHost, st));
     OZTT_CUDA(cudaMemcpyAsync(hcert.data(), cert.p, hcert.size() * 8, cudaMemcpyDeviceToHost, st));
     OZTT_CUDA(cudaStreamSynchronize(st));
+    if (row_max) {
+        row_max->resize(rows_a);
+        for (uint64_t r = 0; r < rows_a; ++r) std::memcpy(&(*row_max)[r], &hcert[r * kCertW], 8);
+    }
     // the power-of-two scale of each part (the magnitude patterns order like the magnitudes)
     const auto scale_of = [](double top) {
         if (!(top > 0) || !std::isfinite(top)) return 1.0;

@@ -44,7 +44,8 @@ std::vector<double> policy_vectors_host(uint32_t N);
 PolicyBounds certified_policy_bounds(const double* cert, uint64_t m, uint64_t k, const double* col_max, uint64_t n,
                                      double nB_lo, double nB_hi, double rgB);
 PolicyStats estimate_policy_stats(const double* a, uint64_t rows_a, uint64_t k, const double* b, uint64_t cols_b,
-                                  uint64_t ldb, const double* g, uint64_t N, cudaStream_t st, bool& ok);
+                                  uint64_t ldb, const double* g, uint64_t N, cudaStream_t st, bool& ok,
+                                  std::vector<uint64_t>* row_max);
 constexpr uint64_t kCertWidth = 19;   // doubles per row of A written by launch_band_certify
 constexpr uint64_t kBCertWidth = 17;  // doubles per row of B accumulated by launch_bcert_block
 
@@ -52,6 +53,47 @@ namespace {
 StreamedPhases g_last_phases;
 std::mutex g_phases_mu;
 constexpr uint64_t kUploadChunkBytes = 64ull << 20;
+
+// One pinned staging buffer kept for the process (pinning a few MiB per call costs about a millisecond);
+// a call that finds it in use pins its own.
+struct PinnedStage {
+    std::mutex mu;
+    double* p = nullptr;
+    uint64_t bytes = 0;
+    bool busy = false;
+} g_stage;
+
+double* acquire_stage(uint64_t bytes, bool& shared) {
+    {
+        std::lock_guard<std::mutex> lock(g_stage.mu);
+        if (!g_stage.busy) {
+            if (g_stage.bytes < bytes) {
+                if (g_stage.p) OZTT_CUDA(cudaFreeHost(g_stage.p));
+                g_stage.p = nullptr;
+                g_stage.bytes = 0;
+                OZTT_CUDA(cudaHostAlloc((void**)&g_stage.p, bytes, cudaHostAllocPortable));
+                g_stage.bytes = bytes;
+            }
+            g_stage.busy = true;
+            shared = true;
+            return g_stage.p;
+        }
+    }
+    double* p = nullptr;
+    OZTT_CUDA(cudaHostAlloc((void**)&p, bytes, cudaHostAllocPortable));
+    shared = false;
+    return p;
+}
+
+void release_stage(double* p, bool shared) {
+    if (!p) return;
+    if (shared) {
+        std::lock_guard<std::mutex> lock(g_stage.mu);
+        g_stage.busy = false;
+    } else {
+        cudaFreeHost(p);
+    }
+}
 }  // namespace
 
 StreamedPhases last_streamed_phases() {
@@ -78,7 +120,10 @@ StreamedCall::~StreamedCall() {
     dc_.reset();
     da_.reset();
     db_.reset();
+    release_stage(stage_, stage_shared_);
     for (cudaEvent_t e : events_) cudaEventDestroy(e);
+    for (cudaEvent_t e : {tl_start_, tl_[0], tl_[1], tl_[2], tl_[3]})
+        if (e) cudaEventDestroy(e);
     for (cudaStream_t s : {up_, down_, stat_, cert_, est_, work_})
         if (s) {
             cudaStreamSynchronize(s);
@@ -141,6 +186,8 @@ PolicyStats StreamedCall::upload(std::vector<uint64_t>& row_max, std::vector<uin
 std::vector<cudaEvent_t> StreamedCall::upload_prefix_first(uint64_t pre_rows, uint64_t band_rows, uint64_t block_cols,
                                                            std::vector<cudaEvent_t>& b_landed) {
     const uint64_t N = round_up(n_, 64);  // the planners' padded width
+    double* da = da_->as<double>();
+    double* db = db_->as<double>();
     int lo = 0, hi = 0;
     OZTT_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
     OZTT_CUDA(cudaStreamCreateWithPriority(&cert_, cudaStreamNonBlocking, hi));
@@ -149,15 +196,14 @@ std::vector<cudaEvent_t> StreamedCall::upload_prefix_first(uint64_t pre_rows, ui
     cert_buf_ = std::make_unique<DevBuf>(cert_, m_ * kCertWidth * 8);
     bparts_ = std::make_unique<DevBuf>(cert_, (k_ * kBCertWidth + n_ + 1 + 8 * k_ + k_ + 8 * N) * 8);
     cert_flags_ = std::make_unique<DevBuf>(cert_, 16);
-    OZTT_CUDA(cudaMemsetAsync(cert_flags_->p, 0, 16, cert_));
-    OZTT_CUDA(cudaMemsetAsync(bparts_->p, 0, (k_ * kBCertWidth + n_) * 8, cert_));  // accumulators, maxima
+    // the probe vectors (1 MiB) first, while the copy engine is idle; then A's first half at once
     const std::vector<double> g = policy_vectors_host((uint32_t)N);
     OZTT_CUDA(cudaMemcpyAsync(b_probe(), g.data(), g.size() * 8, cudaMemcpyHostToDevice, cert_));
     OZTT_CUDA(cudaStreamSynchronize(cert_));  // the probe vectors leave the host vector
     g_ready_ = mark(cert_);
-    order(cert_, up_);  // every allocation before the first copy
-    double* da = da_->as<double>();
-    double* db = db_->as<double>();
+    order(work_, up_);
+    OZTT_CUDA(cudaEventCreate(&tl_start_));
+    OZTT_CUDA(cudaEventRecord(tl_start_, up_));
     std::vector<cudaEvent_t> landed;
     const auto a_band = [&](uint64_t r0) {
         const uint64_t rows = std::min(band_rows, m_ - r0);
@@ -165,6 +211,8 @@ std::vector<cudaEvent_t> StreamedCall::upload_prefix_first(uint64_t pre_rows, ui
         landed.push_back(mark(up_));
     };
     for (uint64_t r0 = 0; r0 < pre_rows; r0 += band_rows) a_band(r0);
+    OZTT_CUDA(cudaMemsetAsync(cert_flags_->p, 0, 16, cert_));
+    OZTT_CUDA(cudaMemsetAsync(bparts_->p, 0, (k_ * kBCertWidth + n_) * 8, cert_));  // accumulators, maxima
     // B's blocks, each measured as it lands (its columns' maxima exactly, its rows' partial sketch sums bounded)
     b_landed.clear();
     for (uint64_t c0 = 0; c0 < n_; c0 += block_cols) {
@@ -183,39 +231,42 @@ std::vector<cudaEvent_t> StreamedCall::upload_prefix_first(uint64_t pre_rows, ui
         launch_band_certify(da + r0 * k_, rows, k_, b_y(), b_ew(), cert_buf_->as<double>() + r0 * kCertWidth,
                             cert_flags_->as<uint32_t>(), cert_);
     }
+    timeline(cert_, 3);
+    // the measurements come back to the host as soon as they are written, ahead of C's read-back in the
+    // copy engine (pinned memory, so that the copies are queued now and the host does not wait for them)
+    const uint64_t words = m_ * kCertWidth + k_ * kBCertWidth + n_ + 2;
+    stage_ = acquire_stage(words * 8, stage_shared_);
+    OZTT_CUDA(cudaMemcpyAsync(stage_, cert_buf_->p, m_ * kCertWidth * 8, cudaMemcpyDeviceToHost, cert_));
+    OZTT_CUDA(cudaMemcpyAsync(stage_ + m_ * kCertWidth, b_acc(), (k_ * kBCertWidth + n_ + 1) * 8,
+                              cudaMemcpyDeviceToHost, cert_));  // accumulators, column maxima, scale
+    OZTT_CUDA(cudaMemcpyAsync(stage_ + words - 1, cert_flags_->p, 8, cudaMemcpyDeviceToHost, cert_));
     a_last_ = landed.back();
     b_last_ = b_landed.back();
     return landed;
 }
 
 PolicyStats StreamedCall::prefix_estimate(uint64_t pre_rows, uint64_t block_cols, cudaEvent_t a_landed,
-                                          cudaEvent_t b_landed, bool& ok) {
+                                          cudaEvent_t b_landed, bool& ok, std::vector<uint64_t>* row_max) {
     OZTT_CUDA(cudaStreamWaitEvent(est_, a_landed, 0));
     OZTT_CUDA(cudaStreamWaitEvent(est_, b_landed, 0));
     OZTT_CUDA(cudaStreamWaitEvent(est_, g_ready_, 0));
     return estimate_policy_stats(da_->as<double>(), pre_rows, k_, db_->as<double>(), std::min(block_cols, n_), n_,
-                                 b_probe(), round_up(n_, 64), est_, ok);
+                                 b_probe(), round_up(n_, 64), est_, ok, row_max);
 }
 
-PolicyBounds StreamedCall::certified_bounds(std::vector<uint64_t>& row_max, std::vector<uint64_t>& col_max) {
+PolicyBounds StreamedCall::certified_bounds() {
     OZTT_CUDA(cudaEventSynchronize(a_last_));
     phases_.upload_ms = ms_since_start();
-    std::vector<double> cert(m_ * kCertWidth), acc(k_ * kBCertWidth);
-    col_max.assign(n_, 0);
-    double rgB = 1.0;
-    uint32_t flags[2] = {0, 0};
-    OZTT_CUDA(cudaMemcpyAsync(cert.data(), cert_buf_->p, cert.size() * 8, cudaMemcpyDeviceToHost, cert_));
-    OZTT_CUDA(cudaMemcpyAsync(flags, cert_flags_->p, 8, cudaMemcpyDeviceToHost, cert_));
-    OZTT_CUDA(cudaMemcpyAsync(col_max.data(), b_colmax(), n_ * 8, cudaMemcpyDeviceToHost, cert_));
-    OZTT_CUDA(cudaMemcpyAsync(acc.data(), b_acc(), acc.size() * 8, cudaMemcpyDeviceToHost, cert_));
-    OZTT_CUDA(cudaMemcpyAsync(&rgB, b_rg(), 8, cudaMemcpyDeviceToHost, cert_));
-    OZTT_CUDA(cudaStreamSynchronize(cert_));
-    row_max.resize(m_);
-    for (uint64_t r = 0; r < m_; ++r) std::memcpy(&row_max[r], &cert[r * kCertWidth], 8);
+    OZTT_CUDA(cudaStreamSynchronize(cert_));  // the measurements, copied to stage_ as they were written
+    const double* cert = stage_;
+    const double* acc = stage_ + m_ * kCertWidth;
+    const double* col_max = acc + k_ * kBCertWidth;  // magnitude patterns, which order like the magnitudes
+    const double rgB = col_max[n_];
+    uint32_t flags[2];
+    std::memcpy(flags, col_max + n_ + 1, 8);
     double nb_lo = 0, nb_hi = 0;
-    bounded_nb(acc.data(), k_, n_, rgB, nb_lo, nb_hi);
-    PolicyBounds pb = certified_policy_bounds(cert.data(), m_, k_, reinterpret_cast<const double*>(col_max.data()),
-                                              n_, nb_lo, nb_hi, rgB);
+    bounded_nb(acc, k_, n_, rgB, nb_lo, nb_hi);
+    PolicyBounds pb = certified_policy_bounds(cert, m_, k_, col_max, n_, nb_lo, nb_hi, rgB);
     if (flags[0] || flags[1]) pb.usable = false;  // elements below 2^-383: the bounds do not hold
     phases_.stats_ms = ms_since_start() - phases_.upload_ms;
     return pb;
@@ -244,7 +295,17 @@ double* StreamedCall::c_dev() {
     return dc_->as<double>();
 }
 
-void StreamedCall::band_done(uint64_t r0, uint64_t rows) { bands_.push_back({r0, rows, mark(work_)}); }
+void StreamedCall::band_done(uint64_t r0, uint64_t rows) { bands_.push_back({r0, rows, 0, n_, mark(work_)}); }
+
+void StreamedCall::tile_done(uint64_t r0, uint64_t rows, uint64_t c0, uint64_t cols) {
+    bands_.push_back({r0, rows, c0, cols, mark(work_)});
+}
+
+void StreamedCall::timeline(cudaStream_t s, int slot) {
+    if (!tl_start_ || slot < 0 || slot > 3) return;
+    if (!tl_[slot]) OZTT_CUDA(cudaEventCreate(&tl_[slot]));
+    OZTT_CUDA(cudaEventRecord(tl_[slot], s));
+}
 
 void StreamedCall::read_back(double* c) {
     // all bands are queued before the first read-back is issued: a read-back into pageable memory
@@ -252,15 +313,26 @@ void StreamedCall::read_back(double* c) {
     const double* dc = c_dev();
     for (const Band& band : bands_) {
         OZTT_CUDA(cudaStreamWaitEvent(down_, band.done, 0));
-        OZTT_CUDA(cudaMemcpyAsync(c + band.r0 * n_, dc + band.r0 * n_, band.rows * n_ * 8, cudaMemcpyDeviceToHost,
-                                  down_));
+        if (band.c0 == 0 && band.cols == n_)
+            OZTT_CUDA(cudaMemcpyAsync(c + band.r0 * n_, dc + band.r0 * n_, band.rows * n_ * 8,
+                                      cudaMemcpyDeviceToHost, down_));
+        else
+            OZTT_CUDA(cudaMemcpy2DAsync(c + band.r0 * n_ + band.c0, n_ * 8, dc + band.r0 * n_ + band.c0, n_ * 8,
+                                        band.cols * 8, band.rows, cudaMemcpyDeviceToHost, down_));
     }
+    timeline(down_, 2);
     order(down_, work_);
 }
 
 void StreamedCall::finish(double pipeline_start_ms) {
     OZTT_CUDA(cudaStreamSynchronize(work_));
     phases_.total_ms = ms_since_start();
+    double* gpu[4] = {&phases_.gpu_prefix_ms, &phases_.gpu_compute_ms, &phases_.gpu_readback_ms,
+                      &phases_.gpu_bounds_ms};
+    for (int i = 0; i < 4; ++i) {
+        float ms = 0;
+        if (tl_start_ && tl_[i] && cudaEventElapsedTime(&ms, tl_start_, tl_[i]) == cudaSuccess) *gpu[i] = ms;
+    }
     phases_.pipeline_ms = phases_.total_ms - pipeline_start_ms;
     phases_.bands = (int)bands_.size();
     std::lock_guard<std::mutex> lock(g_phases_mu);

@@ -308,11 +308,11 @@ def test_device_run_matches_host_run(oztt, oracle, cuda):
 
 
 # ---- Context.gemm's streamed path: chunked upload, statistics as chunks land, banded read-back ----------
-# Sizes: B and A in blocks of max(512, 64 MiB / 8k) and max(512, 64 MiB / 8m) columns, row bands of about
-# 2048 rows (up to 8). (9000, 256, 256): one piece each, 4 bands, a ragged last band; (4500, 4608, 2048):
-# B in two column blocks, A in two column blocks (the last ones ragged), 2 bands.
-# (3000, 2048, 4608): two column blocks of B and of A, with tiny elements (below 2^-383) in
-# both operands.
+# Sizes: 4096 rows and more compute while their operands upload (A's first half, B in blocks of about n/8
+# columns, the rest of A in bands of 1024 rows): (9000, 256, 256) one block of B, a ragged last band;
+# (4500, 4608, 2048) six blocks of B (the last one ragged). Below 4096 rows B and A go up in blocks of
+# max(512, 64 MiB / 8k) and max(512, 64 MiB / 8m) columns, then row bands of about 2048 rows (up to 8):
+# (3000, 2048, 4608) two column blocks of B and of A, with tiny elements (below 2^-383) in both operands.
 @pytest.mark.parametrize("m,n,k,phi,seed", [(9000, 256, 256, 0.5, 31), (4500, 4608, 2048, 1.0, 32),
                                             (3000, 2048, 4608, 1.0, 33)])
 def test_context_streamed_matches_planned_run(oztt, oracle, cuda, m, n, k, phi, seed):
@@ -328,14 +328,18 @@ def test_context_streamed_matches_planned_run(oztt, oracle, cuda, m, n, k, phi, 
     assert info.reconstruction_passes == (2 if plan.two_pass else 1)
     assert np.array_equal(c.view(np.uint64), c_ref.view(np.uint64))
     ph = oztt.ii_int8_last_phases()
-    assert ph["bands"] == expected_bands(m)
+    assert ph["bands"] == expected_bands(m, n)
     assert ph["total_ms"] > 0 and ph["upload_ms"] > 0
 
 
-def expected_bands(m):
+def expected_bands(m, n):
     mp = round_up(m, 128)
-    if mp >= 4096:  # the path that computes while its operands upload: bands of 1024 rows
-        return -(-m // 1024)
+    if mp >= 4096:  # the path that computes while its operands upload: A's first half read back in one tile
+        pre = min(round_up(m // 2, 1024), m)  # per block of B's columns, then bands of 1024 rows (the last
+        nb = round_up(-(-n // 8), 256)        # one in halves when it has more than 512 rows)
+        rest = m - pre
+        last = rest - (rest - 1) // 1024 * 1024 if rest else 0
+        return -(-n // nb) + -(-rest // 1024) + (1 if last > 512 else 0)
     bm = round_up(-(-mp // min(8, max(1, mp // 2048))), 128)
     return -(-mp // bm)
 

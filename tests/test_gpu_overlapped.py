@@ -63,6 +63,26 @@ def test_invalid_value_in_the_last_band_leaves_c_untouched(oztt, oracle, cuda):
     assert np.all(c == 123.0)
 
 
+@pytest.mark.parametrize("where,message", [("a_first_half", "A contains NaN or infinity"),
+                                           ("b", "B contains NaN or infinity"),
+                                           ("a_range", "each nonzero row maximum of A")])
+def test_invalid_values_reported_in_order_and_c_untouched(oztt, oracle, cuda, where, message):
+    """Invalid values in A's first half (its maxima measured on the device) or in B (on the host's threads):
+    the front end's report, C never written."""
+    m, n, k = 4224, 300, 200
+    a, b = oracle.gen_inputs(m, n, k, 0.5, 26)
+    if where == "a_first_half":
+        a[10 * k + 3] = np.nan
+    elif where == "b":
+        b[(k - 1) * n + 7] = -np.inf
+    else:
+        a[20 * k: 21 * k] = 2.0 ** -140  # a row whose maximum is below 2^-126
+    c = np.full(m * n, 5.0)
+    with pytest.raises(ValueError, match=message):
+        oztt.Context().gemm(a, b, c, m, n, k, _opts(oztt))
+    assert np.all(c == 5.0)
+
+
 def test_failing_plan_leaves_c_untouched(oztt, oracle, cuda):
     """Eight moduli cannot cover 53 bits: no plan exists, the error is reported and C is not written."""
     m, n, k = 4224, 256, 512
