@@ -7,7 +7,8 @@
 // recon_elem.h / f64_tf.h:296-400. The reference evaluates frac = sum_s k_s/m_s mod 1 in FP32
 // triple-float because its device has no FP64 (absolute error about 2^-67 for one pass), folds it in
 // 128-bit fixed point and multiplies by M*2^-2b. Here the same quantity is computed without error:
-//     X  = sum_s k_s * (M/m_s)                  (multiword integer, NW 32-bit words, X < S*M < 2^(32 NW))
+//     X  = sum_s k_s * (M/m_s)                  (multiword integer, NW 32-bit words, X < S*M < 2^(32 NW);
+//                                                formed two moduli at a time on the FP64 pipe, recon_pair_kernel)
 //     q  = rint(top 64 bits of X * 2^t / M)     (FP64; the window margin |C'|/M <= 1/2 - 2^-31.4
 //                                                makes this q = round(X/M) exactly)
 //     C' = X - q*M                              (|C'| < M/2, two's complement in NW words)
@@ -24,16 +25,22 @@
 
 namespace oztt {
 
-constexpr int kLimbBits = 39;  // radix of the FP64 limbs of M/m_s: S * 255 * 2^39 < 2^52 for S <= 24
-constexpr int kMaxLimbs = 5;   // M <= 255^24 < 2^192 < 2^(39*5)
+
+constexpr int kMaxPairs = (OZTT_MAXS + 1) / 2;
+constexpr int kPairLimbs = 6;  // M/(m_s m_t) < 2^192 in 32-bit limbs
 
 struct ReconConst {
     uint32_t S;
     int32_t two_b, sh2;
     uint32_t M[8];
     uint32_t Q[OZTT_MAXS][8];
-    double Qd[OZTT_MAXS][kMaxLimbs];  // M/m_s in radix-2^39 limbs, as doubles (exact)
     double top_scale;  // 2^(32 (NW-3)) / M: X/M from the top three words of X
+    // the moduli in pairs (s, t) = (2p, 2p+1), the last one alone when S is odd: u_p = (k_s m_t + k_t m_s) mod
+    // m_s m_t and M/(m_s m_t) (or M/m_s) in 32-bit limbs as doubles (exact): X = sum_p u_p M/(m_s m_t) mod M
+    uint32_t P;
+    uint32_t pm_s[kMaxPairs], pm_t[kMaxPairs];  // the multipliers of k_t and k_s: m_s and m_t (m_s = 0 alone)
+    uint32_t pm_st[kMaxPairs];                   // m_s m_t (m_s alone)
+    double Qp[kMaxPairs][kPairLimbs];
 };
 
 // Finishes one element from its column sums acc (X = sum_w acc[w] 2^(32w)).
@@ -161,17 +168,20 @@ __global__ void __launch_bounds__(256) recon_kernel(const D* __restrict__ kp, ui
     }
 }
 
-// The same with X = sum_s k_s (M/m_s) accumulated on the FP64 pipe: M/m_s is held in NL radix-2^39
-// limbs, each limb sum sum_s k_s q_{s,l} < 24 * 255 * 2^39 < 2^52 is exact in binary64 (every fused
-// multiply-add of two integers below 2^53 with an integer sum below 2^53 is exact), and the limbs are
-// then read back as integers (adding 2^52 puts the integer in the significand bits) and placed at their
-// bit offsets 39 l in the 32-bit column sums of crt_finish. The integer pipe keeps only the final
-// step, so the two pipes share the work.
+// The same with X accumulated on the FP64 pipe, two moduli at a time. For a pair (s, t),
+// k_s (M/m_s) + k_t (M/m_t) = (k_s m_t + k_t m_s) (M/(m_s m_t)), and only X mod M matters (q is taken from
+// X itself), so u = (k_s m_t + k_t m_s) mod (m_s m_t) < 2^16 -- one integer, formed on the integer pipe, against
+// one multiplier: the pairs halve the FP64 work. The sum X' = sum_p u_p M/(m_s m_t) < (S/2) M is X plus a
+// multiple of M. M/(m_s m_t) is held in NL 32-bit limbs; each limb sum, < 12 * 2^16 * 2^32 < 2^52, is exact
+// in binary64 (every fused multiply-add of integers below 2^53 whose sum stays below 2^53 is exact). A limb
+// sum is read back as an integer by adding 2^52 (the integer lands in the significand bits), and the limbs,
+// 32 bits apart, are the column sums of crt_finish directly.
 template <int NW, int NL>
-__global__ void __launch_bounds__(256) recon_fp64_kernel(const uint8_t* __restrict__ kp, uint64_t mp, uint64_t np,
+__global__ void __launch_bounds__(256) recon_pair_kernel(const uint8_t* __restrict__ kp, uint64_t mp, uint64_t np,
                                                          const int32_t* __restrict__ dA,
                                                          const int32_t* __restrict__ dB, double* __restrict__ c,
                                                          uint64_t m, uint64_t n, uint64_t ldc, const ReconConst rc) {
+    static_assert(NL <= NW && NL <= kPairLimbs, "limbs");
     const uint64_t nq = (n + 3) >> 2, total = m * nq, plane = mp * np;
     constexpr double two52 = 4503599627370496.0;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
@@ -188,14 +198,18 @@ __global__ void __launch_bounds__(256) recon_fp64_kernel(const uint8_t* __restri
 #pragma unroll
             for (int l = 0; l < NL; ++l) lim[e][l] = 0.0;
 #pragma unroll
-        for (int s = 0; s < OZTT_MAXS; ++s) {
-            if ((uint32_t)s >= rc.S) break;
+        for (int p = 0; p < kMaxPairs; ++p) {
+            if ((uint32_t)p >= rc.P) break;
+            const uint32_t ws = kw[2 * p], wt = kw[2 * p + 1];
+            const uint32_t ms = rc.pm_s[p], mt = rc.pm_t[p], mm = rc.pm_st[p];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                // k as a double: 2^52 + k has k in its low significand bits; subtracting 2^52 is exact
-                const double kd = __dsub_rn(__hiloint2double(0x43300000, (kw[s] >> (8 * e)) & 0xFFu), two52);
+                const uint32_t u2 = ((ws >> (8 * e)) & 0xFFu) * mt + ((wt >> (8 * e)) & 0xFFu) * ms;  // < 2 mm
+                const uint32_t u = min(u2, u2 - mm);  // u2 mod mm (u2 - mm wraps above u2 when u2 < mm)
+                // u as a double: 2^52 + u has u in its low significand bits; subtracting 2^52 is exact
+                const double ud = __dsub_rn(__hiloint2double(0x43300000, (int)u), two52);
 #pragma unroll
-                for (int l = 0; l < NL; ++l) lim[e][l] = __fma_rn(kd, rc.Qd[s][l], lim[e][l]);
+                for (int l = 0; l < NL; ++l) lim[e][l] = __fma_rn(ud, rc.Qp[p][l], lim[e][l]);
             }
         }
         const int32_t da = __ldg(dA + i);
@@ -204,18 +218,10 @@ __global__ void __launch_bounds__(256) recon_fp64_kernel(const uint8_t* __restri
         for (int e = 0; e < 4; ++e) {
             uint64_t acc[NW];
 #pragma unroll
-            for (int w = 0; w < NW; ++w) acc[w] = 0;
-#pragma unroll
-            for (int l = 0; l < NL; ++l) {
-                const uint64_t v = (uint64_t)__double_as_longlong(__dadd_rn(lim[e][l], two52)) & 0xFFFFFFFFFFFFFull;
-                const int off = kLimbBits * l, w0 = off >> 5, sh = off & 31;
-                // v * 2^sh spans at most three 32-bit words from w0 (52 + 31 bits)
-                const uint64_t lo = v << sh;
-                const uint64_t hi = sh ? (v >> (64 - sh)) : 0;
-                if (w0 < NW) acc[w0] += lo & 0xFFFFFFFFull;
-                if (w0 + 1 < NW) acc[w0 + 1] += lo >> 32;
-                if (w0 + 2 < NW) acc[w0 + 2] += hi;
-            }
+            for (int w = 0; w < NW; ++w)
+                acc[w] = w < NL ? (uint64_t)__double_as_longlong(__dadd_rn(lim[e][w < NL ? w : 0], two52)) &
+                                      0xFFFFFFFFFFFFFull
+                                : 0ull;
             if (j0 + e < n) {
                 const int32_t g = rc.sh2 - (da + __ldg(dB + j0 + e));
                 crow[e] = crt_finish<NW>(acc, g, rc);
@@ -265,16 +271,27 @@ static ReconConst recon_const(const oztt_ii_plan& p, int& nw, int& nl) {
             if (t != s) q = big_mul(q, (uint32_t)p.moduli[t]);
         for (int w = 0; w < 8; ++w) rc.Q[s][w] = q.w[w];
     }
-    for (int s = 0; s < p.S; ++s)
-        for (int l = 0; l < kMaxLimbs; ++l) {
-            // bits [39 l, 39 l + 39) of Q_s
-            uint64_t v = 0;
-            for (int b = 0; b < kLimbBits; ++b) {
-                const int bit = kLimbBits * l + b;
-                if (bit < 256 && ((rc.Q[s][bit >> 5] >> (bit & 31)) & 1u)) v |= 1ull << b;
-            }
-            rc.Qd[s][l] = (double)v;
+    // the pairs: u_p = k_s m_t + k_t m_s against M/(m_s m_t); the last modulus alone (u = k_s) when S is odd
+    rc.P = (uint32_t)((p.S + 1) / 2);
+    int pair_bits = 0;
+    for (int q = 0; q < (int)rc.P && q < kMaxPairs; ++q) {
+        const int s0 = 2 * q, s1 = 2 * q + 1;
+        Big qp;
+        qp.w[0] = 1;
+        for (int t = 0; t < p.S; ++t)
+            if (t != s0 && t != s1) qp = big_mul(qp, (uint32_t)p.moduli[t]);
+        if (s1 < p.S) {
+            rc.pm_s[q] = (uint32_t)p.moduli[s0];
+            rc.pm_t[q] = (uint32_t)p.moduli[s1];
+            rc.pm_st[q] = (uint32_t)(p.moduli[s0] * p.moduli[s1]);
+        } else {
+            rc.pm_s[q] = 0;
+            rc.pm_t[q] = 1;
+            rc.pm_st[q] = (uint32_t)p.moduli[s0];
         }
+        for (int l = 0; l < kPairLimbs; ++l) rc.Qp[q][l] = (double)qp.w[l];  // limbs above 192 bits: u16 path only
+        pair_bits = std::max(pair_bits, big_bits(qp));
+    }
     // X = sum_s k_s (M/m_s) < S*M must fit the words, and the three top words must carry X/M to
     // better than the window margin: 32 (NW-3) <= bits(M) - 40 holds for this choice of NW.
     int sbits = 0;
@@ -287,8 +304,8 @@ static ReconConst recon_const(const oztt_ii_plan& p, int& nw, int& nl) {
         for (int w = 7; w >= 0; --w) Ml = Ml * 4294967296.0L + (long double)M.w[w];
         rc.top_scale = (double)(ldexpl(1.0L, 32 * (nw - 3)) / Ml);
     }
-    // limbs needed for the largest M/m_s (below M)
-    nl = std::max(1, (big_bits(M) + kLimbBits - 1) / kLimbBits);
+    // 32-bit limbs of the largest pair multiplier (at most kPairLimbs for moduli below 256)
+    nl = std::max(1, (pair_bits + 31) / 32);
     return rc;
 }
 
@@ -315,18 +332,19 @@ void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA
     // (identical results)
     const bool fp64 = option_value(OZTT_OPT_RECON_INT) != 1;
     if (fp64) {
-#define OZTT_RECON_FP64(NW_, NL_) \
-    recon_fp64_kernel<NW_, NL_><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc)
-        switch (nw * 10 + std::min(nl, kMaxLimbs)) {
-        case 31: case 32: case 33: OZTT_RECON_FP64(3, 3); break;
-        case 41: case 42: case 43: OZTT_RECON_FP64(4, 3); break;
-        case 44: OZTT_RECON_FP64(4, 4); break;
-        case 51: case 52: case 53: case 54: OZTT_RECON_FP64(5, 4); break;
-        case 55: OZTT_RECON_FP64(5, 5); break;
-        case 61: case 62: case 63: case 64: case 65: OZTT_RECON_FP64(6, 5); break;
-        default: OZTT_RECON_FP64(7, 5); break;
+#define OZTT_RECON_PAIR(NW_, NL_) \
+    case NW_ * 10 + NL_: \
+        recon_pair_kernel<NW_, NL_><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); \
+        break
+        switch (nw * 10 + nl) {
+            OZTT_RECON_PAIR(3, 1); OZTT_RECON_PAIR(3, 2); OZTT_RECON_PAIR(3, 3);
+            OZTT_RECON_PAIR(4, 2); OZTT_RECON_PAIR(4, 3); OZTT_RECON_PAIR(4, 4);
+            OZTT_RECON_PAIR(5, 3); OZTT_RECON_PAIR(5, 4); OZTT_RECON_PAIR(5, 5);
+            OZTT_RECON_PAIR(6, 4); OZTT_RECON_PAIR(6, 5); OZTT_RECON_PAIR(6, 6);
+            OZTT_RECON_PAIR(7, 5); OZTT_RECON_PAIR(7, 6);
+        default: throw Error(OZTT_EINVAL, "recon: no kernel for these moduli");
         }
-#undef OZTT_RECON_FP64
+#undef OZTT_RECON_PAIR
     } else {
         switch (nw) {
         case 3: recon_kernel<3><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); break;
