@@ -205,66 +205,90 @@ __global__ void __launch_bounds__(128) sketch_kernel(const double* __restrict__ 
         out[l * ostride + r] = ext80::to_double(acc);
 }
 
-// Bounded statistics of rows of A (x: rows x k, row-major; one warp per row, the lanes striding the row),
-// for deciding the plan without the reference's sequential long-double sums: per row, into out[r*kCertW ..]:
+// Bounded statistics of rows of A (x: rows x k, row-major; a block of 256 threads per 2 rows, the threads
+// striding the columns, each column's sketch values loaded once for both rows), for deciding the plan
+// without the reference's sequential long-double sums: per row, into out[r*kCertW ..]:
 //   [0]          the largest magnitude as its bit pattern (NaN and Inf patterns order above every number)
 //   [1]          sum x^2            [2 .. 9]   sum x * y_l            [10 .. 17]  sum |x * y_l|
 //   [18]         sum |x| * ew       (0 when ew is null)
-// all unscaled, in FP64 (fused multiply-adds, the warp's order); the host turns them into bounds that
+// all unscaled, in FP64 (in the threads', then the warps' order); the host turns them into bounds that
 // contain the reference's values. y: the 8 x k sketch y_l = B g_l (scaled), as the reference has it or as
 // bcert_finish_kernel bounds it (then ew[j] bounds |y_l[j] - the reference's y_l[j]| over l). flags |= 1
 // when a nonzero element below 2^-383 makes the scaled squares leave the normal range (no bounds then).
 constexpr int kCertW = 19;
+constexpr int kCertRows = 2;  // rows of A per block: each column's 8 sketch values are loaded once for both
 __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restrict__ x, uint64_t rows, uint64_t k,
                                                            const double* __restrict__ y,
                                                            const double* __restrict__ ew, double* __restrict__ out,
                                                            uint32_t* __restrict__ flags) {
-    const uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (r >= rows) return;
-    const double* xr = x + r * k;
-    unsigned long long mx = 0;
+    constexpr int R = kCertRows, V = 2 + 2 * kVectors + 1;  // per row: s2, sl[8], al[8], se; then the maximum
+    const uint64_t r0 = (uint64_t)blockIdx.x * R;
+    const int nr = rows - r0 < (uint64_t)R ? (int)(rows - r0) : R;
+    unsigned long long mx[R];
+    double acc[R][V];
     bool tiny = false;
-    double s2 = 0.0, se = 0.0, sl[kVectors], al[kVectors];
 #pragma unroll
-    for (int l = 0; l < kVectors; ++l) sl[l] = al[l] = 0.0;
-    for (uint64_t j = lane; j < k; j += 32) {
-        const double v = __ldg(xr + j);
-        const unsigned long long pat = (unsigned long long)__double_as_longlong(v) & 0x7FFFFFFFFFFFFFFFull;
-        mx = pat > mx ? pat : mx;
-        tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);  // 0 < |v| < 2^-383
-        s2 = fma(v, v, s2);
-        if (ew) se = fma(fabs(v), __ldg(ew + j), se);
+    for (int r = 0; r < R; ++r) {
+        mx[r] = 0;
 #pragma unroll
-        for (int l = 0; l < kVectors; ++l) {
-            const double t = v * __ldg(y + (uint64_t)l * k + j);
-            sl[l] += t;
-            al[l] += fabs(t);
+        for (int v = 0; v < V; ++v) acc[r][v] = 0.0;
+    }
+    for (uint64_t j = threadIdx.x; j < k; j += blockDim.x) {
+        double yl[kVectors];
+#pragma unroll
+        for (int l = 0; l < kVectors; ++l) yl[l] = __ldg(y + (uint64_t)l * k + j);
+        const double e = ew ? __ldg(ew + j) : 0.0;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            if (r >= nr) break;
+            const double v = __ldg(x + (r0 + r) * k + j);
+            const unsigned long long pat = (unsigned long long)__double_as_longlong(v) & 0x7FFFFFFFFFFFFFFFull;
+            mx[r] = pat > mx[r] ? pat : mx[r];
+            tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);  // 0 < |v| < 2^-383
+            acc[r][0] = fma(v, v, acc[r][0]);
+            acc[r][V - 1] = fma(fabs(v), e, acc[r][V - 1]);
+#pragma unroll
+            for (int l = 0; l < kVectors; ++l) {
+                const double t = v * yl[l];
+                acc[r][1 + l] += t;
+                acc[r][1 + kVectors + l] += fabs(t);
+            }
         }
     }
+    // the warps' sums, then the block's (any order: the bounds hold for every order of the k terms)
+    __shared__ double part[8][R][V];
+    __shared__ unsigned long long pmx[8][R];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        const unsigned long long om = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
-        mx = om > mx ? om : mx;
-        s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
-        se += __shfl_xor_sync(0xFFFFFFFFu, se, o);
+    for (int r = 0; r < R; ++r) {
 #pragma unroll
-        for (int l = 0; l < kVectors; ++l) {
-            sl[l] += __shfl_xor_sync(0xFFFFFFFFu, sl[l], o);
-            al[l] += __shfl_xor_sync(0xFFFFFFFFu, al[l], o);
+        for (int o = 16; o; o >>= 1) {
+            const unsigned long long om = __shfl_xor_sync(0xFFFFFFFFu, mx[r], o);
+            mx[r] = om > mx[r] ? om : mx[r];
+#pragma unroll
+            for (int v = 0; v < V; ++v) acc[r][v] += __shfl_xor_sync(0xFFFFFFFFu, acc[r][v], o);
+        }
+        if (lane == 0) {
+            pmx[warp][r] = mx[r];
+#pragma unroll
+            for (int v = 0; v < V; ++v) part[warp][r][v] = acc[r][v];
         }
     }
     if (__any_sync(0xFFFFFFFFu, tiny) && lane == 0) atomicOr(flags, 1u);
-    if (lane == 0) {
-        double* o = out + r * kCertW;
-        o[0] = __longlong_as_double((long long)mx);
-        o[1] = s2;
-#pragma unroll
-        for (int l = 0; l < kVectors; ++l) {
-            o[2 + l] = sl[l];
-            o[2 + kVectors + l] = al[l];
-        }
-        o[18] = se;
+    __syncthreads();
+    const int nw = (int)(blockDim.x >> 5);
+    for (int i = threadIdx.x; i < nr * V; i += blockDim.x) {
+        const int r = i / V, v = i % V;
+        double sum = 0.0;
+        for (int w = 0; w < nw; ++w) sum += part[w][r][v];
+        double* o = out + (r0 + r) * kCertW;
+        // output layout: [1] s2, [2..9] sl, [10..17] al, [18] se
+        o[1 + v] = sum;
+    }
+    for (int r = threadIdx.x; r < nr; r += blockDim.x) {
+        unsigned long long m = 0;
+        for (int w = 0; w < nw; ++w) m = pmx[w][r] > m ? pmx[w][r] : m;
+        out[(r0 + r) * kCertW] = __longlong_as_double((long long)m);
     }
 }
 
@@ -718,7 +742,7 @@ std::vector<double> policy_vectors_host(uint32_t N) { return *policy_vectors(N);
 void launch_band_certify(const double* x, uint64_t rows, uint64_t k, const double* y, const double* ew, double* out,
                          uint32_t* flags, cudaStream_t st) {
     if (!rows) return;
-    band_certify_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(x, rows, k, y, ew, out, flags);
+    band_certify_kernel<<<(unsigned)((rows + kCertRows - 1) / kCertRows), 256, 0, st>>>(x, rows, k, y, ew, out, flags);
     OZTT_CUDA(cudaGetLastError());
 }
 
@@ -906,7 +930,7 @@ PolicyStats estimate_policy_stats(const double* a, uint64_t rows_a, uint64_t k, 
     block_rows_kernel<<<(unsigned)((k * 32 + 255) / 256), 256, 0, st>>>(b, k, cols_b, ldb, g, N, y.as<double>(),
                                                                         sq.as<double>());
     OZTT_CUDA(cudaGetLastError());
-    band_certify_kernel<<<(unsigned)((rows_a * 32 + 255) / 256), 256, 0, st>>>(
+    band_certify_kernel<<<(unsigned)((rows_a + kCertRows - 1) / kCertRows), 256, 0, st>>>(
         a, rows_a, k, y.as<double>(), nullptr, cert.as<double>(), flags.as<uint32_t>());
     OZTT_CUDA(cudaGetLastError());
     std::vector<double> hcmax(cols_b), hsq(k), hcert(rows_a * kCertW);
