@@ -41,6 +41,8 @@ struct ReconConst {
     uint32_t pm_s[kMaxPairs], pm_t[kMaxPairs];  // the multipliers of k_t and k_s: m_s and m_t (m_s = 0 alone)
     uint32_t pm_st[kMaxPairs];                   // m_s m_t (m_s alone)
     double Qp[kMaxPairs][kPairLimbs];
+    // for the finish on FP64 limbs: 2^(32 l) / M (rounded), and M's 32-bit words as doubles (exact)
+    double Rl[kPairLimbs], Ml[kPairLimbs];
 };
 
 // Finishes one element from its column sums acc (X = sum_w acc[w] 2^(32w)).
@@ -111,6 +113,87 @@ __device__ __forceinline__ double crt_finish(const uint64_t (&acc)[NW], int32_t 
     return neg ? -r : r;
 }
 
+// Finishes one element from its limb sums on the FP64 pipe: X' = sum_l lim[l] 2^(32 l) (exact integers
+// below 2^52, X' < 13 M), the same value as crt_finish gives, bit for bit.
+//   q    = rint(sum_l lim[l] * fl(2^(32 l)/M)): within 2^-45 of X'/M, which the window margin keeps
+//          2^-31.4 from a half-integer, so q = round(X'/M);
+//   c[l] = lim[l] - q M_l (M's 32-bit words; exact, |c| < 2^53), C' = sum_l c[l] 2^(32 l), |C'| <= M/2;
+//   the limbs carried into balanced digits |c[l]| <= 2^31 (each step exact), so the top nonzero digit
+//   T carries the sign and C' = 2^(32(T-2)) (a 2^64 + b 2^32 + c2 + R) with |R| < 1/2 + 2^-32;
+//   two TwoSums give t + f = a 2^64 + b 2^32 + c2 exactly, t = RN(that), f an integer; R changes the
+//   rounding only when f is exactly half the spacing next to t on its side (|t| >= 2^62 when a != 0, so the
+//   spacing is at least 2^10, and below that a, b, c2 hold C' entirely), and then only by its sign;
+//   the result is scaled by 2^(32(T-2) + g - 2b) in the exponent field, below 2^-1022 flushed to +-0 and
+//   above the range to +-inf, as crt_finish.
+template <int NL, int L>
+__device__ __forceinline__ double crt_finish_limbs(const double (&lim)[NL], int32_t g, const ReconConst& rc) {
+    constexpr double magic = 6755399441055744.0;  // 1.5 * 2^52: x + magic - magic = rint(x) for |x| < 2^51
+    constexpr double two32 = 4294967296.0, inv32 = 2.3283064365386963e-10;
+    double xm = 0.0;
+#pragma unroll
+    for (int l = NL - 1; l >= 0; --l) xm = __fma_rn(lim[l], rc.Rl[l], xm);
+    const double q = __dsub_rn(__dadd_rn(xm, magic), magic);
+    double c[L];
+#pragma unroll
+    for (int l = 0; l < L; ++l) c[l] = __fma_rn(-q, rc.Ml[l], l < NL ? lim[l < NL ? l : 0] : 0.0);
+#pragma unroll
+    for (int l = 0; l + 1 < L; ++l) {
+        const double t = __dsub_rn(__fma_rn(c[l], inv32, magic), magic);
+        c[l] = __fma_rn(-t, two32, c[l]);
+        c[l + 1] = __dadd_rn(c[l + 1], t);
+    }
+    // the top nonzero digit a = c[T], the next two, and the sign of what lies below them
+    double a = 0.0, b = 0.0, c2 = 0.0, sR = 0.0;
+    int T = -1;
+#pragma unroll
+    for (int l = L - 1; l >= 0; --l) {
+        const bool nz = c[l] != 0.0;
+        if (T < 0) {
+            if (nz) {
+                T = l;
+                a = c[l];
+            }
+        } else if (l == T - 1) {
+            b = c[l];
+        } else if (l == T - 2) {
+            c2 = c[l];
+        } else if (sR == 0.0 && nz) {
+            sR = c[l] > 0.0 ? 1.0 : -1.0;
+        }
+    }
+    if (T < 0) return 0.0;
+    // t + f = a 2^64 + b 2^32 + c2 exactly (in units of 2^(32(T-2)))
+    const double ah = __dmul_rn(a, two32);
+    const double s = __dadd_rn(ah, b);
+    const double bb = __dsub_rn(s, ah);
+    const double e = __dadd_rn(__dsub_rn(ah, __dsub_rn(s, bb)), __dsub_rn(b, bb));
+    const double sh32 = __dmul_rn(s, two32);
+    const double l2 = __fma_rn(e, two32, c2);  // exact: |e| <= 2^10
+    const double t = __dadd_rn(sh32, l2);
+    const double tt = __dsub_rn(t, sh32);
+    const double f = __dadd_rn(__dsub_rn(sh32, __dsub_rn(t, tt)), __dsub_rn(l2, tt));
+    const bool negt = t < 0.0;
+    long long mag = __double_as_longlong(t) & 0x7FFFFFFFFFFFFFFFll;
+    const int E = (int)(mag >> 52);
+    const double fa = negt ? -f : f;  // f away from zero when positive
+    if (fa != 0.0 && sR != 0.0) {
+        // spacing next to |t| on f's side: the ulp, or half of it below a power of two
+        const double ulp = __longlong_as_double((long long)(E - 52) << 52);  // |t| >= 2^62 here: E - 52 >= 1
+        const double sp = (fa < 0.0 && (mag & 0xFFFFFFFFFFFFFll) == 0) ? 0.5 * ulp : ulp;
+        if (fabs(f) == 0.5 * sp && (negt ? -sR : sR) * fa > 0.0) mag += fa > 0.0 ? 1 : -1;
+    }
+    const int sh = 32 * (T - 2) + g - rc.two_b;
+    const int Ef = (int)(mag >> 52) - 1023 + sh;
+    double r;
+    if (Ef < -1022)
+        r = 0.0;
+    else if (Ef > 1023)
+        r = __longlong_as_double(0x7FF0000000000000ll);
+    else
+        r = __longlong_as_double(mag + ((long long)sh << 52));
+    return negt ? -r : r;
+}
+
 // Four consecutive digits of one plane in one load (uint8 digits of the INT8 path, uint16 digits of
 // the FP8 path), the first in the low bits.
 template <typename D>
@@ -173,15 +256,15 @@ __global__ void __launch_bounds__(256) recon_kernel(const D* __restrict__ kp, ui
 // X itself), so u = (k_s m_t + k_t m_s) mod (m_s m_t) < 2^16 -- one integer, formed on the integer pipe, against
 // one multiplier: the pairs halve the FP64 work. The sum X' = sum_p u_p M/(m_s m_t) < (S/2) M is X plus a
 // multiple of M. M/(m_s m_t) is held in NL 32-bit limbs; each limb sum, < 12 * 2^16 * 2^32 < 2^52, is exact
-// in binary64 (every fused multiply-add of integers below 2^53 whose sum stays below 2^53 is exact). A limb
-// sum is read back as an integer by adding 2^52 (the integer lands in the significand bits), and the limbs,
-// 32 bits apart, are the column sums of crt_finish directly.
-template <int NW, int NL>
+// in binary64 (every fused multiply-add of integers below 2^53 whose sum stays below 2^53 is exact). The
+// limbs, 32 bits apart, then go through the finish on the FP64 pipe (crt_finish_limbs); L is the number of
+// M's 32-bit words.
+template <int NL, int L>
 __global__ void __launch_bounds__(256) recon_pair_kernel(const uint8_t* __restrict__ kp, uint64_t mp, uint64_t np,
                                                          const int32_t* __restrict__ dA,
                                                          const int32_t* __restrict__ dB, double* __restrict__ c,
                                                          uint64_t m, uint64_t n, uint64_t ldc, const ReconConst rc) {
-    static_assert(NL <= NW && NL <= kPairLimbs, "limbs");
+    static_assert(NL <= L && L <= kPairLimbs, "limbs");
     const uint64_t nq = (n + 3) >> 2, total = m * nq, plane = mp * np;
     constexpr double two52 = 4503599627370496.0;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
@@ -216,15 +299,9 @@ __global__ void __launch_bounds__(256) recon_pair_kernel(const uint8_t* __restri
         double* crow = c + i * ldc + j0;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            uint64_t acc[NW];
-#pragma unroll
-            for (int w = 0; w < NW; ++w)
-                acc[w] = w < NL ? (uint64_t)__double_as_longlong(__dadd_rn(lim[e][w < NL ? w : 0], two52)) &
-                                      0xFFFFFFFFFFFFFull
-                                : 0ull;
             if (j0 + e < n) {
                 const int32_t g = rc.sh2 - (da + __ldg(dB + j0 + e));
-                crow[e] = crt_finish<NW>(acc, g, rc);
+                crow[e] = crt_finish_limbs<NL, L>(lim[e], g, rc);
             }
         }
     }
@@ -245,6 +322,11 @@ Big big_mul(const Big& a, uint32_t k) {
     }
     if (c) throw Error(OZTT_EINVAL, "recon: the product of the moduli exceeds 256 bits");
     return r;
+}
+int big_bits_of(const uint32_t (&w)[8]) {
+    for (int i = 7; i >= 0; --i)
+        if (w[i]) return 32 * i + 32 - __builtin_clz(w[i]);
+    return 0;
 }
 int big_bits(const Big& a) {
     for (int i = 7; i >= 0; --i)
@@ -306,6 +388,14 @@ static ReconConst recon_const(const oztt_ii_plan& p, int& nw, int& nl) {
     }
     // 32-bit limbs of the largest pair multiplier (at most kPairLimbs for moduli below 256)
     nl = std::max(1, (pair_bits + 31) / 32);
+    {
+        long double Mld = 0;
+        for (int w = 7; w >= 0; --w) Mld = Mld * 4294967296.0L + (long double)M.w[w];
+        for (int l = 0; l < kPairLimbs; ++l) {
+            rc.Rl[l] = (double)(ldexpl(1.0L, 32 * l) / Mld);
+            rc.Ml[l] = (double)M.w[l];
+        }
+    }
     return rc;
 }
 
@@ -332,16 +422,15 @@ void launch_recon(const uint8_t* kp, uint64_t mp, uint64_t np, const int32_t* dA
     // (identical results)
     const bool fp64 = option_value(OZTT_OPT_RECON_INT) != 1;
     if (fp64) {
-#define OZTT_RECON_PAIR(NW_, NL_) \
-    case NW_ * 10 + NL_: \
-        recon_pair_kernel<NW_, NL_><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); \
+#define OZTT_RECON_PAIR(NL_, L_) \
+    case NL_ * 10 + L_: \
+        recon_pair_kernel<NL_, L_><<<blocks, 256, 0, st>>>(kp, mp, np, dA, dB, c, m, n, ldc, rc); \
         break
-        switch (nw * 10 + nl) {
-            OZTT_RECON_PAIR(3, 1); OZTT_RECON_PAIR(3, 2); OZTT_RECON_PAIR(3, 3);
-            OZTT_RECON_PAIR(4, 2); OZTT_RECON_PAIR(4, 3); OZTT_RECON_PAIR(4, 4);
-            OZTT_RECON_PAIR(5, 3); OZTT_RECON_PAIR(5, 4); OZTT_RECON_PAIR(5, 5);
-            OZTT_RECON_PAIR(6, 4); OZTT_RECON_PAIR(6, 5); OZTT_RECON_PAIR(6, 6);
-            OZTT_RECON_PAIR(7, 5); OZTT_RECON_PAIR(7, 6);
+        const int words_m = std::max(1, (big_bits_of(rc.M) + 31) / 32);
+        switch (nl * 10 + words_m) {
+            OZTT_RECON_PAIR(1, 1); OZTT_RECON_PAIR(1, 2); OZTT_RECON_PAIR(2, 2); OZTT_RECON_PAIR(2, 3);
+            OZTT_RECON_PAIR(3, 3); OZTT_RECON_PAIR(3, 4); OZTT_RECON_PAIR(4, 4); OZTT_RECON_PAIR(4, 5);
+            OZTT_RECON_PAIR(5, 5); OZTT_RECON_PAIR(5, 6); OZTT_RECON_PAIR(6, 6);
         default: throw Error(OZTT_EINVAL, "recon: no kernel for these moduli");
         }
 #undef OZTT_RECON_PAIR
