@@ -220,7 +220,7 @@ int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* 
  *   7 when the first plan was made, 8 1 if the complete statistics gave another plan, 9 1 if the bounds of
  *   the statistics left a decision open so that the exact sums were computed, 10 1 if C was read back as
  *   its pieces finished (before the plan was confirmed); the device timeline in ms from the first copy:
- *   11 A's first half done against every block of B, 12 the last reconstruction, 13 the end of the
+ *   11 A's first part (9/16 of its rows) done against every block of B, 12 the last reconstruction, 13 the end of the
  *   read-back of C, 14 the last band's bounded statistics; 15 when the host's value checks were ready
  *   (ms from the call).
  * Zeros before the first such call. */
@@ -426,7 +426,7 @@ int oztt_resident_gemm(oztt_resident* a, oztt_resident* b, double* c, int32_t c_
  *   OZTT_OPT_GEMM_CTA_PAIRS  1: the INT8 residue GEMMs and Scheme I diagonal GEMMs on CTA pairs
  *                            (tcgen05 cta_group::2, M = 256 per pair); 0: one CTA per tile.
  *   OZTT_OPT_RECON_INT       1: the Scheme II INT8 reconstruction on the integer pipe (32-bit words);
- *                            0: the FP64-pipe kernel (radix-2^39 limbs). */
+ *                            0: the FP64-pipe kernel (moduli in pairs, 32-bit FP64 limbs). */
 #define OZTT_OPT_GEMM_CTA_PAIRS 1
 #define OZTT_OPT_RECON_INT 2
 /* Sets an option to 0 or 1 (OZTT_EINVAL for an unknown option or value). */

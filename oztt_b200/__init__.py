@@ -375,7 +375,7 @@ def ii_int8_last_phases() -> dict:
     computes while its operands upload also when the first plan was made, whether the complete statistics
     replanned, whether the bounds left the decision open so that the exact sums were computed, whether C
     was read back as its pieces finished (before the plan was confirmed), the device timeline (ms from the
-    first copy: A's first half done against every block of B, the last reconstruction, the end of C's
+    first copy: A's first part done against every block of B, the last reconstruction, the end of C's
     read-back, the last band's bounded statistics) and when the host's value checks were ready."""
     out = np.zeros(16, dtype=np.float64)
     _lib().oztt_ii_int8_last_phases(out.ctypes.data, 16)

@@ -291,16 +291,16 @@ bool overlaps(const void* p, uint64_t pbytes, const void* q, uint64_t qbytes) {
     return p0 < q0 + qbytes && q0 < p0 + pbytes;
 }
 
-// Context::gemm from host buffers, computing while the operands upload. The upload order is A's first half
-// (bands of 1024 rows), then B in eight blocks of columns, then the rest of A. The precision decision depends
-// on the statistics of the whole A and B, so the pipeline starts on a first plan made from an estimate: A's
-// first half and B's first block, each standing for its matrix (the decision depends on the size-free ratio
-// (TA nB + TB nA) / 12 nC, which such parts estimate closely). On that plan A's first half is split once and
-// multiplied by each block of B as the block lands; then each later band of A by the whole B as it lands.
-// The value checks need the maxima of every row of A and column of B: the device measures A's first half
-// for the first plan, the host's threads measure the rest of A and all of B from the caller's buffers
-// meanwhile. Once every value is checked, the pieces of C (A's first half against each block of B, then
-// the bands) are read back as they finish -- when that cannot change the outcome of the call:
+// Context::gemm from host buffers, computing while the operands upload. The upload order is A's first part
+// (9/16 of its rows, bands of 1024), then B in eight blocks of columns, then the rest of A. The precision
+// decision depends on the statistics of the whole A and B, so the pipeline starts on a first plan made from
+// an estimate: A's first part and B's first block, each standing for its matrix (the decision depends on the
+// size-free ratio (TA nB + TB nA) / 12 nC, which such parts estimate closely). On that plan A's first part
+// is split once and multiplied by each block of B as the block lands; then each later band of A by the whole
+// B as it lands. The value checks need the maxima of every row of A and column of B: the device measures A's
+// first part for the first plan, the host's threads measure the rest of A and all of B from the caller's
+// buffers meanwhile. Once every value is checked, the pieces of C (A's first part against each block of B,
+// then the bands) are read back as they finish -- when that cannot change the outcome of the call:
 // no plan for these dimensions can fail, and C does not overlap A or B. When A has landed, the reference's
 // plan is decided from bounds of its statistics measured as the blocks and bands landed (only a decision
 // that lies within the bounds needs the exact long-double sums). If it equals the first plan, C is its
@@ -315,7 +315,10 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     cudaStream_t st = call.work();
     const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
     const uint64_t bm = 1024;
-    const uint64_t pre = std::min(round_up(m / 2, bm), m);  // A's first part: whole bands
+    // A's first part, whole bands: 9/16 of A. Each block of B then costs about as much device time (the
+    // first part's GEMM against it) as the next block takes to arrive, so the B phase stays upload-bound
+    // while as little as possible of A is left for after it.
+    const uint64_t pre = std::min(round_up(m * 9 / 16, bm), m);
     const uint64_t pre_bands = (pre + bm - 1) / bm;
     const uint64_t nb = round_up((n + 7) / 8, 256);  // B's blocks of columns
     HostMaxima host(a, b, m, n, k, pre);

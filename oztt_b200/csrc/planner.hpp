@@ -220,7 +220,7 @@ struct StreamedPhases {
     double pipeline_ms = 0;    // scale, split, banded GEMM and reconstruction, C read back
     double total_ms = 0;
     int bands = 0;
-    double first_plan_ms = 0;  // overlapped INT8 path: when the first plan (A's first half, B's first block) was made
+    double first_plan_ms = 0;  // overlapped INT8 path: when the first plan (A's first part, B's first block) was made
     int replanned = 0;         // 1 if the complete statistics gave another plan and the pipeline ran again
     int exact_stats = 0;       // 1 if the bounds left the decision open and the exact sums were computed
     int early_readback = 0;    // 1 if C's bands were read back as they finished, before the plan was confirmed

@@ -196,7 +196,7 @@ std::vector<cudaEvent_t> StreamedCall::upload_prefix_first(uint64_t pre_rows, ui
     cert_buf_ = std::make_unique<DevBuf>(cert_, m_ * kCertWidth * 8);
     bparts_ = std::make_unique<DevBuf>(cert_, (k_ * kBCertWidth + n_ + 1 + 8 * k_ + k_ + 8 * N) * 8);
     cert_flags_ = std::make_unique<DevBuf>(cert_, 16);
-    // the probe vectors (1 MiB) first, while the copy engine is idle; then A's first half at once
+    // the probe vectors (1 MiB) first, while the copy engine is idle; then A's first part at once
     const std::vector<double> g = policy_vectors_host((uint32_t)N);
     OZTT_CUDA(cudaMemcpyAsync(b_probe(), g.data(), g.size() * 8, cudaMemcpyHostToDevice, cert_));
     OZTT_CUDA(cudaStreamSynchronize(cert_));  // the probe vectors leave the host vector

@@ -1,7 +1,7 @@
 """Context::gemm for Scheme II INT8 computing while its operands upload (calls of at least 4096 rows).
 
-The upload order is A's first half, B in blocks of columns, the rest of A. The pipeline starts on a plan
-estimated from A's first half and B's first block and is confirmed, or run again, with the reference's plan
+The upload order is A's first part (9/16 of its rows), B in blocks of columns, the rest of A. The pipeline starts on a plan
+estimated from A's first part and B's first block and is confirmed, or run again, with the reference's plan
 from the complete statistics; C is read back as its bands finish once the host has checked every value
 (unless C overlaps A or B, or some plan for the dimensions could fail). The result must be the device
 pipeline's under the reference's plan, bit for bit, in either case; an invalid value in A's last band, or a
@@ -35,7 +35,7 @@ def test_overlapped_equals_device_pipeline(oztt, oracle, cuda):
 
 
 def test_replanned_when_the_first_part_misleads(oztt, oracle, cuda):
-    """A's first half has a narrow range of magnitudes and the rest a wide one: the first plan's width
+    """A's first part has a narrow range of magnitudes and the rest a wide one: the first plan's width
     (53 bits) differs from the reference's (56), the pipeline runs again after C's bands were read back on
     the first plan, and C is the reference plan's."""
     m, n, k = 4224, 512, 640
@@ -67,7 +67,7 @@ def test_invalid_value_in_the_last_band_leaves_c_untouched(oztt, oracle, cuda):
                                            ("b", "B contains NaN or infinity"),
                                            ("a_range", "each nonzero row maximum of A")])
 def test_invalid_values_reported_in_order_and_c_untouched(oztt, oracle, cuda, where, message):
-    """Invalid values in A's first half (its maxima measured on the device) or in B (on the host's threads):
+    """Invalid values in A's first part (its maxima measured on the device) or in B (on the host's threads):
     the front end's report, C never written."""
     m, n, k = 4224, 300, 200
     a, b = oracle.gen_inputs(m, n, k, 0.5, 26)
