@@ -711,8 +711,8 @@ def run_single(args) -> None:
                          "phases_ms_last_call": {key: round(v, 2) if isinstance(v, float) else v
                                                  for key, v in phases.items()},
                          "h2d_bytes_per_step": 8 * (m * k + k * n), "d2h_bytes_per_step": 8 * m * n,
-                         "path": "ozTTgemm::Context::gemm via oztt_gemm: pinned H2D in the order A's first 9/16 of rows, B "
-                                 "by column blocks, the rest of A; the pipeline on a first plan estimated from A's first "
+                         "path": "ozTTgemm::Context::gemm via oztt_gemm: pinned H2D in the order B's first column block, A's "
+                                 "first 9/16 of rows, B's other column blocks, the rest of A; the pipeline on a first plan estimated from A's first "
                                  "part and B's first block (A's first part times each block of B as it lands, then each "
                                  "later band of A); the host's value checks meanwhile, then each band of C read back as "
                                  "it finishes; the reference's plan from bounds of the statistics measured as the "

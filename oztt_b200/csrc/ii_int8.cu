@@ -291,21 +291,22 @@ bool overlaps(const void* p, uint64_t pbytes, const void* q, uint64_t qbytes) {
     return p0 < q0 + qbytes && q0 < p0 + pbytes;
 }
 
-// Context::gemm from host buffers, computing while the operands upload. The upload order is A's first part
-// (9/16 of its rows, bands of 1024), then B in eight blocks of columns, then the rest of A. The precision
-// decision depends on the statistics of the whole A and B, so the pipeline starts on a first plan made from
-// an estimate: A's first part and B's first block, each standing for its matrix (the decision depends on the
-// size-free ratio (TA nB + TB nA) / 12 nC, which such parts estimate closely). On that plan A's first part
-// is split once and multiplied by each block of B as the block lands; then each later band of A by the whole
-// B as it lands. The value checks need the maxima of every row of A and column of B: the device measures A's
-// first part for the first plan, the host's threads measure the rest of A and all of B from the caller's
-// buffers meanwhile. Once every value is checked, the pieces of C (A's first part against each block of B,
-// then the bands) are read back as they finish -- when that cannot change the outcome of the call:
-// no plan for these dimensions can fail, and C does not overlap A or B. When A has landed, the reference's
-// plan is decided from bounds of its statistics measured as the blocks and bands landed (only a decision
-// that lies within the bounds needs the exact long-double sums). If it equals the first plan, C is its
-// result; otherwise the pipeline runs again with it and C is read back again. An invalid input is reported
-// before anything is written to C, as the front end requires.
+// Context::gemm from host buffers, computing while the operands upload. The upload order is B's first block
+// of columns, A's first part (9/16 of its rows, bands of 1024), B's seven other blocks, then the rest of A.
+// The precision decision depends on the statistics of the whole A and B, so the pipeline starts on a first
+// plan made from an estimate: A's first part and B's first block, each standing for its matrix (the decision
+// depends on the size-free ratio (TA nB + TB nA) / 12 nC, which such parts estimate closely), measured as
+// they land. On that plan A's first part is split once and multiplied by each block of B (the first one at
+// once, the others as they land); then each later band of A by the whole B as it lands. The value checks
+// need the maxima of every row of A and column of B: the device measures A's first part for the first plan,
+// the host's threads measure the rest of A and all of B from the caller's buffers meanwhile. Once every value
+// is checked, the pieces of C (A's first part against each block of B, then the bands) are read back as they
+// finish -- when that cannot change the outcome of the call: no plan for these dimensions can fail, and C
+// does not overlap A or B. When A has landed, the reference's plan is decided from bounds of its statistics
+// measured as the blocks and bands landed (only a decision that lies within the bounds needs the exact
+// long-double sums). If it equals the first plan, C is its result; otherwise the pipeline runs again with it
+// and C is read back again. An invalid input is reported before anything is written to C, as the front end
+// requires.
 int run_ii_int8_overlapped(int device_id, const double* a, const double* b, double* c, uint64_t m, uint64_t n,
                            uint64_t k, uint32_t max_moduli, int32_t reconstruction,
                            const std::function<void(const uint64_t*, const uint64_t*)>& check, oztt_ii_plan& p,
@@ -327,7 +328,7 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     // the first plan, from A's first part and B's first block
     bool estimated = false;
     std::vector<uint64_t> pre_max;
-    const PolicyStats first = call.prefix_estimate(pre, nb, landed[pre_bands - 1], b_landed[0], estimated, &pre_max);
+    const PolicyStats first = call.prefix_estimate(estimated, &pre_max);
     oztt_ii_plan p0{};
     std::string err0;
     const int rc0 = estimated ? plan_ii_int8_with([&](uint32_t, uint32_t) { return first; }, m, n, k, max_moduli,

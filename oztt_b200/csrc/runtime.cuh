@@ -132,6 +132,25 @@ private:
     std::shared_ptr<const std::vector<double>> g_;
 };
 
+// The first plan's estimate of the policy statistics from A's first rows_a rows and B's first cols_b columns,
+// in steps that follow the upload on stream st (stats.cu).
+class PrefixEstimate {
+public:
+    PrefixEstimate(uint64_t rows_a, uint64_t k, uint64_t cols_b, cudaStream_t st);
+    // B's first block (rows ldb apart) with the probe vectors g (8 rows gstride apart), once it has landed
+    void b_block(const double* b, uint64_t ldb, const double* g, uint64_t gstride);
+    // rows r0 .. r0+rows-1 of A (the whole row-major A), after b_block, once they have landed
+    void a_band(const double* a, uint64_t r0, uint64_t rows);
+    // waits for the steps; ok is false when no estimate could be made; row_max receives the magnitude
+    // patterns of the maxima of A's rows_a rows
+    PolicyStats finish(bool& ok, std::vector<uint64_t>* row_max);
+
+private:
+    uint64_t rows_a_, k_, cols_b_;
+    cudaStream_t st_;
+    DevBuf cmax_, y_, sq_, cert_, flags_;
+};
+
 class StreamedCall {
 public:
     StreamedCall(int device_id, const double* a, const double* b, uint64_t m, uint64_t n, uint64_t k);
@@ -155,18 +174,18 @@ public:
     // waits for everything (the read-back included) and records the phases of the call, the pipeline
     // counted from pipeline_start_ms (ms_since_start when it was issued)
     void finish(double pipeline_start_ms);
-    // The upload of the INT8 path that computes while its operands land: A's first pre_rows rows in bands of
-    // band_rows, then B in blocks of block_cols columns, then the rest of A in bands. Each block of B is
-    // measured as it lands and each band of A once B has landed (one fast pass each that bounds the
+    // The upload of the INT8 path that computes while its operands land: B's first block of block_cols
+    // columns, A's first pre_rows rows in bands of band_rows, B's other blocks, then the rest of A in bands
+    // (B's first block first, so that the first plan's estimate follows A's bands as they land). Each block
+    // of B is measured as it lands and each band of A once B has landed (one fast pass each that bounds the
     // reference's statistics, on a high-priority stream, so that it runs between the GEMM's launches).
     // Returns the events that mark each band's arrival and fills b_landed with those of B's blocks.
     std::vector<cudaEvent_t> upload_prefix_first(uint64_t pre_rows, uint64_t band_rows, uint64_t block_cols,
                                                  std::vector<cudaEvent_t>& b_landed);
     // After upload_prefix_first: the estimate of the statistics from A's first pre_rows rows and B's first
-    // block (estimate_policy_stats); waits for both. ok is false when no estimate could be made; row_max
-    // receives the magnitude patterns of those rows' maxima.
-    PolicyStats prefix_estimate(uint64_t pre_rows, uint64_t block_cols, cudaEvent_t a_landed, cudaEvent_t b_landed,
-                                bool& ok, std::vector<uint64_t>* row_max);
+    // block (PrefixEstimate, measured as they landed); waits for it. ok is false when no estimate could be
+    // made; row_max receives the magnitude patterns of those rows' maxima.
+    PolicyStats prefix_estimate(bool& ok, std::vector<uint64_t>* row_max);
     // After upload_prefix_first: bounds of the statistics that contain the reference's values. Waits for
     // every band's measurements.
     PolicyBounds certified_bounds();
@@ -201,6 +220,7 @@ private:
     // B's bounded measurements (upload_prefix_first): per row of B 17 accumulators, the column maxima (n
     // patterns), the scale, the scaled sketch (8 x k), its error bounds (k), the probe vectors (8 x N)
     std::unique_ptr<DevBuf> bparts_;
+    std::unique_ptr<PrefixEstimate> est_run_;
     double* stage_ = nullptr;  // pinned: the measurements of A's bands and B, copied back as they are written
     bool stage_shared_ = false;
     double* b_acc() const { return bparts_->as<double>(); }

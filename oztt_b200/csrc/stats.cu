@@ -910,34 +910,43 @@ __global__ void __launch_bounds__(256) block_rows_kernel(const double* __restric
     }
 }
 
-// An estimate of the precision policy's statistics with rows [0, rows_a) of A (row-major, k columns)
-// standing for the whole A and columns [0, cols_b) of B (rows ldb apart) for the whole B: each part is
-// measured as if it were the matrix (the statistics enter the width cap through the size-free ratio
-// (TA nB + TB nA) / nC). It is what the first plan of a call that computes while its operands are still
-// uploading is made from, and is then confirmed by the reference's statistics. g: the probe vectors on
-// the device (8 x N). ok is false when a part holds a value that is not finite or the estimate degenerates.
-// row_max, when given, receives the magnitude patterns of the maxima of A's rows_a rows (for the value checks).
-PolicyStats estimate_policy_stats(const double* a, uint64_t rows_a, uint64_t k, const double* b, uint64_t cols_b,
-                                  uint64_t ldb, const double* g, uint64_t N, cudaStream_t st, bool& ok,
-                                  std::vector<uint64_t>* row_max) {
+// An estimate of the policy statistics with rows [0, rows_a) of A (row-major, k columns) standing for the
+// whole A and columns [0, cols_b) of B (rows ldb apart) for the whole B: each part is measured as if it
+// were the matrix (the statistics enter the width cap through the size-free ratio (TA nB + TB nA) / nC).
+// It is what the first plan of a call that computes while its operands are still uploading is made from,
+// and is then confirmed by the reference's statistics. The steps follow the upload: b_block measures B's
+// block as soon as it lands (its column maxima, its rows' sums of squares and its sketch y_l = B g_l, g the
+// probe vectors on the device), a_band each band of A's rows as it lands (band_certify_kernel with that
+// sketch), finish combines them on the host.
+PrefixEstimate::PrefixEstimate(uint64_t rows_a, uint64_t k, uint64_t cols_b, cudaStream_t st)
+    : rows_a_(rows_a), k_(k), cols_b_(cols_b), st_(st), cmax_(st, cols_b * 8), y_(st, (uint64_t)kVectors * k * 8),
+      sq_(st, k * 8), cert_(st, rows_a * kCertW * 8), flags_(st, 16) {
+    OZTT_CUDA(cudaMemsetAsync(cmax_.p, 0, cols_b * 8, st));
+    OZTT_CUDA(cudaMemsetAsync(flags_.p, 0, 16, st));
+}
+
+void PrefixEstimate::b_block(const double* b, uint64_t ldb, const double* g, uint64_t gstride) {
+    launch_col_absmax(b, k_, cols_b_, ldb, cmax_.as<unsigned long long>(), st_);
+    block_rows_kernel<<<(unsigned)((k_ * 32 + 255) / 256), 256, 0, st_>>>(b, k_, cols_b_, ldb, g, gstride,
+                                                                         y_.as<double>(), sq_.as<double>());
+    OZTT_CUDA(cudaGetLastError());
+}
+
+void PrefixEstimate::a_band(const double* a, uint64_t r0, uint64_t rows) {
+    if (!rows) return;
+    band_certify_kernel<<<(unsigned)((rows + kCertRows - 1) / kCertRows), 256, 0, st_>>>(
+        a + r0 * k_, rows, k_, y_.as<double>(), nullptr, cert_.as<double>() + r0 * kCertW, flags_.as<uint32_t>());
+    OZTT_CUDA(cudaGetLastError());
+}
+
+PolicyStats PrefixEstimate::finish(bool& ok, std::vector<uint64_t>* row_max) {
     ok = false;
-    if (!rows_a || !cols_b || !k) return {};
-    DevBuf cmax(st, cols_b * 8), y(st, (uint64_t)kVectors * k * 8), sq(st, k * 8), cert(st, rows_a * kCertW * 8),
-        flags(st, 16);
-    OZTT_CUDA(cudaMemsetAsync(cmax.p, 0, cols_b * 8, st));
-    OZTT_CUDA(cudaMemsetAsync(flags.p, 0, 16, st));
-    launch_col_absmax(b, k, cols_b, ldb, cmax.as<unsigned long long>(), st);
-    block_rows_kernel<<<(unsigned)((k * 32 + 255) / 256), 256, 0, st>>>(b, k, cols_b, ldb, g, N, y.as<double>(),
-                                                                        sq.as<double>());
-    OZTT_CUDA(cudaGetLastError());
-    band_certify_kernel<<<(unsigned)((rows_a + kCertRows - 1) / kCertRows), 256, 0, st>>>(
-        a, rows_a, k, y.as<double>(), nullptr, cert.as<double>(), flags.as<uint32_t>());
-    OZTT_CUDA(cudaGetLastError());
+    const uint64_t rows_a = rows_a_, k = k_, cols_b = cols_b_;
     std::vector<double> hcmax(cols_b), hsq(k), hcert(rows_a * kCertW);
-    OZTT_CUDA(cudaMemcpyAsync(hcmax.data(), cmax.p, cols_b * 8, cudaMemcpyDeviceToHost, st));
-    OZTT_CUDA(cudaMemcpyAsync(hsq.data(), sq.p, k * 8, cudaMemcpyDeviceToHost, st));
-    OZTT_CUDA(cudaMemcpyAsync(hcert.data(), cert.p, hcert.size() * 8, cudaMemcpyDeviceToHost, st));
-    OZTT_CUDA(cudaStreamSynchronize(st));
+    OZTT_CUDA(cudaMemcpyAsync(hcmax.data(), cmax_.p, cols_b * 8, cudaMemcpyDeviceToHost, st_));
+    OZTT_CUDA(cudaMemcpyAsync(hsq.data(), sq_.p, k * 8, cudaMemcpyDeviceToHost, st_));
+    OZTT_CUDA(cudaMemcpyAsync(hcert.data(), cert_.p, hcert.size() * 8, cudaMemcpyDeviceToHost, st_));
+    OZTT_CUDA(cudaStreamSynchronize(st_));
     if (row_max) {
         row_max->resize(rows_a);
         for (uint64_t r = 0; r < rows_a; ++r) std::memcpy(&(*row_max)[r], &hcert[r * kCertW], 8);

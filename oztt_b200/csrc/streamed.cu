@@ -43,9 +43,6 @@ void bounded_nb(const double* acc, uint64_t k, uint64_t n, double rgB, double& l
 std::vector<double> policy_vectors_host(uint32_t N);
 PolicyBounds certified_policy_bounds(const double* cert, uint64_t m, uint64_t k, const double* col_max, uint64_t n,
                                      double nB_lo, double nB_hi, double rgB);
-PolicyStats estimate_policy_stats(const double* a, uint64_t rows_a, uint64_t k, const double* b, uint64_t cols_b,
-                                  uint64_t ldb, const double* g, uint64_t N, cudaStream_t st, bool& ok,
-                                  std::vector<uint64_t>* row_max);
 constexpr uint64_t kCertWidth = 19;   // doubles per row of A written by launch_band_certify
 constexpr uint64_t kBCertWidth = 17;  // doubles per row of B accumulated by launch_bcert_block
 
@@ -114,6 +111,7 @@ StreamedCall::~StreamedCall() {
         if (s) cudaStreamSynchronize(s);
     // the buffers go back to the pool on the work stream, after everything that used them
     stats_.reset();
+    est_run_.reset();
     cert_buf_.reset();
     bparts_.reset();
     cert_flags_.reset();
@@ -204,24 +202,38 @@ std::vector<cudaEvent_t> StreamedCall::upload_prefix_first(uint64_t pre_rows, ui
     order(work_, up_);
     OZTT_CUDA(cudaEventCreate(&tl_start_));
     OZTT_CUDA(cudaEventRecord(tl_start_, up_));
-    std::vector<cudaEvent_t> landed;
-    const auto a_band = [&](uint64_t r0) {
-        const uint64_t rows = std::min(band_rows, m_ - r0);
-        OZTT_CUDA(cudaMemcpyAsync(da + r0 * k_, a_ + r0 * k_, rows * k_ * 8, cudaMemcpyHostToDevice, up_));
-        landed.push_back(mark(up_));
-    };
-    for (uint64_t r0 = 0; r0 < pre_rows; r0 += band_rows) a_band(r0);
+    est_run_ = std::make_unique<PrefixEstimate>(pre_rows, k_, std::min(block_cols, n_), est_);
+    OZTT_CUDA(cudaStreamWaitEvent(est_, g_ready_, 0));
     OZTT_CUDA(cudaMemsetAsync(cert_flags_->p, 0, 16, cert_));
     OZTT_CUDA(cudaMemsetAsync(bparts_->p, 0, (k_ * kBCertWidth + n_) * 8, cert_));  // accumulators, maxima
-    // B's blocks, each measured as it lands (its columns' maxima exactly, its rows' partial sketch sums bounded)
+    order(cert_, up_);
+    // B's blocks, each measured as it lands (its columns' maxima exactly, its rows' partial sketch sums
+    // bounded); the first block also for the first plan's estimate
     b_landed.clear();
-    for (uint64_t c0 = 0; c0 < n_; c0 += block_cols) {
+    const auto b_block = [&](uint64_t c0) {
         const uint64_t w = std::min(block_cols, n_ - c0);
         OZTT_CUDA(cudaMemcpy2DAsync(db + c0, n_ * 8, b_ + c0, n_ * 8, w * 8, k_, cudaMemcpyHostToDevice, up_));
         b_landed.push_back(order(up_, cert_));
         launch_col_absmax(db + c0, k_, w, n_, b_colmax() + c0, cert_);
         launch_bcert_block(db + c0, k_, w, n_, b_probe() + c0, N, b_acc(), cert_flags_->as<uint32_t>() + 1, cert_);
+    };
+    b_block(0);
+    OZTT_CUDA(cudaStreamWaitEvent(est_, b_landed[0], 0));
+    est_run_->b_block(db, n_, b_probe(), N);
+    // A's first part, each band measured for the estimate as it lands
+    std::vector<cudaEvent_t> landed;
+    const auto a_band = [&](uint64_t r0) {
+        const uint64_t rows = std::min(band_rows, m_ - r0);
+        OZTT_CUDA(cudaMemcpyAsync(da + r0 * k_, a_ + r0 * k_, rows * k_ * 8, cudaMemcpyHostToDevice, up_));
+        landed.push_back(mark(up_));
+        return rows;
+    };
+    for (uint64_t r0 = 0; r0 < pre_rows; r0 += band_rows) {
+        const uint64_t rows = a_band(r0);
+        OZTT_CUDA(cudaStreamWaitEvent(est_, landed.back(), 0));
+        est_run_->a_band(da, r0, std::min(rows, pre_rows - r0));
     }
+    for (uint64_t c0 = block_cols; c0 < n_; c0 += block_cols) b_block(c0);
     launch_bcert_finish(b_colmax(), n_, b_acc(), k_, bcert_error_factor(n_), b_rg(), b_y(), b_ew(), cert_);
     for (uint64_t r0 = pre_rows; r0 < m_; r0 += band_rows) a_band(r0);
     // the bands' bounded statistics need B's sketch: all of them after B, each after its band
@@ -245,13 +257,8 @@ std::vector<cudaEvent_t> StreamedCall::upload_prefix_first(uint64_t pre_rows, ui
     return landed;
 }
 
-PolicyStats StreamedCall::prefix_estimate(uint64_t pre_rows, uint64_t block_cols, cudaEvent_t a_landed,
-                                          cudaEvent_t b_landed, bool& ok, std::vector<uint64_t>* row_max) {
-    OZTT_CUDA(cudaStreamWaitEvent(est_, a_landed, 0));
-    OZTT_CUDA(cudaStreamWaitEvent(est_, b_landed, 0));
-    OZTT_CUDA(cudaStreamWaitEvent(est_, g_ready_, 0));
-    return estimate_policy_stats(da_->as<double>(), pre_rows, k_, db_->as<double>(), std::min(block_cols, n_), n_,
-                                 b_probe(), round_up(n_, 64), est_, ok, row_max);
+PolicyStats StreamedCall::prefix_estimate(bool& ok, std::vector<uint64_t>* row_max) {
+    return est_run_->finish(ok, row_max);
 }
 
 PolicyBounds StreamedCall::certified_bounds() {

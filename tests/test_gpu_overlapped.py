@@ -1,9 +1,10 @@
 """Context::gemm for Scheme II INT8 computing while its operands upload (calls of at least 4096 rows).
 
-The upload order is A's first part (9/16 of its rows), B in blocks of columns, the rest of A. The pipeline starts on a plan
-estimated from A's first part and B's first block and is confirmed, or run again, with the reference's plan
-from the complete statistics; C is read back as its bands finish once the host has checked every value
-(unless C overlaps A or B, or some plan for the dimensions could fail). The result must be the device
+The upload order is B's first block of columns, A's first part (9/16 of its rows), B's other blocks, the
+rest of A. The pipeline starts on a plan estimated from A's first part and B's first block and is
+confirmed, or run again, with the reference's plan from the complete statistics; C is read back as its
+pieces finish once every value is checked (unless C overlaps A or B, or some plan for the dimensions could
+fail). The result must be the device
 pipeline's under the reference's plan, bit for bit, in either case; an invalid value in A's last band, or a
 plan that fails, must leave C untouched; and C may alias A.
 """
