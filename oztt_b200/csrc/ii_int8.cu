@@ -34,6 +34,7 @@ void launch_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, co
 void launch_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
                        const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st,
                        uint64_t plane_rows = 0);
+void launch_transpose(const double* b, uint64_t k, uint64_t n, uint64_t ldb, double* bt, cudaStream_t st);
 void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
                          const oztt_ii_plan& p, int mode, void* out, int* err_word, cudaStream_t st,
                          uint64_t a_plane_rows = 0, uint64_t b_plane_rows = 0);
@@ -97,18 +98,22 @@ void run_ii_int8_device(const double* a, const double* b, double* c, uint64_t m,
     check_plan(p);
     const uint64_t S = (uint64_t)p.S;
     const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
-    DevBuf dA(st, mp * 4), dB(st, np * 4), colmax(st, n * 8), words(st, 16);
+    DevBuf dA(st, mp * 4), dB(st, np * 4), words(st, 16), bt(st, n * k * 8);
     DevBuf ra(st, S * mp * kp), rb(st, S * np * kp), kpl(st, S * mp * np);
     OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
     Pipeline pl;
     pl.add(kScale, kHead, 0, [&] { launch_scale_rows(a, m, k, k, p.shift, dA.as<int32_t>(), nullptr, flags, st); });
+    // B transposed once (an HBM-bound copy), then scaled and split by rows: its columns are B^T's rows, with
+    // the same maxima, exponent deltas, flags and residue planes [S][np][kp] as the column kernels give
     pl.add(kScale, kHead, 1, [&] {
-        launch_scale_cols(b, k, n, n, p.shift, dB.as<int32_t>(), nullptr, flags, colmax.as<unsigned long long>(), st);
+        launch_transpose(b, k, n, n, bt.as<double>(), st);
+        launch_scale_rows(bt.as<double>(), n, k, k, p.shift, dB.as<int32_t>(), nullptr, flags, st);
     });
     pl.add(kSlice, kHead, 2, [&] { launch_split_rows(a, m, k, k, dA.as<int32_t>(), p, ra.as<int8_t>(), mp, kp, st); });
-    pl.add(kSlice, kHead, 3, [&] { launch_split_cols(b, k, n, n, dB.as<int32_t>(), p, rb.as<int8_t>(), np, kp, st); });
+    pl.add(kSlice, kHead, 3,
+           [&] { launch_split_rows(bt.as<double>(), n, k, k, dB.as<int32_t>(), p, rb.as<int8_t>(), np, kp, st); });
     pl.add(kGemm, kGemmStep, 4,
            [&] { launch_residue_gemm(ra.as<int8_t>(), rb.as<int8_t>(), mp, np, kp, p, 1, kpl.p, gemm_err, st); });
     const uint64_t halves = (evaluation_active() && p.two_pass && m > 1) ? 2 : 1;
@@ -121,6 +126,7 @@ void run_ii_int8_device(const double* a, const double* b, double* c, uint64_t m,
     }
     pl.writes(dA.p, mp * 4);
     pl.writes(dB.p, np * 4);
+    pl.writes(bt.p, n * k * 8);
     pl.writes(ra.p, S * mp * kp);
     pl.writes(rb.p, S * np * kp);
     pl.writes(kpl.p, S * mp * np);

@@ -503,6 +503,27 @@ __global__ void __launch_bounds__(256) split_cols_kernel(const double* __restric
     }
 }
 
+// B transposed (bt[j][i] = b[i][j], k x n to n x k), through 32 x 32 tiles in shared memory: B's columns
+// then split as rows (split_rows_kernel), whose loads and stores are contiguous, instead of through the
+// column kernel's strided loads and scattered 16-byte stores. Blocks of 32 x 8 threads, 4 elements each.
+__global__ void __launch_bounds__(256) transpose_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
+                                                        uint64_t ldb, double* __restrict__ bt) {
+    __shared__ double tile[32][33];
+    const uint64_t c0 = (uint64_t)blockIdx.x * 32, r0 = (uint64_t)blockIdx.y * 32;
+    const int tx = threadIdx.x, ty = threadIdx.y;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+        const uint64_t r = r0 + ty + j, c = c0 + tx;
+        tile[ty + j][tx] = (r < k && c < n) ? __ldg(b + r * ldb + c) : 0.0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+        const uint64_t c = c0 + ty + j, r = r0 + tx;
+        if (c < n && r < k) bt[c * k + r] = tile[tx][ty + j];
+    }
+}
+
 // ---- host side -------------------------------------------------------------------------------
 static int device_sms() {
     int dev = 0, sms = 148;
@@ -579,6 +600,14 @@ void launch_scale_cols_mode(const double* b, uint64_t k, uint64_t n, uint64_t ld
 void launch_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, int32_t shift, int32_t* delta,
                        uint16_t* bfmax, uint32_t* flags, cudaStream_t st) {
     launch_scale_rows_mode(a, m, k, lda, shift, 1u, delta, bfmax, flags, st);
+}
+
+void launch_transpose(const double* b, uint64_t k, uint64_t n, uint64_t ldb, double* bt, cudaStream_t st) {
+    if (!k || !n) return;
+    if ((n + 31) / 32 > 0x7FFFFFFFull || (k + 31) / 32 > 65535) throw Error(OZTT_EINVAL, "transpose: too large");
+    transpose_kernel<<<dim3((unsigned)((n + 31) / 32), (unsigned)((k + 31) / 32)), dim3(32, 8), 0, st>>>(b, k, n, ldb,
+                                                                                                      bt);
+    OZTT_CUDA(cudaGetLastError());
 }
 
 void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
