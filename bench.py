@@ -620,6 +620,7 @@ def run_single(args) -> None:
                                          "times the N GPUs"},
               "stage_ms": {"scale_rows": stage_ms[0], "scale_cols": stage_ms[1], "split_rows": stage_ms[2],
                            "split_cols": stage_ms[3], "residue_gemm": stage_ms[4], "recon": stage_ms[5]},
+              "stages": "scale_cols = B transposed on the device and its rows scaled; split_cols = B^T's rows split",
               "roofline": {"bound": "tensor", "kernel": "residue_gemm_kernel<1> (tcgen05 kind::i8)",
                            "achieved": gemm_tops, "peak": int8_peak, "unit": "TOP/s (int8)",
                            "frac": gemm_tops / int8_peak, "frac_of_burst": gemm_tops / int8_burst,
