@@ -105,15 +105,6 @@ public:
     // or for rows r0 .. r1-1 of A, whole rows (bands in any order, together covering every row), after b_done
     void a_rows(const double* a, uint64_t r0, uint64_t r1);
     void a_done(const double* a);
-    // B's finished parts on the device, valid on st after b_done: the magnitude patterns of its column
-    // maxima, its scaled column sums of squares, its scale (one double) and the sketch y (8 x k doubles)
-    struct BParts {
-        const unsigned long long* col_max;
-        const double* col_sumsq;
-        const double* rgB;
-        const double* y;
-    };
-    BParts b_parts() const;
     // row_max / col_max, when given, receive the magnitude patterns of A's row and B's column maxima;
     // row_sumsq / col_sumsq the scaled squared norms of A's rows and B's columns; rg the scales of A and B
     PolicyStats collect(std::vector<uint64_t>* row_max = nullptr, std::vector<uint64_t>* col_max = nullptr,

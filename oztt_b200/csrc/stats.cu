@@ -445,8 +445,6 @@ __global__ void __launch_bounds__(1024) pow2_scale_kernel(const unsigned long lo
     }
 }
 
-double pattern_to_double(unsigned long long u) { return ext80::double_of(u); }
-
 // The 8 Gaussian vectors of length N from mt19937(12345), in the reference's draw order, kept for the
 // last few N of the process (drawing them costs milliseconds at N = 16384).
 std::shared_ptr<const std::vector<double>> policy_vectors(uint32_t N) {
@@ -640,10 +638,6 @@ void PolicyStatsRun::a_rows(const double* a, uint64_t r0, uint64_t r1) {
     OZTT_CUDA(cudaGetLastError());
 }
 
-PolicyStatsRun::BParts PolicyStatsRun::b_parts() const {
-    return {bufs_->cmax.as<unsigned long long>(), bufs_->s2c.as<double>(), bufs_->rg.as<double>() + 1,
-            bufs_->dy.as<double>()};
-}
 
 void PolicyStatsRun::a_done(const double* a) {
     double* rgA = bufs_->rg.as<double>();
