@@ -77,7 +77,9 @@ def build_library(force: bool = False) -> Path:
             _run([CXX, *CXX_FLAGS, *CXX_FLAGS_BY_SOURCE.get(src, []), "-c", str(s), "-o", str(o)])
         objs.append(o)
     if force or _stale(LIB, objs):
-        _run([NVCC, *ARCH, "-shared", "-ccbin", CXX, "-o", str(LIB), *map(str, objs), "-lpthread"])
+        # every symbol resolved at link time: a missing definition fails the build, not the first load
+        _run([NVCC, *ARCH, "-shared", "-ccbin", CXX, "-Xlinker", "--no-undefined", "-o", str(LIB), *map(str, objs),
+              "-lpthread"])
     return LIB
 
 

@@ -41,9 +41,12 @@ struct ReconConst {
     uint32_t pm_s[kMaxPairs], pm_t[kMaxPairs];  // the multipliers of k_t and k_s: m_s and m_t (m_s = 0 alone)
     uint32_t pm_st[kMaxPairs];                   // m_s m_t (m_s alone)
     double Qp[kMaxPairs][kPairLimbs];
-    // for the finish on FP64 limbs: 2^(32 l) / M (rounded), and M's 32-bit words as doubles (exact)
-    double Rl[kPairLimbs], Ml[kPairLimbs];
+    // for q in the finish of the limb sums: 2^(32 l) / M (rounded)
+    double Rl[kPairLimbs];
 };
+
+template <int NW>
+__device__ __forceinline__ double round_scaled(uint32_t (&y)[NW], int32_t g, const ReconConst& rc);
 
 // Finishes one element from its column sums acc (X = sum_w acc[w] 2^(32w)).
 template <int NW>
@@ -71,6 +74,13 @@ __device__ __forceinline__ double crt_finish(const uint64_t (&acc)[NW], int32_t 
         y[w] = (uint32_t)d;
         br = d >> 32;
     }
+    return round_scaled<NW>(y, g, rc);
+}
+
+// C' * 2^(g - 2b) rounded to nearest even, from C' in two's complement in NW words (|C'| < 2^(32 NW - 1)):
+// below 2^-1022 -> +-0, as pack_f64 of the reference flushes, above the range -> +-inf.
+template <int NW>
+__device__ __forceinline__ double round_scaled(uint32_t (&y)[NW], int32_t g, const ReconConst& rc) {
     const bool neg = (y[NW - 1] >> 31) != 0;
     if (neg) {
         uint32_t c = 1;
@@ -81,20 +91,25 @@ __device__ __forceinline__ double crt_finish(const uint64_t (&acc)[NW], int32_t 
             c = (uint32_t)(t >> 32);
         }
     }
+    // the top nonzero word w0 = y[hw], the two below it and whether any word under those is nonzero: one
+    // pass upwards with a window of the last two words (constant indices only, so y stays in registers)
     int hw = -1;
-#pragma unroll
-    for (int w = 0; w < NW; ++w)
-        if (y[w]) hw = w;
-    if (hw < 0) return 0.0;
-    uint32_t w0 = 0, w1 = 0, w2 = 0;
-    bool sticky = false;
+    uint32_t w0 = 0, w1 = 0, w2 = 0, a = 0, b = 0;
+    bool sticky = false, below = false;
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
-        if (w == hw) w0 = y[w];
-        if (w == hw - 1) w1 = y[w];
-        if (w == hw - 2) w2 = y[w];
-        if (w < hw - 2 && y[w]) sticky = true;
+        if (y[w]) {
+            hw = w;
+            w0 = y[w];
+            w1 = a;
+            w2 = b;
+            sticky = below;
+        }
+        below = below || b != 0u;
+        b = a;
+        a = y[w];
     }
+    if (hw < 0) return 0.0;
     const int lz = __clz(w0);
     const uint64_t top = ((uint64_t)w0 << 32) | w1;
     const uint64_t top64 = lz ? ((top << lz) | (w2 >> (32 - lz))) : top;
@@ -113,85 +128,34 @@ __device__ __forceinline__ double crt_finish(const uint64_t (&acc)[NW], int32_t 
     return neg ? -r : r;
 }
 
-// Finishes one element from its limb sums on the FP64 pipe: X' = sum_l lim[l] 2^(32 l) (exact integers
-// below 2^52, X' < 13 M), the same value as crt_finish gives, bit for bit.
-//   q    = rint(sum_l lim[l] * fl(2^(32 l)/M)): within 2^-45 of X'/M, which the window margin keeps
-//          2^-31.4 from a half-integer, so q = round(X'/M);
-//   c[l] = lim[l] - q M_l (M's 32-bit words; exact, |c| < 2^53), C' = sum_l c[l] 2^(32 l), |C'| <= M/2;
-//   the limbs carried into balanced digits |c[l]| <= 2^31 (each step exact), so the top nonzero digit
-//   T carries the sign and C' = 2^(32(T-2)) (a 2^64 + b 2^32 + c2 + R) with |R| < 1/2 + 2^-32;
-//   two TwoSums give t + f = a 2^64 + b 2^32 + c2 exactly, t = RN(that), f an integer; R changes the
-//   rounding only when f is exactly half the spacing next to t on its side (|t| >= 2^62 when a != 0, so the
-//   spacing is at least 2^10, and below that a, b, c2 hold C' entirely), and then only by its sign;
-//   the result is scaled by 2^(32(T-2) + g - 2b) in the exponent field, below 2^-1022 flushed to +-0 and
-//   above the range to +-inf, as crt_finish.
+// Finishes one element from its limb sums. Each limb was accumulated on top of 2^52: lim[l] = 2^52 + L_l
+// with L_l < 2^52 an exact integer, so the low 52 bits of its pattern are L_l, and X' = sum_l L_l 2^(32 l)
+// (X' < P M, P pairs).
+//   q  = rint(sum_l L_l * fl(2^(32 l)/M)) over the limbs l >= L-3 (as doubles, L_l = lim[l] - 2^52 exactly):
+//        the limbs below add less than 2^52 2^(32(L-4)) / 2^(32(L-1)) = 2^-44 to X'/M (M >= 2^(32(L-1))) and
+//        the rounding errors are below 2^-45, while the window margin keeps X'/M 2^-31.4 from a half-integer,
+//        so q = round(X'/M) (at most P, taken from the low word of q + 1.5 2^52);
+//   C' = X' - q M in L 32-bit words, two's complement: every limb difference L_l - q M_l plus the carry is
+//        below 2^53 in magnitude, and |C'| <= M/2 < 2^(32 L - 1), so the words modulo 2^(32 L) hold C';
+//   then the rounding of crt_finish (round_scaled): the same result bit for bit.
 template <int NL, int L>
-__device__ __forceinline__ double crt_finish_limbs(const double (&lim)[NL], int32_t g, const ReconConst& rc) {
-    constexpr double magic = 6755399441055744.0;  // 1.5 * 2^52: x + magic - magic = rint(x) for |x| < 2^51
-    constexpr double two32 = 4294967296.0, inv32 = 2.3283064365386963e-10;
+__device__ __forceinline__ double crt_finish_biased(const double (&lim)[NL], int32_t g, const ReconConst& rc) {
+    constexpr double two52 = 4503599627370496.0, magic = 6755399441055744.0;  // 2^52, 1.5 * 2^52
+    constexpr int LQ = L > 3 ? L - 3 : 0;
     double xm = 0.0;
 #pragma unroll
-    for (int l = NL - 1; l >= 0; --l) xm = __fma_rn(lim[l], rc.Rl[l], xm);
-    const double q = __dsub_rn(__dadd_rn(xm, magic), magic);
-    double c[L];
+    for (int l = NL - 1; l >= LQ; --l) xm = __fma_rn(__dsub_rn(lim[l], two52), rc.Rl[l], xm);
+    const uint32_t q = (uint32_t)__double2loint(__dadd_rn(xm, magic));
+    uint32_t y[L];
+    int64_t cr = 0;
 #pragma unroll
-    for (int l = 0; l < L; ++l) c[l] = __fma_rn(-q, rc.Ml[l], l < NL ? lim[l < NL ? l : 0] : 0.0);
-#pragma unroll
-    for (int l = 0; l + 1 < L; ++l) {
-        const double t = __dsub_rn(__fma_rn(c[l], inv32, magic), magic);
-        c[l] = __fma_rn(-t, two32, c[l]);
-        c[l + 1] = __dadd_rn(c[l + 1], t);
+    for (int l = 0; l < L; ++l) {
+        int64_t v = cr - (int64_t)((uint64_t)q * rc.M[l]);
+        if (l < NL) v += (int64_t)((uint64_t)__double_as_longlong(lim[l < NL ? l : 0]) & 0xFFFFFFFFFFFFFull);
+        y[l] = (uint32_t)v;
+        cr = v >> 32;
     }
-    // the top nonzero digit a = c[T], the next two, and the sign of what lies below them
-    double a = 0.0, b = 0.0, c2 = 0.0, sR = 0.0;
-    int T = -1;
-#pragma unroll
-    for (int l = L - 1; l >= 0; --l) {
-        const bool nz = c[l] != 0.0;
-        if (T < 0) {
-            if (nz) {
-                T = l;
-                a = c[l];
-            }
-        } else if (l == T - 1) {
-            b = c[l];
-        } else if (l == T - 2) {
-            c2 = c[l];
-        } else if (sR == 0.0 && nz) {
-            sR = c[l] > 0.0 ? 1.0 : -1.0;
-        }
-    }
-    if (T < 0) return 0.0;
-    // t + f = a 2^64 + b 2^32 + c2 exactly (in units of 2^(32(T-2)))
-    const double ah = __dmul_rn(a, two32);
-    const double s = __dadd_rn(ah, b);
-    const double bb = __dsub_rn(s, ah);
-    const double e = __dadd_rn(__dsub_rn(ah, __dsub_rn(s, bb)), __dsub_rn(b, bb));
-    const double sh32 = __dmul_rn(s, two32);
-    const double l2 = __fma_rn(e, two32, c2);  // exact: |e| <= 2^10
-    const double t = __dadd_rn(sh32, l2);
-    const double tt = __dsub_rn(t, sh32);
-    const double f = __dadd_rn(__dsub_rn(sh32, __dsub_rn(t, tt)), __dsub_rn(l2, tt));
-    const bool negt = t < 0.0;
-    long long mag = __double_as_longlong(t) & 0x7FFFFFFFFFFFFFFFll;
-    const int E = (int)(mag >> 52);
-    const double fa = negt ? -f : f;  // f away from zero when positive
-    if (fa != 0.0 && sR != 0.0) {
-        // spacing next to |t| on f's side: the ulp, or half of it below a power of two
-        const double ulp = __longlong_as_double((long long)(E - 52) << 52);  // |t| >= 2^62 here: E - 52 >= 1
-        const double sp = (fa < 0.0 && (mag & 0xFFFFFFFFFFFFFll) == 0) ? 0.5 * ulp : ulp;
-        if (fabs(f) == 0.5 * sp && (negt ? -sR : sR) * fa > 0.0) mag += fa > 0.0 ? 1 : -1;
-    }
-    const int sh = 32 * (T - 2) + g - rc.two_b;
-    const int Ef = (int)(mag >> 52) - 1023 + sh;
-    double r;
-    if (Ef < -1022)
-        r = 0.0;
-    else if (Ef > 1023)
-        r = __longlong_as_double(0x7FF0000000000000ll);
-    else
-        r = __longlong_as_double(mag + ((long long)sh << 52));
-    return negt ? -r : r;
+    return round_scaled<L>(y, g, rc);
 }
 
 // Four consecutive digits of one plane in one load (uint8 digits of the INT8 path, uint16 digits of
@@ -255,10 +219,10 @@ __global__ void __launch_bounds__(256) recon_kernel(const D* __restrict__ kp, ui
 // k_s (M/m_s) + k_t (M/m_t) = (k_s m_t + k_t m_s) (M/(m_s m_t)), and only X mod M matters (q is taken from
 // X itself), so u = (k_s m_t + k_t m_s) mod (m_s m_t) < 2^16 -- one integer, formed on the integer pipe, against
 // one multiplier: the pairs halve the FP64 work. The sum X' = sum_p u_p M/(m_s m_t) < (S/2) M is X plus a
-// multiple of M. M/(m_s m_t) is held in NL 32-bit limbs; each limb sum, < 12 * 2^16 * 2^32 < 2^52, is exact
-// in binary64 (every fused multiply-add of integers below 2^53 whose sum stays below 2^53 is exact). The
-// limbs, 32 bits apart, then go through the finish on the FP64 pipe (crt_finish_limbs); L is the number of
-// M's 32-bit words.
+// multiple of M. M/(m_s m_t) is held in NL 32-bit limbs; each limb sum starts at 2^52 and stays below
+// 2^52 + 12 * 2^16 * 2^32 <= 2^53, exact in binary64 (every fused multiply-add of integers below 2^53 whose sum
+// stays below 2^53 is exact), so the sum itself is the low 52 bits of the limb's pattern. The limbs, 32 bits
+// apart, then go through the integer finish (crt_finish_biased); L is the number of M's 32-bit words.
 template <int NL, int L>
 __global__ void __launch_bounds__(256) recon_pair_kernel(const uint8_t* __restrict__ kp, uint64_t mp, uint64_t np,
                                                          const int32_t* __restrict__ dA,
@@ -279,7 +243,7 @@ __global__ void __launch_bounds__(256) recon_pair_kernel(const uint8_t* __restri
 #pragma unroll
         for (int e = 0; e < 4; ++e)
 #pragma unroll
-            for (int l = 0; l < NL; ++l) lim[e][l] = 0.0;
+            for (int l = 0; l < NL; ++l) lim[e][l] = two52;
 #pragma unroll
         for (int p = 0; p < kMaxPairs; ++p) {
             if ((uint32_t)p >= rc.P) break;
@@ -301,7 +265,7 @@ __global__ void __launch_bounds__(256) recon_pair_kernel(const uint8_t* __restri
         for (int e = 0; e < 4; ++e) {
             if (j0 + e < n) {
                 const int32_t g = rc.sh2 - (da + __ldg(dB + j0 + e));
-                crow[e] = crt_finish_limbs<NL, L>(lim[e], g, rc);
+                crow[e] = crt_finish_biased<NL, L>(lim[e], g, rc);
             }
         }
     }
@@ -393,7 +357,6 @@ static ReconConst recon_const(const oztt_ii_plan& p, int& nw, int& nl) {
         for (int w = 7; w >= 0; --w) Mld = Mld * 4294967296.0L + (long double)M.w[w];
         for (int l = 0; l < kPairLimbs; ++l) {
             rc.Rl[l] = (double)(ldexpl(1.0L, 32 * l) / Mld);
-            rc.Ml[l] = (double)M.w[l];
         }
     }
     return rc;
