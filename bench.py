@@ -713,11 +713,11 @@ def run_single(args) -> None:
                                                  for key, v in phases.items()},
                          "h2d_bytes_per_step": 8 * (m * k + k * n), "d2h_bytes_per_step": 8 * m * n,
                          "path": "ozTTgemm::Context::gemm via oztt_gemm: pinned H2D in the order B's first column block, A's "
-                                 "first 9/16 of rows, B's other column blocks, the rest of A; the pipeline on a first plan estimated from A's first "
-                                 "part and B's first block (A's first part times each block of B as it lands, then each "
-                                 "later band of A); the host's value checks meanwhile, then each band of C read back as "
-                                 "it finishes; the reference's plan from bounds of the statistics measured as the "
-                                 "operands landed (pipeline run again if it differs)"}
+                                 "first half of rows, B's next four column blocks, the rest of A, B's last three blocks; the "
+                                 "pipeline on a first plan estimated from A's first half and B's first block (each piece "
+                                 "times everything already there as it lands); the host's value checks meanwhile, then "
+                                 "each piece of C read back as it finishes; the reference's plan from bounds of the "
+                                 "statistics measured as the operands landed (pipeline run again if it differs)"}
     # ---- CPU baseline (rank 0 at N=1) ------------------------------------------------------------------
     if not args.no_cpu_baseline:
         result["cpu_baseline"] = time_cpu_dot2(a, b, n, k, target_s=12.0)

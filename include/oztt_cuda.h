@@ -220,7 +220,7 @@ int oztt_ii_int8_run_device_timed(int device_id, const double* a, const double* 
  *   7 when the first plan was made, 8 1 if the complete statistics gave another plan, 9 1 if the bounds of
  *   the statistics left a decision open so that the exact sums were computed, 10 1 if C was read back as
  *   its pieces finished (before the plan was confirmed); the device timeline in ms from the first copy:
- *   11 A's first part (9/16 of its rows) done against every block of B, 12 the last reconstruction, 13 the end of the
+ *   11 A's first part (half of its rows) done against B's first blocks, 12 the last reconstruction, 13 the end of the
  *   read-back of C, 14 the last band's bounded statistics; 15 when the host's value checks were ready
  *   (ms from the call).
  * Zeros before the first such call. */

@@ -213,6 +213,7 @@ _SIGNATURES = {
     "oztt_test_certified_plan": [_P, _U64, _U64, _U64, _P, ctypes.c_double, ctypes.c_double, ctypes.c_double,
                                  ctypes.c_uint32, _I32, ctypes.POINTER(IIPlan), ctypes.POINTER(_I32), _P, _ERR, _SZ],
     "oztt_test_bounded_nb": [_P, _U64, _U64, ctypes.c_double, _P, _ERR, _SZ],
+    "oztt_test_band_certify": [_P, _U64, _U64, _P, _P, _P, _P, _P, _ERR, _SZ],
 }
 
 _RESTYPES = {"oztt_test_scheme1_kblock": None, "oztt_format_name": ctypes.c_char_p, "oztt_policy_vectors": None, "oztt_test_udiv_small": ctypes.c_uint32, "oztt_test_ext80_dot": ctypes.c_double, "oztt_ii_padded_dims": None, "oztt_eval_inputs": None,

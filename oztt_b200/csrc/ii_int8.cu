@@ -30,11 +30,13 @@ void launch_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, in
 void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
                        uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax, cudaStream_t st);
 void launch_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
-                       const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st);
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st,
+                       uint64_t plane_rows = 0);
 void launch_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
                        const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st,
                        uint64_t plane_rows = 0);
-void launch_transpose(const double* b, uint64_t k, uint64_t n, uint64_t ldb, double* bt, cudaStream_t st);
+void launch_transpose_scale(const double* b, uint64_t k, uint64_t n, uint64_t ldb, double* bt, int32_t shift,
+                            int32_t* delta, uint32_t* flags, unsigned long long* colmax, cudaStream_t st);
 void launch_residue_gemm(const int8_t* ap, const int8_t* bp, uint64_t mp, uint64_t np, uint64_t kp,
                          const oztt_ii_plan& p, int mode, void* out, int* err_word, cudaStream_t st,
                          uint64_t a_plane_rows = 0, uint64_t b_plane_rows = 0);
@@ -98,18 +100,19 @@ void run_ii_int8_device(const double* a, const double* b, double* c, uint64_t m,
     check_plan(p);
     const uint64_t S = (uint64_t)p.S;
     const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
-    DevBuf dA(st, mp * 4), dB(st, np * 4), words(st, 16), bt(st, n * k * 8);
+    DevBuf dA(st, mp * 4), dB(st, np * 4), words(st, 16), bt(st, n * k * 8), colmax(st, n * 8);
     DevBuf ra(st, S * mp * kp), rb(st, S * np * kp), kpl(st, S * mp * np);
     OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
     Pipeline pl;
     pl.add(kScale, kHead, 0, [&] { launch_scale_rows(a, m, k, k, p.shift, dA.as<int32_t>(), nullptr, flags, st); });
-    // B transposed once (an HBM-bound copy), then scaled and split by rows: its columns are B^T's rows, with
-    // the same maxima, exponent deltas, flags and residue planes [S][np][kp] as the column kernels give
+    // B transposed once (an HBM-bound copy that also takes its column maxima), then split by rows: its columns
+    // are B^T's rows, with the same maxima, exponent deltas, flags and residue planes [S][np][kp] as the column
+    // kernels give
     pl.add(kScale, kHead, 1, [&] {
-        launch_transpose(b, k, n, n, bt.as<double>(), st);
-        launch_scale_rows(bt.as<double>(), n, k, k, p.shift, dB.as<int32_t>(), nullptr, flags, st);
+        launch_transpose_scale(b, k, n, n, bt.as<double>(), p.shift, dB.as<int32_t>(), flags,
+                               colmax.as<unsigned long long>(), st);
     });
     pl.add(kSlice, kHead, 2, [&] { launch_split_rows(a, m, k, k, dA.as<int32_t>(), p, ra.as<int8_t>(), mp, kp, st); });
     pl.add(kSlice, kHead, 3,
@@ -127,6 +130,7 @@ void run_ii_int8_device(const double* a, const double* b, double* c, uint64_t m,
     pl.writes(dA.p, mp * 4);
     pl.writes(dB.p, np * 4);
     pl.writes(bt.p, n * k * 8);
+    pl.writes(colmax.p, n * 8);
     pl.writes(ra.p, S * mp * kp);
     pl.writes(rb.p, S * np * kp);
     pl.writes(kpl.p, S * mp * np);
@@ -298,17 +302,18 @@ bool overlaps(const void* p, uint64_t pbytes, const void* q, uint64_t qbytes) {
 }
 
 // Context::gemm from host buffers, computing while the operands upload. The upload order is B's first block
-// of columns, A's first part (9/16 of its rows, bands of 1024), B's seven other blocks, then the rest of A.
-// The precision decision depends on the statistics of the whole A and B, so the pipeline starts on a first
-// plan made from an estimate: A's first part and B's first block, each standing for its matrix (the decision
-// depends on the size-free ratio (TA nB + TB nA) / 12 nC, which such parts estimate closely), measured as
-// they land. On that plan A's first part is split once and multiplied by each block of B (the first one at
-// once, the others as they land); then each later band of A by the whole B as it lands. The value checks
-// need the maxima of every row of A and column of B: the device measures A's first part for the first plan,
+// of columns (of eight), A's first half (bands of 1024 rows), B's next four blocks, the rest of A, then B's
+// last three blocks. The precision decision depends on the statistics of the whole A and B, so the pipeline
+// starts on a first plan made from an estimate: A's first half and B's first block, each standing for its
+// matrix (the decision depends on the size-free ratio (TA nB + TB nA) / 12 nC, which such parts estimate
+// closely), measured as they land. On that plan A's first half is split once and multiplied by each of B's
+// first five blocks (the first one at once, the others as they land); each later band of A is split and
+// multiplied by those five blocks as it lands; each of B's last blocks by the whole A. The value checks
+// need the maxima of every row of A and column of B: the device measures A's first half for the first plan,
 // the host's threads measure the rest of A and all of B from the caller's buffers meanwhile. Once every value
-// is checked, the pieces of C (A's first part against each block of B, then the bands) are read back as they
-// finish -- when that cannot change the outcome of the call: no plan for these dimensions can fail, and C
-// does not overlap A or B. When A has landed, the reference's plan is decided from bounds of its statistics
+// is checked, the pieces of C (a block of rows against a block of columns) are read back as they finish --
+// when that cannot change the outcome of the call: no plan for these dimensions can fail, and C does not
+// overlap A or B. When A has landed, the reference's plan is decided from bounds of its statistics
 // measured as the blocks and bands landed (only a decision that lies within the bounds needs the exact
 // long-double sums). If it equals the first plan, C is its result; otherwise the pipeline runs again with it
 // and C is read back again. An invalid input is reported before anything is written to C, as the front end
@@ -322,15 +327,21 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     cudaStream_t st = call.work();
     const uint64_t mp = round_up(m, 128), np = round_up(n, 256), kp = round_up(k, 128);
     const uint64_t bm = 1024;
-    // A's first part, whole bands: 9/16 of A. Each block of B then costs about as much device time (the
-    // first part's GEMM against it) as the next block takes to arrive, so the B phase stays upload-bound
-    // while as little as possible of A is left for after it.
-    const uint64_t pre = std::min(round_up(m * 9 / 16, bm), m);
+    // The upload order: B's first block, A's first half (whole bands), B's next blocks up to 5/8 of B, the
+    // rest of A, B's last blocks. The first plan waits for A's first half; then each piece that lands brings
+    // its products with everything already there, and the order keeps that work close to the rate at which
+    // the pieces arrive: the first half of A against each block of B (about 0.8 of a block's upload time at
+    // 16384^3), each later band against 5/8 of B (0.9 of a band's), each last block against the whole A
+    // (1.5 of a block's, the excess left for the end), so that the device is idle little after the first
+    // plan and the last work is short. (9/16 of A first and all of B before the rest of A: about 3 ms more.)
+    const uint64_t pre = std::min(round_up(m / 2, bm), m);
     const uint64_t pre_bands = (pre + bm - 1) / bm;
     const uint64_t nb = round_up((n + 7) / 8, 256);  // B's blocks of columns
+    const uint64_t nblocks = (n + nb - 1) / nb;
+    const uint64_t mid_blocks = nblocks / 2;         // B's blocks after the first one, before the rest of A
     HostMaxima host(a, b, m, n, k, pre);
     std::vector<cudaEvent_t> b_landed;
-    const std::vector<cudaEvent_t> landed = call.upload_prefix_first(pre, bm, nb, b_landed);
+    const std::vector<cudaEvent_t> landed = call.upload_prefix_first(pre, bm, nb, mid_blocks, m - pre, b_landed);
     // the first plan, from A's first part and B's first block
     bool estimated = false;
     std::vector<uint64_t> pre_max;
@@ -347,7 +358,7 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
-    std::unique_ptr<DevBuf> rb, ra, kpl;
+    std::unique_ptr<DevBuf> rb, ra, kpl, bt;
     const auto buffers = [&](const oztt_ii_plan& q, uint64_t a_rows) {
         const uint64_t S = (uint64_t)q.S;
         rb = std::make_unique<DevBuf>(st, S * np * kp);
@@ -364,35 +375,58 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
                      n, st);
         call.band_done(r0, rows);
     };
-    // on the first plan, following the upload: A's first part against each block of B, then the later bands
+    // on the first plan, following the upload: every piece that lands is split and multiplied by everything
+    // already split (A's planes kept whole, [S][mp][kp]): A's first half, then each block of B against the
+    // rows there, each band of A against the columns there
     const auto following = [&](const oztt_ii_plan& q) {
-        buffers(q, pre);
-        OZTT_CUDA(cudaStreamWaitEvent(st, landed[pre_bands - 1], 0));
-        launch_scale_rows(da, pre, k, k, q.shift, dA.as<int32_t>(), nullptr, flags, st);
-        launch_split_rows(da, pre, k, k, dA.as<int32_t>(), q, ra->as<int8_t>(), pre, kp, st);
-        for (uint64_t j = 0, c0 = 0; c0 < n; ++j, c0 += nb) {
-            const uint64_t cols_p = std::min(nb, np - c0), cols = std::min(n, c0 + cols_p) - c0;
+        buffers(q, mp);
+        bt = std::make_unique<DevBuf>(st, std::min(nb, n) * k * 8);
+        uint64_t rows_done = 0, cols_done = 0;
+        // rows [r0, r0 + rows) of A (a multiple of 128 rows unless they end A): split into the whole planes
+        const auto a_rows = [&](uint64_t r0, uint64_t rows_p) {
+            const uint64_t rows = std::min(m, r0 + rows_p) - r0;
+            launch_scale_rows(da + r0 * k, rows, k, k, q.shift, dA.as<int32_t>() + r0, nullptr, flags, st);
+            launch_split_rows(da + r0 * k, rows, k, k, dA.as<int32_t>() + r0, q, ra->as<int8_t>() + r0 * kp, rows_p,
+                              kp, st, mp);
+            return rows;
+        };
+        // the product of rows [r0, r0 + rows) with columns [c0, c0 + cols), both split, and its read-back
+        const auto tile = [&](uint64_t r0, uint64_t rows, uint64_t c0, uint64_t cols) {
+            const uint64_t rows_p = std::min(round_up(rows, 128), mp - r0);
+            const uint64_t cols_p = std::min(round_up(cols, 256), np - c0);
+            launch_residue_gemm(ra->as<int8_t>() + r0 * kp, rb->as<int8_t>() + c0 * kp, rows_p, cols_p, kp, q, 1,
+                                kpl->p, gemm_err, st, mp, np);
+            launch_recon(kpl->as<uint8_t>(), rows_p, cols_p, dA.as<int32_t>() + r0, dB.as<int32_t>() + c0, q,
+                         dc + r0 * n + c0, rows, cols, n, st);
+            call.tile_done(r0, rows, c0, cols);  // read back as soon as it is written (2-D copy)
+        };
+        // block j of B against the rows there; chunk: rows per product once all of A is there, so that the
+        // read-back of one part overlaps the product of the next
+        // (B's block transposed into bt with its column maxima taken on the way, then split by rows)
+        const auto b_block = [&](uint64_t j, uint64_t chunk) {
+            const uint64_t c0 = j * nb, cols_p = std::min(nb, np - c0), cols = std::min(n, c0 + cols_p) - c0;
             OZTT_CUDA(cudaStreamWaitEvent(st, b_landed.at(j), 0));
-            launch_scale_cols(db + c0, k, cols, n, q.shift, dB.as<int32_t>() + c0, nullptr, flags,
-                              colmax.as<unsigned long long>() + c0, st);
-            launch_split_cols(db + c0, k, cols, n, dB.as<int32_t>() + c0, q, rb->as<int8_t>() + c0 * kp, cols_p, kp,
-                              st, np);
-            launch_residue_gemm(ra->as<int8_t>(), rb->as<int8_t>() + c0 * kp, pre, cols_p, kp, q, 1, kpl->p, gemm_err,
-                                st, 0, np);
-            launch_recon(kpl->as<uint8_t>(), pre, cols_p, dA.as<int32_t>(), dB.as<int32_t>() + c0, q, dc + c0, pre,
-                         cols, n, st);
-            call.tile_done(0, pre, c0, cols);  // read back as soon as it is written (2-D copy)
-        }
-        call.timeline(st, 0);
-        for (uint64_t i = pre_bands, r0 = pre; r0 < m; ++i, r0 += bm) {
+            launch_transpose_scale(db + c0, k, cols, n, bt->as<double>(), q.shift, dB.as<int32_t>() + c0, flags,
+                                   colmax.as<unsigned long long>() + c0, st);
+            launch_split_rows(bt->as<double>(), cols, k, k, dB.as<int32_t>() + c0, q, rb->as<int8_t>() + c0 * kp,
+                              cols_p, kp, st, np);
+            for (uint64_t r0 = 0; r0 < rows_done; r0 += chunk) tile(r0, std::min(chunk, rows_done - r0), c0, cols);
+            cols_done = c0 + cols;
+        };
+        // band i of A (h rows from r0) against the columns there
+        const auto a_band = [&](uint64_t i, uint64_t r0, uint64_t h) {
             OZTT_CUDA(cudaStreamWaitEvent(st, landed[i], 0));
-            if (r0 + bm >= m && m - r0 > bm / 2) {  // the last band in two halves: the last read-back is shorter
-                band(q, r0, bm / 2);
-                band(q, r0 + bm / 2, bm / 2);
-            } else {
-                band(q, r0);
-            }
-        }
+            const uint64_t rows = a_rows(r0, std::min(h, mp - r0));
+            if (cols_done) tile(r0, rows, 0, cols_done);
+            rows_done = r0 + rows;
+        };
+        OZTT_CUDA(cudaStreamWaitEvent(st, landed[pre_bands - 1], 0));
+        rows_done = a_rows(0, std::min(round_up(pre, 128), mp));
+        uint64_t j = 0;
+        for (; j <= mid_blocks && j < nblocks; ++j) b_block(j, rows_done);
+        call.timeline(st, 0);
+        for (uint64_t i = pre_bands, r0 = pre; r0 < m; ++i, r0 += bm) a_band(i, r0, bm);
+        for (; j < nblocks; ++j) b_block(j, j + 1 < nblocks ? 4 * bm : 2 * bm);
         call.timeline(st, 1);
     };
     // after everything has landed: the whole pipeline on a plan

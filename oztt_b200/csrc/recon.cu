@@ -91,32 +91,32 @@ __device__ __forceinline__ double round_scaled(uint32_t (&y)[NW], int32_t g, con
             c = (uint32_t)(t >> 32);
         }
     }
-    // the top nonzero word w0 = y[hw], the two below it and whether any word under those is nonzero: one
-    // pass upwards with a window of the last two words (constant indices only, so y stays in registers)
-    int hw = -1;
-    uint32_t w0 = 0, w1 = 0, w2 = 0, a = 0, b = 0;
+    // |C'| in 64-bit halves, low first; the top nonzero half t0, the one below it t1 and whether any half
+    // under those is nonzero, found in one upward pass (constant indices only, so the words stay in registers)
+    constexpr int NH = (NW + 1) / 2;
+    int hh = -1;
+    uint64_t t0 = 0, t1 = 0, a = 0;
     bool sticky = false, below = false;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) {
-        if (y[w]) {
-            hw = w;
-            w0 = y[w];
-            w1 = a;
-            w2 = b;
+    for (int i = 0; i < NH; ++i) {
+        const uint64_t h = ((uint64_t)(2 * i + 1 < NW ? y[2 * i + 1 < NW ? 2 * i + 1 : 0] : 0u) << 32) | y[2 * i];
+        if (h) {
+            hh = i;
+            t0 = h;
+            t1 = a;
             sticky = below;
         }
-        below = below || b != 0u;
-        b = a;
-        a = y[w];
+        below = below || a != 0;
+        a = h;
     }
-    if (hw < 0) return 0.0;
-    const int lz = __clz(w0);
-    const uint64_t top = ((uint64_t)w0 << 32) | w1;
-    const uint64_t top64 = lz ? ((top << lz) | (w2 >> (32 - lz))) : top;
-    const uint32_t rem = lz ? (w2 << lz) : w2;
-    sticky = sticky || rem != 0u;
+    if (hh < 0) return 0.0;
+    // the top 64 bits from the leading one, and a sticky bit for every bit under them (bit 0 is far below
+    // the rounding position, so setting it decides a tie without moving any other rounding)
+    const int lz = __clzll((long long)t0);
+    const uint64_t top64 = lz ? ((t0 << lz) | (t1 >> (64 - lz))) : t0;
+    sticky = sticky || (t1 << lz) != 0;
     const double v = __ull2double_rn(top64 | (sticky ? 1ull : 0ull));  // in [2^63, 2^64]
-    const int p = 32 * hw + 31 - lz;                                    // position of the leading bit
+    const int p = 64 * hh + 63 - lz;                                    // position of the leading bit
     const int lead = p + g - rc.two_b + (v == 18446744073709551616.0 ? 1 : 0);
     double r;
     if (lead < -1022)

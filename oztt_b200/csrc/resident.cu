@@ -32,7 +32,8 @@ void launch_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, in
 void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, int32_t shift, int32_t* delta,
                        uint16_t* bfmax, uint32_t* flags, unsigned long long* colmax, cudaStream_t st);
 void launch_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
-                       const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st);
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st,
+                       uint64_t plane_rows = 0);
 void launch_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,
                        const oztt_ii_plan& p, int8_t* planes, uint64_t np, uint64_t kp, cudaStream_t st,
                        uint64_t plane_rows = 0);

@@ -166,12 +166,14 @@ public:
     // counted from pipeline_start_ms (ms_since_start when it was issued)
     void finish(double pipeline_start_ms);
     // The upload of the INT8 path that computes while its operands land: B's first block of block_cols
-    // columns, A's first pre_rows rows in bands of band_rows, B's other blocks, then the rest of A in bands
-    // (B's first block first, so that the first plan's estimate follows A's bands as they land). Each block
-    // of B is measured as it lands and each band of A once B has landed (one fast pass each that bounds the
-    // reference's statistics, on a high-priority stream, so that it runs between the GEMM's launches).
-    // Returns the events that mark each band's arrival and fills b_landed with those of B's blocks.
+    // columns, A's first pre_rows rows in bands of band_rows, B's next mid_blocks blocks, A's next mid_rows
+    // rows, B's other blocks, then the rest of A in bands (B's first block first, so that the first plan's
+    // estimate follows A's bands as they land). Each block of B is measured as it lands and each band of A
+    // once B has landed (one fast pass each that bounds the reference's statistics, on a high-priority
+    // stream, so that it runs between the GEMM's launches). Returns the events that mark each band's arrival
+    // and fills b_landed with those of B's blocks.
     std::vector<cudaEvent_t> upload_prefix_first(uint64_t pre_rows, uint64_t band_rows, uint64_t block_cols,
+                                                 uint64_t mid_blocks, uint64_t mid_rows,
                                                  std::vector<cudaEvent_t>& b_landed);
     // After upload_prefix_first: the estimate of the statistics from A's first pre_rows rows and B's first
     // block (PrefixEstimate, measured as they landed); waits for it. ok is false when no estimate could be

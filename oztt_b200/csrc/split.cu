@@ -238,6 +238,15 @@ __device__ __forceinline__ f32x2 mod_round2(f32x2 d, f32x2 negm, f32x2 rinv, f32
     return fma2(rint2(mul2(d, rinv, nz)), negm, d);
 }
 
+// ModRound of an exact integer x for an odd m, with the product and the rounding to an integer in one fused
+// operation (x * fl(1/m) + 1.5*2^23, then - 1.5*2^23): x * fl(1/m) is within 1/(4m) of x/m, and x/m is at least
+// 1/(2m) from a half-integer when m is odd, so rounding once or twice gives the same quotient, and the
+// residue x - q m is exact. (The even modulus keeps mod_round2, whose two roundings decide its ties.)
+__device__ __forceinline__ f32x2 mod_round2_odd(f32x2 x, f32x2 negm, f32x2 rinv) {
+    const f32x2 mg = splat2(kRoundMagic);
+    return fma2(sub2(fma2(x, rinv, mg), mg), negm, x);
+}
+
 // Residues of A' from its digits (top first), the reference's chain; products of a reduced digit
 // and a weight, and the partial sums, are exact integers below 2^22.
 template <int ND>
@@ -320,7 +329,7 @@ __device__ __forceinline__ void store_residues_part(const f32x2 (&dg)[8][ND], co
                 f32x2 acc = t[e][NT];
 #pragma unroll
                 for (int j = 0; j < NT; ++j) acc = fma2(t[e][j], splat2(sc.w[j][s]), acc);
-                r[e] = mod_round2(acc, negm, ri, nz);
+                r[e] = mod_round2_odd(acc, negm, ri);
             }
         } else {
             const f32x2 c0 = splat2(sc.c[0][s]), c1 = splat2(sc.c[1][s]), c2 = splat2(sc.c[2][s]),
@@ -443,15 +452,16 @@ __device__ __forceinline__ void store_planes(const f32x2 (&dg)[8][ND], const Spl
         store_residues<ND, MODE == kTopSplit, ROWS>(dg, sc, dst, plane);
 }
 
-// A: one thread = 16 consecutive elements of one row. (ND = 3 with the top digit whole, the widths of the
+// A: one thread = 16 consecutive elements of one row; the planes are `plane` bytes apart (mp * kp, or more
+// for a band of the rows of taller planes). (ND = 3 with the top digit whole, the widths of the
 // usual plans: at most 85 registers, so that three blocks share an SM -- measured 2.78 against 3.08 ms at
 // 16384^2 x 17 moduli with two.)
 template <int ND, int MODE>
 __global__ void __launch_bounds__(256, (ND == 3 && MODE == kTopWhole) ? 3 : 1) split_rows_kernel(const double* __restrict__ a, uint64_t m, uint64_t k,
                                                          uint64_t lda, const int32_t* __restrict__ delta,
                                                          int8_t* __restrict__ planes, uint64_t mp, uint64_t kp,
-                                                         const SplitConst sc) {
-    const uint64_t chunks = kp >> 4, total = mp * chunks, plane = mp * kp;
+                                                         uint64_t plane, const SplitConst sc) {
+    const uint64_t chunks = kp >> 4, total = mp * chunks;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
          t += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t row = t / chunks, k0 = (t - row * chunks) << 4;
@@ -503,24 +513,48 @@ __global__ void __launch_bounds__(256) split_cols_kernel(const double* __restric
     }
 }
 
-// B transposed (bt[j][i] = b[i][j], k x n to n x k), through 32 x 32 tiles in shared memory: B's columns
-// then split as rows (split_rows_kernel), whose loads and stores are contiguous, instead of through the
-// column kernel's strided loads and scattered 16-byte stores. Blocks of 32 x 8 threads, 4 elements each.
-__global__ void __launch_bounds__(256) transpose_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
-                                                        uint64_t ldb, double* __restrict__ bt) {
+// B transposed (bt[j][i] = b[i][j], k x n to n x k) through 32 x 32 tiles in shared memory, so that B's columns
+// are split as rows (split_rows_kernel), whose loads and stores are contiguous, instead of through the column
+// kernel's strided loads and scattered 16-byte stores. The maxima of |B|'s columns (B^T's rows) are taken on
+// the way, so that B^T needs no separate pass for its scale (col_finish_kernel turns them into deltas and
+// flags, as scale_rows_kernel would). Blocks of 32 x 8 threads take 32 columns over kTransposeTiles tiles of
+// 32 rows, 4 elements per thread and tile; at the store a warp's lanes hold the
+// 32 rows of one column of a tile, four columns per warp, so each column's maximum is kept per lane across
+// the tiles, reduced across the warp once and given to one atomicMax per block (non-negative FP64 patterns
+// order like unsigned integers, NaN patterns above infinity, as in scale_rows_kernel).
+constexpr int kTransposeTiles = 8;
+__global__ void __launch_bounds__(256) transpose_max_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
+                                                            uint64_t ldb, double* __restrict__ bt,
+                                                            unsigned long long* __restrict__ colmax) {
     __shared__ double tile[32][33];
-    const uint64_t c0 = (uint64_t)blockIdx.x * 32, r0 = (uint64_t)blockIdx.y * 32;
+    constexpr uint64_t MASK = 0x7FFFFFFFFFFFFFFFull;
+    const uint64_t c0 = (uint64_t)blockIdx.x * 32;
     const int tx = threadIdx.x, ty = threadIdx.y;
+    uint64_t mx[4] = {0, 0, 0, 0};
+    for (int it = 0; it < kTransposeTiles; ++it) {
+        const uint64_t r0 = ((uint64_t)blockIdx.y * kTransposeTiles + it) * 32;
+        if (r0 >= k) break;  // the same for the whole block
+        if (it) __syncthreads();  // the previous tile read out before it is overwritten
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-        const uint64_t r = r0 + ty + j, c = c0 + tx;
-        tile[ty + j][tx] = (r < k && c < n) ? __ldg(b + r * ldb + c) : 0.0;
+        for (int j = 0; j < 32; j += 8) {
+            const uint64_t r = r0 + ty + j, c = c0 + tx;
+            tile[ty + j][tx] = (r < k && c < n) ? __ldg(b + r * ldb + c) : 0.0;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+            const uint64_t c = c0 + ty + j, r = r0 + tx;
+            const double v = tile[tx][ty + j];
+            mx[j >> 3] = mx64(mx[j >> 3], (uint64_t)__double_as_longlong(v) & MASK);
+            if (c < n && r < k) bt[c * k + r] = v;
+        }
     }
-    __syncthreads();
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-        const uint64_t c = c0 + ty + j, r = r0 + tx;
-        if (c < n && r < k) bt[c * k + r] = tile[tx][ty + j];
+    for (int j = 0; j < 4; ++j) {
+        uint64_t v = mx[j];
+        for (int o = 16; o; o >>= 1) v = mx64(v, (uint64_t)__shfl_xor_sync(0xffffffffu, (unsigned long long)v, o));
+        const uint64_t c = c0 + ty + 8 * j;
+        if (tx == 0 && v && c < n) atomicMax(colmax + c, (unsigned long long)v);
     }
 }
 
@@ -602,11 +636,21 @@ void launch_scale_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, in
     launch_scale_rows_mode(a, m, k, lda, shift, 1u, delta, bfmax, flags, st);
 }
 
-void launch_transpose(const double* b, uint64_t k, uint64_t n, uint64_t ldb, double* bt, cudaStream_t st) {
-    if (!k || !n) return;
-    if ((n + 31) / 32 > 0x7FFFFFFFull || (k + 31) / 32 > 65535) throw Error(OZTT_EINVAL, "transpose: too large");
-    transpose_kernel<<<dim3((unsigned)((n + 31) / 32), (unsigned)((k + 31) / 32)), dim3(32, 8), 0, st>>>(b, k, n, ldb,
-                                                                                                      bt);
+// B^T = B transposed into bt (n x k), and the exponent deltas and flags of B's columns (B^T's rows) from the
+// maxima taken on the way; colmax: n words of scratch.
+void launch_transpose_scale(const double* b, uint64_t k, uint64_t n, uint64_t ldb, double* bt, int32_t shift,
+                            int32_t* delta, uint32_t* flags, unsigned long long* colmax, cudaStream_t st) {
+    if (n == 0) return;
+    const uint64_t rows_per_block = 32ull * kTransposeTiles;
+    if ((n + 31) / 32 > 0x7FFFFFFFull || (k + rows_per_block - 1) / rows_per_block > 65535)
+        throw Error(OZTT_EINVAL, "transpose: too large");
+    OZTT_CUDA(cudaMemsetAsync(colmax, 0, n * sizeof(unsigned long long), st));
+    if (k > 0) {
+        transpose_max_kernel<<<dim3((unsigned)((n + 31) / 32), (unsigned)((k + rows_per_block - 1) / rows_per_block)),
+                               dim3(32, 8), 0, st>>>(b, k, n, ldb, bt, colmax);
+        OZTT_CUDA(cudaGetLastError());
+    }
+    col_finish_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(colmax, n, shift, 1u, delta, nullptr, flags);
     OZTT_CUDA(cudaGetLastError());
 }
 
@@ -617,15 +661,18 @@ void launch_scale_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, in
 
 template <int MODE>
 static void split_rows_nd(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta, int nd,
-                          const SplitConst& sc, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
+                          const SplitConst& sc, int8_t* planes, uint64_t mp, uint64_t kp, uint64_t plane_rows,
+                          cudaStream_t st) {
     if (mp % 16 || kp % 16) throw Error(OZTT_EINVAL, "split_rows: padded dimensions must be multiples of 16");
+    if (plane_rows < mp) throw Error(OZTT_EINVAL, "split_rows: band taller than its planes");
+    const uint64_t plane = plane_rows * kp;
     const uint64_t total = mp * (kp / 16);
     const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)device_sms() * 32);
     if (total == 0) return;
     switch (nd) {
-    case 3: split_rows_kernel<3, MODE><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
-    case 4: split_rows_kernel<4, MODE><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
-    case 5: split_rows_kernel<5, MODE><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, sc); break;
+    case 3: split_rows_kernel<3, MODE><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, plane, sc); break;
+    case 4: split_rows_kernel<4, MODE><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, plane, sc); break;
+    case 5: split_rows_kernel<5, MODE><<<blocks, 256, 0, st>>>(a, m, k, lda, delta, planes, mp, kp, plane, sc); break;
     default: throw Error(OZTT_EINVAL, "split: the number of digits must be 3, 4 or 5");
     }
     OZTT_CUDA(cudaGetLastError());
@@ -650,12 +697,16 @@ static void split_cols_nd(const double* b, uint64_t k, uint64_t n, uint64_t ldb,
     OZTT_CUDA(cudaGetLastError());
 }
 
+// plane_rows: when nonzero, planes points at row r0 of planes that are plane_rows tall (rows r0 .. r0+mp-1 of
+// taller planes: a band of A's rows, split as it lands).
 void launch_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
-                       const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
+                       const oztt_ii_plan& p, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st,
+                       uint64_t plane_rows) {
+    const uint64_t pr = plane_rows ? plane_rows : mp;
     if (residue_mode(p) == kTopWhole)
-        split_rows_nd<kTopWhole>(a, m, k, lda, delta, p.nd, split_const(p), planes, mp, kp, st);
+        split_rows_nd<kTopWhole>(a, m, k, lda, delta, p.nd, split_const(p), planes, mp, kp, pr, st);
     else
-        split_rows_nd<kTopSplit>(a, m, k, lda, delta, p.nd, split_const(p), planes, mp, kp, st);
+        split_rows_nd<kTopSplit>(a, m, k, lda, delta, p.nd, split_const(p), planes, mp, kp, pr, st);
 }
 
 // plane_rows: when nonzero, planes points at row c0 of planes that are plane_rows tall (columns c0 ..
@@ -684,7 +735,7 @@ static SplitConst digit_const(const oztt_digit_plan& fp) {
 // Digit planes of A ([nplane][mp][kp]) and of B transposed ([nplane][np][kp]).
 void launch_digit_split_rows(const double* a, uint64_t m, uint64_t k, uint64_t lda, const int32_t* delta,
                              const oztt_digit_plan& fp, int8_t* planes, uint64_t mp, uint64_t kp, cudaStream_t st) {
-    split_rows_nd<kDigits>(a, m, k, lda, delta, fp.base.nd, digit_const(fp), planes, mp, kp, st);
+    split_rows_nd<kDigits>(a, m, k, lda, delta, fp.base.nd, digit_const(fp), planes, mp, kp, mp, st);
 }
 
 void launch_digit_split_cols(const double* b, uint64_t k, uint64_t n, uint64_t ldb, const int32_t* delta,

@@ -205,25 +205,34 @@ __global__ void __launch_bounds__(128) sketch_kernel(const double* __restrict__ 
         out[l * ostride + r] = ext80::to_double(acc);
 }
 
-// Bounded statistics of rows of A (x: rows x k, row-major; a block of 256 threads per 2 rows, the threads
-// striding the columns, each column's sketch values loaded once for both rows), for deciding the plan
-// without the reference's sequential long-double sums: per row, into out[r*kCertW ..]:
+// Bounded statistics of rows of A (x: rows x k, row-major), for deciding the plan without the reference's
+// sequential long-double sums: per row, into out[r*kCertW ..]:
 //   [0]          the largest magnitude as its bit pattern (NaN and Inf patterns order above every number)
 //   [1]          sum x^2            [2 .. 9]   sum x * y_l            [10 .. 17]  sum |x * y_l|
 //   [18]         sum |x| * ew       (0 when ew is null)
-// all unscaled, in FP64 (in the threads', then the warps' order); the host turns them into bounds that
-// contain the reference's values. y: the 8 x k sketch y_l = B g_l (scaled), as the reference has it or as
+// all unscaled, in FP64 (in the lanes', then the warp's order); the host turns them into bounds that contain
+// the reference's values. y: the 8 x k sketch y_l = B g_l (scaled), as the reference has it or as
 // bcert_finish_kernel bounds it (then ew[j] bounds |y_l[j] - the reference's y_l[j]| over l). flags |= 1
 // when a nonzero element below 2^-383 makes the scaled squares leave the normal range (no bounds then).
+// A block of 8 warps takes 16 rows, two per warp, the lanes striding the columns; the sketch and ew go
+// through shared memory a chunk of kCertChunk columns at a time, so that each value is read from L2 once
+// per 16 rows and from shared memory once per 2 (the kernel is then bound by its 26 FP64 operations per
+// element, not by the reads of the sketch).
 constexpr int kCertW = 19;
-constexpr int kCertRows = 2;  // rows of A per block: each column's 8 sketch values are loaded once for both
+constexpr int kCertRowsPerWarp = 2, kCertWarps = 8, kCertRows = kCertRowsPerWarp * kCertWarps;
+constexpr int kCertChunk = 256;
 __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restrict__ x, uint64_t rows, uint64_t k,
                                                            const double* __restrict__ y,
                                                            const double* __restrict__ ew, double* __restrict__ out,
                                                            uint32_t* __restrict__ flags) {
-    constexpr int R = kCertRows, V = 2 + 2 * kVectors + 1;  // per row: s2, sl[8], al[8], se; then the maximum
-    const uint64_t r0 = (uint64_t)blockIdx.x * R;
-    const int nr = rows - r0 < (uint64_t)R ? (int)(rows - r0) : R;
+    // per row V = kCertW - 1 sums: s2, sl[8], al[8], se (slots 1 .. 18 of the row's output; slot 0 the maximum)
+    constexpr int R = kCertRowsPerWarp, V = 1 + 2 * kVectors + 1;
+    static_assert(V + 1 == kCertW, "the sums and the maximum fill a row of the output");
+    __shared__ double ys[kVectors][kCertChunk];
+    __shared__ double es[kCertChunk];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t r0 = ((uint64_t)blockIdx.x * kCertWarps + warp) * R;
+    const int nr = r0 >= rows ? 0 : (rows - r0 < (uint64_t)R ? (int)(rows - r0) : R);
     unsigned long long mx[R];
     double acc[R][V];
     bool tiny = false;
@@ -233,32 +242,40 @@ __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restr
 #pragma unroll
         for (int v = 0; v < V; ++v) acc[r][v] = 0.0;
     }
-    for (uint64_t j = threadIdx.x; j < k; j += blockDim.x) {
-        double yl[kVectors];
+    for (uint64_t j0 = 0; j0 < k; j0 += kCertChunk) {
+        const int cw = k - j0 < (uint64_t)kCertChunk ? (int)(k - j0) : kCertChunk;
+        __syncthreads();  // the previous chunk read by every warp
+        for (int i = threadIdx.x; i < kVectors * kCertChunk; i += blockDim.x) {
+            const int l = i / kCertChunk, j = i % kCertChunk;
+            ys[l][j] = j < cw ? __ldg(y + (uint64_t)l * k + j0 + j) : 0.0;
+        }
+        for (int j = threadIdx.x; j < kCertChunk; j += blockDim.x) es[j] = (ew && j < cw) ? __ldg(ew + j0 + j) : 0.0;
+        __syncthreads();
+        if (nr == 0) continue;
+        for (int j = lane; j < cw; j += 32) {
+            double yl[kVectors];
 #pragma unroll
-        for (int l = 0; l < kVectors; ++l) yl[l] = __ldg(y + (uint64_t)l * k + j);
-        const double e = ew ? __ldg(ew + j) : 0.0;
+            for (int l = 0; l < kVectors; ++l) yl[l] = ys[l][j];
+            const double e = es[j];
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-            if (r >= nr) break;
-            const double v = __ldg(x + (r0 + r) * k + j);
-            const unsigned long long pat = (unsigned long long)__double_as_longlong(v) & 0x7FFFFFFFFFFFFFFFull;
-            mx[r] = pat > mx[r] ? pat : mx[r];
-            tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);  // 0 < |v| < 2^-383
-            acc[r][0] = fma(v, v, acc[r][0]);
-            acc[r][V - 1] = fma(fabs(v), e, acc[r][V - 1]);
+            for (int r = 0; r < R; ++r) {
+                if (r >= nr) break;
+                const double v = __ldg(x + (r0 + r) * k + j0 + j);
+                const unsigned long long pat = (unsigned long long)__double_as_longlong(v) & 0x7FFFFFFFFFFFFFFFull;
+                mx[r] = pat > mx[r] ? pat : mx[r];
+                tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);  // 0 < |v| < 2^-383
+                acc[r][0] = fma(v, v, acc[r][0]);
+                acc[r][V - 1] = fma(fabs(v), e, acc[r][V - 1]);
 #pragma unroll
-            for (int l = 0; l < kVectors; ++l) {
-                const double t = v * yl[l];
-                acc[r][1 + l] += t;
-                acc[r][1 + kVectors + l] += fabs(t);
+                for (int l = 0; l < kVectors; ++l) {
+                    const double t = v * yl[l];
+                    acc[r][1 + l] += t;
+                    acc[r][1 + kVectors + l] += fabs(t);
+                }
             }
         }
     }
-    // the warps' sums, then the block's (any order: the bounds hold for every order of the k terms)
-    __shared__ double part[8][R][V];
-    __shared__ unsigned long long pmx[8][R];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // the lanes' sums (any order: the bounds hold for every order of the k terms)
 #pragma unroll
     for (int r = 0; r < R; ++r) {
 #pragma unroll
@@ -268,27 +285,17 @@ __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restr
 #pragma unroll
             for (int v = 0; v < V; ++v) acc[r][v] += __shfl_xor_sync(0xFFFFFFFFu, acc[r][v], o);
         }
-        if (lane == 0) {
-            pmx[warp][r] = mx[r];
-#pragma unroll
-            for (int v = 0; v < V; ++v) part[warp][r][v] = acc[r][v];
-        }
     }
     if (__any_sync(0xFFFFFFFFu, tiny) && lane == 0) atomicOr(flags, 1u);
-    __syncthreads();
-    const int nw = (int)(blockDim.x >> 5);
-    for (int i = threadIdx.x; i < nr * V; i += blockDim.x) {
-        const int r = i / V, v = i % V;
-        double sum = 0.0;
-        for (int w = 0; w < nw; ++w) sum += part[w][r][v];
+    // lane v < V writes sum v of each row into slot 1 + v, lane V the maximum into slot 0
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        if (r >= nr) break;
         double* o = out + (r0 + r) * kCertW;
-        // output layout: [1] s2, [2..9] sl, [10..17] al, [18] se
-        o[1 + v] = sum;
-    }
-    for (int r = threadIdx.x; r < nr; r += blockDim.x) {
-        unsigned long long m = 0;
-        for (int w = 0; w < nw; ++w) m = pmx[w][r] > m ? pmx[w][r] : m;
-        out[(r0 + r) * kCertW] = __longlong_as_double((long long)m);
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+            if (lane == v) o[1 + v] = acc[r][v];
+        if (lane == V) o[0] = __longlong_as_double((long long)mx[r]);
     }
 }
 
@@ -988,7 +995,7 @@ PolicyStats device_policy_stats(const double* a, const double* b, uint64_t m, ui
 
 }  // namespace oztt
 
-// Test hook: the certified decision from host copies of the bounded row statistics (m x 18, as
+// Test hook: the certified decision from host copies of the bounded row statistics (m x 19, as
 // band_certify_kernel writes them) and B's exact parts; bounds5 (NULL or 4 doubles) receives nA lo/hi and nC
 // lo/hi, *decided whether the bounds decided the plan (which is then in *plan).
 extern "C" int oztt_test_certified_plan(const double* cert, uint64_t m, uint64_t n, uint64_t k, const double* col_max,
@@ -1010,6 +1017,15 @@ extern "C" int oztt_test_certified_plan(const double* cert, uint64_t m, uint64_t
         const int rc = oztt::plan_ii_int8_certified(pb, m, n, k, max_moduli, reconstruction, *plan, msg, ok);
         if (rc != OZTT_OK) throw oztt::Error(rc, msg);
         *decided = ok ? 1 : 0;
+    });
+}
+
+// Test hook: band_certify_kernel on device rows x (rows x k), the device sketch y (8 x k) and ew (k, or NULL),
+// into the device rows out (rows x 19: the maximum's pattern, then the sums) and the device flag word.
+extern "C" int oztt_test_band_certify(const double* x, uint64_t rows, uint64_t k, const double* y, const double* ew,
+                                      double* out, uint32_t* flags, void* stream, char* err, size_t errlen) {
+    return oztt::guarded(err, errlen, [&] {
+        oztt::launch_band_certify(x, rows, k, y, ew, out, flags, reinterpret_cast<cudaStream_t>(stream));
     });
 }
 

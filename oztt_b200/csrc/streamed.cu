@@ -4,8 +4,9 @@
 // the INT8 and digit-format Scheme II paths.
 //
 //   copy-up stream   B, then A, in blocks of columns of about 64 MiB (2-D copies of all rows); for the
-//                    INT8 path that computes while its operands land (upload_prefix_first): A's first
-//                    half in bands of rows, B in blocks of columns, the rest of A in bands
+//                    INT8 path that computes while its operands land (upload_prefix_first): B's first
+//                    block of columns, A's first part in bands of rows, then further blocks of B and bands
+//                    of A
 //   work stream      the precision-policy statistics of each piece as it lands (PolicyStatsRun), then
 //                    the caller's pipeline, which marks each finished band of rows of C
 //   copy-down stream each finished band of C read back while the next is computed
@@ -182,6 +183,7 @@ PolicyStats StreamedCall::upload(std::vector<uint64_t>& row_max, std::vector<uin
 }
 
 std::vector<cudaEvent_t> StreamedCall::upload_prefix_first(uint64_t pre_rows, uint64_t band_rows, uint64_t block_cols,
+                                                           uint64_t mid_blocks, uint64_t mid_rows,
                                                            std::vector<cudaEvent_t>& b_landed) {
     const uint64_t N = round_up(n_, 64);  // the planners' padded width
     double* da = da_->as<double>();
@@ -233,11 +235,24 @@ std::vector<cudaEvent_t> StreamedCall::upload_prefix_first(uint64_t pre_rows, ui
         OZTT_CUDA(cudaStreamWaitEvent(est_, landed.back(), 0));
         est_run_->a_band(da, r0, std::min(rows, pre_rows - r0));
     }
-    for (uint64_t c0 = block_cols; c0 < n_; c0 += block_cols) b_block(c0);
+    // B's next blocks, A's next bands, B's other blocks, the rest of A
+    const uint64_t mid_end = std::min(m_, pre_rows + mid_rows);
+    uint64_t c0 = block_cols;
+    for (uint64_t j = 0; j < mid_blocks && c0 < n_; ++j, c0 += block_cols) b_block(c0);
+    uint64_t r0 = pre_rows;
+    for (; r0 < mid_end; r0 += band_rows) a_band(r0);
+    for (; c0 < n_; c0 += block_cols) b_block(c0);
     launch_bcert_finish(b_colmax(), n_, b_acc(), k_, bcert_error_factor(n_), b_rg(), b_y(), b_ew(), cert_);
-    for (uint64_t r0 = pre_rows; r0 < m_; r0 += band_rows) a_band(r0);
-    // the bands' bounded statistics need B's sketch: all of them after B, each after its band
-    for (uint64_t r0 = 0, i = 0; r0 < m_; r0 += band_rows, ++i) {
+    const uint64_t early_rows = r0, early_bands = landed.size();  // A's rows that landed before B's last block
+    for (; r0 < m_; r0 += band_rows) a_band(r0);
+    // the bands' bounded statistics need B's sketch: those that landed before B's last block in one pass (all
+    // the rows at once keep every SM busy), each later one after it lands
+    if (early_rows) {
+        OZTT_CUDA(cudaStreamWaitEvent(cert_, landed[early_bands - 1], 0));
+        launch_band_certify(da, early_rows, k_, b_y(), b_ew(), cert_buf_->as<double>(), cert_flags_->as<uint32_t>(),
+                            cert_);
+    }
+    for (uint64_t r0 = early_rows, i = early_bands; r0 < m_; r0 += band_rows, ++i) {
         const uint64_t rows = std::min(band_rows, m_ - r0);
         OZTT_CUDA(cudaStreamWaitEvent(cert_, landed[i], 0));
         launch_band_certify(da + r0 * k_, rows, k_, b_y(), b_ew(), cert_buf_->as<double>() + r0 * kCertWidth,

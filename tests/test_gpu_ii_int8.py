@@ -308,8 +308,8 @@ def test_device_run_matches_host_run(oztt, oracle, cuda):
 
 
 # ---- Context.gemm's streamed path: chunked upload, statistics as chunks land, banded read-back ----------
-# Sizes: 4096 rows and more compute while their operands upload (A's first 9/16, B in blocks of about n/8
-# columns, the rest of A in bands of 1024 rows): (9000, 256, 256) one block of B, a ragged last band;
+# Sizes: 4096 rows and more compute while their operands upload (A's first half, B in blocks of about n/8
+# columns, the rest of A in bands of 1024 rows, B's last blocks): (9000, 256, 256) one block of B, a ragged last band;
 # (4500, 4608, 2048) six blocks of B (the last one ragged). Below 4096 rows B and A go up in blocks of
 # max(512, 64 MiB / 8k) and max(512, 64 MiB / 8m) columns, then row bands of about 2048 rows (up to 8):
 # (3000, 2048, 4608) two column blocks of B and of A, with tiny elements (below 2^-383) in both operands.
@@ -334,12 +334,13 @@ def test_context_streamed_matches_planned_run(oztt, oracle, cuda, m, n, k, phi, 
 
 def expected_bands(m, n):
     mp = round_up(m, 128)
-    if mp >= 4096:  # the path that computes while its operands upload: A's first 9/16 read back in one tile
-        pre = min(round_up(m * 9 // 16, 1024), m)  # per block of B's columns, then bands of 1024 rows (the last
-        nb = round_up(-(-n // 8), 256)        # one in halves when it has more than 512 rows)
-        rest = m - pre
-        last = rest - (rest - 1) // 1024 * 1024 if rest else 0
-        return -(-n // nb) + -(-rest // 1024) + (1 if last > 512 else 0)
+    if mp >= 4096:  # the path that computes while its operands upload: A's first half against each of B's
+        pre = min(round_up(m // 2, 1024), m)  # first blocks (one tile each), each later band of 1024 rows (one
+        nb = round_up(-(-n // 8), 256)        # tile), then each of B's last blocks against the whole A in parts
+        nblocks = -(-n // nb)                 # of 4096 rows (the last block: 2048)
+        first = min(nblocks // 2, nblocks - 1) + 1
+        last = sum(-(-m // (4096 if j + 1 < nblocks else 2048)) for j in range(first, nblocks))
+        return first + -(-(m - pre) // 1024) + last
     bm = round_up(-(-mp // min(8, max(1, mp // 2048))), 128)
     return -(-mp // bm)
 

@@ -1,7 +1,7 @@
 """Context::gemm for Scheme II INT8 computing while its operands upload (calls of at least 4096 rows).
 
-The upload order is B's first block of columns, A's first part (9/16 of its rows), B's other blocks, the
-rest of A. The pipeline starts on a plan estimated from A's first part and B's first block and is
+The upload order is B's first block of columns, A's first part (half of its rows, whole bands of 1024), B's
+next blocks, the rest of A, B's last blocks. The pipeline starts on a plan estimated from A's first part and B's first block and is
 confirmed, or run again, with the reference's plan from the complete statistics; C is read back as its
 pieces finish once every value is checked (unless C overlaps A or B, or some plan for the dimensions could
 fail). The result must be the device

@@ -14,9 +14,11 @@ from fractions import Fraction
 
 import pytest
 
-# the moduli of the 16384^3 metric plan (S = 17, b = 56) and a shorter even-S set
+# the moduli of the 16384^3 metric plan (S = 17, b = 56), a shorter even-S set, and a longer one whose
+# product (about 2^150) takes five words, so that C' has halves under the top two
 MODULI_17 = [255, 254, 253, 251, 247, 241, 239, 233, 229, 227, 223, 217, 211, 199, 197, 29, 37]
 MODULI_8 = [255, 254, 253, 251, 247, 241, 239, 233]
+MODULI_20 = MODULI_17 + [193, 191, 181]
 
 TWO52 = 2.0 ** 52
 MAGIC = 1.5 * 2.0 ** 52
@@ -76,7 +78,8 @@ def finish(kvals, moduli, g, two_b):
 
 
 def round_scaled(y, g, two_b):
-    """round_scaled: sign, the top word and the two below it with a sticky bit, one conversion, the scale."""
+    """round_scaled: sign, the top 64-bit half and the one below it with a sticky bit, one conversion, the
+    scale."""
     nw = len(y)
     neg = (y[-1] >> 31) != 0
     if neg:
@@ -84,21 +87,20 @@ def round_scaled(y, g, two_b):
         for w in range(nw):
             t = ((~y[w]) & 0xFFFFFFFF) + c
             y[w], c = t & 0xFFFFFFFF, t >> 32
-    hw, w0, w1, w2, a, b, sticky, below = -1, 0, 0, 0, 0, 0, False, False
-    for w in range(nw):
-        if y[w]:
-            hw, w0, w1, w2, sticky = w, y[w], a, b, below
-        below = below or b != 0
-        b, a = a, y[w]
-    if hw < 0:
+    halves = [((y[2 * i + 1] if 2 * i + 1 < nw else 0) << 32) | y[2 * i] for i in range((nw + 1) // 2)]
+    hh, t0, t1, a, sticky, below = -1, 0, 0, 0, False, False
+    for i, h in enumerate(halves):
+        if h:
+            hh, t0, t1, sticky = i, h, a, below
+        below = below or a != 0
+        a = h
+    if hh < 0:
         return 0.0
-    lz = 32 - w0.bit_length()
-    top = (w0 << 32) | w1
-    top64 = ((top << lz) | (w2 >> (32 - lz))) & (2 ** 64 - 1) if lz else top
-    rem = (w2 << lz) & 0xFFFFFFFF if lz else w2
-    sticky = sticky or rem != 0
+    lz = 64 - t0.bit_length()
+    top64 = ((t0 << lz) | (t1 >> (64 - lz))) & (2 ** 64 - 1) if lz else t0
+    sticky = sticky or ((t1 << lz) & (2 ** 64 - 1)) != 0
     v = float(top64 | (1 if sticky else 0))  # int -> float rounds to nearest even
-    p = 32 * hw + 31 - lz
+    p = 64 * hh + 63 - lz
     lead = p + g - two_b + (1 if v == 2.0 ** 64 else 0)
     if lead < -1022:
         r = 0.0
@@ -138,9 +140,9 @@ def cases(M, rng, count):
            (2 ** 53 + 1) * 2 ** 40, -((2 ** 53 + 1) * 2 ** 70), (2 ** 53 + 3) * 2 ** 60,  # ties of the rounding
            2 ** 54 - 1, -(2 ** 54 - 1)]  # rounds up to 2^54: at e = -1076 onto 2^-1022, kept
     # exact ties of the rounding to 53 bits, (2^53 + odd) 2^k, and the same one unit above or below in some
-    # lower bit j: the bit decides the direction through the sticky bit of the words under the top three
-    # (j < 32 (hw - 2)) or of the bits shifted out of the third word
-    for k in (1, 11, 31, 40, 60, 70):
+    # lower bit j: the bit decides the direction through the sticky bit of the halves under the top two or of
+    # the bits shifted out of the second
+    for k in (1, 11, 31, 40, 60, 70, 90, 96):
         for j in (0, 5, k - 1):
             if j < 0 or j >= k:
                 continue
@@ -155,7 +157,7 @@ def cases(M, rng, count):
     return [c for c in out if abs(c) <= hi]
 
 
-@pytest.mark.parametrize("moduli", [MODULI_17, MODULI_8], ids=["S17", "S8"])
+@pytest.mark.parametrize("moduli", [MODULI_17, MODULI_8, MODULI_20], ids=["S17", "S8", "S20"])
 def test_finish_matches_exact_rounding(moduli):
     rng = random.Random(20261202)
     M = math.prod(moduli)
