@@ -243,7 +243,8 @@ std::vector<cudaEvent_t> StreamedCall::upload_prefix_first(uint64_t pre_rows, ui
     for (; r0 < mid_end; r0 += band_rows) a_band(r0);
     for (; c0 < n_; c0 += block_cols) b_block(c0);
     launch_bcert_finish(b_colmax(), n_, b_acc(), k_, bcert_error_factor(n_), b_rg(), b_y(), b_ew(), cert_);
-    const uint64_t early_rows = r0, early_bands = landed.size();  // A's rows that landed before B's last block
+    // A's rows that landed before B's last block (r0 steps by whole bands, past m after a short last one)
+    const uint64_t early_rows = std::min(r0, m_), early_bands = landed.size();
     for (; r0 < m_; r0 += band_rows) a_band(r0);
     // the bands' bounded statistics need B's sketch: those that landed before B's last block in one pass (all
     // the rows at once keep every SM busy), each later one after it lands
