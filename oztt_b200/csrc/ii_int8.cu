@@ -358,7 +358,7 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     OZTT_CUDA(cudaMemsetAsync(words.p, 0, 16, st));
     uint32_t* flags = words.as<uint32_t>();
     int* gemm_err = words.as<int>() + 1;
-    std::unique_ptr<DevBuf> rb, ra, kpl, bt;
+    std::unique_ptr<DevBuf> rb, ra, kpl;
     const auto buffers = [&](const oztt_ii_plan& q, uint64_t a_rows) {
         const uint64_t S = (uint64_t)q.S;
         rb = std::make_unique<DevBuf>(st, S * np * kp);
@@ -380,7 +380,6 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     // rows there, each band of A against the columns there
     const auto following = [&](const oztt_ii_plan& q) {
         buffers(q, mp);
-        bt = std::make_unique<DevBuf>(st, std::min(nb, n) * k * 8);
         uint64_t rows_done = 0, cols_done = 0;
         // rows [r0, r0 + rows) of A (a multiple of 128 rows unless they end A): split into the whole planes
         const auto a_rows = [&](uint64_t r0, uint64_t rows_p) {
@@ -402,14 +401,14 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
         };
         // block j of B against the rows there; chunk: rows per product once all of A is there, so that the
         // read-back of one part overlaps the product of the next
-        // (B's block transposed into bt with its column maxima taken on the way, then split by rows)
+        // (a block of 2048 columns: the column kernels cost about what a transpose and the row split would)
         const auto b_block = [&](uint64_t j, uint64_t chunk) {
             const uint64_t c0 = j * nb, cols_p = std::min(nb, np - c0), cols = std::min(n, c0 + cols_p) - c0;
             OZTT_CUDA(cudaStreamWaitEvent(st, b_landed.at(j), 0));
-            launch_transpose_scale(db + c0, k, cols, n, bt->as<double>(), q.shift, dB.as<int32_t>() + c0, flags,
-                                   colmax.as<unsigned long long>() + c0, st);
-            launch_split_rows(bt->as<double>(), cols, k, k, dB.as<int32_t>() + c0, q, rb->as<int8_t>() + c0 * kp,
-                              cols_p, kp, st, np);
+            launch_scale_cols(db + c0, k, cols, n, q.shift, dB.as<int32_t>() + c0, nullptr, flags,
+                              colmax.as<unsigned long long>() + c0, st);
+            launch_split_cols(db + c0, k, cols, n, dB.as<int32_t>() + c0, q, rb->as<int8_t>() + c0 * kp, cols_p, kp,
+                              st, np);
             for (uint64_t r0 = 0; r0 < rows_done; r0 += chunk) tile(r0, std::min(chunk, rows_done - r0), c0, cols);
             cols_done = c0 + cols;
         };

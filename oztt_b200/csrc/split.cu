@@ -522,7 +522,7 @@ __global__ void __launch_bounds__(256) split_cols_kernel(const double* __restric
 // 32 rows of one column of a tile, four columns per warp, so each column's maximum is kept per lane across
 // the tiles, reduced across the warp once and given to one atomicMax per block (non-negative FP64 patterns
 // order like unsigned integers, NaN patterns above infinity, as in scale_rows_kernel).
-constexpr int kTransposeTiles = 8;
+constexpr int kTransposeTiles = 2;
 __global__ void __launch_bounds__(256) transpose_max_kernel(const double* __restrict__ b, uint64_t k, uint64_t n,
                                                             uint64_t ldb, double* __restrict__ bt,
                                                             unsigned long long* __restrict__ colmax) {

@@ -214,34 +214,44 @@ __global__ void __launch_bounds__(128) sketch_kernel(const double* __restrict__ 
 // the reference's values. y: the 8 x k sketch y_l = B g_l (scaled), as the reference has it or as
 // bcert_finish_kernel bounds it (then ew[j] bounds |y_l[j] - the reference's y_l[j]| over l). flags |= 1
 // when a nonzero element below 2^-383 makes the scaled squares leave the normal range (no bounds then).
-// A block of 8 warps takes 16 rows, two per warp, the lanes striding the columns; the sketch and ew go
-// through shared memory a chunk of kCertChunk columns at a time, so that each value is read from L2 once
-// per 16 rows and from shared memory once per 2 (the kernel is then bound by its 26 FP64 operations per
-// element, not by the reads of the sketch).
+// A block of 8 warps takes 8 rows, one per warp, the lanes striding the columns four at a time (all four
+// loads in flight before any is used); the sketch and ew go through shared memory a chunk of kCertChunk
+// columns at a time, so that each value is read from L2 once per 8 rows. Under 80 registers and 36 KB of
+// shared memory: three blocks share an SM, and each block's chunk loads overlap the others' arithmetic.
 constexpr int kCertW = 19;
-constexpr int kCertRowsPerWarp = 2, kCertWarps = 8, kCertRows = kCertRowsPerWarp * kCertWarps;
-constexpr int kCertChunk = 256;
+constexpr int kCertWarps = 8, kCertRows = kCertWarps;
+constexpr int kCertChunk = 512;
 __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restrict__ x, uint64_t rows, uint64_t k,
                                                            const double* __restrict__ y,
                                                            const double* __restrict__ ew, double* __restrict__ out,
                                                            uint32_t* __restrict__ flags) {
     // per row V = kCertW - 1 sums: s2, sl[8], al[8], se (slots 1 .. 18 of the row's output; slot 0 the maximum)
-    constexpr int R = kCertRowsPerWarp, V = 1 + 2 * kVectors + 1;
+    constexpr int V = 1 + 2 * kVectors + 1;
     static_assert(V + 1 == kCertW, "the sums and the maximum fill a row of the output");
     __shared__ double ys[kVectors][kCertChunk];
     __shared__ double es[kCertChunk];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint64_t r0 = ((uint64_t)blockIdx.x * kCertWarps + warp) * R;
-    const int nr = r0 >= rows ? 0 : (rows - r0 < (uint64_t)R ? (int)(rows - r0) : R);
-    unsigned long long mx[R];
-    double acc[R][V];
+    const uint64_t row = (uint64_t)blockIdx.x * kCertWarps + warp;
+    const bool live = row < rows;
+    const double* xr = x + (live ? row : 0) * k;
+    unsigned long long mx = 0;
+    double acc[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) acc[v] = 0.0;
     bool tiny = false;
+    const auto add = [&](double v, int j) {
+        const unsigned long long pat = (unsigned long long)__double_as_longlong(v) & 0x7FFFFFFFFFFFFFFFull;
+        mx = pat > mx ? pat : mx;
+        tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);  // 0 < |v| < 2^-383
+        acc[0] = fma(v, v, acc[0]);
+        acc[V - 1] = fma(fabs(v), es[j], acc[V - 1]);
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-        mx[r] = 0;
-#pragma unroll
-        for (int v = 0; v < V; ++v) acc[r][v] = 0.0;
-    }
+        for (int l = 0; l < kVectors; ++l) {
+            const double t = v * ys[l][j];
+            acc[1 + l] += t;
+            acc[1 + kVectors + l] += fabs(t);
+        }
+    };
     for (uint64_t j0 = 0; j0 < k; j0 += kCertChunk) {
         const int cw = k - j0 < (uint64_t)kCertChunk ? (int)(k - j0) : kCertChunk;
         __syncthreads();  // the previous chunk read by every warp
@@ -251,52 +261,32 @@ __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restr
         }
         for (int j = threadIdx.x; j < kCertChunk; j += blockDim.x) es[j] = (ew && j < cw) ? __ldg(ew + j0 + j) : 0.0;
         __syncthreads();
-        if (nr == 0) continue;
-        for (int j = lane; j < cw; j += 32) {
-            double yl[kVectors];
+        if (!live) continue;
+        for (int j = lane; j < cw; j += 128) {
+            double v[4];
 #pragma unroll
-            for (int l = 0; l < kVectors; ++l) yl[l] = ys[l][j];
-            const double e = es[j];
+            for (int u = 0; u < 4; ++u) v[u] = j + 32 * u < cw ? __ldg(xr + j0 + j + 32 * u) : 0.0;
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                if (r >= nr) break;
-                const double v = __ldg(x + (r0 + r) * k + j0 + j);
-                const unsigned long long pat = (unsigned long long)__double_as_longlong(v) & 0x7FFFFFFFFFFFFFFFull;
-                mx[r] = pat > mx[r] ? pat : mx[r];
-                tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);  // 0 < |v| < 2^-383
-                acc[r][0] = fma(v, v, acc[r][0]);
-                acc[r][V - 1] = fma(fabs(v), e, acc[r][V - 1]);
-#pragma unroll
-                for (int l = 0; l < kVectors; ++l) {
-                    const double t = v * yl[l];
-                    acc[r][1 + l] += t;
-                    acc[r][1 + kVectors + l] += fabs(t);
-                }
-            }
+            for (int u = 0; u < 4; ++u)
+                if (j + 32 * u < cw) add(v[u], j + 32 * u);
         }
     }
     // the lanes' sums (any order: the bounds hold for every order of the k terms)
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long om = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+        mx = om > mx ? om : mx;
 #pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            const unsigned long long om = __shfl_xor_sync(0xFFFFFFFFu, mx[r], o);
-            mx[r] = om > mx[r] ? om : mx[r];
-#pragma unroll
-            for (int v = 0; v < V; ++v) acc[r][v] += __shfl_xor_sync(0xFFFFFFFFu, acc[r][v], o);
-        }
+        for (int v = 0; v < V; ++v) acc[v] += __shfl_xor_sync(0xFFFFFFFFu, acc[v], o);
     }
     if (__any_sync(0xFFFFFFFFu, tiny) && lane == 0) atomicOr(flags, 1u);
-    // lane v < V writes sum v of each row into slot 1 + v, lane V the maximum into slot 0
+    if (!live) return;
+    // lane v < V writes sum v into slot 1 + v, lane V the maximum into slot 0
+    double* o = out + row * kCertW;
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-        if (r >= nr) break;
-        double* o = out + (r0 + r) * kCertW;
-#pragma unroll
-        for (int v = 0; v < V; ++v)
-            if (lane == v) o[1 + v] = acc[r][v];
-        if (lane == V) o[0] = __longlong_as_double((long long)mx[r]);
-    }
+    for (int v = 0; v < V; ++v)
+        if (lane == v) o[1 + v] = acc[v];
+    if (lane == V) o[0] = __longlong_as_double((long long)mx);
 }
 
 // Bounded statistics of B, a block of columns at a time as the blocks land (b: k rows of w elements from the
