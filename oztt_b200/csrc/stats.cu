@@ -245,11 +245,13 @@ __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restr
         tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);  // 0 < |v| < 2^-383
         acc[0] = fma(v, v, acc[0]);
         acc[V - 1] = fma(fabs(v), es[j], acc[V - 1]);
+        // the products fused into the sums: one rounding per term instead of two, within the same
+        // gamma(k) bound of sum |x y_l| that the host's bounds take for these sums
 #pragma unroll
         for (int l = 0; l < kVectors; ++l) {
-            const double t = v * ys[l][j];
-            acc[1 + l] += t;
-            acc[1 + kVectors + l] += fabs(t);
+            const double yl = ys[l][j];
+            acc[1 + l] = fma(v, yl, acc[1 + l]);
+            acc[1 + kVectors + l] = fma(fabs(v), fabs(yl), acc[1 + kVectors + l]);
         }
     };
     for (uint64_t j0 = 0; j0 < k; j0 += kCertChunk) {
