@@ -333,7 +333,9 @@ int run_ii_int8_overlapped(int device_id, const double* a, const double* b, doub
     // the pieces arrive: the first half of A against each block of B (about 0.8 of a block's upload time at
     // 16384^3), each later band against 5/8 of B (0.9 of a band's), each last block against the whole A
     // (1.5 of a block's, the excess left for the end), so that the device is idle little after the first
-    // plan and the last work is short. (9/16 of A first and all of B before the rest of A: about 3 ms more.)
+    // plan and the last work is short. (9/16 of A first and all of B before the rest of A measured the same
+    // per call; this order leaves the pass over A that needs all of B until after the last upload, where one
+    // launch over all rows keeps every SM busy.)
     const uint64_t pre = std::min(round_up(m / 2, bm), m);
     const uint64_t pre_bands = (pre + bm - 1) / bm;
     const uint64_t nb = round_up((n + 7) / 8, 256);  // B's blocks of columns
