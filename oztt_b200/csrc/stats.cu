@@ -216,11 +216,17 @@ __global__ void __launch_bounds__(128) sketch_kernel(const double* __restrict__ 
 // when a nonzero element below 2^-383 makes the scaled squares leave the normal range (no bounds then).
 // A block of 8 warps takes 8 rows, one per warp, the lanes striding the columns four at a time (all four
 // loads in flight before any is used); the sketch and ew go through shared memory a chunk of kCertChunk
-// columns at a time, so that each value is read from L2 once per 8 rows. Under 80 registers and 36 KB of
-// shared memory: three blocks share an SM, and each block's chunk loads overlap the others' arithmetic.
+// columns at a time, so that each value is read from L2 once per 8 rows, in two buffers: the next chunk's
+// asynchronous copies are in flight while this one is summed. 36 KB of shared memory a block.
 constexpr int kCertW = 19;
 constexpr int kCertWarps = 8, kCertRows = kCertWarps;
-constexpr int kCertChunk = 512;
+constexpr int kCertChunk = 256;
+// An 8-byte asynchronous copy from global into shared memory; when !valid nothing is read (src is then any
+// valid address) and the 8 bytes are zero-filled.
+__device__ __forceinline__ void cp_async8(double* dst, const double* src, bool valid) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 8 : 0) : "memory");
+}
 __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restrict__ x, uint64_t rows, uint64_t k,
                                                            const double* __restrict__ y,
                                                            const double* __restrict__ ew, double* __restrict__ out,
@@ -228,8 +234,8 @@ __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restr
     // per row V = kCertW - 1 sums: s2, sl[8], al[8], se (slots 1 .. 18 of the row's output; slot 0 the maximum)
     constexpr int V = 1 + 2 * kVectors + 1;
     static_assert(V + 1 == kCertW, "the sums and the maximum fill a row of the output");
-    __shared__ double ys[kVectors][kCertChunk];
-    __shared__ double es[kCertChunk];
+    __shared__ double ys[2][kVectors][kCertChunk];
+    __shared__ double es[2][kCertChunk];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint64_t row = (uint64_t)blockIdx.x * kCertWarps + warp;
     const bool live = row < rows;
@@ -239,40 +245,59 @@ __global__ void __launch_bounds__(256) band_certify_kernel(const double* __restr
 #pragma unroll
     for (int v = 0; v < V; ++v) acc[v] = 0.0;
     bool tiny = false;
-    const auto add = [&](double v, int j) {
+    const auto add = [&](double v, int j, int b) {
         const unsigned long long pat = (unsigned long long)__double_as_longlong(v) & 0x7FFFFFFFFFFFFFFFull;
         mx = pat > mx ? pat : mx;
         tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);  // 0 < |v| < 2^-383
         acc[0] = fma(v, v, acc[0]);
-        acc[V - 1] = fma(fabs(v), es[j], acc[V - 1]);
+        acc[V - 1] = fma(fabs(v), es[b][j], acc[V - 1]);
         // the products fused into the sums: one rounding per term instead of two, within the same
         // gamma(k) bound of sum |x y_l| that the host's bounds take for these sums
 #pragma unroll
         for (int l = 0; l < kVectors; ++l) {
-            const double yl = ys[l][j];
+            const double yl = ys[b][l][j];
             acc[1 + l] = fma(v, yl, acc[1 + l]);
             acc[1 + kVectors + l] = fma(fabs(v), fabs(yl), acc[1 + kVectors + l]);
         }
     };
-    for (uint64_t j0 = 0; j0 < k; j0 += kCertChunk) {
-        const int cw = k - j0 < (uint64_t)kCertChunk ? (int)(k - j0) : kCertChunk;
-        __syncthreads();  // the previous chunk read by every warp
+    // the sketch and ew of chunk c into buffer c & 1, asynchronously (zeros past k)
+    const auto stage = [&](uint64_t j0, int b) {
         for (int i = threadIdx.x; i < kVectors * kCertChunk; i += blockDim.x) {
             const int l = i / kCertChunk, j = i % kCertChunk;
-            ys[l][j] = j < cw ? __ldg(y + (uint64_t)l * k + j0 + j) : 0.0;
+            const bool in = j0 + j < k;
+            cp_async8(&ys[b][l][j], in ? y + (uint64_t)l * k + j0 + j : y, in);
         }
-        for (int j = threadIdx.x; j < kCertChunk; j += blockDim.x) es[j] = (ew && j < cw) ? __ldg(ew + j0 + j) : 0.0;
-        __syncthreads();
-        if (!live) continue;
-        for (int j = lane; j < cw; j += 128) {
-            double v[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) v[u] = j + 32 * u < cw ? __ldg(xr + j0 + j + 32 * u) : 0.0;
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-                if (j + 32 * u < cw) add(v[u], j + 32 * u);
+        for (int j = threadIdx.x; j < kCertChunk; j += blockDim.x) {
+            const bool in = ew && j0 + j < k;
+            cp_async8(&es[b][j], in ? ew + j0 + j : y, in);
         }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    };
+    stage(0, 0);
+    for (uint64_t j0 = 0, c = 0; j0 < k; j0 += kCertChunk, ++c) {
+        const int b = (int)(c & 1);
+        const int cw = k - j0 < (uint64_t)kCertChunk ? (int)(k - j0) : kCertChunk;
+        // the next chunk's copies go out before this one is summed (an empty group after the last chunk);
+        // its buffer was last read in the previous iteration, which every warp has left (the barrier below)
+        if (j0 + kCertChunk < k)
+            stage(j0 + kCertChunk, b ^ 1);
+        else
+            asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");  // this chunk's copies (this thread's) landed
+        __syncthreads();                                           // ... and every thread's
+        if (live) {
+            for (int j = lane; j < cw; j += 128) {
+                double v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) v[u] = j + 32 * u < cw ? __ldg(xr + j0 + j + 32 * u) : 0.0;
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (j + 32 * u < cw) add(v[u], j + 32 * u, b);
+            }
+        }
+        __syncthreads();  // every warp done with buffer b before the next iteration's copies refill it
     }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     // the lanes' sums (any order: the bounds hold for every order of the k terms)
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
