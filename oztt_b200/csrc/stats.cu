@@ -326,26 +326,53 @@ constexpr int kBCertW = 17;
 __global__ void __launch_bounds__(256) bcert_block_kernel(const double* __restrict__ b, uint64_t k, uint64_t w,
                                                           uint64_t ldb, const double* __restrict__ g, uint64_t gstride,
                                                           double* __restrict__ acc, uint32_t* __restrict__ flags) {
-    const uint64_t r = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (r >= k) return;
-    const double* br = b + r * ldb;
+    // the probe vectors over the block's columns go through shared memory kCertChunk columns at a time, in two
+    // buffers (the next chunk's asynchronous copies in flight while this one is summed), read from L2 once
+    // per 8 rows instead of once per row
+    __shared__ double gs[2][kVectors][kCertChunk];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t r = (uint64_t)blockIdx.x * kCertWarps + warp;
+    const bool live = r < k;
+    const double* br = b + (live ? r : 0) * ldb;
     bool tiny = false;
     double s2 = 0.0, sl[kVectors], al[kVectors];
 #pragma unroll
     for (int l = 0; l < kVectors; ++l) sl[l] = al[l] = 0.0;
-    for (uint64_t c = lane; c < w; c += 32) {
-        const double v = __ldg(br + c);
-        const unsigned long long pat = (unsigned long long)__double_as_longlong(v) & 0x7FFFFFFFFFFFFFFFull;
-        tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);
-        s2 = fma(v, v, s2);
-#pragma unroll
-        for (int l = 0; l < kVectors; ++l) {
-            const double t = v * __ldg(g + (uint64_t)l * gstride + c);
-            sl[l] += t;
-            al[l] += fabs(t);
+    const auto stage = [&](uint64_t c0, int buf) {
+        for (int i = threadIdx.x; i < kVectors * kCertChunk; i += blockDim.x) {
+            const int l = i / kCertChunk, c = i % kCertChunk;
+            const bool in = c0 + c < w;
+            cp_async8(&gs[buf][l][c], in ? g + (uint64_t)l * gstride + c0 + c : g, in);
         }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    };
+    stage(0, 0);
+    for (uint64_t c0 = 0, ch = 0; c0 < w; c0 += kCertChunk, ++ch) {
+        const int buf = (int)(ch & 1);
+        const int cw = w - c0 < (uint64_t)kCertChunk ? (int)(w - c0) : kCertChunk;
+        if (c0 + kCertChunk < w)
+            stage(c0 + kCertChunk, buf ^ 1);
+        else
+            asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+        __syncthreads();
+        if (live) {
+            for (int c = lane; c < cw; c += 32) {
+                const double v = __ldg(br + c0 + c);
+                const unsigned long long pat = (unsigned long long)__double_as_longlong(v) & 0x7FFFFFFFFFFFFFFFull;
+                tiny = tiny || (pat != 0 && pat < 0x1800000000000000ull);
+                s2 = fma(v, v, s2);
+#pragma unroll
+                for (int l = 0; l < kVectors; ++l) {
+                    const double t = v * gs[buf][l][c];
+                    sl[l] += t;
+                    al[l] += fabs(t);
+                }
+            }
+        }
+        __syncthreads();
     }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
         s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
@@ -356,7 +383,7 @@ __global__ void __launch_bounds__(256) bcert_block_kernel(const double* __restri
         }
     }
     if (__any_sync(0xFFFFFFFFu, tiny) && lane == 0) atomicOr(flags, 1u);
-    if (lane == 0) {
+    if (live && lane == 0) {
         double* o = acc + r * kBCertW;
 #pragma unroll
         for (int l = 0; l < kVectors; ++l) {
@@ -784,7 +811,8 @@ void launch_col_absmax(const double* b, uint64_t k, uint64_t w, uint64_t ldb, un
 void launch_bcert_block(const double* b, uint64_t k, uint64_t w, uint64_t ldb, const double* g, uint64_t gstride,
                         double* acc, uint32_t* flags, cudaStream_t st) {
     if (!k || !w) return;
-    bcert_block_kernel<<<(unsigned)((k * 32 + 255) / 256), 256, 0, st>>>(b, k, w, ldb, g, gstride, acc, flags);
+    bcert_block_kernel<<<(unsigned)((k + kCertWarps - 1) / kCertWarps), 256, 0, st>>>(b, k, w, ldb, g, gstride, acc,
+                                                                                       flags);
     OZTT_CUDA(cudaGetLastError());
 }
 
