@@ -248,10 +248,13 @@ __global__ void __launch_bounds__(256) recon_pair_kernel(const uint8_t* __restri
         for (int p = 0; p < kMaxPairs; ++p) {
             if ((uint32_t)p >= rc.P) break;
             const uint32_t ws = kw[2 * p], wt = kw[2 * p + 1];
-            const uint32_t ms = rc.pm_s[p], mt = rc.pm_t[p], mm = rc.pm_st[p];
+            const uint32_t mm = rc.pm_st[p];
+            const uint32_t mts = rc.pm_t[p] | (rc.pm_s[p] << 8);  // the multipliers as bytes: m_t, m_s, 0, 0
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const uint32_t u2 = ((ws >> (8 * e)) & 0xFFu) * mt + ((wt >> (8 * e)) & 0xFFu) * ms;  // < 2 mm
+                // k_s and k_t of element e in bytes 0 and 1 (bytes 2 and 3 meet zero multipliers): one byte dot
+                // product gives u2 = k_s m_t + k_t m_s < 2 mm (the moduli and the digits are below 256)
+                const uint32_t u2 = __dp4a(__byte_perm(ws, wt, (uint32_t)(e | ((4 + e) << 4))), mts, 0u);
                 const uint32_t u = min(u2, u2 - mm);  // u2 mod mm (u2 - mm wraps above u2 when u2 < mm)
                 // u as a double: 2^52 + u has u in its low significand bits; subtracting 2^52 is exact
                 const double ud = __dsub_rn(__hiloint2double(0x43300000, (int)u), two52);
